@@ -1,0 +1,360 @@
+"""Training engine protocol and the native B200 training engine.
+
+``TrainEngine`` is the protocol the trainer talks to (reference
+``engine/train_engine.py:90-171``).  ``B200TrainEngine`` replaces the
+reference's three backends (FSDP, Megatron3D, Megatron-Core) with one engine:
+
+* parameters: one flat bf16 buffer; ``nn.Parameter`` objects alias slices of it.
+* gradients: one flat fp32 buffer, filled by the GEMM epilogues through the
+  ``main_grad`` views (Megatron-Core's gradient-accumulation fusion).
+* optimizer: AdamW (betas 0.9/0.95, eps 1e-8, wd 0.01, clip 1.0 — reference
+  ``engine/megatron_core_train_engine.py:228-261``) over a flat fp32 master copy.
+  With ``use_distributed_optimizer`` and DP > 1 each rank owns a 1/DP shard of
+  master/Adam state; gradients are reduce-scattered and the updated bf16 shard
+  is all-gathered (distributed optimizer of Megatron-Core).
+* GRPO loss: PPO-clip with the log-ratio clamped to [-20, 20] and the k3 KL
+  ``(r - 1) - log r`` (reference ``engine/megatron_core_train_engine.py:950-986``);
+  per micro-batch masked token mean, averaged over micro-batches.
+* micro-batches: ``micro_batch_size`` consecutive trajectories packed into one
+  token stream (no padding); logprob recompute uses ``recompute_micro_batch_size``.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+import time
+from dataclasses import dataclass
+from typing import Any, Dict, Iterable, List, Optional, Protocol
+
+import torch
+import torch.distributed as dist
+
+from libra_b200 import ops
+from libra_b200.models.qwen3 import (PackedBatch, ParamLayout, Qwen3Config, Qwen3Model, get_config, init_params,
+                                     pack_sequences, param_shapes)
+
+
+class TrainEngine(Protocol):
+    """What the async trainer needs from a training backend."""
+
+    def initialize(self, max_seq_length: int = 2048) -> None: ...
+    def get_version(self) -> int: ...
+    def set_version(self, version: int) -> None: ...
+    def grpo_update(self, trajectories: List[Dict[str, Any]], ppo_epochs: int = 1) -> Dict[str, float]: ...
+    def recompute_logprobs(self, trajectories: List[Dict[str, Any]]) -> None: ...
+    def save_weights(self, path: str, version: int) -> None: ...
+    def get_data_parallel_rank(self) -> int: ...
+    def get_data_parallel_world_size(self) -> int: ...
+    def is_batch_source(self) -> bool: ...
+    def get_local_batch_size(self, global_batch_size: int) -> int: ...
+    def distribute_trajectories(self, trajectories): ...
+    def align_distributed_trajectories(self, trajectories): ...
+
+
+@dataclass
+class OptimConfig:
+    lr: float = 1e-6
+    betas: tuple = (0.9, 0.95)
+    eps: float = 1e-8
+    weight_decay: float = 0.01
+    max_grad_norm: float = 1.0
+
+
+class B200TrainEngine:
+    """Native GRPO training engine (single process per GPU)."""
+
+    train_backend = "b200"
+
+    def __init__(self, model: Any = "qwen3-4b", learning_rate: float = 1e-6, kl_coef: float = 0.001,
+                 clip_epsilon: float = 0.2, micro_batch_size: int = 4, recompute_micro_batch_size: int = 0,
+                 device: Optional[torch.device] = None, seed: int = 0, recompute_activations: bool = False,
+                 use_distributed_optimizer: bool = True, dp_group=None, temperature: float = 1.0,
+                 max_grad_norm: float = 1.0, tp_size: int = 1, model_path: str = ""):
+        self.cfg: Qwen3Config = get_config(model)
+        self.model_path = model_path
+        self.optim = OptimConfig(lr=learning_rate, max_grad_norm=max_grad_norm)
+        self.kl_coef = kl_coef
+        self.clip_epsilon = clip_epsilon
+        self.micro_batch_size = max(1, int(micro_batch_size))
+        self.recompute_micro_batch_size = int(recompute_micro_batch_size) or self.micro_batch_size
+        self.seed = seed
+        self.recompute_activations = recompute_activations
+        self.use_distributed_optimizer = use_distributed_optimizer
+        self.temperature = temperature
+        self.tp_size = tp_size
+        self.current_version = 0
+        self.step_count = 0
+        self.dp_group = dp_group
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.world_size = int(os.environ.get("WORLD_SIZE", "1"))
+        if device is None:
+            if torch.cuda.is_available():
+                device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+            else:
+                device = torch.device("cpu")
+        self.device = torch.device(device)
+        self.model: Optional[Qwen3Model] = None
+        self.last_timing: Dict[str, float] = {}
+
+    # ------------------------------------------------------------------ setup
+    def initialize(self, max_seq_length: int = 2048) -> None:
+        if self.device.type == "cuda":
+            torch.cuda.set_device(self.device)
+            ops.ext()  # fail loudly when the kernels are not built
+        self.max_seq_length = max_seq_length
+        self.dp_size = dist.get_world_size(self.dp_group) if dist.is_initialized() else 1
+        self.dp_rank = dist.get_rank(self.dp_group) if dist.is_initialized() else 0
+        shapes = param_shapes(self.cfg)
+        self.layout = ParamLayout(shapes)
+        P = self.layout.numel
+        # pad so the flat buffer splits evenly into DP shards of 128-element multiples
+        unit = ParamLayout.ALIGN * self.dp_size
+        self.padded_numel = (P + unit - 1) // unit * unit
+        dev = self.device
+        self.flat_param = torch.zeros(self.padded_numel, dtype=torch.bfloat16, device=dev)
+        self.flat_grad = torch.zeros(self.padded_numel, dtype=torch.float32, device=dev)
+        views = self.layout.views(self.flat_param)
+        init_params(self.cfg, views, seed=self.seed)
+        grad_views = self.layout.views(self.flat_grad)
+        self.params: Dict[str, torch.nn.Parameter] = {}
+        for name, v in views.items():
+            p = torch.nn.Parameter(v, requires_grad=True)
+            p.main_grad = grad_views[name]
+            self.params[name] = p
+        self.sharded = self.use_distributed_optimizer and self.dp_size > 1
+        shard = self.padded_numel // self.dp_size if self.sharded else self.padded_numel
+        self.shard_numel = shard
+        self.shard_start = self.dp_rank * shard if self.sharded else 0
+        self.master = self.flat_param[self.shard_start:self.shard_start + shard].float().clone()
+        self.exp_avg = torch.zeros_like(self.master)
+        self.exp_avg_sq = torch.zeros_like(self.master)
+        self.grad_shard = (torch.zeros(shard, dtype=torch.float32, device=dev) if self.sharded else self.flat_grad)
+        self.sq_norm = torch.zeros(1, dtype=torch.float32, device=dev)
+        self.model = Qwen3Model(self.cfg, self.params, recompute=self.recompute_activations)
+
+    # ------------------------------------------------------------------ protocol helpers
+    def get_version(self) -> int:
+        return self.current_version
+
+    def set_version(self, version: int) -> None:
+        self.current_version = int(version)
+
+    def get_data_parallel_rank(self) -> int:
+        return getattr(self, "dp_rank", 0)
+
+    def get_data_parallel_world_size(self) -> int:
+        return getattr(self, "dp_size", 1)
+
+    def is_batch_source(self) -> bool:
+        return True  # TP=1: every rank is a DP replica that owns its batch
+
+    def get_local_batch_size(self, global_batch_size: int) -> int:
+        return int(global_batch_size) // max(1, self.get_data_parallel_world_size())
+
+    def distribute_trajectories(self, trajectories):
+        return trajectories or []
+
+    def align_distributed_trajectories(self, trajectories):
+        return trajectories  # packed sequences need no cross-rank padding
+
+    def num_parameters(self) -> int:
+        return self.layout.numel
+
+    # ------------------------------------------------------------------ batching
+    @staticmethod
+    def _traj_tensors(traj: Dict[str, Any]):
+        ids = traj["input_ids"].reshape(-1)
+        mask = traj.get("loss_mask")
+        mask = torch.ones_like(ids) if mask is None else mask.reshape(-1)
+        return ids, mask
+
+    def pack(self, trajectories: List[Dict[str, Any]], with_old_logprobs: bool = True) -> Dict[str, Any]:
+        """Pack trajectories (host tensors) into one pinned host micro-batch."""
+        ids, masks = zip(*(self._traj_tensors(t) for t in trajectories))
+        batch = pack_sequences(list(ids), list(masks))
+        extra: Dict[str, torch.Tensor] = {}
+        if with_old_logprobs:
+            old = torch.cat([t["logprobs"].reshape(-1).float() for t in trajectories])
+            # old logprob of the action token at packed row r+1
+            extra["old_logp"] = old.index_select(0, batch.action_rows + 1)
+            adv = torch.tensor([float(t.get("advantages", t["rewards"]).reshape(-1)[0]) for t in trajectories])
+            extra["adv"] = adv.index_select(0, batch.seq_index.long())
+            extra["rewards"] = torch.tensor([float(t["rewards"].reshape(-1)[0]) for t in trajectories])
+        return {"batch": batch, **extra}
+
+    def to_device(self, packed: Dict[str, Any]) -> Dict[str, Any]:
+        dev = self.device
+        if dev.type == "cuda":
+            out = {"batch": _pin_batch(packed["batch"]).to(dev, non_blocking=True)}
+            for k, v in packed.items():
+                if k != "batch":
+                    out[k] = v.pin_memory().to(dev, non_blocking=True)
+            return out
+        return {"batch": packed["batch"], **{k: v for k, v in packed.items() if k != "batch"}}
+
+    def micro_batches(self, trajectories: List[Dict[str, Any]], size: int) -> Iterable[List[Dict[str, Any]]]:
+        for s in range(0, len(trajectories), size):
+            yield trajectories[s:s + size]
+
+    # ------------------------------------------------------------------ math
+    def loss(self, logp, old_logp, adv):
+        log_ratio = logp - old_logp
+        ratio = torch.exp(log_ratio.clamp(-20.0, 20.0))
+        clipped = ratio.clamp(1.0 - self.clip_epsilon, 1.0 + self.clip_epsilon)
+        pg = torch.maximum(-adv * ratio, -adv * clipped)
+        count = max(int(logp.numel()), 1)
+        pg_loss = pg.sum() / count
+        kl = ((ratio - 1.0) - log_ratio).sum() / count
+        return pg_loss + self.kl_coef * kl, pg_loss, kl
+
+    # ------------------------------------------------------------------ public API
+    @torch.no_grad()
+    def recompute_logprobs(self, trajectories: List[Dict[str, Any]]) -> None:
+        """Refresh trajectory["logprobs"] with the current policy (host tensors)."""
+        results = []
+        for mb in self.micro_batches(trajectories, self.recompute_micro_batch_size):
+            dev_mb = self.to_device(self.pack(mb, with_old_logprobs=False))
+            lp = self.model.action_logprobs(dev_mb["batch"], self.temperature)
+            results.append((mb, dev_mb["batch"], lp.to("cpu", non_blocking=True)))
+        if self.device.type == "cuda":
+            torch.cuda.current_stream(self.device).synchronize()
+        for mb, batch, lp in results:
+            rows = batch.action_rows.cpu() + 1
+            start = 0
+            cu = batch.cu_seqlens.cpu().tolist()
+            for i, traj in enumerate(mb):
+                L = cu[i + 1] - cu[i]
+                sel = (rows >= cu[i]) & (rows < cu[i + 1])
+                updated = torch.zeros(L, dtype=torch.float32)
+                updated[rows[sel] - cu[i]] = lp[sel]
+                traj["logprobs"] = updated.view(1, L).to(traj["logprobs"].dtype if "logprobs" in traj else torch.float32)
+
+    def grpo_update(self, trajectories: List[Dict[str, Any]], ppo_epochs: int = 1) -> Dict[str, float]:
+        """One optimizer step per PPO epoch over all micro-batches (host inputs)."""
+        epoch_stats = []
+        for _ in range(ppo_epochs):
+            mbs = [self.to_device(self.pack(mb)) for mb in self.micro_batches(trajectories, self.micro_batch_size)]
+            epoch_stats.append(self.update_packed(mbs))
+        merged = _merge_stats(epoch_stats)
+        merged["version"] = self.current_version
+        return merged
+
+    def update_packed(self, device_micro_batches: List[Dict[str, Any]], sync_stats: bool = True) -> Dict[str, Any]:
+        """Forward/backward over device-resident micro-batches + optimizer step."""
+        self.flat_grad.zero_()
+        n_mb = max(len(device_micro_batches), 1)
+        loss_acc = torch.zeros(3, dtype=torch.float32, device=self.device)
+        reward_sum, n_samples = 0.0, 0
+        for mb in device_micro_batches:
+            logp = self.model.action_logprobs(mb["batch"], self.temperature)
+            loss, pg, kl = self.loss(logp, mb["old_logp"], mb["adv"])
+            (loss / n_mb).backward()
+            loss_acc += torch.stack([loss.detach(), pg.detach(), kl.detach()])
+            if "rewards" in mb:
+                reward_sum_t = mb["rewards"].sum()
+                reward_sum += float(reward_sum_t) if not sync_stats or self.device.type == "cpu" else 0.0
+                n_samples += int(mb["rewards"].numel())
+        self._reduce_gradients()
+        self._optimizer_step()
+        stats = {"loss_sum": loss_acc, "n_updates": float(n_mb), "n_samples": float(n_samples)}
+        if sync_stats:
+            values = (loss_acc / n_mb).tolist()
+            rewards = torch.cat([mb["rewards"] for mb in device_micro_batches if "rewards" in mb]) \
+                if any("rewards" in mb for mb in device_micro_batches) else torch.zeros(0)
+            rs = float(rewards.sum()) if rewards.numel() else 0.0
+            out = {"loss": values[0], "pg_loss": values[1], "kl": values[2], "reward_sum": rs,
+                   "n_samples": float(rewards.numel()), "n_updates": 1.0,
+                   "reward_mean": rs / max(rewards.numel(), 1),
+                   "grad_norm": float(self.sq_norm.sqrt())}
+            return self._reduce_stats(out)
+        return stats
+
+    # ------------------------------------------------------------------ gradients/optimizer
+    def _reduce_gradients(self) -> None:
+        if self.dp_size <= 1 or not dist.is_initialized():
+            return
+        if self.sharded:
+            dist.reduce_scatter_tensor(self.grad_shard, self.flat_grad, op=dist.ReduceOp.SUM, group=self.dp_group)
+            self.grad_shard.div_(self.dp_size)
+        else:
+            dist.all_reduce(self.flat_grad, op=dist.ReduceOp.SUM, group=self.dp_group)
+            self.flat_grad.div_(self.dp_size)
+
+    def _optimizer_step(self) -> None:
+        self.step_count += 1
+        self.sq_norm.zero_()
+        ops.grad_sq_norm(self.grad_shard, self.sq_norm)
+        if self.sharded:
+            dist.all_reduce(self.sq_norm, op=dist.ReduceOp.SUM, group=self.dp_group)
+        shard_param = self.flat_param[self.shard_start:self.shard_start + self.shard_numel]
+        o = self.optim
+        ops.adamw_step(self.master, self.grad_shard, self.exp_avg, self.exp_avg_sq, shard_param, lr=o.lr,
+                       beta1=o.betas[0], beta2=o.betas[1], eps=o.eps, weight_decay=o.weight_decay,
+                       step=self.step_count, max_grad_norm=o.max_grad_norm, sq_norm=self.sq_norm)
+        if self.sharded:
+            dist.all_gather_into_tensor(self.flat_param, shard_param.clone(), group=self.dp_group)
+
+    def _reduce_stats(self, stats: Dict[str, float]) -> Dict[str, float]:
+        if self.dp_size <= 1 or not dist.is_initialized():
+            return stats
+        vec = torch.tensor([stats["loss"], stats["pg_loss"], stats["kl"], stats["reward_sum"], stats["n_samples"],
+                            stats["n_updates"], stats["grad_norm"]], dtype=torch.float32, device=self.device)
+        dist.all_reduce(vec, group=self.dp_group)
+        n = self.dp_size
+        v = vec.tolist()
+        return {"loss": v[0] / n, "pg_loss": v[1] / n, "kl": v[2] / n, "reward_sum": v[3], "n_samples": v[4],
+                "n_updates": v[5], "reward_mean": v[3] / max(v[4], 1.0), "grad_norm": v[6] / n}
+
+    # ------------------------------------------------------------------ weights
+    def state_dict(self) -> Dict[str, torch.Tensor]:
+        return {k: v.detach() for k, v in self.params.items()}
+
+    def save_weights(self, path: str, version: int) -> None:
+        from libra_b200.engine.checkpointing import DistributedCheckpointManager
+
+        DistributedCheckpointManager(path).save(self, version)
+
+    def load_weights(self, path: str, version: Optional[int] = None) -> None:
+        from libra_b200.engine.checkpointing import DistributedCheckpointManager
+
+        DistributedCheckpointManager(path).load(self, version)
+
+
+def _pin_batch(b: PackedBatch) -> PackedBatch:
+    pin = lambda t: t if t is None or t.is_pinned() else t.pin_memory()  # noqa: E731
+    return PackedBatch(pin(b.tokens), pin(b.positions), pin(b.cu_seqlens), b.max_seqlen, pin(b.action_rows),
+                       pin(b.action_targets), pin(b.seq_index))
+
+
+def _merge_stats(stats: List[Dict[str, float]]) -> Dict[str, float]:
+    if not stats:
+        return {"loss": 0.0, "pg_loss": 0.0, "kl": 0.0, "reward_sum": 0.0, "reward_mean": 0.0, "n_samples": 0.0,
+                "n_updates": 0.0}
+    updates = sum(float(s.get("n_updates", 1.0)) for s in stats)
+    samples = sum(float(s.get("n_samples", 0.0)) for s in stats)
+    rsum = sum(float(s.get("reward_sum", 0.0)) for s in stats)
+    wavg = lambda key: sum(float(s.get(key, 0.0)) * float(s.get("n_updates", 1.0)) for s in stats) / max(updates, 1.0)  # noqa: E731
+    return {"loss": wavg("loss"), "pg_loss": wavg("pg_loss"), "kl": wavg("kl"), "reward_sum": rsum,
+            "reward_mean": rsum / max(samples, 1.0), "n_samples": samples, "n_updates": updates,
+            "grad_norm": wavg("grad_norm")}
+
+
+def create_train_engine(config) -> B200TrainEngine:
+    """Factory from an AsyncRLConfig (reference ``engine/train_factory.py:11-76``).
+
+    Every ``train_backend`` value maps onto the native engine; the model preset
+    is taken from ``model_path`` when it names a preset, else from model_arch.
+    """
+    name = os.path.basename(str(config.model_path)).lower()
+    try:
+        cfg = get_config(name)
+    except KeyError:
+        from libra_b200.models.qwen3 import config_from_arch
+
+        cfg = config_from_arch(config.model_arch)
+    return B200TrainEngine(model=cfg, learning_rate=config.learning_rate, kl_coef=config.kl_coef,
+                           clip_epsilon=config.clip_epsilon, micro_batch_size=config.micro_batch_size,
+                           recompute_micro_batch_size=config.recompute_micro_batch_size, seed=config.seed,
+                           use_distributed_optimizer=config.use_distributed_optimizer,
+                           temperature=config.temperature, model_path=config.model_path)

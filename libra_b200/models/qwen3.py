@@ -1,0 +1,399 @@
+"""Qwen3 decoder family (dense and MoE) on the libra_b200 fused operators.
+
+Architecture as trained by the reference through Megatron-Core / HF
+(``engine/megatron_core_train_engine.py:279-317``, model arch YAMLs
+``configs/model_arch_config/qwen3-*.yaml``): pre-norm decoder blocks with GQA
+attention, per-head q/k RMSNorm, rotary embedding (theta 1e6), SwiGLU MLP or a
+top-k routed expert MLP, final RMSNorm and an LM head (tied to the embedding
+for Qwen3-4B).
+
+B200 design choices:
+
+* Sequences are **packed** into one token stream with ``cu_seqlens`` instead of
+  being padded to the batch maximum (the reference pads,
+  ``engine/megatron_core_train_engine.py:400-488``), so no FLOPs are spent on
+  padding.
+* All parameters live in **one flat bf16 buffer** (``ParamLayout``); the
+  optimizer, the gradient reduction and the rollout weight sync each operate
+  on a single contiguous buffer.  Gradients accumulate into a parallel flat
+  fp32 buffer through ``weight.main_grad`` views.
+* QKV and gate/up projections are fused column blocks; the o-proj and down
+  projections add the residual inside the GEMM epilogue.
+* The LM head is evaluated only on rows whose next token is an action token and
+  is fused with the log-softmax (no fp32 [tokens, vocab] tensor).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field, asdict
+from typing import Dict, List, Optional, Tuple
+
+import torch
+import torch.nn as nn
+
+from libra_b200 import ops
+
+
+@dataclass
+class Qwen3Config:
+    vocab_size: int = 151936
+    hidden_size: int = 2560
+    intermediate_size: int = 9728
+    num_hidden_layers: int = 36
+    num_attention_heads: int = 32
+    num_key_value_heads: int = 8
+    head_dim: int = 128
+    rope_theta: float = 1_000_000.0
+    rms_norm_eps: float = 1e-6
+    tie_word_embeddings: bool = True
+    max_position_embeddings: int = 40960
+    initializer_range: float = 0.02
+    # MoE (num_experts == 0 -> dense)
+    num_experts: int = 0
+    num_experts_per_tok: int = 8
+    moe_intermediate_size: int = 768
+    norm_topk_prob: bool = True
+    router_init_std: float = 1.0
+
+    @property
+    def is_moe(self) -> bool:
+        return self.num_experts > 0
+
+    @property
+    def q_width(self) -> int:
+        return self.num_attention_heads * self.head_dim
+
+    @property
+    def kv_width(self) -> int:
+        return self.num_key_value_heads * self.head_dim
+
+    def num_params(self) -> int:
+        return sum(math.prod(shape) for _, shape in param_shapes(self))
+
+    def active_params(self) -> int:
+        if not self.is_moe:
+            return self.num_params()
+        total = 0
+        for name, shape in param_shapes(self):
+            n = math.prod(shape)
+            if ".experts." in name:
+                n = n * self.num_experts_per_tok // self.num_experts
+            total += n
+        return total
+
+    def to_dict(self) -> dict:
+        return asdict(self)
+
+
+PRESETS: Dict[str, Qwen3Config] = {
+    "qwen3-4b": Qwen3Config(),
+    "qwen3-14b": Qwen3Config(hidden_size=5120, intermediate_size=17408, num_hidden_layers=40,
+                             num_attention_heads=40, num_key_value_heads=8, tie_word_embeddings=False),
+    "qwen3-30b-a3b": Qwen3Config(hidden_size=2048, intermediate_size=6144, num_hidden_layers=48,
+                                 num_attention_heads=32, num_key_value_heads=4, tie_word_embeddings=False,
+                                 num_experts=128, num_experts_per_tok=8, moe_intermediate_size=768),
+    # CPU plumbing model (2 layers, hidden 256, 4/2 heads of 64, FFN 704, vocab 1024)
+    "tiny": Qwen3Config(vocab_size=1024, hidden_size=256, intermediate_size=704, num_hidden_layers=2,
+                        num_attention_heads=4, num_key_value_heads=2, head_dim=64, tie_word_embeddings=True,
+                        max_position_embeddings=4096),
+    # smallest GPU-kernel-compatible model (head_dim 128) for tests and smoke runs
+    "tiny-gpu": Qwen3Config(vocab_size=2048, hidden_size=512, intermediate_size=1024, num_hidden_layers=2,
+                            num_attention_heads=4, num_key_value_heads=2, head_dim=128, tie_word_embeddings=True,
+                            max_position_embeddings=8192),
+    "tiny-moe": Qwen3Config(vocab_size=2048, hidden_size=512, intermediate_size=1024, num_hidden_layers=2,
+                            num_attention_heads=4, num_key_value_heads=2, head_dim=128, tie_word_embeddings=False,
+                            num_experts=8, num_experts_per_tok=2, moe_intermediate_size=256,
+                            max_position_embeddings=8192),
+}
+
+
+def get_config(name_or_cfg) -> Qwen3Config:
+    if isinstance(name_or_cfg, Qwen3Config):
+        return name_or_cfg
+    key = str(name_or_cfg).lower()
+    if key not in PRESETS:
+        raise KeyError(f"unknown model preset {name_or_cfg!r}; known: {sorted(PRESETS)}")
+    return PRESETS[key]
+
+
+# ---------------------------------------------------------------------------
+# parameter layout
+# ---------------------------------------------------------------------------
+
+def param_shapes(cfg: Qwen3Config, tp_size: int = 1, tp_rank: int = 0) -> List[Tuple[str, Tuple[int, ...]]]:
+    """Canonical (name, local shape) list for one tensor-parallel rank.
+
+    Column-parallel blocks (QKV, gate/up, expert w1) are split along their
+    output rows, row-parallel blocks (o-proj, down, expert w2) along their input
+    columns, and the embedding / LM head along the vocabulary.
+    """
+    H, D = cfg.hidden_size, cfg.head_dim
+    nq, nkv = cfg.num_attention_heads, cfg.num_key_value_heads
+    if nq % tp_size or cfg.intermediate_size % tp_size or cfg.vocab_size % tp_size:
+        raise ValueError(f"tp_size={tp_size} does not divide the model dimensions")
+    kv_local = max(1, nkv // tp_size)  # replicate KV heads when tp > nkv
+    nq_l = nq // tp_size
+    V_l = cfg.vocab_size // tp_size
+    shapes: List[Tuple[str, Tuple[int, ...]]] = [("embed_tokens", (V_l, H))]
+    for i in range(cfg.num_hidden_layers):
+        p = f"layers.{i}."
+        shapes += [
+            (p + "input_layernorm", (H,)),
+            (p + "qkv_proj", ((nq_l + 2 * kv_local) * D, H)),
+            (p + "q_norm", (D,)),
+            (p + "k_norm", (D,)),
+            (p + "o_proj", (H, nq_l * D)),
+            (p + "post_attention_layernorm", (H,)),
+        ]
+        if cfg.is_moe:
+            E, Fe = cfg.num_experts, cfg.moe_intermediate_size
+            shapes += [
+                (p + "router", (E, H)),
+                (p + "experts.w1", (E, 2 * Fe // tp_size, H)),
+                (p + "experts.w2", (E, H, Fe // tp_size)),
+            ]
+        else:
+            F = cfg.intermediate_size // tp_size
+            shapes += [(p + "gate_up_proj", (2 * F, H)), (p + "down_proj", (H, F))]
+    shapes.append(("norm", (H,)))
+    if not cfg.tie_word_embeddings:
+        shapes.append(("lm_head", (V_l, H)))
+    return shapes
+
+
+class ParamLayout:
+    """Offsets of every parameter inside the flat buffer (256-byte aligned)."""
+
+    ALIGN = 128  # elements; keeps every view 16-byte aligned for TMA in bf16 and fp32
+
+    def __init__(self, shapes: List[Tuple[str, Tuple[int, ...]]]):
+        self.shapes = dict(shapes)
+        self.order = [n for n, _ in shapes]
+        self.offsets: Dict[str, int] = {}
+        off = 0
+        for name, shape in shapes:
+            self.offsets[name] = off
+            n = math.prod(shape)
+            off += (n + self.ALIGN - 1) // self.ALIGN * self.ALIGN
+        self.numel = off
+
+    def views(self, flat: torch.Tensor) -> Dict[str, torch.Tensor]:
+        out = {}
+        for name in self.order:
+            shape = self.shapes[name]
+            off = self.offsets[name]
+            out[name] = flat[off:off + math.prod(shape)].view(shape)
+        return out
+
+    def segment(self, name: str) -> Tuple[int, int]:
+        off = self.offsets[name]
+        return off, off + math.prod(self.shapes[name])
+
+
+def init_params(cfg: Qwen3Config, views: Dict[str, torch.Tensor], seed: int = 0) -> None:
+    """Random init in place: N(0, initializer_range) for matrices, 1 for norms,
+    N(0, router_init_std) for MoE routers (router logits ~ N(0,1) scale)."""
+    gen_device = next(iter(views.values())).device
+    g = torch.Generator(device=gen_device)
+    g.manual_seed(seed)
+    with torch.no_grad():
+        for name, t in views.items():
+            if t.dim() == 1:
+                t.fill_(1.0)
+            elif name.endswith("router"):
+                t.normal_(0.0, cfg.router_init_std / math.sqrt(cfg.hidden_size), generator=g)
+            else:
+                t.normal_(0.0, cfg.initializer_range, generator=g)
+
+
+# ---------------------------------------------------------------------------
+# packed batch
+# ---------------------------------------------------------------------------
+
+@dataclass
+class PackedBatch:
+    """Sequences packed into one stream.
+
+    tokens/positions: [T]; cu_seqlens: [B+1] int32; max_seqlen: int.
+    action_rows: indices t whose next token tokens[t+1] is scored (loss rows);
+    action_targets: tokens[t+1] for those rows.
+    """
+
+    tokens: torch.Tensor
+    positions: torch.Tensor
+    cu_seqlens: torch.Tensor
+    max_seqlen: int
+    action_rows: torch.Tensor
+    action_targets: torch.Tensor
+    seq_index: Optional[torch.Tensor] = None  # sequence id of each action row
+
+    def to(self, device, non_blocking: bool = True) -> "PackedBatch":
+        mv = lambda t: None if t is None else t.to(device, non_blocking=non_blocking)  # noqa: E731
+        return PackedBatch(mv(self.tokens), mv(self.positions), mv(self.cu_seqlens), self.max_seqlen,
+                           mv(self.action_rows), mv(self.action_targets), mv(self.seq_index))
+
+    @property
+    def num_tokens(self) -> int:
+        return int(self.tokens.numel())
+
+
+def pack_sequences(seqs: List[torch.Tensor], masks: Optional[List[torch.Tensor]] = None,
+                   pin: bool = False) -> PackedBatch:
+    """Pack 1-D token tensors; ``masks[i][t] = 1`` marks tokens[t] as an action token
+    (its logprob is computed from the row t-1)."""
+    lens = [int(s.numel()) for s in seqs]
+    cu = torch.zeros(len(seqs) + 1, dtype=torch.int32)
+    cu[1:] = torch.tensor(lens, dtype=torch.int32).cumsum(0)
+    tokens = torch.cat([s.reshape(-1).long() for s in seqs]) if seqs else torch.zeros(0, dtype=torch.long)
+    positions = torch.cat([torch.arange(n, dtype=torch.int32) for n in lens]) if seqs else torch.zeros(0, dtype=torch.int32)
+    rows, targets, sidx = [], [], []
+    for i, s in enumerate(seqs):
+        start = int(cu[i])
+        m = masks[i].reshape(-1) if masks is not None else torch.ones(lens[i], dtype=torch.bool)
+        idx = torch.nonzero(m[1:].bool(), as_tuple=False).reshape(-1)  # positions t+1 that are actions
+        rows.append(idx + start)
+        targets.append(s.reshape(-1)[idx + 1].long())
+        sidx.append(torch.full((idx.numel(),), i, dtype=torch.int32))
+    action_rows = torch.cat(rows) if rows else torch.zeros(0, dtype=torch.long)
+    action_targets = torch.cat(targets) if targets else torch.zeros(0, dtype=torch.long)
+    seq_index = torch.cat(sidx) if sidx else torch.zeros(0, dtype=torch.int32)
+    batch = PackedBatch(tokens, positions, cu, max(lens) if lens else 0, action_rows.long(), action_targets, seq_index)
+    if pin:
+        batch = PackedBatch(*(t.pin_memory() if isinstance(t, torch.Tensor) else t for t in
+                              (batch.tokens, batch.positions, batch.cu_seqlens, batch.max_seqlen, batch.action_rows,
+                               batch.action_targets, batch.seq_index)))
+    return batch
+
+
+# ---------------------------------------------------------------------------
+# model
+# ---------------------------------------------------------------------------
+
+class Qwen3Model(nn.Module):
+    """Stateless-compute model over externally owned parameter views.
+
+    ``params`` maps canonical names to tensors (views into a flat buffer); the
+    module never allocates parameters itself, which lets the engine place them
+    in a flat buffer or in peer-visible memory.
+    """
+
+    def __init__(self, cfg: Qwen3Config, params: Dict[str, torch.Tensor], recompute: bool = False,
+                 tp_group=None, tp_size: int = 1, tp_rank: int = 0):
+        super().__init__()
+        self.cfg = cfg
+        self.p = params
+        self.recompute = recompute
+        self.tp_group, self.tp_size, self.tp_rank = tp_group, tp_size, tp_rank
+        dev = next(iter(params.values())).device
+        cos, sin = ops.ref.rope_tables(cfg.max_position_embeddings, cfg.head_dim, cfg.rope_theta, dev)
+        self.register_buffer("rope_cos", cos, persistent=False)
+        self.register_buffer("rope_sin", sin, persistent=False)
+        self.nq_local = cfg.num_attention_heads // tp_size
+        self.nkv_local = max(1, cfg.num_key_value_heads // tp_size)
+
+    # -- blocks ------------------------------------------------------------
+    def _attention_block(self, i: int, x, pos, cu, max_len):
+        p, cfg = self.p, self.cfg
+        pre = f"layers.{i}."
+        h = ops.rmsnorm(x, p[pre + "input_layernorm"], cfg.rms_norm_eps)
+        qkv = ops.linear(h, p[pre + "qkv_proj"])
+        q, k, v = ops.qk_norm_rope(qkv, p[pre + "q_norm"], p[pre + "k_norm"], pos, self.rope_cos, self.rope_sin,
+                                   self.nq_local, self.nkv_local, cfg.rms_norm_eps)
+        attn = ops.varlen_causal_attention(q, k, v, cu, max_len)
+        return self._row_parallel(attn.reshape(attn.shape[0], -1), p[pre + "o_proj"], x)
+
+    def _mlp_block(self, i: int, x):
+        p, cfg = self.p, self.cfg
+        pre = f"layers.{i}."
+        h = ops.rmsnorm(x, p[pre + "post_attention_layernorm"], cfg.rms_norm_eps)
+        if cfg.is_moe:
+            from libra_b200.models.moe import moe_mlp
+
+            return moe_mlp(h, x, p[pre + "router"], p[pre + "experts.w1"], p[pre + "experts.w2"], cfg)
+        gu = ops.linear(h, p[pre + "gate_up_proj"])
+        a = ops.swiglu(gu)
+        return self._row_parallel(a, p[pre + "down_proj"], x)
+
+    def _row_parallel(self, a, w, residual):
+        if self.tp_size == 1:
+            return ops.linear(a, w, residual=residual)
+        from libra_b200.parallel.tensor_parallel import row_parallel_linear
+
+        return row_parallel_linear(a, w, residual, self.tp_group)
+
+    def _layer(self, i, x, pos, cu, max_len):
+        x = self._attention_block(i, x, pos, cu, max_len)
+        return self._mlp_block(i, x)
+
+    # -- public ------------------------------------------------------------
+    def embed(self, tokens):
+        w = self.p["embed_tokens"]
+        if self.tp_size == 1:
+            return _Embedding.apply(tokens, w)
+        from libra_b200.parallel.tensor_parallel import vocab_parallel_embedding
+
+        return vocab_parallel_embedding(tokens, w, self.tp_group, self.tp_rank)
+
+    def hidden_states(self, batch: PackedBatch) -> torch.Tensor:
+        x = self.embed(batch.tokens)
+        for i in range(self.cfg.num_hidden_layers):
+            if self.recompute and torch.is_grad_enabled():
+                x = torch.utils.checkpoint.checkpoint(self._layer, i, x, batch.positions, batch.cu_seqlens,
+                                                      batch.max_seqlen, use_reentrant=False)
+            else:
+                x = self._layer(i, x, batch.positions, batch.cu_seqlens, batch.max_seqlen)
+        return ops.rmsnorm(x, self.p["norm"], self.cfg.rms_norm_eps)
+
+    @property
+    def lm_head_weight(self):
+        return self.p["embed_tokens"] if self.cfg.tie_word_embeddings else self.p["lm_head"]
+
+    def action_logprobs(self, batch: PackedBatch, temperature: float = 1.0, entropy_out=None) -> torch.Tensor:
+        """Logprob of every action token (rows ``batch.action_rows``)."""
+        h = self.hidden_states(batch)
+        rows = h.index_select(0, batch.action_rows)
+        if self.tp_size == 1:
+            return ops.lm_head_logprob(rows, self.lm_head_weight, batch.action_targets, temperature, entropy_out)
+        from libra_b200.parallel.tensor_parallel import vocab_parallel_logprob
+
+        return vocab_parallel_logprob(rows, self.lm_head_weight, batch.action_targets, temperature, self.tp_group,
+                                      self.tp_rank, entropy_out)
+
+    def logits(self, batch: PackedBatch) -> torch.Tensor:
+        """Full logits [T, V] (inference/sampling helper)."""
+        h = self.hidden_states(batch)
+        return ops.linear(h, self.lm_head_weight)
+
+
+class _Embedding(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, tokens, w):
+        ctx.save_for_backward(tokens)
+        ctx.wref = w
+        return w.index_select(0, tokens)
+
+    @staticmethod
+    def backward(ctx, g):
+        (tokens,) = ctx.saved_tensors
+        w = ctx.wref
+        main = getattr(w, "main_grad", None)
+        if main is not None:
+            main.index_add_(0, tokens, g.float())
+            return None, None
+        out = torch.zeros(w.shape, dtype=torch.float32, device=w.device)
+        out.index_add_(0, tokens, g.float())
+        return None, out.to(w.dtype)
+
+
+def config_from_arch(arch) -> Qwen3Config:
+    """Build a model config from the planner's ``ModelArchConfig`` section."""
+    return Qwen3Config(
+        vocab_size=int(arch.vocab_size), hidden_size=int(arch.d_model), intermediate_size=int(arch.intermediate_size),
+        num_hidden_layers=int(arch.n_layers), num_attention_heads=int(arch.n_heads),
+        num_key_value_heads=int(arch.n_kv_heads), head_dim=int(arch.head_dim),
+        tie_word_embeddings=float(arch.num_params) < 8e9 and not arch.is_moe,
+        num_experts=int(arch.num_experts) if arch.is_moe else 0,
+        num_experts_per_tok=int(arch.num_activated_experts),
+        moe_intermediate_size=int(arch.expert_intermediate_size),
+    )

@@ -1,0 +1,369 @@
+"""Fused sm_100a operators with autograd.
+
+Every op dispatches on the device of its inputs:
+
+* CUDA tensors run the hand-written kernels in ``libra_b200._C`` (tcgen05 GEMM,
+  RMSNorm, q/k-norm+RoPE, SwiGLU, fused logprob, AdamW).  If the extension is
+  missing on a machine with a GPU the call raises; there is no silent fallback.
+* CPU tensors run the fp32 PyTorch reference in :mod:`libra_b200.ops.reference`
+  (used by the gloo multi-process plumbing tests and as the numerics oracle).
+
+Weight gradients follow the "main_grad" convention of Megatron-Core's gradient
+accumulation fusion: when a weight carries a ``main_grad`` fp32 tensor (a view
+into the engine's flat gradient buffer) the backward pass accumulates into it
+directly from the GEMM epilogue and returns ``None`` for the weight.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+from typing import Optional
+
+import torch
+
+from . import reference as ref
+
+_EXT = None
+_ERR = {}
+
+EPI_BF16, EPI_F32, EPI_ACC_F32, EPI_BF16_RESIDUAL = 0, 1, 2, 3
+
+
+def ext():
+    """The compiled extension; raises with a build hint when absent."""
+    global _EXT
+    if _EXT is None:
+        try:
+            from libra_b200 import _C  # noqa: WPS433
+        except ImportError as exc:  # pragma: no cover - exercised only without a build
+            raise RuntimeError(
+                "libra_b200._C is not built; run `python setup.py build_ext --inplace` "
+                "(or __graft_entry__.build()) before using CUDA tensors"
+            ) from exc
+        _EXT = _C
+    return _EXT
+
+
+def extension_available() -> bool:
+    try:
+        ext()
+        return True
+    except RuntimeError:
+        return False
+
+
+def error_flag(device: torch.device) -> torch.Tensor:
+    """Per-device int32 word that kernels set when a bounded wait gives up."""
+    key = (device.type, device.index)
+    flag = _ERR.get(key)
+    if flag is None:
+        flag = torch.zeros(1, dtype=torch.int32, device=device)
+        _ERR[key] = flag
+    return flag
+
+
+def check_kernel_errors(device: Optional[torch.device] = None) -> None:
+    """Raise if any kernel on ``device`` reported a timeout (forces a sync)."""
+    for (dtype, index), flag in list(_ERR.items()):
+        if device is not None and (dtype, index) != (device.type, device.index):
+            continue
+        code = int(flag.item())
+        if code:
+            flag.zero_()
+            raise RuntimeError(f"libra_b200 kernel reported error code {code} on {dtype}:{index}")
+
+
+# ---------------------------------------------------------------------------
+# GEMM
+# ---------------------------------------------------------------------------
+
+def gemm(a, b, *, a_mn=False, b_mn=False, out=None, epi=EPI_BF16, residual=None):
+    """C (op)= A . B^T on the tcgen05 kernel.
+
+    ``a`` is [M, K] (``a_mn=False``) or [K, M]; ``b`` is [N, K] or [K, N].
+    """
+    M = a.shape[1] if a_mn else a.shape[0]
+    N = b.shape[1] if b_mn else b.shape[0]
+    if a.device.type != "cuda":
+        A = a.float().t() if a_mn else a.float()
+        B = b.float() if b_mn else b.float().t()
+        res = A @ B
+        if epi == EPI_BF16_RESIDUAL:
+            res = res + residual.float()
+        if out is None:
+            return res.to(torch.float32 if epi in (EPI_F32, EPI_ACC_F32) else torch.bfloat16)
+        if epi == EPI_ACC_F32:
+            out.add_(res)
+        else:
+            out.copy_(res)
+        return out
+    if out is None:
+        dtype = torch.float32 if epi in (EPI_F32, EPI_ACC_F32) else torch.bfloat16
+        out = torch.empty(M, N, dtype=dtype, device=a.device)
+    ext().gemm_bf16(a, b, out, a_mn, b_mn, epi, residual, error_flag(a.device))
+    return out
+
+
+def _accumulate_wgrad(weight, dy2d, x2d):
+    """dW = dY^T X, accumulated into weight.main_grad when present."""
+    main = getattr(weight, "main_grad", None)
+    if main is not None:
+        gemm(dy2d, x2d, a_mn=True, b_mn=True, out=main, epi=EPI_ACC_F32)
+        return None
+    return gemm(dy2d, x2d, a_mn=True, b_mn=True, epi=EPI_F32).to(weight.dtype)
+
+
+class _Linear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, residual):
+        x2d = x.reshape(-1, x.shape[-1])
+        if not x2d.is_contiguous():
+            x2d = x2d.contiguous()
+        if residual is not None:
+            y = gemm(x2d, weight, epi=EPI_BF16_RESIDUAL, residual=residual.reshape(-1, weight.shape[0]))
+        else:
+            y = gemm(x2d, weight)
+        ctx.save_for_backward(x2d, weight)
+        ctx.has_residual = residual is not None
+        ctx.in_shape = x.shape
+        return y.view(*x.shape[:-1], weight.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2d, weight = ctx.saved_tensors
+        dy2d = dy.reshape(-1, weight.shape[0])
+        if not dy2d.is_contiguous():
+            dy2d = dy2d.contiguous()
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = gemm(dy2d, weight, b_mn=True).view(ctx.in_shape)
+        dw = _accumulate_wgrad(weight, dy2d, x2d) if ctx.needs_input_grad[1] else None
+        dres = dy if ctx.has_residual else None
+        return dx, dw, dres
+
+
+def linear(x, weight, residual=None):
+    """y = x W^T (+ residual), bf16 in/out, fp32 accumulation in TMEM."""
+    if x.device.type != "cuda":
+        y = torch.nn.functional.linear(x.float(), weight.float())
+        if residual is not None:
+            y = y + residual.float()
+        return y.to(x.dtype)
+    return _Linear.apply(x, weight, residual)
+
+
+# ---------------------------------------------------------------------------
+# RMSNorm
+# ---------------------------------------------------------------------------
+
+def _grad_sink(weight, grad_fp32):
+    main = getattr(weight, "main_grad", None)
+    if main is not None:
+        main.add_(grad_fp32.view_as(main))
+        return None
+    return grad_fp32.to(weight.dtype)
+
+
+class _RMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        x2d = x.reshape(-1, x.shape[-1]).contiguous()
+        y, rstd = ext().rmsnorm_fwd(x2d, w, eps)
+        ctx.save_for_backward(x2d, w, rstd)
+        ctx.shape = x.shape
+        return y.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2d, w, rstd = ctx.saved_tensors
+        main = getattr(w, "main_grad", None)
+        dw = main if main is not None else torch.zeros(w.shape, dtype=torch.float32, device=w.device)
+        dx = ext().rmsnorm_bwd(dy.reshape(x2d.shape).contiguous(), x2d, w, rstd, dw, main is not None, None)
+        return dx.view(ctx.shape), (None if main is not None else dw.to(w.dtype)), None
+
+
+def rmsnorm(x, w, eps: float = 1e-6):
+    if x.device.type != "cuda":
+        return ref.rmsnorm(x, w, eps)
+    return _RMSNorm.apply(x, w, eps)
+
+
+# ---------------------------------------------------------------------------
+# q/k RMSNorm + RoPE
+# ---------------------------------------------------------------------------
+
+class _QKNormRope(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, qw, kw, pos, cos, sin, nq, nkv, eps):
+        q, k, v, rstd = ext().qk_norm_rope_fwd(qkv, qw, kw, pos, cos, sin, nq, nkv, eps)
+        ctx.save_for_backward(qkv, qw, kw, pos, cos, sin, rstd)
+        ctx.nq, ctx.nkv = nq, nkv
+        return q, k, v
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):
+        qkv, qw, kw, pos, cos, sin, rstd = ctx.saved_tensors
+        mq, mk = getattr(qw, "main_grad", None), getattr(kw, "main_grad", None)
+        gq = mq if mq is not None else torch.zeros(qw.shape, dtype=torch.float32, device=qw.device)
+        gk = mk if mk is not None else torch.zeros(kw.shape, dtype=torch.float32, device=kw.device)
+        dqkv = ext().qk_norm_rope_bwd(qkv, qw, kw, pos, cos, sin, rstd, dq.contiguous(), dk.contiguous(),
+                                      dv.contiguous(), gq, gk, ctx.nq, ctx.nkv)
+        return (dqkv, None if mq is not None else gq.to(qw.dtype), None if mk is not None else gk.to(kw.dtype),
+                None, None, None, None, None, None)
+
+
+def qk_norm_rope(qkv, qw, kw, pos, cos, sin, nq: int, nkv: int, eps: float = 1e-6):
+    """Split the fused QKV output into q [T,nq,D], k, v [T,nkv,D] with per-head
+    RMSNorm on q/k followed by rotary embedding at positions ``pos``."""
+    if qkv.device.type != "cuda":
+        return ref.qk_norm_rope(qkv, qw, kw, pos, cos, sin, nq, nkv, eps)
+    return _QKNormRope.apply(qkv, qw, kw, pos, cos, sin, nq, nkv, eps)
+
+
+# ---------------------------------------------------------------------------
+# SwiGLU
+# ---------------------------------------------------------------------------
+
+class _SwiGLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, gu):
+        ctx.save_for_backward(gu)
+        return ext().swiglu_fwd(gu)
+
+    @staticmethod
+    def backward(ctx, dh):
+        (gu,) = ctx.saved_tensors
+        return ext().swiglu_bwd(gu, dh.contiguous())
+
+
+def swiglu(gu):
+    if gu.device.type != "cuda":
+        return ref.swiglu(gu)
+    return _SwiGLU.apply(gu.contiguous())
+
+
+# ---------------------------------------------------------------------------
+# attention
+# ---------------------------------------------------------------------------
+
+def varlen_causal_attention(q, k, v, cu_seqlens, max_seqlen: int, scale=None):
+    """Causal GQA attention over packed sequences (q [T,Hq,D], k/v [T,Hkv,D])."""
+    if q.device.type != "cuda":
+        return ref.varlen_causal_attention(q, k, v, cu_seqlens, scale)
+    from .attention import flash_varlen_causal
+
+    return flash_varlen_causal(q, k, v, cu_seqlens, max_seqlen, scale)
+
+
+# ---------------------------------------------------------------------------
+# LM head + token logprob
+# ---------------------------------------------------------------------------
+
+LOGPROB_CHUNK_ROWS = int(os.environ.get("LIBRA_LOGPROB_CHUNK_ROWS", "8192"))
+
+
+class _LMHeadLogprob(torch.autograd.Function):
+    """logp[r] = log_softmax(h[r] W^T / T)[target[r]] without an fp32 logits tensor.
+
+    Logits are produced chunk by chunk by the tcgen05 GEMM in bf16, reduced by
+    the fused logprob kernel and (when a backward is needed) kept in bf16 so the
+    backward rewrites them in place as dlogits and feeds the dgrad/wgrad GEMMs.
+    """
+
+    @staticmethod
+    def forward(ctx, h, w, targets, temperature, entropy_out):
+        C = ext()
+        R = h.shape[0]
+        logp = torch.empty(R, dtype=torch.float32, device=h.device)
+        lse = torch.empty(R, dtype=torch.float32, device=h.device)
+        keep = []
+        need_grad = ctx.needs_input_grad[0] or ctx.needs_input_grad[1]
+        for s in range(0, R, LOGPROB_CHUNK_ROWS):
+            e = min(R, s + LOGPROB_CHUNK_ROWS)
+            logits = gemm(h[s:e], w)
+            lp, ent, stats, _ = C.logprob_fwd(logits, targets[s:e], 0, temperature, entropy_out is not None)
+            logp[s:e] = lp
+            lse[s:e] = stats[:, 0] + stats[:, 1].log()
+            if entropy_out is not None:
+                entropy_out[s:e] = ent
+            if need_grad:
+                keep.append(logits)
+        ctx.save_for_backward(h, w, targets, lse)
+        ctx.logits = keep
+        ctx.temperature = temperature
+        return logp
+
+    @staticmethod
+    def backward(ctx, g):
+        h, w, targets, lse = ctx.saved_tensors
+        C = ext()
+        g = g.contiguous().float()
+        dh = torch.empty_like(h) if ctx.needs_input_grad[0] else None
+        main = getattr(w, "main_grad", None)
+        dw_local = None
+        if ctx.needs_input_grad[1] and main is None:
+            dw_local = torch.zeros(w.shape, dtype=torch.float32, device=w.device)
+        R = h.shape[0]
+        for idx, s in enumerate(range(0, R, LOGPROB_CHUNK_ROWS)):
+            e = min(R, s + LOGPROB_CHUNK_ROWS)
+            logits = ctx.logits[idx]
+            C.logprob_bwd_(logits, targets[s:e], 0, ctx.temperature, lse[s:e], g[s:e])
+            if dh is not None:
+                gemm(logits, w, b_mn=True, out=dh[s:e])
+            if ctx.needs_input_grad[1]:
+                gemm(logits, h[s:e], a_mn=True, b_mn=True, out=main if main is not None else dw_local,
+                     epi=EPI_ACC_F32)
+            ctx.logits[idx] = None
+        ctx.logits = []
+        dw = None if dw_local is None else dw_local.to(w.dtype)
+        return dh, dw, None, None, None
+
+
+def lm_head_logprob(h, w, targets, temperature: float = 1.0, entropy_out=None):
+    """Token logprobs of ``targets`` under the LM head ``w`` for hidden rows ``h``."""
+    if h.device.type != "cuda":
+        logits = torch.nn.functional.linear(h.float(), w.float())
+        lp, ent = ref.token_logprobs(logits, targets, temperature)
+        if entropy_out is not None:
+            entropy_out.copy_(ent.detach())
+        return lp
+    h = h.contiguous()
+    return _LMHeadLogprob.apply(h, w, targets.contiguous(), float(temperature), entropy_out)
+
+
+# ---------------------------------------------------------------------------
+# optimizer
+# ---------------------------------------------------------------------------
+
+def adamw_step(master, grad, exp_avg, exp_avg_sq, param_bf16, *, lr, beta1, beta2, eps, weight_decay, step,
+               max_grad_norm=0.0, sq_norm=None, grad_scale=1.0):
+    """One AdamW update over flat fp32 buffers, writing the bf16 copy too."""
+    if master.device.type != "cuda":
+        g = grad * grad_scale
+        if max_grad_norm > 0:
+            total = g.norm() if sq_norm is None else sq_norm.sqrt() * grad_scale
+            g = g * torch.clamp(max_grad_norm / (total + 1e-6), max=1.0)
+        exp_avg.mul_(beta1).add_(g, alpha=1 - beta1)
+        exp_avg_sq.mul_(beta2).addcmul_(g, g, value=1 - beta2)
+        bc1, bc2 = 1 - beta1 ** step, 1 - beta2 ** step
+        master.sub_(lr * ((exp_avg / bc1) / ((exp_avg_sq / bc2).sqrt() + eps) + weight_decay * master))
+        param_bf16.copy_(master)
+        return
+    ext().adamw_step(master, grad, exp_avg, exp_avg_sq, param_bf16, lr, beta1, beta2, eps, weight_decay, step,
+                     sq_norm, max_grad_norm, grad_scale)
+
+
+def grad_sq_norm(grad, out):
+    """out += sum(grad^2) (device scalar)."""
+    if grad.device.type != "cuda":
+        out.add_(grad.float().pow(2).sum())
+        return out
+    ext().grad_sq_norm(grad, out)
+    return out
+
+
+__all__ = [
+    "ext", "extension_available", "check_kernel_errors", "gemm", "linear", "rmsnorm", "qk_norm_rope", "swiglu",
+    "varlen_causal_attention", "lm_head_logprob", "adamw_step", "grad_sq_norm", "ref",
+]

@@ -1,0 +1,43 @@
+// Python bindings for the sm_100a kernels of libra_b200 (module libra_b200._C).
+#include <torch/extension.h>
+
+namespace libra {
+void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, bool b_mn, int64_t epi,
+               c10::optional<torch::Tensor> residual, torch::Tensor err);
+std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps);
+torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dw,
+                          bool accumulate_dw, c10::optional<torch::Tensor> dx_accum);
+std::vector<torch::Tensor> qk_norm_rope_fwd(torch::Tensor qkv, torch::Tensor qw, torch::Tensor kw, torch::Tensor pos,
+                                            torch::Tensor cos_t, torch::Tensor sin_t, int64_t nq, int64_t nkv,
+                                            double eps);
+torch::Tensor qk_norm_rope_bwd(torch::Tensor qkv, torch::Tensor qw, torch::Tensor kw, torch::Tensor pos,
+                               torch::Tensor cos_t, torch::Tensor sin_t, torch::Tensor rstd, torch::Tensor dq,
+                               torch::Tensor dk, torch::Tensor dv, torch::Tensor dqw, torch::Tensor dkw, int64_t nq,
+                               int64_t nkv);
+torch::Tensor swiglu_fwd(torch::Tensor gu);
+torch::Tensor swiglu_bwd(torch::Tensor gu, torch::Tensor dh);
+std::vector<torch::Tensor> logprob_fwd(torch::Tensor logits, torch::Tensor targets, int64_t vocab_start,
+                                       double temperature, bool with_entropy);
+void logprob_bwd_(torch::Tensor logits, torch::Tensor targets, int64_t vocab_start, double temperature,
+                  torch::Tensor lse, torch::Tensor grad);
+void grad_sq_norm(torch::Tensor grad, torch::Tensor out);
+void adamw_step(torch::Tensor master, torch::Tensor grad, torch::Tensor m, torch::Tensor v, torch::Tensor param,
+                double lr, double beta1, double beta2, double eps, double wd, int64_t step,
+                c10::optional<torch::Tensor> sq_norm, double max_norm, double grad_scale);
+}  // namespace libra
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "libra_b200 sm_100a kernels";
+  m.def("gemm_bf16", &libra::gemm_bf16, "tcgen05 bf16 GEMM", py::arg("a"), py::arg("b"), py::arg("c"),
+        py::arg("a_mn"), py::arg("b_mn"), py::arg("epi"), py::arg("residual"), py::arg("err"));
+  m.def("rmsnorm_fwd", &libra::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &libra::rmsnorm_bwd);
+  m.def("qk_norm_rope_fwd", &libra::qk_norm_rope_fwd);
+  m.def("qk_norm_rope_bwd", &libra::qk_norm_rope_bwd);
+  m.def("swiglu_fwd", &libra::swiglu_fwd);
+  m.def("swiglu_bwd", &libra::swiglu_bwd);
+  m.def("logprob_fwd", &libra::logprob_fwd);
+  m.def("logprob_bwd_", &libra::logprob_bwd_);
+  m.def("grad_sq_norm", &libra::grad_sq_norm);
+  m.def("adamw_step", &libra::adamw_step);
+}

@@ -1,0 +1,379 @@
+// Persistent warp-specialised bf16 GEMM on the 5th-generation tensor cores.
+//
+//   C[M, N] (op)= sum_k A(m, k) * B(n, k)
+//
+// A is given either K-major ([M, K] row-major) or MN-major ([K, M] row-major),
+// and likewise B ([N, K] or [K, N]).  That covers the three GEMMs of a linear
+// layer without transposing anything in memory:
+//   forward  Y  = X  W^T : A = X  (K-major), B = W (K-major)
+//   dgrad    dX = dY W   : A = dY (K-major), B = W (MN-major)
+//   wgrad    dW = dY^T X : A = dY (MN-major), B = X (MN-major)
+// which replace the cuBLAS calls the reference reaches through Megatron-Core /
+// F.linear (engine/megatron_core_train_engine.py:887-903, engine/qwen3d_modules.py:149).
+//
+// Structure (one CTA per SM, 192 threads):
+//   warp 0  TMA producer: 128B-swizzled tiles of A and B into an S-stage smem ring
+//   warp 1  TMEM owner + single-thread tcgen05.mma issuer (M=128, N=BN, K=16 per
+//           instruction); commits free smem stages and publish finished tiles
+//   warps 2-5 epilogue: tcgen05.ld the fp32 accumulator (4 warps x 32 TMEM lanes),
+//           convert and store; TMEM is double-buffered (2 x BN columns) so the
+//           epilogue of tile i overlaps the main loop of tile i+1.
+// Every wait is bounded (common.cuh); on a timeout the kernel records an error
+// code, drains its own outstanding TMA copies and MMAs, frees TMEM and returns.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace libra {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = one 128-byte swizzle row
+constexpr int kThreads = 192;
+
+enum Epilogue : int { kStoreBf16 = 0, kStoreF32 = 1, kAccumF32 = 2, kStoreBf16AddResidual = 3 };
+
+template <int BN>
+struct Cfg {
+  static constexpr int kStageA = BM * BK * 2;
+  static constexpr int kStageB = BN * BK * 2;
+  static constexpr int kStageBytes = kStageA + kStageB;
+  static constexpr int kStages = (196608 / kStageBytes) > 8 ? 8 : (196608 / kStageBytes);
+  static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
+  static constexpr int kBarBytes = 8 * (2 * kStages + 4 + 1) + 16;
+  static constexpr int kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + kBarBytes;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int num_n, int& mb, int& nb) {
+  mb = tile / num_n;
+  nb = tile - mb * num_n;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* __restrict__ C,
+                     const __nv_bfloat16* __restrict__ R, int M, int N, int K, int ldc, int ldr, int* err) {
+  using CF = Cfg<BN>;
+  constexpr int S = CF::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + S * CF::kStageA;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * CF::kStageBytes);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;   // [2]
+  uint64_t* tempty = tfull + 2;  // [2]
+  uint64_t* done = tempty + 2;   // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (M + BM - 1) / BM;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4);  // one arrive per epilogue warp
+    }
+    mbar_init(done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, CF::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_phase = 0;  // per stage: ever issued / parity of last issue
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, num_n, mb, nb);
+        const int m0 = mb * BM, n0 = nb * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, err, kTimeoutSmemEmpty)) { ok = false; break; }
+          mbar_expect_tx(&full[stage], CF::kStageBytes);
+          uint8_t* a_dst = smA + stage * CF::kStageA;
+          uint8_t* b_dst = smB + stage * CF::kStageB;
+          const int k0 = kb * BK;
+          if (A_MN) {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d(a_dst + j * 64 * BK * 2, &tmA, &full[stage], m0 + j * 64, k0);
+          } else {
+            tma_load_2d(a_dst, &tmA, &full[stage], k0, m0);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 64 * BK * 2, &tmB, &full[stage], n0 + j * 64, k0);
+          } else {
+            tma_load_2d(b_dst, &tmB, &full[stage], k0, n0);
+          }
+          issued_mask |= 1u << stage;
+          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == S) { stage = 0; phase ^= 1u; }
+        }
+      }
+      // Drain: every copy this thread started must land before the CTA exits.
+      for (int s = 0; s < S; ++s)
+        if (issued_mask & (1u << s)) mbar_wait(&full[s], (issued_phase >> s) & 1u, nullptr, 0);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, err, kTimeoutTmemEmpty)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, err, kTimeoutTmaFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smA + stage * CF::kStageA);
+          const uint32_t b_addr = smem_u32(smB + stage * CF::kStageB);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // K-major: advance 16 elements (32 B) inside the swizzle row; SBO = 8 rows x 128 B.
+            // MN-major: advance 16 K-rows (2 KB); LBO = one 64-wide MN chunk (64 rows x 128 B).
+            const uint64_t adesc = A_MN ? make_sw128_desc(a_addr + k * 2048, 64 * BK * 2, 1024)
+                                        : make_sw128_desc(a_addr + k * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? make_sw128_desc(b_addr + k * 2048, 64 * BK * 2, 1024)
+                                        : make_sw128_desc(b_addr + k * 32, 16, 1024);
+            umma_f16(d_tmem, adesc, bdesc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == S) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+      }
+      // Make sure no MMA is in flight before TMEM is released.
+      umma_commit(done);
+      mbar_wait(done, 0, nullptr, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      int mb, nb;
+      tile_coords(tile, num_n, mb, nb);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, err, kTimeoutTmemFull)) break;
+      tc_fence_after();
+      const int row = mb * BM + row_in_tile;
+      const bool row_ok = row < M;
+#pragma unroll 1
+      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + chunk * 32, r);
+        tmem_ld_wait();
+        const int col0 = nb * BN + chunk * 32;
+        if (!row_ok || col0 >= N) continue;
+        if (EPI == kStoreBf16 || EPI == kStoreBf16AddResidual) {
+          __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(C) + (size_t)row * ldc + col0;
+          const __nv_bfloat16* res = (EPI == kStoreBf16AddResidual) ? R + (size_t)row * ldr + col0 : nullptr;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (col0 + j * 8 >= N) break;
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r[j * 8 + e]);
+            if (EPI == kStoreBf16AddResidual) {
+              uint4 rv = *reinterpret_cast<const uint4*>(res + j * 8);
+              const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[e] += __bfloat162float(rb[e]);
+            }
+            uint4 pk;
+            pk.x = pack_bf16x2(v[0], v[1]);
+            pk.y = pack_bf16x2(v[2], v[3]);
+            pk.z = pack_bf16x2(v[4], v[5]);
+            pk.w = pack_bf16x2(v[6], v[7]);
+            *reinterpret_cast<uint4*>(out + j * 8) = pk;
+          }
+        } else {
+          float* out = reinterpret_cast<float*>(C) + (size_t)row * ldc + col0;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (col0 + j * 4 >= N) break;
+            float4 v = make_float4(__uint_as_float(r[j * 4]), __uint_as_float(r[j * 4 + 1]),
+                                   __uint_as_float(r[j * 4 + 2]), __uint_as_float(r[j * 4 + 3]));
+            if (EPI == kAccumF32) {
+              float4 o = *reinterpret_cast<const float4*>(out + j * 4);
+              v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+            }
+            *reinterpret_cast<float4*>(out + j * 4) = v;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, CF::kTmemCols);
+}
+
+// ------------------------------------------------------------------ host side
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p,
+                "libra_b200: cuTensorMapEncodeTiled is unavailable");
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major matrix [outer, inner] with leading
+// dimension `ld` (elements), box {box_inner, box_outer}, 128-byte swizzle.
+static CUtensorMap make_map(const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_inner, int box_outer) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "libra_b200: cuTensorMapEncodeTiled failed with code ", (int)r);
+  return m;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+static void launch(const CUtensorMap& ta, const CUtensorMap& tb, void* c, const __nv_bfloat16* r, int M, int N, int K,
+                   int ldc, int ldr, int* err, cudaStream_t st) {
+  auto kern = gemm_bf16_kernel<BN, A_MN, B_MN, EPI>;
+  constexpr int smem = Cfg<BN>::kSmemBytes;
+  static bool configured = false;  // one static per instantiation
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    configured = true;
+  }
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  kern<<<grid, kThreads, smem, st>>>(ta, tb, c, r, M, N, K, ldc, ldr, err);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+template <int BN, int EPI>
+static void dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, void* c,
+                           const __nv_bfloat16* r, int M, int N, int K, int ldc, int ldr, int* err, cudaStream_t st) {
+  if (!a_mn && !b_mn) launch<BN, false, false, EPI>(ta, tb, c, r, M, N, K, ldc, ldr, err, st);
+  else if (!a_mn && b_mn) launch<BN, false, true, EPI>(ta, tb, c, r, M, N, K, ldc, ldr, err, st);
+  else if (a_mn && b_mn) launch<BN, true, true, EPI>(ta, tb, c, r, M, N, K, ldc, ldr, err, st);
+  else launch<BN, true, false, EPI>(ta, tb, c, r, M, N, K, ldc, ldr, err, st);
+}
+
+}  // namespace gemm
+
+// Python entry: C (op)= A x B^T in the layouts described at the top of the file.
+//   a: [M, K] (a_mn=false) or [K, M] (a_mn=true), bf16, inner stride 1
+//   b: [N, K] (b_mn=false) or [K, N] (b_mn=true)
+//   c: [M, N] bf16 (epi 0/3) or fp32 (epi 1/2)
+//   residual: [M, N] bf16 for epi 3 (may be c itself)
+void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, bool b_mn, int64_t epi,
+               c10::optional<torch::Tensor> residual, torch::Tensor err) {
+  using namespace gemm;
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm_bf16: CUDA tensors required");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm_bf16: bf16 operands");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2, "gemm_bf16: 2-D tensors");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && c.stride(1) == 1, "gemm_bf16: inner stride must be 1");
+  const int64_t M = a_mn ? a.size(1) : a.size(0);
+  const int64_t K = a_mn ? a.size(0) : a.size(1);
+  const int64_t N = b_mn ? b.size(1) : b.size(0);
+  const int64_t Kb = b_mn ? b.size(0) : b.size(1);
+  TORCH_CHECK(K == Kb, "gemm_bf16: K mismatch ", K, " vs ", Kb);
+  TORCH_CHECK(c.size(0) == M && c.size(1) == N, "gemm_bf16: output shape mismatch");
+  TORCH_CHECK(N % 8 == 0 && K % 8 == 0 && (a.stride(0) % 8) == 0 && (b.stride(0) % 8) == 0 && (c.stride(0) % 8) == 0,
+              "gemm_bf16: N, K and leading dimensions must be multiples of 8 (16-byte TMA strides)");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(a.data_ptr()) & 15) == 0 && (reinterpret_cast<uintptr_t>(b.data_ptr()) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(c.data_ptr()) & 15) == 0,
+              "gemm_bf16: 16-byte aligned base pointers required");
+  const bool f32_out = (epi == kStoreF32 || epi == kAccumF32);
+  TORCH_CHECK(c.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "gemm_bf16: output dtype does not match epilogue");
+  const __nv_bfloat16* rptr = nullptr;
+  int64_t ldr = 0;
+  if (epi == kStoreBf16AddResidual) {
+    TORCH_CHECK(residual.has_value(), "gemm_bf16: residual required");
+    TORCH_CHECK(residual->scalar_type() == at::kBFloat16 && residual->stride(1) == 1 && residual->size(0) == M &&
+                    residual->size(1) == N && residual->stride(0) % 8 == 0,
+                "gemm_bf16: bad residual");
+    rptr = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+    ldr = residual->stride(0);
+  }
+  if (M == 0 || N == 0) return;
+  if (K == 0) {
+    if (epi != kAccumF32) {
+      if (epi == kStoreBf16AddResidual) c.copy_(*residual); else c.zero_();
+    }
+    return;
+  }
+  const c10::cuda::CUDAGuard guard(a.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const int BN = (N <= 128) ? 128 : 256;
+  CUtensorMap ta = a_mn ? make_map(a.data_ptr(), M, K, a.stride(0), 64, 64) : make_map(a.data_ptr(), K, M, a.stride(0), 64, BM);
+  CUtensorMap tb = b_mn ? make_map(b.data_ptr(), N, K, b.stride(0), 64, 64)
+                        : make_map(b.data_ptr(), K, N, b.stride(0), 64, BN);
+  int* errp = err.data_ptr<int>();
+  void* cp = c.data_ptr();
+  const int ldc = (int)c.stride(0);
+#define LIBRA_GEMM_EPI(E)                                                                                   \
+  if (BN == 128) dispatch_major<128, E>(a_mn, b_mn, ta, tb, cp, rptr, M, N, K, ldc, (int)ldr, errp, st); \
+  else dispatch_major<256, E>(a_mn, b_mn, ta, tb, cp, rptr, M, N, K, ldc, (int)ldr, errp, st);
+  switch (epi) {
+    case kStoreBf16: LIBRA_GEMM_EPI(kStoreBf16); break;
+    case kStoreF32: LIBRA_GEMM_EPI(kStoreF32); break;
+    case kAccumF32: LIBRA_GEMM_EPI(kAccumF32); break;
+    case kStoreBf16AddResidual: LIBRA_GEMM_EPI(kStoreBf16AddResidual); break;
+    default: TORCH_CHECK(false, "gemm_bf16: unknown epilogue ", epi);
+  }
+#undef LIBRA_GEMM_EPI
+}
+
+}  // namespace libra

@@ -1,0 +1,409 @@
+// RMSNorm (forward/backward) and the fused per-head q/k RMSNorm + rotary
+// embedding of the Qwen3 attention block (reference call sites: Megatron-Core
+// TorchSequenceParallelNorm and q/k layernorm + RoPE, engine/megatron_core_attention.py:461-489).
+//
+// Layout conventions (all row-major, bf16 activations, fp32 statistics):
+//   x       [T, H]
+//   qkv     [T, (nq + 2 nkv) * D]   (output of the fused QKV projection)
+//   cos/sin [P, D/2] fp32 tables built on the host in double precision.
+// Weight gradients are reduced in two stages: every CTA keeps fp32 partial
+// sums in registers for the columns it owns and writes one row of a
+// [grid, H] buffer; `colsum_kernel` folds those rows.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace libra {
+
+// ------------------------------------------------------------------ RMSNorm fwd
+// One warp per row; each lane walks 8-element (16-byte) vectors.
+__global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                                   __nv_bfloat16* __restrict__ y, float* __restrict__ rstd_out, int T, int H, float eps) {
+  const int warps = blockDim.x >> 5;
+  const int row = blockIdx.x * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= T) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * H);
+  const int nvec = H >> 3;
+  float ss = 0.f;
+  for (int v = lane; v < nvec; v += 32) {
+    uint4 u = xr[v];
+    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float f = __bfloat162float(b[e]);
+      ss += f * f;
+    }
+  }
+  ss = warp_sum(ss);
+  const float rstd = rsqrtf(ss / (float)H + eps);
+  if (lane == 0 && rstd_out) rstd_out[row] = rstd;
+  uint4* yr = reinterpret_cast<uint4*>(y + (size_t)row * H);
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  for (int v = lane; v < nvec; v += 32) {
+    uint4 u = xr[v], wu = wr[v];
+    const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&u);
+    const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wu);
+    float o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = __bfloat162float(b[e]) * rstd * __bfloat162float(wb[e]);
+    uint4 pk;
+    pk.x = pack_bf16x2(o[0], o[1]);
+    pk.y = pack_bf16x2(o[2], o[3]);
+    pk.z = pack_bf16x2(o[4], o[5]);
+    pk.w = pack_bf16x2(o[6], o[7]);
+    yr[v] = pk;
+  }
+}
+
+// ------------------------------------------------------------------ RMSNorm bwd
+// Block of 256 threads per row (grid-stride over rows).  Thread t owns the
+// 8-element vectors t, t+256, ... (at most kMaxVec of them, so H <= 8*256*kMaxVec).
+constexpr int kNormThreads = 256;
+constexpr int kMaxVec = 4;  // H <= 8192
+
+__device__ __forceinline__ float block_sum_256(float v, float* scratch) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) scratch[w] = v;
+  __syncthreads();
+  float r = (l < (kNormThreads >> 5)) ? scratch[l] : 0.f;
+  return warp_sum(r);
+}
+
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
+    const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+    const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx, float* __restrict__ dw_part, int T, int H,
+    int accumulate_dx) {
+  __shared__ float scratch[32];
+  const int nvec = H >> 3;
+  float dwacc[kMaxVec][8];
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) dwacc[i][e] = 0.f;
+  float wf[kMaxVec][8];
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int v = threadIdx.x + i * kNormThreads;
+    if (v < nvec) {
+      uint4 wu = reinterpret_cast<const uint4*>(w)[v];
+      const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wu);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) wf[i][e] = __bfloat162float(wb[e]);
+    }
+  }
+  for (int row = blockIdx.x; row < T; row += gridDim.x) {
+    const float r = rstd[row];
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * H);
+    const uint4* gr = reinterpret_cast<const uint4*>(dy + (size_t)row * H);
+    float xh[kMaxVec][8], g[kMaxVec][8];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxVec; ++i) {
+      const int v = threadIdx.x + i * kNormThreads;
+      if (v < nvec) {
+        uint4 xu = xr[v], gu = gr[v];
+        const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xu);
+        const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&gu);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          xh[i][e] = __bfloat162float(xb[e]) * r;
+          g[i][e] = __bfloat162float(gb[e]);
+          dot += g[i][e] * wf[i][e] * xh[i][e];
+          dwacc[i][e] += g[i][e] * xh[i][e];
+        }
+      }
+    }
+    const float mean = block_sum_256(dot, scratch) / (float)H;
+    uint4* dxr = reinterpret_cast<uint4*>(dx + (size_t)row * H);
+#pragma unroll
+    for (int i = 0; i < kMaxVec; ++i) {
+      const int v = threadIdx.x + i * kNormThreads;
+      if (v < nvec) {
+        float o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = r * (g[i][e] * wf[i][e] - xh[i][e] * mean);
+        if (accumulate_dx) {
+          uint4 prev = dxr[v];
+          const __nv_bfloat16* pb = reinterpret_cast<const __nv_bfloat16*>(&prev);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o[e] += __bfloat162float(pb[e]);
+        }
+        uint4 pk;
+        pk.x = pack_bf16x2(o[0], o[1]);
+        pk.y = pack_bf16x2(o[2], o[3]);
+        pk.z = pack_bf16x2(o[4], o[5]);
+        pk.w = pack_bf16x2(o[6], o[7]);
+        dxr[v] = pk;
+      }
+    }
+  }
+  float* part = dw_part + (size_t)blockIdx.x * H;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int v = threadIdx.x + i * kNormThreads;
+    if (v < nvec) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) part[v * 8 + e] = dwacc[i][e];
+    }
+  }
+}
+
+// out[c] (+)= sum_r part[r, c]
+__global__ void colsum_kernel(const float* __restrict__ part, int rows, int cols, float* __restrict__ out, int accumulate) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  float s = 0.f;
+  for (int r = 0; r < rows; ++r) s += part[(size_t)r * cols + c];
+  out[c] = accumulate ? out[c] + s : s;
+}
+
+// ------------------------------------------------------------------ q/k norm + RoPE
+// One warp per (token, head) of the q and k sections.  Lane l owns the element
+// pairs (2l, 2l+1) and (64+2l, 65+2l) of a 128-wide head so rotate-half stays
+// inside the thread.
+template <int D>
+__global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ qw,
+                                        const __nv_bfloat16* __restrict__ kw, const int* __restrict__ pos,
+                                        const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                        __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_out,
+                                        __nv_bfloat16* __restrict__ v_out, float* __restrict__ rstd_out, int T, int nq,
+                                        int nkv, float eps) {
+  static_assert(D == 128, "head_dim 128");
+  const int heads = nq + nkv;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int stride_row = (nq + 2 * nkv) * D;
+  if (gw < T * heads) {
+    const int t = gw / heads, h = gw - t * heads;
+    const bool is_q = h < nq;
+    const __nv_bfloat16* src = qkv + (size_t)t * stride_row + (size_t)h * D;
+    const __nv_bfloat16* wt = is_q ? qw : kw;
+    const int i0 = 2 * lane, i1 = D / 2 + 2 * lane;
+    __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(src + i0);
+    __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(src + i1);
+    float x0 = __low2float(a), x1 = __high2float(a), x2 = __low2float(b), x3 = __high2float(b);
+    float ss = warp_sum(x0 * x0 + x1 * x1 + x2 * x2 + x3 * x3);
+    const float r = rsqrtf(ss / (float)D + eps);
+    if (lane == 0) rstd_out[gw] = r;
+    __nv_bfloat162 wa = *reinterpret_cast<const __nv_bfloat162*>(wt + i0);
+    __nv_bfloat162 wb = *reinterpret_cast<const __nv_bfloat162*>(wt + i1);
+    float y0 = x0 * r * __low2float(wa), y1 = x1 * r * __high2float(wa);
+    float y2 = x2 * r * __low2float(wb), y3 = x3 * r * __high2float(wb);
+    const int p = pos[t];
+    const float c0 = cos_t[(size_t)p * (D / 2) + i0], c1 = cos_t[(size_t)p * (D / 2) + i0 + 1];
+    const float s0 = sin_t[(size_t)p * (D / 2) + i0], s1 = sin_t[(size_t)p * (D / 2) + i0 + 1];
+    // rotate_half: first half gets -second*sin, second half gets +first*sin
+    float o0 = y0 * c0 - y2 * s0, o1 = y1 * c1 - y3 * s1;
+    float o2 = y2 * c0 + y0 * s0, o3 = y3 * c1 + y1 * s1;
+    __nv_bfloat16* dst = is_q ? q_out + ((size_t)t * nq + h) * D : k_out + ((size_t)t * nkv + (h - nq)) * D;
+    *reinterpret_cast<__nv_bfloat162*>(dst + i0) = __floats2bfloat162_rn(o0, o1);
+    *reinterpret_cast<__nv_bfloat162*>(dst + i1) = __floats2bfloat162_rn(o2, o3);
+    if (!is_q) {
+      const __nv_bfloat16* vs = qkv + (size_t)t * stride_row + (size_t)(nq + nkv + (h - nq)) * D;
+      __nv_bfloat16* vd = v_out + ((size_t)t * nkv + (h - nq)) * D;
+      *reinterpret_cast<__nv_bfloat162*>(vd + i0) = *reinterpret_cast<const __nv_bfloat162*>(vs + i0);
+      *reinterpret_cast<__nv_bfloat162*>(vd + i1) = *reinterpret_cast<const __nv_bfloat162*>(vs + i1);
+    }
+  }
+}
+
+// Backward: grid-stride warps over (token, head); q/k weight-gradient partials
+// live in registers per lane (4 values for q, 4 for k) and are written per warp.
+template <int D>
+__global__ void qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ qw,
+                                        const __nv_bfloat16* __restrict__ kw, const int* __restrict__ pos,
+                                        const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                        const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ dq,
+                                        const __nv_bfloat16* __restrict__ dk, const __nv_bfloat16* __restrict__ dv,
+                                        __nv_bfloat16* __restrict__ dqkv, float* __restrict__ dw_part, int T, int nq,
+                                        int nkv) {
+  const int heads = nq + nkv;
+  const int warps_total = gridDim.x * (blockDim.x >> 5);
+  const int gw0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int stride_row = (nq + 2 * nkv) * D;
+  const int i0 = 2 * lane, i1 = D / 2 + 2 * lane;
+  float accq[4] = {0, 0, 0, 0}, acck[4] = {0, 0, 0, 0};
+  const float wq0 = __bfloat162float(qw[i0]), wq1 = __bfloat162float(qw[i0 + 1]);
+  const float wq2 = __bfloat162float(qw[i1]), wq3 = __bfloat162float(qw[i1 + 1]);
+  const float wk0 = __bfloat162float(kw[i0]), wk1 = __bfloat162float(kw[i0 + 1]);
+  const float wk2 = __bfloat162float(kw[i1]), wk3 = __bfloat162float(kw[i1 + 1]);
+  for (int gw = gw0; gw < T * heads; gw += warps_total) {
+    const int t = gw / heads, h = gw - t * heads;
+    const bool is_q = h < nq;
+    const __nv_bfloat16* g = is_q ? dq + ((size_t)t * nq + h) * D : dk + ((size_t)t * nkv + (h - nq)) * D;
+    __nv_bfloat162 ga = *reinterpret_cast<const __nv_bfloat162*>(g + i0);
+    __nv_bfloat162 gb = *reinterpret_cast<const __nv_bfloat162*>(g + i1);
+    const float g0 = __low2float(ga), g1 = __high2float(ga), g2 = __low2float(gb), g3 = __high2float(gb);
+    const int p = pos[t];
+    const float c0 = cos_t[(size_t)p * (D / 2) + i0], c1 = cos_t[(size_t)p * (D / 2) + i0 + 1];
+    const float s0 = sin_t[(size_t)p * (D / 2) + i0], s1 = sin_t[(size_t)p * (D / 2) + i0 + 1];
+    // transpose of the rotation
+    const float dy0 = g0 * c0 + g2 * s0, dy1 = g1 * c1 + g3 * s1;
+    const float dy2 = g2 * c0 - g0 * s0, dy3 = g3 * c1 - g1 * s1;
+    const __nv_bfloat16* src = qkv + (size_t)t * stride_row + (size_t)h * D;
+    __nv_bfloat162 xa = *reinterpret_cast<const __nv_bfloat162*>(src + i0);
+    __nv_bfloat162 xb = *reinterpret_cast<const __nv_bfloat162*>(src + i1);
+    const float r = rstd[gw];
+    const float xh0 = __low2float(xa) * r, xh1 = __high2float(xa) * r, xh2 = __low2float(xb) * r,
+                xh3 = __high2float(xb) * r;
+    const float w0 = is_q ? wq0 : wk0, w1 = is_q ? wq1 : wk1, w2 = is_q ? wq2 : wk2, w3 = is_q ? wq3 : wk3;
+    const float dot = warp_sum(dy0 * w0 * xh0 + dy1 * w1 * xh1 + dy2 * w2 * xh2 + dy3 * w3 * xh3) / (float)D;
+    const float dx0 = r * (dy0 * w0 - xh0 * dot), dx1 = r * (dy1 * w1 - xh1 * dot);
+    const float dx2 = r * (dy2 * w2 - xh2 * dot), dx3 = r * (dy3 * w3 - xh3 * dot);
+    if (is_q) {
+      accq[0] += dy0 * xh0; accq[1] += dy1 * xh1; accq[2] += dy2 * xh2; accq[3] += dy3 * xh3;
+    } else {
+      acck[0] += dy0 * xh0; acck[1] += dy1 * xh1; acck[2] += dy2 * xh2; acck[3] += dy3 * xh3;
+    }
+    __nv_bfloat16* dst = dqkv + (size_t)t * stride_row + (size_t)h * D;
+    *reinterpret_cast<__nv_bfloat162*>(dst + i0) = __floats2bfloat162_rn(dx0, dx1);
+    *reinterpret_cast<__nv_bfloat162*>(dst + i1) = __floats2bfloat162_rn(dx2, dx3);
+    if (!is_q) {
+      const __nv_bfloat16* vg = dv + ((size_t)t * nkv + (h - nq)) * D;
+      __nv_bfloat16* vd = dqkv + (size_t)t * stride_row + (size_t)(nq + nkv + (h - nq)) * D;
+      *reinterpret_cast<__nv_bfloat162*>(vd + i0) = *reinterpret_cast<const __nv_bfloat162*>(vg + i0);
+      *reinterpret_cast<__nv_bfloat162*>(vd + i1) = *reinterpret_cast<const __nv_bfloat162*>(vg + i1);
+    }
+  }
+  // partial row layout: [q weights (D) | k weights (D)]
+  float* part = dw_part + (size_t)gw0 * 2 * D;
+  part[i0] = accq[0]; part[i0 + 1] = accq[1]; part[i1] = accq[2]; part[i1 + 1] = accq[3];
+  part[D + i0] = acck[0]; part[D + i0 + 1] = acck[1]; part[D + i1] = acck[2]; part[D + i1 + 1] = acck[3];
+}
+
+// ------------------------------------------------------------------ host wrappers
+static void check_bf16_rowmajor(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous(), name,
+              ": contiguous CUDA bf16 tensor required");
+}
+
+std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps) {
+  check_bf16_rowmajor(x, "rmsnorm_fwd x");
+  check_bf16_rowmajor(w, "rmsnorm_fwd w");
+  const int H = (int)x.size(-1);
+  const int T = (int)(x.numel() / H);
+  TORCH_CHECK(H % 8 == 0 && w.numel() == H, "rmsnorm_fwd: H must be a multiple of 8 and match w");
+  const c10::cuda::CUDAGuard guard(x.device());
+  auto y = torch::empty_like(x);
+  auto rstd = torch::empty({T}, x.options().dtype(at::kFloat));
+  if (T == 0) return {y, rstd};
+  const int warps = 8;
+  rmsnorm_fwd_kernel<<<(T + warps - 1) / warps, warps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)y.data_ptr(),
+      rstd.data_ptr<float>(), T, H, (float)eps);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {y, rstd};
+}
+
+static int norm_grid(int T) {
+  int dev, sms;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int g = sms * 4;
+  return T < g ? (T > 0 ? T : 1) : g;
+}
+
+// Returns dx (bf16).  dw (fp32, [H]) is written or accumulated in place.
+torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dw,
+                          bool accumulate_dw, c10::optional<torch::Tensor> dx_accum) {
+  check_bf16_rowmajor(dy, "rmsnorm_bwd dy");
+  check_bf16_rowmajor(x, "rmsnorm_bwd x");
+  const int H = (int)x.size(-1);
+  const int T = (int)(x.numel() / H);
+  TORCH_CHECK(H % 8 == 0 && H <= 8 * kNormThreads * kMaxVec, "rmsnorm_bwd: unsupported H");
+  TORCH_CHECK(dw.scalar_type() == at::kFloat && dw.numel() == H && dw.is_contiguous(), "rmsnorm_bwd: dw fp32 [H]");
+  const c10::cuda::CUDAGuard guard(x.device());
+  torch::Tensor dx;
+  int acc_dx = 0;
+  if (dx_accum.has_value()) {
+    dx = *dx_accum;
+    check_bf16_rowmajor(dx, "rmsnorm_bwd dx_accum");
+    acc_dx = 1;
+  } else {
+    dx = torch::empty_like(x);
+  }
+  const int grid = norm_grid(T);
+  auto part = torch::empty({grid, H}, x.options().dtype(at::kFloat));
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (T > 0) {
+    rmsnorm_bwd_kernel<<<grid, kNormThreads, 0, st>>>(
+        (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(),
+        rstd.data_ptr<float>(), (__nv_bfloat16*)dx.data_ptr(), part.data_ptr<float>(), T, H, acc_dx);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  } else {
+    part.zero_();
+  }
+  colsum_kernel<<<(H + 255) / 256, 256, 0, st>>>(part.data_ptr<float>(), grid, H, dw.data_ptr<float>(),
+                                                 accumulate_dw ? 1 : 0);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return dx;
+}
+
+std::vector<torch::Tensor> qk_norm_rope_fwd(torch::Tensor qkv, torch::Tensor qw, torch::Tensor kw, torch::Tensor pos,
+                                            torch::Tensor cos_t, torch::Tensor sin_t, int64_t nq, int64_t nkv,
+                                            double eps) {
+  check_bf16_rowmajor(qkv, "qk_norm_rope qkv");
+  const int D = 128;
+  TORCH_CHECK(qkv.size(-1) == (nq + 2 * nkv) * D, "qk_norm_rope: qkv width mismatch (head_dim must be 128)");
+  TORCH_CHECK(pos.scalar_type() == at::kInt && cos_t.scalar_type() == at::kFloat, "qk_norm_rope: int32 pos, fp32 tables");
+  const int T = (int)(qkv.numel() / qkv.size(-1));
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  auto q = torch::empty({T, nq, D}, qkv.options());
+  auto k = torch::empty({T, nkv, D}, qkv.options());
+  auto v = torch::empty({T, nkv, D}, qkv.options());
+  auto rstd = torch::empty({T * (nq + nkv)}, qkv.options().dtype(at::kFloat));
+  const int total = T * (int)(nq + nkv);
+  if (total == 0) return {q, k, v, rstd};
+  const int warps = 8;
+  qk_norm_rope_fwd_kernel<128><<<(total + warps - 1) / warps, warps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      (const __nv_bfloat16*)qkv.data_ptr(), (const __nv_bfloat16*)qw.data_ptr(), (const __nv_bfloat16*)kw.data_ptr(),
+      pos.data_ptr<int>(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), (__nv_bfloat16*)q.data_ptr(),
+      (__nv_bfloat16*)k.data_ptr(), (__nv_bfloat16*)v.data_ptr(), rstd.data_ptr<float>(), T, (int)nq, (int)nkv,
+      (float)eps);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {q, k, v, rstd};
+}
+
+// Returns dqkv; dqw/dkw (fp32 [128]) are accumulated in place.
+torch::Tensor qk_norm_rope_bwd(torch::Tensor qkv, torch::Tensor qw, torch::Tensor kw, torch::Tensor pos,
+                               torch::Tensor cos_t, torch::Tensor sin_t, torch::Tensor rstd, torch::Tensor dq,
+                               torch::Tensor dk, torch::Tensor dv, torch::Tensor dqw, torch::Tensor dkw, int64_t nq,
+                               int64_t nkv) {
+  const int D = 128;
+  const int T = (int)(qkv.numel() / qkv.size(-1));
+  TORCH_CHECK(dq.is_contiguous() && dk.is_contiguous() && dv.is_contiguous(), "qk_norm_rope_bwd: contiguous grads");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  auto dqkv = torch::empty_like(qkv);
+  const int warps = 8;
+  int dev, sms;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int total = T * (int)(nq + nkv);
+  int blocks = sms * 8;
+  if (blocks * warps > total) blocks = (total + warps - 1) / warps;
+  if (blocks < 1) blocks = 1;
+  auto part = torch::zeros({blocks * warps, 2 * D}, qkv.options().dtype(at::kFloat));
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (total > 0) {
+    qk_norm_rope_bwd_kernel<128><<<blocks, warps * 32, 0, st>>>(
+        (const __nv_bfloat16*)qkv.data_ptr(), (const __nv_bfloat16*)qw.data_ptr(), (const __nv_bfloat16*)kw.data_ptr(),
+        pos.data_ptr<int>(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), rstd.data_ptr<float>(),
+        (const __nv_bfloat16*)dq.data_ptr(), (const __nv_bfloat16*)dk.data_ptr(), (const __nv_bfloat16*)dv.data_ptr(),
+        (__nv_bfloat16*)dqkv.data_ptr(), part.data_ptr<float>(), T, (int)nq, (int)nkv);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  auto sums = torch::empty({2 * D}, qkv.options().dtype(at::kFloat));
+  colsum_kernel<<<1, 256, 0, st>>>(part.data_ptr<float>(), blocks * warps, 2 * D, sums.data_ptr<float>(), 0);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  dqw.add_(sums.narrow(0, 0, D));
+  dkw.add_(sums.narrow(0, D, D));
+  return dqkv;
+}
+
+}  // namespace libra

@@ -1,0 +1,68 @@
+import os
+
+import pytest
+
+from libra_b200.config import AsyncRLConfig, compose_config_dict, load_config, merge_dicts
+
+CFG_DIR = os.path.join(os.path.dirname(os.path.dirname(__file__)), "libra_b200", "configs")
+
+
+def test_presets_load(tmp_path):
+    cfg = AsyncRLConfig.from_file(os.path.join(CFG_DIR, "qwen3_4b_grpo_8xb200.yaml"))
+    assert cfg.train_tp_size == 2 and cfg.train_dp_size == 2
+    assert cfg.hardware.flops_peak == pytest.approx(1.622e15)
+    assert cfg.model_arch.d_model == 2560 and cfg.model_arch.head_dim == 128
+    assert cfg.heterogeneous_rollout.tp_list == [1, 1, 2]
+    assert cfg.heterogeneous_rollout.instances[2].instance_id == "hetero_tp2_2"
+    assert cfg.heterogeneous_rollout.scheduling.scheduler_type == "cmlfq"
+    tiny = AsyncRLConfig.from_file(os.path.join(CFG_DIR, "tiny_cpu_gloo.yaml"))
+    assert tiny.train_dp_size == 2 and tiny.n_total_gpus == 3
+
+
+def test_numeric_string_coercion():
+    cfg = AsyncRLConfig.from_dict({"model_path": "x", "learning_rate": "1e-6", "batch_size": "32",
+                                   "hardware": {"flops_peak": "2.25e15", "gpus_per_node": "8"}})
+    assert cfg.learning_rate == 1e-6 and cfg.batch_size == 32
+    assert isinstance(cfg.hardware.gpus_per_node, int)
+
+
+@pytest.mark.parametrize("kw,msg", [
+    ({"train_gpus": 3, "train_tp_size": 2}, "divisible"),
+    ({"batch_size": 30}, "batch_size must be divisible"),
+    ({"weight_sync_mode": "foo"}, "weight_sync_mode"),
+    ({"rollout_weight_sync_mode": "nccl"}, "requires weight_sync_mode"),
+    ({"train_pp_size": 2}, "train_pp_size=1"),
+    ({"train_cp_size": 2, "train_gpus": 8}, "train_cp_size=1"),
+    ({"train_backend": "deepspeed"}, "train_backend"),
+    ({"megatron_optimizer_offload_fraction": 0.5}, "cpu_offload"),
+])
+def test_validation_errors(kw, msg, tmp_path):
+    base = {"model_path": "m", "sync_path": str(tmp_path / "s"), "log_dir": str(tmp_path / "l")}
+    with pytest.raises(ValueError, match=msg):
+        AsyncRLConfig.from_dict({**base, **kw})
+
+
+def test_composition_order(tmp_path):
+    (tmp_path / "hw.yaml").write_text("flops_peak: 1.0\nmem_bw: 2.0\n")
+    (tmp_path / "base.yaml").write_text("model_path: a\nbatch_size: 8\nmicro_batch_size: 1\nhardware: {mem_bw: 5.0}\n")
+    (tmp_path / "exp.yaml").write_text("base_config: base.yaml\nhardware_config: hw.yaml\nbatch_size: 16\n"
+                                       f"sync_path: {tmp_path}/s\nlog_dir: {tmp_path}/l\n")
+    cfg = load_config(str(tmp_path / "exp.yaml"))
+    assert cfg.batch_size == 16 and cfg.hardware.flops_peak == 1.0 and cfg.hardware.mem_bw == 2.0
+    (tmp_path / "cyc.yaml").write_text("base_config: cyc.yaml\n")
+    with pytest.raises(ValueError, match="cyclic"):
+        load_config(str(tmp_path / "cyc.yaml"))
+
+
+def test_merge_and_roundtrip(tmp_path):
+    assert merge_dicts({"a": {"b": 1, "c": 2}}, {"a": {"c": 3}}) == {"a": {"b": 1, "c": 3}}
+    cfg = AsyncRLConfig.from_dict({"model_path": "m", "sync_path": str(tmp_path / "s"), "log_dir": str(tmp_path / "l")})
+    cfg.to_yaml(str(tmp_path / "o.yaml"))
+    again = AsyncRLConfig.from_file(str(tmp_path / "o.yaml"))
+    assert again.to_dict() == cfg.to_dict()
+
+
+def test_load_config_requires_path(monkeypatch):
+    monkeypatch.delenv("ASYNC_RL_CONFIG", raising=False)
+    with pytest.raises(ValueError, match="No configuration file"):
+        load_config(None)

@@ -26,6 +26,9 @@
 
 #include "common.cuh"
 
+#include <cstdio>
+#include <cstdlib>
+
 namespace libra {
 namespace gemm {
 
@@ -330,8 +333,13 @@ void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, boo
   const int64_t Kb = b_mn ? b.size(0) : b.size(1);
   TORCH_CHECK(K == Kb, "gemm_bf16: K mismatch ", K, " vs ", Kb);
   TORCH_CHECK(c.size(0) == M && c.size(1) == N, "gemm_bf16: output shape mismatch");
-  TORCH_CHECK(N % 8 == 0 && K % 8 == 0 && (a.stride(0) % 8) == 0 && (b.stride(0) % 8) == 0 && (c.stride(0) % 8) == 0,
-              "gemm_bf16: N, K and leading dimensions must be multiples of 8 (16-byte TMA strides)");
+  // TMA needs 16-byte strides (leading dims % 8); the epilogue stores 16-byte
+  // vectors (N % 8).  K and M may be anything: out-of-range rows/columns of a
+  // box are zero-filled and the K loop steps in aligned 64-element blocks.
+  TORCH_CHECK(N % 8 == 0 && (a.stride(0) % 8) == 0 && (b.stride(0) % 8) == 0 && (c.stride(0) % 8) == 0,
+              "gemm_bf16: N and every leading dimension must be multiples of 8 (16-byte TMA strides); got N=", N,
+              " lda=", a.stride(0), " ldb=", b.stride(0), " ldc=", c.stride(0));
+  TORCH_CHECK(a.size(1) >= 1 && b.size(1) >= 1, "gemm_bf16: empty inner dimension");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(a.data_ptr()) & 15) == 0 && (reinterpret_cast<uintptr_t>(b.data_ptr()) & 15) == 0 &&
                   (reinterpret_cast<uintptr_t>(c.data_ptr()) & 15) == 0,
               "gemm_bf16: 16-byte aligned base pointers required");
@@ -354,12 +362,19 @@ void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, boo
     }
     return;
   }
+  static const bool trace = std::getenv("LIBRA_GEMM_TRACE") != nullptr;
+  if (trace)
+    fprintf(stderr, "[gemm] M=%ld N=%ld K=%ld a_mn=%d b_mn=%d epi=%ld lda=%ld ldb=%ld ldc=%ld a=%p b=%p c=%p\n",
+            (long)M, (long)N, (long)K, (int)a_mn, (int)b_mn, (long)epi, (long)a.stride(0), (long)b.stride(0),
+            (long)c.stride(0), a.data_ptr(), b.data_ptr(), c.data_ptr());
   const c10::cuda::CUDAGuard guard(a.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (trace) fprintf(stderr, "[gemm] stream=%p\n", (void*)st);
   const int BN = (N <= 128) ? 128 : 256;
   CUtensorMap ta = a_mn ? make_map(a.data_ptr(), M, K, a.stride(0), 64, 64) : make_map(a.data_ptr(), K, M, a.stride(0), 64, BM);
   CUtensorMap tb = b_mn ? make_map(b.data_ptr(), N, K, b.stride(0), 64, 64)
                         : make_map(b.data_ptr(), K, N, b.stride(0), 64, BN);
+  if (trace) fprintf(stderr, "[gemm] tensor maps encoded\n");
   int* errp = err.data_ptr<int>();
   void* cp = c.data_ptr();
   const int ldc = (int)c.stride(0);
@@ -374,6 +389,7 @@ void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, boo
     default: TORCH_CHECK(false, "gemm_bf16: unknown epilogue ", epi);
   }
 #undef LIBRA_GEMM_EPI
+  if (trace) fprintf(stderr, "[gemm] launched\n");
 }
 
 }  // namespace libra

@@ -22,7 +22,7 @@ def _rel(a, b):
 
 # ---------------------------------------------------------------- GEMM
 GEMM_SHAPES = [(128, 128, 64), (300, 264, 200), (1000, 520, 136), (4096, 4096, 2560), (129, 2048, 4096),
-               (2056, 256, 8)]
+               (2056, 256, 8), (200, 136, 777)]
 
 
 @pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
@@ -30,6 +30,8 @@ GEMM_SHAPES = [(128, 128, 64), (300, 264, 200), (1000, 520, 136), (4096, 4096, 2
 def test_gemm_layouts(M, N, K, a_mn, b_mn):
     from libra_b200 import ops
 
+    if (a_mn and M % 8) or (b_mn and N % 8):
+        pytest.skip("MN-major operand needs its leading dimension to be a multiple of 8")
     A = _bf16(M, K, seed=1)  # logical [M, K]
     B = _bf16(N, K, seed=2)  # logical [N, K]
     a = A.t().contiguous() if a_mn else A

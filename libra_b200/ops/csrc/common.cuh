@@ -10,6 +10,29 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdio>
+#include <stdexcept>
+
+// Argument checks for the host wrappers.  The message is formatted with
+// snprintf and raised as std::runtime_error (RuntimeError in Python):
+// c10-formatted error messages with numeric arguments crash the process in
+// this toolchain combination, so they are not used anywhere in the extension.
+#define LIBRA_CHECK(cond, ...)                                       \
+  do {                                                               \
+    if (!(cond)) {                                                   \
+      char libra_msg_[768];                                          \
+      std::snprintf(libra_msg_, sizeof(libra_msg_), __VA_ARGS__);    \
+      throw std::runtime_error(libra_msg_);                          \
+    }                                                                \
+  } while (0)
+
+#define LIBRA_LAUNCH_CHECK()                                                             \
+  do {                                                                                   \
+    cudaError_t libra_e_ = cudaGetLastError();                                           \
+    LIBRA_CHECK(libra_e_ == cudaSuccess, "libra_b200: kernel launch failed: %s (%s:%d)", \
+                cudaGetErrorString(libra_e_), __FILE__, __LINE__);                       \
+  } while (0)
+
 #ifndef LIBRA_WAIT_NS
 #define LIBRA_WAIT_NS 2000000000ull  // 2 s
 #endif

@@ -276,9 +276,9 @@ static int sm_count() {
 }
 
 torch::Tensor swiglu_fwd(torch::Tensor gu) {
-  TORCH_CHECK(gu.is_cuda() && gu.scalar_type() == at::kBFloat16 && gu.is_contiguous(), "swiglu_fwd: bf16 contiguous");
+  LIBRA_CHECK(gu.is_cuda() && gu.scalar_type() == at::kBFloat16 && gu.is_contiguous(), "swiglu_fwd: bf16 contiguous");
   const int F = (int)(gu.size(-1) / 2);
-  TORCH_CHECK(F % 8 == 0, "swiglu_fwd: F % 8");
+  LIBRA_CHECK(F % 8 == 0, "swiglu_fwd: F % 8");
   const int64_t T = gu.numel() / (2 * F);
   const c10::cuda::CUDAGuard guard(gu.device());
   auto sizes = gu.sizes().vec();
@@ -287,12 +287,12 @@ torch::Tensor swiglu_fwd(torch::Tensor gu) {
   if (T == 0) return h;
   swiglu_fwd_kernel<<<sm_count() * 8, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       (const __nv_bfloat16*)gu.data_ptr(), (__nv_bfloat16*)h.data_ptr(), T, F);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  LIBRA_LAUNCH_CHECK();
   return h;
 }
 
 torch::Tensor swiglu_bwd(torch::Tensor gu, torch::Tensor dh) {
-  TORCH_CHECK(dh.is_contiguous() && gu.is_contiguous(), "swiglu_bwd: contiguous inputs");
+  LIBRA_CHECK(dh.is_contiguous() && gu.is_contiguous(), "swiglu_bwd: contiguous inputs");
   const int F = (int)(gu.size(-1) / 2);
   const int64_t T = gu.numel() / (2 * F);
   const c10::cuda::CUDAGuard guard(gu.device());
@@ -300,16 +300,16 @@ torch::Tensor swiglu_bwd(torch::Tensor gu, torch::Tensor dh) {
   if (T == 0) return dgu;
   swiglu_bwd_kernel<<<sm_count() * 8, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       (const __nv_bfloat16*)gu.data_ptr(), (const __nv_bfloat16*)dh.data_ptr(), (__nv_bfloat16*)dgu.data_ptr(), T, F);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  LIBRA_LAUNCH_CHECK();
   return dgu;
 }
 
 // Returns {logp [R], entropy [R], stats [R, 2] (max, sumexp), target_logit [R]}.
 std::vector<torch::Tensor> logprob_fwd(torch::Tensor logits, torch::Tensor targets, int64_t vocab_start,
                                        double temperature, bool with_entropy) {
-  TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == at::kBFloat16 && logits.dim() == 2 && logits.stride(1) == 1,
+  LIBRA_CHECK(logits.is_cuda() && logits.scalar_type() == at::kBFloat16 && logits.dim() == 2 && logits.stride(1) == 1,
               "logprob_fwd: 2-D bf16 logits");
-  TORCH_CHECK(logits.stride(0) % 8 == 0 && targets.scalar_type() == at::kLong, "logprob_fwd: ld % 8, int64 targets");
+  LIBRA_CHECK(logits.stride(0) % 8 == 0 && targets.scalar_type() == at::kLong, "logprob_fwd: ld % 8, int64 targets");
   const int R = (int)logits.size(0), V = (int)logits.size(1);
   const c10::cuda::CUDAGuard guard(logits.device());
   auto opts = logits.options().dtype(at::kFloat);
@@ -322,43 +322,43 @@ std::vector<torch::Tensor> logprob_fwd(torch::Tensor logits, torch::Tensor targe
       (const __nv_bfloat16*)logits.data_ptr(), logits.stride(0), targets.data_ptr<int64_t>(), V, (int)vocab_start,
       (float)(1.0 / temperature), logp.data_ptr<float>(), with_entropy ? ent.data_ptr<float>() : nullptr,
       stats.data_ptr<float>(), tl.data_ptr<float>());
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  LIBRA_LAUNCH_CHECK();
   return {logp, ent, stats, tl};
 }
 
 void logprob_bwd_(torch::Tensor logits, torch::Tensor targets, int64_t vocab_start, double temperature,
                   torch::Tensor lse, torch::Tensor grad) {
   const int R = (int)logits.size(0), V = (int)logits.size(1);
-  TORCH_CHECK(lse.is_contiguous() && grad.is_contiguous() && lse.numel() == R && grad.numel() == R,
+  LIBRA_CHECK(lse.is_contiguous() && grad.is_contiguous() && lse.numel() == R && grad.numel() == R,
               "logprob_bwd: lse/grad [R] fp32");
   const c10::cuda::CUDAGuard guard(logits.device());
   if (R == 0) return;
   logprob_bwd_kernel<<<R, kLpThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
       (__nv_bfloat16*)logits.data_ptr(), logits.stride(0), targets.data_ptr<int64_t>(), V, (int)vocab_start,
       (float)(1.0 / temperature), lse.data_ptr<float>(), grad.data_ptr<float>());
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  LIBRA_LAUNCH_CHECK();
 }
 
 void grad_sq_norm(torch::Tensor grad, torch::Tensor out) {
-  TORCH_CHECK(grad.scalar_type() == at::kFloat && grad.is_contiguous() && out.scalar_type() == at::kFloat,
+  LIBRA_CHECK(grad.scalar_type() == at::kFloat && grad.is_contiguous() && out.scalar_type() == at::kFloat,
               "grad_sq_norm: fp32");
   const c10::cuda::CUDAGuard guard(grad.device());
   const int64_t n = grad.numel();
   if (n == 0) return;
   grad_sq_norm_kernel<<<sm_count() * 4, 512, 0, at::cuda::getCurrentCUDAStream()>>>(grad.data_ptr<float>(), n,
                                                                                     out.data_ptr<float>());
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  LIBRA_LAUNCH_CHECK();
 }
 
 void adamw_step(torch::Tensor master, torch::Tensor grad, torch::Tensor m, torch::Tensor v, torch::Tensor param,
                 double lr, double beta1, double beta2, double eps, double wd, int64_t step,
                 c10::optional<torch::Tensor> sq_norm, double max_norm, double grad_scale) {
-  TORCH_CHECK(master.scalar_type() == at::kFloat && grad.scalar_type() == at::kFloat && m.scalar_type() == at::kFloat &&
+  LIBRA_CHECK(master.scalar_type() == at::kFloat && grad.scalar_type() == at::kFloat && m.scalar_type() == at::kFloat &&
                   v.scalar_type() == at::kFloat && param.scalar_type() == at::kBFloat16,
               "adamw_step: fp32 master/grad/m/v and bf16 param");
   const int64_t n = master.numel();
-  TORCH_CHECK(grad.numel() == n && m.numel() == n && v.numel() == n && param.numel() == n, "adamw_step: size mismatch");
-  TORCH_CHECK(master.is_contiguous() && grad.is_contiguous() && m.is_contiguous() && v.is_contiguous() &&
+  LIBRA_CHECK(grad.numel() == n && m.numel() == n && v.numel() == n && param.numel() == n, "adamw_step: size mismatch");
+  LIBRA_CHECK(master.is_contiguous() && grad.is_contiguous() && m.is_contiguous() && v.is_contiguous() &&
                   param.is_contiguous(),
               "adamw_step: contiguous buffers");
   const c10::cuda::CUDAGuard guard(master.device());
@@ -369,7 +369,7 @@ void adamw_step(torch::Tensor master, torch::Tensor grad, torch::Tensor m, torch
       master.data_ptr<float>(), grad.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
       (__nv_bfloat16*)param.data_ptr(), n, (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd, bc1, bc2,
       sq_norm.has_value() ? sq_norm->data_ptr<float>() : nullptr, (float)max_norm, (float)grad_scale);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  LIBRA_LAUNCH_CHECK();
 }
 
 }  // namespace libra

@@ -28,6 +28,8 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
+#include <vector>
 
 namespace libra {
 namespace gemm {
@@ -256,7 +258,7 @@ static EncodeTiledFn encode_fn() {
     cudaDriverEntryPointQueryResult q;
     void* p = nullptr;
     cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
-    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p,
+    LIBRA_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p,
                 "libra_b200: cuTensorMapEncodeTiled is unavailable");
     fn = reinterpret_cast<EncodeTiledFn>(p);
   }
@@ -274,7 +276,7 @@ static CUtensorMap make_map(const void* ptr, int64_t inner, int64_t outer, int64
   CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "libra_b200: cuTensorMapEncodeTiled failed with code ", (int)r);
+  LIBRA_CHECK(r == CUDA_SUCCESS, "libra_b200: cuTensorMapEncodeTiled failed with code %d", (int)r);
   return m;
 }
 
@@ -301,7 +303,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, void* c, const 
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
   kern<<<grid, kThreads, smem, st>>>(ta, tb, c, r, M, N, K, ldc, ldr, err);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  LIBRA_LAUNCH_CHECK();
 }
 
 template <int BN, int EPI>
@@ -323,33 +325,34 @@ static void dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CU
 void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, bool b_mn, int64_t epi,
                c10::optional<torch::Tensor> residual, torch::Tensor err) {
   using namespace gemm;
-  TORCH_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm_bf16: CUDA tensors required");
-  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm_bf16: bf16 operands");
-  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2, "gemm_bf16: 2-D tensors");
-  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && c.stride(1) == 1, "gemm_bf16: inner stride must be 1");
+  LIBRA_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm_bf16: CUDA tensors required");
+  LIBRA_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm_bf16: bf16 operands");
+  LIBRA_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2, "gemm_bf16: 2-D tensors");
+  LIBRA_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && c.stride(1) == 1, "gemm_bf16: inner stride must be 1");
   const int64_t M = a_mn ? a.size(1) : a.size(0);
   const int64_t K = a_mn ? a.size(0) : a.size(1);
   const int64_t N = b_mn ? b.size(1) : b.size(0);
   const int64_t Kb = b_mn ? b.size(0) : b.size(1);
-  TORCH_CHECK(K == Kb, "gemm_bf16: K mismatch ", K, " vs ", Kb);
-  TORCH_CHECK(c.size(0) == M && c.size(1) == N, "gemm_bf16: output shape mismatch");
+  LIBRA_CHECK(K == Kb, "gemm_bf16: K mismatch %lld vs %lld", (long long)K, (long long)Kb);
+  LIBRA_CHECK(c.size(0) == M && c.size(1) == N, "gemm_bf16: output shape mismatch");
   // TMA needs 16-byte strides (leading dims % 8); the epilogue stores 16-byte
   // vectors (N % 8).  K and M may be anything: out-of-range rows/columns of a
   // box are zero-filled and the K loop steps in aligned 64-element blocks.
-  TORCH_CHECK(N % 8 == 0 && (a.stride(0) % 8) == 0 && (b.stride(0) % 8) == 0 && (c.stride(0) % 8) == 0,
-              "gemm_bf16: N and every leading dimension must be multiples of 8 (16-byte TMA strides); got N=", N,
-              " lda=", a.stride(0), " ldb=", b.stride(0), " ldc=", c.stride(0));
-  TORCH_CHECK(a.size(1) >= 1 && b.size(1) >= 1, "gemm_bf16: empty inner dimension");
-  TORCH_CHECK((reinterpret_cast<uintptr_t>(a.data_ptr()) & 15) == 0 && (reinterpret_cast<uintptr_t>(b.data_ptr()) & 15) == 0 &&
+  LIBRA_CHECK(N % 8 == 0 && (a.stride(0) % 8) == 0 && (b.stride(0) % 8) == 0 && (c.stride(0) % 8) == 0,
+              "gemm_bf16: N and every leading dimension must be multiples of 8 (16-byte TMA strides); "
+              "got N=%lld lda=%lld ldb=%lld ldc=%lld", (long long)N, (long long)a.stride(0), (long long)b.stride(0),
+              (long long)c.stride(0));
+  LIBRA_CHECK(a.size(1) >= 1 && b.size(1) >= 1, "gemm_bf16: empty inner dimension");
+  LIBRA_CHECK((reinterpret_cast<uintptr_t>(a.data_ptr()) & 15) == 0 && (reinterpret_cast<uintptr_t>(b.data_ptr()) & 15) == 0 &&
                   (reinterpret_cast<uintptr_t>(c.data_ptr()) & 15) == 0,
               "gemm_bf16: 16-byte aligned base pointers required");
   const bool f32_out = (epi == kStoreF32 || epi == kAccumF32);
-  TORCH_CHECK(c.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "gemm_bf16: output dtype does not match epilogue");
+  LIBRA_CHECK(c.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "gemm_bf16: output dtype does not match epilogue");
   const __nv_bfloat16* rptr = nullptr;
   int64_t ldr = 0;
   if (epi == kStoreBf16AddResidual) {
-    TORCH_CHECK(residual.has_value(), "gemm_bf16: residual required");
-    TORCH_CHECK(residual->scalar_type() == at::kBFloat16 && residual->stride(1) == 1 && residual->size(0) == M &&
+    LIBRA_CHECK(residual.has_value(), "gemm_bf16: residual required");
+    LIBRA_CHECK(residual->scalar_type() == at::kBFloat16 && residual->stride(1) == 1 && residual->size(0) == M &&
                     residual->size(1) == N && residual->stride(0) % 8 == 0,
                 "gemm_bf16: bad residual");
     rptr = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
@@ -386,7 +389,7 @@ void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, boo
     case kStoreF32: LIBRA_GEMM_EPI(kStoreF32); break;
     case kAccumF32: LIBRA_GEMM_EPI(kAccumF32); break;
     case kStoreBf16AddResidual: LIBRA_GEMM_EPI(kStoreBf16AddResidual); break;
-    default: TORCH_CHECK(false, "gemm_bf16: unknown epilogue ", epi);
+    default: LIBRA_CHECK(false, "gemm_bf16: unknown epilogue %lld", (long long)epi);
   }
 #undef LIBRA_GEMM_EPI
   if (trace) fprintf(stderr, "[gemm] launched\n");

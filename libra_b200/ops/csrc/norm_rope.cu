@@ -279,8 +279,8 @@ __global__ void qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ qkv, c
 
 // ------------------------------------------------------------------ host wrappers
 static void check_bf16_rowmajor(const torch::Tensor& t, const char* name) {
-  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous(), name,
-              ": contiguous CUDA bf16 tensor required");
+  LIBRA_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous(),
+              "%s: contiguous CUDA bf16 tensor required", name);
 }
 
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps) {
@@ -288,7 +288,7 @@ std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double 
   check_bf16_rowmajor(w, "rmsnorm_fwd w");
   const int H = (int)x.size(-1);
   const int T = (int)(x.numel() / H);
-  TORCH_CHECK(H % 8 == 0 && w.numel() == H, "rmsnorm_fwd: H must be a multiple of 8 and match w");
+  LIBRA_CHECK(H % 8 == 0 && w.numel() == H, "rmsnorm_fwd: H must be a multiple of 8 and match w");
   const c10::cuda::CUDAGuard guard(x.device());
   auto y = torch::empty_like(x);
   auto rstd = torch::empty({T}, x.options().dtype(at::kFloat));
@@ -297,7 +297,7 @@ std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double 
   rmsnorm_fwd_kernel<<<(T + warps - 1) / warps, warps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
       (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)y.data_ptr(),
       rstd.data_ptr<float>(), T, H, (float)eps);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  LIBRA_LAUNCH_CHECK();
   return {y, rstd};
 }
 
@@ -316,8 +316,8 @@ torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, to
   check_bf16_rowmajor(x, "rmsnorm_bwd x");
   const int H = (int)x.size(-1);
   const int T = (int)(x.numel() / H);
-  TORCH_CHECK(H % 8 == 0 && H <= 8 * kNormThreads * kMaxVec, "rmsnorm_bwd: unsupported H");
-  TORCH_CHECK(dw.scalar_type() == at::kFloat && dw.numel() == H && dw.is_contiguous(), "rmsnorm_bwd: dw fp32 [H]");
+  LIBRA_CHECK(H % 8 == 0 && H <= 8 * kNormThreads * kMaxVec, "rmsnorm_bwd: unsupported H");
+  LIBRA_CHECK(dw.scalar_type() == at::kFloat && dw.numel() == H && dw.is_contiguous(), "rmsnorm_bwd: dw fp32 [H]");
   const c10::cuda::CUDAGuard guard(x.device());
   torch::Tensor dx;
   int acc_dx = 0;
@@ -335,13 +335,13 @@ torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, to
     rmsnorm_bwd_kernel<<<grid, kNormThreads, 0, st>>>(
         (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(),
         rstd.data_ptr<float>(), (__nv_bfloat16*)dx.data_ptr(), part.data_ptr<float>(), T, H, acc_dx);
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    LIBRA_LAUNCH_CHECK();
   } else {
     part.zero_();
   }
   colsum_kernel<<<(H + 255) / 256, 256, 0, st>>>(part.data_ptr<float>(), grid, H, dw.data_ptr<float>(),
                                                  accumulate_dw ? 1 : 0);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  LIBRA_LAUNCH_CHECK();
   return dx;
 }
 
@@ -350,8 +350,8 @@ std::vector<torch::Tensor> qk_norm_rope_fwd(torch::Tensor qkv, torch::Tensor qw,
                                             double eps) {
   check_bf16_rowmajor(qkv, "qk_norm_rope qkv");
   const int D = 128;
-  TORCH_CHECK(qkv.size(-1) == (nq + 2 * nkv) * D, "qk_norm_rope: qkv width mismatch (head_dim must be 128)");
-  TORCH_CHECK(pos.scalar_type() == at::kInt && cos_t.scalar_type() == at::kFloat, "qk_norm_rope: int32 pos, fp32 tables");
+  LIBRA_CHECK(qkv.size(-1) == (nq + 2 * nkv) * D, "qk_norm_rope: qkv width mismatch (head_dim must be 128)");
+  LIBRA_CHECK(pos.scalar_type() == at::kInt && cos_t.scalar_type() == at::kFloat, "qk_norm_rope: int32 pos, fp32 tables");
   const int T = (int)(qkv.numel() / qkv.size(-1));
   const c10::cuda::CUDAGuard guard(qkv.device());
   auto q = torch::empty({T, nq, D}, qkv.options());
@@ -366,7 +366,7 @@ std::vector<torch::Tensor> qk_norm_rope_fwd(torch::Tensor qkv, torch::Tensor qw,
       pos.data_ptr<int>(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), (__nv_bfloat16*)q.data_ptr(),
       (__nv_bfloat16*)k.data_ptr(), (__nv_bfloat16*)v.data_ptr(), rstd.data_ptr<float>(), T, (int)nq, (int)nkv,
       (float)eps);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  LIBRA_LAUNCH_CHECK();
   return {q, k, v, rstd};
 }
 
@@ -377,7 +377,7 @@ torch::Tensor qk_norm_rope_bwd(torch::Tensor qkv, torch::Tensor qw, torch::Tenso
                                int64_t nkv) {
   const int D = 128;
   const int T = (int)(qkv.numel() / qkv.size(-1));
-  TORCH_CHECK(dq.is_contiguous() && dk.is_contiguous() && dv.is_contiguous(), "qk_norm_rope_bwd: contiguous grads");
+  LIBRA_CHECK(dq.is_contiguous() && dk.is_contiguous() && dv.is_contiguous(), "qk_norm_rope_bwd: contiguous grads");
   const c10::cuda::CUDAGuard guard(qkv.device());
   auto dqkv = torch::empty_like(qkv);
   const int warps = 8;
@@ -396,11 +396,11 @@ torch::Tensor qk_norm_rope_bwd(torch::Tensor qkv, torch::Tensor qw, torch::Tenso
         pos.data_ptr<int>(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), rstd.data_ptr<float>(),
         (const __nv_bfloat16*)dq.data_ptr(), (const __nv_bfloat16*)dk.data_ptr(), (const __nv_bfloat16*)dv.data_ptr(),
         (__nv_bfloat16*)dqkv.data_ptr(), part.data_ptr<float>(), T, (int)nq, (int)nkv);
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    LIBRA_LAUNCH_CHECK();
   }
   auto sums = torch::empty({2 * D}, qkv.options().dtype(at::kFloat));
   colsum_kernel<<<1, 256, 0, st>>>(part.data_ptr<float>(), blocks * warps, 2 * D, sums.data_ptr<float>(), 0);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  LIBRA_LAUNCH_CHECK();
   dqw.add_(sums.narrow(0, 0, D));
   dkw.add_(sums.narrow(0, D, D));
   return dqkv;

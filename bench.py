@@ -47,8 +47,10 @@ def parse_args():
     ap.add_argument("--model", default="qwen3-4b")
     ap.add_argument("--prompts-per-gpu", type=int, default=8)
     ap.add_argument("--group", type=int, default=8)
-    ap.add_argument("--micro-batch", type=int, default=8, help="trajectories per micro-batch")
+    ap.add_argument("--micro-batch", type=int, default=8, help="trajectories per loss-normalisation group")
     ap.add_argument("--recompute-micro-batch", type=int, default=16)
+    ap.add_argument("--max-tokens", type=int, default=16384, help="tokens per execution chunk (update)")
+    ap.add_argument("--max-recompute-tokens", type=int, default=65536, help="tokens per execution chunk (recompute)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-launch-count", action="store_true")
     return ap.parse_args()
@@ -86,7 +88,7 @@ def base_record(args, world, impl):
         "impl": impl,
         "config": {"model": MODEL, "global_batch": global_batch, "seq_len": "prompt ~LN(300) [64,1024] + response ~LN(1500) [1,4096]",
                    "parallelism": f"dp{world}", "prompts_per_gpu": args.prompts_per_gpu, "group": args.group,
-                   "micro_batch_trajectories": args.micro_batch,
+                   "micro_batch_trajectories": args.micro_batch, "max_tokens_per_chunk": args.max_tokens,
                    "l2": "inputs larger than L2 (8 GB of weights and >10 GB of activations per step)"},
     }
 
@@ -119,7 +121,9 @@ def run_ours(args, rank, world, local):
     dev = torch.device("cuda", local)
     wl = WORKLOADS["qwen3-4b-grpo"]
     eng = B200TrainEngine(args.model, learning_rate=1e-6, micro_batch_size=args.micro_batch,
-                          recompute_micro_batch_size=args.recompute_micro_batch, device=dev, seed=0)
+                          recompute_micro_batch_size=args.recompute_micro_batch, device=dev, seed=0,
+                          max_tokens_per_micro_batch=args.max_tokens,
+                          max_tokens_per_recompute_batch=args.max_recompute_tokens)
     eng.initialize(max_seq_length=5120)
     n_steps = args.warmup + args.steps
 
@@ -133,9 +137,8 @@ def run_ours(args, rank, world, local):
     staged = []
     for s in range(n_steps):
         trajs = host_step(s)
-        upd = [eng.to_device(eng.pack(mb)) for mb in eng.micro_batches(trajs, eng.micro_batch_size)]
-        rec = [eng.to_device(eng.pack(mb, with_old_logprobs=False))["batch"]
-               for mb in eng.micro_batches(trajs, eng.recompute_micro_batch_size)]
+        upd = [eng.to_device(h) for h in eng.prepare_update(trajs)]
+        rec = [eng.to_device(h)["batch"] for _, h in eng.prepare_recompute(trajs)]
         staged.append((tokens_of(trajs), rec, upd))
     torch.cuda.synchronize(dev)
 
@@ -175,39 +178,23 @@ def run_ours(args, rank, world, local):
     e2e = None
     if not args.no_e2e:
         host = [host_step(1000 + s) for s in range(n_steps)]
-        h2d = [0]
-        d2h = [0]
-
         def api_step(trajs):
             eng.recompute_logprobs(trajs)
-            stats = eng.grpo_update(trajs)
-            return stats
-
-        def io_bytes(trajs):
-            # per micro-batch: tokens int64, positions int32, cu_seqlens, action rows/targets int64,
-            # seq index int32, old logprobs/adv fp32 (update) -> H2D; logprobs fp32 + 8 stats -> D2H
-            T = tokens_of(trajs)
-            A = sum(int(t["loss_mask"].sum()) for t in trajs)
-            n = len(trajs)
-            n_rec = -(-n // eng.recompute_micro_batch_size)
-            n_upd = -(-n // eng.micro_batch_size)
-            h = (T * 12 + A * 20 + 4 * (n + n_rec)) + (T * 12 + A * 28 + 4 * (n + n_upd) + 4 * n)
-            d = A * 4 + 8 * 8
-            return h, d
+            return eng.grpo_update(trajs)
 
         for s in range(args.warmup):
             api_step(host[s])
         torch.cuda.synchronize(dev)
         barrier(world)
+        eng.io_bytes = {"h2d": 0, "d2h": 0}
         t0 = time.perf_counter()
         for s in range(args.warmup, n_steps):
             api_step(host[s])
-            hb, db = io_bytes(host[s])
-            h2d[0] += hb
-            d2h[0] += db
         torch.cuda.synchronize(dev)
         e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / args.steps, dev)
         barrier(world)
+        h2d = [eng.io_bytes["h2d"]]
+        d2h = [eng.io_bytes["d2h"]]
         e2e_tokens = sum_over_ranks(sum(tokens_of(host[s]) for s in range(args.warmup, n_steps)) / args.steps, dev)
         e2e = {"value": e2e_tokens / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": int(h2d[0] / args.steps), "d2h_bytes_per_step": int(d2h[0] / args.steps),

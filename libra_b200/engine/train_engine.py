@@ -13,10 +13,14 @@ reference's three backends (FSDP, Megatron3D, Megatron-Core) with one engine:
   master/Adam state; gradients are reduce-scattered and the updated bf16 shard
   is all-gathered (distributed optimizer of Megatron-Core).
 * GRPO loss: PPO-clip with the log-ratio clamped to [-20, 20] and the k3 KL
-  ``(r - 1) - log r`` (reference ``engine/megatron_core_train_engine.py:950-986``);
-  per micro-batch masked token mean, averaged over micro-batches.
-* micro-batches: ``micro_batch_size`` consecutive trajectories packed into one
-  token stream (no padding); logprob recompute uses ``recompute_micro_batch_size``.
+  ``(r - 1) - log r`` (reference ``engine/megatron_core_train_engine.py:950-986``),
+  aggregated exactly as the reference does: masked token mean inside each
+  group of ``micro_batch_size`` consecutive trajectories, averaged over the
+  groups.  That aggregation is expressed as one weight per action token, so it
+  does not depend on how the work is chunked for execution.
+* execution chunks: consecutive trajectories packed into one token stream (no
+  padding) up to ``max_tokens_per_micro_batch`` tokens, which bounds activation
+  memory independently of the trajectory lengths.
 """
 
 from __future__ import annotations
@@ -70,7 +74,8 @@ class B200TrainEngine:
                  clip_epsilon: float = 0.2, micro_batch_size: int = 4, recompute_micro_batch_size: int = 0,
                  device: Optional[torch.device] = None, seed: int = 0, recompute_activations: bool = False,
                  use_distributed_optimizer: bool = True, dp_group=None, temperature: float = 1.0,
-                 max_grad_norm: float = 1.0, tp_size: int = 1, model_path: str = ""):
+                 max_grad_norm: float = 1.0, tp_size: int = 1, model_path: str = "",
+                 max_tokens_per_micro_batch: int = 16384, max_tokens_per_recompute_batch: int = 65536):
         self.cfg: Qwen3Config = get_config(model)
         self.model_path = model_path
         self.optim = OptimConfig(lr=learning_rate, max_grad_norm=max_grad_norm)
@@ -78,6 +83,8 @@ class B200TrainEngine:
         self.clip_epsilon = clip_epsilon
         self.micro_batch_size = max(1, int(micro_batch_size))
         self.recompute_micro_batch_size = int(recompute_micro_batch_size) or self.micro_batch_size
+        self.max_tokens_per_micro_batch = int(max_tokens_per_micro_batch)
+        self.max_tokens_per_recompute_batch = int(max_tokens_per_recompute_batch)
         self.seed = seed
         self.recompute_activations = recompute_activations
         self.use_distributed_optimizer = use_distributed_optimizer
@@ -94,8 +101,11 @@ class B200TrainEngine:
             else:
                 device = torch.device("cpu")
         self.device = torch.device(device)
+        if self.device.type == "cuda" and self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
         self.model: Optional[Qwen3Model] = None
         self.last_timing: Dict[str, float] = {}
+        self.io_bytes = {"h2d": 0, "d2h": 0}  # host<->device traffic of the public API calls
 
     # ------------------------------------------------------------------ setup
     def initialize(self, max_seq_length: int = 2048) -> None:
@@ -121,6 +131,9 @@ class B200TrainEngine:
         for name, v in views.items():
             p = torch.nn.Parameter(v, requires_grad=True)
             p.main_grad = grad_views[name]
+            # Ops without a fused main_grad path (the CPU reference ops) leave an
+            # ordinary .grad; fold it into the flat fp32 buffer as it arrives.
+            p.register_post_accumulate_grad_hook(_fold_grad_into_main)
             self.params[name] = p
         self.sharded = self.use_distributed_optimizer and self.dp_size > 1
         shard = self.padded_numel // self.dp_size if self.sharded else self.padded_numel
@@ -169,8 +182,12 @@ class B200TrainEngine:
         mask = torch.ones_like(ids) if mask is None else mask.reshape(-1)
         return ids, mask
 
-    def pack(self, trajectories: List[Dict[str, Any]], with_old_logprobs: bool = True) -> Dict[str, Any]:
-        """Pack trajectories (host tensors) into one pinned host micro-batch."""
+    def pack(self, trajectories: List[Dict[str, Any]], with_old_logprobs: bool = True,
+             traj_weights: Optional[List[float]] = None) -> Dict[str, Any]:
+        """Pack trajectories (host tensors) into one host micro-batch.
+
+        ``traj_weights[i]`` is the loss weight of every action token of
+        trajectory i (see ``loss_weights``)."""
         ids, masks = zip(*(self._traj_tensors(t) for t in trajectories))
         batch = pack_sequences(list(ids), list(masks))
         extra: Dict[str, torch.Tensor] = {}
@@ -179,96 +196,143 @@ class B200TrainEngine:
             # old logprob of the action token at packed row r+1
             extra["old_logp"] = old.index_select(0, batch.action_rows + 1)
             adv = torch.tensor([float(t.get("advantages", t["rewards"]).reshape(-1)[0]) for t in trajectories])
-            extra["adv"] = adv.index_select(0, batch.seq_index.long())
+            sidx = batch.seq_index.long()
+            extra["adv"] = adv.index_select(0, sidx)
+            w = torch.tensor(traj_weights if traj_weights is not None else [1.0] * len(trajectories),
+                             dtype=torch.float32)
+            extra["w"] = w.index_select(0, sidx)
             extra["rewards"] = torch.tensor([float(t["rewards"].reshape(-1)[0]) for t in trajectories])
         return {"batch": batch, **extra}
+
+    def loss_weights(self, trajectories: List[Dict[str, Any]]) -> List[float]:
+        """Per-trajectory token weight reproducing the reference loss aggregation:
+        mean over groups of ``micro_batch_size`` trajectories of the group's
+        masked token mean  =>  w = 1 / (actions in the group * number of groups)."""
+        n = len(trajectories)
+        groups = [list(range(s, min(n, s + self.micro_batch_size))) for s in range(0, n, self.micro_batch_size)]
+        w = [0.0] * n
+        for g in groups:
+            count = sum(int(self._traj_tensors(trajectories[i])[1].reshape(-1)[1:].sum()) for i in g)
+            for i in g:
+                w[i] = 1.0 / (max(count, 1) * len(groups))
+        return w
 
     def to_device(self, packed: Dict[str, Any]) -> Dict[str, Any]:
         dev = self.device
         if dev.type == "cuda":
-            out = {"batch": _pin_batch(packed["batch"]).to(dev, non_blocking=True)}
+            b = _pin_batch(packed["batch"])
+            self.io_bytes["h2d"] += sum(t.numel() * t.element_size() for t in
+                                        (b.tokens, b.positions, b.cu_seqlens, b.action_rows, b.action_targets,
+                                         b.seq_index) if t is not None)
+            out = {"batch": b.to(dev, non_blocking=True)}
             for k, v in packed.items():
                 if k != "batch":
-                    out[k] = v.pin_memory().to(dev, non_blocking=True)
+                    out[k] = (v if v.is_pinned() else v.pin_memory()).to(dev, non_blocking=True)
+                    self.io_bytes["h2d"] += v.numel() * v.element_size()
             return out
         return {"batch": packed["batch"], **{k: v for k, v in packed.items() if k != "batch"}}
+
+    @staticmethod
+    def chunk_by_tokens(trajectories: List[Dict[str, Any]], max_tokens: int) -> List[List[int]]:
+        """Consecutive trajectory index chunks of at most ``max_tokens`` tokens (>= 1 trajectory each)."""
+        chunks, cur, cur_tokens = [], [], 0
+        for i, t in enumerate(trajectories):
+            n = int(t["input_ids"].numel())
+            if cur and cur_tokens + n > max_tokens:
+                chunks.append(cur)
+                cur, cur_tokens = [], 0
+            cur.append(i)
+            cur_tokens += n
+        if cur:
+            chunks.append(cur)
+        return chunks
 
     def micro_batches(self, trajectories: List[Dict[str, Any]], size: int) -> Iterable[List[Dict[str, Any]]]:
         for s in range(0, len(trajectories), size):
             yield trajectories[s:s + size]
 
+    def prepare_update(self, trajectories: List[Dict[str, Any]]) -> List[Dict[str, Any]]:
+        """Host-side packed execution chunks (with loss weights) for one update."""
+        w = self.loss_weights(trajectories)
+        return [self.pack([trajectories[i] for i in idx], True, [w[i] for i in idx])
+                for idx in self.chunk_by_tokens(trajectories, self.max_tokens_per_micro_batch)]
+
+    def prepare_recompute(self, trajectories: List[Dict[str, Any]]):
+        """(trajectory chunk, packed host batch) pairs for logprob recompute."""
+        out = []
+        for idx in self.chunk_by_tokens(trajectories, self.max_tokens_per_recompute_batch):
+            chunk = [trajectories[i] for i in idx]
+            out.append((chunk, self.pack(chunk, with_old_logprobs=False)))
+        return out
+
     # ------------------------------------------------------------------ math
-    def loss(self, logp, old_logp, adv):
+    def loss(self, logp, old_logp, adv, weight=None):
+        """Weighted PPO-clip + k3-KL.  Without ``weight`` every token gets 1/count
+        (the masked token mean of one micro-batch)."""
         log_ratio = logp - old_logp
         ratio = torch.exp(log_ratio.clamp(-20.0, 20.0))
         clipped = ratio.clamp(1.0 - self.clip_epsilon, 1.0 + self.clip_epsilon)
         pg = torch.maximum(-adv * ratio, -adv * clipped)
-        count = max(int(logp.numel()), 1)
-        pg_loss = pg.sum() / count
-        kl = ((ratio - 1.0) - log_ratio).sum() / count
-        return pg_loss + self.kl_coef * kl, pg_loss, kl
+        kl = (ratio - 1.0) - log_ratio
+        if weight is None:
+            weight = torch.full_like(logp, 1.0 / max(int(logp.numel()), 1))
+        pg_loss = (pg * weight).sum()
+        kl_loss = (kl * weight).sum()
+        return pg_loss + self.kl_coef * kl_loss, pg_loss, kl_loss
 
     # ------------------------------------------------------------------ public API
     @torch.no_grad()
     def recompute_logprobs(self, trajectories: List[Dict[str, Any]]) -> None:
-        """Refresh trajectory["logprobs"] with the current policy (host tensors)."""
+        """Refresh trajectory["logprobs"] with the current policy (host tensors in, host tensors out)."""
         results = []
-        for mb in self.micro_batches(trajectories, self.recompute_micro_batch_size):
-            dev_mb = self.to_device(self.pack(mb, with_old_logprobs=False))
+        for chunk, host in self.prepare_recompute(trajectories):
+            dev_mb = self.to_device(host)
             lp = self.model.action_logprobs(dev_mb["batch"], self.temperature)
-            results.append((mb, dev_mb["batch"], lp.to("cpu", non_blocking=True)))
+            results.append((chunk, host["batch"], lp.to("cpu", non_blocking=True)))
+            self.io_bytes["d2h"] += lp.numel() * lp.element_size()
         if self.device.type == "cuda":
             torch.cuda.current_stream(self.device).synchronize()
-        for mb, batch, lp in results:
-            rows = batch.action_rows.cpu() + 1
-            start = 0
-            cu = batch.cu_seqlens.cpu().tolist()
-            for i, traj in enumerate(mb):
+        for chunk, batch, lp in results:
+            cu = batch.cu_seqlens.tolist()
+            rows = batch.action_rows + 1
+            for i, traj in enumerate(chunk):
                 L = cu[i + 1] - cu[i]
                 sel = (rows >= cu[i]) & (rows < cu[i + 1])
                 updated = torch.zeros(L, dtype=torch.float32)
                 updated[rows[sel] - cu[i]] = lp[sel]
-                traj["logprobs"] = updated.view(1, L).to(traj["logprobs"].dtype if "logprobs" in traj else torch.float32)
+                traj["logprobs"] = updated.view(1, L)
 
     def grpo_update(self, trajectories: List[Dict[str, Any]], ppo_epochs: int = 1) -> Dict[str, float]:
-        """One optimizer step per PPO epoch over all micro-batches (host inputs)."""
+        """One optimizer step per PPO epoch over the whole batch (host inputs)."""
         epoch_stats = []
         for _ in range(ppo_epochs):
-            mbs = [self.to_device(self.pack(mb)) for mb in self.micro_batches(trajectories, self.micro_batch_size)]
+            mbs = [self.to_device(h) for h in self.prepare_update(trajectories)]
             epoch_stats.append(self.update_packed(mbs))
         merged = _merge_stats(epoch_stats)
         merged["version"] = self.current_version
         return merged
 
     def update_packed(self, device_micro_batches: List[Dict[str, Any]], sync_stats: bool = True) -> Dict[str, Any]:
-        """Forward/backward over device-resident micro-batches + optimizer step."""
+        """Forward/backward over device-resident weighted chunks + optimizer step."""
         self.flat_grad.zero_()
-        n_mb = max(len(device_micro_batches), 1)
-        loss_acc = torch.zeros(3, dtype=torch.float32, device=self.device)
-        reward_sum, n_samples = 0.0, 0
+        acc = torch.zeros(3, dtype=torch.float32, device=self.device)
         for mb in device_micro_batches:
             logp = self.model.action_logprobs(mb["batch"], self.temperature)
-            loss, pg, kl = self.loss(logp, mb["old_logp"], mb["adv"])
-            (loss / n_mb).backward()
-            loss_acc += torch.stack([loss.detach(), pg.detach(), kl.detach()])
-            if "rewards" in mb:
-                reward_sum_t = mb["rewards"].sum()
-                reward_sum += float(reward_sum_t) if not sync_stats or self.device.type == "cpu" else 0.0
-                n_samples += int(mb["rewards"].numel())
+            loss, pg, kl = self.loss(logp, mb["old_logp"], mb["adv"], mb.get("w"))
+            loss.backward()
+            acc += torch.stack([loss.detach(), pg.detach(), kl.detach()])
         self._reduce_gradients()
         self._optimizer_step()
-        stats = {"loss_sum": loss_acc, "n_updates": float(n_mb), "n_samples": float(n_samples)}
-        if sync_stats:
-            values = (loss_acc / n_mb).tolist()
-            rewards = torch.cat([mb["rewards"] for mb in device_micro_batches if "rewards" in mb]) \
-                if any("rewards" in mb for mb in device_micro_batches) else torch.zeros(0)
-            rs = float(rewards.sum()) if rewards.numel() else 0.0
-            out = {"loss": values[0], "pg_loss": values[1], "kl": values[2], "reward_sum": rs,
-                   "n_samples": float(rewards.numel()), "n_updates": 1.0,
-                   "reward_mean": rs / max(rewards.numel(), 1),
-                   "grad_norm": float(self.sq_norm.sqrt())}
-            return self._reduce_stats(out)
-        return stats
+        if not sync_stats:
+            return {"loss_sum": acc}
+        rewards = [mb["rewards"] for mb in device_micro_batches if "rewards" in mb]
+        r = torch.cat(rewards) if rewards else torch.zeros(0, device=self.device)
+        vals = torch.cat([acc, r.sum().reshape(1).float(), self.sq_norm]).tolist()
+        self.io_bytes["d2h"] += 4 * len(vals)
+        out = {"loss": vals[0], "pg_loss": vals[1], "kl": vals[2], "reward_sum": vals[3],
+               "n_samples": float(r.numel()), "n_updates": 1.0, "reward_mean": vals[3] / max(r.numel(), 1),
+               "grad_norm": math.sqrt(max(vals[4], 0.0))}
+        return self._reduce_stats(out)
 
     # ------------------------------------------------------------------ gradients/optimizer
     def _reduce_gradients(self) -> None:
@@ -319,6 +383,12 @@ class B200TrainEngine:
         from libra_b200.engine.checkpointing import DistributedCheckpointManager
 
         DistributedCheckpointManager(path).load(self, version)
+
+
+def _fold_grad_into_main(p: torch.nn.Parameter) -> None:
+    if p.grad is not None:
+        p.main_grad.add_(p.grad.float())
+        p.grad = None
 
 
 def _pin_batch(b: PackedBatch) -> PackedBatch:

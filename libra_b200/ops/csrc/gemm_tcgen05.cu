@@ -268,6 +268,14 @@ static EncodeTiledFn encode_fn() {
 // 2-D bf16 tensor map over a row-major matrix [outer, inner] with leading
 // dimension `ld` (elements), box {box_inner, box_outer}, 128-byte swizzle.
 static CUtensorMap make_map(const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_inner, int box_outer) {
+  // The encoder is a driver-API call and needs the device's primary context to
+  // be current on this thread.  Threads that have not issued a runtime call yet
+  // (autograd's backward worker, for one) do not have it bound: bind it once.
+  static thread_local bool context_bound = false;
+  if (!context_bound) {
+    cudaFree(nullptr);
+    context_bound = true;
+  }
   CUtensorMap m;
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
   cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};

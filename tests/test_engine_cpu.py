@@ -51,3 +51,34 @@ def test_packing_skips_prompt_rows():
     n_actions = sum(int(t["loss_mask"][:, 1:].sum()) for t in trajs)
     assert b.action_rows.numel() == n_actions == packed["old_logp"].numel()
     assert torch.equal(b.tokens[b.action_rows + 1], b.action_targets)
+
+
+def test_loss_weights_make_gradient_chunking_invariant():
+    trajs = _trajs(8, seed=3)
+    grads = []
+    for budget in (10 ** 6, 60):
+        eng = B200TrainEngine("tiny", device="cpu", micro_batch_size=4, seed=5, max_tokens_per_micro_batch=budget)
+        eng.initialize()
+        eng.recompute_logprobs(trajs)
+        chunks = eng.prepare_update(trajs)
+        if budget == 60:
+            assert len(chunks) > 2
+        eng.flat_grad.zero_()
+        for c in chunks:
+            lp = eng.model.action_logprobs(c["batch"])
+            loss, _, _ = eng.loss(lp, c["old_logp"], c["adv"], c["w"])
+            loss.backward()
+        grads.append(eng.flat_grad.clone())
+    # identical maths; only bf16 rounding of differently blocked CPU matmuls differs
+    assert ((grads[0] - grads[1]).norm() / grads[0].norm()).item() < 2e-2
+
+
+def test_loss_weights_match_reference_group_mean():
+    trajs = _trajs(8, seed=4)
+    eng = B200TrainEngine("tiny", device="cpu", micro_batch_size=4)
+    w = eng.loss_weights(trajs)
+    counts = [int(t["loss_mask"][:, 1:].sum()) for t in trajs]
+    g0 = sum(counts[:4])
+    assert abs(w[0] - 1.0 / (g0 * 2)) < 1e-12
+    total = sum(wi * c for wi, c in zip(w, counts))
+    assert abs(total - 1.0) < 1e-9  # mean of two group means -> weights sum to 1

@@ -30,8 +30,10 @@ GEMM_SHAPES = [(128, 128, 64), (300, 264, 200), (1000, 520, 136), (4096, 4096, 2
 def test_gemm_layouts(M, N, K, a_mn, b_mn):
     from libra_b200 import ops
 
-    if (a_mn and M % 8) or (b_mn and N % 8):
-        pytest.skip("MN-major operand needs its leading dimension to be a multiple of 8")
+    lda = M if a_mn else K
+    ldb = N if b_mn else K
+    if lda % 8 or ldb % 8:
+        pytest.skip("TMA needs every leading dimension to be a multiple of 8 elements")
     A = _bf16(M, K, seed=1)  # logical [M, K]
     B = _bf16(N, K, seed=2)  # logical [N, K]
     a = A.t().contiguous() if a_mn else A

@@ -1,0 +1,112 @@
+"""Kernel microbenchmarks: achieved TFLOP/s or GB/s of each sm_100a kernel.
+
+    python -m libra_b200.ops.microbench gemm [--shapes M,N,K;...] [--iters 20]
+    python -m libra_b200.ops.microbench all
+
+Timing: CUDA events on the launching stream after warm-up, synchronize on both
+sides, inputs larger than L2 for the bandwidth-bound kernels.  The GEMM rows
+also time torch.matmul (cuBLAS) on the same operands for comparison.  Prints one
+JSON object per line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from libra_b200 import ops
+
+# Qwen3-4B training shapes for a 16k-token chunk: (M tokens, N out, K in)
+QWEN3_4B_SHAPES = [
+    ("qkv_fwd", 16384, 6144, 2560, False, False),
+    ("o_fwd", 16384, 2560, 4096, False, False),
+    ("gate_up_fwd", 16384, 19456, 2560, False, False),
+    ("down_fwd", 16384, 2560, 9728, False, False),
+    ("gate_up_dgrad", 16384, 2560, 19456, False, True),
+    ("gate_up_wgrad", 19456, 2560, 16384, True, True),
+    ("lm_head_fwd", 8192, 151936, 2560, False, False),
+    ("square_8192", 8192, 8192, 8192, False, False),
+]
+
+
+def _time(fn, iters: int, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(iters):
+        fn()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / iters
+
+
+def bench_gemm(shapes, iters: int):
+    for name, M, N, K, a_mn, b_mn in shapes:
+        A = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+        B = torch.randn(N, K, device="cuda").to(torch.bfloat16)
+        a = A.t().contiguous() if a_mn else A
+        b = B.t().contiguous() if b_mn else B
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        ms = _time(lambda: ops.gemm(a, b, a_mn=a_mn, b_mn=b_mn, out=out), iters)
+        ref_a = a.t() if a_mn else a
+        ref_b = b if b_mn else b.t()
+        ms_ref = _time(lambda: torch.matmul(ref_a, ref_b, out=out), iters)
+        flops = 2.0 * M * N * K
+        ops.check_kernel_errors()
+        print(json.dumps({"kernel": "gemm_bf16_tcgen05", "case": name, "M": M, "N": N, "K": K, "a_mn": a_mn,
+                          "b_mn": b_mn, "ms": ms, "tflops": flops / ms / 1e9, "cublas_ms": ms_ref,
+                          "cublas_tflops": flops / ms_ref / 1e9, "ratio_vs_cublas": ms_ref / ms}), flush=True)
+        del A, B, a, b, out
+
+
+def bench_elementwise(iters: int):
+    T, H = 65536, 2560
+    x = torch.randn(T, H, device="cuda").to(torch.bfloat16)
+    w = torch.ones(H, device="cuda", dtype=torch.bfloat16)
+    ms = _time(lambda: ops.ext().rmsnorm_fwd(x, w, 1e-6), iters)
+    print(json.dumps({"kernel": "rmsnorm_fwd", "T": T, "H": H, "ms": ms, "gbs": 2 * 2 * T * H / ms / 1e6}), flush=True)
+    F = 9728
+    gu = torch.randn(T // 2, 2 * F, device="cuda").to(torch.bfloat16)
+    ms = _time(lambda: ops.ext().swiglu_fwd(gu), iters)
+    print(json.dumps({"kernel": "swiglu_fwd", "T": T // 2, "F": F, "ms": ms,
+                      "gbs": (T // 2) * 3 * F * 2 / ms / 1e6}), flush=True)
+    R, V = 4096, 151936
+    logits = torch.randn(R, V, device="cuda").to(torch.bfloat16)
+    tgt = torch.randint(0, V, (R,), device="cuda")
+    ms = _time(lambda: ops.ext().logprob_fwd(logits, tgt, 0, 1.0, True), iters)
+    print(json.dumps({"kernel": "logprob_fwd", "R": R, "V": V, "ms": ms, "gbs": R * V * 2 / ms / 1e6}), flush=True)
+    n = 1 << 28
+    master = torch.randn(n, device="cuda")
+    grad = torch.randn(n, device="cuda")
+    m, v = torch.zeros_like(master), torch.zeros_like(master)
+    p = master.to(torch.bfloat16)
+    ms = _time(lambda: ops.adamw_step(master, grad, m, v, p, lr=1e-6, beta1=0.9, beta2=0.95, eps=1e-8,
+                                      weight_decay=0.01, step=1), iters)
+    print(json.dumps({"kernel": "adamw", "n": n, "ms": ms, "gbs": n * 30 / ms / 1e6}), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("what", choices=["gemm", "elementwise", "all"])
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--shapes", default="", help="name:M,N,K,a_mn,b_mn;...")
+    args = ap.parse_args()
+    shapes = QWEN3_4B_SHAPES
+    if args.shapes:
+        shapes = []
+        for item in args.shapes.split(";"):
+            name, dims = item.split(":")
+            M, N, K, a_mn, b_mn = dims.split(",")
+            shapes.append((name, int(M), int(N), int(K), a_mn == "1", b_mn == "1"))
+    if args.what in ("gemm", "all"):
+        bench_gemm(shapes, args.iters)
+    if args.what in ("elementwise", "all"):
+        bench_elementwise(args.iters)
+
+
+if __name__ == "__main__":
+    main()

@@ -94,22 +94,26 @@ def base_record(args, world, impl):
 
 
 def count_launches(fn, prefixes=("libra::",)):
-    """Run fn once under torch.profiler and count this repo's kernels."""
+    """Run fn once under torch.profiler: count this repo's kernels and return the
+    per-kernel device-time breakdown of the step (all kernels, top 20, ms).
+    The profiled step is separate from the timed steps."""
     from torch.profiler import ProfilerActivity, profile
 
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         fn()
         torch.cuda.synchronize()
     n = 0
-    names = {}
+    counts, times = {}, {}
     for ev in prof.events():
-        if ev.device_type == torch.autograd.DeviceType.CUDA:
-            name = ev.name
-            if any(p in name for p in prefixes):
-                n += 1
-                key = name.split("(")[0][:60]
-                names[key] = names.get(key, 0) + 1
-    return n, names
+        if ev.device_type != torch.autograd.DeviceType.CUDA:
+            continue
+        key = ev.name.split("(")[0][:70]
+        times[key] = times.get(key, 0.0) + ev.device_time_total / 1e3
+        if any(p in ev.name for p in prefixes):
+            n += 1
+            counts[key] = counts.get(key, 0) + 1
+    top = dict(sorted(((k, round(v, 2)) for k, v in times.items()), key=lambda kv: -kv[1])[:20])
+    return n, counts, top
 
 
 # ---------------------------------------------------------------------- ours
@@ -167,9 +171,9 @@ def run_ours(args, rank, world, local):
     ops.check_kernel_errors(dev)
 
     launches = None
-    launch_names = {}
+    launch_names, kernel_ms = {}, {}
     if not args.no_launch_count:
-        n, launch_names = count_launches(lambda: device_step(args.warmup))
+        n, launch_names, kernel_ms = count_launches(lambda: device_step(args.warmup))
         launches = int(max_over_ranks(n, dev)) * args.steps
     del staged
     torch.cuda.empty_cache()
@@ -204,6 +208,7 @@ def run_ours(args, rank, world, local):
     rec.update({"value": value, "ms_per_step": ms_step, "tokens_per_step": tokens_step, "e2e": e2e,
                 "gpu_launches": launches, "clocks": clocks})
     rec["config"]["launch_breakdown_per_step"] = launch_names
+    rec["config"]["kernel_ms_per_step_top20"] = kernel_ms
     emit(rank, rec)
 
 

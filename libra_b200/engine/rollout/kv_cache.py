@@ -1,0 +1,188 @@
+"""Paged KV cache with reference-counted, content-addressed (prefix-cached) blocks.
+
+Layout per layer: K and V pools of shape [num_blocks, block_size, kv_heads, head_dim]
+(bf16 on GPU).  A sequence owns a block table (list of block ids).  Full blocks
+are hashed by (parent hash, token ids) so a new request whose prompt shares a
+prefix with a cached sequence (the GRPO group members, or the next turn of a
+multi-turn episode) reuses those blocks instead of recomputing them.
+Replaces vLLM's paged KV + prefix cache used by the reference's rollout servers.
+"""
+
+from __future__ import annotations
+
+import hashlib
+from collections import OrderedDict
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Tuple
+
+import torch
+
+
+def _block_hash(parent: str, tokens: List[int]) -> str:
+    h = hashlib.blake2b(digest_size=16)
+    h.update(parent.encode())
+    h.update(",".join(map(str, tokens)).encode())
+    return h.hexdigest()
+
+
+@dataclass
+class SequenceBlocks:
+    blocks: List[int] = field(default_factory=list)
+    num_tokens: int = 0          # tokens whose KV is written
+    hashes: List[str] = field(default_factory=list)  # hash of each full block
+
+
+class BlockAllocator:
+    """Free list + refcounts + an LRU of unreferenced cached blocks."""
+
+    def __init__(self, num_blocks: int, block_size: int):
+        self.num_blocks, self.block_size = num_blocks, block_size
+        self.refcount = [0] * num_blocks
+        self.free: List[int] = list(range(num_blocks - 1, -1, -1))
+        self.cached: Dict[str, int] = {}            # hash -> block
+        self.block_hash: Dict[int, str] = {}
+        self.evictable: "OrderedDict[int, None]" = OrderedDict()  # cached blocks with refcount 0
+
+    def num_free(self) -> int:
+        return len(self.free) + len(self.evictable)
+
+    def allocate(self) -> int:
+        if self.free:
+            b = self.free.pop()
+        elif self.evictable:
+            b, _ = self.evictable.popitem(last=False)
+            h = self.block_hash.pop(b, None)
+            if h is not None and self.cached.get(h) == b:
+                del self.cached[h]
+        else:
+            raise MemoryError("KV cache out of blocks")
+        self.refcount[b] = 1
+        return b
+
+    def lookup(self, h: str) -> Optional[int]:
+        b = self.cached.get(h)
+        if b is None:
+            return None
+        if self.refcount[b] == 0:
+            self.evictable.pop(b, None)
+        self.refcount[b] += 1
+        return b
+
+    def register(self, b: int, h: str) -> None:
+        if h not in self.cached:
+            self.cached[h] = b
+            self.block_hash[b] = h
+
+    def release(self, b: int) -> None:
+        self.refcount[b] -= 1
+        if self.refcount[b] == 0:
+            if b in self.block_hash:
+                self.evictable[b] = None
+            else:
+                self.free.append(b)
+
+    def clear_cache(self) -> None:
+        """Forget every content hash (after a weight update the cached KV is stale)."""
+        for b in list(self.evictable):
+            self.free.append(b)
+        self.evictable.clear()
+        self.cached.clear()
+        self.block_hash.clear()
+
+
+class PagedKVCache:
+    def __init__(self, num_layers: int, num_blocks: int, block_size: int, kv_heads: int, head_dim: int,
+                 device, dtype=torch.bfloat16):
+        self.num_layers, self.block_size = num_layers, block_size
+        self.kv_heads, self.head_dim = kv_heads, head_dim
+        shape = (num_layers, num_blocks, block_size, kv_heads, head_dim)
+        self.k = torch.zeros(shape, dtype=dtype, device=device)
+        self.v = torch.zeros(shape, dtype=dtype, device=device)
+        self.alloc = BlockAllocator(num_blocks, block_size)
+        self.seqs: Dict[str, SequenceBlocks] = {}
+
+    @staticmethod
+    def blocks_for_budget(budget_bytes: float, num_layers: int, block_size: int, kv_heads: int, head_dim: int,
+                          dtype_bytes: int = 2) -> int:
+        per_block = 2 * num_layers * block_size * kv_heads * head_dim * dtype_bytes
+        return max(1, int(budget_bytes // per_block))
+
+    # -------------------------------------------------------------- sequence ops
+    def match_prefix(self, seq_id: str, tokens: List[int]) -> int:
+        """Attach cached full blocks for the longest cached prefix; returns cached token count."""
+        sb = self.seqs.setdefault(seq_id, SequenceBlocks())
+        assert not sb.blocks, "prefix match only on a fresh sequence"
+        parent = ""
+        bs = self.block_size
+        # never reuse the block holding the last prompt token: its logits must be recomputed
+        limit = (max(len(tokens) - 1, 0) // bs) * bs
+        for s in range(0, limit, bs):
+            h = _block_hash(parent, tokens[s:s + bs])
+            b = self.alloc.lookup(h)
+            if b is None:
+                break
+            sb.blocks.append(b)
+            sb.hashes.append(h)
+            parent = h
+        sb.num_tokens = len(sb.blocks) * bs
+        return sb.num_tokens
+
+    def reserve(self, seq_id: str, new_total_tokens: int) -> None:
+        sb = self.seqs.setdefault(seq_id, SequenceBlocks())
+        need = -(-new_total_tokens // self.block_size)
+        while len(sb.blocks) < need:
+            sb.blocks.append(self.alloc.allocate())
+
+    def can_reserve(self, seq_id: str, new_total_tokens: int) -> bool:
+        sb = self.seqs.get(seq_id)
+        have = len(sb.blocks) if sb else 0
+        return -(-new_total_tokens // self.block_size) - have <= self.alloc.num_free()
+
+    def commit(self, seq_id: str, tokens: List[int]) -> None:
+        """Mark KV of ``tokens`` (the full token list of the sequence so far) as written and
+        publish newly completed full blocks to the prefix cache."""
+        sb = self.seqs[seq_id]
+        sb.num_tokens = len(tokens)
+        bs = self.block_size
+        while len(sb.hashes) < len(tokens) // bs:
+            i = len(sb.hashes)
+            parent = sb.hashes[-1] if sb.hashes else ""
+            h = _block_hash(parent, tokens[i * bs:(i + 1) * bs])
+            sb.hashes.append(h)
+            self.alloc.register(sb.blocks[i], h)
+
+    def free(self, seq_id: str) -> None:
+        sb = self.seqs.pop(seq_id, None)
+        if sb:
+            for b in sb.blocks:
+                self.alloc.release(b)
+
+    def block_table(self, seq_ids: List[str], device) -> torch.Tensor:
+        width = max((len(self.seqs[s].blocks) for s in seq_ids), default=1)
+        tbl = torch.full((len(seq_ids), max(width, 1)), 0, dtype=torch.int32)
+        for i, s in enumerate(seq_ids):
+            bl = self.seqs[s].blocks
+            if bl:
+                tbl[i, :len(bl)] = torch.tensor(bl, dtype=torch.int32)
+        return tbl.to(device, non_blocking=True)
+
+    def slot_mapping(self, seq_id: str, start: int, end: int) -> torch.Tensor:
+        """Flat slot index (block * block_size + offset) for token positions [start, end)."""
+        bl = self.seqs[seq_id].blocks
+        pos = torch.arange(start, end)
+        blocks = torch.tensor(bl, dtype=torch.long)[pos // self.block_size]
+        return blocks * self.block_size + pos % self.block_size
+
+    def gather(self, layer: int, seq_id: str, length: int) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Contiguous K/V [length, kv_heads, D] of one sequence (prefill/extend attention)."""
+        slots = self.slot_mapping(seq_id, 0, length).to(self.k.device)
+        kf = self.k[layer].view(-1, self.kv_heads, self.head_dim)
+        vf = self.v[layer].view(-1, self.kv_heads, self.head_dim)
+        return kf.index_select(0, slots), vf.index_select(0, slots)
+
+    def write(self, layer: int, slots: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
+        self.k[layer].view(-1, self.kv_heads, self.head_dim).index_copy_(0, slots, k)
+        self.v[layer].view(-1, self.kv_heads, self.head_dim).index_copy_(0, slots, v)
+
+    def usage(self) -> float:
+        return 1.0 - self.alloc.num_free() / max(1, self.alloc.num_blocks)

@@ -1,0 +1,303 @@
+"""Continuous-batching generation engine (the rollout side of libra_b200).
+
+Replaces the vLLM server processes of the reference with an in-process engine
+per rollout instance:
+
+* requests wait in a FIFO; each ``step`` admits waiting requests while the
+  prefill token budget and KV blocks allow (prefix-cached blocks are reused),
+  then runs one mixed batch: prefill/extend tokens of admitted requests plus one
+  decode token for every running request;
+* sampling (temperature / top-p / top-k, per-request seed) returns the sampled
+  token's logprob, as vLLM does with ``logprobs=1``;
+* a request finishes on a stop token, ``max_tokens`` or the context limit; its
+  KV blocks return to the cache as reusable prefix blocks;
+* ``generate`` is a coroutine: the step loop runs on a background thread and
+  resolves per-request asyncio futures thread-safely;
+* ``update_weights`` swaps in new weights between steps (in-place copy, or a
+  new parameter dict) and drops the prefix cache, which is stale afterwards;
+  ``pause`` / ``resume`` bracket weight updates.
+"""
+
+from __future__ import annotations
+
+import asyncio
+import itertools
+import threading
+import time
+import uuid
+from collections import deque
+from dataclasses import dataclass, field
+from typing import Deque, Dict, List, Optional
+
+import torch
+
+from libra_b200.engine.rollout.kv_cache import PagedKVCache
+from libra_b200.engine.rollout.runner import InferenceRunner, WorkItem
+from libra_b200.engine.rollout.sampler import SamplingParams, sample
+from libra_b200.models.qwen3 import Qwen3Config
+
+
+@dataclass
+class GenerationResult:
+    request_id: str
+    prompt_tokens: List[int]
+    output_tokens: List[int]
+    output_logprobs: List[float]
+    finish_reason: str
+    metrics: Dict[str, float] = field(default_factory=dict)
+
+
+@dataclass
+class _Request:
+    request_id: str
+    prompt: List[int]
+    params: SamplingParams
+    out: List[int] = field(default_factory=list)
+    logprobs: List[float] = field(default_factory=list)
+    cached: int = 0           # tokens whose KV is in the cache
+    future: Optional[asyncio.Future] = None
+    loop: Optional[asyncio.AbstractEventLoop] = None
+    callback: Optional[object] = None
+    generator: Optional[torch.Generator] = None
+    t_arrive: float = field(default_factory=time.perf_counter)
+    t_first: float = 0.0
+
+    @property
+    def tokens(self) -> List[int]:
+        return self.prompt + self.out
+
+
+class LLMEngine:
+    def __init__(self, cfg: Qwen3Config, params: Dict[str, torch.Tensor], *, kv_blocks: int = 0,
+                 block_size: int = 16, kv_memory_fraction: float = 0.5, max_batch_tokens: int = 8192,
+                 max_running: int = 256, max_model_len: int = 0, instance_id: str = "", tp_group=None,
+                 tp_size: int = 1, eos_token_id: Optional[int] = None):
+        self.cfg = cfg
+        self.params = params
+        self.device = next(iter(params.values())).device
+        self.instance_id = instance_id or f"engine-{uuid.uuid4().hex[:6]}"
+        nkv = max(1, cfg.num_key_value_heads // tp_size)
+        if kv_blocks <= 0:
+            if self.device.type == "cuda":
+                free, _ = torch.cuda.mem_get_info(self.device)
+                budget = free * kv_memory_fraction
+            else:
+                budget = 256 * 1024 * 1024
+            kv_blocks = PagedKVCache.blocks_for_budget(budget, cfg.num_hidden_layers, block_size, nkv, cfg.head_dim)
+        self.kv = PagedKVCache(cfg.num_hidden_layers, kv_blocks, block_size, nkv, cfg.head_dim, self.device,
+                               next(iter(params.values())).dtype)
+        self.runner = InferenceRunner(cfg, params, self.kv, tp_group, tp_size)
+        self.max_batch_tokens = max_batch_tokens
+        self.max_running = max_running
+        self.max_model_len = max_model_len or cfg.max_position_embeddings
+        self.eos_token_id = eos_token_id
+        self.waiting: Deque[_Request] = deque()
+        self.running: List[_Request] = []
+        self._lock = threading.Lock()
+        self._wake = threading.Event()
+        self._paused = threading.Event()
+        self._idle = threading.Event()
+        self._idle.set()
+        self._stop = threading.Event()
+        self._thread: Optional[threading.Thread] = None
+        self.version = 0
+        self.stats = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0, "cached_prefix_tokens": 0,
+                      "finished": 0, "busy_s": 0.0}
+        self._ids = itertools.count()
+
+    # ------------------------------------------------------------------ request API
+    def add_request(self, prompt_tokens: List[int], params: SamplingParams, request_id: str = "",
+                    future=None, loop=None, callback=None) -> str:
+        rid = request_id or f"{self.instance_id}-{next(self._ids)}"
+        gen = None
+        if params.seed is not None:
+            gen = torch.Generator(device=self.device)
+            gen.manual_seed(int(params.seed))
+        req = _Request(rid, list(int(t) for t in prompt_tokens), params, future=future, loop=loop, callback=callback,
+                       generator=gen)
+        with self._lock:
+            self.waiting.append(req)
+            self._idle.clear()
+        self._wake.set()
+        return rid
+
+    async def generate(self, prompt_tokens: List[int], params: Optional[SamplingParams] = None,
+                       request_id: str = "") -> GenerationResult:
+        loop = asyncio.get_running_loop()
+        fut = loop.create_future()
+        self.start()
+        self.add_request(prompt_tokens, params or SamplingParams(), request_id, future=fut, loop=loop)
+        return await fut
+
+    def generate_sync(self, prompts: List[List[int]], params: Optional[SamplingParams] = None) -> List[GenerationResult]:
+        """Blocking batch generation on the calling thread (no background loop)."""
+        results: Dict[str, GenerationResult] = {}
+        ids = [self.add_request(p, params or SamplingParams(), callback=lambda r: results.__setitem__(r.request_id, r))
+               for p in prompts]
+        while len(results) < len(ids):
+            self.step()
+        return [results[i] for i in ids]
+
+    # ------------------------------------------------------------------ background loop
+    def start(self) -> None:
+        if self._thread is not None and self._thread.is_alive():
+            return
+        self._stop.clear()
+        self._thread = threading.Thread(target=self._loop, daemon=True, name=f"llm-{self.instance_id}")
+        self._thread.start()
+
+    def shutdown(self) -> None:
+        self._stop.set()
+        self._wake.set()
+        if self._thread is not None:
+            self._thread.join(timeout=10)
+
+    def _loop(self) -> None:
+        if self.device.type == "cuda":
+            torch.cuda.set_device(self.device)
+        while not self._stop.is_set():
+            if self._paused.is_set() or (not self.waiting and not self.running):
+                self._idle.set()
+                self._wake.wait(timeout=0.05)
+                self._wake.clear()
+                continue
+            try:
+                self.step()
+            except Exception as exc:  # noqa: BLE001 - fail every in-flight request, keep serving
+                self._fail_all(exc)
+
+    def _fail_all(self, exc: Exception) -> None:
+        with self._lock:
+            reqs = list(self.running) + list(self.waiting)
+            self.running.clear()
+            self.waiting.clear()
+        for r in reqs:
+            self.kv.free(r.request_id)
+            if r.future is not None and r.loop is not None:
+                r.loop.call_soon_threadsafe(lambda f=r.future: f.done() or f.set_exception(RuntimeError(str(exc))))
+
+    def pause(self, timeout: float = 600.0) -> None:
+        """Stop stepping after the current step (requests stay queued)."""
+        self._paused.set()
+        deadline = time.monotonic() + timeout
+        while self._thread is not None and self._thread.is_alive() and not self._idle.is_set():
+            if time.monotonic() > deadline:
+                raise TimeoutError("engine did not pause in time")
+            time.sleep(0.005)
+
+    def resume(self) -> None:
+        self._paused.clear()
+        self._wake.set()
+
+    def wait_until_idle(self, timeout: float = 3600.0) -> None:
+        deadline = time.monotonic() + timeout
+        while self.waiting or self.running:
+            if time.monotonic() > deadline:
+                raise TimeoutError("engine still has requests")
+            time.sleep(0.01)
+
+    # ------------------------------------------------------------------ weights
+    @torch.no_grad()
+    def update_weights(self, new_params: Dict[str, torch.Tensor], version: Optional[int] = None,
+                       copy: bool = True) -> None:
+        """Install new weights between steps (copy into the existing buffers, or rebind)."""
+        was_paused = self._paused.is_set()
+        self.pause()
+        try:
+            if copy:
+                for k, v in new_params.items():
+                    self.params[k].copy_(v, non_blocking=True)
+                if self.device.type == "cuda":
+                    torch.cuda.current_stream(self.device).synchronize()
+            else:
+                self.params = new_params
+                self.runner.p = new_params
+            self.kv.alloc.clear_cache()
+            if version is not None:
+                self.version = int(version)
+        finally:
+            if not was_paused:
+                self.resume()
+
+    # ------------------------------------------------------------------ scheduling
+    def _admit(self) -> List[_Request]:
+        admitted, budget = [], self.max_batch_tokens - len(self.running)
+        with self._lock:
+            while self.waiting and len(self.running) + len(admitted) < self.max_running:
+                r = self.waiting[0]
+                if not r.cached and r.request_id not in self.kv.seqs:
+                    r.cached = self.kv.match_prefix(r.request_id, r.prompt)
+                    self.stats["cached_prefix_tokens"] += r.cached
+                need = len(r.tokens) - r.cached
+                if admitted and need > budget:
+                    break
+                if not self.kv.can_reserve(r.request_id, len(r.tokens) + 1):
+                    if not admitted and not self.running:
+                        self.waiting.popleft()
+                        self._finish(r, "kv_cache_exhausted")
+                        continue
+                    break
+                self.waiting.popleft()
+                admitted.append(r)
+                budget -= need
+        return admitted
+
+    def step(self) -> int:
+        t0 = time.perf_counter()
+        admitted = self._admit()
+        decode = [r for r in self.running if r.cached == len(r.tokens) - 1]
+        batch = admitted + decode
+        if not batch:
+            return 0
+        items = [WorkItem(r.request_id, r.tokens, r.cached) for r in batch]
+        logits = self.runner.step(items)
+        temps = torch.tensor([r.params.temperature for r in batch], device=logits.device, dtype=torch.float32)
+        top_p = torch.tensor([r.params.top_p for r in batch], device=logits.device, dtype=torch.float32)
+        top_k = torch.tensor([r.params.top_k for r in batch], device=logits.device, dtype=torch.long)
+        gens = [r.generator for r in batch] if any(r.generator is not None for r in batch) else None
+        toks, lps = sample(logits, temps, top_p, top_k, gens)
+        toks, lps = toks.tolist(), lps.tolist()
+        now = time.perf_counter()
+        self.stats["prefill_tokens"] += sum(len(r.tokens) - r.cached for r in admitted)
+        self.stats["decode_tokens"] += len(decode)
+        still = []
+        for r, t, lp in zip(batch, toks, lps):
+            r.cached = len(r.tokens)
+            r.out.append(int(t))
+            r.logprobs.append(float(lp))
+            if not r.t_first:
+                r.t_first = now
+            reason = self._stop_reason(r, int(t))
+            if reason:
+                self._finish(r, reason)
+            else:
+                still.append(r)
+        keep = {id(r) for r in still}
+        self.running = [r for r in self.running if id(r) in keep] + [r for r in admitted if id(r) in keep]
+        self.stats["steps"] += 1
+        self.stats["busy_s"] += time.perf_counter() - t0
+        return len(batch)
+
+    def _stop_reason(self, r: _Request, tok: int) -> str:
+        if tok in r.params.stop_token_ids or (self.eos_token_id is not None and tok == self.eos_token_id):
+            return "stop"
+        if len(r.out) >= r.params.max_tokens:
+            return "length"
+        if len(r.tokens) >= self.max_model_len:
+            return "length"
+        return ""
+
+    def _finish(self, r: _Request, reason: str) -> None:
+        self.kv.free(r.request_id)
+        self.stats["finished"] += 1
+        res = GenerationResult(r.request_id, r.prompt, list(r.out), list(r.logprobs), reason,
+                               {"ttft_s": (r.t_first - r.t_arrive) if r.t_first else 0.0,
+                                "latency_s": time.perf_counter() - r.t_arrive, "cached_tokens": 0})
+        if r.callback is not None:
+            r.callback(res)
+        if r.future is not None and r.loop is not None:
+            r.loop.call_soon_threadsafe(lambda f=r.future, x=res: f.done() or f.set_result(x))
+
+    # ------------------------------------------------------------------ introspection
+    def load(self) -> Dict[str, float]:
+        return {"running": len(self.running), "waiting": len(self.waiting), "kv_usage": self.kv.usage()}

@@ -1,0 +1,178 @@
+"""Forward pass of the rollout engine over a paged KV cache.
+
+One ``step`` runs a mixed batch: sequences that append several tokens
+(prefill of a new prompt, or the tool-return tokens of the next turn of an
+agentic episode) and sequences that decode one token.  All new tokens are
+packed into one stream, so the GEMMs (tcgen05 kernel) see every token of the
+step at once; attention is split:
+
+* decode rows -> ``paged_decode_attention`` (sm_100a kernel, KV read in place);
+* extend rows -> the sequence's KV is gathered to a contiguous buffer and run
+  through causal varlen attention with the queries aligned to the end of the
+  key range.
+* CPU tensors use the fp32 reference for both.
+
+Only the last position of each sequence goes through the final norm and the
+LM head.  Weights are the training engine's parameter views when rollout and
+training share a process (zero-copy weight updates), or this instance's own
+buffer otherwise.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence
+
+import torch
+
+from libra_b200 import ops
+from libra_b200.engine.rollout.kv_cache import PagedKVCache
+from libra_b200.models.qwen3 import Qwen3Config
+
+
+@dataclass
+class WorkItem:
+    seq_id: str
+    tokens: List[int]   # full token list of the sequence after this step's tokens are appended
+    start: int          # number of tokens whose KV is already in the cache
+
+
+def _extend_attention_ref(q, k, v, q_start: int):
+    """q [n, Hq, D] at positions q_start..; k/v [L, Hkv, D] (positions 0..L-1)."""
+    n, hq, d = q.shape
+    L, hkv = k.shape[0], k.shape[1]
+    kk = k.float().transpose(0, 1).repeat_interleave(hq // hkv, 0)
+    vv = v.float().transpose(0, 1).repeat_interleave(hq // hkv, 0)
+    s = (q.float().transpose(0, 1) @ kk.transpose(-1, -2)) / math.sqrt(d)
+    qpos = torch.arange(q_start, q_start + n, device=q.device).unsqueeze(1)
+    kpos = torch.arange(L, device=q.device).unsqueeze(0)
+    s = s.masked_fill(kpos > qpos, float("-inf"))
+    return (s.softmax(-1) @ vv).transpose(0, 1).to(q.dtype)
+
+
+class InferenceRunner:
+    def __init__(self, cfg: Qwen3Config, params: Dict[str, torch.Tensor], kv_cache: PagedKVCache,
+                 tp_group=None, tp_size: int = 1):
+        self.cfg, self.p, self.kv = cfg, params, kv_cache
+        self.device = next(iter(params.values())).device
+        self.tp_group, self.tp_size = tp_group, tp_size
+        self.nq = cfg.num_attention_heads // tp_size
+        self.nkv = max(1, cfg.num_key_value_heads // tp_size)
+        cos, sin = ops.ref.rope_tables(cfg.max_position_embeddings, cfg.head_dim, cfg.rope_theta, self.device)
+        self.cos, self.sin = cos, sin
+        self.scale = 1.0 / math.sqrt(cfg.head_dim)
+
+    @property
+    def lm_head(self):
+        return self.p["embed_tokens"] if self.cfg.tie_word_embeddings else self.p["lm_head"]
+
+    def _attention(self, layer: int, q, items: Sequence[WorkItem], offsets: List[int], decode_only: bool):
+        dev = q.device
+        out = torch.empty_like(q)
+        dec = [i for i, it in enumerate(items) if len(it.tokens) - it.start == 1]
+        ext = [i for i in range(len(items)) if i not in set(dec)]
+        if dec:
+            rows = torch.tensor([offsets[i] for i in dec], device=dev, dtype=torch.long)
+            if dev.type == "cuda" and self.cfg.head_dim == 128:
+                ids = [items[i].seq_id for i in dec]
+                tbl = self._tables.get(tuple(ids))
+                if tbl is None:
+                    tbl = self.kv.block_table(ids, dev)
+                    self._tables[tuple(ids)] = tbl
+                lens = self._lens_dec
+                o = ops.ext().paged_decode_attention(q.index_select(0, rows).contiguous(), self.kv.k[layer],
+                                                     self.kv.v[layer], tbl, lens, self._max_len_dec, self.scale)
+                out.index_copy_(0, rows, o)
+            else:
+                for i in dec:
+                    k, v = self.kv.gather(layer, items[i].seq_id, len(items[i].tokens))
+                    out[offsets[i]:offsets[i] + 1] = _extend_attention_ref(q[offsets[i]:offsets[i] + 1], k, v,
+                                                                           len(items[i].tokens) - 1)
+        if ext:
+            if dev.type == "cuda" and self.cfg.head_dim == 128:
+                ks, vs, cu_q, cu_k, rows = [], [], [0], [0], []
+                for i in ext:
+                    it = items[i]
+                    k, v = self.kv.gather(layer, it.seq_id, len(it.tokens))
+                    ks.append(k)
+                    vs.append(v)
+                    n_new = len(it.tokens) - it.start
+                    cu_q.append(cu_q[-1] + n_new)
+                    cu_k.append(cu_k[-1] + len(it.tokens))
+                    rows.append(torch.arange(offsets[i], offsets[i] + n_new, device=dev))
+                rows_t = torch.cat(rows)
+                from torch.nn.attention.varlen import varlen_attn
+
+                o = varlen_attn(q.index_select(0, rows_t).contiguous(), torch.cat(ks), torch.cat(vs),
+                                torch.tensor(cu_q, device=dev, dtype=torch.int32),
+                                torch.tensor(cu_k, device=dev, dtype=torch.int32),
+                                max(b - a for a, b in zip(cu_q[:-1], cu_q[1:])),
+                                max(b - a for a, b in zip(cu_k[:-1], cu_k[1:])), window_size=(-1, 0))
+                out.index_copy_(0, rows_t, o)
+            else:
+                for i in ext:
+                    it = items[i]
+                    n_new = len(it.tokens) - it.start
+                    k, v = self.kv.gather(layer, it.seq_id, len(it.tokens))
+                    out[offsets[i]:offsets[i] + n_new] = _extend_attention_ref(q[offsets[i]:offsets[i] + n_new],
+                                                                               k, v, it.start)
+        return out
+
+    @torch.no_grad()
+    def step(self, items: Sequence[WorkItem]) -> torch.Tensor:
+        """Write KV for every new token and return last-position logits [B, V]."""
+        cfg, p, dev = self.cfg, self.p, self.device
+        toks, pos, slots, offsets = [], [], [], []
+        off = 0
+        for it in items:
+            self.kv.reserve(it.seq_id, len(it.tokens))
+            new = it.tokens[it.start:]
+            offsets.append(off)
+            toks.extend(new)
+            pos.extend(range(it.start, len(it.tokens)))
+            slots.append(self.kv.slot_mapping(it.seq_id, it.start, len(it.tokens)))
+            off += len(new)
+        tok_t = torch.tensor(toks, dtype=torch.long).to(dev, non_blocking=True)
+        pos_t = torch.tensor(pos, dtype=torch.int32).to(dev, non_blocking=True)
+        slot_t = torch.cat(slots).to(dev, non_blocking=True)
+        last_rows = torch.tensor([o + len(it.tokens) - it.start - 1 for o, it in zip(offsets, items)],
+                                 dtype=torch.long).to(dev, non_blocking=True)
+        self._tables = {}
+        decode_only = all(len(it.tokens) - it.start == 1 for it in items)
+        dec_items = [it for it in items if len(it.tokens) - it.start == 1]
+        self._lens_dec = torch.tensor([len(it.tokens) for it in dec_items], dtype=torch.int32).to(dev)
+        self._max_len_dec = max((len(it.tokens) for it in dec_items), default=1)
+        x = self.p["embed_tokens"].index_select(0, tok_t)
+        for layer in range(cfg.num_hidden_layers):
+            pre = f"layers.{layer}."
+            h = ops.rmsnorm(x, p[pre + "input_layernorm"], cfg.rms_norm_eps)
+            qkv = ops.linear(h, p[pre + "qkv_proj"])
+            q, k, v = ops.qk_norm_rope(qkv, p[pre + "q_norm"], p[pre + "k_norm"], pos_t, self.cos, self.sin,
+                                       self.nq, self.nkv, cfg.rms_norm_eps)
+            self.kv.write(layer, slot_t, k, v)
+            attn = self._attention(layer, q, items, offsets, decode_only)
+            x = self._row_parallel(attn.reshape(attn.shape[0], -1), p[pre + "o_proj"], x)
+            h = ops.rmsnorm(x, p[pre + "post_attention_layernorm"], cfg.rms_norm_eps)
+            if cfg.is_moe:
+                from libra_b200.models.moe import moe_mlp
+
+                x = moe_mlp(h, x, p[pre + "router"], p[pre + "experts.w1"], p[pre + "experts.w2"], cfg)
+            else:
+                x = self._row_parallel(ops.swiglu(ops.linear(h, p[pre + "gate_up_proj"])), p[pre + "down_proj"], x)
+        last = ops.rmsnorm(x.index_select(0, last_rows), p["norm"], cfg.rms_norm_eps)
+        logits = ops.linear(last, self.lm_head)
+        if self.tp_size > 1:
+            from libra_b200.parallel.tensor_parallel import gather_vocab_logits
+
+            logits = gather_vocab_logits(logits, self.tp_group)
+        for it in items:
+            self.kv.commit(it.seq_id, it.tokens)
+        return logits
+
+    def _row_parallel(self, a, w, residual):
+        if self.tp_size == 1:
+            return ops.linear(a, w, residual=residual)
+        from libra_b200.parallel.tensor_parallel import row_parallel_linear_allreduce
+
+        return row_parallel_linear_allreduce(a, w, residual, self.tp_group)

@@ -24,6 +24,9 @@ void grad_sq_norm(torch::Tensor grad, torch::Tensor out);
 void adamw_step(torch::Tensor master, torch::Tensor grad, torch::Tensor m, torch::Tensor v, torch::Tensor param,
                 double lr, double beta1, double beta2, double eps, double wd, int64_t step,
                 c10::optional<torch::Tensor> sq_norm, double max_norm, double grad_scale);
+torch::Tensor paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                                     torch::Tensor block_tables, torch::Tensor seq_lens, int64_t max_len,
+                                     double scale);
 }  // namespace libra
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -40,4 +43,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("logprob_bwd_", &libra::logprob_bwd_);
   m.def("grad_sq_norm", &libra::grad_sq_norm);
   m.def("adamw_step", &libra::adamw_step);
+  m.def("paged_decode_attention", &libra::paged_decode_attention);
 }

@@ -51,9 +51,19 @@ struct Cfg {
   static constexpr int kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + kBarBytes;
 };
 
-__device__ __forceinline__ void tile_coords(int tile, int num_n, int& mb, int& nb) {
-  mb = tile / num_n;
-  nb = tile - mb * num_n;
+// Grouped rasterisation: consecutive tiles (which run concurrently on the
+// persistent CTAs) cover kGroupM M-blocks x a few N-blocks, so both operand
+// panels of a wave stay in L2 instead of re-streaming the larger operand.
+constexpr int kGroupM = 16;
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+  const int per_group = kGroupM * num_n;
+  const int group = tile / per_group;
+  const int first_m = group * kGroupM;
+  const int gm = min(num_m - first_m, kGroupM);
+  const int in = tile - group * per_group;
+  mb = first_m + in % gm;
+  nb = in / gm;
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
@@ -109,7 +119,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         int mb, nb;
-        tile_coords(tile, num_n, mb, nb);
+        tile_coords(tile, num_m, num_n, mb, nb);
         const int m0 = mb * BM, n0 = nb * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, err, kTimeoutSmemEmpty)) { ok = false; break; }
@@ -184,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       int mb, nb;
-      tile_coords(tile, num_n, mb, nb);
+      tile_coords(tile, num_m, num_n, mb, nb);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, err, kTimeoutTmemFull)) break;

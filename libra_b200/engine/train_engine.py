@@ -370,6 +370,17 @@ class B200TrainEngine:
         return {"loss": v[0] / n, "pg_loss": v[1] / n, "kl": v[2] / n, "reward_sum": v[3], "n_samples": v[4],
                 "n_updates": v[5], "reward_mean": v[3] / max(v[4], 1.0), "grad_norm": v[6] / n}
 
+    def release_optimizer_state(self) -> None:
+        """Drop master/Adam/gradient buffers (inference-only holders of the weights)."""
+        self.master = self.exp_avg = self.exp_avg_sq = None
+        self.grad_shard = None
+        self.flat_grad = torch.zeros(0, dtype=torch.float32, device=self.device)
+        for p in self.params.values():
+            p.main_grad = None
+            p.requires_grad_(False)
+        if self.device.type == "cuda":
+            torch.cuda.empty_cache()
+
     # ------------------------------------------------------------------ weights
     def state_dict(self) -> Dict[str, torch.Tensor]:
         return {k: v.detach() for k, v in self.params.items()}

@@ -335,15 +335,30 @@ class B200TrainEngine:
         return self._reduce_stats(out)
 
     # ------------------------------------------------------------------ gradients/optimizer
+    def _gloo(self) -> bool:
+        return dist.get_backend(self.dp_group) == "gloo"
+
     def _reduce_gradients(self) -> None:
+        """DP gradient reduction: reduce-scatter (distributed optimizer) or all-reduce."""
         if self.dp_size <= 1 or not dist.is_initialized():
             return
         if self.sharded:
-            dist.reduce_scatter_tensor(self.grad_shard, self.flat_grad, op=dist.ReduceOp.SUM, group=self.dp_group)
+            if self._gloo():  # gloo has no reduce_scatter_tensor
+                dist.all_reduce(self.flat_grad, op=dist.ReduceOp.SUM, group=self.dp_group)
+                self.grad_shard.copy_(self.flat_grad[self.shard_start:self.shard_start + self.shard_numel])
+            else:
+                dist.reduce_scatter_tensor(self.grad_shard, self.flat_grad, op=dist.ReduceOp.SUM, group=self.dp_group)
             self.grad_shard.div_(self.dp_size)
         else:
             dist.all_reduce(self.flat_grad, op=dist.ReduceOp.SUM, group=self.dp_group)
             self.flat_grad.div_(self.dp_size)
+
+    def _gather_params(self, shard_param: torch.Tensor) -> None:
+        if self._gloo():
+            parts = list(self.flat_param.chunk(self.dp_size))
+            dist.all_gather(parts, shard_param.clone(), group=self.dp_group)
+            return
+        dist.all_gather_into_tensor(self.flat_param, shard_param.clone(), group=self.dp_group)
 
     def _optimizer_step(self) -> None:
         self.step_count += 1
@@ -357,7 +372,7 @@ class B200TrainEngine:
                        beta1=o.betas[0], beta2=o.betas[1], eps=o.eps, weight_decay=o.weight_decay,
                        step=self.step_count, max_grad_norm=o.max_grad_norm, sq_norm=self.sq_norm)
         if self.sharded:
-            dist.all_gather_into_tensor(self.flat_param, shard_param.clone(), group=self.dp_group)
+            self._gather_params(shard_param)
 
     def _reduce_stats(self, stats: Dict[str, float]) -> Dict[str, float]:
         if self.dp_size <= 1 or not dist.is_initialized():

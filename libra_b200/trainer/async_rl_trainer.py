@@ -1,0 +1,500 @@
+"""Asynchronous GRPO trainer (the orchestrator).
+
+Step structure follows the reference (``trainer/async_rl_trainer.py:741-1022``):
+collect complete GRPO groups through the staleness-bounded dispatcher ->
+distribute to data-parallel ranks -> group-normalised advantages -> logprob
+recompute -> ``grpo_update`` -> (every ``sync_interval`` steps) drain rollouts,
+sync weights, bump the policy version, resume -> history / phase trace ->
+Global Resource Planner -> periodic checkpoint.
+
+Single-box process model:
+
+* one trainer process per training GPU (torchrun); NCCL between training GPUs,
+  gloo on CPU;
+* rollout instances are either in-process engines on the rollout GPUs owned by
+  rank 0 (``rollout_backend: native``), HTTP servers (``vllm`` / ``http``), or
+  mocks.  With in-process engines rank 0 is the only batch source: it collects
+  the global batch and scatters the data-parallel slices;
+* weight sync for in-process engines is a device-to-device copy of the
+  trainer's parameters into each instance's buffers (NVLink peer copies); for
+  HTTP instances the trainer writes a versioned HF export and calls
+  ``/reload_weights`` on every instance.
+"""
+
+from __future__ import annotations
+
+import copy
+import datetime
+import itertools
+import json
+import os
+import threading
+import time
+from collections import defaultdict
+from concurrent.futures import Future, ThreadPoolExecutor
+from pathlib import Path
+from typing import Any, Dict, List, Optional
+
+import torch
+import torch.distributed as dist
+
+from libra_b200.config import AsyncRLConfig
+from libra_b200.infra.execution.async_runner import AsyncTaskRunner
+from libra_b200.infra.execution.batch_dispatcher import BatchTaskDispatcher, TaskInput
+from libra_b200.infra.observability.history_collector import HistoryDataCollector
+from libra_b200.infra.observability.phase_tracer import PhaseTracer
+from libra_b200.infra.sync.staleness import StalenessManager
+
+
+def compute_group_advantages(trajectories: List[Dict[str, Any]]) -> Dict[str, float]:
+    """(r - mean) / (std + 1e-6) within each GRPO group; zero-variance groups -> 0;
+    singleton groups keep the raw reward (reference ``trainer/async_rl_trainer.py:557-598``)."""
+    groups: Dict[str, List[int]] = defaultdict(list)
+    for i, t in enumerate(trajectories):
+        r = t["rewards"].reshape(-1)
+        if r.numel() != 1:
+            raise ValueError("The current GRPO implementation requires exactly one outcome reward per trajectory")
+        groups[str(t.get("grpo_group_id", f"singleton:{i}"))].append(i)
+    zero_var = singles = 0
+    for idx in groups.values():
+        scores = torch.stack([trajectories[i]["rewards"].reshape(-1).float()[0] for i in idx])
+        if len(idx) == 1:
+            adv = scores
+            singles += 1
+        else:
+            std = scores.std()
+            if not torch.isfinite(std) or std <= 1e-6:
+                adv = torch.zeros_like(scores)
+                zero_var += 1
+            else:
+                adv = (scores - scores.mean()) / (std + 1e-6)
+        for i, a in zip(idx, adv):
+            trajectories[i]["advantages"] = a.reshape(1)
+    return {"grpo_num_groups": len(groups), "grpo_mean_group_size": len(trajectories) / max(len(groups), 1),
+            "grpo_singleton_groups": singles, "grpo_zero_variance_groups": zero_var}
+
+
+class AsyncRLTrainer:
+    def __init__(self, config: AsyncRLConfig, train_engine=None, rollout_engine=None):
+        self.config = config
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.world_size = int(os.environ.get("WORLD_SIZE", "1"))
+        self.is_main_process = self.rank == 0
+        self.train_engine = train_engine
+        self.rollout_engine = rollout_engine
+        self._local_engines: List[Any] = []
+        self.staleness_manager: Optional[StalenessManager] = None
+        self.async_runner: Optional[AsyncTaskRunner] = None
+        self.dispatcher: Optional[BatchTaskDispatcher] = None
+        self.workflow = None
+        self.global_step = 0
+        self.stats: Dict[str, Any] = {}
+        self.start_step = int(os.environ.get("RL_TRAIN_START_STEP", "0") or 0)
+        self.initial_model_version = int(os.environ.get("RL_INITIAL_MODEL_VERSION", str(self.start_step))
+                                         or self.start_step)
+        self._task_counter = itertools.count()
+        self._pending_groups: Dict[str, List[Dict[str, Any]]] = {}
+        self._advantage_stats: Dict[str, float] = {}
+        self.history_collector: Optional[HistoryDataCollector] = None
+        self.global_resource_planner = None
+        self.runtime_elastic_executor = None
+        self._grp_pool: Optional[ThreadPoolExecutor] = None
+        self._grp_future: Optional[Future] = None
+        trace = os.environ.get("RL_TRAIN_PHASE_TRACE", "0") == "1" or bool(config.phase_trace_enabled)
+        trace_dir = (os.environ.get("RL_TRAIN_PHASE_TRACE_DIR", "") or config.phase_trace_dir
+                     or os.path.join(config.log_dir, "phase_trace"))
+        self._tracer = PhaseTracer(Path(trace_dir) / f"phase_trace_rank{self.rank}.jsonl", rank=self.rank,
+                                   world_size=self.world_size) if trace else None
+        self._single_batch_source = False
+
+    # ================================================================== setup
+    def _trace(self, step: int, name: str, **details) -> None:
+        if self._tracer is None:
+            return
+        if name.endswith("_start"):
+            self._tracer.start(step, name[:-6], details)
+        elif name.endswith("_done"):
+            self._tracer.end(step, name[:-5], details)
+
+    def _init_distributed(self) -> None:
+        if self.world_size <= 1 or (dist.is_available() and dist.is_initialized()):
+            return
+        timeout = datetime.timedelta(seconds=float(os.environ.get("TORCH_DISTRIBUTED_TIMEOUT", "1800")))
+        use_cuda = torch.cuda.is_available() and os.environ.get("DIST_BACKEND", "") != "gloo"
+        if use_cuda:
+            torch.cuda.set_device(self.local_rank)
+        dist.init_process_group("nccl" if use_cuda else "gloo", timeout=timeout)
+
+    def _check_preflight(self) -> None:
+        p = self.config.global_resource_planner
+        if p.enabled and p.initial_allocation_strategy == "grp" and not p.initial_allocation_applied:
+            raise RuntimeError("global_resource_planner.initial_allocation_strategy='grp' requires the GRP "
+                               "preflight plan (PreflightPlanner) to be applied before training starts")
+
+    def _make_local_engine(self, inst) -> Any:
+        """In-process rollout instance on the first GPU of ``inst.gpus`` with its own weight copy."""
+        from libra_b200.engine.rollout.llm_engine import LLMEngine
+        from libra_b200.engine.rollout_engine import LocalRolloutEngine
+        from libra_b200.engine.tokenizer import load_tokenizer
+
+        eng = self.train_engine
+        if torch.cuda.is_available() and getattr(inst, "gpus", None):
+            dev = torch.device("cuda", int(inst.gpus[0]) % torch.cuda.device_count())
+        else:
+            dev = eng.device
+        params = {k: v.detach().to(dev, copy=True) for k, v in eng.params.items()}
+        tok = load_tokenizer(self.config.tokenizer_path, eng.cfg.vocab_size)
+        llm = LLMEngine(eng.cfg, params, instance_id=getattr(inst, "instance_id", "") or f"local-{dev}",
+                        kv_memory_fraction=float(self.config.heterogeneous_rollout.gpu_memory_utilization) * 0.5,
+                        eos_token_id=None, max_model_len=int(self.config.max_seq_length) or 0)
+        llm.version = eng.get_version()
+        self._local_engines.append(llm)
+        return LocalRolloutEngine(llm, tok)
+
+    def _build_rollout_engine(self) -> None:
+        from libra_b200.engine.heterogeneous_engine import HeterogeneousRolloutEngine
+        from libra_b200.engine.rollout_engine import HTTPRolloutEngine, MockRolloutEngine, MultiInstanceRolloutEngine
+
+        c = self.config
+        native = c.rollout_backend in ("native", "local")
+        self._single_batch_source = native and self.world_size > 1
+        if native and not self.is_main_process:
+            return  # rank 0 owns the in-process rollout pool
+        if c.heterogeneous_rollout.enabled and c.heterogeneous_rollout.instances:
+            self.rollout_engine = HeterogeneousRolloutEngine.from_config(c, engine_factory=self._make_local_engine)
+        elif c.rollout_backend == "mock":
+            self.rollout_engine = MockRolloutEngine()
+        elif native:
+            from types import SimpleNamespace
+
+            gpus = [int(x) for x in c.rollout_gpu_ids.split(",") if x.strip()] if c.rollout_gpu_ids else []
+            self.rollout_engine = self._make_local_engine(SimpleNamespace(gpus=gpus, instance_id="native-0"))
+        else:
+            n = max(1, c.vllm_num_instances)
+            eps = [e.strip() for e in c.vllm_endpoints.split(",") if e.strip()] or \
+                  [f"{c.vllm_host}:{c.vllm_port + i}" for i in range(n)]
+            self.rollout_engine = MultiInstanceRolloutEngine(
+                [HTTPRolloutEngine(e.split(":")[0], int(e.split(":")[1]), c.model_path) for e in eps])
+
+    def setup(self, workflow) -> None:
+        self._check_preflight()
+        self._init_distributed()
+        self.workflow = workflow
+        if self.train_engine is None:
+            from libra_b200.engine.train_engine import create_train_engine
+
+            self.train_engine = create_train_engine(self.config)
+            self.train_engine.initialize(max_seq_length=self.config.max_seq_length)
+        self.train_engine.set_version(self.initial_model_version)
+        if self.rollout_engine is None:
+            self._build_rollout_engine()
+        if self.rollout_engine is not None and hasattr(self.rollout_engine, "wait_for_ready"):
+            self.rollout_engine.wait_for_ready(float(self.config.heterogeneous_rollout.startup_timeout))
+        if self._is_batch_source():
+            local = self._collect_size()
+            self.staleness_manager = StalenessManager(self.train_engine, self.config.max_concurrent_rollouts, local,
+                                                      self.config.max_head_offpolicyness)
+            self.async_runner = AsyncTaskRunner(max_queue_size=self.config.queue_size,
+                                                enable_tracing=self.config.enable_rollout_tracing)
+            self.async_runner.initialize()
+            self.dispatcher = BatchTaskDispatcher(self.async_runner, self.staleness_manager,
+                                                  self._create_rollout_task, self.config.enable_rollout_tracing)
+            self.dispatcher.initialize()
+        if self.is_main_process and self.config.enable_history_collection:
+            out = self.config.history_output_dir or os.path.join(self.config.log_dir, "history")
+            p = self.config.global_resource_planner
+            self.history_collector = HistoryDataCollector(
+                out, self.config.history_save_raw_lengths, self.config.history_flush_interval,
+                self.config.history_experiment_name,
+                (p.runtime_length_profile_jsonl or os.path.join(out, "runtime_length_profile.jsonl"))
+                if p.runtime_length_profile_enabled else "")
+            self.history_collector.initialize()
+        if self.is_main_process and self.config.global_resource_planner.enabled:
+            from libra_b200.infra.cost_model.global_resource_planner import GlobalResourcePlanner
+
+            self.global_resource_planner = GlobalResourcePlanner.from_config(self.config)
+            if self.config.global_resource_planner.runtime_async_planning:
+                self._grp_pool = ThreadPoolExecutor(max_workers=1, thread_name_prefix="grp")
+
+    def _is_batch_source(self) -> bool:
+        if self._single_batch_source:
+            return self.is_main_process
+        return self.train_engine.is_batch_source()
+
+    def _collect_size(self) -> int:
+        if self._single_batch_source:
+            return int(self.config.batch_size)
+        return self.train_engine.get_local_batch_size(self.config.batch_size)
+
+    # ================================================================== rollout tasks
+    def _create_rollout_task(self, task_input: TaskInput):
+        workflow, sm, eng = self.workflow, self.staleness_manager, self.train_engine
+        max_stale = self.config.max_head_offpolicyness
+
+        async def _execute():
+            try:
+                traj = await workflow.run_episode(self.rollout_engine, task_input.data, version=task_input.version,
+                                                  rollout_index=task_input.rollout_index)
+                traj["grpo_group_id"] = task_input.group_id or f"task:{task_input.task_id}"
+                traj["grpo_rollout_index"] = task_input.rollout_index
+                v = int(traj.get("versions", torch.tensor([task_input.version])).min())
+                if eng.get_version() - v <= max_stale:
+                    sm.on_rollout_accepted()
+                    return traj
+                sm.on_rollout_rejected()
+                return None
+            except Exception as exc:  # noqa: BLE001 - a failed rollout is a rejected rollout
+                sm.on_rollout_rejected()
+                if self.is_main_process:
+                    print(f"ERROR: Rollout task_id={task_input.task_id} failed: {exc}")
+                return None
+
+        return _execute
+
+    def _data_generator(self, dataset):
+        n = int(self.config.n_samples)
+        if n < 1:
+            raise ValueError(f"n_samples must be positive; got {n}")
+        dp_rank = 0 if self._single_batch_source else self.train_engine.get_data_parallel_rank()
+        dp_size = 1 if self._single_batch_source else self.train_engine.get_data_parallel_world_size()
+        g = torch.Generator().manual_seed(int(self.config.seed))
+        for epoch in itertools.count():
+            order = torch.randperm(len(dataset), generator=g).tolist()[dp_rank::dp_size]
+            for sample_index, idx in enumerate(order):
+                item = dataset[idx]
+                if not isinstance(item, dict):
+                    raise TypeError("GRPO items must be dictionaries so that a stable group ID can be attached")
+                gid = f"dp{dp_rank}:epoch{epoch}:sample{sample_index}"
+                for r in range(n):
+                    yield TaskInput(task_id=next(self._task_counter), data=item, version=self.train_engine.get_version(),
+                                    group_id=gid, rollout_index=r)
+
+    def _collect_complete_grpo_batch(self, data_gen, batch_size: int) -> List[Dict[str, Any]]:
+        n = int(self.config.n_samples)
+        p = self.config.global_resource_planner
+        timeout = float(p.runtime_batch_collection_timeout_s)
+        retries_left = int(p.runtime_batch_collection_max_retries)
+        chosen: List[Dict[str, Any]] = []
+        while len(chosen) < batch_size:
+            try:
+                raw = self.dispatcher.active_submit_and_wait(data_gen, batch_size, timeout if timeout > 0 else None)
+            except TimeoutError:
+                self.dispatcher.reset_after_reconfigure()
+                if retries_left <= 0:
+                    raise
+                retries_left -= 1
+                continue
+            self.staleness_manager.on_batch_consumed(len(raw))
+            for t in raw:
+                self._pending_groups.setdefault(str(t["grpo_group_id"]), []).append(t)
+            for gid in list(self._pending_groups):
+                members = self._pending_groups[gid]
+                if len(members) < n:
+                    continue
+                if batch_size - len(chosen) < n:
+                    break
+                chosen.extend(members[:n])
+                del self._pending_groups[gid]
+            while len(self._pending_groups) > max(64, batch_size * 8):
+                del self._pending_groups[next(iter(self._pending_groups))]
+        return chosen
+
+    def _distribute(self, batch):
+        """Scatter data-parallel slices (whole groups) when rank 0 is the only batch source."""
+        if not self._single_batch_source:
+            return self.train_engine.distribute_trajectories(batch)
+        world = self.world_size
+        payload = [None]
+        if self.is_main_process:
+            per = len(batch) // world
+            payload = [[batch[r * per:(r + 1) * per] for r in range(world)]]
+        dist.broadcast_object_list(payload, src=0)
+        return payload[0][self.rank]
+
+    # ================================================================== weight sync
+    def _sync_weights(self, target_version: int) -> float:
+        """Push the trainer's weights to every rollout instance; returns seconds."""
+        t0 = time.perf_counter()
+        if self._local_engines:
+            # in-process instances: device-to-device copies (NVLink peer copies across GPUs)
+            src = {k: v.detach() for k, v in self.train_engine.params.items()}
+            for llm in self._local_engines:
+                llm.update_weights(src, version=target_version)
+        elif self.config.rollout_backend not in ("mock",) and (
+                self.config.rollout_weight_sync_mode != "none" or self.config.require_rollout_weight_sync):
+            self._sync_weights_disk(target_version)
+        return time.perf_counter() - t0
+
+    def _sync_weights_disk(self, version: int) -> None:
+        from libra_b200.engine.checkpointing import DistributedCheckpointManager
+
+        mgr = DistributedCheckpointManager(self.config.sync_path)
+        vdir = mgr.save(self.train_engine, version, export_for_rollout=True,
+                        include_optimizer=False, export_only=self.config.rollout_weight_sync_export_only)
+        if self.is_main_process and self.rollout_engine is not None:
+            from libra_b200.infra.sync.weight_sync import reload_http_instances
+
+            reload_http_instances(self.rollout_engine, str(vdir), version,
+                                  timeout=self.config.rollout_weight_sync_timeout_s)
+
+    # ================================================================== main loop
+    def train(self, workflow, dataset=None) -> Dict[str, Any]:
+        self.setup(workflow)
+        if dataset is None:
+            raise ValueError("dataset cannot be None")
+        c = self.config
+        if not 0 <= self.start_step < c.total_steps:
+            raise ValueError(f"RL_TRAIN_START_STEP must be in [0, total_steps): start_step={self.start_step}, "
+                             f"total_steps={c.total_steps}")
+        gen = self._data_generator(dataset) if self._is_batch_source() else None
+        local = self.train_engine.get_local_batch_size(c.batch_size)
+        if local % int(c.n_samples):
+            raise ValueError(f"Each data-parallel replica's local batch size must be divisible by n_samples: "
+                             f"local_batch_size={local}, n_samples={c.n_samples}")
+        t_start = time.time()
+        for step in range(self.start_step, c.total_steps):
+            self.global_step = step
+            t_step = time.time()
+            self._trace(step, "step_start")
+            if hasattr(self.rollout_engine, "on_epoch_start"):
+                self.rollout_engine.on_epoch_start(step)
+            batch = None
+            if self._is_batch_source():
+                self._trace(step, "collect_batch_start")
+                batch = self._collect_complete_grpo_batch(gen, self._collect_size())
+                self._trace(step, "collect_batch_done", batch_size=len(batch))
+            if batch is not None:
+                self._advantage_stats = compute_group_advantages(batch)
+            self._trace(step, "distribute_start")
+            batch = self._distribute(batch)
+            self._trace(step, "distribute_done", batch_size=len(batch or []))
+            if not batch:
+                continue
+            batch = self.train_engine.align_distributed_trajectories(batch)
+            rollout_time = time.time() - t_step
+            t_adv = time.time()
+            if not self._advantage_stats:
+                self._advantage_stats = compute_group_advantages(batch)
+            advantage_time = time.time() - t_adv
+            recompute_time = 0.0
+            if c.recompute_logprobs:
+                t_r = time.time()
+                self._trace(step, "recompute_logprobs_start")
+                self.train_engine.recompute_logprobs(batch)
+                recompute_time = time.time() - t_r
+                self._trace(step, "recompute_logprobs_done", seconds=f"{recompute_time:.3f}")
+            t_train = time.time()
+            self._trace(step, "grpo_update_start")
+            stats = self.train_engine.grpo_update(batch, ppo_epochs=c.ppo_epochs)
+            rewards = torch.cat([t["rewards"].reshape(-1).float() for t in batch])
+            stats.update({"reward_mean": float(rewards.mean()), "reward_std": float(rewards.std(unbiased=False)),
+                          "reward_min": float(rewards.min()), "reward_max": float(rewards.max())})
+            train_time = time.time() - t_train
+            self._trace(step, "grpo_update_done", seconds=f"{train_time:.3f}")
+            sync_time = 0.0
+            if c.sync_interval > 0 and (step + 1) % c.sync_interval == 0:
+                self._trace(step, "weight_sync_start")
+                if self.dispatcher is not None:
+                    self.dispatcher.pause()
+                    self.dispatcher.wait_until_idle(timeout=float(c.rollout_weight_sync_timeout_s))
+                if self.world_size > 1:
+                    dist.barrier()
+                sync_time = self._sync_weights(step + 1)
+                self.train_engine.set_version(step + 1)
+                if self.dispatcher is not None:
+                    self.dispatcher.resume()
+                self._trace(step, "weight_sync_done", seconds=f"{sync_time:.3f}")
+            step_time = time.time() - t_step
+            stats.update({"n_trajectories": len(batch), "rollout_time": rollout_time, "train_time": train_time,
+                          "weight_sync_time": sync_time, "advantage_time": advantage_time,
+                          "recompute_logprob_time": recompute_time, "step_time": step_time,
+                          "version": self.train_engine.get_version(), **self._advantage_stats})
+            self._advantage_stats = {}
+            self.stats = stats
+            if self.is_main_process:
+                self._record_history(step, batch, stats)
+                self._run_planner(step, batch, stats)
+                if hasattr(self.rollout_engine, "on_epoch_end"):
+                    self.rollout_engine.on_epoch_end(step)
+                if step % 10 == 0 or c.total_steps <= 10 or step == c.total_steps - 1:
+                    print(f"Step {step}/{c.total_steps}: {time.time() - t_start:.1f}s loss={stats.get('loss', 0):.4f} "
+                          f"kl={stats.get('kl', 0):.4f} reward={stats['reward_mean']:.3f} "
+                          f"n={len(batch)} rollout={rollout_time:.2f}s train={train_time:.2f}s", flush=True)
+            if c.save_interval > 0 and (step + 1) % c.save_interval == 0:
+                self._save_checkpoint(step)
+        self.shutdown()
+        return self.stats
+
+    # ================================================================== bookkeeping
+    def _record_history(self, step: int, batch, stats) -> None:
+        if self.history_collector is None:
+            return
+        seqs = [{"input_len": int(t.get("prompt_len", 0)), "output_len": int(t.get("output_len", 0)),
+                 "prompt_id": str(t.get("prompt_id", "")), "total_output_tokens": int(t.get("total_output_tokens",
+                                                                                            t.get("output_len", 0))),
+                 "tool_returns": t.get("tool_events", [])} for t in batch]
+        sm = self.staleness_manager.get_stats() if self.staleness_manager else None
+        self.history_collector.record_step(
+            step, sequence_records=seqs, rollout_time=stats["rollout_time"], train_time=stats["train_time"],
+            weight_sync_time=stats["weight_sync_time"], advantage_time=stats["advantage_time"],
+            recompute_logprob_time=stats["recompute_logprob_time"], step_total_time=stats["step_time"],
+            training_stats=stats, pipeline_running=getattr(sm, "running", 0),
+            pipeline_accepted=getattr(sm, "accepted", 0), pipeline_rejected=getattr(sm, "rejected", 0),
+            model_version=self.train_engine.get_version(),
+            resource_config=HistoryDataCollector.snapshot_resource_config(self.config))
+
+    def _run_planner(self, step: int, batch, stats) -> None:
+        grp = self.global_resource_planner
+        if grp is None:
+            return
+        if self._grp_future is not None and self._grp_future.done():
+            decision = self._grp_future.result()
+            self._grp_future = None
+            self._apply_decision(decision)
+        grp.observe_batch([{"input_len": t.get("prompt_len", 0), "output_len": t.get("output_len", 0)} for t in batch])
+        metrics = grp.observe_runtime(step=step, dispatcher_metrics=self.dispatcher.get_runtime_metrics()
+                                      if self.dispatcher else {},
+                                      step_stats={"rollout_time": stats["rollout_time"],
+                                                  "train_time": stats["train_time"], "step_time": stats["step_time"],
+                                                  "max_concurrent_rollouts": self.config.max_concurrent_rollouts})
+        cfg = copy.deepcopy(self.config)
+        if self._grp_pool is not None:
+            if self._grp_future is None:
+                self._grp_future = self._grp_pool.submit(grp.plan_if_needed, step, cfg, None, metrics)
+        else:
+            self._apply_decision(grp.plan_if_needed(step, cfg, None, metrics))
+
+    def _apply_decision(self, decision) -> None:
+        self.last_planner_decision = decision
+        log = os.path.join(self.config.log_dir, "global_resource_planner_decisions.jsonl")
+        os.makedirs(self.config.log_dir, exist_ok=True)
+        with open(log, "a", encoding="utf-8") as fh:
+            fh.write(json.dumps(decision.to_dict(), default=str) + "\n")
+        if decision.should_reconfigure and self.runtime_elastic_executor is not None:
+            self.runtime_elastic_executor.execute(decision)
+
+    def _save_checkpoint(self, step: int) -> None:
+        from libra_b200.engine.checkpointing import DistributedCheckpointManager
+
+        mgr = DistributedCheckpointManager(os.path.join(self.config.log_dir, "checkpoints"))
+        mgr.save(self.train_engine, step + 1, export_for_rollout=False)
+        if self.is_main_process:
+            light = {"step": step, "version": self.train_engine.get_version(),
+                     "stats": {k: v for k, v in self.stats.items() if isinstance(v, (int, float, str))},
+                     "config": self.config.to_dict()}
+            torch.save(light, os.path.join(self.config.log_dir, "checkpoints", f"step_{step}.pt"))
+            mgr.prune(self.config.keep_latest_checkpoints, protect=self.start_step or None)
+
+    def shutdown(self) -> None:
+        if self.dispatcher is not None:
+            self.dispatcher.destroy()
+            self.dispatcher = None
+        for llm in self._local_engines:
+            llm.shutdown()
+        if self._grp_pool is not None:
+            self._grp_pool.shutdown(wait=False)
+        if self.history_collector is not None:
+            self.history_collector.close()
+        if self._tracer is not None:
+            self._tracer.close()

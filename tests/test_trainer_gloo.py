@@ -1,0 +1,46 @@
+"""End-to-end async GRPO plumbing: torchrun, 2 gloo ranks on CPU, tiny model."""
+
+import glob
+import json
+import os
+import socket
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _run(tmp_path, task):
+    env = dict(os.environ, DIST_BACKEND="gloo", CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="2")
+    out = tmp_path / "stats.json"
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+           "--master-port", str(_free_port()), os.path.join(ROOT, "examples", "synthetic_grpo.py"),
+           "--config", os.path.join(ROOT, "libra_b200", "configs", "tiny_cpu_gloo.yaml"), "--total-steps", "3",
+           "--log-dir", str(tmp_path), "--stats-out", str(out), "--task", task]
+    proc = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    assert proc.returncode == 0, proc.stderr[-3000:]
+    return json.loads(out.read_text())
+
+
+def test_two_rank_async_grpo_plumbing(tmp_path):
+    stats = _run(tmp_path, "target_token")
+    assert stats["n_trajectories"] == 16 and stats["version"] == 3
+    hist = glob.glob(str(tmp_path / "history" / "*history_*.jsonl"))
+    assert hist and len(open(hist[0]).read().splitlines()) == 3
+    traces = glob.glob(str(tmp_path / "phase_trace" / "phase_trace_rank*.jsonl"))
+    assert len(traces) == 2
+    phases = {json.loads(l)["phase"] for l in open(sorted(traces)[0]) if '"phase_span"' in l}
+    assert {"collect_batch", "grpo_update", "weight_sync", "recompute_logprobs"} <= phases
+
+
+def test_two_rank_agentic_multiturn(tmp_path):
+    stats = _run(tmp_path, "agentic")
+    assert stats["n_trajectories"] == 16

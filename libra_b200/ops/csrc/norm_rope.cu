@@ -59,107 +59,115 @@ __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __
 }
 
 // ------------------------------------------------------------------ RMSNorm bwd
-// Block of 256 threads per row (grid-stride over rows).  Thread t owns the
-// 8-element vectors t, t+256, ... (at most kMaxVec of them, so H <= 8*256*kMaxVec).
-constexpr int kNormThreads = 256;
-constexpr int kMaxVec = 4;  // H <= 8192
-
-__device__ __forceinline__ float block_sum_256(float v, float* scratch) {
-  v = warp_sum(v);
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  __syncthreads();
-  if (l == 0) scratch[w] = v;
-  __syncthreads();
-  float r = (l < (kNormThreads >> 5)) ? scratch[l] : 0.f;
-  return warp_sum(r);
-}
-
-__global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
-    const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
-    const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx, float* __restrict__ dw_part, int T, int H,
-    int accumulate_dx) {
-  __shared__ float scratch[32];
+// One warp per row (grid-stride over rows); lane l owns the 8-element vectors
+// l, l+32, ...  The row is read twice: pass 1 forms sum(dy*w*xhat), pass 2
+// (L1 hits) writes dx and adds dy*xhat into this warp's fp32 row of shared
+// memory.  At the end the CTA folds its warps' rows into one row of the
+// [grid, H] partial buffer, which `colsum_kernel` then reduces over CTAs.
+// Every partial row is written by its CTA, so the buffer needs no zeroing.
+__global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                                   const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
+                                   __nv_bfloat16* __restrict__ dx, float* __restrict__ dw_part, int T, int H,
+                                   int accumulate_dx) {
+  extern __shared__ float s_dw[];  // [warps, H]
+  const int warps = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nvec = H >> 3;
-  float dwacc[kMaxVec][8];
-#pragma unroll
-  for (int i = 0; i < kMaxVec; ++i)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) dwacc[i][e] = 0.f;
-  float wf[kMaxVec][8];
-#pragma unroll
-  for (int i = 0; i < kMaxVec; ++i) {
-    const int v = threadIdx.x + i * kNormThreads;
-    if (v < nvec) {
-      uint4 wu = reinterpret_cast<const uint4*>(w)[v];
-      const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wu);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) wf[i][e] = __bfloat162float(wb[e]);
-    }
-  }
-  for (int row = blockIdx.x; row < T; row += gridDim.x) {
+  for (int i = threadIdx.x; i < warps * H; i += blockDim.x) s_dw[i] = 0.f;
+  __syncthreads();
+  float* my = s_dw + (size_t)warp * H;
+  const uint4* wv = reinterpret_cast<const uint4*>(w);
+  for (int row = blockIdx.x * warps + warp; row < T; row += gridDim.x * warps) {
     const float r = rstd[row];
     const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * H);
     const uint4* gr = reinterpret_cast<const uint4*>(dy + (size_t)row * H);
-    float xh[kMaxVec][8], g[kMaxVec][8];
     float dot = 0.f;
+#pragma unroll 4
+    for (int v = lane; v < nvec; v += 32) {
+      uint4 xu = xr[v], gu = gr[v], wu = __ldg(wv + v);
+      const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xu);
+      const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&gu);
+      const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wu);
 #pragma unroll
-    for (int i = 0; i < kMaxVec; ++i) {
-      const int v = threadIdx.x + i * kNormThreads;
-      if (v < nvec) {
-        uint4 xu = xr[v], gu = gr[v];
-        const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xu);
-        const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&gu);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          xh[i][e] = __bfloat162float(xb[e]) * r;
-          g[i][e] = __bfloat162float(gb[e]);
-          dot += g[i][e] * wf[i][e] * xh[i][e];
-          dwacc[i][e] += g[i][e] * xh[i][e];
-        }
-      }
+      for (int e = 0; e < 8; ++e) dot += __bfloat162float(gb[e]) * __bfloat162float(wb[e]) * __bfloat162float(xb[e]);
     }
-    const float mean = block_sum_256(dot, scratch) / (float)H;
+    const float mean = warp_sum(dot) * r / (float)H;
     uint4* dxr = reinterpret_cast<uint4*>(dx + (size_t)row * H);
+#pragma unroll 2
+    for (int v = lane; v < nvec; v += 32) {
+      uint4 xu = xr[v], gu = gr[v], wu = __ldg(wv + v);
+      const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xu);
+      const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&gu);
+      const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wu);
+      float o[8];
+      float4* acc = reinterpret_cast<float4*>(my + v * 8);
+      float4 a0 = acc[0], a1 = acc[1];
+      float* af0 = reinterpret_cast<float*>(&a0);
+      float* af1 = reinterpret_cast<float*>(&a1);
 #pragma unroll
-    for (int i = 0; i < kMaxVec; ++i) {
-      const int v = threadIdx.x + i * kNormThreads;
-      if (v < nvec) {
-        float o[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = r * (g[i][e] * wf[i][e] - xh[i][e] * mean);
-        if (accumulate_dx) {
-          uint4 prev = dxr[v];
-          const __nv_bfloat16* pb = reinterpret_cast<const __nv_bfloat16*>(&prev);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) o[e] += __bfloat162float(pb[e]);
-        }
-        uint4 pk;
-        pk.x = pack_bf16x2(o[0], o[1]);
-        pk.y = pack_bf16x2(o[2], o[3]);
-        pk.z = pack_bf16x2(o[4], o[5]);
-        pk.w = pack_bf16x2(o[6], o[7]);
-        dxr[v] = pk;
+      for (int e = 0; e < 8; ++e) {
+        const float xh = __bfloat162float(xb[e]) * r;
+        const float g = __bfloat162float(gb[e]);
+        o[e] = r * (g * __bfloat162float(wb[e]) - xh * mean);
+        if (e < 4) af0[e] += g * xh; else af1[e - 4] += g * xh;
       }
+      acc[0] = a0;
+      acc[1] = a1;
+      if (accumulate_dx) {
+        uint4 prev = dxr[v];
+        const __nv_bfloat16* pb = reinterpret_cast<const __nv_bfloat16*>(&prev);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] += __bfloat162float(pb[e]);
+      }
+      uint4 pk;
+      pk.x = pack_bf16x2(o[0], o[1]);
+      pk.y = pack_bf16x2(o[2], o[3]);
+      pk.z = pack_bf16x2(o[4], o[5]);
+      pk.w = pack_bf16x2(o[6], o[7]);
+      dxr[v] = pk;
     }
   }
+  __syncthreads();
   float* part = dw_part + (size_t)blockIdx.x * H;
-#pragma unroll
-  for (int i = 0; i < kMaxVec; ++i) {
-    const int v = threadIdx.x + i * kNormThreads;
-    if (v < nvec) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) part[v * 8 + e] = dwacc[i][e];
-    }
+  for (int c = threadIdx.x; c < H; c += blockDim.x) {
+    float sum = 0.f;
+    for (int k = 0; k < warps; ++k) sum += s_dw[(size_t)k * H + c];
+    part[c] = sum;
   }
 }
 
-// out[c] (+)= sum_r part[r, c]
-__global__ void colsum_kernel(const float* __restrict__ part, int rows, int cols, float* __restrict__ out, int accumulate) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= cols) return;
-  float s = 0.f;
-  for (int r = 0; r < rows; ++r) s += part[(size_t)r * cols + c];
-  out[c] = accumulate ? out[c] + s : s;
+// out[c] (+)= sum_r part[r, c].  Block (32 columns x 8 row groups); each
+// thread keeps four independent partial sums, then the 8 groups are folded
+// through shared memory.
+constexpr int kColsumRowGroups = 8;
+__global__ void colsum_kernel(const float* __restrict__ part, int rows, int cols, float* __restrict__ out,
+                              int accumulate) {
+  __shared__ float red[kColsumRowGroups][33];
+  const int c = blockIdx.x * 32 + threadIdx.x;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  if (c < cols) {
+    int r = threadIdx.y;
+    const int step = kColsumRowGroups;
+    for (; r + 3 * step < rows; r += 4 * step) {
+      s0 += part[(size_t)r * cols + c];
+      s1 += part[(size_t)(r + step) * cols + c];
+      s2 += part[(size_t)(r + 2 * step) * cols + c];
+      s3 += part[(size_t)(r + 3 * step) * cols + c];
+    }
+    for (; r < rows; r += step) s0 += part[(size_t)r * cols + c];
+  }
+  red[threadIdx.y][threadIdx.x] = (s0 + s1) + (s2 + s3);
+  __syncthreads();
+  if (threadIdx.y == 0 && c < cols) {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < kColsumRowGroups; ++k) s += red[k][threadIdx.x];
+    out[c] = accumulate ? out[c] + s : s;
+  }
+}
+
+static inline void launch_colsum(const float* part, int rows, int cols, float* out, bool accumulate,
+                                 cudaStream_t st) {
+  colsum_kernel<<<(cols + 31) / 32, dim3(32, kColsumRowGroups), 0, st>>>(part, rows, cols, out, accumulate ? 1 : 0);
 }
 
 // ------------------------------------------------------------------ q/k norm + RoPE
@@ -213,7 +221,7 @@ __global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, c
 }
 
 // Backward: grid-stride warps over (token, head); q/k weight-gradient partials
-// live in registers per lane (4 values for q, 4 for k) and are written per warp.
+// live in registers per lane (4 values for q, 4 for k) and are folded per CTA.
 template <int D>
 __global__ void qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ qw,
                                         const __nv_bfloat16* __restrict__ kw, const int* __restrict__ pos,
@@ -271,10 +279,18 @@ __global__ void qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ qkv, c
       *reinterpret_cast<__nv_bfloat162*>(vd + i1) = *reinterpret_cast<const __nv_bfloat162*>(vg + i1);
     }
   }
-  // partial row layout: [q weights (D) | k weights (D)]
-  float* part = dw_part + (size_t)gw0 * 2 * D;
-  part[i0] = accq[0]; part[i0 + 1] = accq[1]; part[i1] = accq[2]; part[i1 + 1] = accq[3];
-  part[D + i0] = acck[0]; part[D + i0 + 1] = acck[1]; part[D + i1] = acck[2]; part[D + i1 + 1] = acck[3];
+  // fold the warps' partials in shared memory, then write this CTA's row of
+  // the [gridDim.x, 2D] partial buffer: [q weights (D) | k weights (D)]
+  __shared__ float s_acc[2 * D];
+  for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) s_acc[i] = 0.f;
+  __syncthreads();
+  atomicAdd(&s_acc[i0], accq[0]); atomicAdd(&s_acc[i0 + 1], accq[1]);
+  atomicAdd(&s_acc[i1], accq[2]); atomicAdd(&s_acc[i1 + 1], accq[3]);
+  atomicAdd(&s_acc[D + i0], acck[0]); atomicAdd(&s_acc[D + i0 + 1], acck[1]);
+  atomicAdd(&s_acc[D + i1], acck[2]); atomicAdd(&s_acc[D + i1 + 1], acck[3]);
+  __syncthreads();
+  float* part = dw_part + (size_t)blockIdx.x * 2 * D;
+  for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) part[i] = s_acc[i];
 }
 
 // ------------------------------------------------------------------ host wrappers
@@ -301,13 +317,30 @@ std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double 
   return {y, rstd};
 }
 
-static int norm_grid(int T) {
-  int dev, sms;
+// Warps per CTA for rmsnorm_bwd: each warp keeps an fp32 [H] row in shared
+// memory, so wide rows get fewer warps.
+static int rmsnorm_bwd_warps(int H) {
+  int w = (int)((200 * 1024) / ((size_t)H * 4));
+  return w < 1 ? 1 : (w > 8 ? 8 : w);
+}
+
+// CTAs for rmsnorm_bwd: all co-resident CTAs of one wave, but no more than the
+// rows need.
+static int rmsnorm_bwd_grid(int T, int H, int warps) {
+  int dev, sms, per_sm = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  int g = sms * 4;
-  return T < g ? (T > 0 ? T : 1) : g;
+  const size_t smem = (size_t)warps * H * 4;
+  cudaFuncSetAttribute(rmsnorm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rmsnorm_bwd_kernel, warps * 32, smem);
+  if (per_sm < 1) per_sm = 1;
+  const int need = (T + warps - 1) / warps;
+  int g = sms * per_sm;
+  if (need < g) g = need;
+  return g < 1 ? 1 : g;
 }
+
+static constexpr int kRmsnormBwdMaxH = 51200;  // one warp's fp32 row fits in 200 KB of shared memory
 
 // Returns dx (bf16).  dw (fp32, [H]) is written or accumulated in place.
 torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dw,
@@ -316,7 +349,7 @@ torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, to
   check_bf16_rowmajor(x, "rmsnorm_bwd x");
   const int H = (int)x.size(-1);
   const int T = (int)(x.numel() / H);
-  LIBRA_CHECK(H % 8 == 0 && H <= 8 * kNormThreads * kMaxVec, "rmsnorm_bwd: unsupported H");
+  LIBRA_CHECK(H % 8 == 0 && H <= kRmsnormBwdMaxH, "rmsnorm_bwd: unsupported H=%d", H);
   LIBRA_CHECK(dw.scalar_type() == at::kFloat && dw.numel() == H && dw.is_contiguous(), "rmsnorm_bwd: dw fp32 [H]");
   const c10::cuda::CUDAGuard guard(x.device());
   torch::Tensor dx;
@@ -328,19 +361,19 @@ torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, to
   } else {
     dx = torch::empty_like(x);
   }
-  const int grid = norm_grid(T);
-  auto part = torch::empty({grid, H}, x.options().dtype(at::kFloat));
   auto st = at::cuda::getCurrentCUDAStream();
-  if (T > 0) {
-    rmsnorm_bwd_kernel<<<grid, kNormThreads, 0, st>>>(
-        (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(),
-        rstd.data_ptr<float>(), (__nv_bfloat16*)dx.data_ptr(), part.data_ptr<float>(), T, H, acc_dx);
-    LIBRA_LAUNCH_CHECK();
-  } else {
-    part.zero_();
+  if (T == 0) {
+    if (!accumulate_dw) dw.zero_();
+    return dx;
   }
-  colsum_kernel<<<(H + 255) / 256, 256, 0, st>>>(part.data_ptr<float>(), grid, H, dw.data_ptr<float>(),
-                                                 accumulate_dw ? 1 : 0);
+  const int warps = rmsnorm_bwd_warps(H);
+  const int grid = rmsnorm_bwd_grid(T, H, warps);
+  auto part = torch::empty({grid, H}, x.options().dtype(at::kFloat));
+  rmsnorm_bwd_kernel<<<grid, warps * 32, (size_t)warps * H * 4, st>>>(
+      (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(),
+      rstd.data_ptr<float>(), (__nv_bfloat16*)dx.data_ptr(), part.data_ptr<float>(), T, H, acc_dx);
+  LIBRA_LAUNCH_CHECK();
+  launch_colsum(part.data_ptr<float>(), grid, H, dw.data_ptr<float>(), accumulate_dw, st);
   LIBRA_LAUNCH_CHECK();
   return dx;
 }
@@ -388,7 +421,7 @@ torch::Tensor qk_norm_rope_bwd(torch::Tensor qkv, torch::Tensor qw, torch::Tenso
   int blocks = sms * 8;
   if (blocks * warps > total) blocks = (total + warps - 1) / warps;
   if (blocks < 1) blocks = 1;
-  auto part = torch::zeros({blocks * warps, 2 * D}, qkv.options().dtype(at::kFloat));
+  auto part = torch::empty({blocks, 2 * D}, qkv.options().dtype(at::kFloat));
   auto st = at::cuda::getCurrentCUDAStream();
   if (total > 0) {
     qk_norm_rope_bwd_kernel<128><<<blocks, warps * 32, 0, st>>>(
@@ -399,7 +432,7 @@ torch::Tensor qk_norm_rope_bwd(torch::Tensor qkv, torch::Tensor qw, torch::Tenso
     LIBRA_LAUNCH_CHECK();
   }
   auto sums = torch::empty({2 * D}, qkv.options().dtype(at::kFloat));
-  colsum_kernel<<<1, 256, 0, st>>>(part.data_ptr<float>(), blocks * warps, 2 * D, sums.data_ptr<float>(), 0);
+  launch_colsum(part.data_ptr<float>(), total > 0 ? blocks : 0, 2 * D, sums.data_ptr<float>(), false, st);
   LIBRA_LAUNCH_CHECK();
   dqw.add_(sums.narrow(0, 0, D));
   dkw.add_(sums.narrow(0, D, D));

@@ -69,6 +69,24 @@ def bench_elementwise(iters: int):
     w = torch.ones(H, device="cuda", dtype=torch.bfloat16)
     ms = _time(lambda: ops.ext().rmsnorm_fwd(x, w, 1e-6), iters)
     print(json.dumps({"kernel": "rmsnorm_fwd", "T": T, "H": H, "ms": ms, "gbs": 2 * 2 * T * H / ms / 1e6}), flush=True)
+    T2 = 16384
+    xb, dy = x[:T2].contiguous(), torch.randn(T2, H, device="cuda").to(torch.bfloat16)
+    rstd = torch.rsqrt(xb.float().pow(2).mean(-1) + 1e-6).contiguous()
+    dw = torch.zeros(H, device="cuda")
+    ms = _time(lambda: ops.ext().rmsnorm_bwd(dy, xb, w, rstd, dw, False, None), iters)
+    print(json.dumps({"kernel": "rmsnorm_bwd+colsum", "T": T2, "H": H, "ms": ms,
+                      "gbs": 3 * 2 * T2 * H / ms / 1e6}), flush=True)
+    nq, nkv, D = 32, 8, 128
+    qkv = torch.randn(T2, (nq + 2 * nkv) * D, device="cuda").to(torch.bfloat16)
+    qw = torch.ones(D, device="cuda", dtype=torch.bfloat16)
+    pos = torch.arange(T2, device="cuda", dtype=torch.int32) % 4096
+    from libra_b200.ops import reference as _ref
+    cos, sin = [t.float().cuda().contiguous() for t in _ref.rope_tables(4096, D, 1e6)]
+    q, k, v, r = ops.ext().qk_norm_rope_fwd(qkv, qw, qw, pos, cos, sin, nq, nkv, 1e-6)
+    dqw, dkw = torch.zeros(D, device="cuda"), torch.zeros(D, device="cuda")
+    ms = _time(lambda: ops.ext().qk_norm_rope_bwd(qkv, qw, qw, pos, cos, sin, r, q, k, v, dqw, dkw, nq, nkv), iters)
+    print(json.dumps({"kernel": "qk_norm_rope_bwd", "T": T2, "ms": ms,
+                      "gbs": 3 * 2 * T2 * (nq + 2 * nkv) * D / ms / 1e6}), flush=True)
     F = 9728
     gu = torch.randn(T // 2, 2 * F, device="cuda").to(torch.bfloat16)
     ms = _time(lambda: ops.ext().swiglu_fwd(gu), iters)

@@ -106,6 +106,9 @@ class B200TrainEngine:
         self.model: Optional[Qwen3Model] = None
         self.last_timing: Dict[str, float] = {}
         self.io_bytes = {"h2d": 0, "d2h": 0}  # host<->device traffic of the public API calls
+        self.elastic_gradient_domain = None
+        self._pending_hybrid_gradients: List[Any] = []
+        self.elastic_update_publisher = None  # callable(reduced flat grad, step, version) for lockstep hybrids
 
     # ------------------------------------------------------------------ setup
     def initialize(self, max_seq_length: int = 2048) -> None:
@@ -321,7 +324,9 @@ class B200TrainEngine:
             loss, pg, kl = self.loss(logp, mb["old_logp"], mb["adv"], mb.get("w"))
             loss.backward()
             acc += torch.stack([loss.detach(), pg.detach(), kl.detach()])
+        self._apply_elastic_inter_replica_gradients()
         self._reduce_gradients()
+        self._publish_elastic_update()
         self._optimizer_step()
         if not sync_stats:
             return {"loss_sum": acc}
@@ -395,6 +400,127 @@ class B200TrainEngine:
             p.requires_grad_(False)
         if self.device.type == "cuda":
             torch.cuda.empty_cache()
+
+
+    # ------------------------------------------------------------------ elastic hybrid hooks
+    # Reference contract: engine/train_engine.py:854-960 (core replica ids,
+    # domain attach, payload queue, snapshot capture/load, merge before the
+    # DP reduction).  Here the whole gradient is the flat fp32 buffer, so a
+    # payload is one tensor and the merge is an in-place add into it.
+    def get_elastic_core_replica_ids(self) -> List[str]:
+        return [f"dp{i}" for i in range(max(1, getattr(self, "dp_size", self.world_size)))]
+
+    def get_elastic_core_process_group(self):
+        return self.dp_group if self.dp_group is not None else (dist.group.WORLD if dist.is_initialized() else None)
+
+    def configure_elastic_training(self, core_replica_ids: Optional[List[str]] = None,
+                                   decouple_communication_domains: bool = True):
+        from libra_b200.infra.elastic.hybrid_pool import InterReplicaGradientDomain
+
+        self.elastic_gradient_domain = InterReplicaGradientDomain(
+            core_replica_ids=core_replica_ids or self.get_elastic_core_replica_ids(),
+            process_group=None if decouple_communication_domains else self.get_elastic_core_process_group(),
+            decouple_communication_domains=decouple_communication_domains)
+        return self.elastic_gradient_domain
+
+    def set_elastic_gradient_domain(self, domain) -> None:
+        self.elastic_gradient_domain = domain
+        if domain is not None and not domain.decoupled_communication_domains:
+            domain.process_group = self.get_elastic_core_process_group()
+
+    def enqueue_hybrid_gradient_payload(self, payload) -> None:
+        self._pending_hybrid_gradients.append(payload)
+
+    def _apply_elastic_inter_replica_gradients(self) -> int:
+        """Add matching hybrid payloads into this core replica's gradient
+        before the core DP reduction; returns how many were merged."""
+        pending, self._pending_hybrid_gradients = self._pending_hybrid_gradients, []
+        if not pending or self.elastic_gradient_domain is None:
+            return 0
+        core_id = f"dp{getattr(self, 'dp_rank', 0)}"
+        used = self.elastic_gradient_domain.usable_payloads(core_id, pending, step=self.step_count + 1,
+                                                            state_version=-1)
+        for p in used:
+            (g,) = p.tensors
+            if g.numel() != self.flat_grad.numel():
+                raise ValueError(f"hybrid payload has {g.numel()} elements, expected {self.flat_grad.numel()}")
+            self.flat_grad.add_(g.to(device=self.flat_grad.device, dtype=torch.float32).view(-1))
+        return len(used)
+
+    def _publish_elastic_update(self) -> None:
+        if self.elastic_update_publisher is None:
+            return
+        if self.sharded and dist.is_initialized():
+            full = torch.empty_like(self.flat_grad)
+            if self._gloo():
+                parts = list(full.chunk(self.dp_size))
+                dist.all_gather(parts, self.grad_shard.clone(), group=self.dp_group)
+            else:
+                dist.all_gather_into_tensor(full, self.grad_shard, group=self.dp_group)
+        else:
+            full = self.flat_grad
+        self.elastic_update_publisher(full, self.step_count + 1, self.current_version)
+
+    def get_elastic_state_snapshot_path(self, version: int) -> str:
+        root = os.environ.get("ELASTIC_TRAINING_STATE_DIR", "./logs/elastic_training_state")
+        return os.path.join(root, f"v{version}", f"rank_{self.rank}.pt")
+
+    def capture_elastic_state_snapshot(self, worker_id: str = "", target_core_id: str = "") -> int:
+        """Write weights + this rank's optimizer shard for a joining replica."""
+        path = self.get_elastic_state_snapshot_path(self.current_version)
+        os.makedirs(os.path.dirname(path), exist_ok=True)
+        snap = {"flat_param": self.flat_param.cpu(), "version": self.current_version, "step": self.step_count,
+                "dp_rank": getattr(self, "dp_rank", 0), "dp_size": getattr(self, "dp_size", 1),
+                "hidden_size": self.cfg.hidden_size, "num_layers": self.cfg.num_hidden_layers}
+        if self.master is not None:
+            snap.update(master=self.master.cpu(), exp_avg=self.exp_avg.cpu(), exp_avg_sq=self.exp_avg_sq.cpu(),
+                        shard_start=self.shard_start)
+        tmp = path + ".tmp"
+        torch.save(snap, tmp)
+        os.replace(tmp, path)
+        return self.current_version
+
+    def load_elastic_state_snapshot(self, snapshot_path: str) -> int:
+        snap = torch.load(snapshot_path, map_location="cpu", weights_only=True)
+        if snap["flat_param"].numel() != self.flat_param.numel():
+            raise ValueError("elastic snapshot does not match this model's parameter layout")
+        self.flat_param.copy_(snap["flat_param"])
+        if self.master is not None and "master" in snap:
+            if snap["master"].numel() == self.master.numel():
+                self.master.copy_(snap["master"])
+                self.exp_avg.copy_(snap["exp_avg"])
+                self.exp_avg_sq.copy_(snap["exp_avg_sq"])
+            else:  # different sharding: rebuild the fp32 master from the weights, restart moments
+                self.master.copy_(self.flat_param[self.shard_start:self.shard_start + self.shard_numel].float())
+                self.exp_avg.zero_()
+                self.exp_avg_sq.zero_()
+        self.current_version = int(snap["version"])
+        self.step_count = int(snap["step"])
+        return self.current_version
+
+    def compute_gradient_payload(self, trajectories: List[Dict[str, Any]], *, replica_id: str, target_core_id: str,
+                                 step: int, membership_epoch: int, replica_rank: int = 0,
+                                 replica_world_size: int = 1, loss_scale: float = 1.0):
+        """Hybrid-replica side: forward/backward into the flat gradient, no
+        reduction and no optimizer step; the payload aliases ``flat_grad``."""
+        from libra_b200.infra.elastic.hybrid_pool import GradientPayload
+
+        self.flat_grad.zero_()
+        for hb in self.prepare_update(trajectories):
+            mb = self.to_device(hb)
+            logp = self.model.action_logprobs(mb["batch"], self.temperature)
+            loss, _, _ = self.loss(logp, mb["old_logp"], mb["adv"], mb.get("w"))
+            (loss * loss_scale).backward()
+        return GradientPayload(replica_id, target_core_id, (self.flat_grad,), False, replica_rank,
+                               replica_world_size, step, self.current_version, membership_epoch)
+
+    def apply_gradient_update(self, reduced_flat_grad: torch.Tensor) -> None:
+        """Hybrid-replica side of lockstep: take the core's post-reduce
+        gradient and run the same optimizer step, keeping weights identical."""
+        self.flat_grad.copy_(reduced_flat_grad.to(self.flat_grad.device, torch.float32).view(-1))
+        if self.sharded:
+            self.grad_shard.copy_(self.flat_grad[self.shard_start:self.shard_start + self.shard_numel])
+        self._optimizer_step()
 
     # ------------------------------------------------------------------ weights
     def state_dict(self) -> Dict[str, torch.Tensor]:

@@ -367,16 +367,23 @@ class InterReplicaGradientDomain:
         with self._lock:
             return dict(self._targets), set(self._joining), dict(self._epochs)
 
+    def usable_payloads(self, core_replica_id: str, hybrid_payloads: Iterable[GradientPayload], *, step: int = -1,
+                        state_version: int = -1) -> List[GradientPayload]:
+        """The payloads that count for ``core_replica_id`` now: target matches,
+        replica active (not joining), not a zero placeholder, membership epoch
+        current, step/state version matching when both sides give one, and
+        the payload's replica rank equal to this lane's rank."""
+        self._check_core(core_replica_id)
+        targets, joining, epochs = self._snapshot()
+        return [p for p in hybrid_payloads
+                if self._usable(p, core_replica_id, targets, joining, epochs, step, state_version, True)]
+
     def accumulate_local_gradients(self, *, core_replica_id: str, core_gradients: Iterable[torch.Tensor],
                                    hybrid_payloads: Iterable[GradientPayload] = (), step: int = -1,
                                    state_version: int = -1) -> Tuple[torch.Tensor, ...]:
         """core gradients + every matching hybrid payload for this core replica."""
-        self._check_core(core_replica_id)
         out = [t.clone() for t in core_gradients]
-        targets, joining, epochs = self._snapshot()
-        for p in hybrid_payloads:
-            if not self._usable(p, core_replica_id, targets, joining, epochs, step, state_version, True):
-                continue
+        for p in self.usable_payloads(core_replica_id, hybrid_payloads, step=step, state_version=state_version):
             if len(p.tensors) != len(out):
                 raise ValueError("hybrid payload tensor count mismatch")
             for i, extra in enumerate(p.tensors):

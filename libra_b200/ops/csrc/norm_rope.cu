@@ -13,7 +13,12 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <cstdio>
+#include <cstdint>
+#include <mutex>
+
 #include "common.cuh"
+#include "libra_noalloc.h"
 
 namespace libra {
 
@@ -440,3 +445,83 @@ torch::Tensor qk_norm_rope_bwd(torch::Tensor qkv, torch::Tensor qw, torch::Tenso
 }
 
 }  // namespace libra
+
+// ------------------------------------------------------------------ RMSNorm bwd without allocation
+// C entry point declared in libra_noalloc.h.  Same math and kernels as
+// libra::rmsnorm_bwd; the [grid, H] weight-gradient partials live in the
+// file-scope device array below instead of a torch allocation, and the grid is
+// capped so that grid * H fits in it.
+namespace {
+
+constexpr size_t kNoAllocScratchFloats = 512 * 1024;  // 2 MiB of fp32 partials per device
+__device__ __align__(256) float g_rmsnorm_bwd_scratch[kNoAllocScratchFloats];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+float* g_noalloc_scratch_ptr[kNoAllocMaxDevices] = {};
+thread_local char g_noalloc_error[256] = "";
+
+int noalloc_fail(int code, const char* msg) {
+  std::snprintf(g_noalloc_error, sizeof(g_noalloc_error), "%s", msg);
+  return code;
+}
+
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) const char* libra_rmsnorm_bwd_noalloc_error(void) {
+  return g_noalloc_error;
+}
+
+extern "C" __attribute__((visibility("default"))) int libra_rmsnorm_bwd_noalloc(
+    const void* dy, const void* x, const void* w, const float* rstd, void* dx, float* dw, int T, int H,
+    int accumulate_dx, int accumulate_dw, cudaStream_t stream) {
+  using namespace libra;
+  g_noalloc_error[0] = 0;
+  if (T < 0 || H <= 0 || H % 8 != 0) return noalloc_fail(1, "libra_rmsnorm_bwd_noalloc: need T >= 0 and H a positive multiple of 8");
+  if ((size_t)H > kNoAllocScratchFloats || H > kRmsnormBwdMaxH)
+    return noalloc_fail(2, "libra_rmsnorm_bwd_noalloc: H exceeds the no-alloc limit (H <= 51200)");
+  if (!dw || (T > 0 && (!dy || !x || !w || !rstd || !dx)))
+    return noalloc_fail(1, "libra_rmsnorm_bwd_noalloc: null pointer argument");
+  const uintptr_t align_or = (uintptr_t)dy | (uintptr_t)x | (uintptr_t)w | (uintptr_t)dx;
+  if (T > 0 && (align_or & 15u)) return noalloc_fail(1, "libra_rmsnorm_bwd_noalloc: dy/x/w/dx must be 16-byte aligned");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices)
+    return noalloc_fail(3, "libra_rmsnorm_bwd_noalloc: no usable current CUDA device");
+  float* scratch = nullptr;
+  {
+    // first call on each device: resolve the scratch array's address once,
+    // with that device current
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_scratch_ptr[dev]) {
+      void* p = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&p, g_rmsnorm_bwd_scratch);
+      if (e != cudaSuccess || !p) {
+        char msg[200];
+        std::snprintf(msg, sizeof(msg), "libra_rmsnorm_bwd_noalloc: cudaGetSymbolAddress failed: %s",
+                      cudaGetErrorString(e));
+        return noalloc_fail(3, msg);
+      }
+      g_noalloc_scratch_ptr[dev] = static_cast<float*>(p);
+    }
+    scratch = g_noalloc_scratch_ptr[dev];
+  }
+  if (T == 0) {
+    colsum_kernel<<<(H + 31) / 32, dim3(32, kColsumRowGroups), 0, stream>>>(scratch, 0, H, dw, accumulate_dw ? 1 : 0);
+  } else {
+    const int warps = rmsnorm_bwd_warps(H);
+    int grid = rmsnorm_bwd_grid(T, H, warps);
+    const int cap = (int)(kNoAllocScratchFloats / (size_t)H);
+    if (grid > cap) grid = cap;
+    rmsnorm_bwd_kernel<<<grid, warps * 32, (size_t)warps * H * 4, stream>>>(
+        (const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, rstd, (__nv_bfloat16*)dx, scratch,
+        T, H, accumulate_dx ? 1 : 0);
+    colsum_kernel<<<(H + 31) / 32, dim3(32, kColsumRowGroups), 0, stream>>>(scratch, grid, H, dw, accumulate_dw ? 1 : 0);
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    char msg[200];
+    std::snprintf(msg, sizeof(msg), "libra_rmsnorm_bwd_noalloc: launch failed: %s", cudaGetErrorString(e));
+    return noalloc_fail(4, msg);
+  }
+  return 0;
+}

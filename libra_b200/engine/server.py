@@ -148,7 +148,10 @@ def main(argv=None) -> None:
     ap.add_argument("--port", type=int, default=8000)
     ap.add_argument("--kv-memory-fraction", type=float, default=0.8)
     ap.add_argument("--max-batch-tokens", type=int, default=8192)
+    ap.add_argument("--tp", type=int, default=1, help="tensor-parallel degree (one process per GPU via torchrun)")
     a = ap.parse_args(argv)
+    if a.tp > 1:
+        raise SystemExit("libra_b200.engine.server: --tp > 1 needs the tensor-parallel rollout runner")
     holder = B200TrainEngine(a.model, device=a.device, use_distributed_optimizer=False)
     holder.initialize()
     holder.release_optimizer_state()

@@ -109,6 +109,7 @@ class B200TrainEngine:
         self.elastic_gradient_domain = None
         self._pending_hybrid_gradients: List[Any] = []
         self.elastic_update_publisher = None  # callable(reduced flat grad, step, version) for lockstep hybrids
+        self.elastic_payload_wait_s = 0.0  # >0: wait this long for every active hybrid replica's payload
 
     # ------------------------------------------------------------------ setup
     def initialize(self, max_seq_length: int = 2048) -> None:
@@ -434,6 +435,8 @@ class B200TrainEngine:
     def _apply_elastic_inter_replica_gradients(self) -> int:
         """Add matching hybrid payloads into this core replica's gradient
         before the core DP reduction; returns how many were merged."""
+        if self.elastic_gradient_domain is not None and self.elastic_payload_wait_s > 0:
+            self._wait_for_hybrid_payloads(self.step_count + 1, self.elastic_payload_wait_s)
         pending, self._pending_hybrid_gradients = self._pending_hybrid_gradients, []
         if not pending or self.elastic_gradient_domain is None:
             return 0
@@ -446,6 +449,22 @@ class B200TrainEngine:
                 raise ValueError(f"hybrid payload has {g.numel()} elements, expected {self.flat_grad.numel()}")
             self.flat_grad.add_(g.to(device=self.flat_grad.device, dtype=torch.float32).view(-1))
         return len(used)
+
+    def _wait_for_hybrid_payloads(self, step: int, timeout_s: float) -> bool:
+        """Bounded wait until every active hybrid replica targeting this core
+        replica has queued its payload for ``step``; a late replica simply
+        misses the step (its payload is dropped by the step check)."""
+        domain = self.elastic_gradient_domain
+        want = set(domain.active_hybrid_ids_for_core(f"dp{getattr(self, 'dp_rank', 0)}"))
+        deadline = time.monotonic() + timeout_s
+        while want:
+            have = {p.replica_id for p in list(self._pending_hybrid_gradients) if p.step in (step, -1)}
+            if want <= have:
+                return True
+            if time.monotonic() > deadline:
+                return False
+            time.sleep(0.002)
+        return True
 
     def _publish_elastic_update(self) -> None:
         if self.elastic_update_publisher is None:
@@ -471,7 +490,10 @@ class B200TrainEngine:
         os.makedirs(os.path.dirname(path), exist_ok=True)
         snap = {"flat_param": self.flat_param.cpu(), "version": self.current_version, "step": self.step_count,
                 "dp_rank": getattr(self, "dp_rank", 0), "dp_size": getattr(self, "dp_size", 1),
-                "hidden_size": self.cfg.hidden_size, "num_layers": self.cfg.num_hidden_layers}
+                "hidden_size": self.cfg.hidden_size, "num_layers": self.cfg.num_hidden_layers,
+                "optim": {"lr": self.optim.lr, "betas": list(self.optim.betas), "eps": self.optim.eps,
+                          "weight_decay": self.optim.weight_decay, "max_grad_norm": self.optim.max_grad_norm},
+                "loss": {"kl_coef": self.kl_coef, "clip_epsilon": self.clip_epsilon, "temperature": self.temperature}}
         if self.master is not None:
             snap.update(master=self.master.cpu(), exp_avg=self.exp_avg.cpu(), exp_avg_sq=self.exp_avg_sq.cpu(),
                         shard_start=self.shard_start)
@@ -496,6 +518,13 @@ class B200TrainEngine:
                 self.exp_avg_sq.zero_()
         self.current_version = int(snap["version"])
         self.step_count = int(snap["step"])
+        if "optim" in snap:  # a joining replica must step exactly like its core replica
+            o = snap["optim"]
+            self.optim = OptimConfig(lr=float(o["lr"]), betas=tuple(o["betas"]), eps=float(o["eps"]),
+                                     weight_decay=float(o["weight_decay"]), max_grad_norm=float(o["max_grad_norm"]))
+            self.kl_coef = float(snap["loss"]["kl_coef"])
+            self.clip_epsilon = float(snap["loss"]["clip_epsilon"])
+            self.temperature = float(snap["loss"]["temperature"])
         return self.current_version
 
     def compute_gradient_payload(self, trajectories: List[Dict[str, Any]], *, replica_id: str, target_core_id: str,

@@ -419,7 +419,25 @@ class RuntimeElasticExecutor:
                 "planner_signal": dict(self._signal or {})}
 
     # ------------------------------------------------------------------ training pool
+    def _ensure_gradient_server(self) -> None:
+        if self.gradient_server is not None or self.train_engine is None:
+            return
+        if not hasattr(self.train_engine, "enqueue_hybrid_gradient_payload"):
+            return
+        from libra_b200.infra.elastic.worker import attach_gradient_server, write_endpoint
+
+        import secrets
+
+        self.gradient_server = attach_gradient_server(
+            self.train_engine, host=self._opt("gradient_server_host", "") or "127.0.0.1",
+            authkey=secrets.token_hex(16))
+        self.train_engine.elastic_payload_wait_s = float(self._opt("elastic_hybrid_payload_wait_s", 0.0) or 0.0)
+        write_endpoint(self._opt("hybrid_worker_task_dir", "./logs/elastic_training_tasks"),
+                       int(os.environ.get("RANK", "0")), self.gradient_server.endpoint,
+                       data_parallel_rank=int(getattr(self.train_engine, "dp_rank", 0)))
+
     def _ensure_pool(self) -> None:
+        self._ensure_gradient_server()
         if self.elastic_pool is not None or self.train_engine is None:
             return
         from libra_b200.infra.elastic.hybrid_pool import ElasticHybridPool

@@ -76,6 +76,7 @@ class FakeRollout:
 def _cfg(tmp_path, **grp):
     cfg = AsyncRLConfig.from_file(CFG)
     cfg.log_dir = str(tmp_path / "logs")
+    cfg.global_resource_planner.hybrid_worker_task_dir = str(tmp_path / "tasks")
     for k, v in grp.items():
         setattr(cfg.global_resource_planner, k, v)
     return cfg
@@ -217,7 +218,7 @@ def test_signal_joins_then_release_cancels_pending(tmp_path):
 
 def test_join_completes_and_is_reported(tmp_path):
     cfg = _cfg(tmp_path, runtime_reconfigure_training=True, runtime_training_pool_plan_only=False,
-               runtime_training_pool_target_gpus=6)
+               runtime_training_pool_target_gpus=6, hybrid_worker_task_dir=str(tmp_path / "tasks"))
     pool = _pool()
     ex = _executor(cfg, [], elastic_pool=pool)
     ex.execute(_decision(_plan()))
@@ -226,10 +227,8 @@ def test_join_completes_and_is_reported(tmp_path):
         time.sleep(0.02)
     st = ex.hybrid_runtime_state()
     assert st["active_hybrid_replicas"] == 1 and st["replica_size_gpus"] == 2
-    member = json.loads((tmp_path / "logs").joinpath("..").resolve().joinpath(
-        cfg.global_resource_planner.hybrid_worker_task_dir, "membership", "ehp_replica_rollout0.json").read_text()) \
-        if os.path.isabs(cfg.global_resource_planner.hybrid_worker_task_dir) else None
-    assert member is None or member["role"] == "hybrid_training"
+    member = json.loads((tmp_path / "tasks" / "membership" / "ehp_replica_rollout0.json").read_text())
+    assert member["role"] == "hybrid_training" and member["members"] == ["rollout0", "rollout1"]
     res = ex.execute(_decision(_plan()))  # target reached: no second join
     assert any(a.startswith("training_gpus_unchanged") for a in res.training_actions)
     pool.close()

@@ -227,7 +227,7 @@ class B200TrainEngine:
             b = _pin_batch(packed["batch"])
             self.io_bytes["h2d"] += sum(t.numel() * t.element_size() for t in
                                         (b.tokens, b.positions, b.cu_seqlens, b.action_rows, b.action_targets,
-                                         b.seq_index) if t is not None)
+                                         b.seq_index, b.attn_tiles) if t is not None)
             out = {"batch": b.to(dev, non_blocking=True)}
             for k, v in packed.items():
                 if k != "batch":
@@ -575,7 +575,7 @@ def _fold_grad_into_main(p: torch.nn.Parameter) -> None:
 def _pin_batch(b: PackedBatch) -> PackedBatch:
     pin = lambda t: t if t is None or t.is_pinned() else t.pin_memory()  # noqa: E731
     return PackedBatch(pin(b.tokens), pin(b.positions), pin(b.cu_seqlens), b.max_seqlen, pin(b.action_rows),
-                       pin(b.action_targets), pin(b.seq_index))
+                       pin(b.action_targets), pin(b.seq_index), pin(b.attn_tiles))
 
 
 def _merge_stats(stats: List[Dict[str, float]]) -> Dict[str, float]:

@@ -227,11 +227,12 @@ class PackedBatch:
     action_rows: torch.Tensor
     action_targets: torch.Tensor
     seq_index: Optional[torch.Tensor] = None  # sequence id of each action row
+    attn_tiles: Optional[torch.Tensor] = None  # int32 [n, 2] (sequence, 128-row q tile), heaviest first
 
     def to(self, device, non_blocking: bool = True) -> "PackedBatch":
         mv = lambda t: None if t is None else t.to(device, non_blocking=non_blocking)  # noqa: E731
         return PackedBatch(mv(self.tokens), mv(self.positions), mv(self.cu_seqlens), self.max_seqlen,
-                           mv(self.action_rows), mv(self.action_targets), mv(self.seq_index))
+                           mv(self.action_rows), mv(self.action_targets), mv(self.seq_index), mv(self.attn_tiles))
 
     @property
     def num_tokens(self) -> int:
@@ -258,11 +259,14 @@ def pack_sequences(seqs: List[torch.Tensor], masks: Optional[List[torch.Tensor]]
     action_rows = torch.cat(rows) if rows else torch.zeros(0, dtype=torch.long)
     action_targets = torch.cat(targets) if targets else torch.zeros(0, dtype=torch.long)
     seq_index = torch.cat(sidx) if sidx else torch.zeros(0, dtype=torch.int32)
-    batch = PackedBatch(tokens, positions, cu, max(lens) if lens else 0, action_rows.long(), action_targets, seq_index)
+    from libra_b200.ops.attention import attn_tiles
+
+    batch = PackedBatch(tokens, positions, cu, max(lens) if lens else 0, action_rows.long(), action_targets, seq_index,
+                        attn_tiles(cu.tolist(), causal=True))
     if pin:
         batch = PackedBatch(*(t.pin_memory() if isinstance(t, torch.Tensor) else t for t in
                               (batch.tokens, batch.positions, batch.cu_seqlens, batch.max_seqlen, batch.action_rows,
-                               batch.action_targets, batch.seq_index)))
+                               batch.action_targets, batch.seq_index, batch.attn_tiles)))
     return batch
 
 
@@ -293,14 +297,14 @@ class Qwen3Model(nn.Module):
         self.nkv_local = max(1, cfg.num_key_value_heads // tp_size)
 
     # -- blocks ------------------------------------------------------------
-    def _attention_block(self, i: int, x, pos, cu, max_len):
+    def _attention_block(self, i: int, x, pos, cu, max_len, tiles=None):
         p, cfg = self.p, self.cfg
         pre = f"layers.{i}."
         h = ops.rmsnorm(x, p[pre + "input_layernorm"], cfg.rms_norm_eps)
         qkv = ops.linear(h, p[pre + "qkv_proj"])
         q, k, v = ops.qk_norm_rope(qkv, p[pre + "q_norm"], p[pre + "k_norm"], pos, self.rope_cos, self.rope_sin,
                                    self.nq_local, self.nkv_local, cfg.rms_norm_eps)
-        attn = ops.varlen_causal_attention(q, k, v, cu, max_len)
+        attn = ops.varlen_causal_attention(q, k, v, cu, max_len, tiles=tiles)
         return self._row_parallel(attn.reshape(attn.shape[0], -1), p[pre + "o_proj"], x)
 
     def _mlp_block(self, i: int, x):
@@ -322,8 +326,8 @@ class Qwen3Model(nn.Module):
 
         return row_parallel_linear(a, w, residual, self.tp_group)
 
-    def _layer(self, i, x, pos, cu, max_len):
-        x = self._attention_block(i, x, pos, cu, max_len)
+    def _layer(self, i, x, pos, cu, max_len, tiles=None):
+        x = self._attention_block(i, x, pos, cu, max_len, tiles)
         return self._mlp_block(i, x)
 
     # -- public ------------------------------------------------------------
@@ -340,9 +344,9 @@ class Qwen3Model(nn.Module):
         for i in range(self.cfg.num_hidden_layers):
             if self.recompute and torch.is_grad_enabled():
                 x = torch.utils.checkpoint.checkpoint(self._layer, i, x, batch.positions, batch.cu_seqlens,
-                                                      batch.max_seqlen, use_reentrant=False)
+                                                      batch.max_seqlen, batch.attn_tiles, use_reentrant=False)
             else:
-                x = self._layer(i, x, batch.positions, batch.cu_seqlens, batch.max_seqlen)
+                x = self._layer(i, x, batch.positions, batch.cu_seqlens, batch.max_seqlen, batch.attn_tiles)
         return ops.rmsnorm(x, self.p["norm"], self.cfg.rms_norm_eps)
 
     @property

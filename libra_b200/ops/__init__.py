@@ -247,13 +247,16 @@ def swiglu(gu):
 # attention
 # ---------------------------------------------------------------------------
 
-def varlen_causal_attention(q, k, v, cu_seqlens, max_seqlen: int, scale=None):
-    """Causal GQA attention over packed sequences (q [T,Hq,D], k/v [T,Hkv,D])."""
+def varlen_causal_attention(q, k, v, cu_seqlens, max_seqlen: int, scale=None, tiles=None):
+    """Causal GQA attention over packed sequences (q [T,Hq,D], k/v [T,Hkv,D]).
+
+    ``tiles``: the (sequence, q tile) table of the packed batch, built once per
+    batch (``attention.attn_tiles``); computed from ``cu_seqlens`` when absent."""
     if q.device.type != "cuda":
         return ref.varlen_causal_attention(q, k, v, cu_seqlens, scale)
     from .attention import flash_varlen_causal
 
-    return flash_varlen_causal(q, k, v, cu_seqlens, max_seqlen, scale)
+    return flash_varlen_causal(q, k, v, cu_seqlens, max_seqlen, scale, tiles)
 
 
 # ---------------------------------------------------------------------------

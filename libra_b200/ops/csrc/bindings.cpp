@@ -27,6 +27,10 @@ void adamw_step(torch::Tensor master, torch::Tensor grad, torch::Tensor m, torch
 torch::Tensor paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                                      torch::Tensor block_tables, torch::Tensor seq_lens, int64_t max_len,
                                      double scale);
+namespace attn {
+std::vector<torch::Tensor> flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor cu_seqlens,
+                                     torch::Tensor tiles, double scale, bool causal, torch::Tensor err);
+}  // namespace attn
 }  // namespace libra
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -44,4 +48,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grad_sq_norm", &libra::grad_sq_norm);
   m.def("adamw_step", &libra::adamw_step);
   m.def("paged_decode_attention", &libra::paged_decode_attention);
+  m.def("flash_fwd", &libra::attn::flash_fwd, "tcgen05 varlen GQA attention forward");
 }

@@ -90,6 +90,7 @@ class AsyncRLTrainer:
         self.workflow = None
         self.global_step = 0
         self.stats: Dict[str, Any] = {}
+        self._tracker = None
         self.start_step = int(os.environ.get("RL_TRAIN_START_STEP", "0") or 0)
         self.initial_model_version = int(os.environ.get("RL_INITIAL_MODEL_VERSION", str(self.start_step))
                                          or self.start_step)
@@ -414,6 +415,11 @@ class AsyncRLTrainer:
             self.stats = stats
             if self.is_main_process:
                 self._record_history(step, batch, stats)
+                if self._tracker is None:
+                    from libra_b200.utils.tracking import Tracker
+
+                    self._tracker = Tracker.create(self.config, self.rank)
+                self._tracker.log(stats, step)
                 self._run_planner(step, batch, stats)
                 if hasattr(self.rollout_engine, "on_epoch_end"):
                     self.rollout_engine.on_epoch_end(step)
@@ -498,3 +504,5 @@ class AsyncRLTrainer:
             self.history_collector.close()
         if self._tracer is not None:
             self._tracer.close()
+        if self._tracker is not None:
+            self._tracker.finish()

@@ -228,11 +228,17 @@ class PackedBatch:
     action_targets: torch.Tensor
     seq_index: Optional[torch.Tensor] = None  # sequence id of each action row
     attn_tiles: Optional[torch.Tensor] = None  # int32 [n, 2] (sequence, 128-row q tile), heaviest first
+    attn_kv_tiles: Optional[torch.Tensor] = None  # int32 [n, 2] (sequence, 128-row kv tile), heaviest first
 
     def to(self, device, non_blocking: bool = True) -> "PackedBatch":
         mv = lambda t: None if t is None else t.to(device, non_blocking=non_blocking)  # noqa: E731
         return PackedBatch(mv(self.tokens), mv(self.positions), mv(self.cu_seqlens), self.max_seqlen,
-                           mv(self.action_rows), mv(self.action_targets), mv(self.seq_index), mv(self.attn_tiles))
+                           mv(self.action_rows), mv(self.action_targets), mv(self.seq_index), mv(self.attn_tiles),
+                           mv(self.attn_kv_tiles))
+
+    @property
+    def tiles(self):
+        return (self.attn_tiles, self.attn_kv_tiles)
 
     @property
     def num_tokens(self) -> int:
@@ -261,12 +267,13 @@ def pack_sequences(seqs: List[torch.Tensor], masks: Optional[List[torch.Tensor]]
     seq_index = torch.cat(sidx) if sidx else torch.zeros(0, dtype=torch.int32)
     from libra_b200.ops.attention import attn_tiles
 
+    cul = cu.tolist()
     batch = PackedBatch(tokens, positions, cu, max(lens) if lens else 0, action_rows.long(), action_targets, seq_index,
-                        attn_tiles(cu.tolist(), causal=True))
+                        attn_tiles(cul, causal=True), attn_tiles(cul, causal=True, kv=True))
     if pin:
         batch = PackedBatch(*(t.pin_memory() if isinstance(t, torch.Tensor) else t for t in
                               (batch.tokens, batch.positions, batch.cu_seqlens, batch.max_seqlen, batch.action_rows,
-                               batch.action_targets, batch.seq_index, batch.attn_tiles)))
+                               batch.action_targets, batch.seq_index, batch.attn_tiles, batch.attn_kv_tiles)))
     return batch
 
 
@@ -300,7 +307,7 @@ class Qwen3Model(nn.Module):
     def _attention_block(self, i: int, x, pos, cu, max_len, tiles=None):
         p, cfg = self.p, self.cfg
         pre = f"layers.{i}."
-        h = ops.rmsnorm(x, p[pre + "input_layernorm"], cfg.rms_norm_eps)
+        h = self._tp_in(ops.rmsnorm(x, p[pre + "input_layernorm"], cfg.rms_norm_eps))
         qkv = ops.linear(h, p[pre + "qkv_proj"])
         q, k, v = ops.qk_norm_rope(qkv, p[pre + "q_norm"], p[pre + "k_norm"], pos, self.rope_cos, self.rope_sin,
                                    self.nq_local, self.nkv_local, cfg.rms_norm_eps)
@@ -315,9 +322,17 @@ class Qwen3Model(nn.Module):
             from libra_b200.models.moe import moe_mlp
 
             return moe_mlp(h, x, p[pre + "router"], p[pre + "experts.w1"], p[pre + "experts.w2"], cfg)
-        gu = ops.linear(h, p[pre + "gate_up_proj"])
+        gu = ops.linear(self._tp_in(h), p[pre + "gate_up_proj"])
         a = ops.swiglu(gu)
         return self._row_parallel(a, p[pre + "down_proj"], x)
+
+    def _tp_in(self, h):
+        """Replicated input of a column-parallel linear (gradient all-reduced over TP)."""
+        if self.tp_size == 1:
+            return h
+        from libra_b200.parallel.tensor_parallel import copy_to_tp
+
+        return copy_to_tp(h, self.tp_group)
 
     def _row_parallel(self, a, w, residual):
         if self.tp_size == 1:
@@ -344,9 +359,9 @@ class Qwen3Model(nn.Module):
         for i in range(self.cfg.num_hidden_layers):
             if self.recompute and torch.is_grad_enabled():
                 x = torch.utils.checkpoint.checkpoint(self._layer, i, x, batch.positions, batch.cu_seqlens,
-                                                      batch.max_seqlen, batch.attn_tiles, use_reentrant=False)
+                                                      batch.max_seqlen, batch.tiles, use_reentrant=False)
             else:
-                x = self._layer(i, x, batch.positions, batch.cu_seqlens, batch.max_seqlen, batch.attn_tiles)
+                x = self._layer(i, x, batch.positions, batch.cu_seqlens, batch.max_seqlen, batch.tiles)
         return ops.rmsnorm(x, self.p["norm"], self.cfg.rms_norm_eps)
 
     @property

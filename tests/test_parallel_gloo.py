@@ -1,0 +1,151 @@
+"""TP / PP / EP equivalence against one rank, as 2 gloo processes on CPU."""
+
+import os
+import socket
+import sys
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from libra_b200.parallel.mesh import ParallelMesh
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _spawn(fn, world, *args):
+    port = _free_port()
+    mp.start_processes(fn, args=(world, port, *args), nprocs=world, join=True, start_method="spawn")
+
+
+def _init(rank, world, port):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+
+
+def _model_inputs(cfg_name="tiny"):
+    from libra_b200.models.qwen3 import ParamLayout, get_config, init_params, pack_sequences, param_shapes
+
+    cfg = get_config(cfg_name)
+    shapes = param_shapes(cfg)
+    flat = torch.zeros(ParamLayout(shapes).numel)
+    views = ParamLayout(shapes).views(flat)
+    init_params(cfg, views, seed=1)
+    g = torch.Generator().manual_seed(0)
+    seqs = [torch.randint(4, cfg.vocab_size, (n,), generator=g) for n in (9, 14, 5)]
+    return cfg, {k: v.clone() for k, v in views.items()}, pack_sequences(seqs)
+
+
+def _run_model(cfg, params, batch, tp_group=None, tp_size=1, tp_rank=0):
+    from libra_b200.models.qwen3 import Qwen3Model
+
+    ps = {k: torch.nn.Parameter(v.clone()) for k, v in params.items()}
+    m = Qwen3Model(cfg, ps, tp_group=tp_group, tp_size=tp_size, tp_rank=tp_rank)
+    lp = m.action_logprobs(batch)
+    w = torch.linspace(0.5, 1.5, lp.numel())
+    (lp * w).sum().backward()
+    return lp.detach(), {k: p.grad for k, p in ps.items()}
+
+
+def _tp_worker(rank, world, port, out_dir):
+    _init(rank, world, port)
+    from libra_b200.parallel.tensor_parallel import shard_full_params, tp_partial_grad_params
+
+    cfg, full, batch = _model_inputs()
+    ref_lp, ref_g = _run_model(cfg, full, batch)
+    local = shard_full_params(full, cfg, world, rank)
+    lp, grads = _run_model(cfg, local, batch, dist.group.WORLD, world, rank)
+    for n in tp_partial_grad_params(list(grads)):
+        dist.all_reduce(grads[n])
+    torch.testing.assert_close(lp, ref_lp, rtol=1e-4, atol=1e-4)
+    ref_local = shard_full_params(ref_g, cfg, world, rank)
+    for n, gr in grads.items():
+        torch.testing.assert_close(gr, ref_local[n], rtol=1e-3, atol=1e-4, msg=n)
+    open(os.path.join(out_dir, f"tp_ok_{rank}"), "w").close()
+    dist.destroy_process_group()
+
+
+def _pp_worker(rank, world, port, out_dir):
+    _init(rank, world, port)
+    from libra_b200.models.qwen3 import Qwen3Model
+    from libra_b200.parallel.pipeline import P2P, PipelineStage, allreduce_tied_embedding_grad, one_f_one_b
+
+    cfg, full, batch = _model_inputs()
+    mbs = [{"batch": batch}, {"batch": batch}, {"batch": batch}]
+
+    def loss_fn(logp, mb):
+        return -logp.mean()
+
+    # single-stage reference
+    ps_ref = {k: torch.nn.Parameter(v.clone()) for k, v in full.items()}
+    ref = PipelineStage(Qwen3Model(cfg, ps_ref), 0, cfg.num_hidden_layers, True, True, loss_fn)
+    ref_losses = [float(ref(mb, None).backward() or 0) for mb in mbs]
+    ps = {k: torch.nn.Parameter(v.clone()) for k, v in full.items()}
+    r = PipelineStage.split_layers(cfg.num_hidden_layers, world)[rank]
+    stage = PipelineStage(Qwen3Model(cfg, ps), r.start, r.stop, rank == 0, rank == world - 1, loss_fn)
+    p2p = P2P(None, rank - 1 if rank > 0 else None, rank + 1 if rank < world - 1 else None, dtype=torch.float32)
+    losses = one_f_one_b(stage, mbs, p2p, world, rank)
+    assert cfg.tie_word_embeddings
+    allreduce_tied_embedding_grad(ps["embed_tokens"], dist.group.WORLD)
+    for name, p in ps.items():
+        if p.grad is not None:
+            torch.testing.assert_close(p.grad, ps_ref[name].grad, rtol=1e-4, atol=1e-5, msg=name)
+    if rank == world - 1:
+        assert len(losses) == 3
+    open(os.path.join(out_dir, f"pp_ok_{rank}"), "w").close()
+    dist.destroy_process_group()
+
+
+def _ep_worker(rank, world, port, out_dir):
+    _init(rank, world, port)
+    from libra_b200.models.moe import moe_mlp
+    from libra_b200.models.qwen3 import get_config
+    from libra_b200.parallel.expert_parallel import ep_moe_mlp
+
+    cfg = get_config("tiny-moe")
+    g = torch.Generator().manual_seed(7)
+    E, H, F = cfg.num_experts, cfg.hidden_size, cfg.moe_intermediate_size
+    h = torch.randn(40, H, generator=g) * 0.5
+    res = torch.randn(40, H, generator=g)
+    router = torch.randn(E, H, generator=g) * 0.05
+    w1 = torch.randn(E, 2 * F, H, generator=g) * 0.05
+    w2 = torch.randn(E, H, F, generator=g) * 0.05
+    hh = h[rank * 20:(rank + 1) * 20]  # each rank owns different tokens
+    ref = moe_mlp(hh, res[rank * 20:(rank + 1) * 20], router, w1, w2, cfg)
+    El = E // world
+    w1l = w1[rank * El:(rank + 1) * El].clone().requires_grad_(True)
+    out = ep_moe_mlp(hh, res[rank * 20:(rank + 1) * 20], router, w1l, w2[rank * El:(rank + 1) * El], cfg,
+                     dist.group.WORLD)
+    torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4)
+    out.sum().backward()
+    assert w1l.grad is not None and torch.isfinite(w1l.grad).all()
+    open(os.path.join(out_dir, f"ep_ok_{rank}"), "w").close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("kind,fn", [("tp", _tp_worker), ("pp", _pp_worker), ("ep", _ep_worker)])
+def test_parallel_equivalence(tmp_path, kind, fn):
+    _spawn(fn, 2, str(tmp_path))
+    assert {p.name for p in tmp_path.iterdir()} == {f"{kind}_ok_0", f"{kind}_ok_1"}
+
+
+def test_mesh_layout():
+    m = ParallelMesh(8, tp=2, pp=2, ep=2, create_groups=False)
+    assert m.dp == 2
+    assert m.members("tp", 5) == [4, 5]
+    assert m.members("dp", 1) == [1, 3] and m.members("pp", 1) == [1, 5]
+    assert m.members("ep", 0) == [0, 2] and m.members("mp", 0) == [0, 1, 4, 5]
+    c = m.coords(7)
+    assert (c.tp, c.dp, c.pp) == (1, 1, 1)
+    assert m.is_batch_source(0) and not m.is_batch_source(1) and m.is_pipeline_last(4)
+    with pytest.raises(ValueError):
+        ParallelMesh(8, tp=3)

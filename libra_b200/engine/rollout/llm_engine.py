@@ -71,7 +71,11 @@ class LLMEngine:
     def __init__(self, cfg: Qwen3Config, params: Dict[str, torch.Tensor], *, kv_blocks: int = 0,
                  block_size: int = 16, kv_memory_fraction: float = 0.5, max_batch_tokens: int = 8192,
                  max_running: int = 256, max_model_len: int = 0, instance_id: str = "", tp_group=None,
-                 tp_size: int = 1, eos_token_id: Optional[int] = None):
+                 tp_size: int = 1, eos_token_id: Optional[int] = None, tp_channel=None):
+        """``tp_size > 1``: one engine per TP rank.  TP rank 0 (the driver)
+        schedules, samples and serves; the other ranks run ``follower_loop``
+        and replay, step by step, the driver's KV-cache operations and model
+        steps, which it broadcasts over ``tp_channel`` (a gloo group)."""
         self.cfg = cfg
         self.params = params
         self.device = next(iter(params.values())).device
@@ -104,6 +108,63 @@ class LLMEngine:
         self.stats = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0, "cached_prefix_tokens": 0,
                       "finished": 0, "busy_s": 0.0}
         self._ids = itertools.count()
+        self.tp_size, self.tp_group, self.tp_channel = tp_size, tp_group, tp_channel
+        self.tp_rank = 0
+        self._tp_src = 0
+        if tp_size > 1:
+            import torch.distributed as dist
+
+            self.tp_rank = dist.get_rank(tp_group)
+            self._tp_src = dist.get_global_rank(tp_channel, 0) if tp_channel is not None else 0
+        self._kv_ops: List[tuple] = []  # KV-cache calls the followers must replay, in order
+        self.tp_reload_hook = None  # follower side: callable(request) -> (params, version)
+
+    # ------------------------------------------------------------------ tensor-parallel replay
+    def _kv_call(self, op: str, *args):
+        """Apply a scheduler-side KV-cache call and record it for the followers."""
+        if self.tp_size > 1:
+            self._kv_ops.append((op, args))
+        if op == "match_prefix":
+            return self.kv.match_prefix(*args)
+        if op == "free":
+            return self.kv.free(*args)
+        if op == "clear_cache":
+            return self.kv.alloc.clear_cache()
+        raise ValueError(op)
+
+    def _broadcast_plan(self, plan: Dict) -> Dict:
+        import torch.distributed as dist
+
+        box = [plan]
+        dist.broadcast_object_list(box, src=self._tp_src, group=self.tp_channel)
+        return box[0]
+
+    def _publish(self, items=None, **extra) -> None:
+        if self.tp_size > 1 and self.tp_rank == 0:
+            ops, self._kv_ops = self._kv_ops, []
+            self._broadcast_plan({"ops": ops, "items": [(i.seq_id, list(i.tokens), i.start) for i in items or []],
+                                  **extra})
+
+    def follower_loop(self) -> None:
+        """TP rank > 0: replay the driver's steps until it broadcasts a stop."""
+        if self.device.type == "cuda":
+            torch.cuda.set_device(self.device)
+        while True:
+            plan = self._broadcast_plan({})
+            if plan.get("reload") is not None and self.tp_reload_hook is not None:
+                params, version = self.tp_reload_hook(plan["reload"])
+                if params:
+                    with torch.no_grad():
+                        for k, v in params.items():
+                            self.params[k].copy_(v)
+                if version is not None:
+                    self.version = int(version)
+            for op, args in plan.get("ops", []):
+                getattr(self.kv, op)(*args) if op != "clear_cache" else self.kv.alloc.clear_cache()
+            if plan.get("items"):
+                self.runner.step([WorkItem(rid, toks, start) for rid, toks, start in plan["items"]])
+            if plan.get("stop"):
+                return
 
     # ------------------------------------------------------------------ request API
     def add_request(self, prompt_tokens: List[int], params: SamplingParams, request_id: str = "",
@@ -151,6 +212,7 @@ class LLMEngine:
         self._wake.set()
         if self._thread is not None:
             self._thread.join(timeout=10)
+        self._publish(stop=True)
 
     def _loop(self) -> None:
         if self.device.type == "cuda":
@@ -172,7 +234,7 @@ class LLMEngine:
             self.running.clear()
             self.waiting.clear()
         for r in reqs:
-            self.kv.free(r.request_id)
+            self._kv_call("free", r.request_id)
             if r.future is not None and r.loop is not None:
                 r.loop.call_soon_threadsafe(lambda f=r.future: f.done() or f.set_exception(RuntimeError(str(exc))))
 
@@ -199,11 +261,17 @@ class LLMEngine:
     # ------------------------------------------------------------------ weights
     @torch.no_grad()
     def update_weights(self, new_params: Dict[str, torch.Tensor], version: Optional[int] = None,
-                       copy: bool = True) -> None:
-        """Install new weights between steps (copy into the existing buffers, or rebind)."""
+                       copy: bool = True, reload_request: Optional[Dict] = None) -> None:
+        """Install new weights between steps (copy into the existing buffers, or rebind).
+
+        With TP, ``reload_request`` is forwarded to the followers, which load
+        their own shards through ``tp_reload_hook``; the driver's loop is paused
+        first, so the broadcast cannot interleave with a step's."""
         was_paused = self._paused.is_set()
         self.pause()
         try:
+            if self.tp_size > 1 and reload_request is not None:
+                self._publish(reload=reload_request)
             if copy:
                 for k, v in new_params.items():
                     self.params[k].copy_(v, non_blocking=True)
@@ -212,7 +280,7 @@ class LLMEngine:
             else:
                 self.params = new_params
                 self.runner.p = new_params
-            self.kv.alloc.clear_cache()
+            self._kv_call("clear_cache")
             if version is not None:
                 self.version = int(version)
         finally:
@@ -226,7 +294,7 @@ class LLMEngine:
             while self.waiting and len(self.running) + len(admitted) < self.max_running:
                 r = self.waiting[0]
                 if not r.cached and r.request_id not in self.kv.seqs:
-                    r.cached = self.kv.match_prefix(r.request_id, r.prompt)
+                    r.cached = self._kv_call("match_prefix", r.request_id, r.prompt)
                     self.stats["cached_prefix_tokens"] += r.cached
                 need = len(r.tokens) - r.cached
                 if admitted and need > budget:
@@ -250,6 +318,7 @@ class LLMEngine:
         if not batch:
             return 0
         items = [WorkItem(r.request_id, r.tokens, r.cached) for r in batch]
+        self._publish(items)
         logits = self.runner.step(items)
         temps = torch.tensor([r.params.temperature for r in batch], device=logits.device, dtype=torch.float32)
         top_p = torch.tensor([r.params.top_p for r in batch], device=logits.device, dtype=torch.float32)
@@ -288,7 +357,7 @@ class LLMEngine:
         return ""
 
     def _finish(self, r: _Request, reason: str) -> None:
-        self.kv.free(r.request_id)
+        self._kv_call("free", r.request_id)
         self.stats["finished"] += 1
         res = GenerationResult(r.request_id, r.prompt, list(r.out), list(r.logprobs), reason,
                                {"ttft_s": (r.t_first - r.t_arrive) if r.t_first else 0.0,

@@ -143,7 +143,13 @@ class InferenceRunner:
         dec_items = [it for it in items if len(it.tokens) - it.start == 1]
         self._lens_dec = torch.tensor([len(it.tokens) for it in dec_items], dtype=torch.int32).to(dev)
         self._max_len_dec = max((len(it.tokens) for it in dec_items), default=1)
-        x = self.p["embed_tokens"].index_select(0, tok_t)
+        if self.tp_size > 1:
+            from libra_b200.parallel.tensor_parallel import vocab_parallel_embedding
+            import torch.distributed as dist
+
+            x = vocab_parallel_embedding(tok_t, self.p["embed_tokens"], self.tp_group, dist.get_rank(self.tp_group))
+        else:
+            x = self.p["embed_tokens"].index_select(0, tok_t)
         for layer in range(cfg.num_hidden_layers):
             pre = f"layers.{layer}."
             h = ops.rmsnorm(x, p[pre + "input_layernorm"], cfg.rms_norm_eps)

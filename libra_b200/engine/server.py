@@ -23,6 +23,7 @@ from __future__ import annotations
 import argparse
 import asyncio
 import json
+import os
 import time
 import uuid
 from typing import Any, Dict, Optional
@@ -81,9 +82,11 @@ def build_app(engine, tokenizer, model_name: str = "libra", weight_loader=None) 
         body = await request.json()
         async with reload_lock:
             t0 = time.perf_counter()
-            params, version = await asyncio.get_running_loop().run_in_executor(None, weight_loader, dict(body, kind=kind))
+            req = dict(body, kind=kind)
+            params, version = await asyncio.get_running_loop().run_in_executor(None, weight_loader, req)
             if params:
-                await asyncio.get_running_loop().run_in_executor(None, engine.update_weights, params, version)
+                await asyncio.get_running_loop().run_in_executor(
+                    None, lambda: engine.update_weights(params, version, reload_request=req))
             return web.json_response({"status": "ok", "version": engine.version, "seconds": time.perf_counter() - t0})
 
     app.router.add_get("/health", health)
@@ -150,27 +153,62 @@ def main(argv=None) -> None:
     ap.add_argument("--max-batch-tokens", type=int, default=8192)
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel degree (one process per GPU via torchrun)")
     a = ap.parse_args(argv)
-    if a.tp > 1:
-        raise SystemExit("libra_b200.engine.server: --tp > 1 needs the tensor-parallel rollout runner")
-    holder = B200TrainEngine(a.model, device=a.device, use_distributed_optimizer=False)
+    tp_group = channel = None
+    rank = 0
+    device = a.device
+    if a.tp > 1:  # launched by torch.distributed.run, one process per GPU of the instance
+        import datetime
+
+        import torch.distributed as dist
+
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        device = f"cuda:{local}"
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+        if dist.get_world_size() != a.tp:
+            raise SystemExit(f"--tp {a.tp} needs exactly {a.tp} processes, got {dist.get_world_size()}")
+        rank, tp_group = dist.get_rank(), dist.group.WORLD
+        channel = dist.new_group(backend="gloo")
+    holder = B200TrainEngine(a.model, device=device, use_distributed_optimizer=False, tp_size=a.tp)
     holder.initialize()
     holder.release_optimizer_state()
+
+    def load_disk(path: str) -> Dict[str, torch.Tensor]:
+        params = {k: v.clone() for k, v in holder.params.items()}
+        if a.tp == 1:
+            load_params_into(params, path)
+            return params
+        from libra_b200.models.qwen3 import ParamLayout, param_shapes
+        from libra_b200.parallel.tensor_parallel import shard_full_params
+
+        layout = ParamLayout(param_shapes(holder.cfg))  # full (TP=1) shapes, on the host
+        full = layout.views(torch.empty(layout.numel, dtype=torch.bfloat16))
+        load_params_into(full, path, cfg=holder.cfg)
+        for k, v in shard_full_params(full, holder.cfg, a.tp, holder.tp_rank).items():
+            params[k].copy_(v)
+        return params
+
     if a.checkpoint:
-        load_params_into(holder.params, a.checkpoint)
+        for k, v in load_disk(a.checkpoint).items():
+            holder.params[k].data.copy_(v)
     tok = load_tokenizer(a.tokenizer or a.checkpoint, holder.cfg.vocab_size)
     llm = LLMEngine(holder.cfg, {k: v.detach() for k, v in holder.params.items()},
                     kv_memory_fraction=a.kv_memory_fraction, max_batch_tokens=a.max_batch_tokens,
-                    instance_id=f"{a.host}:{a.port}", eos_token_id=getattr(tok, "eos_token_id", None))
+                    instance_id=f"{a.host}:{a.port}", eos_token_id=getattr(tok, "eos_token_id", None),
+                    tp_group=tp_group, tp_size=a.tp, tp_channel=channel)
 
     def loader(req: Dict[str, Any]):
         if req.get("kind") == "disk":
-            params = {k: v.clone() for k, v in holder.params.items()}
-            load_params_into(params, req["checkpoint_path"])
-            return params, req.get("version")
+            return load_disk(req["checkpoint_path"]), req.get("version")
         from libra_b200.infra.sync.peer_weight_sync import receive_peer_weights
 
         return receive_peer_weights(req, holder.params), req.get("version")
 
+    if rank > 0:
+        llm.tp_reload_hook = loader
+        llm.follower_loop()
+        return
     web.run_app(build_app(llm, tok, a.model, loader), host=a.host, port=a.port)
 
 

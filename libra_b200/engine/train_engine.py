@@ -117,9 +117,22 @@ class B200TrainEngine:
             torch.cuda.set_device(self.device)
             ops.ext()  # fail loudly when the kernels are not built
         self.max_seq_length = max_seq_length
+        self.tp_group, self.tp_rank, self.mesh = None, 0, None
+        if self.tp_size > 1:
+            # TP groups are consecutive ranks (inside the box); DP runs across them
+            from libra_b200.parallel.mesh import ParallelMesh
+
+            if not dist.is_initialized():
+                raise RuntimeError("tensor parallelism needs an initialized process group")
+            self.mesh = ParallelMesh(dist.get_world_size(), tp=self.tp_size)
+            rank = dist.get_rank()
+            self.tp_group = self.mesh.group("tp", rank)
+            self.tp_rank = self.mesh.coords(rank).tp
+            if self.dp_group is None:
+                self.dp_group = self.mesh.group("dp", rank)
         self.dp_size = dist.get_world_size(self.dp_group) if dist.is_initialized() else 1
         self.dp_rank = dist.get_rank(self.dp_group) if dist.is_initialized() else 0
-        shapes = param_shapes(self.cfg)
+        shapes = param_shapes(self.cfg, self.tp_size, self.tp_rank)
         self.layout = ParamLayout(shapes)
         P = self.layout.numel
         # pad so the flat buffer splits evenly into DP shards of 128-element multiples
@@ -129,7 +142,7 @@ class B200TrainEngine:
         self.flat_param = torch.zeros(self.padded_numel, dtype=torch.bfloat16, device=dev)
         self.flat_grad = torch.zeros(self.padded_numel, dtype=torch.float32, device=dev)
         views = self.layout.views(self.flat_param)
-        init_params(self.cfg, views, seed=self.seed)
+        init_params(self.cfg, views, seed=self.seed + 7919 * self.tp_rank)
         grad_views = self.layout.views(self.flat_grad)
         self.params: Dict[str, torch.nn.Parameter] = {}
         for name, v in views.items():
@@ -148,7 +161,23 @@ class B200TrainEngine:
         self.exp_avg_sq = torch.zeros_like(self.master)
         self.grad_shard = (torch.zeros(shard, dtype=torch.float32, device=dev) if self.sharded else self.flat_grad)
         self.sq_norm = torch.zeros(1, dtype=torch.float32, device=dev)
-        self.model = Qwen3Model(self.cfg, self.params, recompute=self.recompute_activations)
+        self.model = Qwen3Model(self.cfg, self.params, recompute=self.recompute_activations, tp_group=self.tp_group,
+                                tp_size=self.tp_size, tp_rank=self.tp_rank)
+        from libra_b200.parallel.tensor_parallel import tp_partial_grad_params
+
+        self._tp_partial = [self.params[n].main_grad for n in tp_partial_grad_params(list(self.params))
+                            ] if self.tp_size > 1 else []
+        # replicated (1-D) parameters inside this rank's optimizer shard: the
+        # global grad norm counts them once, not once per TP rank
+        self._tp_replicated = []
+        if self.tp_size > 1:
+            lo, hi = self.shard_start, self.shard_start + self.shard_numel
+            for n, p in self.params.items():
+                if p.dim() == 1:
+                    a, b = self.layout.segment(n)
+                    a, b = max(a, lo), min(b, hi)
+                    if a < b:
+                        self._tp_replicated.append((a - lo, b - lo))
 
     # ------------------------------------------------------------------ protocol helpers
     def get_version(self) -> int:
@@ -227,7 +256,7 @@ class B200TrainEngine:
             b = _pin_batch(packed["batch"])
             self.io_bytes["h2d"] += sum(t.numel() * t.element_size() for t in
                                         (b.tokens, b.positions, b.cu_seqlens, b.action_rows, b.action_targets,
-                                         b.seq_index, b.attn_tiles) if t is not None)
+                                         b.seq_index, b.attn_tiles, b.attn_kv_tiles) if t is not None)
             out = {"batch": b.to(dev, non_blocking=True)}
             for k, v in packed.items():
                 if k != "batch":
@@ -326,6 +355,8 @@ class B200TrainEngine:
             loss.backward()
             acc += torch.stack([loss.detach(), pg.detach(), kl.detach()])
         self._apply_elastic_inter_replica_gradients()
+        for g in self._tp_partial:  # per-head norm weights see only this rank's heads
+            dist.all_reduce(g, group=self.tp_group)
         self._reduce_gradients()
         self._publish_elastic_update()
         self._optimizer_step()
@@ -370,7 +401,17 @@ class B200TrainEngine:
         self.step_count += 1
         self.sq_norm.zero_()
         ops.grad_sq_norm(self.grad_shard, self.sq_norm)
-        if self.sharded:
+        if self.tp_size > 1:
+            rep = torch.zeros(1, dtype=torch.float32, device=self.device)
+            for a, b in self._tp_replicated:
+                rep += self.grad_shard[a:b].float().pow(2).sum()
+            both = torch.cat([self.sq_norm, rep])
+            if self.sharded:
+                dist.all_reduce(both, group=self.dp_group)
+            total = both[:1].clone()
+            dist.all_reduce(total, group=self.tp_group)
+            self.sq_norm.copy_(total - (self.tp_size - 1) * both[1:])
+        elif self.sharded:
             dist.all_reduce(self.sq_norm, op=dist.ReduceOp.SUM, group=self.dp_group)
         shard_param = self.flat_param[self.shard_start:self.shard_start + self.shard_numel]
         o = self.optim
@@ -575,7 +616,7 @@ def _fold_grad_into_main(p: torch.nn.Parameter) -> None:
 def _pin_batch(b: PackedBatch) -> PackedBatch:
     pin = lambda t: t if t is None or t.is_pinned() else t.pin_memory()  # noqa: E731
     return PackedBatch(pin(b.tokens), pin(b.positions), pin(b.cu_seqlens), b.max_seqlen, pin(b.action_rows),
-                       pin(b.action_targets), pin(b.seq_index), pin(b.attn_tiles))
+                       pin(b.action_targets), pin(b.seq_index), pin(b.attn_tiles), pin(b.attn_kv_tiles))
 
 
 def _merge_stats(stats: List[Dict[str, float]]) -> Dict[str, float]:

@@ -149,3 +149,31 @@ def test_mesh_layout():
     assert m.is_batch_source(0) and not m.is_batch_source(1) and m.is_pipeline_last(4)
     with pytest.raises(ValueError):
         ParallelMesh(8, tp=3)
+
+
+def _tp_engine_worker(rank, world, port, out_dir):
+    _init(rank, world, port)
+    from libra_b200.engine.train_engine import B200TrainEngine
+    from libra_b200.workflow.synthetic import GRPOWorkload, LengthDist
+
+    eng = B200TrainEngine("tiny", device="cpu", tp_size=2, learning_rate=1e-3, use_distributed_optimizer=False)
+    eng.initialize()
+    wl = GRPOWorkload("t", vocab_size=eng.cfg.vocab_size, prompts_per_step=2, group_size=4,
+                      prompt=LengthDist(12, 0.3, 4, 24), response=LengthDist(16, 0.3, 2, 32))
+    trajs = wl.trajectories(0)
+    eng.recompute_logprobs(trajs)
+    stats = eng.grpo_update(trajs)
+    assert stats["grad_norm"] > 0 and stats["loss"] == stats["loss"]
+    # replicated parameters must stay identical on both TP ranks
+    for n, p in eng.params.items():
+        if p.dim() == 1:
+            other = p.detach().clone()
+            dist.broadcast(other, src=0)
+            torch.testing.assert_close(p.detach(), other, rtol=0, atol=0, msg=n)
+    open(os.path.join(out_dir, f"tpe_ok_{rank}"), "w").close()
+    dist.destroy_process_group()
+
+
+def test_tp_engine_keeps_replicated_params_in_sync(tmp_path):
+    _spawn(_tp_engine_worker, 2, str(tmp_path))
+    assert {p.name for p in tmp_path.iterdir()} == {"tpe_ok_0", "tpe_ok_1"}

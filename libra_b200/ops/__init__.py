@@ -250,13 +250,14 @@ def swiglu(gu):
 def varlen_causal_attention(q, k, v, cu_seqlens, max_seqlen: int, scale=None, tiles=None):
     """Causal GQA attention over packed sequences (q [T,Hq,D], k/v [T,Hkv,D]).
 
-    ``tiles``: the (sequence, q tile) table of the packed batch, built once per
-    batch (``attention.attn_tiles``); computed from ``cu_seqlens`` when absent."""
+    ``tiles``: the (q tiles, kv tiles) tables of the packed batch, built once
+    per batch (``attention.attn_tiles``); computed from ``cu_seqlens`` when absent."""
     if q.device.type != "cuda":
         return ref.varlen_causal_attention(q, k, v, cu_seqlens, scale)
     from .attention import flash_varlen_causal
 
-    return flash_varlen_causal(q, k, v, cu_seqlens, max_seqlen, scale, tiles)
+    qt, kvt = tiles if isinstance(tiles, (tuple, list)) else (tiles, None)
+    return flash_varlen_causal(q, k, v, cu_seqlens, max_seqlen, scale, qt, kvt)
 
 
 # ---------------------------------------------------------------------------

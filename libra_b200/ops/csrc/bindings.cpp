@@ -30,7 +30,17 @@ torch::Tensor paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, tor
 namespace attn {
 std::vector<torch::Tensor> flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor cu_seqlens,
                                      torch::Tensor tiles, double scale, bool causal, torch::Tensor err);
+std::vector<torch::Tensor> flash_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
+                                     torch::Tensor out, torch::Tensor lse, torch::Tensor cu_seqlens,
+                                     torch::Tensor q_tiles, torch::Tensor kv_tiles, double scale, bool causal,
+                                     torch::Tensor err);
 }  // namespace attn
+namespace tp {
+std::vector<torch::Tensor> allreduce_add_rmsnorm(std::vector<int64_t> data_ptrs, std::vector<int64_t> flag_ptrs,
+                                                 int64_t me, int64_t slot_offset_bytes, torch::Tensor residual,
+                                                 torch::Tensor w, double eps, int64_t epoch, int64_t grid,
+                                                 torch::Tensor err);
+}  // namespace tp
 }  // namespace libra
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -49,4 +59,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &libra::adamw_step);
   m.def("paged_decode_attention", &libra::paged_decode_attention);
   m.def("flash_fwd", &libra::attn::flash_fwd, "tcgen05 varlen GQA attention forward");
+  m.def("flash_bwd", &libra::attn::flash_bwd, "tcgen05 varlen GQA attention backward (dq, dk, dv)");
+  m.def("tp_allreduce_add_rmsnorm", &libra::tp::allreduce_add_rmsnorm,
+        "peer-memory all-reduce of TP partials + residual + RMSNorm");
 }

@@ -107,11 +107,38 @@ def bench_elementwise(iters: int):
     print(json.dumps({"kernel": "adamw", "n": n, "ms": ms, "gbs": n * 30 / ms / 1e6}), flush=True)
 
 
+def bench_attention(iters: int, lens=None):
+    import math
+
+    from libra_b200.ops.attention import attn_tiles
+
+    cases = [lens] if lens else [[4096] * 4, [2048] * 8, [1024] * 16]
+    for ls in cases:
+        T, hq, hkv, d = sum(ls), 32, 8, 128
+        cu = torch.tensor([0] + list(torch.tensor(ls).cumsum(0).tolist()), dtype=torch.int32, device="cuda")
+        q = torch.randn(T, hq, d, device="cuda").bfloat16()
+        k = torch.randn(T, hkv, d, device="cuda").bfloat16()
+        v = torch.randn(T, hkv, d, device="cuda").bfloat16()
+        do = torch.randn(T, hq, d, device="cuda").bfloat16()
+        qt, kvt = attn_tiles(cu.tolist(), True, "cuda"), attn_tiles(cu.tolist(), True, "cuda", kv=True)
+        err = ops.error_flag(q.device)
+        sc = 1 / math.sqrt(d)
+        o, lse = ops.ext().flash_fwd(q, k, v, cu, qt, sc, True, err)
+        fwd_flops = sum(4 * L * L / 2 * d * hq for L in ls)
+        ms_f = _time(lambda: ops.ext().flash_fwd(q, k, v, cu, qt, sc, True, err), iters)
+        ms_b = _time(lambda: ops.ext().flash_bwd(do, q, k, v, o, lse, cu, qt, kvt, sc, True, err), iters)
+        print(json.dumps({"kernel": "flash_attn_tcgen05", "lens": f"{ls[0]}x{len(ls)}", "fwd_ms": ms_f,
+                          "fwd_tflops": fwd_flops / ms_f / 1e9, "bwd_ms": ms_b,
+                          "bwd_tflops_2.5x": 2.5 * fwd_flops / ms_b / 1e9}), flush=True)
+        ops.check_kernel_errors()
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "elementwise", "all"])
+    ap.add_argument("what", choices=["gemm", "elementwise", "attention", "all"])
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--shapes", default="", help="name:M,N,K,a_mn,b_mn;...")
+    ap.add_argument("--lens", default="", help="attention: sequence lengths, e.g. 2048x4")
     args = ap.parse_args()
     shapes = QWEN3_4B_SHAPES
     if args.shapes:
@@ -124,6 +151,12 @@ def main():
         bench_gemm(shapes, args.iters)
     if args.what in ("elementwise", "all"):
         bench_elementwise(args.iters)
+    if args.what in ("attention", "all"):
+        lens = None
+        if args.lens:
+            n, c = args.lens.split("x")
+            lens = [int(n)] * int(c)
+        bench_attention(args.iters, lens)
 
 
 if __name__ == "__main__":

@@ -84,3 +84,27 @@ def test_flash_matches_torch_flash_lse():
     to, tlse = torch.ops.aten._flash_attention_forward(q, k, v, cu, cu, max(lens), max(lens), 0.0, True, False)[:2]
     torch.testing.assert_close(o.float(), to.float(), rtol=2e-2, atol=2e-2)
     torch.testing.assert_close(lse, tlse.float(), rtol=1e-3, atol=2e-3)
+
+
+@pytest.mark.parametrize("lens,hq,hkv", [([128], 4, 1), ([1, 7, 130, 255, 256, 513], 8, 2), ([1000, 3, 1900], 32, 8)])
+def test_flash_backward_kernels_match_fp32_reference(lens, hq, hkv):
+    from libra_b200 import ops
+    from libra_b200.ops.attention import attn_tiles
+
+    q, k, v, cu = _inputs(lens, hq=hq, hkv=hkv, seed=11 + len(lens))
+    scale = 1.0 / math.sqrt(128)
+    cul = cu.tolist()
+    qt, kvt = attn_tiles(cul, True, "cuda"), attn_tiles(cul, True, "cuda", kv=True)
+    o, lse = ops.ext().flash_fwd(q, k, v, cu, qt, scale, True, ops.error_flag(q.device))
+    g = torch.Generator(device="cuda").manual_seed(3)
+    do = torch.randn(q.shape, device="cuda", generator=g).bfloat16()
+    dq, dk, dv = ops.ext().flash_bwd(do, q, k, v, o, lse, cu, qt, kvt, scale, True, ops.error_flag(q.device))
+    torch.cuda.synchronize()
+    ops.check_kernel_errors()
+    qr, kr, vr = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+    ro, _ = _ref_with_lse(qr, kr, vr, cu, scale)
+    (ro * do.float()).sum().backward()
+    for name, a, b in (("dq", dq, qr.grad), ("dk", dk, kr.grad), ("dv", dv, vr.grad)):
+        err = (a.float() - b).abs().max().item()
+        ref = b.abs().max().item()
+        assert err <= 2e-2 * max(ref, 1.0), f"{name}: max err {err} (max ref {ref})"

@@ -27,6 +27,8 @@ void adamw_step(torch::Tensor master, torch::Tensor grad, torch::Tensor m, torch
 torch::Tensor paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                                      torch::Tensor block_tables, torch::Tensor seq_lens, int64_t max_len,
                                      double scale);
+void gemm_swiglu(torch::Tensor x, torch::Tensor w, torch::Tensor a, c10::optional<torch::Tensor> gu,
+                 torch::Tensor err);
 namespace attn {
 std::vector<torch::Tensor> flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor cu_seqlens,
                                      torch::Tensor tiles, double scale, bool causal, torch::Tensor err);
@@ -35,6 +37,11 @@ std::vector<torch::Tensor> flash_bwd(torch::Tensor dout, torch::Tensor q, torch:
                                      torch::Tensor q_tiles, torch::Tensor kv_tiles, double scale, bool causal,
                                      torch::Tensor err);
 }  // namespace attn
+namespace ipc {
+std::tuple<py::bytes, int64_t> ipc_export(torch::Tensor t);
+int64_t ipc_open(py::bytes handle);
+void ipc_close(int64_t ptr);
+}  // namespace ipc
 namespace tp {
 std::vector<torch::Tensor> allreduce_add_rmsnorm(std::vector<int64_t> data_ptrs, std::vector<int64_t> flag_ptrs,
                                                  int64_t me, int64_t slot_offset_bytes, torch::Tensor residual,
@@ -47,6 +54,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "libra_b200 sm_100a kernels";
   m.def("gemm_bf16", &libra::gemm_bf16, "tcgen05 bf16 GEMM", py::arg("a"), py::arg("b"), py::arg("c"),
         py::arg("a_mn"), py::arg("b_mn"), py::arg("epi"), py::arg("residual"), py::arg("err"));
+  m.def("gemm_swiglu", &libra::gemm_swiglu, "tcgen05 gate/up GEMM with fused SwiGLU epilogue", py::arg("x"),
+        py::arg("w"), py::arg("a"), py::arg("gu"), py::arg("err"));
   m.def("rmsnorm_fwd", &libra::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &libra::rmsnorm_bwd);
   m.def("qk_norm_rope_fwd", &libra::qk_norm_rope_fwd);
@@ -60,6 +69,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_decode_attention", &libra::paged_decode_attention);
   m.def("flash_fwd", &libra::attn::flash_fwd, "tcgen05 varlen GQA attention forward");
   m.def("flash_bwd", &libra::attn::flash_bwd, "tcgen05 varlen GQA attention backward (dq, dk, dv)");
+  m.def("ipc_export", &libra::ipc::ipc_export, "CUDA IPC handle of the allocation holding a tensor + offset");
+  m.def("ipc_open", &libra::ipc::ipc_open, "map a peer allocation into the current device's context");
+  m.def("ipc_close", &libra::ipc::ipc_close);
   m.def("tp_allreduce_add_rmsnorm", &libra::tp::allreduce_add_rmsnorm,
         "peer-memory all-reduce of TP partials + residual + RMSNorm");
 }

@@ -35,22 +35,33 @@ class PeerAllReduce:
         self.slot_bytes = (self.max_rows * self.hidden * 2 + 255) // 256 * 256
         flag_bytes = MAX_CTAS * MAX_RANKS * 4
         self.buf = torch.zeros(2 * self.slot_bytes + flag_bytes, dtype=torch.uint8, device=device)
-        peers = [self.buf]
+        self.data_ptrs = [int(self.buf.data_ptr())]
+        self._opened = []
         if self.n > 1:
-            from torch.multiprocessing.reductions import reduce_tensor
-
+            # map every peer's buffer into THIS device's context, so kernels
+            # running here can load from it over NVLink
+            C = ops.ext()
             handles = [None] * self.n
-            dist.all_gather_object(handles, reduce_tensor(self.buf), group=self.group)
-            peers = []
-            for r, (fn, args) in enumerate(handles):
-                peers.append(self.buf if r == self.me else fn(*args))
-        self._peers = peers  # keep the mappings alive
-        self.data_ptrs = [int(t.data_ptr()) for t in peers]
+            dist.all_gather_object(handles, C.ipc_export(self.buf), group=self.group)
+            self.data_ptrs = []
+            with torch.cuda.device(self.buf.device):
+                for r, (h, off) in enumerate(handles):
+                    if r == self.me:
+                        self.data_ptrs.append(int(self.buf.data_ptr()))
+                    else:
+                        base = C.ipc_open(h)
+                        self._opened.append(base)
+                        self.data_ptrs.append(base + int(off))
         self.flag_ptrs = [p + 2 * self.slot_bytes for p in self.data_ptrs]
         self.epoch = 0
         if self.n > 1:
             torch.cuda.synchronize(device)
             dist.barrier(group=self.group)
+
+    def close(self) -> None:
+        for base in self._opened:
+            ops.ext().ipc_close(base)
+        self._opened = []
 
     def _slot(self, epoch: int) -> int:
         return epoch % 2

@@ -165,7 +165,7 @@ class InferenceRunner:
 
                 x = moe_mlp(h, x, p[pre + "router"], p[pre + "experts.w1"], p[pre + "experts.w2"], cfg)
             else:
-                x = self._row_parallel(ops.swiglu(ops.linear(h, p[pre + "gate_up_proj"])), p[pre + "down_proj"], x)
+                x = self._row_parallel(ops.linear_swiglu(h, p[pre + "gate_up_proj"]), p[pre + "down_proj"], x)
         last = ops.rmsnorm(x.index_select(0, last_rows), p["norm"], cfg.rms_norm_eps)
         logits = ops.linear(last, self.lm_head)
         if self.tp_size > 1:

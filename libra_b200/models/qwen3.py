@@ -322,8 +322,7 @@ class Qwen3Model(nn.Module):
             from libra_b200.models.moe import moe_mlp
 
             return moe_mlp(h, x, p[pre + "router"], p[pre + "experts.w1"], p[pre + "experts.w2"], cfg)
-        gu = ops.linear(self._tp_in(h), p[pre + "gate_up_proj"])
-        a = ops.swiglu(gu)
+        a = ops.linear_swiglu(self._tp_in(h), p[pre + "gate_up_proj"])
         return self._row_parallel(a, p[pre + "down_proj"], x)
 
     def _tp_in(self, h):

@@ -243,6 +243,42 @@ def swiglu(gu):
     return _SwiGLU.apply(gu.contiguous())
 
 
+class _LinearSwiGLU(torch.autograd.Function):
+    """a = silu(x Wg^T) * (x Wu^T) for W = [Wg; Wu] in one tcgen05 GEMM whose
+    epilogue applies SwiGLU; the pre-activation gate/up outputs are kept only
+    when a backward pass will need them."""
+
+    @staticmethod
+    def forward(ctx, x, weight):
+        x2d = x.reshape(-1, x.shape[-1])
+        if not x2d.is_contiguous():
+            x2d = x2d.contiguous()
+        M, F = x2d.shape[0], weight.shape[0] // 2
+        a = torch.empty(M, F, dtype=x.dtype, device=x.device)
+        need_grad = ctx.needs_input_grad[0] or ctx.needs_input_grad[1]
+        gu = torch.empty(M, 2 * F, dtype=x.dtype, device=x.device) if need_grad else None
+        ext().gemm_swiglu(x2d, weight, a, gu, error_flag(x.device))
+        ctx.save_for_backward(x2d, weight, gu)
+        ctx.in_shape = x.shape
+        return a.view(*x.shape[:-1], F)
+
+    @staticmethod
+    def backward(ctx, da):
+        x2d, weight, gu = ctx.saved_tensors
+        dgu = ext().swiglu_bwd(gu, da.reshape(gu.shape[0], -1).contiguous())
+        dx = gemm(dgu, weight, b_mn=True).view(ctx.in_shape) if ctx.needs_input_grad[0] else None
+        dw = _accumulate_wgrad(weight, dgu, x2d) if ctx.needs_input_grad[1] else None
+        return dx, dw
+
+
+def linear_swiglu(x, weight):
+    """SwiGLU MLP input half: silu(x W_gate^T) * (x W_up^T), W = [W_gate; W_up] ([2F, H])."""
+    F2 = weight.shape[0]
+    if x.device.type != "cuda" or F2 % 256 != 0:
+        return swiglu(linear(x, weight))
+    return _LinearSwiGLU.apply(x, weight)
+
+
 # ---------------------------------------------------------------------------
 # attention
 # ---------------------------------------------------------------------------
@@ -369,5 +405,5 @@ def grad_sq_norm(grad, out):
 
 __all__ = [
     "ext", "extension_available", "check_kernel_errors", "gemm", "linear", "rmsnorm", "qk_norm_rope", "swiglu",
-    "varlen_causal_attention", "lm_head_logprob", "adamw_step", "grad_sq_norm", "ref",
+    "varlen_causal_attention", "lm_head_logprob", "adamw_step", "grad_sq_norm", "ref", "linear_swiglu",
 ]

@@ -40,9 +40,13 @@ constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kTile;
 constexpr int kOffV = kOffK + kStages * kTile;
 constexpr int kOffP = kOffV + kStages * kTile;
-constexpr int kOffBar = kOffP + kTile;
-// q_full q_empty | k_full[2] v_full[2] kv_empty[2] | s_full[2] s_empty[2] | p_full pv_done o_empty done
-constexpr int kNumBars = 2 + 3 * kStages + 4 + 4;
+constexpr int kOffX = kOffP + kTile;  // row max / sum exchange between the two warps of a row: [2][2][128] fp32
+constexpr int kOffBar = kOffX + 2 * 2 * 128 * 4;
+// q_full q_empty | k_full[2] v_full[2] kv_empty[2] | s_full[2] s_empty[2] | p_full pv_done o_empty done grp
+constexpr int kNumBars = 2 + 3 * kStages + 4 + 5;
+// softmax: two warps per row (warps w and w+4 share a TMEM lane quarter), 64 columns each
+constexpr int kFwdSoftmaxWarps = 8;
+constexpr int kFwdThreads = 64 + 32 * kFwdSoftmaxWarps;
 constexpr int kSmemBytes = 1024 + kOffBar + 8 * kNumBars + 16;
 constexpr uint32_t kColO = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -65,7 +69,7 @@ __device__ __forceinline__ Item decode(int item, const int* __restrict__ cu, con
   return it;
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kFwdThreads, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const int* __restrict__ cu,
                      const int2* __restrict__ tiles, int n_tiles, int Hq, int Hkv, __nv_bfloat16* __restrict__ O,
@@ -84,7 +88,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* pv_done = p_full + 1;
   uint64_t* o_empty = pv_done + 1;
   uint64_t* done = o_empty + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* grp = done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(grp + 1);
+  float* xchg = reinterpret_cast<float*>(smem + kOffX);  // [parity][half][row]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -104,12 +110,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&s_empty[b], 4);
+      mbar_init(&s_empty[b], kFwdSoftmaxWarps);
     }
-    mbar_init(p_full, 4);
+    mbar_init(p_full, kFwdSoftmaxWarps);
     mbar_init(pv_done, 1);
-    mbar_init(o_empty, 4);
+    mbar_init(o_empty, kFwdSoftmaxWarps);
     mbar_init(done, 1);
+    mbar_init(grp, 32 * kFwdSoftmaxWarps);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
@@ -220,8 +227,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ softmax + epilogue
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
+    const int half = (warp - 2) >> 2;  // which 64 of the 128 key columns (and of the 128 O columns)
+    const int c0 = half * 64;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    uint32_t s_it = 0, pv_it = 0, item_it = 0;
+    uint32_t s_it = 0, pv_it = 0, item_it = 0, nsync = 0;
+    // exchange a per-row value with the partner warp (other half of the same row)
+    auto exchange = [&](float mine, float& theirs) -> bool {
+      const int par = nsync & 1;
+      xchg[(par * 2 + half) * 128 + row] = mine;
+      mbar_arrive(grp);
+      const bool okw = mbar_wait(grp, nsync & 1u, err, kTimeoutAttnS);
+      ++nsync;
+      theirs = xchg[(par * 2 + (half ^ 1)) * 128 + row];
+      return okw;
+    };
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++item_it) {
       const Item it = decode(item, cu, tiles, Hq, group, causal);
       const int qp = it.q0 + row;
@@ -231,26 +250,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int sb = s_it & 1;
         if (!mbar_wait(&s_full[sb], (s_it >> 1) & 1u, err, kTimeoutAttnS)) { ok = false; break; }
         tc_fence_after();
-        uint32_t r[128];
+        uint32_t r[64];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          tmem_ld_32x32b_x32(tmem_base + lane_addr + sb * BKV + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
+        for (int c = 0; c < 2; ++c)
+          tmem_ld_32x32b_x32(tmem_base + lane_addr + sb * BKV + c0 + c * 32,
+                             *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
         tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_empty[sb]);
         ++s_it;
         // scale into log2 units and mask
-        const int kb = j * BKV;
-        const int lim = causal ? min(qp + 1, it.L) : it.L;  // keys [kb, kb+128) below lim are visible
+        const int kb = j * BKV + c0;
+        const int lim = causal ? min(qp + 1, it.L) : it.L;  // keys below lim are visible
         float bm = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 128; ++c) {
+        for (int c = 0; c < 64; ++c) {
           float v = __uint_as_float(r[c]) * scale_log2;
           v = (kb + c < lim) ? v : -INFINITY;
           r[c] = __float_as_uint(v);
           bm = fmaxf(bm, v);
         }
+        float bm_other;
+        if (!exchange(bm, bm_other)) { ok = false; break; }
+        bm = fmaxf(bm, bm_other);  // both halves now hold the same block max
         const float m_new = fmaxf(m, bm);
         const bool rescale = (j > 0) && (m_new > m + kRescaleThreshold);
         if (j == 0) m = m_new;
@@ -261,13 +284,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (__any_sync(0xffffffffu, rescale)) {
           const float f = rescale ? ex2_approx(m - m_new) : 1.f;
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < 2; ++c) {
             uint32_t o[32];
-            tmem_ld_32x32b_x32(tmem_base + lane_addr + kColO + c * 32, o);
+            tmem_ld_32x32b_x32(tmem_base + lane_addr + kColO + c0 + c * 32, o);
             tmem_ld_wait();
 #pragma unroll
             for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
-            tmem_st_32x32b_x32(tmem_base + lane_addr + kColO + c * 32, o);
+            tmem_st_32x32b_x32(tmem_base + lane_addr + kColO + c0 + c * 32, o);
           }
           tmem_st_wait();
           if (rescale) {
@@ -275,14 +298,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             m = m_new;
           }
         }
-        // P = 2^(s - m) as bf16, row `row` of a 128B-swizzled K-major tile
+        // P = 2^(s - m) as bf16: this half's 64 columns of row `row` in the 128B-swizzled K-major tile
         float sum = 0.f;
 #pragma unroll
-        for (int vi = 0; vi < 16; ++vi) {
+        for (int j8 = 0; j8 < 8; ++j8) {
           float p[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            p[e] = ex2_approx(__uint_as_float(r[vi * 8 + e]) - m);
+            p[e] = ex2_approx(__uint_as_float(r[j8 * 8 + e]) - m);
             sum += p[e];
           }
           uint4 pk;
@@ -290,6 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           pk.y = pack_bf16x2(p[2], p[3]);
           pk.z = pack_bf16x2(p[4], p[5]);
           pk.w = pack_bf16x2(p[6], p[7]);
+          const int vi = half * 8 + j8;
           const int unit = (vi & 7) ^ (row & 7);
           *reinterpret_cast<uint4*>(smP + (vi >> 3) * kChunk + row * 128 + unit * 16) = pk;
         }
@@ -301,16 +325,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++pv_it;
       }
       if (!ok) break;
-      // epilogue
+      // epilogue: row sum of both halves, then this half's 64 O columns
+      float l_other;
+      if (!exchange(l, l_other)) break;
+      l += l_other;
       if (!mbar_wait(pv_done, (pv_it - 1) & 1u, err, kTimeoutAttnPV)) break;
       tc_fence_after();
       const bool row_ok = qp < it.L;
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* orow = O + ((size_t)(it.s0 + qp) * Hq + it.h) * D;
+      __nv_bfloat16* orow = O + ((size_t)(it.s0 + qp) * Hq + it.h) * D + c0;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t o[32];
-        tmem_ld_32x32b_x32(tmem_base + lane_addr + kColO + c * 32, o);
+        tmem_ld_32x32b_x32(tmem_base + lane_addr + kColO + c0 + c * 32, o);
         tmem_ld_wait();
         if (row_ok) {
 #pragma unroll
@@ -327,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(o_empty);
-      if (row_ok) lse[(size_t)it.h * T + it.s0 + qp] = (m + lg2_approx(l)) * 0.6931471805599453f;
+      if (row_ok && half == 0) lse[(size_t)it.h * T + it.s0 + qp] = (m + lg2_approx(l)) * 0.6931471805599453f;
     }
   }
 
@@ -368,7 +395,7 @@ std::vector<torch::Tensor> flash_fwd(torch::Tensor q, torch::Tensor k, torch::Te
   const int items = n_tiles * Hq;
   const int grid = items < sms ? items : sms;
   const float scale_log2 = (float)(scale * 1.4426950408889634);
-  flash_fwd_kernel<<<grid, kThreads, kSmemBytes, at::cuda::getCurrentCUDAStream()>>>(
+  flash_fwd_kernel<<<grid, kFwdThreads, kSmemBytes, at::cuda::getCurrentCUDAStream()>>>(
       mq, mk, mv, cu_seqlens.data_ptr<int>(), reinterpret_cast<const int2*>(tiles.data_ptr<int>()), n_tiles, Hq, Hkv,
       reinterpret_cast<__nv_bfloat16*>(o.data_ptr()), lse.data_ptr<float>(), T, scale_log2, causal ? 1 : 0,
       err.data_ptr<int>());

@@ -38,7 +38,15 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = one 128-byte swizzle row
 constexpr int kThreads = 192;
 
-enum Epilogue : int { kStoreBf16 = 0, kStoreF32 = 1, kAccumF32 = 2, kStoreBf16AddResidual = 3 };
+enum Epilogue : int { kStoreBf16 = 0, kStoreF32 = 1, kAccumF32 = 2, kStoreBf16AddResidual = 3, kSwiGLU = 4 };
+
+// kSwiGLU (fused gate/up projection + SwiGLU): B is the [2F, K] gate_up
+// weight; the B tile of output block nb stacks gate rows [128 nb, 128 nb + 128)
+// on top of up rows [F + 128 nb, ...), so TMEM columns [0,128) hold the gate
+// and [128,256) the up projection of the same 128 features.  The epilogue
+// writes a = silu(gate) * up into C ([M, F]) and, when C2 is given, the
+// pre-activation gate/up values into C2 ([M, 2F]) for the backward pass.
+__device__ __forceinline__ float silu_f(float x) { return x * (1.f / (1.f + __expf(-x))); }
 
 template <int BN>
 struct Cfg {
@@ -69,7 +77,11 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* __restrict__ C,
-                     const __nv_bfloat16* __restrict__ R, int M, int N, int K, int ldc, int ldr, int* err) {
+                     const __nv_bfloat16* __restrict__ R, int M, int N, int K, int ldc, int ldr, int* err,
+                     __nv_bfloat16* __restrict__ C2, int ldc2) {
+  static_assert(EPI != kSwiGLU || (BN == 256 && !B_MN), "SwiGLU epilogue: BN 256, K-major weight");
+  // output columns per tile: BN, or 128 features for SwiGLU (N is then F)
+  constexpr int kTileN = EPI == kSwiGLU ? 128 : BN;
   using CF = Cfg<BN>;
   constexpr int S = CF::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -86,7 +98,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_m = (M + BM - 1) / BM;
-  const int num_n = (N + BN - 1) / BN;
+  const int num_n = (N + kTileN - 1) / kTileN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (K + BK - 1) / BK;
 
@@ -133,7 +145,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             tma_load_2d(a_dst, &tmA, &full[stage], k0, m0);
           }
-          if (B_MN) {
+          if (EPI == kSwiGLU) {  // gate rows then up rows of the same 128 features
+            tma_load_2d(b_dst, &tmB, &full[stage], k0, nb * 128);
+            tma_load_2d(b_dst + 128 * BK * 2, &tmB, &full[stage], k0, N + nb * 128);
+          } else if (B_MN) {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 64 * BK * 2, &tmB, &full[stage], n0 + j * 64, k0);
           } else {
@@ -201,6 +216,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int row = mb * BM + row_in_tile;
       const bool row_ok = row < M;
+      if (EPI == kSwiGLU) {
+#pragma unroll 1
+        for (int chunk = 0; chunk < 4; ++chunk) {
+          uint32_t g[32], u[32];
+          const uint32_t t0 = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + chunk * 32;
+          tmem_ld_32x32b_x32(t0, g);
+          tmem_ld_32x32b_x32(t0 + 128, u);
+          tmem_ld_wait();
+          const int col0 = nb * 128 + chunk * 32;
+          if (!row_ok || col0 >= N) continue;
+          __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(C) + (size_t)row * ldc + col0;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float a[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              // round gate/up to bf16 first so the result equals the unfused gate_up -> swiglu path
+              const float gv = __bfloat162float(__float2bfloat16(__uint_as_float(g[j * 8 + e])));
+              const float uv = __bfloat162float(__float2bfloat16(__uint_as_float(u[j * 8 + e])));
+              a[e] = silu_f(gv) * uv;
+            }
+            uint4 pk;
+            pk.x = pack_bf16x2(a[0], a[1]);
+            pk.y = pack_bf16x2(a[2], a[3]);
+            pk.z = pack_bf16x2(a[4], a[5]);
+            pk.w = pack_bf16x2(a[6], a[7]);
+            *reinterpret_cast<uint4*>(out + j * 8) = pk;
+            if (C2 != nullptr) {
+              uint4 pg, pu;
+              pg.x = pack_bf16x2(__uint_as_float(g[j * 8 + 0]), __uint_as_float(g[j * 8 + 1]));
+              pg.y = pack_bf16x2(__uint_as_float(g[j * 8 + 2]), __uint_as_float(g[j * 8 + 3]));
+              pg.z = pack_bf16x2(__uint_as_float(g[j * 8 + 4]), __uint_as_float(g[j * 8 + 5]));
+              pg.w = pack_bf16x2(__uint_as_float(g[j * 8 + 6]), __uint_as_float(g[j * 8 + 7]));
+              pu.x = pack_bf16x2(__uint_as_float(u[j * 8 + 0]), __uint_as_float(u[j * 8 + 1]));
+              pu.y = pack_bf16x2(__uint_as_float(u[j * 8 + 2]), __uint_as_float(u[j * 8 + 3]));
+              pu.z = pack_bf16x2(__uint_as_float(u[j * 8 + 4]), __uint_as_float(u[j * 8 + 5]));
+              pu.w = pack_bf16x2(__uint_as_float(u[j * 8 + 6]), __uint_as_float(u[j * 8 + 7]));
+              __nv_bfloat16* gr = C2 + (size_t)row * ldc2 + col0 + j * 8;
+              *reinterpret_cast<uint4*>(gr) = pg;
+              *reinterpret_cast<uint4*>(gr + N) = pu;
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        continue;
+      }
 #pragma unroll 1
       for (int chunk = 0; chunk < BN / 32; ++chunk) {
         uint32_t r[32];
@@ -320,7 +383,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, void* c, const 
   }
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  kern<<<grid, kThreads, smem, st>>>(ta, tb, c, r, M, N, K, ldc, ldr, err);
+  kern<<<grid, kThreads, smem, st>>>(ta, tb, c, r, M, N, K, ldc, ldr, err, nullptr, 0);
   LIBRA_LAUNCH_CHECK();
 }
 
@@ -333,7 +396,61 @@ static void dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CU
   else launch<BN, true, false, EPI>(ta, tb, c, r, M, N, K, ldc, ldr, err, st);
 }
 
+// SwiGLU launch (K-major A, K-major gate_up weight).
+static void launch_swiglu(const CUtensorMap& ta, const CUtensorMap& tb, __nv_bfloat16* a_out, int lda_out,
+                          __nv_bfloat16* gu_out, int ldgu, int M, int F, int K, int* err, cudaStream_t st) {
+  auto kern = gemm_bf16_kernel<256, false, false, kSwiGLU>;
+  constexpr int smem = Cfg<256>::kSmemBytes;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    configured = true;
+  }
+  const int tiles = ((M + BM - 1) / BM) * (F / 128);
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  kern<<<grid, kThreads, smem, st>>>(ta, tb, a_out, nullptr, M, F, K, lda_out, 0, err, gu_out, ldgu);
+  LIBRA_LAUNCH_CHECK();
+}
+
 }  // namespace gemm
+
+// Fused gate/up projection + SwiGLU: a = silu(x w_gate^T) * (x w_up^T) with
+// w = [w_gate; w_up] ([2F, K], K-major), x [M, K].  a: [M, F] bf16.  gu
+// (optional, [M, 2F] bf16) receives the pre-activation gate/up outputs.
+void gemm_swiglu(torch::Tensor x, torch::Tensor w, torch::Tensor a, c10::optional<torch::Tensor> gu,
+                 torch::Tensor err) {
+  using namespace gemm;
+  LIBRA_CHECK(x.is_cuda() && w.is_cuda() && a.is_cuda() && x.scalar_type() == at::kBFloat16 &&
+                  w.scalar_type() == at::kBFloat16 && a.scalar_type() == at::kBFloat16,
+              "gemm_swiglu: CUDA bf16 tensors required");
+  LIBRA_CHECK(x.dim() == 2 && w.dim() == 2 && a.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1 &&
+                  a.stride(1) == 1, "gemm_swiglu: 2-D tensors with inner stride 1");
+  const int64_t M = x.size(0), K = x.size(1), F2 = w.size(0);
+  LIBRA_CHECK(w.size(1) == K && F2 % 256 == 0, "gemm_swiglu: weight [2F, K] with F a multiple of 128");
+  const int64_t F = F2 / 2;
+  LIBRA_CHECK(a.size(0) == M && a.size(1) == F, "gemm_swiglu: output must be [M, F]");
+  LIBRA_CHECK(x.stride(0) % 8 == 0 && w.stride(0) % 8 == 0 && a.stride(0) % 8 == 0 && K >= 1,
+              "gemm_swiglu: leading dimensions must be multiples of 8");
+  LIBRA_CHECK((reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0 && (reinterpret_cast<uintptr_t>(w.data_ptr()) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(a.data_ptr()) & 15) == 0,
+              "gemm_swiglu: 16-byte aligned base pointers required");
+  __nv_bfloat16* gup = nullptr;
+  int ldgu = 0;
+  if (gu.has_value()) {
+    LIBRA_CHECK(gu->scalar_type() == at::kBFloat16 && gu->dim() == 2 && gu->size(0) == M && gu->size(1) == F2 &&
+                    gu->stride(1) == 1 && gu->stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(gu->data_ptr()) & 15) == 0,
+                "gemm_swiglu: gu must be bf16 [M, 2F] with 16-byte rows");
+    gup = reinterpret_cast<__nv_bfloat16*>(gu->data_ptr());
+    ldgu = (int)gu->stride(0);
+  }
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  CUtensorMap ta = make_map(x.data_ptr(), K, M, x.stride(0), 64, BM);
+  CUtensorMap tb = make_map(w.data_ptr(), K, F2, w.stride(0), 64, 128);
+  launch_swiglu(ta, tb, reinterpret_cast<__nv_bfloat16*>(a.data_ptr()), (int)a.stride(0), gup, ldgu, (int)M, (int)F,
+                (int)K, err.data_ptr<int>(), st);
+}
 
 // Python entry: C (op)= A x B^T in the layouts described at the top of the file.
 //   a: [M, K] (a_mn=false) or [K, M] (a_mn=true), bf16, inner stride 1

@@ -226,3 +226,26 @@ def test_engine_step_reduces_loss():
     for _ in range(4):
         last = eng.grpo_update(trajs)["loss"]
     assert last < first
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,K,F", [(300, 512, 256), (4096, 2560, 9728), (1, 128, 128)])
+def test_linear_swiglu_matches_unfused(M, K, F):
+    from libra_b200 import ops
+
+    g = torch.Generator(device="cuda").manual_seed(M + F)
+    x = (torch.randn(M, K, device="cuda", generator=g) * 0.5).bfloat16().requires_grad_(True)
+    w = (torch.randn(2 * F, K, device="cuda", generator=g) / K ** 0.5).bfloat16().requires_grad_(True)
+    a = ops.linear_swiglu(x, w)
+    x2, w2 = x.detach().clone().requires_grad_(True), w.detach().clone().requires_grad_(True)
+    a2 = ops.swiglu(ops.linear(x2, w2))
+    torch.cuda.synchronize()
+    ops.check_kernel_errors()
+    torch.testing.assert_close(a.float(), a2.float(), rtol=1e-2, atol=1e-2)
+    da = torch.randn_like(a)
+    a.backward(da)
+    a2.backward(da)
+    torch.testing.assert_close(x.grad.float(), x2.grad.float(), rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(w.grad.float(), w2.grad.float(), rtol=1e-2, atol=1e-2)
+    with torch.no_grad():  # inference path: no gate/up buffer kept
+        torch.testing.assert_close(ops.linear_swiglu(x, w).float(), a2.float(), rtol=1e-2, atol=1e-2)

@@ -102,13 +102,13 @@ class InferenceRunner:
                     cu_k.append(cu_k[-1] + len(it.tokens))
                     rows.append(torch.arange(offsets[i], offsets[i] + n_new, device=dev))
                 rows_t = torch.cat(rows)
-                from torch.nn.attention.varlen import varlen_attn
+                from libra_b200.ops.attention import attn_tiles
 
-                o = varlen_attn(q.index_select(0, rows_t).contiguous(), torch.cat(ks), torch.cat(vs),
-                                torch.tensor(cu_q, device=dev, dtype=torch.int32),
-                                torch.tensor(cu_k, device=dev, dtype=torch.int32),
-                                max(b - a for a, b in zip(cu_q[:-1], cu_q[1:])),
-                                max(b - a for a, b in zip(cu_k[:-1], cu_k[1:])), window_size=(-1, 0))
+                # queries are the new suffix of each sequence; keys span the whole (cached) prefix
+                o, _ = ops.ext().flash_fwd(q.index_select(0, rows_t).contiguous(), torch.cat(ks).contiguous(),
+                                           torch.cat(vs).contiguous(), torch.tensor(cu_q, device=dev, dtype=torch.int32),
+                                           attn_tiles(cu_q, True, dev), self.scale, True, ops.error_flag(dev),
+                                           torch.tensor(cu_k, device=dev, dtype=torch.int32))
                 out.index_copy_(0, rows_t, o)
             else:
                 for i in ext:

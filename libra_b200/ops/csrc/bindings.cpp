@@ -31,7 +31,8 @@ void gemm_swiglu(torch::Tensor x, torch::Tensor w, torch::Tensor a, c10::optiona
                  torch::Tensor err);
 namespace attn {
 std::vector<torch::Tensor> flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor cu_seqlens,
-                                     torch::Tensor tiles, double scale, bool causal, torch::Tensor err);
+                                     torch::Tensor tiles, double scale, bool causal, torch::Tensor err,
+                                     c10::optional<torch::Tensor> cu_k);
 std::vector<torch::Tensor> flash_bwd(torch::Tensor dout, torch::Tensor q, torch::Tensor k, torch::Tensor v,
                                      torch::Tensor out, torch::Tensor lse, torch::Tensor cu_seqlens,
                                      torch::Tensor q_tiles, torch::Tensor kv_tiles, double scale, bool causal,
@@ -67,7 +68,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grad_sq_norm", &libra::grad_sq_norm);
   m.def("adamw_step", &libra::adamw_step);
   m.def("paged_decode_attention", &libra::paged_decode_attention);
-  m.def("flash_fwd", &libra::attn::flash_fwd, "tcgen05 varlen GQA attention forward");
+  m.def("flash_fwd", &libra::attn::flash_fwd, "tcgen05 varlen GQA attention forward", py::arg("q"), py::arg("k"),
+        py::arg("v"), py::arg("cu_seqlens"), py::arg("tiles"), py::arg("scale"), py::arg("causal"), py::arg("err"),
+        py::arg("cu_k") = py::none());
   m.def("flash_bwd", &libra::attn::flash_bwd, "tcgen05 varlen GQA attention backward (dq, dk, dv)");
   m.def("ipc_export", &libra::ipc::ipc_export, "CUDA IPC handle of the allocation holding a tensor + offset");
   m.def("ipc_open", &libra::ipc::ipc_open, "map a peer allocation into the current device's context");

@@ -51,28 +51,36 @@ constexpr int kSmemBytes = 1024 + kOffBar + 8 * kNumBars + 16;
 constexpr uint32_t kColO = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
+// One work item.  Queries may be the suffix of their sequence (prefix-cached
+// extend): q rows [s0, s0 + L) of the packed q tensor are positions
+// [off, off + L) of a key sequence stored at rows [k0, k0 + Lk) of k/v, with
+// off = Lk - L (0 in training, where cu_k == cu_q).
 struct Item {
-  int s0, L, q0, h, hk, nkv;
+  int s0, L, q0, h, hk, nkv, k0, Lk, off;
 };
 
-__device__ __forceinline__ Item decode(int item, const int* __restrict__ cu, const int2* __restrict__ tiles, int Hq,
-                                       int group, int causal) {
+__device__ __forceinline__ Item decode(int item, const int* __restrict__ cu, const int* __restrict__ cu_k,
+                                       const int2* __restrict__ tiles, int Hq, int group, int causal) {
   const int2 t = tiles[item / Hq];
   Item it;
   it.h = item % Hq;
   it.hk = it.h / group;
   it.s0 = cu[t.x];
   it.L = cu[t.x + 1] - it.s0;
+  it.k0 = cu_k[t.x];
+  it.Lk = cu_k[t.x + 1] - it.k0;
+  it.off = it.Lk - it.L;
   it.q0 = t.y * BQ;
-  const int nall = (it.L + BKV - 1) / BKV;
-  it.nkv = causal ? min(t.y + 1, nall) : nall;
+  const int nall = (it.Lk + BKV - 1) / BKV;
+  // causal: key blocks up to the one holding the tile's last query position
+  it.nkv = causal ? min((it.off + it.q0 + BQ - 1) / BKV + 1, nall) : nall;
   return it;
 }
 
 __global__ void __launch_bounds__(kFwdThreads, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const int* __restrict__ cu,
-                     const int2* __restrict__ tiles, int n_tiles, int Hq, int Hkv, __nv_bfloat16* __restrict__ O,
+                     const int* __restrict__ cu_k, const int2* __restrict__ tiles, int n_tiles, int Hq, int Hkv, __nv_bfloat16* __restrict__ O,
                      float* __restrict__ lse, int T, float scale_log2, int causal, int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -138,7 +146,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       uint32_t last_k_par[kStages] = {0, 0}, last_v_par[kStages] = {0, 0};
       bool k_issued[kStages] = {false, false};
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++item_it) {
-        const Item it = decode(item, cu, tiles, Hq, group, causal);
+        const Item it = decode(item, cu, cu_k, tiles, Hq, group, causal);
         if (!mbar_wait(q_empty, (item_it & 1u) ^ 1u, err, kTimeoutAttnQ)) { ok = false; break; }
         mbar_expect_tx(q_full, kTile);
         tma_load_2d(smQ, &tmQ, q_full, it.h * D, it.s0 + it.q0);
@@ -149,7 +157,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           const int st = kv_it % kStages;
           const uint32_t ph = (kv_it / kStages) & 1u;
           if (!mbar_wait(&kv_empty[st], ph ^ 1u, err, kTimeoutAttnKV)) { ok = false; break; }
-          const int y = it.s0 + j * BKV;
+          const int y = it.k0 + j * BKV;
           mbar_expect_tx(&k_full[st], kTile);
           tma_load_2d(smK + st * kTile, &tmK, &k_full[st], it.hk * D, y);
           tma_load_2d(smK + st * kTile + kChunk, &tmK, &k_full[st], it.hk * D + 64, y);
@@ -178,7 +186,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       uint32_t kv_it = 0, s_it = 0, pv_it = 0, item_it = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++item_it) {
-        const Item it = decode(item, cu, tiles, Hq, group, causal);
+        const Item it = decode(item, cu, cu_k, tiles, Hq, group, causal);
         if (!mbar_wait(q_full, item_it & 1u, err, kTimeoutAttnQ)) { ok = false; break; }
         tc_fence_after();
         auto issue_s = [&](int j) -> bool {
@@ -242,7 +250,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       return okw;
     };
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++item_it) {
-      const Item it = decode(item, cu, tiles, Hq, group, causal);
+      const Item it = decode(item, cu, cu_k, tiles, Hq, group, causal);
       const int qp = it.q0 + row;
       float m = -INFINITY, l = 0.f;
       bool ok = true;
@@ -262,7 +270,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         ++s_it;
         // scale into log2 units and mask
         const int kb = j * BKV + c0;
-        const int lim = causal ? min(qp + 1, it.L) : it.L;  // keys below lim are visible
+        const int lim = causal ? min(it.off + qp + 1, it.Lk) : it.Lk;  // keys below lim are visible
         float bm = -INFINITY;
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
@@ -365,16 +373,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 }
 
 // tiles: int32 [n, 2] = (sequence index, q tile index) on the device.
+// cu_k: key offsets when the queries are the suffix of their sequences
+// (prefix-cached extend); defaults to cu_seqlens (training, self-attention).
 std::vector<torch::Tensor> flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor cu_seqlens,
-                                     torch::Tensor tiles, double scale, bool causal, torch::Tensor err) {
+                                     torch::Tensor tiles, double scale, bool causal, torch::Tensor err,
+                                     c10::optional<torch::Tensor> cu_k) {
   check_qkv(q, "q");
   check_qkv(k, "k");
   check_qkv(v, "v");
   const int T = (int)q.size(0), Hq = (int)q.size(1), Hkv = (int)k.size(1);
-  LIBRA_CHECK(k.size(0) == T && v.size(0) == T && v.size(1) == Hkv && Hkv > 0 && Hq % Hkv == 0,
-              "flash_attn: q/k/v token counts must match and Hq must be a multiple of Hkv");
+  LIBRA_CHECK(v.size(0) == k.size(0) && v.size(1) == Hkv && Hkv > 0 && Hq % Hkv == 0,
+              "flash_attn: k/v token counts must match and Hq must be a multiple of Hkv");
   LIBRA_CHECK(cu_seqlens.is_cuda() && cu_seqlens.scalar_type() == at::kInt && cu_seqlens.is_contiguous(),
               "flash_attn: cu_seqlens must be a contiguous CUDA int32 tensor");
+  const torch::Tensor& cuk = cu_k.has_value() ? *cu_k : cu_seqlens;
+  LIBRA_CHECK(cuk.is_cuda() && cuk.scalar_type() == at::kInt && cuk.is_contiguous() &&
+                  cuk.numel() == cu_seqlens.numel(),
+              "flash_attn: cu_k must be a contiguous CUDA int32 tensor shaped like cu_seqlens");
+  LIBRA_CHECK(cu_k.has_value() || k.size(0) == T, "flash_attn: q and k token counts differ but no cu_k given");
   LIBRA_CHECK(tiles.is_cuda() && tiles.scalar_type() == at::kInt && tiles.dim() == 2 && tiles.size(1) == 2 &&
                   tiles.is_contiguous(),
               "flash_attn: tiles must be a contiguous CUDA int32 [n, 2] tensor");
@@ -382,7 +398,7 @@ std::vector<torch::Tensor> flash_fwd(torch::Tensor q, torch::Tensor k, torch::Te
   auto o = torch::empty_like(q);
   auto lse = torch::empty({Hq, T}, q.options().dtype(at::kFloat));
   const int n_tiles = (int)tiles.size(0);
-  if (T == 0 || n_tiles == 0) return {o, lse};
+  if (T == 0 || n_tiles == 0 || k.size(0) == 0) return {o, lse};
   const CUtensorMap mq = head_map(q), mk = head_map(k), mv = head_map(v);
   static bool configured = false;
   if (!configured) {
@@ -396,9 +412,9 @@ std::vector<torch::Tensor> flash_fwd(torch::Tensor q, torch::Tensor k, torch::Te
   const int grid = items < sms ? items : sms;
   const float scale_log2 = (float)(scale * 1.4426950408889634);
   flash_fwd_kernel<<<grid, kFwdThreads, kSmemBytes, at::cuda::getCurrentCUDAStream()>>>(
-      mq, mk, mv, cu_seqlens.data_ptr<int>(), reinterpret_cast<const int2*>(tiles.data_ptr<int>()), n_tiles, Hq, Hkv,
-      reinterpret_cast<__nv_bfloat16*>(o.data_ptr()), lse.data_ptr<float>(), T, scale_log2, causal ? 1 : 0,
-      err.data_ptr<int>());
+      mq, mk, mv, cu_seqlens.data_ptr<int>(), cuk.data_ptr<int>(), reinterpret_cast<const int2*>(tiles.data_ptr<int>()),
+      n_tiles, Hq, Hkv, reinterpret_cast<__nv_bfloat16*>(o.data_ptr()), lse.data_ptr<float>(), T, scale_log2,
+      causal ? 1 : 0, err.data_ptr<int>());
   LIBRA_LAUNCH_CHECK();
   return {o, lse};
 }

@@ -108,3 +108,33 @@ def test_flash_backward_kernels_match_fp32_reference(lens, hq, hkv):
         err = (a.float() - b).abs().max().item()
         ref = b.abs().max().item()
         assert err <= 2e-2 * max(ref, 1.0), f"{name}: max err {err} (max ref {ref})"
+
+
+def test_flash_forward_prefix_extend_matches_reference():
+    """Queries = the last n tokens of each sequence, keys = the whole sequence."""
+    from libra_b200 import ops
+    from libra_b200.ops.attention import attn_tiles
+
+    g = torch.Generator(device="cuda").manual_seed(21)
+    lens_k, lens_q = [300, 1000, 129, 7], [1, 200, 129, 3]
+    hq, hkv, d = 8, 2, 128
+    ks = [torch.randn(L, hkv, d, device="cuda", generator=g).bfloat16() for L in lens_k]
+    vs = [torch.randn(L, hkv, d, device="cuda", generator=g).bfloat16() for L in lens_k]
+    qs = [torch.randn(L, hq, d, device="cuda", generator=g).bfloat16() for L in lens_k]
+    cu_q = [0]
+    cu_k = [0]
+    for a, b in zip(lens_q, lens_k):
+        cu_q.append(cu_q[-1] + a)
+        cu_k.append(cu_k[-1] + b)
+    qx = torch.cat([q[L - n:] for q, L, n in zip(qs, lens_k, lens_q)])
+    scale = 1.0 / math.sqrt(d)
+    o, _ = ops.ext().flash_fwd(qx, torch.cat(ks), torch.cat(vs), torch.tensor(cu_q, device="cuda", dtype=torch.int32),
+                               attn_tiles(cu_q, True, "cuda"), scale, True, ops.error_flag(qx.device),
+                               torch.tensor(cu_k, device="cuda", dtype=torch.int32))
+    torch.cuda.synchronize()
+    ops.check_kernel_errors()
+    refs = []
+    for q, k, v, L, n in zip(qs, ks, vs, lens_k, lens_q):
+        full, _ = _ref_with_lse(q, k, v, torch.tensor([0, L], device="cuda", dtype=torch.int32), scale)
+        refs.append(full[L - n:])
+    torch.testing.assert_close(o.float(), torch.cat(refs), rtol=2e-2, atol=2e-2)

@@ -29,10 +29,13 @@ def main():
     ap.add_argument("--total-steps", type=int, default=0)
     ap.add_argument("--log-dir", default="")
     ap.add_argument("--stats-out", default="")
+    ap.add_argument("--eval-interval", type=int, default=-1, help="override eval_interval (-1 = keep the config's)")
     a = ap.parse_args()
     cfg = load_config(a.config)
     if a.total_steps:
         cfg.total_steps = a.total_steps
+    if a.eval_interval >= 0:
+        cfg.eval_interval = a.eval_interval
     if a.log_dir:
         cfg.log_dir = a.log_dir
         cfg.sync_path = os.path.join(a.log_dir, "weights")

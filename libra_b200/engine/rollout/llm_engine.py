@@ -35,6 +35,7 @@ from libra_b200.engine.rollout.kv_cache import PagedKVCache
 from libra_b200.engine.rollout.runner import InferenceRunner, WorkItem
 from libra_b200.engine.rollout.sampler import SamplingParams, sample
 from libra_b200.models.qwen3 import Qwen3Config
+from libra_b200.utils import nvtx
 
 
 @dataclass
@@ -319,7 +320,8 @@ class LLMEngine:
             return 0
         items = [WorkItem(r.request_id, r.tokens, r.cached) for r in batch]
         self._publish(items)
-        logits = self.runner.step(items)
+        with nvtx.nvtx_range("prefill" if admitted else "decode"):
+            logits = self.runner.step(items)
         temps = torch.tensor([r.params.temperature for r in batch], device=logits.device, dtype=torch.float32)
         top_p = torch.tensor([r.params.top_p for r in batch], device=logits.device, dtype=torch.float32)
         top_k = torch.tensor([r.params.top_k for r in batch], device=logits.device, dtype=torch.long)

@@ -37,6 +37,7 @@ import torch.distributed as dist
 from libra_b200 import ops
 from libra_b200.models.qwen3 import (PackedBatch, ParamLayout, Qwen3Config, Qwen3Model, get_config, init_params,
                                      pack_sequences, param_shapes)
+from libra_b200.utils import nvtx
 
 
 class TrainEngine(Protocol):
@@ -320,7 +321,8 @@ class B200TrainEngine:
         results = []
         for chunk, host in self.prepare_recompute(trajectories):
             dev_mb = self.to_device(host)
-            lp = self.model.action_logprobs(dev_mb["batch"], self.temperature)
+            with nvtx.nvtx_range("recompute_forward"):
+                lp = self.model.action_logprobs(dev_mb["batch"], self.temperature)
             results.append((chunk, host["batch"], lp.to("cpu", non_blocking=True)))
             self.io_bytes["d2h"] += lp.numel() * lp.element_size()
         if self.device.type == "cuda":
@@ -350,16 +352,19 @@ class B200TrainEngine:
         self.flat_grad.zero_()
         acc = torch.zeros(3, dtype=torch.float32, device=self.device)
         for mb in device_micro_batches:
-            logp = self.model.action_logprobs(mb["batch"], self.temperature)
-            loss, pg, kl = self.loss(logp, mb["old_logp"], mb["adv"], mb.get("w"))
-            loss.backward()
+            with nvtx.nvtx_range("forward_backward"):
+                logp = self.model.action_logprobs(mb["batch"], self.temperature)
+                loss, pg, kl = self.loss(logp, mb["old_logp"], mb["adv"], mb.get("w"))
+                loss.backward()
             acc += torch.stack([loss.detach(), pg.detach(), kl.detach()])
-        self._apply_elastic_inter_replica_gradients()
-        for g in self._tp_partial:  # per-head norm weights see only this rank's heads
-            dist.all_reduce(g, group=self.tp_group)
-        self._reduce_gradients()
-        self._publish_elastic_update()
-        self._optimizer_step()
+        with nvtx.nvtx_range("grad_reduce"):
+            self._apply_elastic_inter_replica_gradients()
+            for g in self._tp_partial:  # per-head norm weights see only this rank's heads
+                dist.all_reduce(g, group=self.tp_group)
+            self._reduce_gradients()
+            self._publish_elastic_update()
+        with nvtx.nvtx_range("optimizer_step"):
+            self._optimizer_step()
         if not sync_stats:
             return {"loss_sum": acc}
         rewards = [mb["rewards"] for mb in device_micro_batches if "rewards" in mb]

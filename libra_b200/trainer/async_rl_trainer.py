@@ -44,6 +44,7 @@ from libra_b200.infra.execution.batch_dispatcher import BatchTaskDispatcher, Tas
 from libra_b200.infra.observability.history_collector import HistoryDataCollector
 from libra_b200.infra.observability.phase_tracer import PhaseTracer
 from libra_b200.infra.sync.staleness import StalenessManager
+from libra_b200.utils import nvtx
 
 
 def compute_group_advantages(trajectories: List[Dict[str, Any]]) -> Dict[str, float]:
@@ -108,9 +109,15 @@ class AsyncRLTrainer:
         self._tracer = PhaseTracer(Path(trace_dir) / f"phase_trace_rank{self.rank}.jsonl", rank=self.rank,
                                    world_size=self.world_size) if trace else None
         self._single_batch_source = False
+        self._nvtx_open: Dict[Any, Optional[int]] = {}
 
     # ================================================================== setup
     def _trace(self, step: int, name: str, **details) -> None:
+        if nvtx.enabled():
+            if name.endswith("_start"):
+                self._nvtx_open[(step, name[:-6])] = nvtx.range_start(f"{name[:-6]}[{step}]")
+            elif name.endswith("_done"):
+                nvtx.range_end(self._nvtx_open.pop((step, name[:-5]), None))
         if self._tracer is None:
             return
         if name.endswith("_start"):
@@ -427,10 +434,81 @@ class AsyncRLTrainer:
                     print(f"Step {step}/{c.total_steps}: {time.time() - t_start:.1f}s loss={stats.get('loss', 0):.4f} "
                           f"kl={stats.get('kl', 0):.4f} reward={stats['reward_mean']:.3f} "
                           f"n={len(batch)} rollout={rollout_time:.2f}s train={train_time:.2f}s", flush=True)
+            self._run_periodic_evaluation(workflow, dataset, step)
             if c.save_interval > 0 and (step + 1) % c.save_interval == 0:
                 self._save_checkpoint(step)
         self.shutdown()
         return self.stats
+
+    # ================================================================== evaluation
+    def _run_periodic_evaluation(self, workflow, dataset, step: int) -> None:
+        """Greedy evaluation on rank 0 every ``eval_interval`` steps (not step 0).
+
+        Behaviour of the reference's ``trainer/async_rl_trainer.py:1034-1131``:
+        rollout dispatch is paused; rank 0 runs ``workflow.evaluate`` with the
+        ``EVAL_*`` environment settings, appends the summary to
+        ``<log_dir>/eval/$EVAL_METRICS_FILE``, writes up to a few sample records
+        to ``$EVAL_SAMPLES_FILE`` and drops ``eval_step_<step>.done`` (or
+        ``.error`` with the message).  The other ranks poll for those files
+        instead of sitting in a collective, so an evaluation longer than the
+        process-group timeout does not kill the job.
+        """
+        interval = int(getattr(self.config, "eval_interval", 0) or 0)
+        if interval <= 0 or step <= 0 or step % interval or not hasattr(workflow, "evaluate"):
+            return
+        if self.rollout_engine is None:
+            return
+        env = os.environ.get
+        eval_dir = os.path.join(self.config.log_dir, "eval")
+        done, error = (os.path.join(eval_dir, f"eval_step_{step}.{ext}") for ext in ("done", "error"))
+        if self.dispatcher is not None:
+            self.dispatcher.pause()
+        try:
+            if self.is_main_process:
+                os.makedirs(eval_dir, exist_ok=True)
+                for path in (done, error):
+                    if os.path.exists(path):
+                        os.remove(path)
+                kw = dict(max_samples=int(env("EVAL_MAX_SAMPLES", "0")), concurrency=int(env("EVAL_CONCURRENCY", "16")),
+                          accuracy_threshold=float(env("EVAL_ACCURACY_THRESHOLD", "0.5")),
+                          max_new_tokens=int(env("EVAL_MAX_NEW_TOKENS", str(self.config.max_new_tokens))))
+                try:
+                    import asyncio
+
+                    stats = asyncio.run(workflow.evaluate(self.rollout_engine, dataset, **kw))
+                    stats["step"] = step
+                    records = stats.pop("eval_records", [])
+                    self.stats.update(stats)
+                    print(f"[eval] step={step} accuracy={stats['eval_accuracy']:.4f} "
+                          f"reward_mean={stats['eval_reward_mean']:.4f} failures={stats['eval_failures']} "
+                          f"samples={stats['eval_samples']}", flush=True)
+                    with open(os.path.join(eval_dir, env("EVAL_METRICS_FILE", "eval_metrics.jsonl")), "a",
+                              encoding="utf-8") as f:
+                        f.write(json.dumps(stats, ensure_ascii=False) + "\n")
+                    if records:
+                        with open(os.path.join(eval_dir, env("EVAL_SAMPLES_FILE", f"eval_samples_step_{step}.jsonl")),
+                                  "w", encoding="utf-8") as f:
+                            for r in records:
+                                f.write(json.dumps(r, ensure_ascii=False) + "\n")
+                    if self._tracker is not None:
+                        self._tracker.log({k: v for k, v in stats.items() if isinstance(v, (int, float))}, step)
+                    Path(done).write_text("ok\n", encoding="utf-8")
+                except Exception as exc:
+                    Path(error).write_text(f"{type(exc).__name__}: {exc}", encoding="utf-8")
+                    raise
+            else:
+                limit = float(env("EVAL_WAIT_TIMEOUT", "86400"))
+                poll = float(env("EVAL_WAIT_POLL_S", "2.0"))
+                t0 = time.monotonic()
+                while not os.path.exists(done) and not os.path.exists(error):
+                    if time.monotonic() - t0 > limit:
+                        raise TimeoutError(f"timed out waiting for the evaluation of step {step}")
+                    time.sleep(poll)
+                if os.path.exists(error):
+                    raise RuntimeError(Path(error).read_text(encoding="utf-8"))
+        finally:
+            if self.dispatcher is not None:
+                self.dispatcher.resume()
 
     # ================================================================== bookkeeping
     def _record_history(self, step: int, batch, stats) -> None:

@@ -172,7 +172,11 @@ class MultiTurnWorkflow:
                                    return_exceptions=True)
         return [r for r in res if not isinstance(r, BaseException)]
 
-    async def evaluate(self, engine, data: Dict[str, Any]) -> Dict[str, float]:
-        t = await self.run_episode(engine, data)
-        return {"reward": float(t["rewards"][0]), "num_turns": float(t["num_turns"]),
-                "output_len": float(t["output_len"])}
+    async def evaluate(self, engine, dataset, max_samples: Optional[int] = None, concurrency: int = 16,
+                       accuracy_threshold: float = 1.0, max_new_tokens: Optional[int] = None,
+                       strategy: str = "first", seed: int = 0, record_limit: int = 8) -> Dict[str, Any]:
+        """Greedy evaluation over ``dataset`` (see ``workflow.evaluation``)."""
+        from libra_b200.workflow.evaluation import evaluate_workflow
+
+        return await evaluate_workflow(self, engine, dataset, max_samples, concurrency, accuracy_threshold,
+                                       max_new_tokens, strategy, seed, record_limit)

@@ -71,9 +71,12 @@ class TargetTokenWorkflow:
         return make_trajectory(prompt, [(out, res.get("logprobs") or [0.0] * len(out))], reward, version,
                                {"prompt_id": data.get("prompt_id", "")})
 
-    async def evaluate(self, engine, data: Dict[str, Any]) -> Dict[str, float]:
-        t = await self.run_episode(engine, data)
-        return {"reward": float(t["rewards"][0])}
+    async def evaluate(self, engine, dataset, max_samples=None, concurrency: int = 16,
+                       accuracy_threshold: float = 1.0, max_new_tokens=None, **kw) -> Dict[str, Any]:
+        from libra_b200.workflow.evaluation import evaluate_workflow
+
+        return await evaluate_workflow(self, engine, dataset, max_samples, concurrency, accuracy_threshold,
+                                       max_new_tokens, **kw)
 
 
 def target_token_dataset(n_prompts: int, vocab: int = 1024, lo: int = 16, hi: int = 48, seed: int = 0,

@@ -18,13 +18,13 @@ def _free_port() -> int:
     return port
 
 
-def _run(tmp_path, task):
-    env = dict(os.environ, DIST_BACKEND="gloo", CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="2")
+def _run(tmp_path, task, *extra, **env_extra):
+    env = dict(os.environ, DIST_BACKEND="gloo", CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="2", **env_extra)
     out = tmp_path / "stats.json"
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
            "--master-port", str(_free_port()), os.path.join(ROOT, "examples", "synthetic_grpo.py"),
            "--config", os.path.join(ROOT, "libra_b200", "configs", "tiny_cpu_gloo.yaml"), "--total-steps", "3",
-           "--log-dir", str(tmp_path), "--stats-out", str(out), "--task", task]
+           "--log-dir", str(tmp_path), "--stats-out", str(out), "--task", task, *extra]
     proc = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert proc.returncode == 0, proc.stderr[-3000:]
     return json.loads(out.read_text())
@@ -44,3 +44,17 @@ def test_two_rank_async_grpo_plumbing(tmp_path):
 def test_two_rank_agentic_multiturn(tmp_path):
     stats = _run(tmp_path, "agentic")
     assert stats["n_trajectories"] == 16
+
+
+def test_periodic_evaluation_rank0_with_sentinel(tmp_path):
+    """Rank 0 evaluates at step 2; rank 1 waits on the done file, not a collective."""
+    stats = _run(tmp_path, "target_token", "--eval-interval", "2", EVAL_MAX_SAMPLES="6", EVAL_WAIT_POLL_S="0.1",
+                 EVAL_ACCURACY_THRESHOLD="1.0")
+    assert stats["version"] == 3
+    assert (tmp_path / "eval" / "eval_step_2.done").read_text().strip() == "ok"
+    assert not (tmp_path / "eval" / "eval_step_2.error").exists()
+    rows = [json.loads(l) for l in (tmp_path / "eval" / "eval_metrics.jsonl").read_text().splitlines()]
+    assert len(rows) == 1 and rows[0]["step"] == 2 and rows[0]["eval_samples"] == 6
+    assert 0.0 <= rows[0]["eval_accuracy"] <= 1.0 and rows[0]["eval_failures"] == 0
+    samples = (tmp_path / "eval" / "eval_samples_step_2.jsonl").read_text().splitlines()
+    assert 1 <= len(samples) <= 6

@@ -176,3 +176,40 @@ def test_r2e_length_profile():
     recs = build_r2e_gym_length_profile(rows, tokenizer=TOK, sample_size=4, max_new_tokens=64)
     assert len(recs) == 4
     assert all(r["output_len"] <= 64 and r["input_len"] > 0 for r in recs)
+
+
+def test_dataset_evaluation_greedy_and_failures():
+    import asyncio
+
+    import torch
+
+    from libra_b200.workflow.evaluation import eval_indices, evaluate_workflow
+
+    assert eval_indices(10, 4, "first") == [0, 1, 2, 3]
+    assert eval_indices(10, 4, "spread") == [0, 2, 5, 7]
+    assert eval_indices(10, 20, "random") == list(range(10))
+    r = eval_indices(10, 3, "random", seed=1)
+    assert len(r) == 3 and r == sorted(r) and r == eval_indices(10, 3, "random", seed=1)
+
+    class Wf:
+        temperature, top_p, max_new_tokens = 1.0, 0.9, 64
+        seen = []
+
+        async def run_episode(self, engine, row, version=0, rollout_index=0):
+            Wf.seen.append((self.temperature, self.top_p, self.max_new_tokens))
+            if row["x"] == 3:
+                raise ValueError("bad row")
+            return {"rewards": torch.tensor([row["x"] / 4.0]), "prompt_id": str(row["x"]), "output_len": 2,
+                    "completion": "c"}
+
+    wf = Wf()
+    ds = [{"x": i} for i in range(5)]
+    out = asyncio.run(evaluate_workflow(wf, None, ds, max_samples=0, concurrency=2, accuracy_threshold=0.5,
+                                        max_new_tokens=7, record_limit=2))
+    assert wf.temperature == 1.0  # the caller's workflow is untouched
+    assert set(Wf.seen) == {(0.0, 1.0, 7)}
+    assert out["eval_samples"] == 5 and out["eval_failures"] == 1 and "bad row" in out["eval_first_error"]
+    # rewards 0, .25, .5, fail(0), 1.0 -> accurate at >= .5: rows 2 and 4
+    assert abs(out["eval_accuracy"] - 0.4) < 1e-9
+    assert abs(out["eval_reward_mean"] - 1.75 / 5) < 1e-9 and out["eval_reward_max"] == 1.0
+    assert len(out["eval_records"]) == 2 and out["eval_records"][1]["accurate"] is False

@@ -152,6 +152,18 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
+// D(tmem) (+)= A(tmem) * B(smem desc)^T, kind::f16.  A is M x K with row i in
+// TMEM lane i and two consecutive 16-bit K elements per 32-bit column (lower
+// K index in the low half), so one K=16 step spans 8 columns.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
 // Arrive on an mbarrier once every tcgen05.mma issued so far by this thread is complete.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -186,6 +198,58 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
       : "memory");
 }
 
+// 16-lane TMEM shapes.  With base lane b (a multiple of 16 inside the warp's
+// lane quarter), thread t of the warp covers lanes b + t/4 and b + t/4 + 8.
+//   16x256b.xN: per repetition i (8 columns), registers 4i..4i+3 hold
+//     (lane b+t/4: columns 8i+2(t%4), +1), (lane b+t/4+8: the same two columns).
+//   16x128b.xN: per repetition i (4 columns), registers 2i, 2i+1 hold column
+//     4i+t%4 of lanes b+t/4 and b+t/4+8.
+#define LIBRA_R8(a, o) "=r"(a[o + 0]), "=r"(a[o + 1]), "=r"(a[o + 2]), "=r"(a[o + 3]), "=r"(a[o + 4]), \
+                       "=r"(a[o + 5]), "=r"(a[o + 6]), "=r"(a[o + 7])
+#define LIBRA_W8(a, o) "r"(a[o + 0]), "r"(a[o + 1]), "r"(a[o + 2]), "r"(a[o + 3]), "r"(a[o + 4]), "r"(a[o + 5]), \
+                       "r"(a[o + 6]), "r"(a[o + 7])
+
+__device__ __forceinline__ void tmem_ld_16x256b_x16(uint32_t taddr, uint32_t (&r)[64]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+      : LIBRA_R8(r, 0), LIBRA_R8(r, 8), LIBRA_R8(r, 16), LIBRA_R8(r, 24), LIBRA_R8(r, 32), LIBRA_R8(r, 40),
+        LIBRA_R8(r, 48), LIBRA_R8(r, 56)
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_16x256b_x8(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x8.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : LIBRA_R8(r, 0), LIBRA_R8(r, 8), LIBRA_R8(r, 16), LIBRA_R8(r, 24)
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st_16x256b_x8(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x256b.x8.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      LIBRA_W8(r, 0), LIBRA_W8(r, 8), LIBRA_W8(r, 16), LIBRA_W8(r, 24)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_16x128b_x16(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x128b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      LIBRA_W8(r, 0), LIBRA_W8(r, 8), LIBRA_W8(r, 16), LIBRA_W8(r, 24)
+      : "memory");
+}
+#undef LIBRA_R8
+#undef LIBRA_W8
+
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Order this thread's generic-proxy shared-memory writes before later async-proxy
@@ -199,6 +263,25 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x on the FMA/ALU pipes, for x <= ~64 (softmax arguments), used to take
+// part of the exponentials off the MUFU unit.  Method: Cody-Waite style
+// range reduction x = n + f with n = rint(x) obtained by the 1.5 * 2^23 shifter
+// (f in [-0.5, 0.5]); 2^f by a degree-3 polynomial whose coefficients were
+// fitted here by iteratively reweighted least squares on the relative error
+// over [-0.5, 0.5] (max relative error 1.5e-4, below bf16 rounding); n is
+// added to the exponent field.  Inputs below -126 are clamped, giving 0.
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -126.0f);
+  const float shifter = 12582912.0f;  // 1.5 * 2^23
+  const float t = __fadd_rn(x, shifter);
+  const float n = __fsub_rn(t, shifter);
+  const float f = __fsub_rn(x, n);
+  float p = fmaf(0.055453039705753326f, f, 0.24236291646957397f);
+  p = fmaf(p, f, 0.6931914687156677f);
+  p = fmaf(p, f, 0.999942421913147f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 __device__ __forceinline__ float lg2_approx(float x) {

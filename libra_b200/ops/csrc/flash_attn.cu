@@ -11,19 +11,28 @@
 // host-built tile table (heaviest causal tiles first, the Hq heads of a tile
 // adjacent so the shared K/V of a kv head stay in L2).
 //
-// One CTA (192 threads) per SM:
+// One CTA (320 threads) per SM:
 //   warp 0      TMA producer: Q tile (32 KB), then K_j and V_j (32 KB each) into
 //               a 2-stage ring.  K and V use the same [kv rows][64 dims] box;
 //               K is read as a K-major B operand, V as an MN-major B operand.
 //   warp 1      tcgen05.mma issuer: S_j = Q K_j^T into one of two TMEM S
-//               buffers (issued one block ahead), O += P_j V_j into TMEM O.
-//   warps 2-5   softmax: thread = q row = TMEM lane.  tcgen05.ld the S row,
-//               mask, online max/sum in base 2, P_j as bf16 into a 128B-swizzled
-//               smem tile (the A operand of the PV MMA).  The running max only
+//               buffers (issued one block ahead), O += P_j V_j with P_j read
+//               from TMEM (A operand in tensor memory).
+//   warps 2-9   softmax: warps w and w+4 share a TMEM lane quarter, 16 rows
+//               each; with the 16x256b load shape four threads hold one row
+//               (32 of its 128 scores each), so row max / sum reduce with two
+//               shuffles and no cross-warp synchronisation.  The mask is applied
+//               only on blocks that cross the causal diagonal or the sequence
+//               end; the scale folds into one FFMA per score; a quarter of the
+//               exponentials run as a polynomial on the FMA pipe (ex2_poly),
+//               the rest on MUFU.  P_j goes back to TMEM as packed bf16 (16x128b
+//               shape), double-buffered so the next block's P never waits for
+//               the PV MMA still reading the previous one.  The running max only
 //               moves when it grows by more than 2^8, so O (in TMEM) is rescaled
 //               rarely; the final O / l uses the same max and stays exact.
-//               Epilogue: tcgen05.ld O, divide by l, store bf16 rows and lse.
-// TMEM: S0 [0,128) S1 [128,256) O [256,384) (512 allocated).
+//               Epilogue: tcgen05.ld O, divide by l, stage bf16 rows in a
+//               per-warp swizzled smem area and write them out coalesced, plus lse.
+// TMEM: S0 [0,128) S1 [128,256) O [256,384) P0 [384,448) P1 [448,512).
 // Every wait is bounded; on a timeout the kernel records an error code, drains
 // its in-flight copies and MMAs, frees TMEM and returns.
 #include <torch/extension.h>
@@ -39,17 +48,19 @@ constexpr int kStages = 2;
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kTile;
 constexpr int kOffV = kOffK + kStages * kTile;
-constexpr int kOffP = kOffV + kStages * kTile;
-constexpr int kOffX = kOffP + kTile;  // row max / sum exchange between the two warps of a row: [2][2][128] fp32
-constexpr int kOffBar = kOffX + 2 * 2 * 128 * 4;
-// q_full q_empty | k_full[2] v_full[2] kv_empty[2] | s_full[2] s_empty[2] | p_full pv_done o_empty done grp
-constexpr int kNumBars = 2 + 3 * kStages + 4 + 5;
-// softmax: two warps per row (warps w and w+4 share a TMEM lane quarter), 64 columns each
+constexpr int kOffStage = kOffV + kStages * kTile;  // epilogue staging: 8 warps x 16 rows x 256 B
+constexpr int kOffBar = kOffStage + kTile;
+// q_full q_empty | k_full[2] v_full[2] kv_empty[2] | s_full[2] s_empty[2] | p_full[2] p_empty[2] | o_empty done
+constexpr int kNumBars = 2 + 3 * kStages + 4 + 4 + 2;
 constexpr int kFwdSoftmaxWarps = 8;
 constexpr int kFwdThreads = 64 + 32 * kFwdSoftmaxWarps;
 constexpr int kSmemBytes = 1024 + kOffBar + 8 * kNumBars + 16;
 constexpr uint32_t kColO = 256;
+constexpr uint32_t kColP = 384;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+// Of each group of 16 scores a thread holds per row, this many (the last ones)
+// take the polynomial exponential instead of MUFU.
+constexpr int kPolyPer16 = 4;
 
 // One work item.  Queries may be the suffix of their sequence (prefix-cached
 // extend): q rows [s0, s0 + L) of the packed q tensor are positions
@@ -77,11 +88,22 @@ __device__ __forceinline__ Item decode(int item, const int* __restrict__ cu, con
   return it;
 }
 
+__device__ __forceinline__ float quad_max(float v) {
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+}
+
+__device__ __forceinline__ float quad_sum(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  return v + __shfl_xor_sync(0xffffffffu, v, 2);
+}
+
 __global__ void __launch_bounds__(kFwdThreads, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const int* __restrict__ cu,
-                     const int* __restrict__ cu_k, const int2* __restrict__ tiles, int n_tiles, int Hq, int Hkv, __nv_bfloat16* __restrict__ O,
-                     float* __restrict__ lse, int T, float scale_log2, int causal, int* err) {
+                     const int* __restrict__ cu_k, const int2* __restrict__ tiles, int n_tiles, int Hq, int Hkv,
+                     __nv_bfloat16* __restrict__ O, float* __restrict__ lse, int T, float scale_log2, int causal,
+                     int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
@@ -93,12 +115,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* s_full = kv_empty + kStages;
   uint64_t* s_empty = s_full + 2;
   uint64_t* p_full = s_empty + 2;
-  uint64_t* pv_done = p_full + 1;
-  uint64_t* o_empty = pv_done + 1;
+  uint64_t* p_empty = p_full + 2;
+  uint64_t* o_empty = p_empty + 2;
   uint64_t* done = o_empty + 1;
-  uint64_t* grp = done + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(grp + 1);
-  float* xchg = reinterpret_cast<float*>(smem + kOffX);  // [parity][half][row]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -119,12 +139,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&s_empty[b], kFwdSoftmaxWarps);
+      mbar_init(&p_full[b], kFwdSoftmaxWarps);
+      mbar_init(&p_empty[b], 1);
     }
-    mbar_init(p_full, kFwdSoftmaxWarps);
-    mbar_init(pv_done, 1);
     mbar_init(o_empty, kFwdSoftmaxWarps);
     mbar_init(done, 1);
-    mbar_init(grp, 32 * kFwdSoftmaxWarps);
     fence_barrier_init();
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
@@ -135,7 +154,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint8_t* smQ = smem + kOffQ;
   uint8_t* smK = smem + kOffK;
   uint8_t* smV = smem + kOffV;
-  uint8_t* smP = smem + kOffP;
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
@@ -143,8 +161,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       uint32_t kv_it = 0, item_it = 0;
       bool q_issued = false, ok = true;
       uint32_t q_par = 0;
-      uint32_t last_k_par[kStages] = {0, 0}, last_v_par[kStages] = {0, 0};
-      bool k_issued[kStages] = {false, false};
+      uint32_t issued_mask = 0, par_mask = 0;  // per stage: ever issued / parity of its last fill
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++item_it) {
         const Item it = decode(item, cu, cu_k, tiles, Hq, group, causal);
         if (!mbar_wait(q_empty, (item_it & 1u) ^ 1u, err, kTimeoutAttnQ)) { ok = false; break; }
@@ -164,17 +181,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           mbar_expect_tx(&v_full[st], kTile);
           tma_load_2d(smV + st * kTile, &tmV, &v_full[st], it.hk * D, y);
           tma_load_2d(smV + st * kTile + kChunk, &tmV, &v_full[st], it.hk * D + 64, y);
-          k_issued[st] = true;
-          last_k_par[st] = ph;
-          last_v_par[st] = ph;
+          issued_mask |= 1u << st;
+          par_mask = (par_mask & ~(1u << st)) | (ph << st);
         }
       }
       // drain: every copy this thread issued must land before the CTA exits
       if (q_issued) mbar_wait(q_full, q_par, nullptr, 0);
       for (int s = 0; s < kStages; ++s)
-        if (k_issued[s]) {
-          mbar_wait(&k_full[s], last_k_par[s], nullptr, 0);
-          mbar_wait(&v_full[s], last_v_par[s], nullptr, 0);
+        if ((issued_mask >> s) & 1u) {
+          mbar_wait(&k_full[s], (par_mask >> s) & 1u, nullptr, 0);
+          mbar_wait(&v_full[s], (par_mask >> s) & 1u, nullptr, 0);
         }
     }
   } else if (warp == 1) {
@@ -182,7 +198,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16(BQ, BKV, 0, 0);
       constexpr uint32_t idesc_o = make_idesc_bf16(BQ, D, 0, 1);
-      const uint32_t aQ = smem_u32(smQ), aP = smem_u32(smP);
+      const uint32_t aQ = smem_u32(smQ);
       uint32_t kv_it = 0, s_it = 0, pv_it = 0, item_it = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++item_it) {
@@ -213,17 +229,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           }
           const uint32_t idx = kv_it + j;
           const int st = idx % kStages;
-          if (!mbar_wait(p_full, pv_it & 1u, err, kTimeoutAttnP)) { ok = false; break; }
+          const int pb = pv_it & 1;
+          if (!mbar_wait(&p_full[pb], (pv_it >> 1) & 1u, err, kTimeoutAttnP)) { ok = false; break; }
           if (!mbar_wait(&v_full[st], (idx / kStages) & 1u, err, kTimeoutAttnKV)) { ok = false; break; }
           if (j == 0 && !mbar_wait(o_empty, (item_it & 1u) ^ 1u, err, kTimeoutAttnO)) { ok = false; break; }
           tc_fence_after();
           const uint32_t aV = smem_u32(smV + st * kTile);
 #pragma unroll
           for (int kk = 0; kk < BKV / 16; ++kk)
-            umma_f16(tmem_base + kColO, kmajor_desc(aP, kk), mnmajor_desc(aV, kk), idesc_o,
-                     (j > 0 || kk > 0) ? 1u : 0u);
+            umma_f16_ts(tmem_base + kColO, tmem_base + kColP + pb * 64 + kk * 8, mnmajor_desc(aV, kk), idesc_o,
+                        (j > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&kv_empty[st]);
-          umma_commit(pv_done);
+          umma_commit(&p_empty[pb]);
           ++pv_it;
         }
         kv_it += it.nkv;
@@ -234,135 +251,161 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
     const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const int half = (warp - 2) >> 2;  // which 64 of the 128 key columns (and of the 128 O columns)
-    const int c0 = half * 64;
-    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    uint32_t s_it = 0, pv_it = 0, item_it = 0, nsync = 0;
-    // exchange a per-row value with the partner warp (other half of the same row)
-    auto exchange = [&](float mine, float& theirs) -> bool {
-      const int par = nsync & 1;
-      xchg[(par * 2 + half) * 128 + row] = mine;
-      mbar_arrive(grp);
-      const bool okw = mbar_wait(grp, nsync & 1u, err, kTimeoutAttnS);
-      ++nsync;
-      theirs = xchg[(par * 2 + (half ^ 1)) * 128 + row];
-      return okw;
+    const int sub = (warp - 2) >> 2;      // which 16 rows of the lane quarter
+    const int rl = lane >> 2, cq = lane & 3;
+    const int row0 = quarter * 32 + sub * 16 + rl;  // tile rows of this thread: row0, row0 + 8
+    const uint32_t lane_addr = (uint32_t)(quarter * 32 + sub * 16) << 16;
+    uint8_t* stage = smem + kOffStage + (warp - 2) * 4096;
+    // Waits are made warp-uniform: the tcgen05 loads and stores that follow are
+    // .sync.aligned, so either the whole warp goes on or the whole warp stops.
+    auto wait_all = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, code));
     };
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++item_it) {
+    // wait until PV number g (global block count) has finished reading its P buffer
+    auto pv_wait = [&](uint32_t g) -> bool { return wait_all(&p_empty[g & 1u], (g >> 1) & 1u, kTimeoutAttnPV); };
+    uint32_t g = 0;  // blocks processed by this CTA (S and P buffer sequence)
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       const Item it = decode(item, cu, cu_k, tiles, Hq, group, causal);
-      const int qp = it.q0 + row;
-      float m = -INFINITY, l = 0.f;
-      bool ok = true;
-      for (int j = 0; j < it.nkv; ++j) {
-        const int sb = s_it & 1;
-        if (!mbar_wait(&s_full[sb], (s_it >> 1) & 1u, err, kTimeoutAttnS)) { ok = false; break; }
+      const int qp0 = it.q0 + row0, qp1 = qp0 + 8;
+      const int lim0 = causal ? min(it.off + qp0 + 1, it.Lk) : it.Lk;  // keys below lim are visible
+      const int lim1 = causal ? min(it.off + qp1 + 1, it.Lk) : it.Lk;
+      const int lim_tile = causal ? min(it.off + it.q0 + 1, it.Lk) : it.Lk;  // smallest limit in the tile
+      float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+      for (int j = 0; j < it.nkv; ++j, ++g) {
+        const int sb = g & 1;
+        if (!wait_all(&s_full[sb], (g >> 1) & 1u, kTimeoutAttnS)) { ok = false; break; }
         tc_fence_after();
         uint32_t r[64];
-#pragma unroll
-        for (int c = 0; c < 2; ++c)
-          tmem_ld_32x32b_x32(tmem_base + lane_addr + sb * BKV + c0 + c * 32,
-                             *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
+        tmem_ld_16x256b_x16(tmem_base + lane_addr + sb * BKV, r);
         tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_empty[sb]);
-        ++s_it;
-        // scale into log2 units and mask
-        const int kb = j * BKV + c0;
-        const int lim = causal ? min(it.off + qp + 1, it.Lk) : it.Lk;  // keys below lim are visible
-        float bm = -INFINITY;
+        const int kb = j * BKV + 2 * cq;
+        if ((j + 1) * BKV > lim_tile) {  // block crosses the diagonal or the sequence end
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          float v = __uint_as_float(r[c]) * scale_log2;
-          v = (kb + c < lim) ? v : -INFINITY;
-          r[c] = __float_as_uint(v);
-          bm = fmaxf(bm, v);
+          for (int i = 0; i < 16; ++i) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int key = kb + 8 * i + e;
+              if (key >= lim0) r[4 * i + e] = __float_as_uint(-INFINITY);
+              if (key >= lim1) r[4 * i + 2 + e] = __float_as_uint(-INFINITY);
+            }
+          }
         }
-        float bm_other;
-        if (!exchange(bm, bm_other)) { ok = false; break; }
-        bm = fmaxf(bm, bm_other);  // both halves now hold the same block max
-        const float m_new = fmaxf(m, bm);
-        const bool rescale = (j > 0) && (m_new > m + kRescaleThreshold);
-        if (j == 0) m = m_new;
-        if (j > 0) {  // PV_{j-1} finished: O is stable and the P buffer is free
-          if (!mbar_wait(pv_done, (pv_it - 1) & 1u, err, kTimeoutAttnPV)) { ok = false; break; }
-          tc_fence_after();
+        // raw block max per row (scale > 0, so the scaled max is scale * raw max)
+        float a0 = -INFINITY, a1 = -INFINITY, b0 = -INFINITY, b1 = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          a0 = fmaxf(a0, __uint_as_float(r[4 * i + 0]));
+          b0 = fmaxf(b0, __uint_as_float(r[4 * i + 1]));
+          a1 = fmaxf(a1, __uint_as_float(r[4 * i + 2]));
+          b1 = fmaxf(b1, __uint_as_float(r[4 * i + 3]));
         }
-        if (__any_sync(0xffffffffu, rescale)) {
-          const float f = rescale ? ex2_approx(m - m_new) : 1.f;
+        const float bm0 = quad_max(fmaxf(a0, b0)) * scale_log2;
+        const float bm1 = quad_max(fmaxf(a1, b1)) * scale_log2;
+        const float mn0 = fmaxf(m0, bm0), mn1 = fmaxf(m1, bm1);
+        if (j == 0) {
+          m0 = mn0;
+          m1 = mn1;
+        } else {
+          const bool rs0 = mn0 > m0 + kRescaleThreshold, rs1 = mn1 > m1 + kRescaleThreshold;
+          if (__any_sync(0xffffffffu, rs0 || rs1)) {
+            if (!pv_wait(g - 1)) { ok = false; break; }  // O holds every earlier block
+            tc_fence_after();
+            const float f0 = rs0 ? ex2_approx(m0 - mn0) : 1.f;
+            const float f1 = rs1 ? ex2_approx(m1 - mn1) : 1.f;
 #pragma unroll 1
-          for (int c = 0; c < 2; ++c) {
-            uint32_t o[32];
-            tmem_ld_32x32b_x32(tmem_base + lane_addr + kColO + c0 + c * 32, o);
-            tmem_ld_wait();
+            for (int c = 0; c < 2; ++c) {
+              uint32_t o[32];
+              tmem_ld_16x256b_x8(tmem_base + lane_addr + kColO + c * 64, o);
+              tmem_ld_wait();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
-            tmem_st_32x32b_x32(tmem_base + lane_addr + kColO + c0 + c * 32, o);
-          }
-          tmem_st_wait();
-          if (rescale) {
-            l *= f;
-            m = m_new;
+              for (int i = 0; i < 8; ++i) {
+                o[4 * i + 0] = __float_as_uint(__uint_as_float(o[4 * i + 0]) * f0);
+                o[4 * i + 1] = __float_as_uint(__uint_as_float(o[4 * i + 1]) * f0);
+                o[4 * i + 2] = __float_as_uint(__uint_as_float(o[4 * i + 2]) * f1);
+                o[4 * i + 3] = __float_as_uint(__uint_as_float(o[4 * i + 3]) * f1);
+              }
+              tmem_st_16x256b_x8(tmem_base + lane_addr + kColO + c * 64, o);
+            }
+            tmem_st_wait();
+            if (rs0) {
+              l0 *= f0;
+              m0 = mn0;
+            }
+            if (rs1) {
+              l1 *= f1;
+              m1 = mn1;
+            }
           }
         }
-        // P = 2^(s - m) as bf16: this half's 64 columns of row `row` in the 128B-swizzled K-major tile
-        float sum = 0.f;
+        // P = 2^(s * scale - m) packed to bf16 pairs, in place: r[2i] row0, r[2i+1] row1
+        // (P column 4i + cq).  Group i is read before words 2i, 2i+1 are written.
+        const float nm0 = -m0, nm1 = -m1;
+        float s0a = 0.f, s0b = 0.f, s1a = 0.f, s1b = 0.f;
 #pragma unroll
-        for (int j8 = 0; j8 < 8; ++j8) {
-          float p[8];
+        for (int i = 0; i < 16; ++i) {
+          float p[4];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            p[e] = ex2_approx(__uint_as_float(r[j8 * 8 + e]) - m);
-            sum += p[e];
+          for (int e = 0; e < 4; ++e) {
+            const float x = fmaf(__uint_as_float(r[4 * i + e]), scale_log2, (e < 2) ? nm0 : nm1);
+            p[e] = ((i & 3) * 4 + e >= 16 - kPolyPer16) ? ex2_poly(x) : ex2_approx(x);
           }
-          uint4 pk;
-          pk.x = pack_bf16x2(p[0], p[1]);
-          pk.y = pack_bf16x2(p[2], p[3]);
-          pk.z = pack_bf16x2(p[4], p[5]);
-          pk.w = pack_bf16x2(p[6], p[7]);
-          const int vi = half * 8 + j8;
-          const int unit = (vi & 7) ^ (row & 7);
-          *reinterpret_cast<uint4*>(smP + (vi >> 3) * kChunk + row * 128 + unit * 16) = pk;
+          s0a += p[0];
+          s0b += p[1];
+          s1a += p[2];
+          s1b += p[3];
+          r[2 * i] = pack_bf16x2(p[0], p[1]);
+          r[2 * i + 1] = pack_bf16x2(p[2], p[3]);
         }
-        l += sum;
-        fence_proxy_async_smem();
+        l0 += s0a + s0b;
+        l1 += s1a + s1b;
+        if (g >= 2 && !pv_wait(g - 2)) { ok = false; break; }  // P buffer sb is free again
+        tc_fence_after();
+        tmem_st_16x128b_x16(tmem_base + lane_addr + kColP + sb * 64, *reinterpret_cast<const uint32_t(*)[32]>(r));
+        tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(p_full);
-        ++pv_it;
+        if (lane == 0) mbar_arrive(&p_full[sb]);
       }
       if (!ok) break;
-      // epilogue: row sum of both halves, then this half's 64 O columns
-      float l_other;
-      if (!exchange(l, l_other)) break;
-      l += l_other;
-      if (!mbar_wait(pv_done, (pv_it - 1) & 1u, err, kTimeoutAttnPV)) break;
+      // epilogue: full row sums, then O / l through the staging area
+      l0 = quad_sum(l0);
+      l1 = quad_sum(l1);
+      if (!pv_wait(g - 1)) { ok = false; break; }
       tc_fence_after();
-      const bool row_ok = qp < it.L;
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* orow = O + ((size_t)(it.s0 + qp) * Hq + it.h) * D + c0;
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t o[32];
-        tmem_ld_32x32b_x32(tmem_base + lane_addr + kColO + c0 + c * 32, o);
-        tmem_ld_wait();
-        if (row_ok) {
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            uint4 pk;
-            pk.x = pack_bf16x2(__uint_as_float(o[q4 * 8 + 0]) * inv, __uint_as_float(o[q4 * 8 + 1]) * inv);
-            pk.y = pack_bf16x2(__uint_as_float(o[q4 * 8 + 2]) * inv, __uint_as_float(o[q4 * 8 + 3]) * inv);
-            pk.z = pack_bf16x2(__uint_as_float(o[q4 * 8 + 4]) * inv, __uint_as_float(o[q4 * 8 + 5]) * inv);
-            pk.w = pack_bf16x2(__uint_as_float(o[q4 * 8 + 6]) * inv, __uint_as_float(o[q4 * 8 + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + c * 32 + q4 * 8) = pk;
-          }
-        }
-      }
+      uint32_t o[64];
+      tmem_ld_16x256b_x16(tmem_base + lane_addr + kColO, o);
+      tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(o_empty);
-      if (row_ok && half == 0) lse[(size_t)it.h * T + it.s0 + qp] = (m + lg2_approx(l)) * 0.6931471805599453f;
+      const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
+      const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+      // row rl / rl + 8 of this warp's 16, 16-byte chunk i holds columns 8i..8i+7; word cq of the chunk
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t w0 = pack_bf16x2(__uint_as_float(o[4 * i + 0]) * inv0, __uint_as_float(o[4 * i + 1]) * inv0);
+        const uint32_t w1 = pack_bf16x2(__uint_as_float(o[4 * i + 2]) * inv1, __uint_as_float(o[4 * i + 3]) * inv1);
+        *reinterpret_cast<uint32_t*>(stage + rl * 256 + ((i ^ rl) << 4) + cq * 4) = w0;
+        *reinterpret_cast<uint32_t*>(stage + (rl + 8) * 256 + ((i ^ rl) << 4) + cq * 4) = w1;
+      }
+      __syncwarp();
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int q = k * 32 + lane;
+        const int rr = q >> 4, ch = q & 15;
+        const uint4 v = *reinterpret_cast<const uint4*>(stage + rr * 256 + ((ch ^ (rr & 7)) << 4));
+        const int qp = it.q0 + quarter * 32 + sub * 16 + rr;
+        if (qp < it.L) *reinterpret_cast<uint4*>(O + ((size_t)(it.s0 + qp) * Hq + it.h) * D + ch * 8) = v;
+      }
+      __syncwarp();
+      if (cq == 0) {
+        if (qp0 < it.L) lse[(size_t)it.h * T + it.s0 + qp0] = (m0 + lg2_approx(l0)) * 0.6931471805599453f;
+        if (qp1 < it.L) lse[(size_t)it.h * T + it.s0 + qp1] = (m1 + lg2_approx(l1)) * 0.6931471805599453f;
+      }
     }
   }
 

@@ -124,6 +124,23 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// Untiled bulk copy global -> shared, completing on an mbarrier (both addresses
+// 16-byte aligned, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Bring a 2-D tile into L2 ahead of its load (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -263,25 +280,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// 2^x on the FMA/ALU pipes, for x <= ~64 (softmax arguments), used to take
-// part of the exponentials off the MUFU unit.  Method: Cody-Waite style
-// range reduction x = n + f with n = rint(x) obtained by the 1.5 * 2^23 shifter
-// (f in [-0.5, 0.5]); 2^f by a degree-3 polynomial whose coefficients were
-// fitted here by iteratively reweighted least squares on the relative error
-// over [-0.5, 0.5] (max relative error 1.5e-4, below bf16 rounding); n is
-// added to the exponent field.  Inputs below -126 are clamped, giving 0.
-__device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -126.0f);
-  const float shifter = 12582912.0f;  // 1.5 * 2^23
-  const float t = __fadd_rn(x, shifter);
-  const float n = __fsub_rn(t, shifter);
-  const float f = __fsub_rn(x, n);
-  float p = fmaf(0.055453039705753326f, f, 0.24236291646957397f);
-  p = fmaf(p, f, 0.6931914687156677f);
-  p = fmaf(p, f, 0.999942421913147f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 __device__ __forceinline__ float lg2_approx(float x) {

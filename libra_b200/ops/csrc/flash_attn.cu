@@ -12,9 +12,12 @@
 // adjacent so the shared K/V of a kv head stay in L2).
 //
 // One CTA (320 threads) per SM:
-//   warp 0      TMA producer: Q tile (32 KB), then K_j and V_j (32 KB each) into
-//               a 2-stage ring.  K and V use the same [kv rows][64 dims] box;
-//               K is read as a K-major B operand, V as an MN-major B operand.
+//   warp 0      TMA producer: Q tile (32 KB), then K_j into a 3-stage ring (a
+//               slot frees when S_j is computed) and V_j into a 2-stage ring
+//               (frees after PV_j), K one block ahead of V; K/V blocks are
+//               prefetched into L2 three blocks ahead of their loads.  K and V
+//               use the same [kv rows][64 dims] box; K is read as a K-major B
+//               operand, V as an MN-major B operand.
 //   warp 1      tcgen05.mma issuer: S_j = Q K_j^T into one of two TMEM S
 //               buffers (issued one block ahead), O += P_j V_j with P_j read
 //               from TMEM (A operand in tensor memory).
@@ -23,11 +26,9 @@
 //               (32 of its 128 scores each), so row max / sum reduce with two
 //               shuffles and no cross-warp synchronisation.  The mask is applied
 //               only on blocks that cross the causal diagonal or the sequence
-//               end; the scale folds into one FFMA per score; a quarter of the
-//               exponentials run as a polynomial on the FMA pipe (ex2_poly),
-//               the rest on MUFU.  P_j goes back to TMEM as packed bf16 (16x128b
-//               shape), double-buffered so the next block's P never waits for
-//               the PV MMA still reading the previous one.  The running max only
+//               end; the scale folds into one FFMA per score.  P_j goes back to
+//               TMEM as packed bf16 (16x128b shape), double-buffered so the next
+//               block's P never waits for the PV MMA still reading the previous one.  The running max only
 //               moves when it grows by more than 2^8, so O (in TMEM) is rescaled
 //               rarely; the final O / l uses the same max and stays exact.
 //               Epilogue: tcgen05.ld O, divide by l, stage bf16 rows in a
@@ -44,23 +45,23 @@
 namespace libra {
 namespace attn {
 
-constexpr int kStages = 2;
+constexpr int kKStages = 3;  // K_j frees as soon as S_j is computed, so it can run further ahead
+constexpr int kVStages = 2;  // V_j frees after PV_j
+constexpr int kPrefetch = 3;  // K/V blocks brought into L2 this many blocks ahead of their load
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kTile;
-constexpr int kOffV = kOffK + kStages * kTile;
-constexpr int kOffStage = kOffV + kStages * kTile;  // epilogue staging: 8 warps x 16 rows x 256 B
+constexpr int kOffV = kOffK + kKStages * kTile;
+constexpr int kOffStage = kOffV + kVStages * kTile;  // epilogue staging: 8 warps x 16 rows x 256 B
 constexpr int kOffBar = kOffStage + kTile;
-// q_full q_empty | k_full[2] v_full[2] kv_empty[2] | s_full[2] s_empty[2] | p_full[2] p_empty[2] | o_empty done
-constexpr int kNumBars = 2 + 3 * kStages + 4 + 4 + 2;
+// q_full q_empty | k_full[3] k_empty[3] | v_full[2] v_empty[2] | s_full[2] s_empty[2] | p_full[2] p_empty[2]
+// | o_empty done
+constexpr int kNumBars = 2 + 2 * kKStages + 2 * kVStages + 4 + 4 + 2;
 constexpr int kFwdSoftmaxWarps = 8;
 constexpr int kFwdThreads = 64 + 32 * kFwdSoftmaxWarps;
 constexpr int kSmemBytes = 1024 + kOffBar + 8 * kNumBars + 16;
 constexpr uint32_t kColO = 256;
 constexpr uint32_t kColP = 384;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
-// Of each group of 16 scores a thread holds per row, this many (the last ones)
-// take the polynomial exponential instead of MUFU.
-constexpr int kPolyPer16 = 4;
 
 // One work item.  Queries may be the suffix of their sequence (prefix-cached
 // extend): q rows [s0, s0 + L) of the packed q tensor are positions
@@ -110,9 +111,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* q_full = bars + 0;
   uint64_t* q_empty = bars + 1;
   uint64_t* k_full = bars + 2;
-  uint64_t* v_full = k_full + kStages;
-  uint64_t* kv_empty = v_full + kStages;
-  uint64_t* s_full = kv_empty + kStages;
+  uint64_t* k_empty = k_full + kKStages;
+  uint64_t* v_full = k_empty + kKStages;
+  uint64_t* v_empty = v_full + kVStages;
+  uint64_t* s_full = v_empty + kVStages;
   uint64_t* s_empty = s_full + 2;
   uint64_t* p_full = s_empty + 2;
   uint64_t* p_empty = p_full + 2;
@@ -131,10 +133,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     prefetch_tmap(&tmV);
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kKStages; ++s) {
       mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
@@ -158,10 +163,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
     if (lane == 0) {
-      uint32_t kv_it = 0, item_it = 0;
+      uint32_t k_it = 0, v_it = 0, item_it = 0;
       bool q_issued = false, ok = true;
       uint32_t q_par = 0;
-      uint32_t issued_mask = 0, par_mask = 0;  // per stage: ever issued / parity of its last fill
+      uint32_t k_mask = 0, k_par = 0, v_mask = 0, v_par = 0;  // per stage: ever filled / parity of last fill
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++item_it) {
         const Item it = decode(item, cu, cu_k, tiles, Hq, group, causal);
         if (!mbar_wait(q_empty, (item_it & 1u) ^ 1u, err, kTimeoutAttnQ)) { ok = false; break; }
@@ -170,28 +175,50 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tma_load_2d(smQ + kChunk, &tmQ, q_full, it.h * D + 64, it.s0 + it.q0);
         q_issued = true;
         q_par = item_it & 1u;
-        for (int j = 0; j < it.nkv; ++j, ++kv_it) {
-          const int st = kv_it % kStages;
-          const uint32_t ph = (kv_it / kStages) & 1u;
-          if (!mbar_wait(&kv_empty[st], ph ^ 1u, err, kTimeoutAttnKV)) { ok = false; break; }
+        auto prefetch = [&](int j) {
           const int y = it.k0 + j * BKV;
-          mbar_expect_tx(&k_full[st], kTile);
-          tma_load_2d(smK + st * kTile, &tmK, &k_full[st], it.hk * D, y);
-          tma_load_2d(smK + st * kTile + kChunk, &tmK, &k_full[st], it.hk * D + 64, y);
-          mbar_expect_tx(&v_full[st], kTile);
-          tma_load_2d(smV + st * kTile, &tmV, &v_full[st], it.hk * D, y);
-          tma_load_2d(smV + st * kTile + kChunk, &tmV, &v_full[st], it.hk * D + 64, y);
-          issued_mask |= 1u << st;
-          par_mask = (par_mask & ~(1u << st)) | (ph << st);
+          tma_prefetch_l2_2d(&tmK, it.hk * D, y);
+          tma_prefetch_l2_2d(&tmK, it.hk * D + 64, y);
+          tma_prefetch_l2_2d(&tmV, it.hk * D, y);
+          tma_prefetch_l2_2d(&tmV, it.hk * D + 64, y);
+        };
+        auto load = [&](const CUtensorMap* map, uint8_t* ring, uint64_t* full, uint64_t* empty, int stages,
+                        uint32_t& cnt, uint32_t& mask, uint32_t& par, int j) -> bool {
+          const int st = cnt % stages;
+          const uint32_t ph = (cnt / stages) & 1u;
+          if (!mbar_wait(&empty[st], ph ^ 1u, err, kTimeoutAttnKV)) return false;
+          const int y = it.k0 + j * BKV;
+          mbar_expect_tx(&full[st], kTile);
+          tma_load_2d(ring + st * kTile, map, &full[st], it.hk * D, y);
+          tma_load_2d(ring + st * kTile + kChunk, map, &full[st], it.hk * D + 64, y);
+          mask |= 1u << st;
+          par = (par & ~(1u << st)) | (ph << st);
+          ++cnt;
+          return true;
+        };
+        for (int j = 0; j < it.nkv && j < kPrefetch; ++j) prefetch(j);
+        if (item + (int)gridDim.x < n_items) {  // the next item's Q, so its load hits L2
+          const Item nx = decode(item + gridDim.x, cu, cu_k, tiles, Hq, group, causal);
+          tma_prefetch_l2_2d(&tmQ, nx.h * D, nx.s0 + nx.q0);
+          tma_prefetch_l2_2d(&tmQ, nx.h * D + 64, nx.s0 + nx.q0);
+        }
+        // K runs one block ahead of V (the MMA order is S_{j+1} then PV_j)
+        if (!load(&tmK, smK, k_full, k_empty, kKStages, k_it, k_mask, k_par, 0)) { ok = false; break; }
+        for (int j = 0; j < it.nkv; ++j) {
+          if (j + kPrefetch < it.nkv) prefetch(j + kPrefetch);
+          if (j + 1 < it.nkv && !load(&tmK, smK, k_full, k_empty, kKStages, k_it, k_mask, k_par, j + 1)) {
+            ok = false;
+            break;
+          }
+          if (!load(&tmV, smV, v_full, v_empty, kVStages, v_it, v_mask, v_par, j)) { ok = false; break; }
         }
       }
       // drain: every copy this thread issued must land before the CTA exits
       if (q_issued) mbar_wait(q_full, q_par, nullptr, 0);
-      for (int s = 0; s < kStages; ++s)
-        if ((issued_mask >> s) & 1u) {
-          mbar_wait(&k_full[s], (par_mask >> s) & 1u, nullptr, 0);
-          mbar_wait(&v_full[s], (par_mask >> s) & 1u, nullptr, 0);
-        }
+      for (int s = 0; s < kKStages; ++s)
+        if ((k_mask >> s) & 1u) mbar_wait(&k_full[s], (k_par >> s) & 1u, nullptr, 0);
+      for (int s = 0; s < kVStages; ++s)
+        if ((v_mask >> s) & 1u) mbar_wait(&v_full[s], (v_par >> s) & 1u, nullptr, 0);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
@@ -199,51 +226,49 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       constexpr uint32_t idesc_s = make_idesc_bf16(BQ, BKV, 0, 0);
       constexpr uint32_t idesc_o = make_idesc_bf16(BQ, D, 0, 1);
       const uint32_t aQ = smem_u32(smQ);
-      uint32_t kv_it = 0, s_it = 0, pv_it = 0, item_it = 0;
+      uint32_t s_it = 0, pv_it = 0, item_it = 0;  // S MMAs = K loads, PV MMAs = V loads (CTA totals)
       bool ok = true;
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++item_it) {
         const Item it = decode(item, cu, cu_k, tiles, Hq, group, causal);
         if (!mbar_wait(q_full, item_it & 1u, err, kTimeoutAttnQ)) { ok = false; break; }
         tc_fence_after();
-        auto issue_s = [&](int j) -> bool {
-          const uint32_t idx = kv_it + j;
-          const int st = idx % kStages;
-          if (!mbar_wait(&k_full[st], (idx / kStages) & 1u, err, kTimeoutAttnKV)) return false;
+        auto issue_s = [&]() -> bool {
+          const int ks = s_it % kKStages;
+          if (!mbar_wait(&k_full[ks], (s_it / kKStages) & 1u, err, kTimeoutAttnKV)) return false;
           const int sb = s_it & 1;
           if (!mbar_wait(&s_empty[sb], ((s_it >> 1) & 1u) ^ 1u, err, kTimeoutAttnS)) return false;
           tc_fence_after();
-          const uint32_t aK = smem_u32(smK + st * kTile);
+          const uint32_t aK = smem_u32(smK + ks * kTile);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
             umma_f16(tmem_base + sb * BKV, kmajor_desc(aQ, kk), kmajor_desc(aK, kk), idesc_s, kk > 0 ? 1u : 0u);
           umma_commit(&s_full[sb]);
+          umma_commit(&k_empty[ks]);
           ++s_it;
           return true;
         };
-        if (!issue_s(0)) { ok = false; break; }
+        if (!issue_s()) { ok = false; break; }
         for (int j = 0; j < it.nkv && ok; ++j) {
           if (j + 1 < it.nkv) {
-            if (!issue_s(j + 1)) { ok = false; break; }
+            if (!issue_s()) { ok = false; break; }
           } else {
             umma_commit(q_empty);  // every S MMA of this item is issued: Q frees when they finish
           }
-          const uint32_t idx = kv_it + j;
-          const int st = idx % kStages;
+          const int vs = pv_it % kVStages;
           const int pb = pv_it & 1;
           if (!mbar_wait(&p_full[pb], (pv_it >> 1) & 1u, err, kTimeoutAttnP)) { ok = false; break; }
-          if (!mbar_wait(&v_full[st], (idx / kStages) & 1u, err, kTimeoutAttnKV)) { ok = false; break; }
+          if (!mbar_wait(&v_full[vs], (pv_it / kVStages) & 1u, err, kTimeoutAttnKV)) { ok = false; break; }
           if (j == 0 && !mbar_wait(o_empty, (item_it & 1u) ^ 1u, err, kTimeoutAttnO)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t aV = smem_u32(smV + st * kTile);
+          const uint32_t aV = smem_u32(smV + vs * kTile);
 #pragma unroll
           for (int kk = 0; kk < BKV / 16; ++kk)
             umma_f16_ts(tmem_base + kColO, tmem_base + kColP + pb * 64 + kk * 8, mnmajor_desc(aV, kk), idesc_o,
                         (j > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&kv_empty[st]);
+          umma_commit(&v_empty[vs]);
           umma_commit(&p_empty[pb]);
           ++pv_it;
         }
-        kv_it += it.nkv;
       }
       umma_commit(done);
       mbar_wait(done, 0, nullptr, 0);
@@ -349,10 +374,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int i = 0; i < 16; ++i) {
           float p[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float x = fmaf(__uint_as_float(r[4 * i + e]), scale_log2, (e < 2) ? nm0 : nm1);
-            p[e] = ((i & 3) * 4 + e >= 16 - kPolyPer16) ? ex2_poly(x) : ex2_approx(x);
-          }
+          for (int e = 0; e < 4; ++e)
+            p[e] = ex2_approx(fmaf(__uint_as_float(r[4 * i + e]), scale_log2, (e < 2) ? nm0 : nm1));
           s0a += p[0];
           s0b += p[1];
           s1a += p[2];

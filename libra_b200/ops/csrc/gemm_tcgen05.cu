@@ -74,6 +74,104 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
   nb = in / gm;
 }
 
+// Epilogue of one output tile: this thread's accumulator row (TMEM lane
+// quarter*32+lane, columns from tacc) to row `row` of C, columns of block nb.
+template <int BN, int EPI>
+__device__ __forceinline__ void store_tile_row(uint32_t tacc, int row, int nb, int M, int N, void* __restrict__ C,
+                                               const __nv_bfloat16* __restrict__ R, int ldc, int ldr,
+                                               __nv_bfloat16* __restrict__ C2, int ldc2) {
+  const bool row_ok = row < M;
+  if constexpr (EPI == kSwiGLU) {
+#pragma unroll 1
+    for (int chunk = 0; chunk < 4; ++chunk) {
+      uint32_t g[32], u[32];
+      const uint32_t t0 = tacc + chunk * 32;
+      tmem_ld_32x32b_x32(t0, g);
+      tmem_ld_32x32b_x32(t0 + 128, u);
+      tmem_ld_wait();
+      const int col0 = nb * 128 + chunk * 32;
+      if (!row_ok || col0 >= N) continue;
+      __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(C) + (size_t)row * ldc + col0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float a[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          // round gate/up to bf16 first so the result equals the unfused gate_up -> swiglu path
+          const float gv = __bfloat162float(__float2bfloat16(__uint_as_float(g[j * 8 + e])));
+          const float uv = __bfloat162float(__float2bfloat16(__uint_as_float(u[j * 8 + e])));
+          a[e] = silu_f(gv) * uv;
+        }
+        uint4 pk;
+        pk.x = pack_bf16x2(a[0], a[1]);
+        pk.y = pack_bf16x2(a[2], a[3]);
+        pk.z = pack_bf16x2(a[4], a[5]);
+        pk.w = pack_bf16x2(a[6], a[7]);
+        *reinterpret_cast<uint4*>(out + j * 8) = pk;
+        if (C2 != nullptr) {
+          uint4 pg, pu;
+          pg.x = pack_bf16x2(__uint_as_float(g[j * 8 + 0]), __uint_as_float(g[j * 8 + 1]));
+          pg.y = pack_bf16x2(__uint_as_float(g[j * 8 + 2]), __uint_as_float(g[j * 8 + 3]));
+          pg.z = pack_bf16x2(__uint_as_float(g[j * 8 + 4]), __uint_as_float(g[j * 8 + 5]));
+          pg.w = pack_bf16x2(__uint_as_float(g[j * 8 + 6]), __uint_as_float(g[j * 8 + 7]));
+          pu.x = pack_bf16x2(__uint_as_float(u[j * 8 + 0]), __uint_as_float(u[j * 8 + 1]));
+          pu.y = pack_bf16x2(__uint_as_float(u[j * 8 + 2]), __uint_as_float(u[j * 8 + 3]));
+          pu.z = pack_bf16x2(__uint_as_float(u[j * 8 + 4]), __uint_as_float(u[j * 8 + 5]));
+          pu.w = pack_bf16x2(__uint_as_float(u[j * 8 + 6]), __uint_as_float(u[j * 8 + 7]));
+          __nv_bfloat16* gr = C2 + (size_t)row * ldc2 + col0 + j * 8;
+          *reinterpret_cast<uint4*>(gr) = pg;
+          *reinterpret_cast<uint4*>(gr + N) = pu;
+        }
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int chunk = 0; chunk < BN / 32; ++chunk) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tacc + chunk * 32, r);
+      tmem_ld_wait();
+      const int col0 = nb * BN + chunk * 32;
+      if (!row_ok || col0 >= N) continue;
+      if (EPI == kStoreBf16 || EPI == kStoreBf16AddResidual) {
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(C) + (size_t)row * ldc + col0;
+        const __nv_bfloat16* res = (EPI == kStoreBf16AddResidual) ? R + (size_t)row * ldr + col0 : nullptr;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (col0 + j * 8 >= N) break;
+          float v[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r[j * 8 + e]);
+          if (EPI == kStoreBf16AddResidual) {
+            uint4 rv = *reinterpret_cast<const uint4*>(res + j * 8);
+            const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] += __bfloat162float(rb[e]);
+          }
+          uint4 pk;
+          pk.x = pack_bf16x2(v[0], v[1]);
+          pk.y = pack_bf16x2(v[2], v[3]);
+          pk.z = pack_bf16x2(v[4], v[5]);
+          pk.w = pack_bf16x2(v[6], v[7]);
+          *reinterpret_cast<uint4*>(out + j * 8) = pk;
+        }
+      } else {
+        float* out = reinterpret_cast<float*>(C) + (size_t)row * ldc + col0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (col0 + j * 4 >= N) break;
+          float4 v = make_float4(__uint_as_float(r[j * 4]), __uint_as_float(r[j * 4 + 1]),
+                                 __uint_as_float(r[j * 4 + 2]), __uint_as_float(r[j * 4 + 3]));
+          if (EPI == kAccumF32) {
+            float4 o = *reinterpret_cast<const float4*>(out + j * 4);
+            v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
+          }
+          *reinterpret_cast<float4*>(out + j * 4) = v;
+        }
+      }
+    }
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* __restrict__ C,
@@ -214,100 +312,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, err, kTimeoutTmemFull)) break;
       tc_fence_after();
-      const int row = mb * BM + row_in_tile;
-      const bool row_ok = row < M;
-      if (EPI == kSwiGLU) {
-#pragma unroll 1
-        for (int chunk = 0; chunk < 4; ++chunk) {
-          uint32_t g[32], u[32];
-          const uint32_t t0 = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + chunk * 32;
-          tmem_ld_32x32b_x32(t0, g);
-          tmem_ld_32x32b_x32(t0 + 128, u);
-          tmem_ld_wait();
-          const int col0 = nb * 128 + chunk * 32;
-          if (!row_ok || col0 >= N) continue;
-          __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(C) + (size_t)row * ldc + col0;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            float a[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              // round gate/up to bf16 first so the result equals the unfused gate_up -> swiglu path
-              const float gv = __bfloat162float(__float2bfloat16(__uint_as_float(g[j * 8 + e])));
-              const float uv = __bfloat162float(__float2bfloat16(__uint_as_float(u[j * 8 + e])));
-              a[e] = silu_f(gv) * uv;
-            }
-            uint4 pk;
-            pk.x = pack_bf16x2(a[0], a[1]);
-            pk.y = pack_bf16x2(a[2], a[3]);
-            pk.z = pack_bf16x2(a[4], a[5]);
-            pk.w = pack_bf16x2(a[6], a[7]);
-            *reinterpret_cast<uint4*>(out + j * 8) = pk;
-            if (C2 != nullptr) {
-              uint4 pg, pu;
-              pg.x = pack_bf16x2(__uint_as_float(g[j * 8 + 0]), __uint_as_float(g[j * 8 + 1]));
-              pg.y = pack_bf16x2(__uint_as_float(g[j * 8 + 2]), __uint_as_float(g[j * 8 + 3]));
-              pg.z = pack_bf16x2(__uint_as_float(g[j * 8 + 4]), __uint_as_float(g[j * 8 + 5]));
-              pg.w = pack_bf16x2(__uint_as_float(g[j * 8 + 6]), __uint_as_float(g[j * 8 + 7]));
-              pu.x = pack_bf16x2(__uint_as_float(u[j * 8 + 0]), __uint_as_float(u[j * 8 + 1]));
-              pu.y = pack_bf16x2(__uint_as_float(u[j * 8 + 2]), __uint_as_float(u[j * 8 + 3]));
-              pu.z = pack_bf16x2(__uint_as_float(u[j * 8 + 4]), __uint_as_float(u[j * 8 + 5]));
-              pu.w = pack_bf16x2(__uint_as_float(u[j * 8 + 6]), __uint_as_float(u[j * 8 + 7]));
-              __nv_bfloat16* gr = C2 + (size_t)row * ldc2 + col0 + j * 8;
-              *reinterpret_cast<uint4*>(gr) = pg;
-              *reinterpret_cast<uint4*>(gr + N) = pu;
-            }
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[acc]);
-        continue;
-      }
-#pragma unroll 1
-      for (int chunk = 0; chunk < BN / 32; ++chunk) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + chunk * 32, r);
-        tmem_ld_wait();
-        const int col0 = nb * BN + chunk * 32;
-        if (!row_ok || col0 >= N) continue;
-        if (EPI == kStoreBf16 || EPI == kStoreBf16AddResidual) {
-          __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(C) + (size_t)row * ldc + col0;
-          const __nv_bfloat16* res = (EPI == kStoreBf16AddResidual) ? R + (size_t)row * ldr + col0 : nullptr;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            if (col0 + j * 8 >= N) break;
-            float v[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r[j * 8 + e]);
-            if (EPI == kStoreBf16AddResidual) {
-              uint4 rv = *reinterpret_cast<const uint4*>(res + j * 8);
-              const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) v[e] += __bfloat162float(rb[e]);
-            }
-            uint4 pk;
-            pk.x = pack_bf16x2(v[0], v[1]);
-            pk.y = pack_bf16x2(v[2], v[3]);
-            pk.z = pack_bf16x2(v[4], v[5]);
-            pk.w = pack_bf16x2(v[6], v[7]);
-            *reinterpret_cast<uint4*>(out + j * 8) = pk;
-          }
-        } else {
-          float* out = reinterpret_cast<float*>(C) + (size_t)row * ldc + col0;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            if (col0 + j * 4 >= N) break;
-            float4 v = make_float4(__uint_as_float(r[j * 4]), __uint_as_float(r[j * 4 + 1]),
-                                   __uint_as_float(r[j * 4 + 2]), __uint_as_float(r[j * 4 + 3]));
-            if (EPI == kAccumF32) {
-              float4 o = *reinterpret_cast<const float4*>(out + j * 4);
-              v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
-            }
-            *reinterpret_cast<float4*>(out + j * 4) = v;
-          }
-        }
-      }
+      store_tile_row<BN, EPI>(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN, mb * BM + row_in_tile, nb, M,
+                              N, C, R, ldc, ldr, C2, ldc2);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -318,6 +324,191 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, CF::kTmemCols);
+}
+
+// ------------------------------------------------------------------ CTA-pair kernel
+// 256 x 256 output tiles on a cluster of two CTAs (cta_group::2).  Each CTA
+// TMA-loads its own 128 rows of A and its own 128 rows (N) of B per K block
+// into its shared memory, with the completion counted on the leader's "full"
+// barrier; the leader issues M=256 x N=256 MMAs that read both CTAs' halves
+// and accumulate rows 0-127 into its TMEM and rows 128-255 into the peer's.
+// Per SM and K block this moves 32 KB of operands for 2 x 128 x 256 x 64
+// FLOPs, half of what the single-CTA 128 x 256 tile needs, so the tensor
+// pipe is no longer held back by shared-memory bandwidth.  Commits arrive on
+// both CTAs' barriers (tcgen05.commit multicast); the epilogue warps of both
+// CTAs release an accumulator on the leader's barrier.  Loads are never
+// multicast.  Same bounded waits as the single-CTA kernel; at exit the two
+// CTAs wait for each other (bounded) so neither frees TMEM or shared memory
+// the other may still use.
+namespace pair {
+constexpr int BN = 256;
+constexpr int kStageA = BM * BK * 2;   // this CTA's 128 rows of A
+constexpr int kStageB = 128 * BK * 2;  // this CTA's 128 rows (N) of B
+constexpr int kStageBytes = kStageA + kStageB;
+constexpr int kStages = 6;
+constexpr int kTmemCols = 2 * BN;
+// full[S] empty[S] tfull[2] tempty[2] done exitb
+constexpr int kBarBytes = 8 * (2 * kStages + 4 + 2) + 16;
+constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarBytes;
+}  // namespace pair
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     void* __restrict__ C, const __nv_bfloat16* __restrict__ R, int M, int N, int K, int ldc, int ldr,
+                     int* err, __nv_bfloat16* __restrict__ C2, int ldc2) {
+  using namespace pair;
+  static_assert(EPI != kSwiGLU || !B_MN, "SwiGLU epilogue: K-major weight");
+  constexpr int kTileN = EPI == kSwiGLU ? 128 : BN;
+  constexpr int S = kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + S * kStageA;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * kStageBytes);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;   // [2]
+  uint64_t* tempty = tfull + 2;  // [2]
+  uint64_t* done = tempty + 2;
+  uint64_t* exitb = done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(exitb + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+  const int num_m = (M + 2 * BM - 1) / (2 * BM);
+  const int num_n = (N + kTileN - 1) / kTileN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 8);  // 4 epilogue warps in each CTA
+    }
+    mbar_init(done, 1);
+    mbar_init(exitb, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before any remote arrive or copy targets them
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      const uint32_t full_leader = mapa_shared(smem_u32(full), 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = cluster; tile < num_tiles && ok; tile += nclusters) {
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, mb, nb);
+        const int m0 = mb * 2 * BM + (int)rank * BM;
+        const int n0 = EPI == kSwiGLU ? (rank ? N + nb * 128 : nb * 128) : nb * BN + (int)rank * 128;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, err, kTimeoutSmemEmpty)) { ok = false; break; }
+          if (rank == 0) mbar_expect_tx(&full[stage], 2 * kStageBytes);  // both CTAs' bytes
+          const uint32_t bar = full_leader + 8u * stage;
+          uint8_t* a_dst = smA + stage * kStageA;
+          uint8_t* b_dst = smB + stage * kStageB;
+          const int k0 = kb * BK;
+          if (A_MN) {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d_pair(a_dst + j * 64 * BK * 2, &tmA, bar, m0 + j * 64, k0);
+          } else {
+            tma_load_2d_pair(a_dst, &tmA, bar, k0, m0);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) tma_load_2d_pair(b_dst + j * 64 * BK * 2, &tmB, bar, n0 + j * 64, k0);
+          } else {
+            tma_load_2d_pair(b_dst, &tmB, bar, k0, n0);
+          }
+          if (++stage == S) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(2 * BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = cluster; tile < num_tiles && ok; tile += nclusters, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, err, kTimeoutTmemEmpty)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, err, kTimeoutTmaFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smA + stage * kStageA);
+          const uint32_t b_addr = smem_u32(smB + stage * kStageB);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = A_MN ? make_sw128_desc(a_addr + k * 2048, 64 * BK * 2, 1024)
+                                        : make_sw128_desc(a_addr + k * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? make_sw128_desc(b_addr + k * 2048, 64 * BK * 2, 1024)
+                                        : make_sw128_desc(b_addr + k * 32, 16, 1024);
+            umma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == S) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[acc], 0x3);
+      }
+      umma_commit_pair(done, 0x3);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    const uint32_t tempty_leader = mapa_shared(smem_u32(tempty), 0);
+    int local = 0;
+    for (int tile = cluster; tile < num_tiles; tile += nclusters, ++local) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, err, kTimeoutTmemFull)) break;
+      tc_fence_after();
+      store_tile_row<BN, EPI>(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN,
+                              mb * 2 * BM + (int)rank * BM + row_in_tile, nb, M, N, C, R, ldc, ldr, C2, ldc2);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * acc);
+    }
+  }
+
+  // Teardown: once every role of this CTA is through, wait for the last MMA
+  // (done), then for the peer to get here too before TMEM is freed and shared
+  // memory goes away.
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1 && lane == 0) mbar_wait(done, 0, err, kTimeoutPairExit);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_cluster(mapa_shared(smem_u32(exitb), rank ^ 1u));
+    mbar_wait(exitb, 0, err, kTimeoutPairExit);
+  }
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, kTmemCols);
 }
 
 // ------------------------------------------------------------------ host side
@@ -387,6 +578,44 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, void* c, const 
   LIBRA_LAUNCH_CHECK();
 }
 
+// The CTA-pair kernel takes every GEMM with more than one 128-row block and
+// more than 128 output columns; LIBRA_GEMM_PAIR=0 keeps the single-CTA kernel
+// (for comparisons).
+static bool use_pair(int64_t M, int64_t N) {
+  static const bool enabled = [] {
+    const char* e = std::getenv("LIBRA_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return enabled && M > BM && N > 128 && num_sms() >= 2;
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, void* c, const __nv_bfloat16* r, int M, int N,
+                        int K, int ldc, int ldr, int* err, cudaStream_t st, __nv_bfloat16* c2 = nullptr,
+                        int ldc2 = 0) {
+  auto kern = gemm_pair_kernel<A_MN, B_MN, EPI>;
+  constexpr int smem = pair::kSmemBytes;
+  static bool configured = false;  // one static per instantiation
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    configured = true;
+  }
+  constexpr int kTileN = EPI == kSwiGLU ? 128 : pair::BN;
+  const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + kTileN - 1) / kTileN);
+  const int clusters = tiles < num_sms() / 2 ? tiles : num_sms() / 2;
+  kern<<<2 * clusters, kThreads, smem, st>>>(ta, tb, c, r, M, N, K, ldc, ldr, err, c2, ldc2);
+  LIBRA_LAUNCH_CHECK();
+}
+
+template <int EPI>
+static void dispatch_pair(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, void* c,
+                          const __nv_bfloat16* r, int M, int N, int K, int ldc, int ldr, int* err, cudaStream_t st) {
+  if (!a_mn && !b_mn) launch_pair<false, false, EPI>(ta, tb, c, r, M, N, K, ldc, ldr, err, st);
+  else if (!a_mn && b_mn) launch_pair<false, true, EPI>(ta, tb, c, r, M, N, K, ldc, ldr, err, st);
+  else if (a_mn && b_mn) launch_pair<true, true, EPI>(ta, tb, c, r, M, N, K, ldc, ldr, err, st);
+  else launch_pair<true, false, EPI>(ta, tb, c, r, M, N, K, ldc, ldr, err, st);
+}
+
 template <int BN, int EPI>
 static void dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, void* c,
                            const __nv_bfloat16* r, int M, int N, int K, int ldc, int ldr, int* err, cudaStream_t st) {
@@ -399,6 +628,10 @@ static void dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CU
 // SwiGLU launch (K-major A, K-major gate_up weight).
 static void launch_swiglu(const CUtensorMap& ta, const CUtensorMap& tb, __nv_bfloat16* a_out, int lda_out,
                           __nv_bfloat16* gu_out, int ldgu, int M, int F, int K, int* err, cudaStream_t st) {
+  if (use_pair(M, 2 * F)) {
+    launch_pair<false, false, kSwiGLU>(ta, tb, a_out, nullptr, M, F, K, lda_out, 0, err, st, gu_out, ldgu);
+    return;
+  }
   auto kern = gemm_bf16_kernel<256, false, false, kSwiGLU>;
   constexpr int smem = Cfg<256>::kSmemBytes;
   static bool configured = false;
@@ -508,16 +741,19 @@ void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, boo
   const c10::cuda::CUDAGuard guard(a.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (trace) fprintf(stderr, "[gemm] stream=%p\n", (void*)st);
+  const bool paired = use_pair(M, N);
   const int BN = (N <= 128) ? 128 : 256;
   CUtensorMap ta = a_mn ? make_map(a.data_ptr(), M, K, a.stride(0), 64, 64) : make_map(a.data_ptr(), K, M, a.stride(0), 64, BM);
+  // a CTA of a pair loads 128 of the tile's 256 B rows
   CUtensorMap tb = b_mn ? make_map(b.data_ptr(), N, K, b.stride(0), 64, 64)
-                        : make_map(b.data_ptr(), K, N, b.stride(0), 64, BN);
+                        : make_map(b.data_ptr(), K, N, b.stride(0), 64, paired ? 128 : BN);
   if (trace) fprintf(stderr, "[gemm] tensor maps encoded\n");
   int* errp = err.data_ptr<int>();
   void* cp = c.data_ptr();
   const int ldc = (int)c.stride(0);
 #define LIBRA_GEMM_EPI(E)                                                                                   \
-  if (BN == 128) dispatch_major<128, E>(a_mn, b_mn, ta, tb, cp, rptr, M, N, K, ldc, (int)ldr, errp, st); \
+  if (paired) dispatch_pair<E>(a_mn, b_mn, ta, tb, cp, rptr, M, N, K, ldc, (int)ldr, errp, st);          \
+  else if (BN == 128) dispatch_major<128, E>(a_mn, b_mn, ta, tb, cp, rptr, M, N, K, ldc, (int)ldr, errp, st); \
   else dispatch_major<256, E>(a_mn, b_mn, ta, tb, cp, rptr, M, N, K, ldc, (int)ldr, errp, st);
   switch (epi) {
     case kStoreBf16: LIBRA_GEMM_EPI(kStoreBf16); break;

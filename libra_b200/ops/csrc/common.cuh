@@ -182,6 +182,12 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
+// out[0..3] += v (one vectorised reduction at L2; out 16-byte aligned).
+__device__ __forceinline__ void red_add_f32x4(float* out, float4 v) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(out), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
 // ---------------------------------------------------------------- CTA pairs
 // A cluster of two CTAs on neighbouring SMs issuing cta_group::2 MMAs: the
 // leader (rank 0) issues M=256 MMAs that read A rows and B columns from both

@@ -76,10 +76,12 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
 
 // Epilogue of one output tile: this thread's accumulator row (TMEM lane
 // quarter*32+lane, columns from tacc) to row `row` of C, columns of block nb.
+// With `atomic` (split-K partial tiles of the accumulate epilogue) the fp32
+// additions into C are reductions at L2, so the splits of a tile may overlap.
 template <int BN, int EPI>
 __device__ __forceinline__ void store_tile_row(uint32_t tacc, int row, int nb, int M, int N, void* __restrict__ C,
                                                const __nv_bfloat16* __restrict__ R, int ldc, int ldr,
-                                               __nv_bfloat16* __restrict__ C2, int ldc2) {
+                                               __nv_bfloat16* __restrict__ C2, int ldc2, bool atomic = false) {
   const bool row_ok = row < M;
   if constexpr (EPI == kSwiGLU) {
 #pragma unroll 1
@@ -162,6 +164,10 @@ __device__ __forceinline__ void store_tile_row(uint32_t tacc, int row, int nb, i
           float4 v = make_float4(__uint_as_float(r[j * 4]), __uint_as_float(r[j * 4 + 1]),
                                  __uint_as_float(r[j * 4 + 2]), __uint_as_float(r[j * 4 + 3]));
           if (EPI == kAccumF32) {
+            if (atomic) {
+              red_add_f32x4(out + j * 4, v);
+              continue;
+            }
             float4 o = *reinterpret_cast<const float4*>(out + j * 4);
             v.x += o.x; v.y += o.y; v.z += o.z; v.w += o.w;
           }
@@ -356,7 +362,7 @@ template <bool A_MN, bool B_MN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      void* __restrict__ C, const __nv_bfloat16* __restrict__ R, int M, int N, int K, int ldc, int ldr,
-                     int* err, __nv_bfloat16* __restrict__ C2, int ldc2) {
+                     int* err, __nv_bfloat16* __restrict__ C2, int ldc2, int splits) {
   using namespace pair;
   static_assert(EPI != kSwiGLU || !B_MN, "SwiGLU epilogue: K-major weight");
   constexpr int kTileN = EPI == kSwiGLU ? 128 : BN;
@@ -381,6 +387,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int num_n = (N + kTileN - 1) / kTileN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (K + BK - 1) / BK;
+  // Work unit u = split * num_tiles + tile; split s covers K blocks
+  // [s * kb_per, min(num_kb, (s + 1) * kb_per)).  splits > 1 only with the
+  // accumulate epilogue (the host checks), whose partial tiles add atomically.
+  const int num_units = num_tiles * splits;
+  const int kb_per = (num_kb + splits - 1) / splits;
+  auto unit_range = [&](int u, int& tile, int& kb0, int& kb1) {
+    tile = u % num_tiles;
+    kb0 = (u / num_tiles) * kb_per;
+    kb1 = min(num_kb, kb0 + kb_per);
+  };
 
   if (threadIdx.x == 0) {
     prefetch_tmap(&tmA);
@@ -411,12 +427,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = cluster; tile < num_tiles && ok; tile += nclusters) {
-        int mb, nb;
+      for (int u = cluster; u < num_units && ok; u += nclusters) {
+        int tile, kb0, kb1, mb, nb;
+        unit_range(u, tile, kb0, kb1);
         tile_coords(tile, num_m, num_n, mb, nb);
         const int m0 = mb * 2 * BM + (int)rank * BM;
         const int n0 = EPI == kSwiGLU ? (rank ? N + nb * 128 : nb * 128) : nb * BN + (int)rank * 128;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, err, kTimeoutSmemEmpty)) { ok = false; break; }
           if (rank == 0) mbar_expect_tx(&full[stage], 2 * kStageBytes);  // both CTAs' bytes
           const uint32_t bar = full_leader + 8u * stage;
@@ -447,13 +464,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int tile = cluster; tile < num_tiles && ok; tile += nclusters, ++local) {
+      for (int u = cluster; u < num_units && ok; u += nclusters, ++local) {
+        int tile, kb0, kb1;
+        unit_range(u, tile, kb0, kb1);
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, err, kTimeoutTmemEmpty)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, err, kTimeoutTmaFull)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smA + stage * kStageA);
@@ -464,7 +483,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                         : make_sw128_desc(a_addr + k * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? make_sw128_desc(b_addr + k * 2048, 64 * BK * 2, 1024)
                                         : make_sw128_desc(b_addr + k * 32, 16, 1024);
-            umma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            umma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           umma_commit_pair(&empty[stage], 0x3);
           if (++stage == S) { stage = 0; phase ^= 1u; }
@@ -480,15 +499,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t tempty_leader = mapa_shared(smem_u32(tempty), 0);
     int local = 0;
-    for (int tile = cluster; tile < num_tiles; tile += nclusters, ++local) {
-      int mb, nb;
+    for (int u = cluster; u < num_units; u += nclusters, ++local) {
+      int tile, kb0, kb1, mb, nb;
+      unit_range(u, tile, kb0, kb1);
       tile_coords(tile, num_m, num_n, mb, nb);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, err, kTimeoutTmemFull)) break;
       tc_fence_after();
       store_tile_row<BN, EPI>(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN,
-                              mb * 2 * BM + (int)rank * BM + row_in_tile, nb, M, N, C, R, ldc, ldr, C2, ldc2);
+                              mb * 2 * BM + (int)rank * BM + row_in_tile, nb, M, N, C, R, ldc, ldr, C2, ldc2,
+                              splits > 1);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * acc);
@@ -602,8 +623,27 @@ static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, void* c, c
   }
   constexpr int kTileN = EPI == kSwiGLU ? 128 : pair::BN;
   const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + kTileN - 1) / kTileN);
-  const int clusters = tiles < num_sms() / 2 ? tiles : num_sms() / 2;
-  kern<<<2 * clusters, kThreads, smem, st>>>(ta, tb, c, r, M, N, K, ldc, ldr, err, c2, ldc2);
+  const int max_clusters = num_sms() / 2;
+  // Split K (accumulate epilogue only) when the tiles leave the last wave of
+  // the persistent grid mostly idle: pick the split count (up to 4, at least
+  // 8 K blocks each) whose work units fill the waves best.
+  int splits = 1;
+  if (EPI == kAccumF32 && tiles < 8 * max_clusters) {
+    const int num_kb = (K + BK - 1) / BK;
+    double best = 0.0;
+    for (int s = 1; s <= 4 && num_kb >= 8 * s; ++s) {
+      const int units = tiles * s;
+      const int waves = (units + max_clusters - 1) / max_clusters;
+      const double fill = (double)units / ((double)waves * max_clusters);
+      if (fill > best + 0.02) {
+        best = fill;
+        splits = s;
+      }
+    }
+  }
+  const int units = tiles * splits;
+  const int clusters = units < max_clusters ? units : max_clusters;
+  kern<<<2 * clusters, kThreads, smem, st>>>(ta, tb, c, r, M, N, K, ldc, ldr, err, c2, ldc2, splits);
   LIBRA_LAUNCH_CHECK();
 }
 

@@ -45,7 +45,7 @@ def test_gemm_layouts(M, N, K, a_mn, b_mn):
     assert _rel(out, ref) < 8e-3
 
 
-@pytest.mark.parametrize("M,N,K", [(512, 384, 256), (333, 1024, 520)])
+@pytest.mark.parametrize("M,N,K", [(512, 384, 256), (333, 1024, 520), (1024, 768, 4096)])
 def test_gemm_epilogues(M, N, K):
     from libra_b200 import ops
 

@@ -2,6 +2,9 @@
 #include <torch/extension.h>
 
 namespace libra {
+void gemm_allreduce(torch::Tensor a, torch::Tensor b, bool b_mn, c10::optional<torch::Tensor> residual, torch::Tensor y,
+                    std::vector<int64_t> recv, std::vector<int64_t> gath, std::vector<int64_t> flags, int64_t me,
+                    int64_t parity, int64_t max_rows, torch::Tensor err);
 void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, bool b_mn, int64_t epi,
                c10::optional<torch::Tensor> residual, torch::Tensor err);
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps);
@@ -71,6 +74,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_fwd", &libra::attn::flash_fwd, "tcgen05 varlen GQA attention forward", py::arg("q"), py::arg("k"),
         py::arg("v"), py::arg("cu_seqlens"), py::arg("tiles"), py::arg("scale"), py::arg("causal"), py::arg("err"),
         py::arg("cu_k") = py::none());
+  m.def("gemm_allreduce", &libra::gemm_allreduce,
+        "tensor-parallel GEMM fused with a peer-memory all-reduce (+ residual)");
   m.def("flash_bwd", &libra::attn::flash_bwd, "tcgen05 varlen GQA attention backward (dq, dk, dv)");
   m.def("ipc_export", &libra::ipc::ipc_export, "CUDA IPC handle of the allocation holding a tensor + offset");
   m.def("ipc_open", &libra::ipc::ipc_open, "map a peer allocation into the current device's context");

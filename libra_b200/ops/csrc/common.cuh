@@ -188,6 +188,36 @@ __device__ __forceinline__ void red_add_f32x4(float* out, float4 v) {
                : "memory");
 }
 
+// ---------------------------------------------------------------- peer flags
+// System-scope flag accesses for synchronisation with other GPUs over NVLink.
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void red_add_release_sys(int* p, int v) {
+  asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Spin (bounded) until *flag >= target; false and an error code on timeout.
+__device__ __forceinline__ bool wait_flag_geq(const int* flag, int target, int* err, int code) {
+  if (ld_acquire_sys(flag) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (ld_acquire_sys(flag) < target) {
+    if ((++spins & 1023u) == 0u && globaltimer_ns() - t0 > LIBRA_WAIT_NS) {
+      if (err) atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+  return true;
+}
+
 // ---------------------------------------------------------------- CTA pairs
 // A cluster of two CTAs on neighbouring SMs issuing cta_group::2 MMAs: the
 // leader (rank 0) issues M=256 MMAs that read A rows and B columns from both

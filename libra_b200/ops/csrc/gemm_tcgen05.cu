@@ -358,12 +358,41 @@ constexpr int kBarBytes = 8 * (2 * kStages + 4 + 2) + 16;
 constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarBytes;
 }  // namespace pair
 
-template <bool A_MN, bool B_MN, int EPI>
+// Tensor-parallel all-reduce fused into the GEMM (kPeerAR): every rank of the
+// group computes its partial Y_r = A_r B_r^T; the output is sum_r Y_r (plus an
+// optional residual) on every rank.  Over NVLink peer memory, in one launch:
+//   A  GEMM tiles; the epilogue stores each 256-row block's bf16 partial
+//      straight into the receive area of the block's owner (rank mb % n), slot
+//      [me], and bumps the owner's arrival counter for the block (release).
+//   B  each CTA takes (owned row block, 256-column chunk) units: waits until
+//      all n * num_n * 8 epilogue warps have arrived, sums the n partials in
+//      fp32 and writes the bf16 sum into every rank's gathered buffer, then
+//      bumps every rank's "done" counter for the block (reduce-scatter +
+//      all-gather, each byte crossing NVLink once per direction).
+//   C  each CTA copies finished row blocks of its own gathered buffer (plus
+//      the residual) into the output tensor, so the kernel ends only when the
+//      full sum is here.
+// Counters live in two parity sets; a call zeroes the set the next call uses
+// (safe: no peer can start the next call before this rank's phase B).  Every
+// wait is bounded.  Plain loads and stores to peer memory, no multicast.
+constexpr int kMaxPeers = 8;
+struct PeerAR {
+  uint64_t recv[kMaxPeers];   // rank q's receive area: [n][max_rows, N] bf16
+  uint64_t gath[kMaxPeers];   // rank q's gathered sum: [max_rows, N] bf16
+  uint64_t flags[kMaxPeers];  // rank q's counters: int32 [2 parity][2 kind][max_rb]
+  __nv_bfloat16* y;           // this rank's output [M, N]
+  const __nv_bfloat16* residual;  // optional [M, N]
+  int64_t slot_elems;         // max_rows * N
+  int n, me, parity, max_rb;
+};
+
+template <bool A_MN, bool B_MN, int EPI, bool kPeerAR>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      void* __restrict__ C, const __nv_bfloat16* __restrict__ R, int M, int N, int K, int ldc, int ldr,
-                     int* err, __nv_bfloat16* __restrict__ C2, int ldc2, int splits) {
+                     int* err, __nv_bfloat16* __restrict__ C2, int ldc2, int splits, const __grid_constant__ PeerAR par) {
   using namespace pair;
+  static_assert(!kPeerAR || EPI == kStoreBf16, "peer all-reduce: bf16 partials");
   static_assert(EPI != kSwiGLU || !B_MN, "SwiGLU epilogue: K-major weight");
   constexpr int kTileN = EPI == kSwiGLU ? 128 : BN;
   constexpr int S = kStages;
@@ -412,6 +441,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mbar_init(done, 1);
     mbar_init(exitb, 1);
     fence_barrier_init();
+  }
+  if (kPeerAR && blockIdx.x == 0) {  // counters of the next call (see PeerAR)
+    int* nxt = reinterpret_cast<int*>(par.flags[par.me]) + (par.parity ^ 1) * 2 * par.max_rb;
+    for (int i = threadIdx.x; i < 2 * par.max_rb; i += blockDim.x) nxt[i] = 0;
+    __threadfence_system();
   }
   if (warp == 1) tmem_alloc_pair(tmem_slot, kTmemCols);
   tc_fence_before();
@@ -507,12 +541,94 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, err, kTimeoutTmemFull)) break;
       tc_fence_after();
-      store_tile_row<BN, EPI>(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN,
-                              mb * 2 * BM + (int)rank * BM + row_in_tile, nb, M, N, C, R, ldc, ldr, C2, ldc2,
-                              splits > 1);
+      const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      const int row = mb * 2 * BM + (int)rank * BM + row_in_tile;
+      if constexpr (kPeerAR) {
+        const int owner = mb % par.n;
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(par.recv[owner]) + (int64_t)par.me * par.slot_elems;
+        store_tile_row<BN, EPI>(tacc, row, nb, M, N, dst, nullptr, N, 0, nullptr, 0);
+      } else {
+        store_tile_row<BN, EPI>(tacc, row, nb, M, N, C, R, ldc, ldr, C2, ldc2, splits > 1);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * acc);
+      if constexpr (kPeerAR) {
+        __threadfence_system();  // this lane's partial rows reach the owner before the count
+        __syncwarp();
+        if (lane == 0)
+          red_add_release_sys(reinterpret_cast<int*>(par.flags[mb % par.n]) + par.parity * 2 * par.max_rb + mb, 1);
+      }
+    }
+  }
+
+  if constexpr (kPeerAR) {
+    __syncthreads();
+    __shared__ int s_ok;
+    int* my_flags = reinterpret_cast<int*>(par.flags[par.me]) + par.parity * 2 * par.max_rb;
+    const int n = par.n, me = par.me;
+    const int chunks = (N + BN - 1) / BN;
+    const int owned = me < num_m ? (num_m - me + n - 1) / n : 0;
+    const int arrivals = n * num_n * 8;  // epilogue warps of every rank's tiles in a row block
+    // ---- B: reduce owned row blocks, write the sum to every rank
+    for (int w = blockIdx.x; w < owned * chunks; w += gridDim.x) {
+      const int mb = me + (w / chunks) * n, ch = w % chunks;
+      if (threadIdx.x == 0) s_ok = wait_flag_geq(my_flags + mb, arrivals, err, kTimeoutPeerFlag);
+      __syncthreads();
+      if (!s_ok) break;
+      const __nv_bfloat16* mine = reinterpret_cast<const __nv_bfloat16*>(par.recv[me]);
+      const int r0 = mb * 2 * BM, c0 = ch * BN;
+      for (int v = threadIdx.x; v < 2 * BM * (BN / 8); v += blockDim.x) {
+        const int row = r0 + v / (BN / 8), col = c0 + (v % (BN / 8)) * 8;
+        if (row >= M || col >= N) continue;
+        const int64_t off = (int64_t)row * N + col;
+        float acc8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int q = 0; q < n; ++q) {
+          const uint4 u = *reinterpret_cast<const uint4*>(mine + q * par.slot_elems + off);
+          const __nv_bfloat16* ub = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc8[e] += __bfloat162float(ub[e]);
+        }
+        uint4 o;
+        o.x = pack_bf16x2(acc8[0], acc8[1]);
+        o.y = pack_bf16x2(acc8[2], acc8[3]);
+        o.z = pack_bf16x2(acc8[4], acc8[5]);
+        o.w = pack_bf16x2(acc8[6], acc8[7]);
+        for (int q = 0; q < n; ++q) *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(par.gath[q]) + off) = o;
+      }
+      __threadfence_system();
+      __syncthreads();
+      if (threadIdx.x < n)
+        red_add_release_sys(reinterpret_cast<int*>(par.flags[threadIdx.x]) + par.parity * 2 * par.max_rb +
+                                par.max_rb + mb, 1);
+    }
+    // ---- C: gathered row blocks (+ residual) into the output
+    for (int mb = blockIdx.x; mb < num_m; mb += gridDim.x) {
+      __syncthreads();
+      if (threadIdx.x == 0) s_ok = wait_flag_geq(my_flags + par.max_rb + mb, chunks, err, kTimeoutPeerFlag);
+      __syncthreads();
+      if (!s_ok) break;
+      const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(par.gath[me]);
+      const int r0 = mb * 2 * BM, nv = N / 8;
+      for (int v = threadIdx.x; v < 2 * BM * nv; v += blockDim.x) {
+        const int row = r0 + v / nv, col = (v % nv) * 8;
+        if (row >= M) break;
+        const int64_t off = (int64_t)row * N + col;
+        uint4 o = *reinterpret_cast<const uint4*>(g + off);
+        if (par.residual != nullptr) {
+          const uint4 rr = *reinterpret_cast<const uint4*>(par.residual + off);
+          const __nv_bfloat16* ob = reinterpret_cast<const __nv_bfloat16*>(&o);
+          const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rr);
+          float f[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] = __bfloat162float(ob[e]) + __bfloat162float(rb[e]);
+          o.x = pack_bf16x2(f[0], f[1]);
+          o.y = pack_bf16x2(f[2], f[3]);
+          o.z = pack_bf16x2(f[4], f[5]);
+          o.w = pack_bf16x2(f[6], f[7]);
+        }
+        *reinterpret_cast<uint4*>(par.y + off) = o;
+      }
     }
   }
 
@@ -610,20 +726,44 @@ static bool use_pair(int64_t M, int64_t N) {
   return enabled && M > BM && N > 128 && num_sms() >= 2;
 }
 
-template <bool A_MN, bool B_MN, int EPI>
+// Clusters of the pair kernel that fit on the device at once (SMs that cannot
+// be paired inside a GPC stay out), so the persistent grid has no tail wave
+// and the peer all-reduce's intra-grid waits always have their producers
+// resident.
+template <typename Kern>
+static int pair_clusters(Kern kern, int smem) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * (num_sms() / 2), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = num_sms() / 2;
+  }
+  return n < num_sms() / 2 ? n : num_sms() / 2;
+}
+
+template <bool A_MN, bool B_MN, int EPI, bool kPeerAR = false>
 static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, void* c, const __nv_bfloat16* r, int M, int N,
                         int K, int ldc, int ldr, int* err, cudaStream_t st, __nv_bfloat16* c2 = nullptr,
-                        int ldc2 = 0) {
-  auto kern = gemm_pair_kernel<A_MN, B_MN, EPI>;
+                        int ldc2 = 0, const PeerAR* par = nullptr) {
+  auto kern = gemm_pair_kernel<A_MN, B_MN, EPI, kPeerAR>;
   constexpr int smem = pair::kSmemBytes;
-  static bool configured = false;  // one static per instantiation
-  if (!configured) {
+  static int max_clusters = 0;  // one static per instantiation
+  if (!max_clusters) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    configured = true;
+    max_clusters = pair_clusters(kern, smem);
   }
   constexpr int kTileN = EPI == kSwiGLU ? 128 : pair::BN;
   const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + kTileN - 1) / kTileN);
-  const int max_clusters = num_sms() / 2;
   // Split K (accumulate epilogue only) when the tiles leave the last wave of
   // the persistent grid mostly idle: pick the split count (up to 4, at least
   // 8 K blocks each) whose work units fill the waves best.
@@ -642,8 +782,11 @@ static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, void* c, c
     }
   }
   const int units = tiles * splits;
-  const int clusters = units < max_clusters ? units : max_clusters;
-  kern<<<2 * clusters, kThreads, smem, st>>>(ta, tb, c, r, M, N, K, ldc, ldr, err, c2, ldc2, splits);
+  // the all-reduce phases need every cluster resident and some work for all
+  const int clusters = kPeerAR ? max_clusters : (units < max_clusters ? units : max_clusters);
+  PeerAR none = {};
+  kern<<<2 * clusters, kThreads, smem, st>>>(ta, tb, c, r, M, N, K, ldc, ldr, err, c2, ldc2, splits,
+                                             par ? *par : none);
   LIBRA_LAUNCH_CHECK();
 }
 
@@ -723,6 +866,63 @@ void gemm_swiglu(torch::Tensor x, torch::Tensor w, torch::Tensor a, c10::optiona
   CUtensorMap tb = make_map(w.data_ptr(), K, F2, w.stride(0), 64, 128);
   launch_swiglu(ta, tb, reinterpret_cast<__nv_bfloat16*>(a.data_ptr()), (int)a.stride(0), gup, ldgu, (int)M, (int)F,
                 (int)K, err.data_ptr<int>(), st);
+}
+
+// Tensor-parallel GEMM + all-reduce over peer memory (see PeerAR):
+//   y = sum over the group of (a_r b_r^T) (+ residual), on every rank.
+//   a: [M, K] bf16 K-major; b: [N, K] (b_mn=false) or [K, N] (b_mn=true);
+//   y, residual: [M, N] bf16 contiguous; recv/gath/flags: one device address
+//   per rank (this rank's own at index me), all mapped in this context.
+void gemm_allreduce(torch::Tensor a, torch::Tensor b, bool b_mn, c10::optional<torch::Tensor> residual, torch::Tensor y,
+                    std::vector<int64_t> recv, std::vector<int64_t> gath, std::vector<int64_t> flags, int64_t me,
+                    int64_t parity, int64_t max_rows, torch::Tensor err) {
+  using namespace gemm;
+  const int n = (int)recv.size();
+  LIBRA_CHECK(n >= 1 && n <= kMaxPeers && (int)gath.size() == n && (int)flags.size() == n && me >= 0 && me < n,
+              "gemm_allreduce: 1..8 ranks with one address of each buffer per rank");
+  LIBRA_CHECK(a.is_cuda() && b.is_cuda() && y.is_cuda() && a.scalar_type() == at::kBFloat16 &&
+                  b.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16,
+              "gemm_allreduce: CUDA bf16 tensors required");
+  LIBRA_CHECK(a.dim() == 2 && b.dim() == 2 && y.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1 && y.is_contiguous(),
+              "gemm_allreduce: 2-D operands with inner stride 1 and a contiguous output");
+  const int64_t M = a.size(0), K = a.size(1);
+  const int64_t N = b_mn ? b.size(1) : b.size(0);
+  LIBRA_CHECK((b_mn ? b.size(0) : b.size(1)) == K && y.size(0) == M && y.size(1) == N, "gemm_allreduce: shape mismatch");
+  LIBRA_CHECK(M >= 1 && M <= max_rows && K >= 1 && N % 8 == 0 && a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0,
+              "gemm_allreduce: need 1 <= M <= max_rows, N and leading dimensions multiples of 8");
+  const __nv_bfloat16* rp = nullptr;
+  if (residual.has_value()) {
+    LIBRA_CHECK(residual->scalar_type() == at::kBFloat16 && residual->is_contiguous() && residual->size(0) == M &&
+                    residual->size(1) == N,
+                "gemm_allreduce: residual must be a contiguous bf16 [M, N] tensor");
+    rp = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+  }
+  for (int q = 0; q < n; ++q)
+    LIBRA_CHECK(((recv[q] | gath[q]) & 15) == 0 && (flags[q] & 3) == 0, "gemm_allreduce: misaligned peer buffer");
+  PeerAR par = {};
+  for (int q = 0; q < n; ++q) {
+    par.recv[q] = (uint64_t)recv[q];
+    par.gath[q] = (uint64_t)gath[q];
+    par.flags[q] = (uint64_t)flags[q];
+  }
+  par.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  par.residual = rp;
+  par.slot_elems = max_rows * N;
+  par.n = n;
+  par.me = (int)me;
+  par.parity = (int)(parity & 1);
+  par.max_rb = (int)((max_rows + 2 * BM - 1) / (2 * BM));
+  const c10::cuda::CUDAGuard guard(a.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  CUtensorMap ta = make_map(a.data_ptr(), K, M, a.stride(0), 64, BM);
+  CUtensorMap tb = b_mn ? make_map(b.data_ptr(), N, K, b.stride(0), 64, 64) : make_map(b.data_ptr(), K, N, b.stride(0), 64, 128);
+  int* errp = err.data_ptr<int>();
+  if (b_mn)
+    launch_pair<false, true, kStoreBf16, true>(ta, tb, nullptr, nullptr, (int)M, (int)N, (int)K, (int)N, 0, errp, st,
+                                               nullptr, 0, &par);
+  else
+    launch_pair<false, false, kStoreBf16, true>(ta, tb, nullptr, nullptr, (int)M, (int)N, (int)K, (int)N, 0, errp, st,
+                                                nullptr, 0, &par);
 }
 
 // Python entry: C (op)= A x B^T in the layouts described at the top of the file.

@@ -29,16 +29,6 @@ constexpr int kMaxRanks = 8;
 constexpr int kMaxCtas = 128;
 constexpr int kWarps = 8;
 
-__device__ __forceinline__ void st_release_sys(int* p, int v) {
-  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ int ld_acquire_sys(const int* p) {
-  int v;
-  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 struct PeerPtrs {
   uint64_t data[kMaxRanks];   // base of each rank's slot area
   uint64_t flags[kMaxRanks];  // base of each rank's flag area

@@ -1,0 +1,206 @@
+"""Tensor-parallel GEMM fused with its all-reduce over NVLink peer memory.
+
+The row-parallel linear of Megatron-style tensor parallelism (attention output
+projection, MLP down projection) computes a partial ``a_r w_r^T`` on every
+rank and all-reduces it; the reference reaches this through Megatron-Core's
+``RowParallelLinear`` (NCCL all-reduce after cuBLAS, engine/megatron_core_
+train_engine.py:887-903).  Here one kernel (``gemm_allreduce`` in
+``ops/csrc/gemm_tcgen05.cu``) does both: the CTA-pair GEMM's epilogue stores
+each 256-row block of the partial into the receive area of the rank that owns
+that block, the owner sums the partials in fp32 and writes the sum to every
+rank, and each rank copies the finished blocks (plus the residual) into its
+output.  Each byte crosses NVLink once per direction, as in a reduce-scatter +
+all-gather, and the transfers overlap the GEMM tiles still running.
+
+``PeerGemmAllReduce`` owns one symmetric buffer per (group, N): receive area
+``[n][max_rows, N]``, gathered sum ``[max_rows, N]`` and the arrival counters,
+shared through CUDA IPC handles and opened in this device's context.  Calls
+must be made in the same order on every rank of the group.
+"""
+
+from __future__ import annotations
+
+from typing import Dict, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+from libra_b200 import ops
+
+MAX_RANKS = 8
+ROW_BLOCK = 256
+
+
+class PeerGemmAllReduce:
+    def __init__(self, group, max_rows: int, n_cols: int, device):
+        self.group = group
+        self.n = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.me = dist.get_rank(group) if dist.is_initialized() else 0
+        if self.n > MAX_RANKS:
+            raise ValueError(f"at most {MAX_RANKS} ranks")
+        if n_cols % 8:
+            raise ValueError("N must be a multiple of 8")
+        self.max_rows, self.n_cols = int(max_rows), int(n_cols)
+        slot = self.max_rows * self.n_cols * 2
+        self.recv_bytes = (self.n * slot + 255) // 256 * 256
+        self.gath_bytes = (slot + 255) // 256 * 256
+        max_rb = (self.max_rows + ROW_BLOCK - 1) // ROW_BLOCK
+        flag_bytes = (4 * max_rb * 4 + 255) // 256 * 256
+        self.buf = torch.zeros(self.recv_bytes + self.gath_bytes + flag_bytes, dtype=torch.uint8, device=device)
+        bases = [int(self.buf.data_ptr())]
+        self._opened = []
+        if self.n > 1:
+            C = ops.ext()
+            handles = [None] * self.n
+            dist.all_gather_object(handles, C.ipc_export(self.buf), group=self.group)
+            bases = []
+            with torch.cuda.device(self.buf.device):
+                for r, (h, off) in enumerate(handles):
+                    if r == self.me:
+                        bases.append(int(self.buf.data_ptr()))
+                    else:
+                        base = C.ipc_open(h)
+                        self._opened.append(base)
+                        bases.append(base + int(off))
+        self.recv = bases
+        self.gath = [b + self.recv_bytes for b in bases]
+        self.flags = [b + self.recv_bytes + self.gath_bytes for b in bases]
+        self.calls = 0
+        if self.n > 1:
+            torch.cuda.synchronize(self.buf.device)
+            dist.barrier(group=self.group)
+
+    def close(self) -> None:
+        for base in self._opened:
+            ops.ext().ipc_close(base)
+        self._opened = []
+
+    def __call__(self, a: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None,
+                 b_mn: bool = False) -> torch.Tensor:
+        """sum over ranks of a_r @ w_r^T (w_r: [N, K], or [K, N] with ``b_mn``) + residual."""
+        a2 = a.reshape(-1, a.shape[-1])
+        if not a2.is_contiguous():
+            a2 = a2.contiguous()
+        N = w.shape[1] if b_mn else w.shape[0]
+        if N != self.n_cols or a2.shape[0] > self.max_rows:
+            raise ValueError(f"buffer is for N={self.n_cols}, up to {self.max_rows} rows; got N={N}, "
+                             f"{a2.shape[0]} rows")
+        y = torch.empty(a2.shape[0], N, dtype=a.dtype, device=a.device)
+        res = residual.reshape(-1, N).contiguous() if residual is not None else None
+        ops.ext().gemm_allreduce(a2, w, bool(b_mn), res, y, self.recv, self.gath, self.flags, self.me,
+                                 self.calls & 1, self.max_rows, ops.error_flag(a.device))
+        self.calls += 1
+        return y.view(*a.shape[:-1], N)
+
+
+_REGISTRY: Dict[Tuple[int, int], PeerGemmAllReduce] = {}
+
+
+def enable_fused_row_parallel(group, max_rows: int, n_cols_list, device) -> None:
+    """Create the peer buffers for the row-parallel GEMMs of a TP group (one per
+    output width); afterwards ``row_parallel_linear`` on that group runs the
+    fused kernel.  Collective: call on every rank of the group."""
+    for n_cols in sorted(set(int(c) for c in n_cols_list)):
+        key = (id(group), n_cols)
+        if key not in _REGISTRY:
+            _REGISTRY[key] = PeerGemmAllReduce(group, max_rows, n_cols, device)
+
+
+def fused_for(group, n_cols: int, rows: int) -> Optional[PeerGemmAllReduce]:
+    f = _REGISTRY.get((id(group), int(n_cols)))
+    return f if f is not None and rows <= f.max_rows else None
+
+
+def disable_fused_row_parallel() -> None:
+    for f in _REGISTRY.values():
+        f.close()
+    _REGISTRY.clear()
+
+
+class _RowParallelFused(torch.autograd.Function):
+    """Forward: fused GEMM + all-reduce (+ residual).  Backward needs no
+    collective: dA_r = dY W_r and dW_r = dY^T A_r on every rank."""
+
+    @staticmethod
+    def forward(ctx, a, w, residual, fused):
+        a2 = a.reshape(-1, a.shape[-1])
+        if not a2.is_contiguous():
+            a2 = a2.contiguous()
+        y = fused(a2, w, residual)
+        ctx.save_for_backward(a2, w)
+        ctx.in_shape = a.shape
+        ctx.has_residual = residual is not None
+        return y.view(*a.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        a2, w = ctx.saved_tensors
+        dy2 = dy.reshape(-1, w.shape[0]).contiguous()
+        da = ops.gemm(dy2, w, b_mn=True).view(ctx.in_shape) if ctx.needs_input_grad[0] else None
+        dw = ops._accumulate_wgrad(w, dy2, a2) if ctx.needs_input_grad[1] else None
+        return da, dw, (dy if ctx.has_residual else None), None
+
+
+def row_parallel_fused(a, w, residual, fused: PeerGemmAllReduce):
+    return _RowParallelFused.apply(a, w, residual, fused)
+
+
+def _bench(argv=None) -> None:
+    """torchrun --nproc-per-node N -m libra_b200.parallel.peer_gemm --rows 16384 --cols 2560 --inner 2048:
+    device time of the fused kernel against our GEMM + NCCL all-reduce (max over ranks)."""
+    import argparse
+    import datetime
+    import json
+    import os
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--rows", dest="m", type=int, default=16384)
+    ap.add_argument("--cols", dest="n", type=int, default=2560)
+    ap.add_argument("--inner", dest="k", type=int, default=2048)
+    ap.add_argument("--iters", type=int, default=20)
+    args = ap.parse_args(argv)
+    rank = int(os.environ.get("RANK", "0"))
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", torch.cuda.current_device()))
+    g = torch.Generator(device="cuda").manual_seed(rank)
+    a = torch.randn(args.m, args.k, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(args.n, args.k, device="cuda", generator=g) / args.k ** 0.5).bfloat16()
+    f = PeerGemmAllReduce(dist.group.WORLD, args.m, args.n, "cuda")
+
+    def fused():
+        return f(a, w)
+
+    def baseline():
+        y = ops.gemm(a, w)
+        dist.all_reduce(y)
+        return y
+
+    res = {}
+    for name, fn in (("fused", fused), ("gemm_plus_nccl", baseline)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / args.iters], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        res[name] = t.item()
+    ops.check_kernel_errors()
+    flops = 2.0 * args.m * args.n * args.k
+    if rank == 0:
+        print(json.dumps({"kernel": "gemm_allreduce", "ranks": dist.get_world_size(), "M": args.m, "N": args.n,
+                          "K": args.k, "fused_ms": res["fused"], "gemm_plus_nccl_ms": res["gemm_plus_nccl"],
+                          "speedup": res["gemm_plus_nccl"] / res["fused"],
+                          "fused_tflops_per_gpu": flops / res["fused"] / 1e9}), flush=True)
+    f.close()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    _bench()

@@ -66,7 +66,17 @@ def reduce_from_tp(x, group):
 
 
 def row_parallel_linear(a, w_local, residual, group):
-    """residual + all_reduce(a_local @ w_local^T) with autograd."""
+    """residual + all_reduce(a_local @ w_local^T) with autograd.
+
+    On CUDA with peer buffers registered for the group
+    (``peer_gemm.enable_fused_row_parallel``) this is one fused GEMM +
+    peer-memory all-reduce kernel; otherwise our GEMM followed by NCCL."""
+    if _ws(group) > 1 and a.is_cuda:
+        from libra_b200.parallel.peer_gemm import fused_for, row_parallel_fused
+
+        fused = fused_for(group, w_local.shape[0], a.numel() // a.shape[-1])
+        if fused is not None:
+            return row_parallel_fused(a, w_local, residual, fused)
     y = reduce_from_tp(ops.linear(a, w_local), group)
     return y + residual if residual is not None else y
 

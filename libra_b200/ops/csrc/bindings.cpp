@@ -4,7 +4,10 @@
 namespace libra {
 void gemm_allreduce(torch::Tensor a, torch::Tensor b, bool b_mn, c10::optional<torch::Tensor> residual, torch::Tensor y,
                     std::vector<int64_t> recv, std::vector<int64_t> gath, std::vector<int64_t> flags, int64_t me,
-                    int64_t parity, int64_t max_rows, torch::Tensor err);
+                    int64_t parity, int64_t max_rows, int64_t rs_rows, torch::Tensor err);
+void gemm_allgather(torch::Tensor a, torch::Tensor b, bool b_mn, torch::Tensor y, std::vector<int64_t> shards,
+                    std::vector<int64_t> ready, torch::Tensor gath, torch::Tensor counter, int64_t me, int64_t call,
+                    torch::Tensor err);
 void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, bool b_mn, int64_t epi,
                c10::optional<torch::Tensor> residual, torch::Tensor err);
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps);
@@ -75,7 +78,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("v"), py::arg("cu_seqlens"), py::arg("tiles"), py::arg("scale"), py::arg("causal"), py::arg("err"),
         py::arg("cu_k") = py::none());
   m.def("gemm_allreduce", &libra::gemm_allreduce,
-        "tensor-parallel GEMM fused with a peer-memory all-reduce (+ residual)");
+        "tensor-parallel GEMM fused with a peer-memory all-reduce or reduce-scatter (+ residual)");
+  m.def("gemm_allgather", &libra::gemm_allgather,
+        "sequence-parallel all-gather of the A rows fused into the tensor-parallel GEMM");
   m.def("flash_bwd", &libra::attn::flash_bwd, "tcgen05 varlen GQA attention backward (dq, dk, dv)");
   m.def("ipc_export", &libra::ipc::ipc_export, "CUDA IPC handle of the allocation holding a tensor + offset");
   m.def("ipc_open", &libra::ipc::ipc_open, "map a peer allocation into the current device's context");

@@ -376,23 +376,57 @@ constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarBytes;
 // (safe: no peer can start the next call before this rank's phase B).  Every
 // wait is bounded.  Plain loads and stores to peer memory, no multicast.
 constexpr int kMaxPeers = 8;
+// With rs_rows > 0 the same kernel is a GEMM + reduce-scatter (sequence
+// parallel): rank q owns rows [q rs_rows, (q+1) rs_rows) (rs_rows a multiple of
+// 256), phase B writes the owned sum (+ residual shard) straight into y
+// ([rs_rows, N]) and there is no all-gather and no phase C.
 struct PeerAR {
   uint64_t recv[kMaxPeers];   // rank q's receive area: [n][max_rows, N] bf16
   uint64_t gath[kMaxPeers];   // rank q's gathered sum: [max_rows, N] bf16
   uint64_t flags[kMaxPeers];  // rank q's counters: int32 [2 parity][2 kind][max_rb]
-  __nv_bfloat16* y;           // this rank's output [M, N]
-  const __nv_bfloat16* residual;  // optional [M, N]
+  __nv_bfloat16* y;           // this rank's output: [M, N], or [rs_rows, N]
+  const __nv_bfloat16* residual;  // optional, shaped like y
   int64_t slot_elems;         // max_rows * N
-  int n, me, parity, max_rb;
+  int n, me, parity, max_rb, rs_rows;
 };
 
-template <bool A_MN, bool B_MN, int EPI, bool kPeerAR>
+__device__ __forceinline__ int peer_owner(const PeerAR& p, int mb) {
+  return p.rs_rows > 0 ? (mb * 2 * BM) / p.rs_rows : mb % p.n;
+}
+
+// All-gather fused into the GEMM (sequence-parallel column-parallel linear):
+// the A operand's rows are sharded over the group (rank q holds rows
+// [q shard_rows, (q+1) shard_rows), shard_rows a multiple of 256).  At kernel
+// start the epilogue warps of every CTA copy the peers' shards over NVLink into
+// the local gathered buffer (each byte crosses once) and count themselves done
+// on a local counter; meanwhile the producer and MMA warps run the tiles of
+// the local shard (row blocks rotated so they come first), whose A tiles come
+// from the local shard directly.  Tiles of remote rows wait (bounded) for the
+// counter before their first TMA load.
+// Shards sit in per-rank symmetric slots (two, alternating by call parity);
+// rank q publishes "slot ready for call c" in ready[q][parity] at kernel start
+// (its host copied the shard in before the launch), and readers wait for it.
+// A slot is rewritten two calls later, which no rank reaches before every
+// peer has started the call in between, i.e. finished reading this one.
+struct PeerAG {
+  uint64_t shard[kMaxPeers];  // rank q's A shard slot for this call [shard_rows, K] bf16, mapped here
+  uint64_t ready[kMaxPeers];  // rank q's int32 ready[2]
+  __nv_bfloat16* gath;        // local [M, K] buffer for the peers' rows
+  int* counter;               // local, zero at launch; every epilogue warp adds 1 when its copy is done
+  int shard_rows, n, me, parity, call;
+};
+
+// kPeer: 0 plain GEMM, 1 GEMM + all-reduce / reduce-scatter (PeerAR),
+// 2 all-gather + GEMM (PeerAG).
+template <bool A_MN, bool B_MN, int EPI, int kPeer>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      void* __restrict__ C, const __nv_bfloat16* __restrict__ R, int M, int N, int K, int ldc, int ldr,
-                     int* err, __nv_bfloat16* __restrict__ C2, int ldc2, int splits, const __grid_constant__ PeerAR par) {
+                     int* err, __nv_bfloat16* __restrict__ C2, int ldc2, int splits, const __grid_constant__ PeerAR par,
+                     const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ PeerAG ag) {
   using namespace pair;
-  static_assert(!kPeerAR || EPI == kStoreBf16, "peer all-reduce: bf16 partials");
+  constexpr bool kPeerAR = kPeer == 1, kPeerAG = kPeer == 2;
+  static_assert(!kPeer || (EPI == kStoreBf16 && !A_MN), "peer modes: K-major A, bf16 output");
   static_assert(EPI != kSwiGLU || !B_MN, "SwiGLU epilogue: K-major weight");
   constexpr int kTileN = EPI == kSwiGLU ? 128 : BN;
   constexpr int S = kStages;
@@ -426,6 +460,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     kb0 = (u / num_tiles) * kb_per;
     kb1 = min(num_kb, kb0 + kb_per);
   };
+  // tile -> (row block, column block); with the all-gather the local shard's
+  // row blocks come first
+  const int rb_rot = kPeerAG ? ag.me * (ag.shard_rows / (2 * BM)) : 0;
+  auto coords = [&](int tile, int& mb, int& nb) {
+    tile_coords(tile, num_m, num_n, mb, nb);
+    if (kPeerAG) mb = (mb + rb_rot) % num_m;
+  };
 
   if (threadIdx.x == 0) {
     prefetch_tmap(&tmA);
@@ -441,6 +482,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mbar_init(done, 1);
     mbar_init(exitb, 1);
     fence_barrier_init();
+  }
+  if (kPeerAG && blockIdx.x == 0 && threadIdx.x == 0) {  // this rank's shard slot is in place
+    __threadfence_system();
+    st_release_sys(reinterpret_cast<int*>(ag.ready[ag.me]) + ag.parity, ag.call);
   }
   if (kPeerAR && blockIdx.x == 0) {  // counters of the next call (see PeerAR)
     int* nxt = reinterpret_cast<int*>(par.flags[par.me]) + (par.parity ^ 1) * 2 * par.max_rb;
@@ -460,13 +505,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t full_leader = mapa_shared(smem_u32(full), 0);
       int stage = 0;
       uint32_t phase = 0;
-      bool ok = true;
+      bool ok = true, gathered = false;
       for (int u = cluster; u < num_units && ok; u += nclusters) {
         int tile, kb0, kb1, mb, nb;
         unit_range(u, tile, kb0, kb1);
-        tile_coords(tile, num_m, num_n, mb, nb);
+        coords(tile, mb, nb);
         const int m0 = mb * 2 * BM + (int)rank * BM;
         const int n0 = EPI == kSwiGLU ? (rank ? N + nb * 128 : nb * 128) : nb * BN + (int)rank * 128;
+        const CUtensorMap* mapA = &tmA;
+        int ya = m0;
+        if (kPeerAG) {
+          const int owner = m0 / ag.shard_rows;
+          if (owner == ag.me) {
+            ya = m0 - ag.me * ag.shard_rows;  // rows of the local shard
+          } else {
+            mapA = &tmA2;  // the gathered buffer, indexed by global row
+            if (!gathered) {
+              if (!wait_flag_geq(ag.counter, 4 * (int)gridDim.x, err, kTimeoutPeerFlag)) { ok = false; break; }
+              fence_proxy_async_global();
+              gathered = true;
+            }
+          }
+        }
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, err, kTimeoutSmemEmpty)) { ok = false; break; }
           if (rank == 0) mbar_expect_tx(&full[stage], 2 * kStageBytes);  // both CTAs' bytes
@@ -478,7 +538,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int j = 0; j < BM / 64; ++j) tma_load_2d_pair(a_dst + j * 64 * BK * 2, &tmA, bar, m0 + j * 64, k0);
           } else {
-            tma_load_2d_pair(a_dst, &tmA, bar, k0, m0);
+            tma_load_2d_pair(a_dst, mapA, bar, k0, ya);
           }
           if (B_MN) {
 #pragma unroll
@@ -532,11 +592,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t tempty_leader = mapa_shared(smem_u32(tempty), 0);
+    if constexpr (kPeerAG) {  // all-gather of the peers' A shards, 16 bytes per lane and step
+      const int64_t vrow = K / 8, per_rank = (int64_t)ag.shard_rows * vrow;
+      const int64_t total = (int64_t)(ag.n - 1) * per_rank;
+      const int64_t gw = (int64_t)blockIdx.x * 4 + (warp - 2), nw = (int64_t)gridDim.x * 4;
+      bool ready_ok = true;
+      for (int q = 0; q < ag.n && ready_ok; ++q) {
+        if (q == ag.me) continue;
+        if (lane == 0)
+          ready_ok = wait_flag_geq(reinterpret_cast<const int*>(ag.ready[q]) + ag.parity, ag.call, err,
+                                   kTimeoutPeerFlag);
+        ready_ok = __shfl_sync(0xffffffffu, ready_ok, 0);
+      }
+      for (int64_t f = gw * 32 + lane; ready_ok && f < total; f += nw * 32) {
+        const int oi = (int)(f / per_rank);
+        const int o = oi < ag.me ? oi : oi + 1;  // skip this rank
+        const int64_t rem = f - (int64_t)oi * per_rank;
+        const uint4 v = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(ag.shard[o]) + rem * 8);
+        *reinterpret_cast<uint4*>(ag.gath + ((int64_t)o * ag.shard_rows) * K + rem * 8) = v;
+      }
+      fence_proxy_async_global();  // the TMA loads that read these rows go through the async proxy
+      __threadfence();
+      __syncwarp();
+      if (lane == 0 && ready_ok) atomicAdd(ag.counter, 1);
+    }
     int local = 0;
     for (int u = cluster; u < num_units; u += nclusters, ++local) {
       int tile, kb0, kb1, mb, nb;
       unit_range(u, tile, kb0, kb1);
-      tile_coords(tile, num_m, num_n, mb, nb);
+      coords(tile, mb, nb);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, err, kTimeoutTmemFull)) break;
@@ -544,7 +628,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       const int row = mb * 2 * BM + (int)rank * BM + row_in_tile;
       if constexpr (kPeerAR) {
-        const int owner = mb % par.n;
+        const int owner = peer_owner(par, mb);
         __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(par.recv[owner]) + (int64_t)par.me * par.slot_elems;
         store_tile_row<BN, EPI>(tacc, row, nb, M, N, dst, nullptr, N, 0, nullptr, 0);
       } else {
@@ -557,7 +641,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         __threadfence_system();  // this lane's partial rows reach the owner before the count
         __syncwarp();
         if (lane == 0)
-          red_add_release_sys(reinterpret_cast<int*>(par.flags[mb % par.n]) + par.parity * 2 * par.max_rb + mb, 1);
+          red_add_release_sys(reinterpret_cast<int*>(par.flags[peer_owner(par, mb)]) + par.parity * 2 * par.max_rb + mb,
+                              1);
       }
     }
   }
@@ -568,11 +653,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     int* my_flags = reinterpret_cast<int*>(par.flags[par.me]) + par.parity * 2 * par.max_rb;
     const int n = par.n, me = par.me;
     const int chunks = (N + BN - 1) / BN;
-    const int owned = me < num_m ? (num_m - me + n - 1) / n : 0;
+    const bool rs = par.rs_rows > 0;
+    const int rb_per = rs ? par.rs_rows / (2 * BM) : 0;
+    const int owned = rs ? rb_per : (me < num_m ? (num_m - me + n - 1) / n : 0);
     const int arrivals = n * num_n * 8;  // epilogue warps of every rank's tiles in a row block
-    // ---- B: reduce owned row blocks, write the sum to every rank
+    // ---- B: reduce owned row blocks; the sum goes to every rank (all-reduce)
+    // or into this rank's shard of y (reduce-scatter)
     for (int w = blockIdx.x; w < owned * chunks; w += gridDim.x) {
-      const int mb = me + (w / chunks) * n, ch = w % chunks;
+      const int mb = rs ? me * rb_per + w / chunks : me + (w / chunks) * n, ch = w % chunks;
+      __syncthreads();  // every thread has read the previous unit's s_ok
       if (threadIdx.x == 0) s_ok = wait_flag_geq(my_flags + mb, arrivals, err, kTimeoutPeerFlag);
       __syncthreads();
       if (!s_ok) break;
@@ -589,6 +678,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 8; ++e) acc8[e] += __bfloat162float(ub[e]);
         }
+        if (rs) {
+          const int64_t loff = (int64_t)(row - me * par.rs_rows) * N + col;
+          if (par.residual != nullptr) {
+            const uint4 rr = *reinterpret_cast<const uint4*>(par.residual + loff);
+            const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rr);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc8[e] += __bfloat162float(rb[e]);
+          }
+          uint4 o;
+          o.x = pack_bf16x2(acc8[0], acc8[1]);
+          o.y = pack_bf16x2(acc8[2], acc8[3]);
+          o.z = pack_bf16x2(acc8[4], acc8[5]);
+          o.w = pack_bf16x2(acc8[6], acc8[7]);
+          *reinterpret_cast<uint4*>(par.y + loff) = o;
+          continue;
+        }
         uint4 o;
         o.x = pack_bf16x2(acc8[0], acc8[1]);
         o.y = pack_bf16x2(acc8[2], acc8[3]);
@@ -596,6 +701,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         o.w = pack_bf16x2(acc8[6], acc8[7]);
         for (int q = 0; q < n; ++q) *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(par.gath[q]) + off) = o;
       }
+      if (rs) continue;
       __threadfence_system();
       __syncthreads();
       if (threadIdx.x < n)
@@ -603,7 +709,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                 par.max_rb + mb, 1);
     }
     // ---- C: gathered row blocks (+ residual) into the output
-    for (int mb = blockIdx.x; mb < num_m; mb += gridDim.x) {
+    for (int mb = blockIdx.x; !rs && mb < num_m; mb += gridDim.x) {
       __syncthreads();
       if (threadIdx.x == 0) s_ok = wait_flag_geq(my_flags + par.max_rb + mb, chunks, err, kTimeoutPeerFlag);
       __syncthreads();
@@ -751,11 +857,12 @@ static int pair_clusters(Kern kern, int smem) {
   return n < num_sms() / 2 ? n : num_sms() / 2;
 }
 
-template <bool A_MN, bool B_MN, int EPI, bool kPeerAR = false>
+template <bool A_MN, bool B_MN, int EPI, int kPeer = 0>
 static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, void* c, const __nv_bfloat16* r, int M, int N,
                         int K, int ldc, int ldr, int* err, cudaStream_t st, __nv_bfloat16* c2 = nullptr,
-                        int ldc2 = 0, const PeerAR* par = nullptr) {
-  auto kern = gemm_pair_kernel<A_MN, B_MN, EPI, kPeerAR>;
+                        int ldc2 = 0, const PeerAR* par = nullptr, const CUtensorMap* ta2 = nullptr,
+                        const PeerAG* ag = nullptr) {
+  auto kern = gemm_pair_kernel<A_MN, B_MN, EPI, kPeer>;
   constexpr int smem = pair::kSmemBytes;
   static int max_clusters = 0;  // one static per instantiation
   if (!max_clusters) {
@@ -782,11 +889,12 @@ static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, void* c, c
     }
   }
   const int units = tiles * splits;
-  // the all-reduce phases need every cluster resident and some work for all
-  const int clusters = kPeerAR ? max_clusters : (units < max_clusters ? units : max_clusters);
-  PeerAR none = {};
+  // the peer phases need every cluster resident (their waits depend on each other)
+  const int clusters = kPeer ? max_clusters : (units < max_clusters ? units : max_clusters);
+  const PeerAR no_par = {};
+  PeerAG no_ag = {};
   kern<<<2 * clusters, kThreads, smem, st>>>(ta, tb, c, r, M, N, K, ldc, ldr, err, c2, ldc2, splits,
-                                             par ? *par : none);
+                                             par ? *par : no_par, ta2 ? *ta2 : ta, ag ? *ag : no_ag);
   LIBRA_LAUNCH_CHECK();
 }
 
@@ -875,7 +983,7 @@ void gemm_swiglu(torch::Tensor x, torch::Tensor w, torch::Tensor a, c10::optiona
 //   per rank (this rank's own at index me), all mapped in this context.
 void gemm_allreduce(torch::Tensor a, torch::Tensor b, bool b_mn, c10::optional<torch::Tensor> residual, torch::Tensor y,
                     std::vector<int64_t> recv, std::vector<int64_t> gath, std::vector<int64_t> flags, int64_t me,
-                    int64_t parity, int64_t max_rows, torch::Tensor err) {
+                    int64_t parity, int64_t max_rows, int64_t rs_rows, torch::Tensor err) {
   using namespace gemm;
   const int n = (int)recv.size();
   LIBRA_CHECK(n >= 1 && n <= kMaxPeers && (int)gath.size() == n && (int)flags.size() == n && me >= 0 && me < n,
@@ -887,14 +995,17 @@ void gemm_allreduce(torch::Tensor a, torch::Tensor b, bool b_mn, c10::optional<t
               "gemm_allreduce: 2-D operands with inner stride 1 and a contiguous output");
   const int64_t M = a.size(0), K = a.size(1);
   const int64_t N = b_mn ? b.size(1) : b.size(0);
-  LIBRA_CHECK((b_mn ? b.size(0) : b.size(1)) == K && y.size(0) == M && y.size(1) == N, "gemm_allreduce: shape mismatch");
+  LIBRA_CHECK((b_mn ? b.size(0) : b.size(1)) == K && y.size(1) == N && y.size(0) == (rs_rows > 0 ? rs_rows : M),
+              "gemm_allreduce: shape mismatch (y is [M, N], or [rs_rows, N] for a reduce-scatter)");
+  LIBRA_CHECK(rs_rows == 0 || (rs_rows % (2 * BM) == 0 && rs_rows * n == M),
+              "gemm_allreduce: reduce-scatter needs M = n * rs_rows with rs_rows a multiple of 256");
   LIBRA_CHECK(M >= 1 && M <= max_rows && K >= 1 && N % 8 == 0 && a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0,
               "gemm_allreduce: need 1 <= M <= max_rows, N and leading dimensions multiples of 8");
   const __nv_bfloat16* rp = nullptr;
   if (residual.has_value()) {
-    LIBRA_CHECK(residual->scalar_type() == at::kBFloat16 && residual->is_contiguous() && residual->size(0) == M &&
-                    residual->size(1) == N,
-                "gemm_allreduce: residual must be a contiguous bf16 [M, N] tensor");
+    LIBRA_CHECK(residual->scalar_type() == at::kBFloat16 && residual->is_contiguous() &&
+                    residual->size(0) == y.size(0) && residual->size(1) == N,
+                "gemm_allreduce: residual must be a contiguous bf16 tensor shaped like y");
     rp = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
   }
   for (int q = 0; q < n; ++q)
@@ -912,17 +1023,75 @@ void gemm_allreduce(torch::Tensor a, torch::Tensor b, bool b_mn, c10::optional<t
   par.me = (int)me;
   par.parity = (int)(parity & 1);
   par.max_rb = (int)((max_rows + 2 * BM - 1) / (2 * BM));
+  par.rs_rows = (int)rs_rows;
   const c10::cuda::CUDAGuard guard(a.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   CUtensorMap ta = make_map(a.data_ptr(), K, M, a.stride(0), 64, BM);
   CUtensorMap tb = b_mn ? make_map(b.data_ptr(), N, K, b.stride(0), 64, 64) : make_map(b.data_ptr(), K, N, b.stride(0), 64, 128);
   int* errp = err.data_ptr<int>();
   if (b_mn)
-    launch_pair<false, true, kStoreBf16, true>(ta, tb, nullptr, nullptr, (int)M, (int)N, (int)K, (int)N, 0, errp, st,
-                                               nullptr, 0, &par);
+    launch_pair<false, true, kStoreBf16, 1>(ta, tb, nullptr, nullptr, (int)M, (int)N, (int)K, (int)N, 0, errp, st,
+                                            nullptr, 0, &par);
   else
-    launch_pair<false, false, kStoreBf16, true>(ta, tb, nullptr, nullptr, (int)M, (int)N, (int)K, (int)N, 0, errp, st,
-                                                nullptr, 0, &par);
+    launch_pair<false, false, kStoreBf16, 1>(ta, tb, nullptr, nullptr, (int)M, (int)N, (int)K, (int)N, 0, errp, st,
+                                             nullptr, 0, &par);
+}
+
+// All-gather fused into the GEMM (see PeerAG): y = concat_q(a_q) b^T with a_q
+// the row shards of the group, y [n * shard_rows, N] on every rank.
+//   a: this rank's shard [shard_rows, K] bf16, already copied into its slot;
+//   shards: the slot of this call (parity = call & 1) on every rank and
+//   ready: every rank's int32 ready[2] (all mapped here); gath: local
+//   [n * shard_rows, K] buffer; counter: a local int32 this call resets;
+//   call: 1-based call index, the same on every rank.
+void gemm_allgather(torch::Tensor a, torch::Tensor b, bool b_mn, torch::Tensor y, std::vector<int64_t> shards,
+                    std::vector<int64_t> ready, torch::Tensor gath, torch::Tensor counter, int64_t me, int64_t call,
+                    torch::Tensor err) {
+  using namespace gemm;
+  const int n = (int)shards.size();
+  LIBRA_CHECK(n >= 1 && n <= kMaxPeers && (int)ready.size() == n && me >= 0 && me < n && call >= 1,
+              "gemm_allgather: 1..8 ranks, one shard slot and one ready pair per rank, call >= 1");
+  LIBRA_CHECK(a.is_cuda() && b.is_cuda() && y.is_cuda() && gath.is_cuda() && a.scalar_type() == at::kBFloat16 &&
+                  b.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16 &&
+                  gath.scalar_type() == at::kBFloat16 && counter.scalar_type() == at::kInt,
+              "gemm_allgather: CUDA bf16 operands and an int32 counter");
+  LIBRA_CHECK(a.is_contiguous() && b.dim() == 2 && b.stride(1) == 1 && y.is_contiguous() && gath.is_contiguous(),
+              "gemm_allgather: contiguous shard, output and gather buffer");
+  const int64_t S = a.size(0), K = a.size(1), M = S * n;
+  const int64_t N = b_mn ? b.size(1) : b.size(0);
+  LIBRA_CHECK((b_mn ? b.size(0) : b.size(1)) == K && y.size(0) == M && y.size(1) == N && gath.size(0) >= M &&
+                  gath.size(1) == K,
+              "gemm_allgather: shape mismatch");
+  LIBRA_CHECK(S % (2 * BM) == 0 && K % 8 == 0 && N % 8 == 0 && b.stride(0) % 8 == 0,
+              "gemm_allgather: shard rows a multiple of 256, K and N multiples of 8");
+  for (int q = 0; q < n; ++q) LIBRA_CHECK((shards[q] & 15) == 0, "gemm_allgather: misaligned shard");
+  PeerAG ag = {};
+  for (int q = 0; q < n; ++q) {
+    LIBRA_CHECK((ready[q] & 7) == 0, "gemm_allgather: misaligned ready flags");
+    ag.shard[q] = (uint64_t)shards[q];
+    ag.ready[q] = (uint64_t)ready[q];
+  }
+  ag.parity = (int)(call & 1);
+  ag.call = (int)call;
+  ag.gath = reinterpret_cast<__nv_bfloat16*>(gath.data_ptr());
+  ag.counter = counter.data_ptr<int>();
+  ag.shard_rows = (int)S;
+  ag.n = n;
+  ag.me = (int)me;
+  const c10::cuda::CUDAGuard guard(a.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  LIBRA_CHECK(cudaMemsetAsync(counter.data_ptr(), 0, sizeof(int), st) == cudaSuccess, "gemm_allgather: memset failed");
+  CUtensorMap ta = make_map(a.data_ptr(), K, S, K, 64, BM);
+  CUtensorMap tg = make_map(gath.data_ptr(), K, M, K, 64, BM);
+  CUtensorMap tb = b_mn ? make_map(b.data_ptr(), N, K, b.stride(0), 64, 64) : make_map(b.data_ptr(), K, N, b.stride(0), 64, 128);
+  void* yp = y.data_ptr();
+  int* errp = err.data_ptr<int>();
+  if (b_mn)
+    launch_pair<false, true, kStoreBf16, 2>(ta, tb, yp, nullptr, (int)M, (int)N, (int)K, (int)N, 0, errp, st, nullptr,
+                                            0, nullptr, &tg, &ag);
+  else
+    launch_pair<false, false, kStoreBf16, 2>(ta, tb, yp, nullptr, (int)M, (int)N, (int)K, (int)N, 0, errp, st, nullptr,
+                                             0, nullptr, &tg, &ag);
 }
 
 // Python entry: C (op)= A x B^T in the layouts described at the top of the file.

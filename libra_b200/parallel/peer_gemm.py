@@ -88,9 +88,85 @@ class PeerGemmAllReduce:
         y = torch.empty(a2.shape[0], N, dtype=a.dtype, device=a.device)
         res = residual.reshape(-1, N).contiguous() if residual is not None else None
         ops.ext().gemm_allreduce(a2, w, bool(b_mn), res, y, self.recv, self.gath, self.flags, self.me,
-                                 self.calls & 1, self.max_rows, ops.error_flag(a.device))
+                                 self.calls & 1, self.max_rows, 0, ops.error_flag(a.device))
         self.calls += 1
         return y.view(*a.shape[:-1], N)
+
+    def reduce_scatter(self, a: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None,
+                       b_mn: bool = False) -> torch.Tensor:
+        """This rank's row shard of sum over ranks of a_r @ w_r^T (+ residual shard):
+        rows [me * M/n, (me+1) * M/n).  M must be a multiple of 256 * n."""
+        a2 = a.reshape(-1, a.shape[-1]).contiguous()
+        M = a2.shape[0]
+        N = w.shape[1] if b_mn else w.shape[0]
+        if N != self.n_cols or M > self.max_rows or M % (ROW_BLOCK * self.n):
+            raise ValueError(f"reduce-scatter needs N={self.n_cols}, M <= {self.max_rows} and M a multiple of "
+                             f"{ROW_BLOCK * self.n}; got N={N}, M={M}")
+        y = torch.empty(M // self.n, N, dtype=a.dtype, device=a.device)
+        res = residual.reshape(-1, N).contiguous() if residual is not None else None
+        ops.ext().gemm_allreduce(a2, w, bool(b_mn), res, y, self.recv, self.gath, self.flags, self.me,
+                                 self.calls & 1, self.max_rows, M // self.n, ops.error_flag(a.device))
+        self.calls += 1
+        return y
+
+
+class PeerAllGatherGemm:
+    """y = [a_0; a_1; ...; a_{n-1}] @ w^T for row shards a_q of the group
+    (sequence-parallel column-parallel linear, K1) in one kernel: peers' shards
+    are copied over NVLink into a local buffer by the GEMM's epilogue warps while
+    its first tiles (the local shard's rows) run.  Shards go through two
+    alternating symmetric slots per rank; calls in the same order on every rank."""
+
+    def __init__(self, group, shard_rows: int, k_cols: int, device):
+        self.group = group
+        self.n = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.me = dist.get_rank(group) if dist.is_initialized() else 0
+        if self.n > MAX_RANKS or shard_rows % ROW_BLOCK or k_cols % 8:
+            raise ValueError("at most 8 ranks, shard rows a multiple of 256, K a multiple of 8")
+        self.shard_rows, self.k_cols = int(shard_rows), int(k_cols)
+        self.slot_bytes = (self.shard_rows * self.k_cols * 2 + 255) // 256 * 256
+        self.buf = torch.zeros(2 * self.slot_bytes + 256, dtype=torch.uint8, device=device)
+        bases = [int(self.buf.data_ptr())]
+        self._opened = []
+        if self.n > 1:
+            C = ops.ext()
+            handles = [None] * self.n
+            dist.all_gather_object(handles, C.ipc_export(self.buf), group=self.group)
+            bases = []
+            with torch.cuda.device(self.buf.device):
+                for r, (h, off) in enumerate(handles):
+                    if r == self.me:
+                        bases.append(int(self.buf.data_ptr()))
+                    else:
+                        base = C.ipc_open(h)
+                        self._opened.append(base)
+                        bases.append(base + int(off))
+        self.slots = [(b, b + self.slot_bytes) for b in bases]
+        self.ready = [b + 2 * self.slot_bytes for b in bases]
+        self.gath = torch.empty(self.n * self.shard_rows, self.k_cols, dtype=torch.bfloat16, device=device)
+        self.counter = torch.zeros(1, dtype=torch.int32, device=device)
+        self.calls = 0
+        if self.n > 1:
+            torch.cuda.synchronize(self.buf.device)
+            dist.barrier(group=self.group)
+
+    def close(self) -> None:
+        for base in self._opened:
+            ops.ext().ipc_close(base)
+        self._opened = []
+
+    def __call__(self, a: torch.Tensor, w: torch.Tensor, b_mn: bool = False) -> torch.Tensor:
+        if a.shape != (self.shard_rows, self.k_cols):
+            raise ValueError(f"shard must be [{self.shard_rows}, {self.k_cols}], got {tuple(a.shape)}")
+        self.calls += 1
+        p = self.calls & 1
+        slot = self.buf[p * self.slot_bytes:p * self.slot_bytes + self.shard_rows * self.k_cols * 2]
+        slot.view(torch.bfloat16).view(self.shard_rows, self.k_cols).copy_(a)
+        N = w.shape[1] if b_mn else w.shape[0]
+        y = torch.empty(self.n * self.shard_rows, N, dtype=a.dtype, device=a.device)
+        ops.ext().gemm_allgather(a.contiguous(), w, bool(b_mn), y, [sl[p] for sl in self.slots], self.ready,
+                                 self.gath, self.counter, self.me, self.calls, ops.error_flag(a.device))
+        return y
 
 
 _REGISTRY: Dict[Tuple[int, int], PeerGemmAllReduce] = {}

@@ -28,6 +28,24 @@ def test_single_rank_fused_gemm_allreduce():
         ops.check_kernel_errors()
         ref = a.float() @ w.float().t() + (res.float() if res is not None else 0)
         torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2)
+    # reduce-scatter with one rank: the whole sum
+    a, wop, w = _inputs(0, 1024, 512, 2560, False, 9)
+    y = f.reduce_scatter(a, wop)
+    torch.testing.assert_close(y.float(), a.float() @ w.float().t(), rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.gpu
+def test_single_rank_fused_allgather_gemm():
+    from libra_b200 import ops
+    from libra_b200.parallel.peer_gemm import PeerAllGatherGemm
+
+    f = PeerAllGatherGemm(None, shard_rows=1024, k_cols=512, device="cuda")
+    for it, b_mn in enumerate([False, True, False]):
+        a, wop, w = _inputs(0, 1024, 512, 3072, b_mn, 20 + it)
+        y = f(a, wop, b_mn=b_mn)
+        torch.cuda.synchronize()
+        ops.check_kernel_errors()
+        torch.testing.assert_close(y.float(), a.float() @ w.float().t(), rtol=2e-2, atol=2e-2)
 
 
 def _port():
@@ -63,6 +81,26 @@ def _worker(rank, world, port, out_dir):
         ops.check_kernel_errors()
         ref = sum(p[0].float() @ p[2].float().t() for p in parts) + res.float()
         torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=3e-2)
+    # reduce-scatter: this rank's row shard of the sum
+    for it, b_mn in enumerate([False, True]):
+        M = 2048
+        parts = [_inputs(r, M, K, 2560, b_mn, 40 + it) for r in range(world)]
+        ref = sum(p[0].float() @ p[2].float().t() for p in parts)
+        y = f.reduce_scatter(parts[rank][0], parts[rank][1], b_mn=b_mn)
+        torch.cuda.synchronize()
+        ops.check_kernel_errors()
+        rows = M // world
+        torch.testing.assert_close(y.float(), ref[rank * rows:(rank + 1) * rows], rtol=2e-2, atol=3e-2)
+    # all-gather of row shards fused into the GEMM
+    ag = peer_gemm.PeerAllGatherGemm(grp, shard_rows=1024, k_cols=K, device="cuda")
+    for it in range(3):
+        shards = [_inputs(r, 1024, K, 8, False, 60 + it)[0] for r in range(world)]
+        _, wop, w = _inputs(0, 8, K, 3072, it == 1, 70 + it)  # the same local weight on every rank
+        y = ag(shards[rank], wop, b_mn=(it == 1))
+        torch.cuda.synchronize()
+        ops.check_kernel_errors()
+        torch.testing.assert_close(y.float(), torch.cat(shards).float() @ w.float().t(), rtol=2e-2, atol=2e-2)
+    ag.close()
     # autograd through row_parallel_linear: fused path against the NCCL path
     peer_gemm.enable_fused_row_parallel(grp, 4096, [2560], "cuda")
     a, _, w = _inputs(rank, 1536, K, 2560, False, 7)

@@ -38,7 +38,13 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = one 128-byte swizzle row
 constexpr int kThreads = 192;
 
-enum Epilogue : int { kStoreBf16 = 0, kStoreF32 = 1, kAccumF32 = 2, kStoreBf16AddResidual = 3, kSwiGLU = 4 };
+enum Epilogue : int {
+  kStoreBf16 = 0,
+  kStoreF32 = 1,
+  kAccumF32 = 2,
+  kStoreBf16AddResidual = 3,
+  kSwiGLU = 4
+};
 
 // kSwiGLU (fused gate/up projection + SwiGLU): B is the [2F, K] gate_up
 // weight; the B tile of output block nb stacks gate rows [128 nb, 128 nb + 128)
@@ -137,6 +143,12 @@ __device__ __forceinline__ void store_tile_row(uint32_t tacc, int row, int nb, i
       if (EPI == kStoreBf16 || EPI == kStoreBf16AddResidual) {
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(C) + (size_t)row * ldc + col0;
         const __nv_bfloat16* res = (EPI == kStoreBf16AddResidual) ? R + (size_t)row * ldr + col0 : nullptr;
+        uint4 rvs[4];
+        if (EPI == kStoreBf16AddResidual) {  // the chunk's residual loads in flight together
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            rvs[j] = col0 + j * 8 < N ? __ldg(reinterpret_cast<const uint4*>(res + j * 8)) : make_uint4(0, 0, 0, 0);
+        }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           if (col0 + j * 8 >= N) break;
@@ -144,7 +156,7 @@ __device__ __forceinline__ void store_tile_row(uint32_t tacc, int row, int nb, i
 #pragma unroll
           for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r[j * 8 + e]);
           if (EPI == kStoreBf16AddResidual) {
-            uint4 rv = *reinterpret_cast<const uint4*>(res + j * 8);
+            const uint4 rv = rvs[j];
             const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rv);
 #pragma unroll
             for (int e = 0; e < 8; ++e) v[e] += __bfloat162float(rb[e]);

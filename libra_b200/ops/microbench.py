@@ -63,6 +63,26 @@ def bench_gemm(shapes, iters: int):
         del A, B, a, b, out
 
 
+def bench_swiglu(iters: int, M: int = 16384, H: int = 2560, F: int = 9728):
+    """Gate/up GEMM with the SwiGLU epilogue (with and without the kept gate/up
+    output) against the plain GEMM of the same shape, and the SwiGLU backward."""
+    err = ops.error_flag(torch.device("cuda"))
+    x = torch.randn(M, H, device="cuda").to(torch.bfloat16)
+    wgu = (torch.randn(2 * F, H, device="cuda") / H ** 0.5).to(torch.bfloat16)
+    a = torch.empty(M, F, device="cuda", dtype=torch.bfloat16)
+    gu = torch.empty(M, 2 * F, device="cuda", dtype=torch.bfloat16)
+    ms_gu = _time(lambda: ops.ext().gemm_swiglu(x, wgu, a, gu, err), iters)
+    ms_nogu = _time(lambda: ops.ext().gemm_swiglu(x, wgu, a, None, err), iters)
+    ms_plain = _time(lambda: ops.gemm(x, wgu, out=gu), iters)
+    ms_bwd = _time(lambda: ops.ext().swiglu_bwd(gu, a), iters)
+    ops.check_kernel_errors()
+    flops = 2.0 * M * H * 2 * F
+    print(json.dumps({"kernel": "gemm_swiglu", "M": M, "H": H, "F": F, "with_gu_ms": ms_gu, "without_gu_ms": ms_nogu,
+                      "plain_gemm_ms": ms_plain, "tflops_with_gu": flops / ms_gu / 1e9,
+                      "tflops_plain": flops / ms_plain / 1e9, "swiglu_bwd_ms": ms_bwd,
+                      "swiglu_bwd_gbs": 5 * M * F * 2 / ms_bwd / 1e6}), flush=True)
+
+
 def bench_elementwise(iters: int):
     T, H = 65536, 2560
     x = torch.randn(T, H, device="cuda").to(torch.bfloat16)
@@ -135,7 +155,7 @@ def bench_attention(iters: int, lens=None):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "elementwise", "attention", "all"])
+    ap.add_argument("what", choices=["gemm", "elementwise", "attention", "swiglu", "all"])
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--shapes", default="", help="name:M,N,K,a_mn,b_mn;...")
     ap.add_argument("--lens", default="", help="attention: sequence lengths, e.g. 2048x4")
@@ -151,6 +171,8 @@ def main():
         bench_gemm(shapes, args.iters)
     if args.what in ("elementwise", "all"):
         bench_elementwise(args.iters)
+    if args.what in ("swiglu", "all"):
+        bench_swiglu(args.iters)
     if args.what in ("attention", "all"):
         lens = None
         if args.lens:

@@ -176,129 +176,198 @@ static inline void launch_colsum(const float* part, int rows, int cols, float* o
 }
 
 // ------------------------------------------------------------------ q/k norm + RoPE
-// One warp per (token, head) of the q and k sections.  Lane l owns the element
-// pairs (2l, 2l+1) and (64+2l, 65+2l) of a 128-wide head so rotate-half stays
-// inside the thread.
+// Eight lanes per (token, head), four heads per warp: lane j of a group owns
+// elements [8j, 8j+8) and [64+8j, 64+8j+8) of the 128-wide head, so the
+// rotate-half partner of every element sits in the same thread, every global
+// access is 16 bytes, and the head's sum of squares reduces over the group
+// with three shuffles.  Grid-stride over (token, head) items.
 template <int D>
-__global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ qw,
-                                        const __nv_bfloat16* __restrict__ kw, const int* __restrict__ pos,
-                                        const float* __restrict__ cos_t, const float* __restrict__ sin_t,
-                                        __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_out,
-                                        __nv_bfloat16* __restrict__ v_out, float* __restrict__ rstd_out, int T, int nq,
-                                        int nkv, float eps) {
+__global__ void __launch_bounds__(256)
+    qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ qw,
+                            const __nv_bfloat16* __restrict__ kw, const int* __restrict__ pos,
+                            const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                            __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_out,
+                            __nv_bfloat16* __restrict__ v_out, float* __restrict__ rstd_out, int T, int nq, int nkv,
+                            float eps) {
   static_assert(D == 128, "head_dim 128");
   const int heads = nq + nkv;
-  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, grp = lane >> 3, j = lane & 7;
+  const unsigned gmask = 0xFFu << (grp * 8);
   const int stride_row = (nq + 2 * nkv) * D;
-  if (gw < T * heads) {
-    const int t = gw / heads, h = gw - t * heads;
+  const int64_t total = (int64_t)T * heads;
+  const int64_t step = (int64_t)gridDim.x * (blockDim.x >> 5) * 4;
+  for (int64_t item = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 4 + grp; item < total;
+       item += step) {
+    const int t = (int)(item / heads), h = (int)(item - (int64_t)t * heads);
     const bool is_q = h < nq;
     const __nv_bfloat16* src = qkv + (size_t)t * stride_row + (size_t)h * D;
+    const int i0 = 8 * j, i1 = D / 2 + 8 * j;
+    const uint4 xa = *reinterpret_cast<const uint4*>(src + i0);
+    const uint4 xb = *reinterpret_cast<const uint4*>(src + i1);
     const __nv_bfloat16* wt = is_q ? qw : kw;
-    const int i0 = 2 * lane, i1 = D / 2 + 2 * lane;
-    __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(src + i0);
-    __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(src + i1);
-    float x0 = __low2float(a), x1 = __high2float(a), x2 = __low2float(b), x3 = __high2float(b);
-    float ss = warp_sum(x0 * x0 + x1 * x1 + x2 * x2 + x3 * x3);
-    const float r = rsqrtf(ss / (float)D + eps);
-    if (lane == 0) rstd_out[gw] = r;
-    __nv_bfloat162 wa = *reinterpret_cast<const __nv_bfloat162*>(wt + i0);
-    __nv_bfloat162 wb = *reinterpret_cast<const __nv_bfloat162*>(wt + i1);
-    float y0 = x0 * r * __low2float(wa), y1 = x1 * r * __high2float(wa);
-    float y2 = x2 * r * __low2float(wb), y3 = x3 * r * __high2float(wb);
+    const uint4 wa = *reinterpret_cast<const uint4*>(wt + i0);
+    const uint4 wb = *reinterpret_cast<const uint4*>(wt + i1);
     const int p = pos[t];
-    const float c0 = cos_t[(size_t)p * (D / 2) + i0], c1 = cos_t[(size_t)p * (D / 2) + i0 + 1];
-    const float s0 = sin_t[(size_t)p * (D / 2) + i0], s1 = sin_t[(size_t)p * (D / 2) + i0 + 1];
-    // rotate_half: first half gets -second*sin, second half gets +first*sin
-    float o0 = y0 * c0 - y2 * s0, o1 = y1 * c1 - y3 * s1;
-    float o2 = y2 * c0 + y0 * s0, o3 = y3 * c1 + y1 * s1;
+    const float4* ct = reinterpret_cast<const float4*>(cos_t + (size_t)p * (D / 2) + i0);
+    const float4* st = reinterpret_cast<const float4*>(sin_t + (size_t)p * (D / 2) + i0);
+    const float4 c0 = ct[0], c1 = ct[1], s0 = st[0], s1 = st[1];
+    const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const __nv_bfloat16* xav = reinterpret_cast<const __nv_bfloat16*>(&xa);
+    const __nv_bfloat16* xbv = reinterpret_cast<const __nv_bfloat16*>(&xb);
+    const __nv_bfloat16* wav = reinterpret_cast<const __nv_bfloat16*>(&wa);
+    const __nv_bfloat16* wbv = reinterpret_cast<const __nv_bfloat16*>(&wb);
+    float x1[8], x2[8], ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      x1[e] = __bfloat162float(xav[e]);
+      x2[e] = __bfloat162float(xbv[e]);
+      ss += x1[e] * x1[e] + x2[e] * x2[e];
+    }
+    ss += __shfl_xor_sync(gmask, ss, 4);
+    ss += __shfl_xor_sync(gmask, ss, 2);
+    ss += __shfl_xor_sync(gmask, ss, 1);
+    const float r = rsqrtf(ss / (float)D + eps);
+    if (j == 0) rstd_out[item] = r;
+    float o1[8], o2[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float y1 = x1[e] * r * __bfloat162float(wav[e]), y2 = x2[e] * r * __bfloat162float(wbv[e]);
+      // rotate_half: first half gets -second*sin, second half gets +first*sin
+      o1[e] = y1 * c[e] - y2 * sn[e];
+      o2[e] = y2 * c[e] + y1 * sn[e];
+    }
+    uint4 pa, pb;
+    pa.x = pack_bf16x2(o1[0], o1[1]); pa.y = pack_bf16x2(o1[2], o1[3]);
+    pa.z = pack_bf16x2(o1[4], o1[5]); pa.w = pack_bf16x2(o1[6], o1[7]);
+    pb.x = pack_bf16x2(o2[0], o2[1]); pb.y = pack_bf16x2(o2[2], o2[3]);
+    pb.z = pack_bf16x2(o2[4], o2[5]); pb.w = pack_bf16x2(o2[6], o2[7]);
     __nv_bfloat16* dst = is_q ? q_out + ((size_t)t * nq + h) * D : k_out + ((size_t)t * nkv + (h - nq)) * D;
-    *reinterpret_cast<__nv_bfloat162*>(dst + i0) = __floats2bfloat162_rn(o0, o1);
-    *reinterpret_cast<__nv_bfloat162*>(dst + i1) = __floats2bfloat162_rn(o2, o3);
+    *reinterpret_cast<uint4*>(dst + i0) = pa;
+    *reinterpret_cast<uint4*>(dst + i1) = pb;
     if (!is_q) {
       const __nv_bfloat16* vs = qkv + (size_t)t * stride_row + (size_t)(nq + nkv + (h - nq)) * D;
       __nv_bfloat16* vd = v_out + ((size_t)t * nkv + (h - nq)) * D;
-      *reinterpret_cast<__nv_bfloat162*>(vd + i0) = *reinterpret_cast<const __nv_bfloat162*>(vs + i0);
-      *reinterpret_cast<__nv_bfloat162*>(vd + i1) = *reinterpret_cast<const __nv_bfloat162*>(vs + i1);
+      *reinterpret_cast<uint4*>(vd + i0) = *reinterpret_cast<const uint4*>(vs + i0);
+      *reinterpret_cast<uint4*>(vd + i1) = *reinterpret_cast<const uint4*>(vs + i1);
     }
   }
 }
 
-// Backward: grid-stride warps over (token, head); q/k weight-gradient partials
-// live in registers per lane (4 values for q, 4 for k) and are folded per CTA.
+// Backward, same lane layout: per-lane q/k weight-gradient partials (16 each,
+// for the lane's fixed elements) folded per CTA into a [gridDim.x, 2D] buffer.
 template <int D>
-__global__ void qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ qw,
-                                        const __nv_bfloat16* __restrict__ kw, const int* __restrict__ pos,
-                                        const float* __restrict__ cos_t, const float* __restrict__ sin_t,
-                                        const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ dq,
-                                        const __nv_bfloat16* __restrict__ dk, const __nv_bfloat16* __restrict__ dv,
-                                        __nv_bfloat16* __restrict__ dqkv, float* __restrict__ dw_part, int T, int nq,
-                                        int nkv) {
+__global__ void __launch_bounds__(256)
+    qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ qw,
+                            const __nv_bfloat16* __restrict__ kw, const int* __restrict__ pos,
+                            const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                            const float* __restrict__ rstd, const __nv_bfloat16* __restrict__ dq,
+                            const __nv_bfloat16* __restrict__ dk, const __nv_bfloat16* __restrict__ dv,
+                            __nv_bfloat16* __restrict__ dqkv, float* __restrict__ dw_part, int T, int nq, int nkv) {
   const int heads = nq + nkv;
-  const int warps_total = gridDim.x * (blockDim.x >> 5);
-  const int gw0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, grp = lane >> 3, j = lane & 7;
+  const unsigned gmask = 0xFFu << (grp * 8);
   const int stride_row = (nq + 2 * nkv) * D;
-  const int i0 = 2 * lane, i1 = D / 2 + 2 * lane;
-  float accq[4] = {0, 0, 0, 0}, acck[4] = {0, 0, 0, 0};
-  const float wq0 = __bfloat162float(qw[i0]), wq1 = __bfloat162float(qw[i0 + 1]);
-  const float wq2 = __bfloat162float(qw[i1]), wq3 = __bfloat162float(qw[i1 + 1]);
-  const float wk0 = __bfloat162float(kw[i0]), wk1 = __bfloat162float(kw[i0 + 1]);
-  const float wk2 = __bfloat162float(kw[i1]), wk3 = __bfloat162float(kw[i1 + 1]);
-  for (int gw = gw0; gw < T * heads; gw += warps_total) {
-    const int t = gw / heads, h = gw - t * heads;
+  const int i0 = 8 * j, i1 = D / 2 + 8 * j;
+  __shared__ float s_w[2 * D];  // [q weights | k weights] in fp32
+  for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) s_w[i] = __bfloat162float(i < D ? qw[i] : kw[i - D]);
+  __syncthreads();
+  float aq1[8] = {}, aq2[8] = {}, ak1[8] = {}, ak2[8] = {};
+  const int64_t total = (int64_t)T * heads;
+  const int64_t step = (int64_t)gridDim.x * (blockDim.x >> 5) * 4;
+  for (int64_t item = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 4 + grp; item < total;
+       item += step) {
+    const int t = (int)(item / heads), h = (int)(item - (int64_t)t * heads);
     const bool is_q = h < nq;
     const __nv_bfloat16* g = is_q ? dq + ((size_t)t * nq + h) * D : dk + ((size_t)t * nkv + (h - nq)) * D;
-    __nv_bfloat162 ga = *reinterpret_cast<const __nv_bfloat162*>(g + i0);
-    __nv_bfloat162 gb = *reinterpret_cast<const __nv_bfloat162*>(g + i1);
-    const float g0 = __low2float(ga), g1 = __high2float(ga), g2 = __low2float(gb), g3 = __high2float(gb);
-    const int p = pos[t];
-    const float c0 = cos_t[(size_t)p * (D / 2) + i0], c1 = cos_t[(size_t)p * (D / 2) + i0 + 1];
-    const float s0 = sin_t[(size_t)p * (D / 2) + i0], s1 = sin_t[(size_t)p * (D / 2) + i0 + 1];
-    // transpose of the rotation
-    const float dy0 = g0 * c0 + g2 * s0, dy1 = g1 * c1 + g3 * s1;
-    const float dy2 = g2 * c0 - g0 * s0, dy3 = g3 * c1 - g1 * s1;
+    const uint4 ga = *reinterpret_cast<const uint4*>(g + i0);
+    const uint4 gb = *reinterpret_cast<const uint4*>(g + i1);
     const __nv_bfloat16* src = qkv + (size_t)t * stride_row + (size_t)h * D;
-    __nv_bfloat162 xa = *reinterpret_cast<const __nv_bfloat162*>(src + i0);
-    __nv_bfloat162 xb = *reinterpret_cast<const __nv_bfloat162*>(src + i1);
-    const float r = rstd[gw];
-    const float xh0 = __low2float(xa) * r, xh1 = __high2float(xa) * r, xh2 = __low2float(xb) * r,
-                xh3 = __high2float(xb) * r;
-    const float w0 = is_q ? wq0 : wk0, w1 = is_q ? wq1 : wk1, w2 = is_q ? wq2 : wk2, w3 = is_q ? wq3 : wk3;
-    const float dot = warp_sum(dy0 * w0 * xh0 + dy1 * w1 * xh1 + dy2 * w2 * xh2 + dy3 * w3 * xh3) / (float)D;
-    const float dx0 = r * (dy0 * w0 - xh0 * dot), dx1 = r * (dy1 * w1 - xh1 * dot);
-    const float dx2 = r * (dy2 * w2 - xh2 * dot), dx3 = r * (dy3 * w3 - xh3 * dot);
-    if (is_q) {
-      accq[0] += dy0 * xh0; accq[1] += dy1 * xh1; accq[2] += dy2 * xh2; accq[3] += dy3 * xh3;
-    } else {
-      acck[0] += dy0 * xh0; acck[1] += dy1 * xh1; acck[2] += dy2 * xh2; acck[3] += dy3 * xh3;
+    const uint4 xa = *reinterpret_cast<const uint4*>(src + i0);
+    const uint4 xb = *reinterpret_cast<const uint4*>(src + i1);
+    const int p = pos[t];
+    const float4* ct = reinterpret_cast<const float4*>(cos_t + (size_t)p * (D / 2) + i0);
+    const float4* st = reinterpret_cast<const float4*>(sin_t + (size_t)p * (D / 2) + i0);
+    const float4 c0 = ct[0], c1 = ct[1], s0 = st[0], s1 = st[1];
+    const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const float r = rstd[item];
+    const __nv_bfloat16* gav = reinterpret_cast<const __nv_bfloat16*>(&ga);
+    const __nv_bfloat16* gbv = reinterpret_cast<const __nv_bfloat16*>(&gb);
+    const __nv_bfloat16* xav = reinterpret_cast<const __nv_bfloat16*>(&xa);
+    const __nv_bfloat16* xbv = reinterpret_cast<const __nv_bfloat16*>(&xb);
+    const float* w = s_w + (is_q ? 0 : D);
+    float dy1[8], dy2[8], xh1[8], xh2[8], dot = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float g1 = __bfloat162float(gav[e]), g2 = __bfloat162float(gbv[e]);
+      // transpose of the rotation
+      dy1[e] = g1 * c[e] + g2 * sn[e];
+      dy2[e] = g2 * c[e] - g1 * sn[e];
+      xh1[e] = __bfloat162float(xav[e]) * r;
+      xh2[e] = __bfloat162float(xbv[e]) * r;
+      dot += dy1[e] * w[i0 + e] * xh1[e] + dy2[e] * w[i1 + e] * xh2[e];
     }
+    dot += __shfl_xor_sync(gmask, dot, 4);
+    dot += __shfl_xor_sync(gmask, dot, 2);
+    dot += __shfl_xor_sync(gmask, dot, 1);
+    dot /= (float)D;
+    float dx1[8], dx2[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      dx1[e] = r * (dy1[e] * w[i0 + e] - xh1[e] * dot);
+      dx2[e] = r * (dy2[e] * w[i1 + e] - xh2[e] * dot);
+      if (is_q) {
+        aq1[e] += dy1[e] * xh1[e];
+        aq2[e] += dy2[e] * xh2[e];
+      } else {
+        ak1[e] += dy1[e] * xh1[e];
+        ak2[e] += dy2[e] * xh2[e];
+      }
+    }
+    uint4 pa, pb;
+    pa.x = pack_bf16x2(dx1[0], dx1[1]); pa.y = pack_bf16x2(dx1[2], dx1[3]);
+    pa.z = pack_bf16x2(dx1[4], dx1[5]); pa.w = pack_bf16x2(dx1[6], dx1[7]);
+    pb.x = pack_bf16x2(dx2[0], dx2[1]); pb.y = pack_bf16x2(dx2[2], dx2[3]);
+    pb.z = pack_bf16x2(dx2[4], dx2[5]); pb.w = pack_bf16x2(dx2[6], dx2[7]);
     __nv_bfloat16* dst = dqkv + (size_t)t * stride_row + (size_t)h * D;
-    *reinterpret_cast<__nv_bfloat162*>(dst + i0) = __floats2bfloat162_rn(dx0, dx1);
-    *reinterpret_cast<__nv_bfloat162*>(dst + i1) = __floats2bfloat162_rn(dx2, dx3);
+    *reinterpret_cast<uint4*>(dst + i0) = pa;
+    *reinterpret_cast<uint4*>(dst + i1) = pb;
     if (!is_q) {
       const __nv_bfloat16* vg = dv + ((size_t)t * nkv + (h - nq)) * D;
       __nv_bfloat16* vd = dqkv + (size_t)t * stride_row + (size_t)(nq + nkv + (h - nq)) * D;
-      *reinterpret_cast<__nv_bfloat162*>(vd + i0) = *reinterpret_cast<const __nv_bfloat162*>(vg + i0);
-      *reinterpret_cast<__nv_bfloat162*>(vd + i1) = *reinterpret_cast<const __nv_bfloat162*>(vg + i1);
+      *reinterpret_cast<uint4*>(vd + i0) = *reinterpret_cast<const uint4*>(vg + i0);
+      *reinterpret_cast<uint4*>(vd + i1) = *reinterpret_cast<const uint4*>(vg + i1);
     }
   }
-  // fold the warps' partials in shared memory, then write this CTA's row of
+  // fold the lanes' partials in shared memory, then write this CTA's row of
   // the [gridDim.x, 2D] partial buffer: [q weights (D) | k weights (D)]
   __shared__ float s_acc[2 * D];
   for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) s_acc[i] = 0.f;
   __syncthreads();
-  atomicAdd(&s_acc[i0], accq[0]); atomicAdd(&s_acc[i0 + 1], accq[1]);
-  atomicAdd(&s_acc[i1], accq[2]); atomicAdd(&s_acc[i1 + 1], accq[3]);
-  atomicAdd(&s_acc[D + i0], acck[0]); atomicAdd(&s_acc[D + i0 + 1], acck[1]);
-  atomicAdd(&s_acc[D + i1], acck[2]); atomicAdd(&s_acc[D + i1 + 1], acck[3]);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    atomicAdd(&s_acc[i0 + e], aq1[e]);
+    atomicAdd(&s_acc[i1 + e], aq2[e]);
+    atomicAdd(&s_acc[D + i0 + e], ak1[e]);
+    atomicAdd(&s_acc[D + i1 + e], ak2[e]);
+  }
   __syncthreads();
   float* part = dw_part + (size_t)blockIdx.x * 2 * D;
   for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) part[i] = s_acc[i];
 }
 
 // ------------------------------------------------------------------ host wrappers
+static int sm_count_nr() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
 static void check_bf16_rowmajor(const torch::Tensor& t, const char* name) {
   LIBRA_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous(),
               "%s: contiguous CUDA bf16 tensor required", name);
@@ -398,8 +467,15 @@ std::vector<torch::Tensor> qk_norm_rope_fwd(torch::Tensor qkv, torch::Tensor qw,
   auto rstd = torch::empty({T * (nq + nkv)}, qkv.options().dtype(at::kFloat));
   const int total = T * (int)(nq + nkv);
   if (total == 0) return {q, k, v, rstd};
-  const int warps = 8;
-  qk_norm_rope_fwd_kernel<128><<<(total + warps - 1) / warps, warps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+  LIBRA_CHECK(pos.is_contiguous() && cos_t.is_contiguous() && sin_t.is_contiguous() && qw.is_contiguous() &&
+                  kw.is_contiguous() && (reinterpret_cast<uintptr_t>(cos_t.data_ptr()) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(sin_t.data_ptr()) & 15) == 0,
+              "qk_norm_rope: contiguous, 16-byte aligned weights and tables");
+  const int warps = 8;  // 32 (token, head) items per CTA
+  int blocks = (total + warps * 4 - 1) / (warps * 4);
+  const int cap = sm_count_nr() * 16;
+  if (blocks > cap) blocks = cap;
+  qk_norm_rope_fwd_kernel<128><<<blocks, warps * 32, 0, at::cuda::getCurrentCUDAStream()>>>(
       (const __nv_bfloat16*)qkv.data_ptr(), (const __nv_bfloat16*)qw.data_ptr(), (const __nv_bfloat16*)kw.data_ptr(),
       pos.data_ptr<int>(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), (__nv_bfloat16*)q.data_ptr(),
       (__nv_bfloat16*)k.data_ptr(), (__nv_bfloat16*)v.data_ptr(), rstd.data_ptr<float>(), T, (int)nq, (int)nkv,
@@ -424,7 +500,7 @@ torch::Tensor qk_norm_rope_bwd(torch::Tensor qkv, torch::Tensor qw, torch::Tenso
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int total = T * (int)(nq + nkv);
   int blocks = sms * 8;
-  if (blocks * warps > total) blocks = (total + warps - 1) / warps;
+  if (blocks * warps * 4 > total) blocks = (total + warps * 4 - 1) / (warps * 4);
   if (blocks < 1) blocks = 1;
   auto part = torch::empty({blocks, 2 * D}, qkv.options().dtype(at::kFloat));
   auto st = at::cuda::getCurrentCUDAStream();

@@ -103,6 +103,9 @@ def bench_elementwise(iters: int):
     from libra_b200.ops import reference as _ref
     cos, sin = [t.float().cuda().contiguous() for t in _ref.rope_tables(4096, D, 1e6)]
     q, k, v, r = ops.ext().qk_norm_rope_fwd(qkv, qw, qw, pos, cos, sin, nq, nkv, 1e-6)
+    ms = _time(lambda: ops.ext().qk_norm_rope_fwd(qkv, qw, qw, pos, cos, sin, nq, nkv, 1e-6), iters)
+    print(json.dumps({"kernel": "qk_norm_rope_fwd", "T": T2, "ms": ms,
+                      "gbs": 2 * 2 * T2 * (nq + 2 * nkv) * D / ms / 1e6}), flush=True)
     dqw, dkw = torch.zeros(D, device="cuda"), torch.zeros(D, device="cuda")
     ms = _time(lambda: ops.ext().qk_norm_rope_bwd(qkv, qw, qw, pos, cos, sin, r, q, k, v, dqw, dkw, nq, nkv), iters)
     print(json.dumps({"kernel": "qk_norm_rope_bwd", "T": T2, "ms": ms,

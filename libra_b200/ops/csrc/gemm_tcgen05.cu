@@ -373,11 +373,14 @@ constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarBytes;
 // Tensor-parallel all-reduce fused into the GEMM (kPeerAR): every rank of the
 // group computes its partial Y_r = A_r B_r^T; the output is sum_r Y_r (plus an
 // optional residual) on every rank.  Over NVLink peer memory, in one launch:
-//   A  GEMM tiles; the epilogue stores each 256-row block's bf16 partial
-//      straight into the receive area of the block's owner (rank mb % n), slot
-//      [me], and bumps the owner's arrival counter for the block (release).
+//   A  GEMM tiles; the epilogue stores each 256-row block's bf16 partial in
+//      this rank's own partial buffer and bumps the arrival counter of the
+//      block's owner (rank mb % n) on that rank (release).  (Pushing the tile
+//      rows to the owner instead means one 16-byte NVLink store per row and
+//      lane, measured several times slower than the owner pulling whole rows.)
 //   B  each CTA takes (owned row block, 256-column chunk) units: waits until
-//      all n * num_n * 8 epilogue warps have arrived, sums the n partials in
+//      all n * num_n * 8 epilogue warps have arrived, reads the n partials
+//      (peers' over NVLink, 512 contiguous bytes per warp load), sums them in
 //      fp32 and writes the bf16 sum into every rank's gathered buffer, then
 //      bumps every rank's "done" counter for the block (reduce-scatter +
 //      all-gather, each byte crossing NVLink once per direction).
@@ -391,14 +394,14 @@ constexpr int kMaxPeers = 8;
 // With rs_rows > 0 the same kernel is a GEMM + reduce-scatter (sequence
 // parallel): rank q owns rows [q rs_rows, (q+1) rs_rows) (rs_rows a multiple of
 // 256), phase B writes the owned sum (+ residual shard) straight into y
-// ([rs_rows, N]) and there is no all-gather and no phase C.
+// ([rs_rows, N]) and there is no all-gather; phase C only waits until every
+// owner is done reading this rank's partial.
 struct PeerAR {
-  uint64_t recv[kMaxPeers];   // rank q's receive area: [n][max_rows, N] bf16
+  uint64_t recv[kMaxPeers];   // rank q's partial [max_rows, N] bf16
   uint64_t gath[kMaxPeers];   // rank q's gathered sum: [max_rows, N] bf16
   uint64_t flags[kMaxPeers];  // rank q's counters: int32 [2 parity][2 kind][max_rb]
   __nv_bfloat16* y;           // this rank's output: [M, N], or [rs_rows, N]
   const __nv_bfloat16* residual;  // optional, shaped like y
-  int64_t slot_elems;         // max_rows * N
   int n, me, parity, max_rb, rs_rows;
 };
 
@@ -639,9 +642,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       const int row = mb * 2 * BM + (int)rank * BM + row_in_tile;
-      if constexpr (kPeerAR) {
-        const int owner = peer_owner(par, mb);
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(par.recv[owner]) + (int64_t)par.me * par.slot_elems;
+      if constexpr (kPeerAR) {  // the partial stays here; its owner pulls it
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(par.recv[par.me]);
         store_tile_row<BN, EPI>(tacc, row, nb, M, N, dst, nullptr, N, 0, nullptr, 0);
       } else {
         store_tile_row<BN, EPI>(tacc, row, nb, M, N, C, R, ldc, ldr, C2, ldc2, splits > 1);
@@ -650,7 +652,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * acc);
       if constexpr (kPeerAR) {
-        __threadfence_system();  // this lane's partial rows reach the owner before the count
+        __threadfence_system();  // this lane's partial rows are visible to the owner before the count
         __syncwarp();
         if (lane == 0)
           red_add_release_sys(reinterpret_cast<int*>(par.flags[peer_owner(par, mb)]) + par.parity * 2 * par.max_rb + mb,
@@ -677,15 +679,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (threadIdx.x == 0) s_ok = wait_flag_geq(my_flags + mb, arrivals, err, kTimeoutPeerFlag);
       __syncthreads();
       if (!s_ok) break;
-      const __nv_bfloat16* mine = reinterpret_cast<const __nv_bfloat16*>(par.recv[me]);
       const int r0 = mb * 2 * BM, c0 = ch * BN;
       for (int v = threadIdx.x; v < 2 * BM * (BN / 8); v += blockDim.x) {
         const int row = r0 + v / (BN / 8), col = c0 + (v % (BN / 8)) * 8;
         if (row >= M || col >= N) continue;
         const int64_t off = (int64_t)row * N + col;
         float acc8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int q = 0; q < n; ++q) {
-          const uint4 u = *reinterpret_cast<const uint4*>(mine + q * par.slot_elems + off);
+        for (int q = 0; q < n; ++q) {  // rank q's partial, over NVLink for q != me (coalesced rows)
+          const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(par.recv[q]) + off);
           const __nv_bfloat16* ub = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll
           for (int e = 0; e < 8; ++e) acc8[e] += __bfloat162float(ub[e]);
@@ -713,19 +714,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         o.w = pack_bf16x2(acc8[6], acc8[7]);
         for (int q = 0; q < n; ++q) *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(par.gath[q]) + off) = o;
       }
-      if (rs) continue;
       __threadfence_system();
       __syncthreads();
       if (threadIdx.x < n)
         red_add_release_sys(reinterpret_cast<int*>(par.flags[threadIdx.x]) + par.parity * 2 * par.max_rb +
                                 par.max_rb + mb, 1);
     }
-    // ---- C: gathered row blocks (+ residual) into the output
-    for (int mb = blockIdx.x; !rs && mb < num_m; mb += gridDim.x) {
+    // ---- C: gathered row blocks (+ residual) into the output.  With the
+    // reduce-scatter the wait alone remains: no rank may overwrite its partial
+    // in the next call before every owner has read it.
+    for (int mb = blockIdx.x; mb < num_m; mb += gridDim.x) {
       __syncthreads();
       if (threadIdx.x == 0) s_ok = wait_flag_geq(my_flags + par.max_rb + mb, chunks, err, kTimeoutPeerFlag);
       __syncthreads();
       if (!s_ok) break;
+      if (rs) continue;
       const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(par.gath[me]);
       const int r0 = mb * 2 * BM, nv = N / 8;
       for (int v = threadIdx.x; v < 2 * BM * nv; v += blockDim.x) {
@@ -1030,7 +1033,6 @@ void gemm_allreduce(torch::Tensor a, torch::Tensor b, bool b_mn, c10::optional<t
   }
   par.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
   par.residual = rp;
-  par.slot_elems = max_rows * N;
   par.n = n;
   par.me = (int)me;
   par.parity = (int)(parity & 1);

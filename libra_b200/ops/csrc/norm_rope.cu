@@ -140,6 +140,91 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const _
   }
 }
 
+// Same contract as rmsnorm_bwd_kernel for rows of up to 32 * 8 * kVPL
+// elements: the lane's kVPL vectors of x and dy (and of the dx being
+// accumulated into) are loaded once, all in flight together, and both passes
+// run from registers.
+template <int kVPL>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_reg_kernel(
+    const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+    const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx, float* __restrict__ dw_part, int T, int H,
+    int accumulate_dx) {
+  extern __shared__ float s_dw[];  // [warps, H]
+  const int warps = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nvec = H >> 3;
+  for (int i = threadIdx.x; i < warps * H; i += blockDim.x) s_dw[i] = 0.f;
+  __syncthreads();
+  float* my = s_dw + (size_t)warp * H;
+  const uint4* wv = reinterpret_cast<const uint4*>(w);
+  for (int row = blockIdx.x * warps + warp; row < T; row += gridDim.x * warps) {
+    const float r = rstd[row];
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * H);
+    const uint4* gr = reinterpret_cast<const uint4*>(dy + (size_t)row * H);
+    uint4* dxr = reinterpret_cast<uint4*>(dx + (size_t)row * H);
+    uint4 xu[kVPL], gu[kVPL], pu[kVPL];
+#pragma unroll
+    for (int i = 0; i < kVPL; ++i) {
+      const int v = lane + 32 * i;
+      if (v < nvec) {
+        xu[i] = xr[v];
+        gu[i] = gr[v];
+        if (accumulate_dx) pu[i] = dxr[v];
+      }
+    }
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kVPL; ++i) {
+      const int v = lane + 32 * i;
+      if (v >= nvec) break;
+      const uint4 wu = __ldg(wv + v);
+      const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xu[i]);
+      const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&gu[i]);
+      const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wu);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) dot += __bfloat162float(gb[e]) * __bfloat162float(wb[e]) * __bfloat162float(xb[e]);
+    }
+    const float mean = warp_sum(dot) * r / (float)H;
+#pragma unroll
+    for (int i = 0; i < kVPL; ++i) {
+      const int v = lane + 32 * i;
+      if (v >= nvec) break;
+      const uint4 wu = __ldg(wv + v);
+      const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&xu[i]);
+      const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&gu[i]);
+      const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wu);
+      const __nv_bfloat16* pb = reinterpret_cast<const __nv_bfloat16*>(&pu[i]);
+      float o[8];
+      float4* acc = reinterpret_cast<float4*>(my + v * 8);
+      float4 a0 = acc[0], a1 = acc[1];
+      float* af0 = reinterpret_cast<float*>(&a0);
+      float* af1 = reinterpret_cast<float*>(&a1);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float xh = __bfloat162float(xb[e]) * r;
+        const float g = __bfloat162float(gb[e]);
+        o[e] = r * (g * __bfloat162float(wb[e]) - xh * mean);
+        if (accumulate_dx) o[e] += __bfloat162float(pb[e]);
+        if (e < 4) af0[e] += g * xh; else af1[e - 4] += g * xh;
+      }
+      acc[0] = a0;
+      acc[1] = a1;
+      uint4 pk;
+      pk.x = pack_bf16x2(o[0], o[1]);
+      pk.y = pack_bf16x2(o[2], o[3]);
+      pk.z = pack_bf16x2(o[4], o[5]);
+      pk.w = pack_bf16x2(o[6], o[7]);
+      dxr[v] = pk;
+    }
+  }
+  __syncthreads();
+  float* part = dw_part + (size_t)blockIdx.x * H;
+  for (int c = threadIdx.x; c < H; c += blockDim.x) {
+    float sum = 0.f;
+    for (int k = 0; k < warps; ++k) sum += s_dw[(size_t)k * H + c];
+    part[c] = sum;
+  }
+}
+
 // out[c] (+)= sum_r part[r, c].  Block (32 columns x 8 row groups); each
 // thread keeps four independent partial sums, then the 8 groups are folded
 // through shared memory.
@@ -400,13 +485,28 @@ static int rmsnorm_bwd_warps(int H) {
 
 // CTAs for rmsnorm_bwd: all co-resident CTAs of one wave, but no more than the
 // rows need.
-static int rmsnorm_bwd_grid(int T, int H, int warps) {
+using RmsnormBwdKernel = void (*)(const __nv_bfloat16*, const __nv_bfloat16*, const __nv_bfloat16*, const float*,
+                                  __nv_bfloat16*, float*, int, int, int);
+
+// The register-resident kernel for rows of up to 4096 elements, else the
+// two-pass one.
+static RmsnormBwdKernel rmsnorm_bwd_pick(int H) {
+  const int vpl = (H / 8 + 31) / 32;
+  if (vpl <= 4) return rmsnorm_bwd_reg_kernel<4>;
+  if (vpl <= 8) return rmsnorm_bwd_reg_kernel<8>;
+  if (vpl <= 10) return rmsnorm_bwd_reg_kernel<10>;  // H = 2560
+  if (vpl <= 12) return rmsnorm_bwd_reg_kernel<12>;
+  if (vpl <= 16) return rmsnorm_bwd_reg_kernel<16>;
+  return rmsnorm_bwd_kernel;
+}
+
+static int rmsnorm_bwd_grid(int T, int H, int warps, RmsnormBwdKernel kern) {
   int dev, sms, per_sm = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const size_t smem = (size_t)warps * H * 4;
-  cudaFuncSetAttribute(rmsnorm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rmsnorm_bwd_kernel, warps * 32, smem);
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, warps * 32, smem);
   if (per_sm < 1) per_sm = 1;
   const int need = (T + warps - 1) / warps;
   int g = sms * per_sm;
@@ -441,9 +541,10 @@ torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, to
     return dx;
   }
   const int warps = rmsnorm_bwd_warps(H);
-  const int grid = rmsnorm_bwd_grid(T, H, warps);
+  const RmsnormBwdKernel kern = rmsnorm_bwd_pick(H);
+  const int grid = rmsnorm_bwd_grid(T, H, warps, kern);
   auto part = torch::empty({grid, H}, x.options().dtype(at::kFloat));
-  rmsnorm_bwd_kernel<<<grid, warps * 32, (size_t)warps * H * 4, st>>>(
+  kern<<<grid, warps * 32, (size_t)warps * H * 4, st>>>(
       (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(),
       rstd.data_ptr<float>(), (__nv_bfloat16*)dx.data_ptr(), part.data_ptr<float>(), T, H, acc_dx);
   LIBRA_LAUNCH_CHECK();
@@ -585,10 +686,11 @@ extern "C" __attribute__((visibility("default"))) int libra_rmsnorm_bwd_noalloc(
     colsum_kernel<<<(H + 31) / 32, dim3(32, kColsumRowGroups), 0, stream>>>(scratch, 0, H, dw, accumulate_dw ? 1 : 0);
   } else {
     const int warps = rmsnorm_bwd_warps(H);
-    int grid = rmsnorm_bwd_grid(T, H, warps);
+    const RmsnormBwdKernel kern = rmsnorm_bwd_pick(H);
+    int grid = rmsnorm_bwd_grid(T, H, warps, kern);
     const int cap = (int)(kNoAllocScratchFloats / (size_t)H);
     if (grid > cap) grid = cap;
-    rmsnorm_bwd_kernel<<<grid, warps * 32, (size_t)warps * H * 4, stream>>>(
+    kern<<<grid, warps * 32, (size_t)warps * H * 4, stream>>>(
         (const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, (const __nv_bfloat16*)w, rstd, (__nv_bfloat16*)dx, scratch,
         T, H, accumulate_dx ? 1 : 0);
     colsum_kernel<<<(H + 31) / 32, dim3(32, kColsumRowGroups), 0, stream>>>(scratch, grid, H, dw, accumulate_dw ? 1 : 0);

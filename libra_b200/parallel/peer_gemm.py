@@ -6,14 +6,14 @@ rank and all-reduces it; the reference reaches this through Megatron-Core's
 ``RowParallelLinear`` (NCCL all-reduce after cuBLAS, engine/megatron_core_
 train_engine.py:887-903).  Here one kernel (``gemm_allreduce`` in
 ``ops/csrc/gemm_tcgen05.cu``) does both: the CTA-pair GEMM's epilogue stores
-each 256-row block of the partial into the receive area of the rank that owns
-that block, the owner sums the partials in fp32 and writes the sum to every
-rank, and each rank copies the finished blocks (plus the residual) into its
-output.  Each byte crosses NVLink once per direction, as in a reduce-scatter +
+each 256-row block of the partial locally and signals the rank that owns the
+block, the owner pulls the partials over NVLink, sums them in fp32 and writes
+the sum to every rank, and each rank copies the finished blocks (plus the
+residual) into its output.  Each byte crosses NVLink once per direction, as in a reduce-scatter +
 all-gather, and the transfers overlap the GEMM tiles still running.
 
-``PeerGemmAllReduce`` owns one symmetric buffer per (group, N): receive area
-``[n][max_rows, N]``, gathered sum ``[max_rows, N]`` and the arrival counters,
+``PeerGemmAllReduce`` owns one symmetric buffer per (group, N): partial
+``[max_rows, N]``, gathered sum ``[max_rows, N]`` and the arrival counters,
 shared through CUDA IPC handles and opened in this device's context.  Calls
 must be made in the same order on every rank of the group.
 """
@@ -42,7 +42,7 @@ class PeerGemmAllReduce:
             raise ValueError("N must be a multiple of 8")
         self.max_rows, self.n_cols = int(max_rows), int(n_cols)
         slot = self.max_rows * self.n_cols * 2
-        self.recv_bytes = (self.n * slot + 255) // 256 * 256
+        self.recv_bytes = (slot + 255) // 256 * 256
         self.gath_bytes = (slot + 255) // 256 * 256
         max_rb = (self.max_rows + ROW_BLOCK - 1) // ROW_BLOCK
         flag_bytes = (4 * max_rb * 4 + 255) // 256 * 256

@@ -97,6 +97,27 @@ def test_rmsnorm_fwd_bwd():
     assert _rel(w.grad, wf.grad) < 1e-2
 
 
+@pytest.mark.parametrize("H", [1024, 2048, 2560, 4096, 6144])
+def test_rmsnorm_bwd_widths_and_accumulate(H):
+    """Every row-width variant of the backward (register-resident up to 4096,
+    two-pass beyond), with dx accumulated into an existing gradient."""
+    from libra_b200 import ops
+
+    T = 777
+    x, dy = _bf16(T, H, seed=21), _bf16(T, H, seed=22)
+    w = (1 + 0.1 * torch.randn(H, device=DEV)).to(torch.bfloat16)
+    prev = _bf16(T, H, seed=23)
+    rstd = torch.rsqrt(x.float().pow(2).mean(-1) + 1e-6).contiguous()
+    dw = torch.zeros(H, device=DEV)
+    dx = prev.clone()
+    ops.ext().rmsnorm_bwd(dy, x, w, rstd, dw, False, dx)
+    torch.cuda.synchronize()
+    xf, wf = x.float().requires_grad_(True), w.float().requires_grad_(True)
+    (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * wf).backward(dy.float())
+    assert _rel(dx, xf.grad + prev.float()) < 1e-2
+    assert _rel(dw, wf.grad) < 1e-2
+
+
 def test_qk_norm_rope_fwd_bwd():
     from libra_b200 import ops
     from libra_b200.ops import reference as ref

@@ -619,12 +619,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                    kTimeoutPeerFlag);
         ready_ok = __shfl_sync(0xffffffffu, ready_ok, 0);
       }
-      for (int64_t f = gw * 32 + lane; ready_ok && f < total; f += nw * 32) {
-        const int oi = (int)(f / per_rank);
-        const int o = oi < ag.me ? oi : oi + 1;  // skip this rank
-        const int64_t rem = f - (int64_t)oi * per_rank;
-        const uint4 v = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(ag.shard[o]) + rem * 8);
-        *reinterpret_cast<uint4*>(ag.gath + ((int64_t)o * ag.shard_rows) * K + rem * 8) = v;
+      constexpr int kBatch = 8;  // loads in flight per lane
+      for (int64_t f0 = gw * 32 + lane; ready_ok && f0 < total; f0 += nw * 32 * kBatch) {
+        uint4 v[kBatch];
+        int64_t dst[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          const int64_t f = f0 + (int64_t)u * nw * 32;
+          dst[u] = -1;
+          if (f < total) {
+            const int oi = (int)(f / per_rank);
+            const int o = oi < ag.me ? oi : oi + 1;  // skip this rank
+            const int64_t rem = f - (int64_t)oi * per_rank;
+            v[u] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(ag.shard[o]) + rem * 8);
+            dst[u] = ((int64_t)o * ag.shard_rows) * K + rem * 8;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u)
+          if (dst[u] >= 0) *reinterpret_cast<uint4*>(ag.gath + dst[u]) = v[u];
       }
       fence_proxy_async_global();  // the TMA loads that read these rows go through the async proxy
       __threadfence();
@@ -680,39 +693,63 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       __syncthreads();
       if (!s_ok) break;
       const int r0 = mb * 2 * BM, c0 = ch * BN;
-      for (int v = threadIdx.x; v < 2 * BM * (BN / 8); v += blockDim.x) {
-        const int row = r0 + v / (BN / 8), col = c0 + (v % (BN / 8)) * 8;
-        if (row >= M || col >= N) continue;
-        const int64_t off = (int64_t)row * N + col;
-        float acc8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // kBatch vectors per thread in flight at once: these loops are bound by
+      // load latency, not bandwidth, when each thread has one load outstanding
+      constexpr int kBatch = 4, kVec = BN / 8;
+      for (int v0 = threadIdx.x; v0 < 2 * BM * kVec; v0 += blockDim.x * kBatch) {
+        int64_t off[kBatch];
+        bool in[kBatch];
+        float acc[kBatch][8];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          const int v = v0 + u * blockDim.x;
+          const int row = r0 + v / kVec, col = c0 + (v % kVec) * 8;
+          in[u] = v < 2 * BM * kVec && row < M && col < N;
+          off[u] = (int64_t)row * N + col;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[u][e] = 0.f;
+        }
         for (int q = 0; q < n; ++q) {  // rank q's partial, over NVLink for q != me (coalesced rows)
-          const uint4 u = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(par.recv[q]) + off);
-          const __nv_bfloat16* ub = reinterpret_cast<const __nv_bfloat16*>(&u);
+          const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(par.recv[q]);
+          uint4 ld[kBatch];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc8[e] += __bfloat162float(ub[e]);
-        }
-        if (rs) {
-          const int64_t loff = (int64_t)(row - me * par.rs_rows) * N + col;
-          if (par.residual != nullptr) {
-            const uint4 rr = *reinterpret_cast<const uint4*>(par.residual + loff);
-            const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rr);
+          for (int u = 0; u < kBatch; ++u)
+            ld[u] = in[u] ? *reinterpret_cast<const uint4*>(src + off[u]) : make_uint4(0, 0, 0, 0);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) acc8[e] += __bfloat162float(rb[e]);
+          for (int u = 0; u < kBatch; ++u) {
+            const __nv_bfloat16* ub = reinterpret_cast<const __nv_bfloat16*>(&ld[u]);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[u][e] += __bfloat162float(ub[e]);
           }
-          uint4 o;
-          o.x = pack_bf16x2(acc8[0], acc8[1]);
-          o.y = pack_bf16x2(acc8[2], acc8[3]);
-          o.z = pack_bf16x2(acc8[4], acc8[5]);
-          o.w = pack_bf16x2(acc8[6], acc8[7]);
-          *reinterpret_cast<uint4*>(par.y + loff) = o;
-          continue;
         }
-        uint4 o;
-        o.x = pack_bf16x2(acc8[0], acc8[1]);
-        o.y = pack_bf16x2(acc8[2], acc8[3]);
-        o.z = pack_bf16x2(acc8[4], acc8[5]);
-        o.w = pack_bf16x2(acc8[6], acc8[7]);
-        for (int q = 0; q < n; ++q) *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(par.gath[q]) + off) = o;
+        if (rs && par.residual != nullptr) {
+          uint4 rr[kBatch];
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u)
+            rr[u] = in[u] ? *reinterpret_cast<const uint4*>(par.residual + off[u] - (int64_t)me * par.rs_rows * N)
+                          : make_uint4(0, 0, 0, 0);
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u) {
+            const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rr[u]);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[u][e] += __bfloat162float(rb[e]);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          if (!in[u]) continue;
+          uint4 o;
+          o.x = pack_bf16x2(acc[u][0], acc[u][1]);
+          o.y = pack_bf16x2(acc[u][2], acc[u][3]);
+          o.z = pack_bf16x2(acc[u][4], acc[u][5]);
+          o.w = pack_bf16x2(acc[u][6], acc[u][7]);
+          if (rs) {
+            *reinterpret_cast<uint4*>(par.y + off[u] - (int64_t)me * par.rs_rows * N) = o;
+          } else {
+            for (int q = 0; q < n; ++q)
+              *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(par.gath[q]) + off[u]) = o;
+          }
+        }
       }
       __threadfence_system();
       __syncthreads();
@@ -731,24 +768,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (rs) continue;
       const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(par.gath[me]);
       const int r0 = mb * 2 * BM, nv = N / 8;
-      for (int v = threadIdx.x; v < 2 * BM * nv; v += blockDim.x) {
-        const int row = r0 + v / nv, col = (v % nv) * 8;
-        if (row >= M) break;
-        const int64_t off = (int64_t)row * N + col;
-        uint4 o = *reinterpret_cast<const uint4*>(g + off);
-        if (par.residual != nullptr) {
-          const uint4 rr = *reinterpret_cast<const uint4*>(par.residual + off);
-          const __nv_bfloat16* ob = reinterpret_cast<const __nv_bfloat16*>(&o);
-          const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rr);
-          float f[8];
+      constexpr int kBatch = 8;
+      for (int v0 = threadIdx.x; v0 < 2 * BM * nv; v0 += blockDim.x * kBatch) {
+        int64_t off[kBatch];
+        bool in[kBatch];
+        uint4 o[kBatch], rr[kBatch];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] = __bfloat162float(ob[e]) + __bfloat162float(rb[e]);
-          o.x = pack_bf16x2(f[0], f[1]);
-          o.y = pack_bf16x2(f[2], f[3]);
-          o.z = pack_bf16x2(f[4], f[5]);
-          o.w = pack_bf16x2(f[6], f[7]);
+        for (int u = 0; u < kBatch; ++u) {
+          const int v = v0 + u * blockDim.x;
+          const int row = r0 + v / nv, col = (v % nv) * 8;
+          in[u] = v < 2 * BM * nv && row < M;
+          off[u] = (int64_t)row * N + col;
+          o[u] = in[u] ? *reinterpret_cast<const uint4*>(g + off[u]) : make_uint4(0, 0, 0, 0);
+          if (par.residual != nullptr)
+            rr[u] = in[u] ? *reinterpret_cast<const uint4*>(par.residual + off[u]) : make_uint4(0, 0, 0, 0);
         }
-        *reinterpret_cast<uint4*>(par.y + off) = o;
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          if (!in[u]) continue;
+          if (par.residual != nullptr) {
+            const __nv_bfloat16* ob = reinterpret_cast<const __nv_bfloat16*>(&o[u]);
+            const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rr[u]);
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = __bfloat162float(ob[e]) + __bfloat162float(rb[e]);
+            o[u].x = pack_bf16x2(f[0], f[1]);
+            o[u].y = pack_bf16x2(f[2], f[3]);
+            o[u].z = pack_bf16x2(f[4], f[5]);
+            o[u].w = pack_bf16x2(f[6], f[7]);
+          }
+          *reinterpret_cast<uint4*>(par.y + off[u]) = o[u];
+        }
       }
     }
   }

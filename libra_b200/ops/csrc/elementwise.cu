@@ -19,7 +19,7 @@
 
 namespace libra {
 
-__device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + __expf(-x)); }
+__device__ __forceinline__ float sigmoidf_(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
 // ------------------------------------------------------------------ SwiGLU
 // gu: [T, 2F] with gate in [:, :F] and up in [:, F:]; h: [T, F]

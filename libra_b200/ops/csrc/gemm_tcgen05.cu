@@ -37,6 +37,10 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = one 128-byte swizzle row
 constexpr int kThreads = 192;
+// The peer modes of the pair kernel add four warps (6-9) that sleep through
+// the GEMM and join the reduce / copy phases and the all-gather copy, which
+// are bound by the number of loads in flight.
+constexpr int kPeerThreads = 320;
 
 enum Epilogue : int {
   kStoreBf16 = 0,
@@ -52,7 +56,9 @@ enum Epilogue : int {
 // and [128,256) the up projection of the same 128 features.  The epilogue
 // writes a = silu(gate) * up into C ([M, F]) and, when C2 is given, the
 // pre-activation gate/up values into C2 ([M, 2F]) for the backward pass.
-__device__ __forceinline__ float silu_f(float x) { return x * (1.f / (1.f + __expf(-x))); }
+// fast reciprocal-based division (MUFU) instead of the IEEE divide: the
+// result is rounded to bf16 anyway
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 
 template <int BN>
 struct Cfg {
@@ -434,7 +440,7 @@ struct PeerAG {
 // kPeer: 0 plain GEMM, 1 GEMM + all-reduce / reduce-scatter (PeerAR),
 // 2 all-gather + GEMM (PeerAG).
 template <bool A_MN, bool B_MN, int EPI, int kPeer>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPeer ? kPeerThreads : kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      void* __restrict__ C, const __nv_bfloat16* __restrict__ R, int M, int N, int K, int ldc, int ldr,
                      int* err, __nv_bfloat16* __restrict__ C2, int ldc2, int splits, const __grid_constant__ PeerAR par,
@@ -602,15 +608,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
       umma_commit_pair(done, 0x3);
     }
-  } else {
+  } else if (warp < 6) {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t tempty_leader = mapa_shared(smem_u32(tempty), 0);
-    if constexpr (kPeerAG) {  // all-gather of the peers' A shards, 16 bytes per lane and step
+    int local = 0;
+    for (int u = cluster; u < num_units; u += nclusters, ++local) {
+      int tile, kb0, kb1, mb, nb;
+      unit_range(u, tile, kb0, kb1);
+      coords(tile, mb, nb);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, err, kTimeoutTmemFull)) break;
+      tc_fence_after();
+      const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      const int row = mb * 2 * BM + (int)rank * BM + row_in_tile;
+      if constexpr (kPeerAR) {  // the partial stays here; its owner pulls it
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(par.recv[par.me]);
+        store_tile_row<BN, EPI>(tacc, row, nb, M, N, dst, nullptr, N, 0, nullptr, 0);
+      } else {
+        store_tile_row<BN, EPI>(tacc, row, nb, M, N, C, R, ldc, ldr, C2, ldc2, splits > 1);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * acc);
+      if constexpr (kPeerAR) {
+        __threadfence_system();  // this lane's partial rows are visible to the owner before the count
+        __syncwarp();
+        if (lane == 0)
+          red_add_release_sys(reinterpret_cast<int*>(par.flags[peer_owner(par, mb)]) + par.parity * 2 * par.max_rb + mb,
+                              1);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ extra warps of the peer modes
+    if constexpr (kPeerAG) {  // all-gather of the peers' A shards, 16 bytes per lane and step (warps 6-9)
       const int64_t vrow = K / 8, per_rank = (int64_t)ag.shard_rows * vrow;
       const int64_t total = (int64_t)(ag.n - 1) * per_rank;
-      const int64_t gw = (int64_t)blockIdx.x * 4 + (warp - 2), nw = (int64_t)gridDim.x * 4;
+      const int64_t gw = (int64_t)blockIdx.x * 4 + (warp - 6), nw = (int64_t)gridDim.x * 4;
       bool ready_ok = true;
       for (int q = 0; q < ag.n && ready_ok; ++q) {
         if (q == ag.me) continue;
@@ -643,34 +679,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       __threadfence();
       __syncwarp();
       if (lane == 0 && ready_ok) atomicAdd(ag.counter, 1);
-    }
-    int local = 0;
-    for (int u = cluster; u < num_units; u += nclusters, ++local) {
-      int tile, kb0, kb1, mb, nb;
-      unit_range(u, tile, kb0, kb1);
-      coords(tile, mb, nb);
-      const int acc = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], acc_phase, err, kTimeoutTmemFull)) break;
-      tc_fence_after();
-      const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-      const int row = mb * 2 * BM + (int)rank * BM + row_in_tile;
-      if constexpr (kPeerAR) {  // the partial stays here; its owner pulls it
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(par.recv[par.me]);
-        store_tile_row<BN, EPI>(tacc, row, nb, M, N, dst, nullptr, N, 0, nullptr, 0);
-      } else {
-        store_tile_row<BN, EPI>(tacc, row, nb, M, N, C, R, ldc, ldr, C2, ldc2, splits > 1);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * acc);
-      if constexpr (kPeerAR) {
-        __threadfence_system();  // this lane's partial rows are visible to the owner before the count
-        __syncwarp();
-        if (lane == 0)
-          red_add_release_sys(reinterpret_cast<int*>(par.flags[peer_owner(par, mb)]) + par.parity * 2 * par.max_rb + mb,
-                              1);
-      }
     }
   }
 
@@ -902,10 +910,10 @@ static bool use_pair(int64_t M, int64_t N) {
 // and the peer all-reduce's intra-grid waits always have their producers
 // resident.
 template <typename Kern>
-static int pair_clusters(Kern kern, int smem) {
+static int pair_clusters(Kern kern, int smem, int threads) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * (num_sms() / 2), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeClusterDimension;
@@ -932,7 +940,7 @@ static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, void* c, c
   static int max_clusters = 0;  // one static per instantiation
   if (!max_clusters) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    max_clusters = pair_clusters(kern, smem);
+    max_clusters = pair_clusters(kern, smem, kPeer ? kPeerThreads : kThreads);
   }
   constexpr int kTileN = EPI == kSwiGLU ? 128 : pair::BN;
   const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + kTileN - 1) / kTileN);
@@ -958,7 +966,7 @@ static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, void* c, c
   const int clusters = kPeer ? max_clusters : (units < max_clusters ? units : max_clusters);
   const PeerAR no_par = {};
   PeerAG no_ag = {};
-  kern<<<2 * clusters, kThreads, smem, st>>>(ta, tb, c, r, M, N, K, ldc, ldr, err, c2, ldc2, splits,
+  kern<<<2 * clusters, kPeer ? kPeerThreads : kThreads, smem, st>>>(ta, tb, c, r, M, N, K, ldc, ldr, err, c2, ldc2, splits,
                                              par ? *par : no_par, ta2 ? *ta2 : ta, ag ? *ag : no_ag);
   LIBRA_LAUNCH_CHECK();
 }

@@ -392,7 +392,8 @@ constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarBytes;
 //      all-gather, each byte crossing NVLink once per direction).
 //   C  each CTA copies finished row blocks of its own gathered buffer (plus
 //      the residual) into the output tensor, so the kernel ends only when the
-//      full sum is here.
+//      full sum is here.  The row blocks this rank owns went to the output
+//      directly in phase B.
 // Counters live in two parity sets; a call zeroes the set the next call uses
 // (safe: no peer can start the next call before this rank's phase B).  Every
 // wait is bounded.  Plain loads and stores to peer memory, no multicast.
@@ -730,6 +731,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPeer ? kPeerThreads
             for (int e = 0; e < 8; ++e) acc[u][e] += __bfloat162float(ub[e]);
           }
         }
+        // the owner's own output: written here (with its residual), not gathered
+        if (!rs) {
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u) {
+            if (!in[u]) continue;
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = acc[u][e];
+            if (par.residual != nullptr) {
+              const uint4 rr = *reinterpret_cast<const uint4*>(par.residual + off[u]);
+              const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&rr);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) f[e] = __bfloat162float(__float2bfloat16(f[e])) + __bfloat162float(rb[e]);
+            }
+            uint4 o;
+            o.x = pack_bf16x2(f[0], f[1]);
+            o.y = pack_bf16x2(f[2], f[3]);
+            o.z = pack_bf16x2(f[4], f[5]);
+            o.w = pack_bf16x2(f[6], f[7]);
+            *reinterpret_cast<uint4*>(par.y + off[u]) = o;
+          }
+        }
         if (rs && par.residual != nullptr) {
           uint4 rr[kBatch];
 #pragma unroll
@@ -755,7 +778,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPeer ? kPeerThreads
             *reinterpret_cast<uint4*>(par.y + off[u] - (int64_t)me * par.rs_rows * N) = o;
           } else {
             for (int q = 0; q < n; ++q)
-              *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(par.gath[q]) + off[u]) = o;
+              if (q != me) *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(par.gath[q]) + off[u]) = o;
           }
         }
       }
@@ -769,6 +792,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPeer ? kPeerThreads
     // reduce-scatter the wait alone remains: no rank may overwrite its partial
     // in the next call before every owner has read it.
     for (int mb = blockIdx.x; mb < num_m; mb += gridDim.x) {
+      if (!rs && peer_owner(par, mb) == me) continue;  // written by phase B
       __syncthreads();
       if (threadIdx.x == 0) s_ok = wait_flag_geq(my_flags + par.max_rb + mb, chunks, err, kTimeoutPeerFlag);
       __syncthreads();

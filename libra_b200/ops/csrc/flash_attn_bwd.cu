@@ -59,23 +59,26 @@ __global__ void __launch_bounds__(256) attn_delta_kernel(const __nv_bfloat16* __
   const int s0 = cu[t.x], L = cu[t.x + 1] - s0;
   const int base = pad_base(s0, t.x) + t.y * BQ;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int r = warp; r < BQ; r += 8) {
+  const int half = lane >> 4, l16 = lane & 15;  // 16 lanes x 16 bytes per row, two rows per warp step
+#pragma unroll 2
+  for (int r = 2 * warp + half; r < BQ; r += 16) {
     const int qp = t.y * BQ + r;
-    float dsum = 0.f, l2 = 0.f;
-    if (qp < L) {  // warp-uniform
+    const bool valid = qp < L;
+    float dsum = 0.f;
+    if (valid) {
       const size_t w = (size_t)(s0 + qp) * Hq + h;
-      const uint2 o = reinterpret_cast<const uint2*>(O + w * D)[lane];
-      const uint2 g = reinterpret_cast<const uint2*>(dO + w * D)[lane];
+      const uint4 o = reinterpret_cast<const uint4*>(O + w * D)[l16];
+      const uint4 g = reinterpret_cast<const uint4*>(dO + w * D)[l16];
       const __nv_bfloat16* ob = reinterpret_cast<const __nv_bfloat16*>(&o);
       const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&g);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) dsum += __bfloat162float(ob[e]) * __bfloat162float(gb[e]);
-      dsum = warp_sum(dsum);
-      l2 = lse[(size_t)h * T + s0 + qp] * kLog2e;
+      for (int e = 0; e < 8; ++e) dsum += __bfloat162float(ob[e]) * __bfloat162float(gb[e]);
     }
-    if (lane == 0) {
+#pragma unroll
+    for (int m = 8; m > 0; m >>= 1) dsum += __shfl_xor_sync(0xffffffffu, dsum, m);  // within the 16-lane half
+    if (l16 == 0) {
       dltp[(size_t)h * T_pad + base + r] = dsum;
-      lse2p[(size_t)h * T_pad + base + r] = l2;
+      lse2p[(size_t)h * T_pad + base + r] = valid ? lse[(size_t)h * T + s0 + qp] * kLog2e : 0.f;
     }
   }
 }

@@ -279,11 +279,11 @@ __global__ void __launch_bounds__(256)
   const int lane = threadIdx.x & 31, grp = lane >> 3, j = lane & 7;
   const unsigned gmask = 0xFFu << (grp * 8);
   const int stride_row = (nq + 2 * nkv) * D;
-  const int64_t total = (int64_t)T * heads;
-  const int64_t step = (int64_t)gridDim.x * (blockDim.x >> 5) * 4;
-  for (int64_t item = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 4 + grp; item < total;
-       item += step) {
-    const int t = (int)(item / heads), h = (int)(item - (int64_t)t * heads);
+  // Item counts stay below 2^31 (checked on the host), so the (token, head) split is a 32-bit division.
+  const int total = T * heads;
+  const int step = gridDim.x * (blockDim.x >> 5) * 4;
+  for (int item = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 4 + grp; item < total; item += step) {
+    const int t = item / heads, h = item - t * heads;
     const bool is_q = h < nq;
     const __nv_bfloat16* src = qkv + (size_t)t * stride_row + (size_t)h * D;
     const int i0 = 8 * j, i1 = D / 2 + 8 * j;
@@ -358,11 +358,11 @@ __global__ void __launch_bounds__(256)
   for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) s_w[i] = __bfloat162float(i < D ? qw[i] : kw[i - D]);
   __syncthreads();
   float aq1[8] = {}, aq2[8] = {}, ak1[8] = {}, ak2[8] = {};
-  const int64_t total = (int64_t)T * heads;
-  const int64_t step = (int64_t)gridDim.x * (blockDim.x >> 5) * 4;
-  for (int64_t item = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 4 + grp; item < total;
-       item += step) {
-    const int t = (int)(item / heads), h = (int)(item - (int64_t)t * heads);
+  // Item counts stay below 2^31 (checked on the host), so the (token, head) split is a 32-bit division.
+  const int total = T * heads;
+  const int step = gridDim.x * (blockDim.x >> 5) * 4;
+  for (int item = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 4 + grp; item < total; item += step) {
+    const int t = item / heads, h = item - t * heads;
     const bool is_q = h < nq;
     const __nv_bfloat16* g = is_q ? dq + ((size_t)t * nq + h) * D : dk + ((size_t)t * nkv + (h - nq)) * D;
     const uint4 ga = *reinterpret_cast<const uint4*>(g + i0);
@@ -566,6 +566,7 @@ std::vector<torch::Tensor> qk_norm_rope_fwd(torch::Tensor qkv, torch::Tensor qw,
   auto k = torch::empty({T, nkv, D}, qkv.options());
   auto v = torch::empty({T, nkv, D}, qkv.options());
   auto rstd = torch::empty({T * (nq + nkv)}, qkv.options().dtype(at::kFloat));
+  LIBRA_CHECK((int64_t)T * (nq + nkv) < ((int64_t)1 << 31), "qk_norm_rope: more than 2^31 (token, head) items");
   const int total = T * (int)(nq + nkv);
   if (total == 0) return {q, k, v, rstd};
   LIBRA_CHECK(pos.is_contiguous() && cos_t.is_contiguous() && sin_t.is_contiguous() && qw.is_contiguous() &&
@@ -599,6 +600,7 @@ torch::Tensor qk_norm_rope_bwd(torch::Tensor qkv, torch::Tensor qw, torch::Tenso
   int dev, sms;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  LIBRA_CHECK((int64_t)T * (nq + nkv) < ((int64_t)1 << 31), "qk_norm_rope_bwd: more than 2^31 (token, head) items");
   const int total = T * (int)(nq + nkv);
   int blocks = sms * 8;
   if (blocks * warps * 4 > total) blocks = (total + warps * 4 - 1) / (warps * 4);

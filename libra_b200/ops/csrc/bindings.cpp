@@ -55,6 +55,15 @@ std::vector<torch::Tensor> allreduce_add_rmsnorm(std::vector<int64_t> data_ptrs,
                                                  torch::Tensor w, double eps, int64_t epoch, int64_t grid,
                                                  torch::Tensor err);
 }  // namespace tp
+namespace ep {
+void ep_push(std::vector<int64_t> rx, std::vector<int64_t> flags, int64_t me, int64_t slot_off, torch::Tensor x,
+             c10::optional<torch::Tensor> scale, torch::Tensor dst_rank, torch::Tensor dst_row, int64_t k,
+             int64_t max_rows, int64_t epoch, int64_t grid, torch::Tensor err);
+void ep_pull(std::vector<int64_t> tx, std::vector<int64_t> flags, int64_t me, int64_t slot_off,
+             c10::optional<torch::Tensor> weight, c10::optional<torch::Tensor> residual, torch::Tensor src_rank,
+             torch::Tensor src_row, int64_t k, int64_t max_rows, torch::Tensor out, c10::optional<torch::Tensor> gath,
+             int64_t epoch, int64_t grid, torch::Tensor err);
+}  // namespace ep
 }  // namespace libra
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -87,4 +96,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_close", &libra::ipc::ipc_close);
   m.def("tp_allreduce_add_rmsnorm", &libra::tp::allreduce_add_rmsnorm,
         "peer-memory all-reduce of TP partials + residual + RMSNorm");
+  m.def("ep_push", &libra::ep::ep_push, "MoE dispatch: rows stored straight into the expert owners' peer buffers");
+  m.def("ep_pull", &libra::ep::ep_pull,
+        "MoE combine: weighted sum of the expert outputs loaded from the owners' peer buffers (+ residual)");
 }

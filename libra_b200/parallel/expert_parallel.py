@@ -8,11 +8,20 @@ destination rank -> ``all_to_all_single`` the rows and their local expert ids
 -> per-local-expert SwiGLU MLP (tcgen05 GEMMs through ``models.moe``) ->
 all-to-all back -> weighted sum into the residual.  Autograd runs the same
 exchanges in reverse.
+
+With a ``PeerExpertExchange`` the two all-to-alls become one kernel each over
+NVLink peer memory (``ops/csrc/ep_exchange.cu``): dispatch stores every
+(token, k) row straight into the expert owner's receive slot, combine loads the
+k expert outputs of each token from the owners and sums them with the routing
+weights and the residual in the same pass.  The routing plan places received
+rows grouped by local expert, so the expert MLP is a grouped GEMM with no
+per-expert gather/scatter.
 """
 
 from __future__ import annotations
 
-from typing import List
+from dataclasses import dataclass
+from typing import List, Optional
 
 import torch
 import torch.distributed as dist
@@ -37,8 +46,11 @@ class _AllToAll(torch.autograd.Function):
         return _all_to_all(g, ctx.rc, ctx.sc, ctx.group), None, None, None
 
 
-def ep_moe_mlp(h, residual, router, w1_local, w2_local, cfg, group):
-    """MoE block with experts sharded over ``group``; returns residual + MoE(h)."""
+def ep_moe_mlp(h, residual, router, w1_local, w2_local, cfg, group, exchange: Optional["PeerExpertExchange"] = None):
+    """MoE block with experts sharded over ``group``; returns residual + MoE(h).
+    With ``exchange`` the dispatch and combine run as peer-memory kernels."""
+    if exchange is not None:
+        return _ep_moe_mlp_peer(h, residual, router, w1_local, w2_local, cfg, exchange)
     ep = dist.get_world_size(group) if dist.is_initialized() else 1
     E_l = w1_local.shape[0]
     T, H = h.shape
@@ -77,3 +89,271 @@ def ep_moe_mlp(h, residual, router, w1_local, w2_local, cfg, group):
     out = torch.zeros((T, H), dtype=torch.float32, device=h.device)
     out = out.index_add(0, tok, y_send.float() * wsel)
     return (out + residual.float()).to(h.dtype)
+
+
+# ----------------------------------------------------------------------------- peer-memory dispatch / combine
+
+GRID = 128  # the same on every rank: arrival counters count CTAs
+
+
+@dataclass
+class RoutePlan:
+    """Where each (token, k) assignment j = t * k + kk lives on the expert side."""
+
+    dst_rank: torch.Tensor  # int32 [T*k]: rank owning the assignment's expert
+    dst_row: torch.Tensor  # int32 [T*k]: row in that rank's receive slot
+    recv_counts: List[int]  # rows this rank receives per local expert (grouped, in order)
+    recv_total: int
+    k: int
+
+
+def route_plan(experts: torch.Tensor, counts_all: torch.Tensor, me: int) -> RoutePlan:
+    """Destination of every assignment, from all ranks' per-expert counts.
+
+    ``experts`` [T, k] global expert ids of this rank's tokens; ``counts_all``
+    [n, E] the number of assignments each rank sends to each expert.  The
+    receive slot of rank d is ordered by (local expert, source rank, source
+    order): row = (rows of d's earlier local experts) + (rows of this expert
+    from lower ranks) + (position among this rank's rows for the expert).
+    """
+    n, E = counts_all.shape
+    E_l = E // n
+    T, k = experts.shape
+    flat = experts.reshape(-1)
+    order = torch.argsort(flat, stable=True)
+    g = flat[order]
+    cnt = counts_all.to(torch.int64)
+    per_dest = cnt.sum(0).view(n, E_l)
+    base = (per_dest.cumsum(1) - per_dest).reshape(-1)
+    lower = (cnt.cumsum(0) - cnt)[me]
+    start = cnt[me].cumsum(0) - cnt[me]
+    i = torch.arange(flat.numel(), device=flat.device)
+    row_sorted = base[g] + lower[g] + i - start[g]
+    dst_rank = torch.empty(flat.numel(), dtype=torch.int32, device=flat.device)
+    dst_row = torch.empty_like(dst_rank)
+    dst_rank[order] = (g // E_l).to(torch.int32)
+    dst_row[order] = row_sorted.to(torch.int32)
+    host = per_dest.cpu()
+    return RoutePlan(dst_rank, dst_row, [int(c) for c in host[me]], int(host[me].sum()), k)
+
+
+class PeerExpertExchange:
+    """Symmetric receive / send slots shared over CUDA IPC by the EP group.
+
+    Per rank: ``rx`` (2 slots of [max_rows, H] bf16, written by peers' dispatch),
+    ``tx`` (2 slots, read by peers' combine) and 16 int32 arrival counters.
+    Calls are collective: every rank makes the same push / pull calls in the
+    same order (forward: dispatch then combine; backward in reverse).
+    """
+
+    def __init__(self, group, max_rows: int, hidden: int, device):
+        from libra_b200.parallel.peer_gemm import MAX_RANKS
+
+        self.group = group
+        self.n = dist.get_world_size(group) if dist.is_initialized() and group is not None else 1
+        self.me = dist.get_rank(group) if dist.is_initialized() and group is not None else 0
+        if self.n > MAX_RANKS:
+            raise ValueError(f"at most {MAX_RANKS} ranks")
+        if hidden % 8:
+            raise ValueError("hidden size must be a multiple of 8")
+        self.max_rows, self.H = int(max_rows), int(hidden)
+        self.slot_bytes = (self.max_rows * self.H * 2 + 255) // 256 * 256
+        self.buf = torch.zeros(4 * self.slot_bytes + 256, dtype=torch.uint8, device=device)
+        bases = [int(self.buf.data_ptr())]
+        self._opened = []
+        if self.n > 1:
+            C = ops.ext()
+            handles = [None] * self.n
+            dist.all_gather_object(handles, C.ipc_export(self.buf), group=self.group)
+            bases = []
+            with torch.cuda.device(self.buf.device):
+                for r, (h, off) in enumerate(handles):
+                    if r == self.me:
+                        bases.append(int(self.buf.data_ptr()))
+                    else:
+                        base = C.ipc_open(h)
+                        self._opened.append(base)
+                        bases.append(base + int(off))
+        self.rx = bases
+        self.tx = [b + 2 * self.slot_bytes for b in bases]
+        self.flags = [b + 4 * self.slot_bytes for b in bases]
+        self.push_calls = 0
+        self.pull_calls = 0
+        if self.n > 1:
+            torch.cuda.synchronize(self.buf.device)
+            dist.barrier(group=self.group)
+
+    def close(self) -> None:
+        for base in self._opened:
+            ops.ext().ipc_close(base)
+        self._opened = []
+
+    def _slot_view(self, area: int, slot: int, rows: int) -> torch.Tensor:
+        off = (2 * area + slot) * self.slot_bytes
+        return self.buf[off:off + rows * self.H * 2].view(torch.bfloat16).view(rows, self.H)
+
+    def plan(self, experts: torch.Tensor, num_experts: int) -> RoutePlan:
+        cnt = torch.bincount(experts.reshape(-1), minlength=num_experts).to(torch.int32)
+        if self.n > 1:
+            parts = [torch.empty_like(cnt) for _ in range(self.n)]
+            dist.all_gather(parts, cnt, group=self.group)
+            counts_all = torch.stack(parts)
+        else:
+            counts_all = cnt[None]
+        plan = route_plan(experts, counts_all, self.me)
+        worst = int(counts_all.to(torch.int64).sum(0).view(self.n, -1).sum(1).max())
+        if worst > self.max_rows:  # the same decision on every rank: all see all counts
+            raise ValueError(f"a rank would receive {worst} rows; the exchange holds {self.max_rows}")
+        return plan
+
+    def push(self, x: torch.Tensor, plan: RoutePlan, scale: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Rows x[j // k] (times scale[j]) to their owners; returns this rank's received rows."""
+        slot = self.push_calls & 1
+        self.push_calls += 1
+        x = x.contiguous()
+        ops.ext().ep_push(self.rx, self.flags, self.me, slot * self.slot_bytes, x,
+                          None if scale is None else scale.reshape(-1).float().contiguous(),
+                          plan.dst_rank, plan.dst_row, plan.k, self.max_rows, self.push_calls, GRID,
+                          ops.error_flag(x.device))
+        return self._slot_view(0, slot, plan.recv_total).clone()
+
+    def pull(self, y: torch.Tensor, plan: RoutePlan, weight: Optional[torch.Tensor] = None,
+             residual: Optional[torch.Tensor] = None, T: int = 0, save_rows: bool = False):
+        """Publishes this rank's rows ``y`` [recv_total, H]; returns (out [T, H], gathered rows or None)
+        with out[t] = residual[t] + sum_kk weight[t, kk] * (row of assignment (t, kk))."""
+        slot = self.pull_calls & 1
+        self.pull_calls += 1
+        if y.shape[0]:
+            self._slot_view(1, slot, y.shape[0]).copy_(y)
+        out = torch.empty(T, self.H, dtype=torch.bfloat16, device=self.buf.device)
+        gath = torch.empty(T * plan.k, self.H, dtype=torch.bfloat16, device=out.device) if save_rows else None
+        ops.ext().ep_pull(self.tx, self.flags, self.me, slot * self.slot_bytes,
+                          None if weight is None else weight.reshape(-1).float().contiguous(),
+                          None if residual is None else residual.contiguous(), plan.dst_rank, plan.dst_row,
+                          plan.k, self.max_rows, out, gath, self.pull_calls, GRID, ops.error_flag(out.device))
+        return out, gath
+
+
+class _PeerDispatch(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, h, plan, xchg):
+        ctx.plan, ctx.xchg, ctx.T = plan, xchg, h.shape[0]
+        return xchg.push(h, plan)
+
+    @staticmethod
+    def backward(ctx, g):
+        dh, _ = ctx.xchg.pull(g.contiguous(), ctx.plan, T=ctx.T)
+        return dh, None, None
+
+
+class _PeerCombine(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, y, weights, residual, plan, xchg):
+        out, gath = xchg.pull(y, plan, weight=weights, residual=residual, T=residual.shape[0],
+                              save_rows=weights.requires_grad)
+        ctx.plan, ctx.xchg = plan, xchg
+        ctx.save_for_backward(weights, gath if gath is not None else weights.new_empty(0))
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        weights, gath = ctx.saved_tensors
+        g = g.contiguous()
+        dy = ctx.xchg.push(g, ctx.plan, scale=weights)
+        dw = None
+        if ctx.needs_input_grad[1]:
+            T, k = weights.shape
+            dw = torch.einsum("th,tkh->tk", g.float(), gath.view(T, k, -1).float())
+        return dy, dw, g, None, None
+
+
+def _ep_moe_mlp_peer(h, residual, router, w1_local, w2_local, cfg, xchg: PeerExpertExchange):
+    from libra_b200.models.moe import GroupedLinear, route
+
+    weights, experts, _ = route(h, router, cfg.num_experts_per_tok, cfg.norm_topk_prob)
+    plan = xchg.plan(experts, cfg.num_experts)
+    x_recv = _PeerDispatch.apply(h, plan, xchg)
+    gu = GroupedLinear.apply(x_recv, w1_local, plan.recv_counts)
+    a = ops.swiglu(gu)
+    y_recv = GroupedLinear.apply(a, w2_local, plan.recv_counts)
+    return _PeerCombine.apply(y_recv, weights, residual, plan, xchg)
+
+
+def _bench(argv=None) -> None:
+    """Device time of MoE dispatch + combine, peer-memory kernels against NCCL all-to-all.
+
+    torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m libra_b200.parallel.expert_parallel
+    Prints one JSON line (rank 0) with the max over ranks of the mean time per dispatch + combine.
+    """
+    import argparse
+    import datetime
+    import json
+    import os
+
+    p = argparse.ArgumentParser()
+    p.add_argument("--tokens", type=int, default=8192)
+    p.add_argument("--hidden", type=int, default=2048)
+    p.add_argument("--experts", type=int, default=128)
+    p.add_argument("--topk", type=int, default=8)
+    p.add_argument("--iters", type=int, default=10)
+    a = p.parse_args(argv)
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", torch.cuda.current_device()))
+    grp = dist.group.WORLD
+    T, H, E, k = a.tokens, a.hidden, a.experts, a.topk
+    g = torch.Generator(device="cuda").manual_seed(rank)
+    h = torch.randn(T, H, device="cuda", generator=g).bfloat16()
+    res = torch.randn(T, H, device="cuda", generator=g).bfloat16()
+    experts = torch.stack([torch.randperm(E, device="cuda", generator=g)[:k] for _ in range(T)])
+    weights = torch.rand(T, k, device="cuda", generator=g)
+    xchg = PeerExpertExchange(grp, max_rows=2 * T * k, hidden=H, device="cuda")
+    plan = xchg.plan(experts, E)
+
+    def peer():
+        x_recv = xchg.push(h, plan)
+        return xchg.pull(x_recv, plan, weight=weights, residual=res, T=T)[0]
+
+    flat = experts.reshape(-1)
+    order = torch.argsort(flat, stable=True)
+    sc = torch.bincount(flat // (E // world), minlength=world)
+    rc = torch.empty_like(sc)
+    dist.all_to_all_single(rc, sc, group=grp)
+    sc, rc = sc.tolist(), rc.tolist()
+    tok = order // k
+    wsel = weights.reshape(-1)[order].unsqueeze(1)
+
+    def nccl():
+        x_recv = _all_to_all(h.index_select(0, tok), sc, rc, grp)
+        y = _all_to_all(x_recv, rc, sc, grp)
+        return (res.float().index_add(0, tok, y.float() * wsel)).bfloat16()
+
+    torch.testing.assert_close(peer().float(), nccl().float(), rtol=2e-2, atol=5e-2)
+    out = {}
+    for name, fn in (("peer", peer), ("nccl", nccl)):
+        for _ in range(3):
+            fn()
+        dist.barrier()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(a.iters):
+            fn()
+        t1.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([t0.elapsed_time(t1) / a.iters], device="cuda")
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX, group=grp)
+        out[name + "_ms"] = round(float(ms), 4)
+    cross = T * k * H * 2 * (world - 1) / world  # bytes leaving this rank per direction, dispatch alone
+    out.update(tokens_per_rank=T, hidden=H, experts=E, topk=k, ranks=world,
+               peer_dispatch_combine_gbs_per_direction=round(2 * cross / out["peer_ms"] / 1e6, 1))
+    if rank == 0:
+        print(json.dumps(out))
+    xchg.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    _bench()

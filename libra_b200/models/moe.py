@@ -26,9 +26,17 @@ class GroupedLinear(torch.autograd.Function):
     """y[rows of group e] = x[rows of group e] W[e]^T for contiguous row groups."""
 
     @staticmethod
-    def forward(ctx, x, w, counts_host):
+    def forward(ctx, x, w, counts_host, dest=None):
         E, N, _ = w.shape
-        y = torch.empty(x.shape[0], N, dtype=x.dtype, device=x.device)
+        if dest is not None:
+            # ``dest`` = (tensor,): caller-provided [rows, N] memory (e.g. a peer-visible send slot).  The
+            # output aliases its storage without being an autograd view of it, so the gradient history
+            # starts here rather than at the buffer the slot is carved from.
+            d = dest[0]
+            y = torch.empty(0, dtype=d.dtype, device=d.device).set_(d.untyped_storage(), d.storage_offset(),
+                                                                     d.shape, d.stride())
+        else:
+            y = torch.empty(x.shape[0], N, dtype=x.dtype, device=x.device)
         s = 0
         for e in range(E):
             c = int(counts_host[e])
@@ -58,7 +66,7 @@ class GroupedLinear(torch.autograd.Function):
                     dx[s:s + c] = (dy[s:s + c].float() @ w[e].float()).to(dx.dtype)
                     target[e] += dy[s:s + c].float().t() @ x[s:s + c].float()
             s += c
-        return dx, (None if main is not None else dw.to(w.dtype)), None
+        return dx, (None if main is not None else dw.to(w.dtype)), None, None
 
 
 def route(h, router_w, top_k: int, normalize: bool = True):

@@ -93,7 +93,7 @@ def ep_moe_mlp(h, residual, router, w1_local, w2_local, cfg, group, exchange: Op
 
 # ----------------------------------------------------------------------------- peer-memory dispatch / combine
 
-GRID = 128  # the same on every rank: arrival counters count CTAs
+CTAS_PER_SM = 4  # grid = 4 x SMs, the same on every rank: arrival counters count CTAs
 
 
 @dataclass
@@ -148,6 +148,8 @@ class PeerExpertExchange:
 
     def __init__(self, group, max_rows: int, hidden: int, device):
         from libra_b200.parallel.peer_gemm import MAX_RANKS
+
+        self.grid = CTAS_PER_SM * torch.cuda.get_device_properties(torch.device(device)).multi_processor_count
 
         self.group = group
         self.n = dist.get_world_size(group) if dist.is_initialized() and group is not None else 1
@@ -213,9 +215,14 @@ class PeerExpertExchange:
         x = x.contiguous()
         ops.ext().ep_push(self.rx, self.flags, self.me, slot * self.slot_bytes, x,
                           None if scale is None else scale.reshape(-1).float().contiguous(),
-                          plan.dst_rank, plan.dst_row, plan.k, self.max_rows, self.push_calls, GRID,
+                          plan.dst_rank, plan.dst_row, plan.k, self.max_rows, self.push_calls, self.grid,
                           ops.error_flag(x.device))
         return self._slot_view(0, slot, plan.recv_total).clone()
+
+    def send_view(self, rows: int) -> torch.Tensor:
+        """The slot the next ``pull`` publishes: a producer that writes its [rows, H] output
+        here saves the copy into the slot."""
+        return self._slot_view(1, self.pull_calls & 1, rows)
 
     def pull(self, y: torch.Tensor, plan: RoutePlan, weight: Optional[torch.Tensor] = None,
              residual: Optional[torch.Tensor] = None, T: int = 0, save_rows: bool = False):
@@ -223,14 +230,15 @@ class PeerExpertExchange:
         with out[t] = residual[t] + sum_kk weight[t, kk] * (row of assignment (t, kk))."""
         slot = self.pull_calls & 1
         self.pull_calls += 1
-        if y.shape[0]:
-            self._slot_view(1, slot, y.shape[0]).copy_(y)
+        dst = self._slot_view(1, slot, y.shape[0])
+        if y.shape[0] and y.data_ptr() != dst.data_ptr():
+            dst.copy_(y)
         out = torch.empty(T, self.H, dtype=torch.bfloat16, device=self.buf.device)
         gath = torch.empty(T * plan.k, self.H, dtype=torch.bfloat16, device=out.device) if save_rows else None
         ops.ext().ep_pull(self.tx, self.flags, self.me, slot * self.slot_bytes,
                           None if weight is None else weight.reshape(-1).float().contiguous(),
                           None if residual is None else residual.contiguous(), plan.dst_rank, plan.dst_row,
-                          plan.k, self.max_rows, out, gath, self.pull_calls, GRID, ops.error_flag(out.device))
+                          plan.k, self.max_rows, out, gath, self.pull_calls, self.grid, ops.error_flag(out.device))
         return out, gath
 
 
@@ -275,7 +283,7 @@ def _ep_moe_mlp_peer(h, residual, router, w1_local, w2_local, cfg, xchg: PeerExp
     x_recv = _PeerDispatch.apply(h, plan, xchg)
     gu = GroupedLinear.apply(x_recv, w1_local, plan.recv_counts)
     a = ops.swiglu(gu)
-    y_recv = GroupedLinear.apply(a, w2_local, plan.recv_counts)
+    y_recv = GroupedLinear.apply(a, w2_local, plan.recv_counts, (xchg.send_view(plan.recv_total),))
     return _PeerCombine.apply(y_recv, weights, residual, plan, xchg)
 
 
@@ -315,6 +323,13 @@ def _bench(argv=None) -> None:
         x_recv = xchg.push(h, plan)
         return xchg.pull(x_recv, plan, weight=weights, residual=res, T=T)[0]
 
+    def dispatch():
+        return xchg.push(h, plan)
+
+    def combine():  # expert outputs already in the send slot, as the MoE block leaves them
+        y = xchg.send_view(plan.recv_total)
+        return xchg.pull(y, plan, weight=weights, residual=res, T=T)[0]
+
     flat = experts.reshape(-1)
     order = torch.argsort(flat, stable=True)
     sc = torch.bincount(flat // (E // world), minlength=world)
@@ -331,7 +346,7 @@ def _bench(argv=None) -> None:
 
     torch.testing.assert_close(peer().float(), nccl().float(), rtol=2e-2, atol=5e-2)
     out = {}
-    for name, fn in (("peer", peer), ("nccl", nccl)):
+    for name, fn in (("peer", peer), ("nccl", nccl), ("peer_dispatch", dispatch), ("peer_combine", combine)):
         for _ in range(3):
             fn()
         dist.barrier()

@@ -77,6 +77,25 @@ def test_route_plan_emulated_exchange_matches_moe_block():
         torch.testing.assert_close(got, ref, rtol=1e-4, atol=1e-4)
 
 
+def test_grouped_linear_writes_into_caller_slot_and_keeps_grads():
+    """The expert GEMM can write into a bf16 slot carved from a byte buffer (the send slot)
+    without cutting the autograd history."""
+    from libra_b200.models.moe import GroupedLinear
+
+    buf = torch.zeros(256 + 6 * 8 * 2, dtype=torch.uint8)
+    slot = buf[256:].view(torch.bfloat16).view(6, 8)
+    x = torch.randn(6, 4).bfloat16().requires_grad_(True)
+    w = torch.randn(2, 8, 4).bfloat16().requires_grad_(True)
+    y = GroupedLinear.apply(x, w, [2, 4], (slot,))
+    assert y.data_ptr() == slot.data_ptr()
+    ref = torch.cat([x[:2].float() @ w[0].float().t(), x[2:].float() @ w[1].float().t()])
+    torch.testing.assert_close(slot.float(), ref, rtol=2e-2, atol=2e-2)
+    y.float().sum().backward()
+    assert x.grad is not None and w.grad is not None
+    torch.testing.assert_close(x.grad.float(), torch.cat([w[0].float().sum(0).expand(2, 4),
+                                                          w[1].float().sum(0).expand(4, 4)]), rtol=2e-2, atol=2e-2)
+
+
 def _moe_inputs(cfg, T, seed, device="cuda"):
     g = torch.Generator().manual_seed(seed)
     E, H, F = cfg.num_experts, cfg.hidden_size, cfg.moe_intermediate_size

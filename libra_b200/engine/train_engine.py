@@ -420,11 +420,28 @@ class B200TrainEngine:
             dist.all_reduce(self.sq_norm, op=dist.ReduceOp.SUM, group=self.dp_group)
         shard_param = self.flat_param[self.shard_start:self.shard_start + self.shard_numel]
         o = self.optim
+        peer = getattr(self, "_peer_param_gather", None)
+        if peer is not None:  # AdamW stores the new bf16 shard straight into every rank's parameters
+            peer.step(self.master, self.grad_shard, self.exp_avg, self.exp_avg_sq, lr=o.lr, beta1=o.betas[0],
+                      beta2=o.betas[1], eps=o.eps, weight_decay=o.weight_decay, step=self.step_count,
+                      max_grad_norm=o.max_grad_norm, sq_norm=self.sq_norm)
+            return
         ops.adamw_step(self.master, self.grad_shard, self.exp_avg, self.exp_avg_sq, shard_param, lr=o.lr,
                        beta1=o.betas[0], beta2=o.betas[1], eps=o.eps, weight_decay=o.weight_decay,
                        step=self.step_count, max_grad_norm=o.max_grad_norm, sq_norm=self.sq_norm)
         if self.sharded:
             self._gather_params(shard_param)
+
+    def enable_fused_param_gather(self) -> bool:
+        """Collective over the DP group: fuse the distributed optimizer's parameter all-gather into the
+        AdamW kernel (peer-memory stores over NVLink).  Returns False where it does not apply
+        (no sharded optimizer, gloo ranks, or a shard that is not a multiple of 4 elements)."""
+        if not self.sharded or self._gloo() or self.shard_numel % 4:
+            return False
+        from libra_b200.parallel.peer_param_gather import PeerParamGather
+
+        self._peer_param_gather = PeerParamGather(self.dp_group, self.flat_param, self.shard_start, self.shard_numel)
+        return True
 
     def _reduce_stats(self, stats: Dict[str, float]) -> Dict[str, float]:
         if self.dp_size <= 1 or not dist.is_initialized():

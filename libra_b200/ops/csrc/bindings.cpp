@@ -30,6 +30,11 @@ void grad_sq_norm(torch::Tensor grad, torch::Tensor out);
 void adamw_step(torch::Tensor master, torch::Tensor grad, torch::Tensor m, torch::Tensor v, torch::Tensor param,
                 double lr, double beta1, double beta2, double eps, double wd, int64_t step,
                 c10::optional<torch::Tensor> sq_norm, double max_norm, double grad_scale);
+void adamw_step_allgather(torch::Tensor master, torch::Tensor grad, torch::Tensor m, torch::Tensor v, double lr,
+                          double beta1, double beta2, double eps, double wd, int64_t step,
+                          c10::optional<torch::Tensor> sq_norm, double max_norm, double grad_scale,
+                          std::vector<int64_t> param_peers, std::vector<int64_t> flag_peers, int64_t me, int64_t epoch,
+                          torch::Tensor err);
 torch::Tensor paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                                      torch::Tensor block_tables, torch::Tensor seq_lens, int64_t max_len,
                                      double scale);
@@ -82,6 +87,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("logprob_bwd_", &libra::logprob_bwd_);
   m.def("grad_sq_norm", &libra::grad_sq_norm);
   m.def("adamw_step", &libra::adamw_step);
+  m.def("adamw_step_allgather", &libra::adamw_step_allgather,
+        "AdamW on this rank's shard with the bf16 result stored into every rank's parameter buffer");
   m.def("paged_decode_attention", &libra::paged_decode_attention);
   m.def("flash_fwd", &libra::attn::flash_fwd, "tcgen05 varlen GQA attention forward", py::arg("q"), py::arg("k"),
         py::arg("v"), py::arg("cu_seqlens"), py::arg("tiles"), py::arg("scale"), py::arg("causal"), py::arg("err"),

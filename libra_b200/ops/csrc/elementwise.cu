@@ -223,10 +223,23 @@ __global__ void grad_sq_norm_kernel(const float* __restrict__ g, int64_t n, floa
   }
 }
 
+// Peer mode of the AdamW kernel (ZeRO-1 step fused with the parameter all-gather): every rank updates
+// its shard and stores the new bf16 values straight into the same shard of every rank's parameter
+// buffer (IPC-mapped peer memory), then bumps an arrival counter on every rank; CTA 0 waits (bounded)
+// until every rank's CTAs have arrived, so the kernel ends only when the whole parameter vector is here.
+constexpr int kAdamPeerMax = 8;
+struct AdamPeers {
+  uint64_t param[kAdamPeerMax];  // this rank's shard inside each rank's bf16 parameter buffer
+  uint64_t flags[kAdamPeerMax];  // int32 arrival counters [kAdamPeerMax] of each rank
+  int n, me, epoch;
+  int* err;
+};
+
+template <bool kPeer>
 __global__ void adamw_kernel(float* __restrict__ master, const float* __restrict__ grad, float* __restrict__ m,
                              float* __restrict__ v, __nv_bfloat16* __restrict__ param, int64_t n, float lr, float beta1,
                              float beta2, float eps, float wd, float bc1, float bc2, const float* __restrict__ sq_norm,
-                             float max_norm, float grad_scale) {
+                             float max_norm, float grad_scale, const AdamPeers peers) {
   float clip = grad_scale;
   if (max_norm > 0.f && sq_norm) {
     const float norm = sqrtf(*sq_norm) * grad_scale;
@@ -256,14 +269,31 @@ __global__ void adamw_kernel(float* __restrict__ master, const float* __restrict
     uint2 pk;
     pk.x = pack_bf16x2(p.x, p.y);
     pk.y = pack_bf16x2(p.z, p.w);
-    reinterpret_cast<uint2*>(param)[i] = pk;
+    if constexpr (kPeer) {
+      for (int r = 0; r < peers.n; ++r) reinterpret_cast<uint2*>(peers.param[r])[i] = pk;
+    } else {
+      reinterpret_cast<uint2*>(param)[i] = pk;
+    }
   }
   for (int64_t i = n4 * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const float g = grad[i] * clip;
     m[i] = beta1 * m[i] + (1.f - beta1) * g;
     v[i] = beta2 * v[i] + (1.f - beta2) * g * g;
     master[i] -= lr * ((m[i] / bc1) / (sqrtf(v[i] / bc2) + eps) + wd * master[i]);
-    param[i] = __float2bfloat16(master[i]);
+    if constexpr (kPeer) {
+      for (int r = 0; r < peers.n; ++r) reinterpret_cast<__nv_bfloat16*>(peers.param[r])[i] = __float2bfloat16(master[i]);
+    } else {
+      param[i] = __float2bfloat16(master[i]);
+    }
+  }
+  if constexpr (kPeer) {
+    __threadfence_system();
+    __syncthreads();
+    if ((int)threadIdx.x < peers.n)
+      red_add_release_sys(reinterpret_cast<int*>(peers.flags[threadIdx.x]) + peers.me, 1);
+    if (blockIdx.x == 0 && (int)threadIdx.x < peers.n)
+      wait_flag_geq(reinterpret_cast<const int*>(peers.flags[peers.me]) + threadIdx.x,
+                    peers.epoch * (int)gridDim.x, peers.err, kTimeoutPeerFlag);
   }
 }
 
@@ -365,10 +395,52 @@ void adamw_step(torch::Tensor master, torch::Tensor grad, torch::Tensor m, torch
   if (n == 0) return;
   const float bc1 = (float)(1.0 - std::pow(beta1, (double)step));
   const float bc2 = (float)(1.0 - std::pow(beta2, (double)step));
-  adamw_kernel<<<sm_count() * 4, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
+  adamw_kernel<false><<<sm_count() * 4, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
       master.data_ptr<float>(), grad.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
       (__nv_bfloat16*)param.data_ptr(), n, (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd, bc1, bc2,
-      sq_norm.has_value() ? sq_norm->data_ptr<float>() : nullptr, (float)max_norm, (float)grad_scale);
+      sq_norm.has_value() ? sq_norm->data_ptr<float>() : nullptr, (float)max_norm, (float)grad_scale, AdamPeers{});
+  LIBRA_LAUNCH_CHECK();
+}
+
+// AdamW on this rank's shard, fused with the parameter all-gather: param_peers[r] is the address of this
+// rank's shard inside rank r's bf16 parameter buffer (mapped into this process), flag_peers[r] rank r's
+// int32 arrival counters.  Same grid on every rank; epoch counts the calls (1, 2, ...).
+void adamw_step_allgather(torch::Tensor master, torch::Tensor grad, torch::Tensor m, torch::Tensor v, double lr,
+                          double beta1, double beta2, double eps, double wd, int64_t step,
+                          c10::optional<torch::Tensor> sq_norm, double max_norm, double grad_scale,
+                          std::vector<int64_t> param_peers, std::vector<int64_t> flag_peers, int64_t me, int64_t epoch,
+                          torch::Tensor err) {
+  LIBRA_CHECK(master.scalar_type() == at::kFloat && grad.scalar_type() == at::kFloat && m.scalar_type() == at::kFloat &&
+                  v.scalar_type() == at::kFloat,
+              "adamw_step_allgather: fp32 master/grad/m/v");
+  const int64_t n = master.numel();
+  LIBRA_CHECK(grad.numel() == n && m.numel() == n && v.numel() == n, "adamw_step_allgather: size mismatch");
+  LIBRA_CHECK(master.is_contiguous() && grad.is_contiguous() && m.is_contiguous() && v.is_contiguous(),
+              "adamw_step_allgather: contiguous buffers");
+  const int nr = (int)param_peers.size();
+  LIBRA_CHECK(nr >= 1 && nr <= kAdamPeerMax && (int)flag_peers.size() == nr && me >= 0 && me < nr,
+              "adamw_step_allgather: 1..8 ranks with one parameter and one flag pointer each");
+  AdamPeers peers{};
+  for (int r = 0; r < nr; ++r) {
+    LIBRA_CHECK((param_peers[r] & 7) == 0 && (flag_peers[r] & 3) == 0,
+                "adamw_step_allgather: parameter shards must be 8-byte aligned");
+    peers.param[r] = (uint64_t)param_peers[r];
+    peers.flags[r] = (uint64_t)flag_peers[r];
+  }
+  const int grid = sm_count() * 4;
+  LIBRA_CHECK(epoch >= 1 && epoch * grid < ((int64_t)1 << 31), "adamw_step_allgather: epoch out of range");
+  peers.n = nr;
+  peers.me = (int)me;
+  peers.epoch = (int)epoch;
+  peers.err = err.data_ptr<int>();
+  const c10::cuda::CUDAGuard guard(master.device());
+  const float bc1 = (float)(1.0 - std::pow(beta1, (double)step));
+  const float bc2 = (float)(1.0 - std::pow(beta2, (double)step));
+  // launched even for an empty shard: the peers wait for this rank's arrivals
+  adamw_kernel<true><<<grid, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
+      master.data_ptr<float>(), grad.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), nullptr, n,
+      (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd, bc1, bc2,
+      sq_norm.has_value() ? sq_norm->data_ptr<float>() : nullptr, (float)max_norm, (float)grad_scale, peers);
   LIBRA_LAUNCH_CHECK();
 }
 

@@ -1,0 +1,84 @@
+"""ZeRO-1 optimizer step fused with the parameter all-gather over NVLink peer memory.
+
+With the distributed optimizer each data-parallel rank owns a contiguous shard
+of the flat fp32 master weights and Adam moments; after the step the updated
+bf16 shards are all-gathered so every rank holds the full bf16 parameters
+(the reference's Megatron distributed optimizer, engine/megatron_core_train_
+engine.py:360-380, does the gather with NCCL after the Adam kernel).  Here the
+AdamW kernel itself (``adamw_step_allgather`` in ``ops/csrc/elementwise.cu``)
+stores each updated bf16 value into the same shard of every rank's parameter
+buffer, so the gather overlaps the update and costs no extra pass over memory;
+an arrival barrier at the end of the kernel makes the full vector visible
+before the next forward.
+
+``PeerParamGather`` maps every rank's flat parameter buffer and a counter area
+into this process (CUDA IPC).  ``step`` is collective: every rank of the group
+calls it once per optimizer step, in the same order.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from libra_b200 import ops
+
+
+class PeerParamGather:
+    def __init__(self, group, flat_param: torch.Tensor, shard_start: int, shard_numel: int):
+        from libra_b200.parallel.peer_gemm import MAX_RANKS
+
+        if flat_param.dtype != torch.bfloat16 or not flat_param.is_cuda or not flat_param.is_contiguous():
+            raise ValueError("flat_param must be a contiguous bf16 CUDA tensor")
+        self.group = group
+        self.n = dist.get_world_size(group) if dist.is_initialized() and group is not None else 1
+        self.me = dist.get_rank(group) if dist.is_initialized() and group is not None else 0
+        if self.n > MAX_RANKS:
+            raise ValueError(f"at most {MAX_RANKS} ranks")
+        if (shard_start * 2) % 8:
+            raise ValueError("shard start must be a multiple of 4 elements")
+        self.flags = torch.zeros(64, dtype=torch.int32, device=flat_param.device)
+        param_bases, flag_bases = [int(flat_param.data_ptr())], [int(self.flags.data_ptr())]
+        self._opened = []
+        if self.n > 1:
+            C = ops.ext()
+            mine = (C.ipc_export(flat_param), C.ipc_export(self.flags))
+            handles = [None] * self.n
+            dist.all_gather_object(handles, mine, group=self.group)
+            param_bases, flag_bases = [], []
+            with torch.cuda.device(flat_param.device):
+                for r, ((hp, op), (hf, of)) in enumerate(handles):
+                    if r == self.me:
+                        param_bases.append(int(flat_param.data_ptr()))
+                        flag_bases.append(int(self.flags.data_ptr()))
+                        continue
+                    bp = C.ipc_open(hp)
+                    bf = C.ipc_open(hf)
+                    self._opened += [bp, bf]
+                    param_bases.append(bp + int(op))
+                    flag_bases.append(bf + int(of))
+        # every rank's flat parameter layout is identical: this rank's shard sits at the same offset
+        self.param_peers = [b + 2 * int(shard_start) for b in param_bases]
+        self.flag_peers = flag_bases
+        self.shard_numel = int(shard_numel)
+        self.calls = 0
+        if self.n > 1:
+            torch.cuda.synchronize(flat_param.device)
+            dist.barrier(group=self.group)
+
+    def close(self) -> None:
+        for base in self._opened:
+            ops.ext().ipc_close(base)
+        self._opened = []
+
+    def step(self, master, grad, exp_avg, exp_avg_sq, *, lr, beta1, beta2, eps, weight_decay, step,
+             max_grad_norm: float = 0.0, sq_norm: Optional[torch.Tensor] = None, grad_scale: float = 1.0) -> None:
+        """AdamW on this rank's shard; afterwards every rank holds the full updated bf16 parameters."""
+        if master.numel() != self.shard_numel:
+            raise ValueError(f"shard has {self.shard_numel} elements, got {master.numel()}")
+        self.calls += 1
+        ops.ext().adamw_step_allgather(master, grad, exp_avg, exp_avg_sq, lr, beta1, beta2, eps, weight_decay, step,
+                                       sq_norm, max_grad_norm, grad_scale, self.param_peers, self.flag_peers,
+                                       self.me, self.calls, ops.error_flag(master.device))

@@ -82,3 +82,72 @@ class PeerParamGather:
         ops.ext().adamw_step_allgather(master, grad, exp_avg, exp_avg_sq, lr, beta1, beta2, eps, weight_decay, step,
                                        sq_norm, max_grad_norm, grad_scale, self.param_peers, self.flag_peers,
                                        self.me, self.calls, ops.error_flag(master.device))
+
+
+def _bench(argv=None) -> None:
+    """Device time of one distributed-optimizer step: fused AdamW + peer all-gather against AdamW followed
+    by NCCL all_gather_into_tensor.
+
+    torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m libra_b200.parallel.peer_param_gather
+    Prints one JSON line (rank 0), max over ranks of the mean per step.
+    """
+    import argparse
+    import datetime
+    import json
+    import os
+
+    p = argparse.ArgumentParser()
+    p.add_argument("--params", type=float, default=1.0e9, help="total parameters over the group")
+    p.add_argument("--iters", type=int, default=10)
+    a = p.parse_args(argv)
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", torch.cuda.current_device()))
+    grp = dist.group.WORLD
+    shard = int(a.params) // world // 4 * 4
+    flat = torch.zeros(world * shard, dtype=torch.bfloat16, device="cuda")
+    master = torch.randn(shard, device="cuda")
+    grad = torch.randn(shard, device="cuda")
+    m, v = torch.zeros_like(master), torch.zeros_like(master)
+    sq = grad.pow(2).sum().reshape(1)
+    hp = dict(lr=1e-5, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.0, max_grad_norm=1.0, sq_norm=sq)
+    pg = PeerParamGather(grp, flat, rank * shard, shard)
+    mine = flat[rank * shard:(rank + 1) * shard]
+    step = [0]
+
+    def fused():
+        step[0] += 1
+        pg.step(master, grad, m, v, step=step[0], **hp)
+
+    def nccl():
+        step[0] += 1
+        ops.adamw_step(master, grad, m, v, mine, step=step[0], **hp)
+        dist.all_gather_into_tensor(flat, mine.clone(), group=grp)
+
+    out = {}
+    for name, fn in (("fused", fused), ("nccl", nccl)):
+        for _ in range(3):
+            fn()
+        dist.barrier()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(a.iters):
+            fn()
+        t1.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([t0.elapsed_time(t1) / a.iters], device="cuda")
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX, group=grp)
+        out[name + "_ms"] = round(float(ms), 3)
+    ops.check_kernel_errors()
+    out.update(params=world * shard, ranks=world, shard=shard)
+    if rank == 0:
+        print(json.dumps(out))
+    pg.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    _bench()

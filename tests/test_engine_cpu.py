@@ -82,3 +82,11 @@ def test_loss_weights_match_reference_group_mean():
     assert abs(w[0] - 1.0 / (g0 * 2)) < 1e-12
     total = sum(wi * c for wi, c in zip(w, counts))
     assert abs(total - 1.0) < 1e-9  # mean of two group means -> weights sum to 1
+
+
+def test_fused_param_gather_declines_without_sharded_nccl_optimizer():
+    """The peer-memory AdamW + parameter all-gather only applies to a sharded optimizer on NCCL ranks;
+    elsewhere the switch leaves the plain optimizer step in place."""
+    eng = B200TrainEngine("tiny", device="cpu")
+    assert eng.enable_fused_param_gather() is False
+    assert getattr(eng, "_peer_param_gather", None) is None

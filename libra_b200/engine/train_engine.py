@@ -435,7 +435,10 @@ class B200TrainEngine:
     def enable_fused_param_gather(self) -> bool:
         """Collective over the DP group: fuse the distributed optimizer's parameter all-gather into the
         AdamW kernel (peer-memory stores over NVLink).  Returns False where it does not apply
-        (no sharded optimizer, gloo ranks, or a shard that is not a multiple of 4 elements)."""
+        (no sharded optimizer, gloo ranks, or a shard that is not a multiple of 4 elements).
+        Call it after ``initialize``."""
+        if not hasattr(self, "sharded"):
+            raise RuntimeError("enable_fused_param_gather() needs an initialized engine (call initialize() first)")
         if not self.sharded or self._gloo() or self.shard_numel % 4:
             return False
         from libra_b200.parallel.peer_param_gather import PeerParamGather

@@ -87,6 +87,11 @@ def test_loss_weights_match_reference_group_mean():
 def test_fused_param_gather_declines_without_sharded_nccl_optimizer():
     """The peer-memory AdamW + parameter all-gather only applies to a sharded optimizer on NCCL ranks;
     elsewhere the switch leaves the plain optimizer step in place."""
+    import pytest
+
     eng = B200TrainEngine("tiny", device="cpu")
+    with pytest.raises(RuntimeError):
+        eng.enable_fused_param_gather()  # before initialize()
+    eng.initialize()
     assert eng.enable_fused_param_gather() is False
     assert getattr(eng, "_peer_param_gather", None) is None

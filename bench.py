@@ -44,6 +44,10 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--mode", choices=["grpo", "train"], default="grpo",
+                    help="grpo: full GRPO step (rollout generation + logprob recompute + update + weight sync); "
+                         "train: trainer half only (recompute + update)")
+    ap.add_argument("--max-running", type=int, default=128, help="rollout engine: concurrent sequences")
     ap.add_argument("--model", default="qwen3-4b")
     ap.add_argument("--prompts-per-gpu", type=int, default=8)
     ap.add_argument("--group", type=int, default=8)
@@ -212,17 +216,120 @@ def run_ours(args, rank, world, local):
     emit(rank, rec)
 
 
+def run_ours_grpo(args, rank, world, local):
+    """Full GRPO step on every rank: the rank's own rollout engine (sharing the
+    GPU with its trainer, with its own weight copy and paged KV cache) generates
+    the step's 8 prompts x 8 samples, the trainer recomputes logprobs and takes
+    the GRPO update (data-parallel gradient reduction across ranks), then the
+    new weights are synced into the rollout engine (one device copy of the flat
+    bf16 buffer) and the policy version advances."""
+    from libra_b200.engine.rollout.llm_engine import LLMEngine
+    from libra_b200.engine.rollout.kv_cache import PagedKVCache
+    from libra_b200.engine.rollout.sampler import SamplingParams
+    from libra_b200.engine.train_engine import B200TrainEngine
+    from libra_b200.utils.timing import ClockSampler, max_over_ranks, sum_over_ranks
+    from libra_b200.workflow.synthetic import WORKLOADS, group_normalize, rollout_requests, rollout_trajectory
+
+    dev = torch.device("cuda", local)
+    wl = WORKLOADS["qwen3-4b-grpo"]
+    eng = B200TrainEngine(args.model, learning_rate=1e-6, micro_batch_size=args.micro_batch,
+                          recompute_micro_batch_size=args.recompute_micro_batch, device=dev, seed=0,
+                          max_tokens_per_micro_batch=args.max_tokens,
+                          max_tokens_per_recompute_batch=args.max_recompute_tokens)
+    max_len = wl.prompt.hi + wl.response.hi + 16
+    eng.initialize(max_seq_length=max_len)
+    rollout_flat = eng.flat_param.clone()
+    n_req = args.prompts_per_gpu * args.group
+    cfg = eng.cfg
+    block = 16
+    worst = n_req * -(-max_len // block) + 64
+    free, _ = torch.cuda.mem_get_info(dev)
+    budget_blocks = PagedKVCache.blocks_for_budget(0.45 * free, cfg.num_hidden_layers, block,
+                                                   cfg.num_key_value_heads, cfg.head_dim)
+    llm = LLMEngine(cfg, eng.layout.views(rollout_flat), kv_blocks=min(worst, budget_blocks), block_size=block,
+                    max_model_len=max_len, max_running=args.max_running, max_batch_tokens=16384, flat=rollout_flat)
+    n_steps = args.warmup + args.steps
+
+    def ev():
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return e
+
+    def grpo_step(s):
+        reqs = rollout_requests(wl, s, rank=rank, prompts=args.prompts_per_gpu)
+        e0 = ev()
+        res = llm.generate_sync([r.prompt for r in reqs],
+                                [SamplingParams(max_tokens=r.response_len, temperature=1.0) for r in reqs])
+        e1 = ev()
+        trajs = [rollout_trajectory(r, g.output_tokens, g.output_logprobs, llm.version, pin=True)
+                 for r, g in zip(reqs, res)]
+        group_normalize(trajs)
+        eng.recompute_logprobs(trajs)
+        eng.grpo_update(trajs)
+        e2 = ev()
+        llm.load_flat_weights(eng.flat_param, version=s + 1)
+        eng.set_version(s + 1)
+        e3 = ev()
+        toks = sum(int(t["input_ids"].numel()) for t in trajs)
+        return toks, (e0, e1, e2, e3), sum(len(g.output_tokens) for g in res)
+
+    for s in range(args.warmup):
+        grpo_step(s)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    sampler = ClockSampler(local).start()
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    tok, gen_tok, marks = 0, 0, []
+    for s in range(args.warmup, n_steps):
+        n, m, g = grpo_step(s)
+        tok += n
+        gen_tok += g
+        marks.append(m)
+    t_end.record()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    clocks = sampler.stop()
+    ms_step = max_over_ranks(t_start.elapsed_time(t_end) / args.steps, dev)
+    roll = sum(m[0].elapsed_time(m[1]) for m in marks) / args.steps
+    train = sum(m[1].elapsed_time(m[2]) for m in marks) / args.steps
+    sync = sum(m[2].elapsed_time(m[3]) for m in marks) / args.steps
+    tokens_step = sum_over_ranks(tok / args.steps, dev)
+    gen_step = sum_over_ranks(gen_tok / args.steps, dev)
+    value = tokens_step / (ms_step / 1e3)
+    from libra_b200 import ops
+    ops.check_kernel_errors(dev)
+    launches = None
+    if not args.no_launch_count:
+        n, _, _ = count_launches(lambda: grpo_step(n_steps), prefixes=("libra::",))
+        launches = int(max_over_ranks(n, dev)) * args.steps
+    sync_bytes = rollout_flat.numel() * rollout_flat.element_size()
+    rec = base_record(args, world, "ours")
+    rec["config"]["step"] = ("rollout (own engine, captured decode graphs, temperature 1.0) + logprob recompute + "
+                             "GRPO update + weight sync to the rollout engine")
+    rec["config"]["rollout"] = f"colocated: one engine per GPU, {args.max_running} concurrent sequences"
+    rec.update({"value": value, "ms_per_step": ms_step, "tokens_per_step": tokens_step,
+                "generated_tokens_per_step": gen_step,
+                "phase_ms": {"rollout": max_over_ranks(roll, dev), "train": max_over_ranks(train, dev),
+                             "weight_sync": max_over_ranks(sync, dev)},
+                "weight_sync": {"ms": max_over_ranks(sync, dev), "bytes": sync_bytes,
+                                "gb_per_s": sync_bytes / (max_over_ranks(sync, dev) / 1e3) / 1e9,
+                                "path": "device copy of the flat bf16 parameter buffer into the rollout engine"},
+                "gpu_launches": launches, "clocks": clocks})
+    emit(rank, rec)
+
+
 # ---------------------------------------------------------------------- reference
 def _make_reference_checkpoint(path, model_name, rank, world):
     """Random-init HF Qwen3 checkpoint + a word-level tokenizer (no network)."""
     from transformers import PreTrainedTokenizerFast, Qwen3Config, Qwen3ForCausalLM
-    from tokenizers import Tokenizer
+    from tokenizers import Tokenizer, pre_tokenizers
     from tokenizers.models import WordLevel
 
     from libra_b200.models.qwen3 import get_config
 
     cfg = get_config(model_name)
-    if rank == 0 and not os.path.exists(os.path.join(path, "done")):
+    if rank == 0 and not os.path.exists(os.path.join(path, "done2")):
         os.makedirs(path, exist_ok=True)
         hf = Qwen3Config(vocab_size=cfg.vocab_size, hidden_size=cfg.hidden_size,
                          intermediate_size=cfg.intermediate_size, num_hidden_layers=cfg.num_hidden_layers,
@@ -238,10 +345,11 @@ def _make_reference_checkpoint(path, model_name, rank, world):
         vocab = {f"t{i}": i for i in range(cfg.vocab_size - 2)}
         vocab["<unk>"] = cfg.vocab_size - 2
         vocab["<eos>"] = cfg.vocab_size - 1
-        tok = PreTrainedTokenizerFast(tokenizer_object=Tokenizer(WordLevel(vocab, unk_token="<unk>")),
-                                      unk_token="<unk>", eos_token="<eos>", pad_token="<eos>")
+        wl = Tokenizer(WordLevel(vocab, unk_token="<unk>"))
+        wl.pre_tokenizer = pre_tokenizers.WhitespaceSplit()  # "t5 t9" -> ids 5, 9 (text round-trips)
+        tok = PreTrainedTokenizerFast(tokenizer_object=wl, unk_token="<unk>", eos_token="<eos>", pad_token="<eos>")
         tok.save_pretrained(path)
-        open(os.path.join(path, "done"), "w").close()
+        open(os.path.join(path, "done2"), "w").close()
     barrier(world)
 
 
@@ -300,6 +408,152 @@ def run_reference(args, rank, world, local):
     emit(rank, rec)
 
 
+def _start_vllm(ckpt: str, ref_root: str, local: int, port: int, gpu_util: float, max_len: int, log_path: str):
+    """vLLM OpenAI server on this rank's GPU with the reference's in-place reload
+    worker extension (RL_Framework.vllm_hot_reload.InplaceReloadWorkerExtension),
+    reachable through vLLM's /collective_rpc route."""
+    import subprocess
+
+    env = dict(os.environ)
+    env.update({"CUDA_VISIBLE_DEVICES": os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")[local]
+                if os.environ.get("CUDA_VISIBLE_DEVICES") else str(local),
+                "PYTHONPATH": ref_root + os.pathsep + env.get("PYTHONPATH", ""), "HF_HUB_OFFLINE": "1",
+                "TRANSFORMERS_OFFLINE": "1", "VLLM_SERVER_DEV_MODE": "1", "TOKENIZERS_PARALLELISM": "false"})
+    for k in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT", "LOCAL_WORLD_SIZE", "GROUP_RANK",
+              "ROLE_RANK", "ROLE_WORLD_SIZE", "TORCHELASTIC_RUN_ID"):
+        env.pop(k, None)
+    cmd = [sys.executable, "-m", "vllm.entrypoints.openai.api_server", "--model", ckpt, "--host", "127.0.0.1",
+           "--port", str(port), "--dtype", "bfloat16", "--gpu-memory-utilization", str(gpu_util),
+           "--max-model-len", str(max_len), "--seed", "0",
+           "--worker-extension-cls", "RL_Framework.vllm_hot_reload.InplaceReloadWorkerExtension"]
+    log = open(log_path, "w")
+    return subprocess.Popen(cmd, env=env, stdout=log, stderr=subprocess.STDOUT, start_new_session=True)
+
+
+def _post_json(url: str, body: dict, timeout: float = 600.0):
+    import urllib.request
+
+    req = urllib.request.Request(url, data=json.dumps(body).encode(), method="POST",
+                                 headers={"Content-Type": "application/json"})
+    with urllib.request.urlopen(req, timeout=timeout) as r:
+        return r.read()
+
+
+def run_reference_grpo(args, rank, world, local):
+    """The reference's GRPO step on the same workload: rollout through its own
+    HTTP client (RL_Framework.engine.rollout_engine.VLLMRolloutEngine) against a
+    vLLM 0.22 server on this rank's GPU, logprob recompute + GRPO update through
+    its FSDPTrainEngine, and its disk weight sync (FSDPTrainEngine.save_weights)
+    followed by its in-place vLLM reload (RL_Framework.vllm_hot_reload)."""
+    import asyncio
+    import signal
+
+    ref_root = os.path.join(HERE, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_root, "RL_Framework")):
+        emit(rank, {"impl": "reference", "unavailable": "baseline/_ref is not installed"})
+        return
+    sys.path.insert(0, ref_root)
+    from RL_Framework.engine.rollout_engine import VLLMRolloutEngine
+    from RL_Framework.engine.train_engine import FSDPTrainEngine
+
+    from libra_b200.utils.timing import ClockSampler, max_over_ranks, sum_over_ranks
+    from libra_b200.workflow.synthetic import WORKLOADS, group_normalize, rollout_requests, rollout_trajectory
+
+    dev = torch.device("cuda", local)
+    ckpt = os.environ.get("LIBRA_REF_CKPT", "/tmp/libra_ref_qwen3_4b")
+    _make_reference_checkpoint(ckpt, args.model, rank, world)
+    wl = WORKLOADS["qwen3-4b-grpo"]
+    max_len = wl.prompt.hi + wl.response.hi + 16
+    port = 8100 + local
+    logdir = os.path.join(HERE, "gpurun_out") if os.path.isdir(os.path.join(HERE, "gpurun_out")) else "/tmp"
+    proc = _start_vllm(ckpt, ref_root, local, port, float(os.environ.get("LIBRA_REF_VLLM_UTIL", "0.3")), max_len,
+                       os.path.join(logdir, f"ref_vllm_rank{rank}.log"))
+    try:
+        client = VLLMRolloutEngine("127.0.0.1", port, ckpt)
+        client.wait_for_ready(timeout=float(os.environ.get("LIBRA_REF_VLLM_TIMEOUT", "900")))
+        barrier(world)
+        train = FSDPTrainEngine(model_path=ckpt, learning_rate=1e-6, kl_coef=0.001, clip_epsilon=0.2,
+                                micro_batch_size=args.micro_batch)
+        train.initialize(max_seq_length=max_len)
+        from transformers import AutoTokenizer
+
+        tok = AutoTokenizer.from_pretrained(ckpt)
+        sync_root = os.environ.get("LIBRA_REF_SYNC_DIR", "/tmp/libra_ref_sync")
+        n_steps = args.warmup + args.steps
+
+        async def rollout(reqs):
+            return await asyncio.gather(*[client.generate(" ".join(f"t{t}" for t in r.prompt),
+                                                          max_new_tokens=r.response_len, temperature=1.0)
+                                          for r in reqs])
+
+        def ev():
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            return e
+
+        def step(s):
+            reqs = rollout_requests(wl, s, rank=rank, prompts=args.prompts_per_gpu)
+            e0 = ev()
+            res = asyncio.run(rollout(reqs))
+            e1 = ev()
+            trajs = []
+            for r, g in zip(reqs, res):
+                ids = tok.convert_tokens_to_ids([t.strip() for t in g["tokens"]])
+                trajs.append(rollout_trajectory(r, [int(i) for i in ids], [float(x or 0.0) for x in g["logprobs"]],
+                                                s, pin=True))
+            group_normalize(trajs)
+            train.recompute_logprobs(trajs)
+            train.grpo_update(trajs)
+            e2 = ev()
+            # the reference's disk weight sync: rank 0 writes v<step>/ (FSDP full state dict), every
+            # instance reloads it in place through the reference's worker extension
+            train.save_weights(sync_root, s + 1)
+            barrier(world)
+            _post_json(f"http://127.0.0.1:{port}/collective_rpc",
+                       {"method": "reload_weights", "args": [os.path.join(sync_root, f"v{s + 1}")]})
+            _post_json(f"http://127.0.0.1:{port}/reset_prefix_cache", {})
+            barrier(world)
+            e3 = ev()
+            return sum(int(t["input_ids"].numel()) for t in trajs), (e0, e1, e2, e3)
+
+        for s in range(args.warmup):
+            step(s)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        sampler = ClockSampler(local).start()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        tokens, marks = 0, []
+        for s in range(args.warmup, n_steps):
+            n, m = step(s)
+            tokens += n
+            marks.append(m)
+        t1.record()
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        clocks = sampler.stop()
+        ms_step = max_over_ranks(t0.elapsed_time(t1) / args.steps, dev)
+        phase = {k: max_over_ranks(sum(m[i].elapsed_time(m[i + 1]) for m in marks) / args.steps, dev)
+                 for i, k in enumerate(("rollout", "train", "weight_sync"))}
+        tokens_step = sum_over_ranks(tokens / args.steps, dev)
+        rec = base_record(args, world, "reference")
+        rec["config"]["step"] = ("rollout (vLLM 0.22 server through RL_Framework VLLMRolloutEngine) + "
+                                 "FSDPTrainEngine.recompute_logprobs + grpo_update + save_weights + in-place reload")
+        rec["config"]["reference_engine"] = "FSDPTrainEngine (Megatron-Core is not installable offline)"
+        rec.update({"value": tokens_step / (ms_step / 1e3), "ms_per_step": ms_step, "tokens_per_step": tokens_step,
+                    "phase_ms": phase, "weight_sync": {"ms": phase["weight_sync"]}, "clocks": clocks,
+                    "gpu_launches": 0,
+                    "e2e": {"value": tokens_step / (ms_step / 1e3), "unit": "tokens/s",
+                            "api": "RL_Framework VLLMRolloutEngine.generate + FSDPTrainEngine"}})
+        emit(rank, rec)
+    finally:
+        try:
+            os.killpg(proc.pid, signal.SIGTERM)
+            proc.wait(timeout=60)
+        except Exception:  # noqa: BLE001 - the server may already be gone
+            pass
+
+
 def main():
     args = parse_args()
     rank, world, local = setup_dist(args.gpus)
@@ -308,9 +562,9 @@ def main():
             emit(rank, {"impl": args.impl, "unavailable": "no CUDA device"})
             return
         if args.impl == "reference":
-            run_reference(args, rank, world, local)
+            run_reference_grpo(args, rank, world, local) if args.mode == "grpo" else run_reference(args, rank, world, local)
         else:
-            run_ours(args, rank, world, local)
+            run_ours_grpo(args, rank, world, local) if args.mode == "grpo" else run_ours(args, rank, world, local)
     finally:
         if world > 1 and dist.is_initialized():
             dist.destroy_process_group()

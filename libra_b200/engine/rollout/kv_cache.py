@@ -151,6 +151,19 @@ class PagedKVCache:
             sb.hashes.append(h)
             self.alloc.register(sb.blocks[i], h)
 
+    def commit_block(self, seq_id: str, num_tokens: int, block_tokens: List[int]) -> None:
+        """Decode-path commit: ``num_tokens`` tokens now have KV; when that
+        completes a block, ``block_tokens`` are its tokens and it is published
+        to the prefix cache (same hash chain as ``commit``)."""
+        sb = self.seqs[seq_id]
+        sb.num_tokens = num_tokens
+        bs = self.block_size
+        if num_tokens % bs == 0 and len(sb.hashes) == num_tokens // bs - 1:
+            parent = sb.hashes[-1] if sb.hashes else ""
+            h = _block_hash(parent, block_tokens)
+            sb.hashes.append(h)
+            self.alloc.register(sb.blocks[len(sb.hashes) - 1], h)
+
     def free(self, seq_id: str) -> None:
         sb = self.seqs.pop(seq_id, None)
         if sb:

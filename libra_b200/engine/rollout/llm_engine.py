@@ -31,6 +31,7 @@ from typing import Deque, Dict, List, Optional
 
 import torch
 
+from libra_b200 import ops
 from libra_b200.engine.rollout.kv_cache import PagedKVCache
 from libra_b200.engine.rollout.runner import InferenceRunner, WorkItem
 from libra_b200.engine.rollout.sampler import SamplingParams, sample
@@ -62,23 +63,38 @@ class _Request:
     generator: Optional[torch.Generator] = None
     t_arrive: float = field(default_factory=time.perf_counter)
     t_first: float = 0.0
+    seed: int = 0             # sampler key of the captured decode path
 
     @property
     def tokens(self) -> List[int]:
         return self.prompt + self.out
+
+    @property
+    def n_tokens(self) -> int:
+        return len(self.prompt) + len(self.out)
+
+    def token_slice(self, a: int, b: int) -> List[int]:
+        P = len(self.prompt)
+        if b <= P:
+            return self.prompt[a:b]
+        if a >= P:
+            return self.out[a - P:b - P]
+        return self.prompt[a:] + self.out[:b - P]
 
 
 class LLMEngine:
     def __init__(self, cfg: Qwen3Config, params: Dict[str, torch.Tensor], *, kv_blocks: int = 0,
                  block_size: int = 16, kv_memory_fraction: float = 0.5, max_batch_tokens: int = 8192,
                  max_running: int = 256, max_model_len: int = 0, instance_id: str = "", tp_group=None,
-                 tp_size: int = 1, eos_token_id: Optional[int] = None, tp_channel=None):
+                 tp_size: int = 1, eos_token_id: Optional[int] = None, tp_channel=None,
+                 flat: Optional[torch.Tensor] = None):
         """``tp_size > 1``: one engine per TP rank.  TP rank 0 (the driver)
         schedules, samples and serves; the other ranks run ``follower_loop``
         and replay, step by step, the driver's KV-cache operations and model
         steps, which it broadcasts over ``tp_channel`` (a gloo group)."""
         self.cfg = cfg
         self.params = params
+        self.flat = flat  # optional single buffer that every parameter views (one-copy weight sync)
         self.device = next(iter(params.values())).device
         self.instance_id = instance_id or f"engine-{uuid.uuid4().hex[:6]}"
         nkv = max(1, cfg.num_key_value_heads // tp_size)
@@ -119,6 +135,10 @@ class LLMEngine:
             self._tp_src = dist.get_global_rank(tp_channel, 0) if tp_channel is not None else 0
         self._kv_ops: List[tuple] = []  # KV-cache calls the followers must replay, in order
         self.tp_reload_hook = None  # follower side: callable(request) -> (params, version)
+        self.block_size = block_size
+        self._graphs = None          # DecodeGraphs, built at the first pure-decode step
+        self._graphs_ok = (self.device.type == "cuda" and tp_size == 1 and not cfg.is_moe and cfg.head_dim == 128)
+        self._seed_rng = torch.Generator().manual_seed(int(uuid.uuid4().int & 0x7FFFFFFF))
 
     # ------------------------------------------------------------------ tensor-parallel replay
     def _kv_call(self, op: str, *args):
@@ -177,6 +197,8 @@ class LLMEngine:
             gen.manual_seed(int(params.seed))
         req = _Request(rid, list(int(t) for t in prompt_tokens), params, future=future, loop=loop, callback=callback,
                        generator=gen)
+        req.seed = int(params.seed) if params.seed is not None else int(
+            torch.randint(0, 2 ** 62, (1,), generator=self._seed_rng))
         with self._lock:
             self.waiting.append(req)
             self._idle.clear()
@@ -191,11 +213,15 @@ class LLMEngine:
         self.add_request(prompt_tokens, params or SamplingParams(), request_id, future=fut, loop=loop)
         return await fut
 
-    def generate_sync(self, prompts: List[List[int]], params: Optional[SamplingParams] = None) -> List[GenerationResult]:
-        """Blocking batch generation on the calling thread (no background loop)."""
+    def generate_sync(self, prompts: List[List[int]], params=None) -> List[GenerationResult]:
+        """Blocking batch generation on the calling thread (no background loop).
+        ``params``: one ``SamplingParams`` for every prompt, or a list with one per prompt."""
         results: Dict[str, GenerationResult] = {}
-        ids = [self.add_request(p, params or SamplingParams(), callback=lambda r: results.__setitem__(r.request_id, r))
-               for p in prompts]
+        plist = params if isinstance(params, (list, tuple)) else [params] * len(prompts)
+        if len(plist) != len(prompts):
+            raise ValueError("generate_sync: one SamplingParams per prompt")
+        ids = [self.add_request(p, sp or SamplingParams(), callback=lambda r: results.__setitem__(r.request_id, r))
+               for p, sp in zip(prompts, plist)]
         while len(results) < len(ids):
             self.step()
         return [results[i] for i in ids]
@@ -281,12 +307,35 @@ class LLMEngine:
             else:
                 self.params = new_params
                 self.runner.p = new_params
+                self._graphs = None  # the captured steps read the old buffers
             self._kv_call("clear_cache")
             if version is not None:
                 self.version = int(version)
         finally:
             if not was_paused:
                 self.resume()
+
+    @torch.no_grad()
+    def load_flat_weights(self, src_flat: torch.Tensor, version: Optional[int] = None) -> float:
+        """Weight sync from a trainer that keeps its parameters in one flat bf16
+        buffer with this engine's layout: a single device copy (an NVLink peer
+        copy when ``src_flat`` lives on another GPU).  Returns seconds."""
+        if self.flat is None or self.flat.numel() != src_flat.numel():
+            raise ValueError("load_flat_weights needs an engine built on a flat buffer of the trainer's layout")
+        t0 = time.perf_counter()
+        was_paused = self._paused.is_set()
+        self.pause()
+        try:
+            self.flat.copy_(src_flat, non_blocking=True)
+            if self.device.type == "cuda":
+                torch.cuda.current_stream(self.device).synchronize()
+            self._kv_call("clear_cache")
+            if version is not None:
+                self.version = int(version)
+        finally:
+            if not was_paused:
+                self.resume()
+        return time.perf_counter() - t0
 
     # ------------------------------------------------------------------ scheduling
     def _admit(self) -> List[_Request]:
@@ -311,10 +360,57 @@ class LLMEngine:
                 budget -= need
         return admitted
 
+    def _graph_runner(self):
+        if self._graphs is None and self._graphs_ok:
+            from libra_b200.engine.rollout.decode_graph import DecodeGraphs, graphs_enabled
+
+            if not graphs_enabled():
+                self._graphs_ok = False
+                return None
+            self._graphs = DecodeGraphs(self.runner, max_batch=self.max_running, max_model_len=self.max_model_len)
+            self._graphs.capture()
+        return self._graphs
+
+    def _decode_step_graph(self, decode: List[_Request], t0: float) -> int:
+        """Pure-decode step through the captured graphs (plain temperature sampling)."""
+        g = self._graph_runner()
+        bs = self.block_size
+        for i, r in enumerate(decode):
+            L = r.cached + 1
+            self.kv.reserve(r.request_id, L)
+            g.set_row(i, r.request_id, r.out[-1], L, r.params.temperature, r.seed)
+        with nvtx.nvtx_range("decode"):
+            toks, lps = g.run(len(decode))
+        now = time.perf_counter()
+        self.stats["decode_tokens"] += len(decode)
+        done = False
+        for r, t, lp in zip(decode, toks, lps):
+            L = r.cached + 1
+            r.cached = L
+            self.kv.commit_block(r.request_id, L, r.token_slice(L - bs, L) if L % bs == 0 else [])
+            r.out.append(t)
+            r.logprobs.append(lp)
+            if not r.t_first:
+                r.t_first = now
+            reason = self._stop_reason(r, t)
+            if reason:
+                self._finish(r, reason)
+                r.cached = -1
+                done = True
+        if done:
+            self.running = [r for r in self.running if r.cached >= 0]
+        self.stats["steps"] += 1
+        self.stats["busy_s"] += time.perf_counter() - t0
+        return len(decode)
+
     def step(self) -> int:
         t0 = time.perf_counter()
         admitted = self._admit()
-        decode = [r for r in self.running if r.cached == len(r.tokens) - 1]
+        decode = [r for r in self.running if r.cached == r.n_tokens - 1]
+        if (not admitted and decode and self._graphs_ok and len(decode) <= self.max_running
+                and all(r.params.top_p >= 1.0 and r.params.top_k <= 0 for r in decode)
+                and self._graph_runner() is not None):
+            return self._decode_step_graph(decode, t0)
         batch = admitted + decode
         if not batch:
             return 0
@@ -323,10 +419,18 @@ class LLMEngine:
         with nvtx.nvtx_range("prefill" if admitted else "decode"):
             logits = self.runner.step(items)
         temps = torch.tensor([r.params.temperature for r in batch], device=logits.device, dtype=torch.float32)
-        top_p = torch.tensor([r.params.top_p for r in batch], device=logits.device, dtype=torch.float32)
-        top_k = torch.tensor([r.params.top_k for r in batch], device=logits.device, dtype=torch.long)
-        gens = [r.generator for r in batch] if any(r.generator is not None for r in batch) else None
-        toks, lps = sample(logits, temps, top_p, top_k, gens)
+        if logits.device.type == "cuda" and all(r.params.top_p >= 1.0 and r.params.top_k <= 0 for r in batch):
+            # the fused sampler (same Philox stream as the captured decode steps)
+            seeds = torch.tensor([r.seed for r in batch], dtype=torch.long).to(logits.device, non_blocking=True)
+            pos = torch.tensor([r.n_tokens - 1 for r in batch], dtype=torch.long).to(logits.device, non_blocking=True)
+            toks = torch.empty(len(batch), dtype=torch.long, device=logits.device)
+            lps = torch.empty(len(batch), dtype=torch.float32, device=logits.device)
+            ops.sample_tokens(logits.contiguous(), temps, seeds, pos, toks, lps)
+        else:
+            top_p = torch.tensor([r.params.top_p for r in batch], device=logits.device, dtype=torch.float32)
+            top_k = torch.tensor([r.params.top_k for r in batch], device=logits.device, dtype=torch.long)
+            gens = [r.generator for r in batch] if any(r.generator is not None for r in batch) else None
+            toks, lps = sample(logits, temps, top_p, top_k, gens)
         toks, lps = toks.tolist(), lps.tolist()
         now = time.perf_counter()
         self.stats["prefill_tokens"] += sum(len(r.tokens) - r.cached for r in admitted)
@@ -354,7 +458,7 @@ class LLMEngine:
             return "stop"
         if len(r.out) >= r.params.max_tokens:
             return "length"
-        if len(r.tokens) >= self.max_model_len:
+        if r.n_tokens >= self.max_model_len:
             return "length"
         return ""
 

@@ -373,6 +373,60 @@ def lm_head_logprob(h, w, targets, temperature: float = 1.0, entropy_out=None):
 
 
 # ---------------------------------------------------------------------------
+# rollout: paged decode attention and sampling
+# ---------------------------------------------------------------------------
+
+def paged_decode(q, k_cache, v_cache, block_tables, seq_lens, out, part_out, part_ml, split_len: int,
+                 scale: float):
+    """Decode attention of one new token per sequence over the paged cache.
+
+    ``out`` [B, Hq, D] and the split workspace ``part_out`` [>=B, Hq, S, D] /
+    ``part_ml`` [>=B, Hq, S, 2] (fp32) are the caller's; ``S * split_len``
+    must cover the longest sequence.  Nothing is allocated, so the call can sit
+    inside a captured CUDA graph."""
+    if q.device.type != "cuda":
+        B, Hq, D = q.shape
+        Hkv, bs = k_cache.shape[2], k_cache.shape[1]
+        for b in range(B):
+            L = int(seq_lens[b])
+            idx = torch.arange(L)
+            blocks = block_tables[b, idx // bs].long()
+            k = k_cache[blocks, idx % bs].float()          # [L, Hkv, D]
+            v = v_cache[blocks, idx % bs].float()
+            kk = k.repeat_interleave(Hq // Hkv, 1)           # [L, Hq, D]
+            vv = v.repeat_interleave(Hq // Hkv, 1)
+            s = torch.einsum("hd,lhd->hl", q[b].float(), kk) * scale
+            out[b] = torch.einsum("hl,lhd->hd", s.softmax(-1), vv).to(out.dtype)
+        return out
+    ext().paged_decode_v2(q, k_cache, v_cache, block_tables, seq_lens, out, part_out, part_ml, int(split_len),
+                          float(scale))
+    return out
+
+
+def sample_tokens(logits, temperature, seeds, positions, out_tok, out_lp, next_tok=None):
+    """Temperature sampling (Gumbel-max over a Philox stream keyed by the
+    request seed and counted by position) with the sampled token's logprob.
+    ``temperature <= 0`` is greedy.  Writes ``out_tok`` (int64) / ``out_lp``."""
+    if logits.device.type != "cuda":
+        B = logits.shape[0]
+        for b in range(B):
+            t = float(temperature[b])
+            x = logits[b].float() / (t if t > 0 else 1.0)
+            if t > 0:
+                g = torch.Generator().manual_seed((int(seeds[b]) * 1000003 + int(positions[b])) & 0x7FFFFFFF)
+                tok = int(torch.multinomial(x.softmax(-1), 1, generator=g))
+            else:
+                tok = int(x.argmax())
+            out_tok[b] = tok
+            out_lp[b] = x.log_softmax(-1)[tok]
+            if next_tok is not None:
+                next_tok[b] = tok
+        return out_tok, out_lp
+    ext().sample_tokens(logits, temperature, seeds, positions, out_tok, out_lp, next_tok)
+    return out_tok, out_lp
+
+
+# ---------------------------------------------------------------------------
 # optimizer
 # ---------------------------------------------------------------------------
 
@@ -406,4 +460,5 @@ def grad_sq_norm(grad, out):
 __all__ = [
     "ext", "extension_available", "check_kernel_errors", "gemm", "linear", "rmsnorm", "qk_norm_rope", "swiglu",
     "varlen_causal_attention", "lm_head_logprob", "adamw_step", "grad_sq_norm", "ref", "linear_swiglu",
+    "paged_decode", "sample_tokens",
 ]

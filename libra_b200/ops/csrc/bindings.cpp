@@ -40,6 +40,13 @@ torch::Tensor paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, tor
                                      double scale);
 void gemm_swiglu(torch::Tensor x, torch::Tensor w, torch::Tensor a, c10::optional<torch::Tensor> gu,
                  torch::Tensor err);
+namespace rollout {
+void paged_decode_v2(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
+                     torch::Tensor seq_lens, torch::Tensor out, torch::Tensor part_out, torch::Tensor part_ml,
+                     int64_t split_len, double scale);
+void sample_tokens(torch::Tensor logits, torch::Tensor temperature, torch::Tensor seeds, torch::Tensor positions,
+                   torch::Tensor out_tok, torch::Tensor out_lp, c10::optional<torch::Tensor> next_tok);
+}  // namespace rollout
 namespace attn {
 std::vector<torch::Tensor> flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor cu_seqlens,
                                      torch::Tensor tiles, double scale, bool causal, torch::Tensor err,
@@ -90,6 +97,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step_allgather", &libra::adamw_step_allgather,
         "AdamW on this rank's shard with the bf16 result stored into every rank's parameter buffer");
   m.def("paged_decode_attention", &libra::paged_decode_attention);
+  m.def("paged_decode_v2", &libra::rollout::paged_decode_v2,
+        "paged decode attention with caller-owned split workspace (graph-capturable)");
+  m.def("sample_tokens", &libra::rollout::sample_tokens,
+        "Gumbel-max temperature sampling with the sampled token's logprob", py::arg("logits"), py::arg("temperature"),
+        py::arg("seeds"), py::arg("positions"), py::arg("out_tok"), py::arg("out_lp"), py::arg("next_tok") = py::none());
   m.def("flash_fwd", &libra::attn::flash_fwd, "tcgen05 varlen GQA attention forward", py::arg("q"), py::arg("k"),
         py::arg("v"), py::arg("cu_seqlens"), py::arg("tiles"), py::arg("scale"), py::arg("causal"), py::arg("err"),
         py::arg("cu_k") = py::none());

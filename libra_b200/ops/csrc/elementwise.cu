@@ -308,7 +308,7 @@ static int sm_count() {
 torch::Tensor swiglu_fwd(torch::Tensor gu) {
   LIBRA_CHECK(gu.is_cuda() && gu.scalar_type() == at::kBFloat16 && gu.is_contiguous(), "swiglu_fwd: bf16 contiguous");
   const int F = (int)(gu.size(-1) / 2);
-  LIBRA_CHECK(F % 8 == 0, "swiglu_fwd: F % 8");
+  LIBRA_CHECK(F % 8 == 0, "swiglu_fwd: F %% 8 == 0 required");
   const int64_t T = gu.numel() / (2 * F);
   const c10::cuda::CUDAGuard guard(gu.device());
   auto sizes = gu.sizes().vec();
@@ -339,7 +339,7 @@ std::vector<torch::Tensor> logprob_fwd(torch::Tensor logits, torch::Tensor targe
                                        double temperature, bool with_entropy) {
   LIBRA_CHECK(logits.is_cuda() && logits.scalar_type() == at::kBFloat16 && logits.dim() == 2 && logits.stride(1) == 1,
               "logprob_fwd: 2-D bf16 logits");
-  LIBRA_CHECK(logits.stride(0) % 8 == 0 && targets.scalar_type() == at::kLong, "logprob_fwd: ld % 8, int64 targets");
+  LIBRA_CHECK(logits.stride(0) % 8 == 0 && targets.scalar_type() == at::kLong, "logprob_fwd: ld %% 8 == 0 and int64 targets required");
   const int R = (int)logits.size(0), V = (int)logits.size(1);
   const c10::cuda::CUDAGuard guard(logits.device());
   auto opts = logits.options().dtype(at::kFloat);

@@ -83,6 +83,55 @@ class GRPOWorkload:
         return out
 
 
+@dataclass
+class RolloutRequest:
+    """One GRPO sample to generate: the group's prompt, the response length to
+    generate (the workload's length distribution; generation ignores stop
+    tokens) and its Bernoulli reward."""
+
+    group_id: str
+    rollout_index: int
+    prompt: List[int]
+    response_len: int
+    reward: float
+
+
+def rollout_requests(wl: GRPOWorkload, step: int, rank: int = 0, prompts: Optional[int] = None) -> List[RolloutRequest]:
+    """The generation side of a synthetic GRPO step: ``prompts`` x group size
+    requests with the workload's prompt/response length distributions."""
+    n_prompts = wl.prompts_per_step if prompts is None else prompts
+    rng = np.random.default_rng([wl.seed, rank, step, 17])
+    plens = wl.prompt.sample(rng, n_prompts)
+    out: List[RolloutRequest] = []
+    for p in range(n_prompts):
+        prompt = rng.integers(wl.token_lo, wl.vocab_size, size=int(plens[p])).tolist()
+        rlens = wl.response.sample(rng, wl.group_size)
+        rewards = (rng.random(wl.group_size) < wl.reward_p).astype(np.float32)
+        for g in range(wl.group_size):
+            out.append(RolloutRequest(f"r{rank}:s{step}:p{p}", g, prompt, max(1, int(rlens[g])), float(rewards[g])))
+    return out
+
+
+def rollout_trajectory(req: RolloutRequest, output_tokens: List[int], output_logprobs: List[float], version: int,
+                       pin: bool = False) -> Dict[str, torch.Tensor]:
+    """Trajectory dict (reference schema) from a generated response."""
+    P, R = len(req.prompt), len(output_tokens)
+    ids = torch.tensor(req.prompt + list(output_tokens), dtype=torch.long).view(1, -1)
+    mask = torch.zeros(1, P + R, dtype=torch.float32)
+    mask[:, P:] = 1.0
+    lps = torch.zeros(1, P + R, dtype=torch.float32)
+    if R:
+        lps[0, P:] = torch.tensor(output_logprobs, dtype=torch.float32)
+    traj = {"input_ids": ids, "attention_mask": torch.ones(1, P + R, dtype=torch.long), "loss_mask": mask,
+            "logprobs": lps, "rewards": torch.tensor([req.reward]), "grpo_group_id": req.group_id,
+            "rollout_index": req.rollout_index, "version": version, "prompt_len": P, "output_len": R}
+    if pin:
+        for k, v in list(traj.items()):
+            if isinstance(v, torch.Tensor):
+                traj[k] = v.pin_memory()
+    return traj
+
+
 def group_normalize(trajectories: List[Dict]) -> None:
     """GRPO advantages: (r - mean) / (std + 1e-6) per group; zero-variance -> 0;
     singleton groups keep the raw reward (reference

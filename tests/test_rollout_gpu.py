@@ -61,3 +61,133 @@ def test_engine_greedy_matches_naive_on_gpu():
             toks.append(int(logits[-1].float().argmax()))
         agree += sum(a == b for a, b in zip(r.output_tokens, toks[len(p):]))
     assert agree >= 0.9 * 24  # bf16 ties may flip a late token
+
+
+def _paged_case(lens, G, Hkv=2, bs=16, seed=0):
+    torch.manual_seed(seed)
+    D = 128
+    nblk = sum(-(-L // bs) for L in lens) + 4
+    kc = torch.randn(nblk, bs, Hkv, D, device="cuda").bfloat16()
+    vc = torch.randn(nblk, bs, Hkv, D, device="cuda").bfloat16()
+    perm = torch.randperm(nblk).tolist()
+    tables, cur = [], 0
+    for L in lens:
+        n = -(-L // bs)
+        tables.append(perm[cur:cur + n])
+        cur += n
+    return kc, vc, tables
+
+
+@pytest.mark.parametrize("G,lens,split", [(4, [1, 17, 300, 2049], 512), (8, [5, 64, 1000], 256), (1, [33], 512),
+                                          (2, [700, 1], 128), (5, [129, 700], 512)])
+def test_paged_decode_v2_matches_reference(G, lens, split):
+    """Fixed-split decode kernel (the one the captured decode step uses) against fp32 attention."""
+    from libra_b200 import ops
+    from libra_b200.engine.rollout.runner import _extend_attention_ref
+
+    Hkv, D, bs = 2, 128, 16
+    kc, vc, tables = _paged_case(lens, G, Hkv, bs)
+    B, Hq = len(lens), G * Hkv
+    max_len = 2100
+    width = -(-max_len // bs)
+    bt = torch.zeros(B, width, dtype=torch.int32)
+    for i, t in enumerate(tables):
+        bt[i, :len(t)] = torch.tensor(t)
+    S = -(-max_len // split)
+    q = torch.randn(B, Hq, D, device="cuda").bfloat16()
+    out = torch.empty_like(q)
+    po = torch.empty(B, Hq, S, D, device="cuda")
+    pml = torch.empty(B, Hq, S, 2, device="cuda")
+    ops.paged_decode(q, kc, vc, bt.cuda(), torch.tensor(lens, dtype=torch.int32).cuda(), out, po, pml, split,
+                     1.0 / math.sqrt(D))
+    torch.cuda.synchronize()
+    for i, L in enumerate(lens):
+        slots = torch.tensor([tables[i][p // bs] * bs + p % bs for p in range(L)], device="cuda")
+        k = kc.view(-1, Hkv, D).index_select(0, slots)
+        v = vc.view(-1, Hkv, D).index_select(0, slots)
+        ref = _extend_attention_ref(q[i:i + 1], k, v, L - 1)
+        err = (out[i].float() - ref[0].float()).abs().max().item()
+        assert err < 2e-2, (G, L, err)
+
+
+def test_sample_tokens_greedy_logprob_and_distribution():
+    from libra_b200 import ops
+
+    torch.manual_seed(1)
+    B, V = 6, 151936
+    logits = (torch.randn(B, V, device="cuda") * 3).bfloat16()
+    temp = torch.tensor([0.0, 1.0, 0.7, 1.3, 0.0, 1.0], device="cuda")
+    seeds = torch.arange(B, dtype=torch.long, device="cuda") * 7919
+    pos = torch.arange(B, dtype=torch.long, device="cuda") + 100
+    tok = torch.empty(B, dtype=torch.long, device="cuda")
+    lp = torch.empty(B, dtype=torch.float32, device="cuda")
+    ops.sample_tokens(logits, temp, seeds, pos, tok, lp)
+    x = logits.float()
+    assert int(tok[0]) == int(x[0].argmax()) and int(tok[4]) == int(x[4].argmax())
+    t = torch.where(temp > 0, temp, torch.ones_like(temp)).unsqueeze(1)
+    ref_lp = torch.log_softmax(x / t, -1).gather(1, tok.unsqueeze(1)).squeeze(1)
+    assert torch.allclose(lp, ref_lp, atol=2e-3), (lp, ref_lp)
+    # same seed and position -> same token; another position -> an independent draw
+    tok2, lp2 = torch.empty_like(tok), torch.empty_like(lp)
+    ops.sample_tokens(logits, temp, seeds, pos, tok2, lp2)
+    assert torch.equal(tok, tok2)
+    # empirical distribution over many positions matches softmax on a small vocabulary
+    V2, N = 16, 20000
+    small = torch.randn(V2, device="cuda").bfloat16()
+    rows = small.unsqueeze(0).expand(N, V2).contiguous()
+    tN = torch.full((N,), 1.0, device="cuda")
+    sN = torch.full((N,), 12345, dtype=torch.long, device="cuda")
+    pN = torch.arange(N, dtype=torch.long, device="cuda")
+    oT, oL = torch.empty(N, dtype=torch.long, device="cuda"), torch.empty(N, device="cuda")
+    ops.sample_tokens(rows, tN, sN, pN, oT, oL)
+    freq = torch.bincount(oT, minlength=V2).float() / N
+    prob = torch.softmax(small.float(), -1)
+    assert (freq - prob).abs().max().item() < 0.015, (freq, prob)
+
+
+def test_decode_graphs_match_eager_steps(monkeypatch):
+    """Greedy generation through the captured decode graphs equals the eager path token for token."""
+    from libra_b200.engine.rollout.llm_engine import LLMEngine
+    from libra_b200.engine.rollout.sampler import SamplingParams
+    from libra_b200.engine.train_engine import B200TrainEngine
+
+    eng = B200TrainEngine("tiny-gpu", device="cuda", seed=5)
+    eng.initialize()
+    prompts = [list(range(5, 45)), [7, 8, 9], list(range(100, 400)), list(range(3, 20))]
+    params = [SamplingParams(max_tokens=n, temperature=0.0) for n in (40, 7, 25, 33)]
+
+    def run(graphs: bool):
+        monkeypatch.setenv("LIBRA_DECODE_GRAPHS", "1" if graphs else "0")
+        llm = LLMEngine(eng.cfg, eng.params, kv_blocks=512, block_size=16, max_model_len=1024, max_running=64)
+        res = {}
+        ids = [llm.add_request(p, sp, callback=lambda r: res.__setitem__(r.request_id, r))
+               for p, sp in zip(prompts, params)]
+        while len(res) < len(ids):
+            llm.step()
+        return [res[i] for i in ids], llm
+
+    eager, _ = run(False)
+    graph, llm = run(True)
+    assert llm._graphs is not None and llm._graphs.replays > 0
+    for a, b in zip(eager, graph):
+        assert a.output_tokens == b.output_tokens
+        assert max(abs(x - y) for x, y in zip(a.output_logprobs, b.output_logprobs)) < 1e-2
+
+
+def test_decode_graphs_seeded_sampling_is_batch_independent(monkeypatch):
+    """A seeded request draws the same tokens alone or inside a larger batch."""
+    from libra_b200.engine.rollout.llm_engine import LLMEngine
+    from libra_b200.engine.rollout.sampler import SamplingParams
+    from libra_b200.engine.train_engine import B200TrainEngine
+
+    monkeypatch.setenv("LIBRA_DECODE_GRAPHS", "1")
+    eng = B200TrainEngine("tiny-gpu", device="cuda", seed=6)
+    eng.initialize()
+    p = SamplingParams(max_tokens=20, temperature=1.0, seed=99)
+    alone = LLMEngine(eng.cfg, eng.params, kv_blocks=512, block_size=16, max_model_len=512, max_running=32)
+    a = alone.generate_sync([list(range(10, 30))], p)[0]
+    crowd = LLMEngine(eng.cfg, eng.params, kv_blocks=512, block_size=16, max_model_len=512, max_running=32)
+    others = [list(range(50 + i, 70 + i)) for i in range(5)]
+    res = crowd.generate_sync(others[:2] + [list(range(10, 30))] + others[2:],
+                              SamplingParams(max_tokens=20, temperature=1.0, seed=99))
+    assert res[2].output_tokens == a.output_tokens

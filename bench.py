@@ -304,6 +304,7 @@ def run_ours_grpo(args, rank, world, local):
         n, _, _ = count_launches(lambda: grpo_step(n_steps), prefixes=("libra::",))
         launches = int(max_over_ranks(n, dev)) * args.steps
     sync_bytes = rollout_flat.numel() * rollout_flat.element_size()
+    e2e = None if args.no_e2e else grpo_e2e_through_trainer(args, rank, world, local, eng, llm, wl)
     rec = base_record(args, world, "ours")
     rec["config"]["step"] = ("rollout (own engine, captured decode graphs, temperature 1.0) + logprob recompute + "
                              "GRPO update + weight sync to the rollout engine")
@@ -315,8 +316,65 @@ def run_ours_grpo(args, rank, world, local):
                 "weight_sync": {"ms": max_over_ranks(sync, dev), "bytes": sync_bytes,
                                 "gb_per_s": sync_bytes / (max_over_ranks(sync, dev) / 1e3) / 1e9,
                                 "path": "device copy of the flat bf16 parameter buffer into the rollout engine"},
-                "gpu_launches": launches, "clocks": clocks})
+                "gpu_launches": launches, "clocks": clocks, "e2e": e2e})
     emit(rank, rec)
+
+
+def grpo_e2e_through_trainer(args, rank, world, local, eng, llm, wl):
+    """The same GRPO workload end to end through the public orchestrator:
+    ``AsyncRLTrainer.train`` with the colocated rollout engine (each rank
+    generates its data-parallel share, staleness bound 1), logprob recompute,
+    update and weight sync every step.  Timed between step boundaries on every
+    rank (synchronize + barrier), max over ranks; counts the host<->device bytes
+    of the rollout engine (prompts, decode inputs, sampled tokens) and of the
+    trainer (trajectories in, stats out)."""
+    from libra_b200.config import AsyncRLConfig
+    from libra_b200.engine.rollout_engine import LocalRolloutEngine
+    from libra_b200.engine.tokenizer import ByteTokenizer
+    from libra_b200.trainer.async_rl_trainer import AsyncRLTrainer
+    from libra_b200.utils.timing import max_over_ranks, sum_over_ranks
+    from libra_b200.workflow.synthetic import rollout_requests
+    from libra_b200.workflow.synthetic_workflows import GRPOLengthWorkflow, grpo_length_dataset
+
+    dev = torch.device("cuda", local)
+    warm, steps = max(3, min(args.warmup, 3)), max(2, args.steps // 4)
+    reqs = []
+    for i in range(warm + steps + 1):
+        reqs += rollout_requests(wl, 5000 + i, rank=0, prompts=args.prompts_per_gpu * world)
+    dataset = grpo_length_dataset(reqs)
+    tmp = os.path.join("/tmp", f"libra_e2e_{os.getpid()}")
+    cfg = AsyncRLConfig.from_dict({
+        "model_path": args.model, "rollout_backend": "colocated", "train_gpus": world, "rollout_gpus": 0,
+        "train_tp_size": 1, "batch_size": args.prompts_per_gpu * args.group * world, "n_samples": args.group,
+        "micro_batch_size": args.micro_batch, "max_concurrent_rollouts": args.max_running,
+        "max_head_offpolicyness": 1, "total_steps": warm + steps, "sync_interval": 1, "recompute_logprobs": True,
+        "max_seq_length": wl.prompt.hi + wl.response.hi + 16, "enable_history_collection": False,
+        "log_dir": tmp + "/logs", "sync_path": tmp + "/sync", "save_interval": 0, "eval_interval": 0,
+        "global_resource_planner": {"enabled": False}, "heterogeneous_rollout": {"enabled": False}})
+    io0 = dict(llm.io_bytes)
+    eng.io_bytes = {"h2d": 0, "d2h": 0}
+    trainer = AsyncRLTrainer(cfg, train_engine=eng, rollout_engine=LocalRolloutEngine(llm, ByteTokenizer(eng.cfg.vocab_size)))
+    marks = {}
+
+    def on_step(step, stats, batch):
+        if step == warm - 1 or step == warm + steps - 1:
+            torch.cuda.synchronize(dev)
+            barrier(world)
+            marks[step] = (time.perf_counter(), dict(llm.io_bytes), dict(eng.io_bytes))
+        if step >= warm:
+            marks.setdefault("tokens", 0)
+            marks["tokens"] += sum(int(t["input_ids"].numel()) for t in batch)
+
+    trainer.step_callback = on_step
+    trainer.train(GRPOLengthWorkflow(), dataset)
+    (t0, r0, e0), (t1, r1, e1) = marks[warm - 1], marks[warm + steps - 1]
+    ms = max_over_ranks((t1 - t0) * 1e3 / steps, dev)
+    tokens = sum_over_ranks(marks["tokens"] / steps, dev)
+    h2d = (r1["h2d"] - r0["h2d"] + e1["h2d"] - e0["h2d"]) / steps
+    d2h = (r1["d2h"] - r0["d2h"] + e1["d2h"] - e0["d2h"]) / steps
+    return {"value": tokens / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps, "warmup": warm,
+            "h2d_bytes_per_step": int(max_over_ranks(h2d, dev)), "d2h_bytes_per_step": int(max_over_ranks(d2h, dev)),
+            "api": "AsyncRLTrainer.train (rollout_backend=colocated, staleness bound 1, sync every step)"}
 
 
 # ---------------------------------------------------------------------- reference

@@ -666,50 +666,55 @@ class AsyncRLConfig:
         if self.rollout_weight_sync_poll_interval_s <= 0:
             raise ValueError("rollout_weight_sync_poll_interval_s must be greater than zero")
 
-    def _validate_backend(self) -> None:
-        if self.train_backend == "megatron3d" and self.weight_sync_mode != "disk":
-            raise ValueError("The legacy Megatron backend supports only weight_sync_mode='disk'")
-        if self.train_backend != "megatron_core":
-            return
-        if self.weight_sync_mode == "nccl" and self.rollout_weight_sync_mode != "nccl":
-            raise ValueError("weight_sync_mode='nccl' requires rollout_weight_sync_mode='nccl'")
-        if not 0.0 <= self.megatron_optimizer_offload_fraction <= 1.0:
-            raise ValueError("megatron_optimizer_offload_fraction must be between 0 and 1")
-        if self.megatron_optimizer_offload_fraction > 0.0 and not self.megatron_optimizer_cpu_offload:
-            raise ValueError(
-                "megatron_optimizer_offload_fraction requires megatron_optimizer_cpu_offload=true"
-            )
-        if self.train_pp_size != 1:
-            raise ValueError("MegatronCoreTrainEngine currently requires train_pp_size=1")
-        if self.train_ep_size <= 0:
-            raise ValueError("train_ep_size must be greater than zero")
-        if self.expert_tensor_parallel_size <= 0:
-            raise ValueError("expert_tensor_parallel_size must be greater than zero")
-        if self.train_tp_size % self.expert_tensor_parallel_size:
-            raise ValueError(
-                "expert_tensor_parallel_size must divide train_tp_size: "
-                f"{self.expert_tensor_parallel_size} vs {self.train_tp_size}"
-            )
-        if self.train_dp_size % self.train_ep_size:
-            raise ValueError(
-                f"train_ep_size must divide train_dp_size: {self.train_ep_size} vs {self.train_dp_size}"
-            )
+    def _engine_constraints(self):
+        """(holds, message) pairs: what the native training engine can run.
+
+        Every ``train_backend`` value selects the same engine, so the rules
+        are the engine's: tensor parallelism must divide the heads, the FFN
+        and the vocabulary; experts are spread over expert-parallel ranks
+        inside the data-parallel group; one pipeline stage and one context
+        shard per rank; checkpoints in the ``torch_dist`` layout."""
         arch = self.model_arch
-        if arch.num_experts > 1:
-            if arch.num_experts % self.train_ep_size:
-                raise ValueError(
-                    f"num_experts must be divisible by train_ep_size: {arch.num_experts} vs {self.train_ep_size}"
-                )
-            if arch.expert_intermediate_size % self.expert_tensor_parallel_size:
-                raise ValueError(
-                    "expert_intermediate_size must be divisible by expert_tensor_parallel_size"
-                )
-        if not self.megatron_use_transformer_engine and self.train_cp_size != 1:
-            raise ValueError("PyTorch SDPA attention requires train_cp_size=1")
-        if self.megatron_checkpoint_format != "torch_dist":
-            raise ValueError(
-                "Megatron-Core integration currently requires megatron_checkpoint_format='torch_dist'"
-            )
+        tp, ep = self.train_tp_size, self.train_ep_size
+        heads, kv = arch.n_heads, arch.n_kv_heads
+        yield (self.train_pp_size == 1,
+               f"train_pp_size={self.train_pp_size}: the native engine keeps every layer on each rank "
+               "(pipeline stages are only available through libra_b200.parallel.pipeline)")
+        yield (self.train_cp_size == 1,
+               f"train_cp_size={self.train_cp_size}: sequences are not split across ranks; long contexts run as "
+               "packed variable-length attention on one rank")
+        yield (heads % tp == 0 and (kv % tp == 0 or tp % kv == 0),
+               f"train_tp_size={tp} must divide num_attention_heads={heads} and divide or be a multiple of "
+               f"num_key_value_heads={kv}")
+        yield (arch.intermediate_size % tp == 0 and arch.vocab_size % tp == 0,
+               f"train_tp_size={tp} must divide intermediate_size={arch.intermediate_size} and "
+               f"vocab_size={arch.vocab_size}")
+        yield ep >= 1 and self.expert_tensor_parallel_size >= 1, "train_ep_size and expert_tensor_parallel_size must be >= 1"
+        yield (self.expert_tensor_parallel_size == 1,
+               f"expert_tensor_parallel_size={self.expert_tensor_parallel_size}: each expert lives whole on one "
+               "expert-parallel rank")
+        if ep > 1:
+            yield arch.num_experts > 1, f"train_ep_size={ep} needs a mixture-of-experts model (num_experts > 1)"
+            yield (arch.num_experts % ep == 0,
+                   f"num_experts={arch.num_experts} must split evenly over train_ep_size={ep}")
+            yield (self.train_dp_size % ep == 0,
+                   f"train_ep_size={ep} must divide the data-parallel size {self.train_dp_size} (experts are "
+                   "exchanged inside the data-parallel group)")
+        yield (0.0 <= self.megatron_optimizer_offload_fraction <= 1.0,
+               "megatron_optimizer_offload_fraction must lie in [0, 1]")
+        yield (not self.megatron_optimizer_cpu_offload and self.megatron_optimizer_offload_fraction == 0.0,
+               "optimizer CPU offload is not used: the optimizer state stays in HBM (180 GB per GPU)")
+        yield (self.megatron_checkpoint_format == "torch_dist",
+               f"megatron_checkpoint_format={self.megatron_checkpoint_format!r}: checkpoints are written as "
+               "torch_dist (DCP) directories")
+        yield (not (self.weight_sync_mode == "nccl" and self.rollout_weight_sync_mode not in ("nccl", "none")),
+               "weight_sync_mode='nccl' pushes weights straight into the rollout engines; pair it with "
+               "rollout_weight_sync_mode='nccl'")
+
+    def _validate_backend(self) -> None:
+        for holds, message in self._engine_constraints():
+            if not holds:
+                raise ValueError(message)
 
     def _fill_derived(self) -> None:
         for directory in (self.sync_path, self.log_dir):

@@ -86,6 +86,7 @@ class DecodeGraphs:
         self.graphs: Dict[int, torch.cuda.CUDAGraph] = {}
         self.pool = None
         self.replays = 0
+        self.io_bytes = {"h2d": 0, "d2h": 0}
 
     # ------------------------------------------------------------------ forward recorded in the graphs
     def _forward(self, b: int) -> None:
@@ -186,6 +187,8 @@ class DecodeGraphs:
             for i in range(n, b):
                 self._row_owner[i] = None
         self._upload(b)
+        self.io_bytes["h2d"] += b * (4 * 8 + 2 * 4 + 4 + 4 * self.max_blocks)
+        self.io_bytes["d2h"] += n * 12
         self.graphs[b].replay()
         self.replays += 1
         self.h_out_tok[:n].copy_(self.out_tok[:n], non_blocking=True)

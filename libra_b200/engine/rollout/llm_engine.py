@@ -124,6 +124,7 @@ class LLMEngine:
         self.version = 0
         self.stats = {"steps": 0, "prefill_tokens": 0, "decode_tokens": 0, "cached_prefix_tokens": 0,
                       "finished": 0, "busy_s": 0.0}
+        self._eager_io = {"h2d": 0, "d2h": 0}  # host<->device bytes of the eager (prefill/extend) steps
         self._ids = itertools.count()
         self.tp_size, self.tp_group, self.tp_channel = tp_size, tp_group, tp_channel
         self.tp_rank = 0
@@ -288,8 +289,9 @@ class LLMEngine:
     # ------------------------------------------------------------------ weights
     @torch.no_grad()
     def update_weights(self, new_params: Dict[str, torch.Tensor], version: Optional[int] = None,
-                       copy: bool = True, reload_request: Optional[Dict] = None) -> None:
-        """Install new weights between steps (copy into the existing buffers, or rebind).
+                       copy: bool = True, reload_request: Optional[Dict] = None, apply=None) -> None:
+        """Install new weights between steps (copy into the existing buffers, or rebind;
+        ``apply()``, when given, writes the buffers in place while the engine is paused).
 
         With TP, ``reload_request`` is forwarded to the followers, which load
         their own shards through ``tp_reload_hook``; the driver's loop is paused
@@ -299,6 +301,8 @@ class LLMEngine:
         try:
             if self.tp_size > 1 and reload_request is not None:
                 self._publish(reload=reload_request)
+            if apply is not None:  # caller-supplied in-place writer (peer reshard into the live buffers)
+                apply()
             if copy:
                 for k, v in new_params.items():
                     self.params[k].copy_(v, non_blocking=True)
@@ -432,6 +436,9 @@ class LLMEngine:
             gens = [r.generator for r in batch] if any(r.generator is not None for r in batch) else None
             toks, lps = sample(logits, temps, top_p, top_k, gens)
         toks, lps = toks.tolist(), lps.tolist()
+        n_new = sum(r.n_tokens - r.cached for r in batch)
+        self._eager_io["h2d"] += 28 * n_new + 32 * len(batch)  # tokens, positions, slots, rows, sampler inputs
+        self._eager_io["d2h"] += 12 * len(batch)
         now = time.perf_counter()
         self.stats["prefill_tokens"] += sum(len(r.tokens) - r.cached for r in admitted)
         self.stats["decode_tokens"] += len(decode)
@@ -474,5 +481,11 @@ class LLMEngine:
             r.loop.call_soon_threadsafe(lambda f=r.future, x=res: f.done() or f.set_result(x))
 
     # ------------------------------------------------------------------ introspection
+    @property
+    def io_bytes(self) -> Dict[str, int]:
+        """Host<->device bytes moved by this engine's steps so far."""
+        g = self._graphs.io_bytes if self._graphs is not None else {"h2d": 0, "d2h": 0}
+        return {k: self._eager_io[k] + g[k] for k in ("h2d", "d2h")}
+
     def load(self) -> Dict[str, float]:
         return {"running": len(self.running), "waiting": len(self.waiting), "kv_usage": self.kv.usage()}

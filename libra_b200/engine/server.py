@@ -11,9 +11,11 @@ Routes (the reference serves the same ones from a patched vLLM API server,
 * ``POST /reload_weights`` ``{"checkpoint_path": dir, "version": v}`` - load a
   checkpoint written by the trainer (disk weight sync), under a lock, then drop
   the prefix cache.
-* ``POST /reload_weights_peer`` ``{"handles": ..., "version": v}`` - map the
-  trainer's exported device buffers (CUDA IPC) and copy/reshard them in place
-  (peer-memory weight sync).
+* ``POST /reload_weights_peer`` ``{"src_tp": k, "sources": [...], "version": v}``
+  - map the trainer ranks' exported flat weight buffers (JSON descriptions of
+  CUDA IPC handles, no pickled objects) and reshard this rank's slice into the
+  served weights in place with the ``weight_reshard`` kernel (peer-memory
+  weight sync).
 
     python -m libra_b200.engine.server --model qwen3-4b --device cuda:4 --port 8000
 """
@@ -83,10 +85,15 @@ def build_app(engine, tokenizer, model_name: str = "libra", weight_loader=None) 
         async with reload_lock:
             t0 = time.perf_counter()
             req = dict(body, kind=kind)
-            params, version = await asyncio.get_running_loop().run_in_executor(None, weight_loader, req)
-            if params:
-                await asyncio.get_running_loop().run_in_executor(
-                    None, lambda: engine.update_weights(params, version, reload_request=req))
+            loop = asyncio.get_running_loop()
+            if kind == "peer":
+                # in-place reshard into the live weight buffers: runs while the engine is paused
+                await loop.run_in_executor(None, lambda: engine.update_weights(
+                    {}, req.get("version"), reload_request=req, apply=lambda: weight_loader(req)))
+            else:
+                params, version = await loop.run_in_executor(None, weight_loader, req)
+                if params:
+                    await loop.run_in_executor(None, lambda: engine.update_weights(params, version, reload_request=req))
             return web.json_response({"status": "ok", "version": engine.version, "seconds": time.perf_counter() - t0})
 
     app.router.add_get("/health", health)
@@ -203,7 +210,9 @@ def main(argv=None) -> None:
             return load_disk(req["checkpoint_path"]), req.get("version")
         from libra_b200.infra.sync.peer_weight_sync import receive_peer_weights
 
-        return receive_peer_weights(req, holder.params), req.get("version")
+        # this rank's slice for its own TP degree and rank, written in place into the served weights
+        receive_peer_weights(req, holder.flat_param, holder.cfg, a.tp, holder.tp_rank)
+        return {}, req.get("version")
 
     if rank > 0:
         llm.tp_reload_hook = loader

@@ -76,7 +76,8 @@ class B200TrainEngine:
                  device: Optional[torch.device] = None, seed: int = 0, recompute_activations: bool = False,
                  use_distributed_optimizer: bool = True, dp_group=None, temperature: float = 1.0,
                  max_grad_norm: float = 1.0, tp_size: int = 1, model_path: str = "",
-                 max_tokens_per_micro_batch: int = 16384, max_tokens_per_recompute_batch: int = 65536):
+                 max_tokens_per_micro_batch: int = 16384, max_tokens_per_recompute_batch: int = 65536,
+                 ep_size: int = 1):
         self.cfg: Qwen3Config = get_config(model)
         self.model_path = model_path
         self.optim = OptimConfig(lr=learning_rate, max_grad_norm=max_grad_norm)
@@ -91,6 +92,9 @@ class B200TrainEngine:
         self.use_distributed_optimizer = use_distributed_optimizer
         self.temperature = temperature
         self.tp_size = tp_size
+        self.ep_size = max(1, int(ep_size))
+        if self.ep_size > 1 and not self.cfg.is_moe:
+            raise ValueError(f"ep_size={self.ep_size} needs a mixture-of-experts model")
         self.current_version = 0
         self.step_count = 0
         self.dp_group = dp_group
@@ -369,8 +373,16 @@ class B200TrainEngine:
             return {"loss_sum": acc}
         rewards = [mb["rewards"] for mb in device_micro_batches if "rewards" in mb]
         r = torch.cat(rewards) if rewards else torch.zeros(0, device=self.device)
-        vals = torch.cat([acc, r.sum().reshape(1).float(), self.sq_norm]).tolist()
+        parts = [acc, r.sum().reshape(1).float(), self.sq_norm]
+        if self.device.type == "cuda":
+            # the error word rides along with the stats read: a bounded wait that gave up inside this step
+            # (the fused parameter gather waits on its peers) surfaces here, before the next forward
+            parts.append(ops.error_flag(self.device)[:1].float())
+        vals = torch.cat(parts).tolist()
         self.io_bytes["d2h"] += 4 * len(vals)
+        if self.device.type == "cuda" and vals[-1] != 0:
+            ops.error_flag(self.device)[0].zero_()
+            raise ops.KernelError(int(vals[-1]), f"{self.device} (GRPO update)")
         out = {"loss": vals[0], "pg_loss": vals[1], "kl": vals[2], "reward_sum": vals[3],
                "n_samples": float(r.numel()), "n_updates": 1.0, "reward_mean": vals[3] / max(r.numel(), 1),
                "grad_norm": math.sqrt(max(vals[4], 0.0))}
@@ -662,6 +674,9 @@ def create_train_engine(config) -> B200TrainEngine:
 
     Every ``train_backend`` value maps onto the native engine; the model preset
     is taken from ``model_path`` when it names a preset, else from model_arch.
+    The parallel layout comes from the config: ``train_tp_size`` (tensor
+    parallel groups of consecutive ranks) and ``train_ep_size`` (experts spread
+    over that many data-parallel ranks).
     """
     name = os.path.basename(str(config.model_path)).lower()
     try:
@@ -670,8 +685,12 @@ def create_train_engine(config) -> B200TrainEngine:
         from libra_b200.models.qwen3 import config_from_arch
 
         cfg = config_from_arch(config.model_arch)
+    if int(getattr(config, "train_pp_size", 1)) != 1:
+        raise ValueError("the native engine runs with train_pp_size=1")
     return B200TrainEngine(model=cfg, learning_rate=config.learning_rate, kl_coef=config.kl_coef,
                            clip_epsilon=config.clip_epsilon, micro_batch_size=config.micro_batch_size,
                            recompute_micro_batch_size=config.recompute_micro_batch_size, seed=config.seed,
                            use_distributed_optimizer=config.use_distributed_optimizer,
-                           temperature=config.temperature, model_path=config.model_path)
+                           temperature=config.temperature, model_path=config.model_path,
+                           tp_size=int(getattr(config, "train_tp_size", 1) or 1),
+                           ep_size=int(getattr(config, "train_ep_size", 1) or 1))

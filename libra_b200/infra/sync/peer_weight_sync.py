@@ -1,132 +1,114 @@
 """Peer-memory weight sync: trainer shards -> rollout instance buffers over NVLink.
 
-The trainer keeps its parameters in one flat bf16 buffer; ``export_handle``
-wraps it in a CUDA IPC handle (plus the parameter layout).  A rollout process
-on the same box ``open_handle``s it - the mapping is a peer view of the
-trainer GPU's memory - and ``copy_resharded`` copies, for every parameter, the
-slice its tensor-parallel rank owns into its local buffers; the copies run on
-the copy engines over NVLink, there is no host staging and no full-tensor
-broadcast (the reference broadcasts whole HF tensors from trainer rank 0
-through a separate NCCL communicator, ``infra/sync/nccl_weight_sync.py``).
+Every trainer tensor-parallel rank keeps its parameters in one flat bf16
+buffer.  ``publish`` (collective over the trainer's TP group) describes those
+buffers as plain JSON — base64 CUDA IPC handle, byte offset, dtype, element
+count, device — so the request can cross an HTTP hop without pickled objects.
+A rollout rank maps the buffers into its own GPU context and runs the
+``weight_reshard`` kernel with the copy plan for its (TP degree, rank): each
+piece of its slice is read once from the trainer rank that owns it, over
+NVLink, and written straight into its flat weight buffer (the reference
+gathers full tensors on trainer rank 0 and broadcasts them through a separate
+NCCL communicator, ``infra/sync/nccl_weight_sync.py:126-197``).
 
-TP slicing rules (column-parallel along output rows, row-parallel along input
-columns, vocabulary split for the embedding / LM head) are the ones of
-``models.qwen3.param_shapes``.
+Plans and mappings are cached, so a steady-state sync is one kernel launch.
 """
 
 from __future__ import annotations
 
-import base64
-import pickle
 import time
-from typing import Any, Dict, Optional, Tuple
+from typing import Any, Dict, List, Optional, Sequence, Tuple
 
 import torch
+import torch.distributed as dist
 
-from libra_b200.models.qwen3 import ParamLayout, Qwen3Config, param_shapes
+from libra_b200.infra.sync.reshard import DeviceReshard, apply_plan, build_plan, export_buffer, open_buffer
+from libra_b200.models.qwen3 import Qwen3Config
 
-COLUMN = ("qkv_proj", "gate_up_proj", "experts.w1", "embed_tokens", "lm_head", "router")
-ROW = ("o_proj", "down_proj", "experts.w2")
-
-
-def export_handle(flat: torch.Tensor, layout: ParamLayout, cfg: Qwen3Config, version: int) -> Dict[str, Any]:
-    """Serialisable description of the trainer's flat buffer (CUDA IPC)."""
-    from torch.multiprocessing.reductions import reduce_tensor
-
-    fn, args = reduce_tensor(flat)
-    blob = base64.b64encode(pickle.dumps((fn, args))).decode()
-    return {"ipc": blob, "layout": {n: list(s) for n, s in layout.shapes.items()}, "order": layout.order,
-            "offsets": layout.offsets, "cfg": cfg.to_dict(), "version": int(version), "numel": flat.numel()}
+_PLANS: Dict[Tuple, DeviceReshard] = {}
 
 
-def open_handle(handle: Dict[str, Any]) -> torch.Tensor:
-    fn, args = pickle.loads(base64.b64decode(handle["ipc"]))
-    return fn(*args)
+def publish(engine, group=None) -> Dict[str, Any]:
+    """Trainer side (collective over the TP group): the JSON request every
+    rollout rank needs to pull its slice of the current weights."""
+    mine = export_buffer(engine.flat_param)
+    tp = int(getattr(engine, "tp_size", 1))
+    group = group if group is not None else getattr(engine, "tp_group", None)
+    if tp > 1:
+        sources: List[Any] = [None] * tp
+        dist.all_gather_object(sources, mine, group=group)
+    else:
+        sources = [mine]
+    return {"kind": "peer", "src_tp": tp, "sources": sources, "cfg": engine.cfg.to_dict(),
+            "version": int(engine.get_version())}
 
 
-def tp_slice(name: str, full: torch.Tensor, cfg: Qwen3Config, tp: int, rank: int) -> torch.Tensor:
-    """The part of a full (TP=1) parameter that rank ``rank`` of a TP group owns."""
-    if tp == 1:
-        return full
-    base = name.split(".", 2)[-1] if name.startswith("layers.") else name
-    if base == "qkv_proj":
-        D, nq, nkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
-        q, k, v = full[:nq * D], full[nq * D:(nq + nkv) * D], full[(nq + nkv) * D:]
-        nq_l = nq // tp
-        kv_l = max(1, nkv // tp)
-        kv_rank = rank * nkv // tp if nkv >= tp else rank * nkv // tp
-        return torch.cat([q[rank * nq_l * D:(rank + 1) * nq_l * D],
-                          k[kv_rank * D:(kv_rank + kv_l) * D], v[kv_rank * D:(kv_rank + kv_l) * D]])
-    if base in ("gate_up_proj",):
-        F = full.shape[0] // 2
-        Fl = F // tp
-        return torch.cat([full[rank * Fl:(rank + 1) * Fl], full[F + rank * Fl:F + (rank + 1) * Fl]])
-    if base == "experts.w1":
-        F = full.shape[1] // 2
-        Fl = F // tp
-        return torch.cat([full[:, rank * Fl:(rank + 1) * Fl], full[:, F + rank * Fl:F + (rank + 1) * Fl]], dim=1)
-    if base in ("embed_tokens", "lm_head"):
-        Vl = full.shape[0] // tp
-        return full[rank * Vl:(rank + 1) * Vl]
-    if base in ("o_proj", "down_proj"):
-        C = full.shape[1] // tp
-        return full[:, rank * C:(rank + 1) * C]
-    if base == "experts.w2":
-        C = full.shape[2] // tp
-        return full[:, :, rank * C:(rank + 1) * C]
-    return full  # norms, router: replicated
+def _validate(request: Dict[str, Any]) -> None:
+    src = request.get("sources")
+    if not isinstance(src, list) or not src or not isinstance(request.get("src_tp"), int) \
+            or len(src) != request["src_tp"]:
+        raise ValueError("peer weight request needs 'src_tp' and one source description per trainer TP rank")
+    for d in src:
+        if not isinstance(d, dict) or d.get("dtype") not in ("bfloat16", "float32"):
+            raise ValueError("peer weight sources must be bf16 or fp32 buffer descriptions")
 
 
-def copy_resharded(src_flat: torch.Tensor, handle: Dict[str, Any], dst: Dict[str, torch.Tensor], tp: int = 1,
-                   rank: int = 0) -> int:
-    """Copy every parameter's TP slice from the trainer's flat buffer into ``dst``; returns bytes moved."""
-    cfg = Qwen3Config(**handle["cfg"])
-    moved = 0
-    with torch.no_grad():
-        for name in handle["order"]:
-            if name not in dst:
-                continue
-            shape = tuple(handle["layout"][name])
-            off = int(handle["offsets"][name])
-            n = 1
-            for s in shape:
-                n *= s
-            full = src_flat[off:off + n].view(shape)
-            part = tp_slice(name, full, cfg, tp, rank)
-            dst[name].copy_(part, non_blocking=True)
-            moved += part.numel() * part.element_size()
+def receive_peer_weights(request: Dict[str, Any], dst_flat: torch.Tensor, cfg: Qwen3Config, tp: int = 1,
+                         rank: int = 0) -> int:
+    """Rollout side: reshard the published trainer buffers into ``dst_flat``
+    (this rank's flat bf16 weights, TP degree ``tp``).  Returns bytes written."""
+    _validate(request)
+    dev = dst_flat.device
+    addrs = [open_buffer(d, dev) for d in request["sources"]]
+    esz = [4 if d["dtype"] == "float32" else 2 for d in request["sources"]]
+    key = (tuple(addrs), int(dst_flat.data_ptr()), int(request["src_tp"]), int(tp), int(rank))
+    plan = _PLANS.get(key)
+    if plan is None:
+        plan = DeviceReshard(cfg, int(request["src_tp"]), tp, rank, addrs, dst_flat, esz)
+        _PLANS[key] = plan
+    with torch.cuda.device(dev):
+        moved = plan.run()
+        torch.cuda.current_stream(dev).synchronize()
     return moved
 
 
-def receive_peer_weights(request: Dict[str, Any], holder_params: Dict[str, torch.Tensor],
-                         tp: int = 1, rank: int = 0) -> Dict[str, torch.Tensor]:
-    """Server-side entry: map the trainer's buffer and pull into a fresh copy of the holder's params."""
-    src = open_handle(request["handle"])
-    params = {k: torch.empty_like(v) for k, v in holder_params.items()}
-    copy_resharded(src, request["handle"], params, tp, rank)
-    torch.cuda.synchronize()
-    return params
-
-
 class PeerWeightSync:
-    """Trainer side: publish the flat buffer handle; in-process consumers copy directly."""
+    """Trainer side of the peer path, plus the in-process variant for rollout
+    engines that live in the trainer's processes."""
 
     def __init__(self, **_):
         self.last_seconds = 0.0
         self.last_bytes = 0
 
     def publish(self, engine) -> Dict[str, Any]:
-        return export_handle(engine.flat_param, engine.layout, engine.cfg, engine.get_version())
+        return publish(engine)
 
-    def push_local(self, engine, targets, tp: int = 1) -> Tuple[float, int]:
-        """Copy into in-process targets: list of (param dict, tp_rank)."""
+    def push_local(self, engine, targets: Sequence[Tuple[torch.Tensor, int, int]]) -> Tuple[float, int]:
+        """Reshard this trainer rank's weights into in-process targets, given as
+        (flat bf16 buffer, TP degree, TP rank); sources and targets must be
+        reachable from the target's GPU (the same GPU, or peer access)."""
         t0 = time.perf_counter()
-        handle = {"layout": {n: list(s) for n, s in engine.layout.shapes.items()}, "order": engine.layout.order,
-                  "offsets": engine.layout.offsets, "cfg": engine.cfg.to_dict()}
         moved = 0
-        for params, r in targets:
-            moved += copy_resharded(engine.flat_param, handle, params, tp, r)
+        tp = int(getattr(engine, "tp_size", 1))
+        if tp != 1:
+            raise ValueError("push_local reads one trainer shard; use publish() for a TP-sharded trainer")
+        for flat, dst_tp, dst_rank in targets:
+            if flat.is_cuda:
+                key = ((int(engine.flat_param.data_ptr()),), int(flat.data_ptr()), 1, int(dst_tp), int(dst_rank))
+                plan = _PLANS.get(key)
+                if plan is None:
+                    plan = DeviceReshard(engine.cfg, 1, dst_tp, dst_rank, [int(engine.flat_param.data_ptr())], flat)
+                    _PLANS[key] = plan
+                moved += plan.run()
+            else:
+                rects = build_plan(engine.cfg, 1, dst_tp, dst_rank)
+                apply_plan(rects, [engine.flat_param], flat)
+                moved += sum(r.rows * r.row_elems for r in rects) * 2
         if engine.flat_param.is_cuda:
             torch.cuda.synchronize()
         self.last_seconds, self.last_bytes = time.perf_counter() - t0, moved
         return self.last_seconds, moved
+
+
+def clear_plans() -> None:
+    _PLANS.clear()

@@ -53,25 +53,49 @@ def extension_available() -> bool:
         return False
 
 
+ERROR_NAMES = {1: "timeout: TMA tile", 2: "timeout: shared-memory stage", 3: "timeout: TMEM full",
+               4: "timeout: TMEM empty", 5: "timeout: peer flag", 6: "bad argument", 7: "timeout: attention Q",
+               8: "timeout: attention K/V", 9: "timeout: attention S", 10: "timeout: attention P",
+               11: "timeout: attention PV", 12: "timeout: attention O", 13: "timeout: CTA-pair exit"}
+TIMEOUT_PEER_FLAG = 5
+
+
+class KernelError(RuntimeError):
+    """A kernel of this library gave up a bounded wait (or rejected an argument) on the device."""
+
+    def __init__(self, code: int, where: str):
+        self.code = int(code)
+        super().__init__(f"libra_b200 kernel reported error code {code} ({ERROR_NAMES.get(code, 'unknown')}) "
+                         f"on {where}")
+
+
 def error_flag(device: torch.device) -> torch.Tensor:
-    """Per-device int32 word that kernels set when a bounded wait gives up."""
+    """Per-device int32[4] error word handed to every kernel: [0] receives the
+    code of the first bounded wait that gave up; [1] > 0 overrides the wait
+    budget (milliseconds)."""
     key = (device.type, device.index)
     flag = _ERR.get(key)
     if flag is None:
-        flag = torch.zeros(1, dtype=torch.int32, device=device)
+        flag = torch.zeros(4, dtype=torch.int32, device=device)
         _ERR[key] = flag
     return flag
 
 
+def set_wait_limit_ms(device: torch.device, ms: int) -> None:
+    """Bound every wait of the kernels launched afterwards on ``device`` by ``ms``
+    milliseconds (0 restores the compiled-in default of 2 s)."""
+    error_flag(device)[1].fill_(int(ms))
+
+
 def check_kernel_errors(device: Optional[torch.device] = None) -> None:
-    """Raise if any kernel on ``device`` reported a timeout (forces a sync)."""
+    """Raise ``KernelError`` if any kernel on ``device`` reported an error (forces a sync)."""
     for (dtype, index), flag in list(_ERR.items()):
         if device is not None and (dtype, index) != (device.type, device.index):
             continue
-        code = int(flag.item())
+        code = int(flag[0].item())
         if code:
-            flag.zero_()
-            raise RuntimeError(f"libra_b200 kernel reported error code {code} on {dtype}:{index}")
+            flag[0].zero_()
+            raise KernelError(code, f"{dtype}:{index}")
 
 
 # ---------------------------------------------------------------------------

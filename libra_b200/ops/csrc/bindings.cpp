@@ -34,7 +34,7 @@ void adamw_step_allgather(torch::Tensor master, torch::Tensor grad, torch::Tenso
                           double beta1, double beta2, double eps, double wd, int64_t step,
                           c10::optional<torch::Tensor> sq_norm, double max_norm, double grad_scale,
                           std::vector<int64_t> param_peers, std::vector<int64_t> flag_peers, int64_t me, int64_t epoch,
-                          torch::Tensor err);
+                          torch::Tensor err, int64_t grid_ctas);
 torch::Tensor paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                                      torch::Tensor block_tables, torch::Tensor seq_lens, int64_t max_len,
                                      double scale);
@@ -47,6 +47,9 @@ void paged_decode_v2(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
 void sample_tokens(torch::Tensor logits, torch::Tensor temperature, torch::Tensor seeds, torch::Tensor positions,
                    torch::Tensor out_tok, torch::Tensor out_lp, c10::optional<torch::Tensor> next_tok);
 }  // namespace rollout
+namespace reshard {
+void weight_reshard(torch::Tensor items, int64_t grid);
+}  // namespace reshard
 namespace attn {
 std::vector<torch::Tensor> flash_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor cu_seqlens,
                                      torch::Tensor tiles, double scale, bool causal, torch::Tensor err,
@@ -97,6 +100,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step_allgather", &libra::adamw_step_allgather,
         "AdamW on this rank's shard with the bf16 result stored into every rank's parameter buffer");
   m.def("paged_decode_attention", &libra::paged_decode_attention);
+  m.def("weight_reshard", &libra::reshard::weight_reshard,
+        "trainer -> rollout weight sync: planned 2-D copies (peer sources over NVLink, fp32/bf16 -> bf16)");
   m.def("paged_decode_v2", &libra::rollout::paged_decode_v2,
         "paged decode attention with caller-owned split workspace (graph-capturable)");
   m.def("sample_tokens", &libra::rollout::sample_tokens,

@@ -1,9 +1,10 @@
 // Shared device helpers for the sm_100a kernels of libra_b200.
 //
 // Everything that waits (mbarrier phases, peer flags) goes through a bounded
-// wait: after LIBRA_WAIT_NS nanoseconds of %globaltimer the wait gives up,
-// records an error code in the caller-provided device word and returns false,
-// so no kernel of this library can spin forever.
+// wait: after LIBRA_WAIT_NS nanoseconds of %globaltimer (or the budget set in
+// the error word, see wait_budget_ns) the wait gives up, records an error code
+// in the caller-provided device word and returns false, so no kernel of this
+// library can spin forever.
 #pragma once
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -62,6 +63,18 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// Wait budget of the bounded waits.  The error word passed to every kernel is
+// an int32[4] array: [0] receives the error code, and [1], when positive,
+// overrides LIBRA_WAIT_NS with that many milliseconds (set by the host through
+// ops.set_wait_limit_ms; tests use it to make a wait run out in a few ms).
+__device__ __forceinline__ uint64_t wait_budget_ns(const int* err) {
+  if (err) {
+    const int ms = *((const volatile int*)err + 1);
+    if (ms > 0) return (uint64_t)ms * 1000000ull;
+  }
+  return LIBRA_WAIT_NS;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -107,7 +120,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   while (true) {
     if (mbar_try_wait(addr, parity)) return true;
     if ((++spins & 255u) == 0u) {
-      if (globaltimer_ns() - start > LIBRA_WAIT_NS) {
+      if (globaltimer_ns() - start > wait_budget_ns(err)) {
         if (err) atomicCAS(err, 0, code);
         return false;
       }
@@ -210,7 +223,7 @@ __device__ __forceinline__ bool wait_flag_geq(const int* flag, int target, int* 
   const uint64_t t0 = globaltimer_ns();
   uint32_t spins = 0;
   while (ld_acquire_sys(flag) < target) {
-    if ((++spins & 1023u) == 0u && globaltimer_ns() - t0 > LIBRA_WAIT_NS) {
+    if ((++spins & 1023u) == 0u && globaltimer_ns() - t0 > wait_budget_ns(err)) {
       if (err) atomicCAS(err, 0, code);
       return false;
     }

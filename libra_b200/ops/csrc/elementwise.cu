@@ -404,12 +404,13 @@ void adamw_step(torch::Tensor master, torch::Tensor grad, torch::Tensor m, torch
 
 // AdamW on this rank's shard, fused with the parameter all-gather: param_peers[r] is the address of this
 // rank's shard inside rank r's bf16 parameter buffer (mapped into this process), flag_peers[r] rank r's
-// int32 arrival counters.  Same grid on every rank; epoch counts the calls (1, 2, ...).
+// int32 arrival counters.  Same grid on every rank (grid_ctas > 0, agreed by the caller; 0 = 4 per SM);
+// epoch counts the calls (1, 2, ...).
 void adamw_step_allgather(torch::Tensor master, torch::Tensor grad, torch::Tensor m, torch::Tensor v, double lr,
                           double beta1, double beta2, double eps, double wd, int64_t step,
                           c10::optional<torch::Tensor> sq_norm, double max_norm, double grad_scale,
                           std::vector<int64_t> param_peers, std::vector<int64_t> flag_peers, int64_t me, int64_t epoch,
-                          torch::Tensor err) {
+                          torch::Tensor err, int64_t grid_ctas) {
   LIBRA_CHECK(master.scalar_type() == at::kFloat && grad.scalar_type() == at::kFloat && m.scalar_type() == at::kFloat &&
                   v.scalar_type() == at::kFloat,
               "adamw_step_allgather: fp32 master/grad/m/v");
@@ -427,7 +428,9 @@ void adamw_step_allgather(torch::Tensor master, torch::Tensor grad, torch::Tenso
     peers.param[r] = (uint64_t)param_peers[r];
     peers.flags[r] = (uint64_t)flag_peers[r];
   }
-  const int grid = sm_count() * 4;
+  // the arrival target is epoch * grid, so every rank must launch the same grid: callers agree on it
+  const int grid = grid_ctas > 0 ? (int)grid_ctas : sm_count() * 4;
+  LIBRA_CHECK(grid <= 65535, "adamw_step_allgather: grid of %d CTAs is too large", grid);
   LIBRA_CHECK(epoch >= 1 && epoch * grid < ((int64_t)1 << 31), "adamw_step_allgather: epoch out of range");
   peers.n = nr;
   peers.me = (int)me;

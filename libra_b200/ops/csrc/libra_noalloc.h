@@ -1,11 +1,13 @@
 // Allocation-free C entry points of libra_b200's CUDA library.
 //
 // libra_rmsnorm_bwd_noalloc has no counterpart in the reference framework; it
-// exists for callers that must not allocate device memory: C/C++ runtimes that
-// link the library without PyTorch (so there is no caching allocator to draw
-// from) and steps that run with the device at its memory limit (a recovery
-// path after an out-of-memory error), where cudaMalloc would fail or
-// implicitly synchronize the device.
+// exists for callers that must not allocate device memory: C or C++ code that
+// calls the kernel through this plain C symbol (dlopen of the extension module;
+// the module itself still links libtorch, so its shared libraries must be
+// loadable) from a context where neither PyTorch's caching allocator nor a
+// fresh cudaMalloc is acceptable, such as a step that runs with the device at
+// its memory limit (a recovery path after an out-of-memory error), where
+// cudaMalloc would fail or implicitly synchronize the device.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -26,7 +28,10 @@ extern "C" {
 // device array (file scope, one per device); the grid is capped at
 // floor(524288 / H) CTAs so they always fit.  The first call on each device
 // resolves that array's address (cudaGetSymbolAddress) with the device
-// current; make that first call before any stream capture.
+// current; make that first call before any stream capture.  The resolved
+// address is cached per device for the life of the process: after a
+// cudaDeviceReset the cache is stale and the entry point must not be called
+// again in that process.
 //
 // Calls whose kernels can overlap on the same device race on the shared
 // scratch: issue them on one stream, or order them with events.

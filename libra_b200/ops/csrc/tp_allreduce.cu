@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(kWarps * 32) allreduce_add_rmsnorm_kernel(
     const uint64_t t0 = globaltimer_ns();
     uint32_t spins = 0;
     while (ld_acquire_sys(mine) < epoch) {
-      if ((++spins & 1023u) == 0u && globaltimer_ns() - t0 > LIBRA_WAIT_NS) {
+      if ((++spins & 1023u) == 0u && globaltimer_ns() - t0 > wait_budget_ns(err)) {
         atomicCAS(err, 0, kTimeoutPeerFlag);
         s_ok = 0;
         break;

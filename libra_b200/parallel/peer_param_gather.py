@@ -64,6 +64,13 @@ class PeerParamGather:
         self.flag_peers = flag_bases
         self.shard_numel = int(shard_numel)
         self.calls = 0
+        # the kernel's arrival target is calls x grid, so all ranks launch the same grid: the smallest
+        # "4 CTAs per SM" of the group (ranks may sit on GPUs with different SM counts)
+        sms = torch.cuda.get_device_properties(flat_param.device).multi_processor_count
+        grid = torch.tensor([sms * 4], dtype=torch.int64, device=flat_param.device)
+        if self.n > 1:
+            dist.all_reduce(grid, op=dist.ReduceOp.MIN, group=self.group)
+        self.grid = int(grid.item())
         if self.n > 1:
             torch.cuda.synchronize(flat_param.device)
             dist.barrier(group=self.group)
@@ -78,10 +85,12 @@ class PeerParamGather:
         """AdamW on this rank's shard; afterwards every rank holds the full updated bf16 parameters."""
         if master.numel() != self.shard_numel:
             raise ValueError(f"shard has {self.shard_numel} elements, got {master.numel()}")
-        self.calls += 1
+        # the epoch advances only once the launch went through, so a rejected call on one rank does not
+        # leave its counters a step ahead of its peers'
         ops.ext().adamw_step_allgather(master, grad, exp_avg, exp_avg_sq, lr, beta1, beta2, eps, weight_decay, step,
                                        sq_norm, max_grad_norm, grad_scale, self.param_peers, self.flag_peers,
-                                       self.me, self.calls, ops.error_flag(master.device))
+                                       self.me, self.calls + 1, ops.error_flag(master.device), self.grid)
+        self.calls += 1
 
 
 def _bench(argv=None) -> None:

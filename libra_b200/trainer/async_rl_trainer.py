@@ -12,9 +12,12 @@ Single-box process model:
 * one trainer process per training GPU (torchrun); NCCL between training GPUs,
   gloo on CPU;
 * rollout instances are either in-process engines on the rollout GPUs owned by
-  rank 0 (``rollout_backend: native``), HTTP servers (``vllm`` / ``http``), or
-  mocks.  With in-process engines rank 0 is the only batch source: it collects
-  the global batch and scatters the data-parallel slices;
+  rank 0 (``rollout_backend: native``), one engine per training GPU sharing it
+  with that rank's trainer (``rollout_backend: colocated``: every rank
+  generates its own data-parallel slice and the weight sync is one device copy
+  of the flat parameter buffer), HTTP servers (``vllm`` / ``http``), or mocks.
+  With ``native`` engines rank 0 is the only batch source: it collects the
+  global batch and scatters the data-parallel slices;
 * weight sync for in-process engines is a device-to-device copy of the
   trainer's parameters into each instance's buffers (NVLink peer copies); for
   HTTP instances the trainer writes a versioned HF export and calls
@@ -110,6 +113,8 @@ class AsyncRLTrainer:
                                    world_size=self.world_size) if trace else None
         self._single_batch_source = False
         self._nvtx_open: Dict[Any, Optional[int]] = {}
+        # optional hook called at the end of every step: (step, stats, batch) on every rank
+        self.step_callback = None
 
     # ================================================================== setup
     def _trace(self, step: int, name: str, **details) -> None:
@@ -160,11 +165,46 @@ class AsyncRLTrainer:
         self._local_engines.append(llm)
         return LocalRolloutEngine(llm, tok)
 
+    def _make_colocated_engine(self) -> Any:
+        """Rollout engine on this rank's own GPU with its own copy of the trainer's
+        flat bf16 weights (same layout, so a weight sync is one device copy)."""
+        from libra_b200.engine.rollout.llm_engine import LLMEngine
+        from libra_b200.engine.rollout.kv_cache import PagedKVCache
+        from libra_b200.engine.rollout_engine import LocalRolloutEngine
+        from libra_b200.engine.tokenizer import load_tokenizer
+
+        eng = self.train_engine
+        if int(getattr(eng, "tp_size", 1)) != 1:
+            raise ValueError("rollout_backend='colocated' runs a full model per GPU: use train_tp_size=1")
+        c = self.config
+        flat = eng.flat_param.detach().clone()
+        cfg = eng.cfg
+        max_len = int(c.max_seq_length)
+        kv_blocks = 0
+        if flat.is_cuda:
+            free, _ = torch.cuda.mem_get_info(flat.device)
+            # the trainer shares this GPU: the KV cache takes at most ~45 % of what initialisation left free
+            frac = min(0.45, float(c.heterogeneous_rollout.gpu_memory_utilization) or 0.45)
+            budget = PagedKVCache.blocks_for_budget(free * frac, cfg.num_hidden_layers, 16, cfg.num_key_value_heads,
+                                                    cfg.head_dim)
+            need = int(c.max_concurrent_rollouts or 256) * -(-max_len // 16) + 64
+            kv_blocks = max(64, min(budget, need))
+        tok = load_tokenizer(c.tokenizer_path, cfg.vocab_size)
+        llm = LLMEngine(cfg, eng.layout.views(flat), kv_blocks=kv_blocks, block_size=16, max_model_len=max_len,
+                        max_running=max(1, min(512, int(c.max_concurrent_rollouts or 256))),
+                        instance_id=f"colocated-{self.rank}", flat=flat)
+        llm.version = eng.get_version()
+        self._local_engines.append(llm)
+        return LocalRolloutEngine(llm, tok)
+
     def _build_rollout_engine(self) -> None:
         from libra_b200.engine.heterogeneous_engine import HeterogeneousRolloutEngine
         from libra_b200.engine.rollout_engine import HTTPRolloutEngine, MockRolloutEngine, MultiInstanceRolloutEngine
 
         c = self.config
+        if c.rollout_backend == "colocated":
+            self.rollout_engine = self._make_colocated_engine()
+            return
         native = c.rollout_backend in ("native", "local")
         self._single_batch_source = native and self.world_size > 1
         if native and not self.is_main_process:
@@ -197,6 +237,12 @@ class AsyncRLTrainer:
         self.train_engine.set_version(self.initial_model_version)
         if self.rollout_engine is None:
             self._build_rollout_engine()
+        else:
+            from libra_b200.engine.rollout_engine import LocalRolloutEngine
+
+            if isinstance(self.rollout_engine, LocalRolloutEngine) and self.rollout_engine.engine not in \
+                    self._local_engines:
+                self._local_engines.append(self.rollout_engine.engine)  # weight sync targets it directly
         if self.rollout_engine is not None and hasattr(self.rollout_engine, "wait_for_ready"):
             self.rollout_engine.wait_for_ready(float(self.config.heterogeneous_rollout.startup_timeout))
         if self._is_batch_source():
@@ -325,10 +371,16 @@ class AsyncRLTrainer:
         """Push the trainer's weights to every rollout instance; returns seconds."""
         t0 = time.perf_counter()
         if self._local_engines:
-            # in-process instances: device-to-device copies (NVLink peer copies across GPUs)
-            src = {k: v.detach() for k, v in self.train_engine.params.items()}
+            # in-process instances: one copy of the flat buffer when the layouts match, else per tensor
+            # (device-to-device; NVLink peer copies across GPUs)
+            src_flat = getattr(self.train_engine, "flat_param", None)
+            src = None
             for llm in self._local_engines:
-                llm.update_weights(src, version=target_version)
+                if llm.flat is not None and src_flat is not None and llm.flat.numel() == src_flat.numel():
+                    llm.load_flat_weights(src_flat, version=target_version)
+                else:
+                    src = src or {k: v.detach() for k, v in self.train_engine.params.items()}
+                    llm.update_weights(src, version=target_version)
         elif self.config.rollout_backend not in ("mock",) and (
                 self.config.rollout_weight_sync_mode != "none" or self.config.require_rollout_weight_sync):
             self._sync_weights_disk(target_version)
@@ -434,6 +486,8 @@ class AsyncRLTrainer:
                     print(f"Step {step}/{c.total_steps}: {time.time() - t_start:.1f}s loss={stats.get('loss', 0):.4f} "
                           f"kl={stats.get('kl', 0):.4f} reward={stats['reward_mean']:.3f} "
                           f"n={len(batch)} rollout={rollout_time:.2f}s train={train_time:.2f}s", flush=True)
+            if self.step_callback is not None:
+                self.step_callback(step, stats, batch)
             self._run_periodic_evaluation(workflow, dataset, step)
             if c.save_interval > 0 and (step + 1) % c.save_interval == 0:
                 self._save_checkpoint(step)

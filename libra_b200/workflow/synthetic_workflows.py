@@ -79,6 +79,37 @@ class TargetTokenWorkflow:
                                        max_new_tokens, **kw)
 
 
+class GRPOLengthWorkflow:
+    """Single turn with prescribed response lengths: rollout ``i`` of a group
+    generates ``data["response_lens"][i]`` tokens at temperature 1.0 and gets
+    reward ``data["rewards"][i]`` (the synthetic GRPO benchmark workload:
+    random prompts, lognormal lengths, Bernoulli rewards)."""
+
+    def __init__(self, temperature: float = 1.0):
+        self.temperature = temperature
+
+    async def run_episode(self, engine, data: Dict[str, Any], version: int = 0, rollout_index: int = 0) -> Dict:
+        prompt = [int(t) for t in data["prompt_ids"]]
+        n = int(data["response_lens"][rollout_index % len(data["response_lens"])])
+        res = await engine.generate(prompt, max_new_tokens=n, temperature=self.temperature,
+                                    prompt_id=str(data.get("prompt_id", "")))
+        out = list(res.get("token_ids") or [])
+        reward = float(data["rewards"][rollout_index % len(data["rewards"])])
+        return make_trajectory(prompt, [(out, res.get("logprobs") or [0.0] * len(out))], reward, version,
+                               {"prompt_id": data.get("prompt_id", "")})
+
+
+def grpo_length_dataset(requests) -> List[Dict[str, Any]]:
+    """Group ``workflow.synthetic.rollout_requests`` output by prompt into dataset items."""
+    items: Dict[str, Dict[str, Any]] = {}
+    for r in requests:
+        it = items.setdefault(r.group_id, {"prompt_id": r.group_id, "prompt_ids": r.prompt, "response_lens": [],
+                                           "rewards": []})
+        it["response_lens"].append(r.response_len)
+        it["rewards"].append(r.reward)
+    return list(items.values())
+
+
 def target_token_dataset(n_prompts: int, vocab: int = 1024, lo: int = 16, hi: int = 48, seed: int = 0,
                          token_lo: int = 4) -> List[Dict[str, Any]]:
     rng = random.Random(seed)

@@ -31,10 +31,12 @@ def test_numeric_string_coercion():
     ({"batch_size": 30}, "batch_size must be divisible"),
     ({"weight_sync_mode": "foo"}, "weight_sync_mode"),
     ({"rollout_weight_sync_mode": "nccl"}, "requires weight_sync_mode"),
-    ({"train_pp_size": 2}, "train_pp_size=1"),
-    ({"train_cp_size": 2, "train_gpus": 8}, "train_cp_size=1"),
+    ({"train_pp_size": 2}, "train_pp_size=2: the native engine keeps every layer"),
+    ({"train_cp_size": 2, "train_gpus": 8}, "train_cp_size=2: sequences are not split"),
     ({"train_backend": "deepspeed"}, "train_backend"),
-    ({"megatron_optimizer_offload_fraction": 0.5}, "cpu_offload"),
+    ({"megatron_optimizer_offload_fraction": 0.5}, "optimizer CPU offload"),
+    ({"train_ep_size": 2, "train_gpus": 2}, "needs a mixture-of-experts model"),
+    ({"train_tp_size": 3, "train_gpus": 3, "batch_size": 3, "micro_batch_size": 1}, "train_tp_size=3 must divide"),
 ])
 def test_validation_errors(kw, msg, tmp_path):
     base = {"model_path": "m", "sync_path": str(tmp_path / "s"), "log_dir": str(tmp_path / "l")}

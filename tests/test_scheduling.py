@@ -1,6 +1,7 @@
 """Scheduler behaviour (reference tests/test_cmlfq_scheduler.py, test_hetero_cmlfq_integration.py)."""
 
 import json
+import os
 from types import SimpleNamespace
 
 import pytest
@@ -20,6 +21,8 @@ from libra_b200.infra.scheduling.cmlfq_tool_state import (DefaultToolStateExtrac
                                                           PayloadSizeClass, ToolReturnState)
 
 S = lambda t="code", size=PayloadSizeClass.SizeSmall, st=ExecutionStatus.ToolSuccess: ToolReturnState(t, size, st)  # noqa: E731
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def _register(s, tps=(1, 1, 2, 4, 8)):
@@ -145,18 +148,47 @@ def test_cmlfq_from_config_and_persistence(tmp_path, monkeypatch):
     assert s2.prefix_tree.get_stats()["total_insertions"] == 1
 
 
-def test_shared_load_ttl(tmp_path):
+def test_shared_load_live_rows(tmp_path):
+    import struct
+    import subprocess
+    import sys
+    import time
+
     a = SharedCMLFQLoadState(str(tmp_path), ttl_s=60, heartbeat_interval_s=10, writer_id="rank_0")
     b = SharedCMLFQLoadState(str(tmp_path), ttl_s=60, heartbeat_interval_s=10, writer_id="rank_1")
     a.increment("i0")
     b.increment("i0")
     b.increment("i1")
     assert a.aggregate() == {"i0": 2, "i1": 1}
-    stale = json.loads((tmp_path / "rank_1.json").read_text())
-    stale["updated_at"] -= 1000
-    b.close()
-    (tmp_path / "rank_1.json").write_text(json.dumps({**stale, "counts": {"i0": 5}}))
+    b.decrement("i1")
+    assert a.aggregate() == {"i0": 2}
+    # a row whose heartbeat is older than the TTL stops counting
+    struct.pack_into("<qd", b._mm, b._base, b._pid, time.time() - 1000)
     assert a.aggregate() == {"i0": 1}
+    b.close()
+    # another process shares the table; once it dies its counts vanish at once
+    code = (
+        "import os, sys, time, pathlib\n"
+        f"sys.path.insert(0, {str(ROOT)!r})\n"
+        "from libra_b200.infra.scheduling.cmlfq_shared_state import SharedCMLFQLoadState\n"
+        f"s = SharedCMLFQLoadState({str(tmp_path)!r}, writer_id='child')\n"
+        "s.increment('i2'); s.increment('i2')\n"
+        f"pathlib.Path({str(tmp_path / 'ready')!r}).write_text('1')\n"
+        "t0 = time.time()\n"
+        f"while not os.path.exists({str(tmp_path / 'go')!r}) and time.time() - t0 < 60: time.sleep(0.01)\n"
+        "os._exit(0)\n")
+    child = subprocess.Popen([sys.executable, "-c", code])
+    t0 = time.time()
+    while not (tmp_path / "ready").exists() and time.time() - t0 < 60:
+        time.sleep(0.01)
+    assert a.aggregate() == {"i0": 1, "i2": 2}
+    (tmp_path / "go").write_text("1")
+    assert child.wait(timeout=60) == 0
+    assert a.aggregate() == {"i0": 1}
+    c = SharedCMLFQLoadState(str(tmp_path), writer_id="rank_2")  # the dead writer's row is reusable
+    c.increment("i1")
+    assert a.aggregate() == {"i0": 1, "i1": 1}
+    c.close()
     a.close()
 
 

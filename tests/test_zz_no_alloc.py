@@ -21,7 +21,7 @@ def _lib():
     return fn, err
 
 
-@pytest.mark.parametrize("T,H", [(4097, 2560), (300, 512), (64, 8192)])
+@pytest.mark.parametrize("T,H", [(4097, 2560), (300, 512), (64, 8192), (4096, 32768)])
 def test_noalloc_matches_rmsnorm_bwd(T, H):
     from libra_b200 import ops
 

@@ -244,7 +244,8 @@ def run_ours_grpo(args, rank, world, local):
     block = 16
     worst = n_req * -(-max_len // block) + 64
     free, _ = torch.cuda.mem_get_info(dev)
-    budget_blocks = PagedKVCache.blocks_for_budget(0.45 * free, cfg.num_hidden_layers, block,
+    # the trainer's activations (tens of GB at 16k-token chunks) are not allocated yet: leave them room
+    budget_blocks = PagedKVCache.blocks_for_budget(0.25 * free, cfg.num_hidden_layers, block,
                                                    cfg.num_key_value_heads, cfg.head_dim)
     llm = LLMEngine(cfg, eng.layout.views(rollout_flat), kv_blocks=min(worst, budget_blocks), block_size=block,
                     max_model_len=max_len, max_running=args.max_running, max_batch_tokens=16384, flat=rollout_flat)
@@ -467,9 +468,12 @@ def run_reference(args, rank, world, local):
 
 
 def _start_vllm(ckpt: str, ref_root: str, local: int, port: int, gpu_util: float, max_len: int, log_path: str):
-    """vLLM OpenAI server on this rank's GPU with the reference's in-place reload
-    worker extension (RL_Framework.vllm_hot_reload.InplaceReloadWorkerExtension),
-    reachable through vLLM's /collective_rpc route."""
+    """vLLM OpenAI server on this rank's GPU, with vLLM's developer routes on so
+    /collective_rpc reaches the workers.  The reference's in-place reload
+    extension (RL_Framework.vllm_hot_reload.InplaceReloadWorkerExtension) cannot
+    be registered on vLLM 0.22, whose Worker already defines reload_weights;
+    that built-in method performs the same in-place load of a checkpoint
+    directory, so the arm calls it instead."""
     import subprocess
 
     env = dict(os.environ)
@@ -482,8 +486,7 @@ def _start_vllm(ckpt: str, ref_root: str, local: int, port: int, gpu_util: float
         env.pop(k, None)
     cmd = [sys.executable, "-m", "vllm.entrypoints.openai.api_server", "--model", ckpt, "--host", "127.0.0.1",
            "--port", str(port), "--dtype", "bfloat16", "--gpu-memory-utilization", str(gpu_util),
-           "--max-model-len", str(max_len), "--seed", "0",
-           "--worker-extension-cls", "RL_Framework.vllm_hot_reload.InplaceReloadWorkerExtension"]
+           "--max-model-len", str(max_len), "--seed", "0"]
     log = open(log_path, "w")
     return subprocess.Popen(cmd, env=env, stdout=log, stderr=subprocess.STDOUT, start_new_session=True)
 
@@ -568,7 +571,7 @@ def run_reference_grpo(args, rank, world, local):
             train.save_weights(sync_root, s + 1)
             barrier(world)
             _post_json(f"http://127.0.0.1:{port}/collective_rpc",
-                       {"method": "reload_weights", "args": [os.path.join(sync_root, f"v{s + 1}")]})
+                       {"method": "reload_weights", "kwargs": {"weights_path": os.path.join(sync_root, f"v{s + 1}")}})
             _post_json(f"http://127.0.0.1:{port}/reset_prefix_cache", {})
             barrier(world)
             e3 = ev()

@@ -79,7 +79,55 @@ def route(h, router_w, top_k: int, normalize: bool = True):
     return weights, experts, probs
 
 
+GROUP_ALIGN = 128  # rows: every expert's group starts on a tensor-core tile boundary
+
+
+def expert_layout(experts: torch.Tensor, num_experts: int, align: int = GROUP_ALIGN):
+    """Padded grouped layout of the (token, k) assignments, computed on the device.
+
+    Returns ``offs`` (int32 [E+1]: group e owns rows [offs[e], offs[e+1]), each
+    start a multiple of ``align``) and ``rows`` (int64 [T*k]: the row of
+    assignment j = t*k + kk).  Nothing is read back to the host: the counts come
+    from a scatter-add, not a bincount whose size depends on the data."""
+    flat = experts.reshape(-1)
+    counts = torch.zeros(num_experts, dtype=torch.int64, device=flat.device)
+    counts.scatter_add_(0, flat, torch.ones_like(flat))
+    padded = (counts + align - 1) // align * align
+    offs = torch.zeros(num_experts + 1, dtype=torch.int64, device=flat.device)
+    offs[1:] = padded.cumsum(0)
+    order = torch.argsort(flat, stable=True)
+    g = flat[order]
+    first = counts.cumsum(0) - counts
+    rank = torch.arange(flat.numel(), device=flat.device) - first[g]
+    rows = torch.empty_like(flat)
+    rows[order] = offs[g] + rank
+    return offs.to(torch.int32), rows
+
+
+def grouped_capacity(tokens: int, k: int, num_groups: int, align: int = GROUP_ALIGN) -> int:
+    """Rows that always hold the padded layout of ``tokens * k`` assignments over ``num_groups`` groups."""
+    return tokens * k + (align - 1) * num_groups + align
+
+
 def moe_mlp(h, residual, router_w, w1, w2, cfg):
+    """residual + sum_k w_k * Expert_{e_k}(h), with every expert's rows in one
+    padded buffer and both expert GEMMs as single grouped launches (no host
+    synchronisation, no per-expert loop)."""
+    T, H = h.shape
+    E, k = cfg.num_experts, cfg.num_experts_per_tok
+    weights, experts, _ = route(h, router_w, k, cfg.norm_topk_prob)
+    offs, rows = expert_layout(experts, E)
+    cap = grouped_capacity(T, k, E)
+    xs = h.new_zeros(cap, H).index_copy(0, rows, h.repeat_interleave(k, dim=0))
+    a = ops.grouped_swiglu(xs, w1, offs)
+    ys = ops.grouped_linear(a, w2, offs)
+    picked = ys.index_select(0, rows).view(T, k, H)
+    out = (picked.float() * weights.unsqueeze(-1)).sum(1) + residual.float()
+    return out.to(h.dtype)
+
+
+def moe_mlp_looped(h, residual, router_w, w1, w2, cfg):
+    """Per-expert loop with host-side counts: the oracle for ``moe_mlp``."""
     T, H = h.shape
     E, k = cfg.num_experts, cfg.num_experts_per_tok
     weights, experts, _ = route(h, router_w, k, cfg.norm_topk_prob)

@@ -304,6 +304,102 @@ def linear_swiglu(x, weight):
 
 
 # ---------------------------------------------------------------------------
+# grouped (per-expert) linear layers over padded row groups
+# ---------------------------------------------------------------------------
+
+EPI_SWIGLU = 4
+
+
+def _grouped_wgrad(w, dy, x, offs):
+    """dW_g (+)= dy[rows of g]^T x[rows of g]; into w.main_grad when present."""
+    main = getattr(w, "main_grad", None)
+    if main is not None:
+        ext().grouped_gemm_wgrad(dy, x, main.view(w.shape), offs, True, error_flag(x.device))
+        return None
+    out = torch.zeros(w.shape, dtype=torch.float32, device=w.device)
+    ext().grouped_gemm_wgrad(dy, x, out, offs, True, error_flag(x.device))
+    return out.to(w.dtype)
+
+
+class _GroupedLinear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, offs, out):
+        if out is not None:
+            # caller-provided memory (e.g. a peer-visible send slot): alias its storage without making the
+            # result an autograd view of that buffer
+            y = torch.empty(0, dtype=out.dtype, device=out.device).set_(out.untyped_storage(), out.storage_offset(),
+                                                                          out.shape, out.stride())
+        else:
+            y = torch.zeros(x.shape[0], w.shape[1], dtype=x.dtype, device=x.device)
+        ext().grouped_gemm(x, w, y, offs, 0, False, EPI_BF16, None, error_flag(x.device))
+        ctx.save_for_backward(x, w, offs)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w, offs = ctx.saved_tensors
+        dy = dy.contiguous()
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.zeros_like(x)
+            ext().grouped_gemm(dy, w, dx, offs, 0, True, EPI_BF16, None, error_flag(x.device))
+        dw = _grouped_wgrad(w, dy, x, offs) if ctx.needs_input_grad[1] else None
+        return dx, dw, None, None
+
+
+class _GroupedSwiGLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, offs):
+        T, F = x.shape[0], w.shape[1] // 2
+        a = torch.zeros(T, F, dtype=x.dtype, device=x.device)
+        need = ctx.needs_input_grad[0] or ctx.needs_input_grad[1]
+        gu = torch.zeros(T, 2 * F, dtype=x.dtype, device=x.device) if need else None
+        ext().grouped_gemm(x, w, a, offs, 0, False, EPI_SWIGLU, gu, error_flag(x.device))
+        ctx.save_for_backward(x, w, offs, gu)
+        return a
+
+    @staticmethod
+    def backward(ctx, da):
+        x, w, offs, gu = ctx.saved_tensors
+        dgu = ext().swiglu_bwd(gu, da.contiguous())
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.zeros_like(x)
+            ext().grouped_gemm(dgu, w, dx, offs, 0, True, EPI_BF16, None, error_flag(x.device))
+        dw = _grouped_wgrad(w, dgu, x, offs) if ctx.needs_input_grad[1] else None
+        return dx, dw, None
+
+
+def _grouped_ref(x, w, offs):
+    y = torch.zeros(x.shape[0], w.shape[1], dtype=torch.float32, device=x.device)
+    o = offs.tolist()
+    for g in range(w.shape[0]):
+        if o[g + 1] > o[g]:
+            y[o[g]:o[g + 1]] = x[o[g]:o[g + 1]].float() @ w[g].float().t()
+    return y
+
+
+def grouped_linear(x, w, offs, out=None):
+    """y[rows of g] = x[rows of g] w[g]^T for the row groups ``offs`` (int32 [G+1] on the device,
+    starts multiples of 128, padding rows zero); w [G, N, K].  One launch for every group."""
+    if x.device.type != "cuda":
+        y = _grouped_ref(x, w, offs).to(x.dtype)
+        if out is not None:
+            out.copy_(y.detach())
+        return y
+    return _GroupedLinear.apply(x, w, offs, out)
+
+
+def grouped_swiglu(x, w, offs):
+    """silu(x W_gate,g^T) * (x W_up,g^T) per row group, w [G, 2F, K] ([gate; up] per group)."""
+    if x.device.type != "cuda":
+        gu = _grouped_ref(x, w, offs)
+        F = w.shape[1] // 2
+        return (torch.nn.functional.silu(gu[:, :F]) * gu[:, F:]).to(x.dtype)
+    return _GroupedSwiGLU.apply(x, w, offs)
+
+
+# ---------------------------------------------------------------------------
 # attention
 # ---------------------------------------------------------------------------
 
@@ -484,5 +580,5 @@ def grad_sq_norm(grad, out):
 __all__ = [
     "ext", "extension_available", "check_kernel_errors", "gemm", "linear", "rmsnorm", "qk_norm_rope", "swiglu",
     "varlen_causal_attention", "lm_head_logprob", "adamw_step", "grad_sq_norm", "ref", "linear_swiglu",
-    "paged_decode", "sample_tokens",
+    "paged_decode", "sample_tokens", "grouped_linear", "grouped_swiglu",
 ]

@@ -40,6 +40,10 @@ torch::Tensor paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, tor
                                      double scale);
 void gemm_swiglu(torch::Tensor x, torch::Tensor w, torch::Tensor a, c10::optional<torch::Tensor> gu,
                  torch::Tensor err);
+void grouped_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor offs, int64_t mode, bool b_mn,
+                  int64_t epi, c10::optional<torch::Tensor> c2, torch::Tensor err);
+void grouped_gemm_wgrad(torch::Tensor dy, torch::Tensor x, torch::Tensor c, torch::Tensor offs, bool accumulate,
+                        torch::Tensor err);
 namespace rollout {
 void paged_decode_v2(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                      torch::Tensor seq_lens, torch::Tensor out, torch::Tensor part_out, torch::Tensor part_ml,
@@ -87,6 +91,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("a_mn"), py::arg("b_mn"), py::arg("epi"), py::arg("residual"), py::arg("err"));
   m.def("gemm_swiglu", &libra::gemm_swiglu, "tcgen05 gate/up GEMM with fused SwiGLU epilogue", py::arg("x"),
         py::arg("w"), py::arg("a"), py::arg("gu"), py::arg("err"));
+  m.def("grouped_gemm", &libra::grouped_gemm,
+        "per-expert tcgen05 GEMM over padded row groups whose offsets live in device memory");
+  m.def("grouped_gemm_wgrad", &libra::grouped_gemm_wgrad,
+        "per-expert weight gradient dW_g (+)= dy[rows of g]^T x[rows of g] over padded row groups");
   m.def("rmsnorm_fwd", &libra::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &libra::rmsnorm_bwd);
   m.def("qk_norm_rope_fwd", &libra::qk_norm_rope_fwd);

@@ -851,6 +851,209 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPeer ? kPeerThreads
   if (warp == 1) tmem_dealloc_pair(tmem_base, kTmemCols);
 }
 
+// ------------------------------------------------------------------ grouped (expert) GEMM
+// The groups are the experts of a MoE layer; their row ranges live in device
+// memory (offs[0..G], rows of a padded layout where every group starts at a
+// multiple of 128 rows and its padding rows are zero), so the layer never
+// reads expert counts back to the host and one launch covers every expert.
+//   kGroupRows (forward, dgrad):  C[rows of g] = A[rows of g] . B_g^T, with B_g
+//       the g-th [N, K] block of B (K-major) or [K, N] block (MN-major);
+//   kGroupK (weight gradient):    C_g [M, N] (op)= sum over rows r of g of
+//       A[r, m] B[r, n]  (A, B MN-major, the K loop runs over the group's rows).
+// Every role walks the same list of (group, tile) units, found by a binary
+// search over the per-group tile prefix kept in shared memory.
+constexpr int kGroupRows = 0, kGroupK = 1;
+constexpr int kMaxGroups = 256;
+
+template <int BN, bool A_MN, bool B_MN, int EPI, int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        void* __restrict__ C, const int* __restrict__ offs, int G, int M, int N, int K, int ldc,
+                        int* err, __nv_bfloat16* __restrict__ C2, int ldc2) {
+  static_assert(MODE == kGroupK ? (A_MN && B_MN) : !A_MN, "grouped GEMM operand layouts");
+  static_assert(EPI != kSwiGLU || (BN == 256 && !B_MN && MODE == kGroupRows), "grouped SwiGLU layout");
+  constexpr int kTileN = EPI == kSwiGLU ? 128 : BN;
+  using CF = Cfg<BN>;
+  constexpr int S = CF::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ int s_off[kMaxGroups + 1];
+  __shared__ int s_tile[kMaxGroups + 1];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smA = smem;
+  uint8_t* smB = smem + S * CF::kStageA;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * CF::kStageBytes);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (M + BM - 1) / BM;  // kGroupK only
+  const int num_n = (N + kTileN - 1) / kTileN;
+  const int num_kb_rows = (K + BK - 1) / BK;  // kGroupRows only
+
+  for (int g = threadIdx.x; g <= G; g += blockDim.x) s_off[g] = offs[g];
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4);
+    }
+    mbar_init(done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, CF::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int g = 0; g < G; ++g) {
+      s_tile[g] = acc;
+      const int rows = max(0, s_off[g + 1] - s_off[g]);
+      acc += MODE == kGroupRows ? ((rows + BM - 1) / BM) * num_n : (rows >= BK ? num_m * num_n : 0);
+    }
+    s_tile[G] = acc;
+  }
+  __syncthreads();
+  const uint32_t tmem_base = *tmem_slot;
+  const int total = s_tile[G];
+
+  // unit -> (group, m block, n block, first row of the group)
+  auto locate = [&](int u, int& g, int& mb, int& nb) {
+    int lo = 0, hi = G - 1;
+    while (lo < hi) {  // last g with s_tile[g] <= u
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_tile[mid] <= u) lo = mid; else hi = mid - 1;
+    }
+    g = lo;
+    const int t = u - s_tile[g];
+    mb = t / num_n;
+    nb = t - mb * num_n;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
+        int g, mb, nb;
+        locate(u, g, mb, nb);
+        const int row0 = s_off[g];
+        const int kbs = MODE == kGroupRows ? num_kb_rows : (s_off[g + 1] - row0) / BK;
+        for (int kb = 0; kb < kbs; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, err, kTimeoutSmemEmpty)) { ok = false; break; }
+          mbar_expect_tx(&full[stage], CF::kStageBytes);
+          uint8_t* a_dst = smA + stage * CF::kStageA;
+          uint8_t* b_dst = smB + stage * CF::kStageB;
+          if (MODE == kGroupRows) {
+            const int k0 = kb * BK;
+            tma_load_2d(a_dst, &tmA, &full[stage], k0, row0 + mb * BM);
+            if (EPI == kSwiGLU) {  // group g's gate rows then its up rows, same 128 features
+              tma_load_2d(b_dst, &tmB, &full[stage], k0, g * 2 * N + nb * 128);
+              tma_load_2d(b_dst + 128 * BK * 2, &tmB, &full[stage], k0, g * 2 * N + N + nb * 128);
+            } else if (B_MN) {
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j)
+                tma_load_2d(b_dst + j * 64 * BK * 2, &tmB, &full[stage], nb * BN + j * 64, g * K + k0);
+            } else {
+              tma_load_2d(b_dst, &tmB, &full[stage], k0, g * N + nb * BN);
+            }
+          } else {
+            const int k0 = row0 + kb * BK;
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_2d(a_dst + j * 64 * BK * 2, &tmA, &full[stage], mb * BM + j * 64, k0);
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(b_dst + j * 64 * BK * 2, &tmB, &full[stage], nb * BN + j * 64, k0);
+          }
+          issued_mask |= 1u << stage;
+          issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == S) { stage = 0; phase ^= 1u; }
+        }
+      }
+      for (int s = 0; s < S; ++s)
+        if (issued_mask & (1u << s)) mbar_wait(&full[s], (issued_phase >> s) & 1u, nullptr, 0);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total && ok; u += gridDim.x, ++local) {
+        int g, mb, nb;
+        locate(u, g, mb, nb);
+        const int kbs = MODE == kGroupRows ? num_kb_rows : (s_off[g + 1] - s_off[g]) / BK;
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, err, kTimeoutTmemEmpty)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < kbs; ++kb) {
+          if (!mbar_wait(&full[stage], phase, err, kTimeoutTmaFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smA + stage * CF::kStageA);
+          const uint32_t b_addr = smem_u32(smB + stage * CF::kStageB);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = A_MN ? make_sw128_desc(a_addr + k * 2048, 64 * BK * 2, 1024)
+                                        : make_sw128_desc(a_addr + k * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? make_sw128_desc(b_addr + k * 2048, 64 * BK * 2, 1024)
+                                        : make_sw128_desc(b_addr + k * 32, 16, 1024);
+            umma_f16(d_tmem, adesc, bdesc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == S) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+      }
+      umma_commit(done);
+      mbar_wait(done, 0, nullptr, 0);
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    int local = 0;
+    for (int u = blockIdx.x; u < total; u += gridDim.x, ++local) {
+      int g, mb, nb;
+      locate(u, g, mb, nb);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, err, kTimeoutTmemFull)) break;
+      tc_fence_after();
+      const uint32_t tacc = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      if (MODE == kGroupRows) {
+        store_tile_row<BN, EPI>(tacc, s_off[g] + mb * BM + row_in_tile, nb, s_off[g + 1], N, C, nullptr, ldc, 0,
+                                C2, ldc2);
+      } else {
+        void* cg = reinterpret_cast<uint8_t*>(C) + (size_t)g * M * ldc * (EPI == kStoreBf16 ? 2 : 4);
+        store_tile_row<BN, EPI>(tacc, mb * BM + row_in_tile, nb, M, N, cg, nullptr, ldc, 0, nullptr, 0);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, CF::kTmemCols);
+}
+
 // ------------------------------------------------------------------ host side
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -1269,6 +1472,118 @@ void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, boo
   }
 #undef LIBRA_GEMM_EPI
   if (trace) fprintf(stderr, "[gemm] launched\n");
+}
+
+
+// Grouped (per-expert) GEMM with group boundaries in device memory.
+//   mode 0 (rows): a [T, K] K-major; b [G, Nb, K] (b_mn false; Nb = N, or 2N for the SwiGLU epilogue whose
+//          output has N = Nb / 2 columns) or [G, K, N] (b_mn true); c [T, N] bf16; c2 optional [T, 2N] gate/up
+//   mode 1 (k):    a [T, M] and b [T, N] (both MN-major: rows are the reduction); c [G, M, N] fp32,
+//          accumulated (epi 2) or stored (epi 1)
+// offs [G + 1] int32 on the device: group g owns rows [offs[g], offs[g+1]); every offs[g] must be a
+// multiple of 128 and rows past a group's real count must be zero (they take part in the products).
+void grouped_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor offs, int64_t mode, bool b_mn,
+                  int64_t epi, c10::optional<torch::Tensor> c2, torch::Tensor err) {
+  using namespace gemm;
+  LIBRA_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda() && offs.is_cuda(), "grouped_gemm: CUDA tensors required");
+  LIBRA_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "grouped_gemm: bf16 operands");
+  LIBRA_CHECK(a.is_contiguous() && b.is_contiguous() && c.is_contiguous(), "grouped_gemm: contiguous tensors");
+  LIBRA_CHECK(offs.scalar_type() == at::kInt && offs.dim() == 1 && offs.numel() >= 2 && offs.numel() <= kMaxGroups + 1,
+              "grouped_gemm: offs must be int32 [G + 1] with G <= %d", kMaxGroups);
+  LIBRA_CHECK(a.dim() == 2 && b.dim() == 3, "grouped_gemm: a [T, *] and b [G, *, *]");
+  const int G = (int)offs.numel() - 1;
+  LIBRA_CHECK(b.size(0) == G, "grouped_gemm: b has %lld groups, offs %d", (long long)b.size(0), G);
+  const int64_t T = a.size(0);
+  const c10::cuda::CUDAGuard guard(a.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  int* errp = err.data_ptr<int>();
+  const int* op = offs.data_ptr<int>();
+  if (T == 0) return;
+  static int sms = 0;
+  if (!sms) sms = num_sms();
+  if (mode == kGroupRows) {
+    const int64_t K = a.size(1);
+    const bool swiglu = epi == kSwiGLU;
+    const int64_t N = b_mn ? b.size(2) : (swiglu ? b.size(1) / 2 : b.size(1));
+    LIBRA_CHECK((b_mn ? b.size(1) : b.size(2)) == K, "grouped_gemm: K mismatch");
+    LIBRA_CHECK(K % 64 == 0 && N % 128 == 0, "grouped_gemm: K must be a multiple of 64 and N of 128");
+    LIBRA_CHECK(c.scalar_type() == at::kBFloat16 && c.dim() == 2 && c.size(0) == T && c.size(1) == N,
+                "grouped_gemm: c must be bf16 [T, N]");
+    LIBRA_CHECK(epi == kStoreBf16 || (swiglu && !b_mn), "grouped_gemm: row mode stores bf16 (or SwiGLU)");
+    __nv_bfloat16* c2p = nullptr;
+    if (c2.has_value()) {
+      LIBRA_CHECK(swiglu && c2->scalar_type() == at::kBFloat16 && c2->is_contiguous() && c2->size(0) == T &&
+                      c2->size(1) == 2 * N, "grouped_gemm: c2 is the SwiGLU gate/up output [T, 2N]");
+      c2p = reinterpret_cast<__nv_bfloat16*>(c2->data_ptr());
+    }
+    CUtensorMap ta = make_map(a.data_ptr(), K, T, K, 64, BM);
+    const int tiles_ub = (int)(((T + BM - 1) / BM) * (N / (swiglu ? 128 : 256)) + 1);
+    const int grid = tiles_ub < sms ? tiles_ub : sms;
+    constexpr int smem = Cfg<256>::kSmemBytes;
+    if (swiglu) {
+      CUtensorMap tb = make_map(b.data_ptr(), K, (int64_t)G * 2 * N, K, 64, 128);
+      auto kern = grouped_gemm_kernel<256, false, false, kSwiGLU, kGroupRows>;
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      kern<<<grid, kThreads, smem, st>>>(ta, tb, c.data_ptr(), op, G, 0, (int)N, (int)K, (int)N, errp, c2p,
+                                         (int)(2 * N));
+    } else if (b_mn) {
+      CUtensorMap tb = make_map(b.data_ptr(), N, (int64_t)G * K, N, 64, 64);
+      auto kern = grouped_gemm_kernel<256, false, true, kStoreBf16, kGroupRows>;
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      kern<<<grid, kThreads, smem, st>>>(ta, tb, c.data_ptr(), op, G, 0, (int)N, (int)K, (int)N, errp, nullptr, 0);
+    } else {
+      CUtensorMap tb = make_map(b.data_ptr(), K, (int64_t)G * N, K, 64, 256);
+      auto kern = grouped_gemm_kernel<256, false, false, kStoreBf16, kGroupRows>;
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      kern<<<grid, kThreads, smem, st>>>(ta, tb, c.data_ptr(), op, G, 0, (int)N, (int)K, (int)N, errp, nullptr, 0);
+    }
+  } else {
+    LIBRA_CHECK(mode == kGroupK && b.dim() == 3, "grouped_gemm: mode must be 0 (rows) or 1 (k)");
+    LIBRA_CHECK(false, "grouped_gemm: use grouped_gemm_wgrad for mode 1");
+  }
+  LIBRA_LAUNCH_CHECK();
+}
+
+// Weight gradient of a grouped linear: c [G, M, N] fp32 (+)= per group, dy[rows]^T x[rows]
+// with dy [T, M] and x [T, N] bf16 row-major (the rows are the reduction); offs as above, every group's
+// row count a multiple of 64 (the padded layout gives 128).
+void grouped_gemm_wgrad(torch::Tensor dy, torch::Tensor x, torch::Tensor c, torch::Tensor offs, bool accumulate,
+                        torch::Tensor err) {
+  using namespace gemm;
+  LIBRA_CHECK(dy.is_cuda() && x.is_cuda() && c.is_cuda() && offs.is_cuda(), "grouped_gemm_wgrad: CUDA tensors");
+  LIBRA_CHECK(dy.scalar_type() == at::kBFloat16 && x.scalar_type() == at::kBFloat16 && c.scalar_type() == at::kFloat,
+              "grouped_gemm_wgrad: bf16 inputs, fp32 output");
+  LIBRA_CHECK(dy.is_contiguous() && x.is_contiguous() && c.is_contiguous() && dy.dim() == 2 && x.dim() == 2 &&
+                  c.dim() == 3 && dy.size(0) == x.size(0),
+              "grouped_gemm_wgrad: dy [T, M], x [T, N], c [G, M, N] contiguous");
+  LIBRA_CHECK(offs.scalar_type() == at::kInt && offs.numel() == c.size(0) + 1 && offs.numel() <= kMaxGroups + 1,
+              "grouped_gemm_wgrad: offs int32 [G + 1]");
+  const int G = (int)c.size(0);
+  const int64_t T = dy.size(0), M = dy.size(1), N = x.size(1);
+  LIBRA_CHECK(c.size(1) == M && c.size(2) == N, "grouped_gemm_wgrad: c must be [G, M, N]");
+  LIBRA_CHECK(M % 64 == 0 && N % 128 == 0, "grouped_gemm_wgrad: M a multiple of 64, N of 128");
+  if (T == 0) return;
+  const c10::cuda::CUDAGuard guard(dy.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  CUtensorMap ta = make_map(dy.data_ptr(), M, T, M, 64, 64);
+  CUtensorMap tb = make_map(x.data_ptr(), N, T, N, 64, 64);
+  static int sms = 0;
+  if (!sms) sms = num_sms();
+  const int tiles_ub = G * (int)((M + BM - 1) / BM) * (int)((N + 255) / 256);
+  const int grid = tiles_ub < sms ? tiles_ub : sms;
+  constexpr int smem = Cfg<256>::kSmemBytes;
+  if (accumulate) {
+    auto kern = grouped_gemm_kernel<256, true, true, kAccumF32, kGroupK>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    kern<<<grid, kThreads, smem, st>>>(ta, tb, c.data_ptr(), offs.data_ptr<int>(), G, (int)M, (int)N, 0, (int)N,
+                                       err.data_ptr<int>(), nullptr, 0);
+  } else {
+    auto kern = grouped_gemm_kernel<256, true, true, kStoreF32, kGroupK>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    kern<<<grid, kThreads, smem, st>>>(ta, tb, c.data_ptr(), offs.data_ptr<int>(), G, (int)M, (int)N, 0, (int)N,
+                                       err.data_ptr<int>(), nullptr, 0);
+  }
+  LIBRA_LAUNCH_CHECK();
 }
 
 }  // namespace libra

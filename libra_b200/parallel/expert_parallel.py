@@ -102,19 +102,24 @@ class RoutePlan:
 
     dst_rank: torch.Tensor  # int32 [T*k]: rank owning the assignment's expert
     dst_row: torch.Tensor  # int32 [T*k]: row in that rank's receive slot
-    recv_counts: List[int]  # rows this rank receives per local expert (grouped, in order)
-    recv_total: int
+    offs: torch.Tensor  # int32 [E_l + 1] on the device: this rank's padded group of each local expert
+    valid: torch.Tensor  # bf16 [recv_total, 1]: 1 on received rows, 0 on group padding
+    recv_total: int  # rows of this rank's padded receive layout
     k: int
 
 
-def route_plan(experts: torch.Tensor, counts_all: torch.Tensor, me: int) -> RoutePlan:
+def route_plan(experts: torch.Tensor, counts_all: torch.Tensor, me: int, align: int = 128) -> RoutePlan:
     """Destination of every assignment, from all ranks' per-expert counts.
 
     ``experts`` [T, k] global expert ids of this rank's tokens; ``counts_all``
     [n, E] the number of assignments each rank sends to each expert.  The
-    receive slot of rank d is ordered by (local expert, source rank, source
-    order): row = (rows of d's earlier local experts) + (rows of this expert
-    from lower ranks) + (position among this rank's rows for the expert).
+    receive slot of rank d holds one group per local expert, each starting at a
+    multiple of ``align`` rows (so the expert GEMM runs as one grouped launch
+    over tile-aligned groups), ordered inside by (source rank, source order):
+    row = (start of the expert's group on d) + (rows of this expert from lower
+    ranks) + (position among this rank's rows for the expert).  One number is
+    read back to the host: this rank's padded receive total, which sizes its
+    buffers.
     """
     n, E = counts_all.shape
     E_l = E // n
@@ -124,7 +129,8 @@ def route_plan(experts: torch.Tensor, counts_all: torch.Tensor, me: int) -> Rout
     g = flat[order]
     cnt = counts_all.to(torch.int64)
     per_dest = cnt.sum(0).view(n, E_l)
-    base = (per_dest.cumsum(1) - per_dest).reshape(-1)
+    padded = (per_dest + align - 1) // align * align
+    base = (padded.cumsum(1) - padded).reshape(-1)
     lower = (cnt.cumsum(0) - cnt)[me]
     start = cnt[me].cumsum(0) - cnt[me]
     i = torch.arange(flat.numel(), device=flat.device)
@@ -133,8 +139,13 @@ def route_plan(experts: torch.Tensor, counts_all: torch.Tensor, me: int) -> Rout
     dst_row = torch.empty_like(dst_rank)
     dst_rank[order] = (g // E_l).to(torch.int32)
     dst_row[order] = row_sorted.to(torch.int32)
-    host = per_dest.cpu()
-    return RoutePlan(dst_rank, dst_row, [int(c) for c in host[me]], int(host[me].sum()), k)
+    offs = torch.zeros(E_l + 1, dtype=torch.int64, device=flat.device)
+    offs[1:] = padded[me].cumsum(0)
+    total = int(offs[-1])
+    r = torch.arange(total, device=flat.device)
+    grp = torch.searchsorted(offs[1:], r, right=True).clamp_(max=E_l - 1)
+    valid = ((r - offs[grp]) < per_dest[me][grp]).to(torch.bfloat16).unsqueeze(1)
+    return RoutePlan(dst_rank, dst_row, offs.to(torch.int32), valid, total, k)
 
 
 class PeerExpertExchange:
@@ -202,11 +213,8 @@ class PeerExpertExchange:
             counts_all = torch.stack(parts)
         else:
             counts_all = cnt[None]
-        plan = route_plan(experts, counts_all, self.me)
-        worst = int(counts_all.to(torch.int64).sum(0).view(self.n, -1).sum(1).max())
-        if worst > self.max_rows:  # the same decision on every rank: all see all counts
-            raise ValueError(f"a rank would receive {worst} rows; the exchange holds {self.max_rows}")
-        return plan
+        # rows beyond max_rows are refused by the dispatch kernel (error word), not checked here
+        return route_plan(experts, counts_all, self.me)
 
     def push(self, x: torch.Tensor, plan: RoutePlan, scale: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Rows x[j // k] (times scale[j]) to their owners; returns this rank's received rows."""
@@ -217,7 +225,8 @@ class PeerExpertExchange:
                           None if scale is None else scale.reshape(-1).float().contiguous(),
                           plan.dst_rank, plan.dst_row, plan.k, self.max_rows, self.push_calls, self.grid,
                           ops.error_flag(x.device))
-        return self._slot_view(0, slot, plan.recv_total).clone()
+        # group padding rows hold whatever the slot held before: zero them for the grouped GEMMs
+        return self._slot_view(0, slot, plan.recv_total) * plan.valid
 
     def send_view(self, rows: int) -> torch.Tensor:
         """The slot the next ``pull`` publishes: a producer that writes its [rows, H] output
@@ -267,7 +276,7 @@ class _PeerCombine(torch.autograd.Function):
     def backward(ctx, g):
         weights, gath = ctx.saved_tensors
         g = g.contiguous()
-        dy = ctx.xchg.push(g, ctx.plan, scale=weights)
+        dy = ctx.xchg.push(g, ctx.plan, scale=weights)  # padding rows zeroed like the forward dispatch
         dw = None
         if ctx.needs_input_grad[1]:
             T, k = weights.shape
@@ -276,14 +285,15 @@ class _PeerCombine(torch.autograd.Function):
 
 
 def _ep_moe_mlp_peer(h, residual, router, w1_local, w2_local, cfg, xchg: PeerExpertExchange):
-    from libra_b200.models.moe import GroupedLinear, route
+    from libra_b200.models.moe import route
 
     weights, experts, _ = route(h, router, cfg.num_experts_per_tok, cfg.norm_topk_prob)
     plan = xchg.plan(experts, cfg.num_experts)
     x_recv = _PeerDispatch.apply(h, plan, xchg)
-    gu = GroupedLinear.apply(x_recv, w1_local, plan.recv_counts)
-    a = ops.swiglu(gu)
-    y_recv = GroupedLinear.apply(a, w2_local, plan.recv_counts, (xchg.send_view(plan.recv_total),))
+    # both expert projections are single grouped launches over the padded per-expert groups; the second
+    # writes straight into the send slot that the combine kernels on the other ranks read
+    a = ops.grouped_swiglu(x_recv, w1_local, plan.offs)
+    y_recv = ops.grouped_linear(a, w2_local, plan.offs, out=xchg.send_view(plan.recv_total))
     return _PeerCombine.apply(y_recv, weights, residual, plan, xchg)
 
 

@@ -68,3 +68,18 @@ def test_load_config_requires_path(monkeypatch):
     monkeypatch.delenv("ASYNC_RL_CONFIG", raising=False)
     with pytest.raises(ValueError, match="No configuration file"):
         load_config(None)
+
+
+def test_parallel_layout_reaches_the_engine():
+    """train_tp_size / train_ep_size from the presets arrive in the engine the factory builds."""
+    from libra_b200.engine.train_engine import create_train_engine
+
+    c14 = AsyncRLConfig.from_file(os.path.join(CFG_DIR, "qwen3_14b_agentic_tp4.yaml"))
+    e14 = create_train_engine(c14)
+    assert e14.tp_size == 4 and e14.ep_size == 1 and e14.cfg.hidden_size == 5120
+    c30 = AsyncRLConfig.from_file(os.path.join(CFG_DIR, "qwen3_30b_a3b_ep8.yaml"))
+    e30 = create_train_engine(c30)
+    assert e30.tp_size == 1 and e30.ep_size == 8 and e30.cfg.num_experts == 128
+    with pytest.raises(ValueError, match="train_pp_size"):
+        c30.train_pp_size = 2
+        create_train_engine(c30)

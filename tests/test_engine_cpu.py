@@ -95,3 +95,26 @@ def test_fused_param_gather_declines_without_sharded_nccl_optimizer():
     eng.initialize()
     assert eng.enable_fused_param_gather() is False
     assert getattr(eng, "_peer_param_gather", None) is None
+
+
+def test_grouped_moe_matches_looped_reference():
+    """Padded grouped MoE (device-side layout, one grouped GEMM per projection) equals the per-expert loop."""
+    import torch
+
+    from libra_b200.models.moe import expert_layout, moe_mlp, moe_mlp_looped
+    from libra_b200.models.qwen3 import get_config
+
+    cfg = get_config("tiny-moe")
+    g = torch.Generator().manual_seed(0)
+    T, H, E, F = 37, cfg.hidden_size, cfg.num_experts, cfg.moe_intermediate_size
+    h = torch.randn(T, H, generator=g)
+    res = torch.randn(T, H, generator=g)
+    router = torch.randn(E, H, generator=g) * 0.1
+    w1 = torch.randn(E, 2 * F, H, generator=g) * 0.05
+    w2 = torch.randn(E, H, F, generator=g) * 0.05
+    ref = moe_mlp_looped(h, res, router, w1, w2, cfg)
+    got = moe_mlp(h, res, router, w1, w2, cfg)
+    assert torch.allclose(got.float(), ref.float(), atol=1e-4, rtol=1e-4)
+    offs, rows = expert_layout(torch.tensor([[3, 1], [1, 1], [7, 3]]), 8)
+    assert offs.tolist() == [0, 0, 128, 128, 256, 256, 256, 256, 384]
+    assert rows.tolist() == [128, 0, 1, 2, 256, 129]

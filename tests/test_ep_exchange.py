@@ -29,10 +29,15 @@ def test_route_plan_layout_is_grouped_permutation():
             flat = experts[s].reshape(-1)[sel]
             tags += [(int(e) % El, s, j) for e, j in zip(flat, sel.nonzero().flatten().tolist())]
         rows = torch.cat(rows)
-        assert sorted(rows.tolist()) == list(range(plans[d].recv_total))
         ordered = [t for _, t in sorted(zip(rows.tolist(), tags))]
         assert ordered == sorted(ordered)  # (local expert, source rank, source order)
-        assert plans[d].recv_counts == [int(counts[:, d * El + e].sum()) for e in range(El)]
+        # each local expert's rows fill the start of a group that begins on a 128-row boundary
+        offs = plans[d].offs.tolist()
+        real = [int(counts[:, d * El + e].sum()) for e in range(El)]
+        want = [offs[e] + i for e in range(El) for i in range(real[e])]
+        assert sorted(rows.tolist()) == want
+        assert all(o % 128 == 0 for o in offs) and offs[-1] == plans[d].recv_total
+        assert plans[d].valid.sum().item() == sum(real)
 
 
 def test_route_plan_emulated_exchange_matches_moe_block():
@@ -58,16 +63,12 @@ def test_route_plan_emulated_exchange_matches_moe_block():
     for s in range(n):
         for j in range(T * k):
             recv[int(plans[s].dst_rank[j])][int(plans[s].dst_row[j])] = hs[s][j // k]
+    from libra_b200 import ops
+
     ys = []
     for d in range(n):
-        out, st = [], 0
-        for e, c in enumerate(plans[d].recv_counts):
-            x = recv[d][st:st + c]
-            gu = x @ w1[d * El + e].t()
-            a = torch.nn.functional.silu(gu[:, :F]) * gu[:, F:]
-            out.append(a @ w2[d * El + e].t())
-            st += c
-        ys.append(torch.cat(out))
+        a = ops.grouped_swiglu(recv[d], w1[d * El:(d + 1) * El], plans[d].offs)
+        ys.append(ops.grouped_linear(a, w2[d * El:(d + 1) * El], plans[d].offs))
     for s in range(n):
         w = routed[s][0].reshape(-1)
         got = res[s].clone()

@@ -36,7 +36,7 @@ import torch.distributed as dist
 
 from libra_b200 import ops
 from libra_b200.models.qwen3 import (PackedBatch, ParamLayout, Qwen3Config, Qwen3Model, get_config, init_params,
-                                     pack_sequences, param_shapes)
+                                     is_expert_param, pack_sequences, param_shapes)
 from libra_b200.utils import nvtx
 
 
@@ -137,17 +137,30 @@ class B200TrainEngine:
                 self.dp_group = self.mesh.group("dp", rank)
         self.dp_size = dist.get_world_size(self.dp_group) if dist.is_initialized() else 1
         self.dp_rank = dist.get_rank(self.dp_group) if dist.is_initialized() else 0
-        shapes = param_shapes(self.cfg, self.tp_size, self.tp_rank)
-        self.layout = ParamLayout(shapes)
-        P = self.layout.numel
-        # pad so the flat buffer splits evenly into DP shards of 128-element multiples
+        self._init_expert_parallel()
+        shapes = param_shapes(self.cfg, self.tp_size, self.tp_rank, self.ep_size)
         unit = ParamLayout.ALIGN * self.dp_size
-        self.padded_numel = (P + unit - 1) // unit * unit
+        if self.ep_size > 1:
+            # dense parameters first (sharded over the data-parallel group by the distributed optimizer),
+            # then this rank's experts (owned whole, reduced over the ranks that hold the same experts)
+            dense = [(n, sh) for n, sh in shapes if not is_expert_param(n)]
+            experts = [(n, sh) for n, sh in shapes if is_expert_param(n)]
+            self.layout = ParamLayout(dense + experts)
+            d_end = self.layout.offsets[experts[0][0]]
+            self.dense_numel = (d_end + unit - 1) // unit * unit
+            self.layout.shift([n for n, _ in experts], self.dense_numel - d_end)
+            self.padded_numel = self.layout.numel
+        else:
+            self.layout = ParamLayout(shapes)
+            # pad so the flat buffer splits evenly into DP shards of 128-element multiples
+            self.padded_numel = (self.layout.numel + unit - 1) // unit * unit
+            self.dense_numel = self.padded_numel
         dev = self.device
         self.flat_param = torch.zeros(self.padded_numel, dtype=torch.bfloat16, device=dev)
         self.flat_grad = torch.zeros(self.padded_numel, dtype=torch.float32, device=dev)
         views = self.layout.views(self.flat_param)
-        init_params(self.cfg, views, seed=self.seed + 7919 * self.tp_rank)
+        E_l = self.cfg.num_experts // self.ep_size if self.cfg.is_moe else 0
+        init_params(self.cfg, views, seed=self.seed + 7919 * self.tp_rank, expert_offset=self.ep_rank * E_l)
         grad_views = self.layout.views(self.flat_grad)
         self.params: Dict[str, torch.nn.Parameter] = {}
         for name, v in views.items():
@@ -158,16 +171,34 @@ class B200TrainEngine:
             p.register_post_accumulate_grad_hook(_fold_grad_into_main)
             self.params[name] = p
         self.sharded = self.use_distributed_optimizer and self.dp_size > 1
-        shard = self.padded_numel // self.dp_size if self.sharded else self.padded_numel
+        shard = self.dense_numel // self.dp_size if self.sharded else self.dense_numel
         self.shard_numel = shard
         self.shard_start = self.dp_rank * shard if self.sharded else 0
         self.master = self.flat_param[self.shard_start:self.shard_start + shard].float().clone()
         self.exp_avg = torch.zeros_like(self.master)
         self.exp_avg_sq = torch.zeros_like(self.master)
-        self.grad_shard = (torch.zeros(shard, dtype=torch.float32, device=dev) if self.sharded else self.flat_grad)
+        self.grad_shard = (torch.zeros(shard, dtype=torch.float32, device=dev) if self.sharded
+                           else self.flat_grad[:self.dense_numel])
         self.sq_norm = torch.zeros(1, dtype=torch.float32, device=dev)
+        # expert segment: fp32 master and Adam moments of this rank's experts (not sharded further)
+        self.x_master = self.x_m = self.x_v = None
+        if self.padded_numel > self.dense_numel:
+            self.x_master = self.flat_param[self.dense_numel:].float().clone()
+            self.x_m = torch.zeros_like(self.x_master)
+            self.x_v = torch.zeros_like(self.x_master)
+        self.ep_exchange = None
+        if self.ep_size > 1 and dev.type == "cuda" and not self._gloo():
+            from libra_b200.parallel.expert_parallel import PeerExpertExchange
+
+            tokens = max(self.max_tokens_per_micro_batch, self.max_tokens_per_recompute_batch)
+            k = self.cfg.num_experts_per_tok
+            # receive capacity: twice a balanced share of the tokens' assignments plus the group padding;
+            # a layer that would receive more rows is refused by the dispatch kernel (error word)
+            rows = 2 * tokens * k + 128 * (self.cfg.num_experts // self.ep_size + 1)
+            self.ep_exchange = PeerExpertExchange(self.ep_group, rows, self.cfg.hidden_size, dev)
         self.model = Qwen3Model(self.cfg, self.params, recompute=self.recompute_activations, tp_group=self.tp_group,
-                                tp_size=self.tp_size, tp_rank=self.tp_rank)
+                                tp_size=self.tp_size, tp_rank=self.tp_rank, ep_group=self.ep_group,
+                                ep_size=self.ep_size, ep_exchange=self.ep_exchange)
         from libra_b200.parallel.tensor_parallel import tp_partial_grad_params
 
         self._tp_partial = [self.params[n].main_grad for n in tp_partial_grad_params(list(self.params))
@@ -183,6 +214,55 @@ class B200TrainEngine:
                     a, b = max(a, lo), min(b, hi)
                     if a < b:
                         self._tp_replicated.append((a - lo, b - lo))
+
+    def _init_expert_parallel(self) -> None:
+        """Expert-parallel groups inside the data-parallel group: ``ep_group`` =
+        ``ep_size`` consecutive DP ranks that split the experts between them;
+        ``edp_group`` = the DP ranks holding the same experts (their expert
+        gradients are summed)."""
+        self.ep_group = self.edp_group = None
+        self.ep_rank = 0
+        if self.ep_size <= 1:
+            return
+        if self.tp_size > 1:
+            raise ValueError("expert parallelism runs with tp_size=1 (attention and dense layers data-parallel)")
+        if not dist.is_initialized():
+            raise RuntimeError("expert parallelism needs an initialized process group")
+        ep = self.ep_size
+        if self.dp_size % ep:
+            raise ValueError(f"ep_size={ep} must divide the data-parallel size {self.dp_size}")
+        ranks = dist.get_process_group_ranks(self.dp_group) if self.dp_group is not None else \
+            list(range(dist.get_world_size()))
+        for g0 in range(0, len(ranks), ep):  # every rank creates every group, in the same order
+            grp = dist.new_group(ranks[g0:g0 + ep])
+            if g0 <= self.dp_rank < g0 + ep:
+                self.ep_group = grp
+        for i in range(ep):
+            grp = dist.new_group(ranks[i::ep])
+            if self.dp_rank % ep == i:
+                self.edp_group = grp
+        self.ep_rank = self.dp_rank % ep
+
+    def _align_chunks(self, chunks: List[List[int]]) -> List[List[int]]:
+        """Expert parallelism exchanges tokens in every MoE layer of every
+        forward/backward, so all ranks of an EP group must run the same number
+        of chunks: split the largest chunks until every rank has the group's
+        maximum."""
+        if self.ep_size <= 1:
+            return chunks
+        dev = self.device if not self._gloo() else torch.device("cpu")
+        n = torch.tensor([len(chunks)], dtype=torch.int64, device=dev)
+        dist.all_reduce(n, op=dist.ReduceOp.MAX, group=self.ep_group)
+        target = int(n.item())
+        chunks = [list(c) for c in chunks]
+        while len(chunks) < target:
+            i = max(range(len(chunks)), key=lambda j: len(chunks[j]))
+            if len(chunks[i]) < 2:
+                raise RuntimeError(f"expert-parallel ranks need {target} chunks but this rank has only "
+                                   f"{sum(len(c) for c in chunks)} trajectories")
+            c = chunks[i]
+            chunks[i:i + 1] = [c[:len(c) // 2], c[len(c) // 2:]]
+        return chunks
 
     # ------------------------------------------------------------------ protocol helpers
     def get_version(self) -> int:
@@ -293,12 +373,13 @@ class B200TrainEngine:
         """Host-side packed execution chunks (with loss weights) for one update."""
         w = self.loss_weights(trajectories)
         return [self.pack([trajectories[i] for i in idx], True, [w[i] for i in idx])
-                for idx in self.chunk_by_tokens(trajectories, self.max_tokens_per_micro_batch)]
+                for idx in self._align_chunks(self.chunk_by_tokens(trajectories, self.max_tokens_per_micro_batch))]
 
     def prepare_recompute(self, trajectories: List[Dict[str, Any]]):
         """(trajectory chunk, packed host batch) pairs for logprob recompute."""
         out = []
-        for idx in self.chunk_by_tokens(trajectories, self.max_tokens_per_recompute_batch):
+        limit = self.max_tokens_per_recompute_batch if self.ep_size <= 1 else self.max_tokens_per_micro_batch
+        for idx in self._align_chunks(self.chunk_by_tokens(trajectories, limit)):
             chunk = [trajectories[i] for i in idx]
             out.append((chunk, self.pack(chunk, with_old_logprobs=False)))
         return out
@@ -396,23 +477,31 @@ class B200TrainEngine:
         """DP gradient reduction: reduce-scatter (distributed optimizer) or all-reduce."""
         if self.dp_size <= 1 or not dist.is_initialized():
             return
+        dense = self.flat_grad[:self.dense_numel]
         if self.sharded:
             if self._gloo():  # gloo has no reduce_scatter_tensor
-                dist.all_reduce(self.flat_grad, op=dist.ReduceOp.SUM, group=self.dp_group)
-                self.grad_shard.copy_(self.flat_grad[self.shard_start:self.shard_start + self.shard_numel])
+                dist.all_reduce(dense, op=dist.ReduceOp.SUM, group=self.dp_group)
+                self.grad_shard.copy_(dense[self.shard_start:self.shard_start + self.shard_numel])
             else:
-                dist.reduce_scatter_tensor(self.grad_shard, self.flat_grad, op=dist.ReduceOp.SUM, group=self.dp_group)
+                dist.reduce_scatter_tensor(self.grad_shard, dense, op=dist.ReduceOp.SUM, group=self.dp_group)
             self.grad_shard.div_(self.dp_size)
         else:
-            dist.all_reduce(self.flat_grad, op=dist.ReduceOp.SUM, group=self.dp_group)
-            self.flat_grad.div_(self.dp_size)
+            dist.all_reduce(dense, op=dist.ReduceOp.SUM, group=self.dp_group)
+            dense.div_(self.dp_size)
+        if self.padded_numel > self.dense_numel:
+            # expert gradients already hold every EP rank's tokens (the exchange's backward brought them);
+            # sum over the replicas of these experts, then average like the dense part
+            xg = self.flat_grad[self.dense_numel:]
+            if self.edp_group is not None and dist.get_world_size(self.edp_group) > 1:
+                dist.all_reduce(xg, op=dist.ReduceOp.SUM, group=self.edp_group)
+            xg.div_(self.dp_size)
 
     def _gather_params(self, shard_param: torch.Tensor) -> None:
         if self._gloo():
-            parts = list(self.flat_param.chunk(self.dp_size))
+            parts = list(self.flat_param[:self.dense_numel].chunk(self.dp_size))
             dist.all_gather(parts, shard_param.clone(), group=self.dp_group)
             return
-        dist.all_gather_into_tensor(self.flat_param, shard_param.clone(), group=self.dp_group)
+        dist.all_gather_into_tensor(self.flat_param[:self.dense_numel], shard_param.clone(), group=self.dp_group)
 
     def _optimizer_step(self) -> None:
         self.step_count += 1
@@ -430,8 +519,20 @@ class B200TrainEngine:
             self.sq_norm.copy_(total - (self.tp_size - 1) * both[1:])
         elif self.sharded:
             dist.all_reduce(self.sq_norm, op=dist.ReduceOp.SUM, group=self.dp_group)
-        shard_param = self.flat_param[self.shard_start:self.shard_start + self.shard_numel]
         o = self.optim
+        if self.x_master is not None:
+            # experts: the global norm adds every EP rank's experts once; the AdamW update of this rank's
+            # experts writes their bf16 values in place (no gather: nobody else holds them)
+            xg = self.flat_grad[self.dense_numel:]
+            x_sq = torch.zeros(1, dtype=torch.float32, device=self.device)
+            ops.grad_sq_norm(xg, x_sq)
+            if self.ep_group is not None:
+                dist.all_reduce(x_sq, op=dist.ReduceOp.SUM, group=self.ep_group)
+            self.sq_norm.add_(x_sq)
+            ops.adamw_step(self.x_master, xg, self.x_m, self.x_v, self.flat_param[self.dense_numel:], lr=o.lr,
+                           beta1=o.betas[0], beta2=o.betas[1], eps=o.eps, weight_decay=o.weight_decay,
+                           step=self.step_count, max_grad_norm=o.max_grad_norm, sq_norm=self.sq_norm)
+        shard_param = self.flat_param[self.shard_start:self.shard_start + self.shard_numel]
         peer = getattr(self, "_peer_param_gather", None)
         if peer is not None:  # AdamW stores the new bf16 shard straight into every rank's parameters
             peer.step(self.master, self.grad_shard, self.exp_avg, self.exp_avg_sq, lr=o.lr, beta1=o.betas[0],

@@ -121,7 +121,12 @@ def get_config(name_or_cfg) -> Qwen3Config:
 # parameter layout
 # ---------------------------------------------------------------------------
 
-def param_shapes(cfg: Qwen3Config, tp_size: int = 1, tp_rank: int = 0) -> List[Tuple[str, Tuple[int, ...]]]:
+def is_expert_param(name: str) -> bool:
+    return name.endswith("experts.w1") or name.endswith("experts.w2")
+
+
+def param_shapes(cfg: Qwen3Config, tp_size: int = 1, tp_rank: int = 0,
+                 ep_size: int = 1) -> List[Tuple[str, Tuple[int, ...]]]:
     """Canonical (name, local shape) list for one tensor-parallel rank.
 
     Column-parallel blocks (QKV, gate/up, expert w1) are split along their
@@ -148,10 +153,13 @@ def param_shapes(cfg: Qwen3Config, tp_size: int = 1, tp_rank: int = 0) -> List[T
         ]
         if cfg.is_moe:
             E, Fe = cfg.num_experts, cfg.moe_intermediate_size
+            if E % ep_size:
+                raise ValueError(f"ep_size={ep_size} does not divide num_experts={E}")
+            El = E // ep_size  # this expert-parallel rank's experts
             shapes += [
                 (p + "router", (E, H)),
-                (p + "experts.w1", (E, 2 * Fe // tp_size, H)),
-                (p + "experts.w2", (E, H, Fe // tp_size)),
+                (p + "experts.w1", (El, 2 * Fe // tp_size, H)),
+                (p + "experts.w2", (El, H, Fe // tp_size)),
             ]
         else:
             F = cfg.intermediate_size // tp_size
@@ -186,23 +194,44 @@ class ParamLayout:
             out[name] = flat[off:off + math.prod(shape)].view(shape)
         return out
 
+    def shift(self, names: List[str], delta: int) -> None:
+        """Move the named parameters ``delta`` elements further into the buffer
+        (a multiple of ALIGN; used to start a segment on a shard boundary)."""
+        if delta % self.ALIGN:
+            raise ValueError("layout shifts must keep the alignment")
+        for n in names:
+            self.offsets[n] += delta
+        self.numel += delta
+
     def segment(self, name: str) -> Tuple[int, int]:
         off = self.offsets[name]
         return off, off + math.prod(self.shapes[name])
 
 
-def init_params(cfg: Qwen3Config, views: Dict[str, torch.Tensor], seed: int = 0) -> None:
+def init_params(cfg: Qwen3Config, views: Dict[str, torch.Tensor], seed: int = 0, expert_offset: int = 0) -> None:
     """Random init in place: N(0, initializer_range) for matrices, 1 for norms,
-    N(0, router_init_std) for MoE routers (router logits ~ N(0,1) scale)."""
+    N(0, router_init_std) for MoE routers (router logits ~ N(0,1) scale).
+
+    Dense parameters draw from one stream in layout order; every expert's
+    weights draw from a stream of their own keyed by (layer, global expert id),
+    so an expert-parallel rank holding experts ``expert_offset ..`` gets exactly
+    the weights the unsharded model has for them."""
     gen_device = next(iter(views.values())).device
     g = torch.Generator(device=gen_device)
     g.manual_seed(seed)
+    ge = torch.Generator(device=gen_device)
     with torch.no_grad():
         for name, t in views.items():
             if t.dim() == 1:
                 t.fill_(1.0)
             elif name.endswith("router"):
                 t.normal_(0.0, cfg.router_init_std / math.sqrt(cfg.hidden_size), generator=g)
+            elif is_expert_param(name):
+                layer = int(name.split(".")[1])
+                which = 1 if name.endswith("w1") else 2
+                for e in range(t.shape[0]):
+                    ge.manual_seed(((seed * 1000003 + layer) * 4099 + expert_offset + e) * 3 + which)
+                    t[e].normal_(0.0, cfg.initializer_range, generator=ge)
             else:
                 t.normal_(0.0, cfg.initializer_range, generator=g)
 
@@ -290,12 +319,16 @@ class Qwen3Model(nn.Module):
     """
 
     def __init__(self, cfg: Qwen3Config, params: Dict[str, torch.Tensor], recompute: bool = False,
-                 tp_group=None, tp_size: int = 1, tp_rank: int = 0):
+                 tp_group=None, tp_size: int = 1, tp_rank: int = 0, ep_group=None, ep_size: int = 1,
+                 ep_exchange=None):
         super().__init__()
         self.cfg = cfg
         self.p = params
         self.recompute = recompute
         self.tp_group, self.tp_size, self.tp_rank = tp_group, tp_size, tp_rank
+        # expert parallelism: this rank holds num_experts / ep_size experts; tokens travel to their
+        # experts' owners through ``ep_exchange`` (peer-memory kernels) or all-to-all over ``ep_group``
+        self.ep_group, self.ep_size, self.ep_exchange = ep_group, ep_size, ep_exchange
         dev = next(iter(params.values())).device
         cos, sin = ops.ref.rope_tables(cfg.max_position_embeddings, cfg.head_dim, cfg.rope_theta, dev)
         self.register_buffer("rope_cos", cos, persistent=False)
@@ -319,6 +352,11 @@ class Qwen3Model(nn.Module):
         pre = f"layers.{i}."
         h = ops.rmsnorm(x, p[pre + "post_attention_layernorm"], cfg.rms_norm_eps)
         if cfg.is_moe:
+            if self.ep_size > 1:
+                from libra_b200.parallel.expert_parallel import ep_moe_mlp
+
+                return ep_moe_mlp(h, x, p[pre + "router"], p[pre + "experts.w1"], p[pre + "experts.w2"], cfg,
+                                  self.ep_group, self.ep_exchange)
             from libra_b200.models.moe import moe_mlp
 
             return moe_mlp(h, x, p[pre + "router"], p[pre + "experts.w1"], p[pre + "experts.w2"], cfg)

@@ -177,3 +177,39 @@ def _tp_engine_worker(rank, world, port, out_dir):
 def test_tp_engine_keeps_replicated_params_in_sync(tmp_path):
     _spawn(_tp_engine_worker, 2, str(tmp_path))
     assert {p.name for p in tmp_path.iterdir()} == {"tpe_ok_0", "tpe_ok_1"}
+
+
+def _ep_engine_worker(rank, world, port, out_dir):
+    """EP=2 engine (each rank: its own trajectories, half the experts) against an EP=1 engine that
+    sees both ranks' trajectories: same loss, same dense parameters, same experts after one update."""
+    _init(rank, world, port)
+    from libra_b200.engine.train_engine import B200TrainEngine
+    from libra_b200.workflow.synthetic import GRPOWorkload, LengthDist
+
+    wl = GRPOWorkload("ep", vocab_size=2048, prompts_per_step=2, group_size=2, prompt=LengthDist(12, 0.3, 6, 20),
+                      response=LengthDist(8, 0.3, 2, 12))
+    trajs = [wl.trajectories(0, rank=r) for r in range(world)]
+    solo_group = [dist.new_group([r]) for r in range(world)][rank]
+    ref = B200TrainEngine("tiny-moe", device="cpu", seed=3, learning_rate=1e-3, micro_batch_size=4,
+                          dp_group=solo_group)
+    ref.initialize()
+    ep = B200TrainEngine("tiny-moe", device="cpu", seed=3, learning_rate=1e-3, micro_batch_size=4, ep_size=2)
+    ep.initialize()
+    El = ref.cfg.num_experts // world
+    for n, p in ep.params.items():
+        want = ref.params[n][rank * El:(rank + 1) * El] if "experts." in n else ref.params[n]
+        assert torch.equal(p.detach(), want.detach()), n
+    s_ref = ref.grpo_update(trajs[0] + trajs[1])
+    s_ep = ep.grpo_update(trajs[rank])
+    assert abs(s_ref["loss"] - s_ep["loss"]) < 1e-3, (s_ref["loss"], s_ep["loss"])
+    assert abs(s_ref["grad_norm"] - s_ep["grad_norm"]) < 1e-2 * max(1.0, s_ref["grad_norm"])
+    for n, p in ep.params.items():
+        want = ref.params[n][rank * El:(rank + 1) * El] if "experts." in n else ref.params[n]
+        torch.testing.assert_close(p.detach().float(), want.detach().float(), rtol=2e-2, atol=2e-3, msg=n)
+    open(os.path.join(out_dir, f"epe_ok_{rank}"), "w").close()
+    dist.destroy_process_group()
+
+
+def test_expert_parallel_engine_matches_one_rank(tmp_path):
+    _spawn(_ep_engine_worker, 2, str(tmp_path))
+    assert {p.name for p in tmp_path.iterdir()} == {"epe_ok_0", "epe_ok_1"}

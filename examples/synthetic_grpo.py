@@ -30,8 +30,15 @@ def main():
     ap.add_argument("--log-dir", default="")
     ap.add_argument("--stats-out", default="")
     ap.add_argument("--eval-interval", type=int, default=-1, help="override eval_interval (-1 = keep the config's)")
+    ap.add_argument("--replan-every", type=int, default=0,
+                    help="turn on the Global Resource Planner with online replanning every N steps")
     a = ap.parse_args()
     cfg = load_config(a.config)
+    if a.replan_every > 0:
+        p = cfg.global_resource_planner
+        p.enabled, p.initial_allocation_strategy = True, "configured"
+        p.plan_interval, p.warmup_steps, p.min_history_size = a.replan_every, 1, 1
+        p.runtime_async_planning, p.runtime_dynamic_reconfiguration_enabled = False, True
     if a.total_steps:
         cfg.total_steps = a.total_steps
     if a.eval_interval >= 0:

@@ -79,7 +79,7 @@ def compute_group_advantages(trajectories: List[Dict[str, Any]]) -> Dict[str, fl
 
 
 class AsyncRLTrainer:
-    def __init__(self, config: AsyncRLConfig, train_engine=None, rollout_engine=None):
+    def __init__(self, config: AsyncRLConfig, train_engine=None, rollout_engine=None, process_launcher=None):
         self.config = config
         self.rank = int(os.environ.get("RANK", "0"))
         self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -104,6 +104,10 @@ class AsyncRLTrainer:
         self.history_collector: Optional[HistoryDataCollector] = None
         self.global_resource_planner = None
         self.runtime_elastic_executor = None
+        self.process_launcher = process_launcher  # the executor's launcher (tests inject a fake one)
+        self.calibrator = None
+        self.reconfigurations: List[Dict[str, Any]] = []
+        self._pending_decision = None
         self._grp_pool: Optional[ThreadPoolExecutor] = None
         self._grp_future: Optional[Future] = None
         trace = os.environ.get("RL_TRAIN_PHASE_TRACE", "0") == "1" or bool(config.phase_trace_enabled)
@@ -270,6 +274,16 @@ class AsyncRLTrainer:
             self.global_resource_planner = GlobalResourcePlanner.from_config(self.config)
             if self.config.global_resource_planner.runtime_async_planning:
                 self._grp_pool = ThreadPoolExecutor(max_workers=1, thread_name_prefix="grp")
+            if self.config.global_resource_planner.runtime_dynamic_reconfiguration_enabled:
+                # online replanning: rank 0 applies the planner's decisions between steps
+                from libra_b200.infra.elastic.runtime_executor import RuntimeElasticExecutor
+
+                self.runtime_elastic_executor = RuntimeElasticExecutor(
+                    config=self.config, planner=self.global_resource_planner, train_engine=self.train_engine,
+                    rollout_engine=self.rollout_engine, dispatcher=self.dispatcher, launcher=self.process_launcher)
+            from libra_b200.infra.cost_model.calibrator import ShadowCalibrator
+
+            self.calibrator = ShadowCalibrator()
 
     def _is_batch_source(self) -> bool:
         if self._single_batch_source:
@@ -486,6 +500,7 @@ class AsyncRLTrainer:
                     print(f"Step {step}/{c.total_steps}: {time.time() - t_start:.1f}s loss={stats.get('loss', 0):.4f} "
                           f"kl={stats.get('kl', 0):.4f} reward={stats['reward_mean']:.3f} "
                           f"n={len(batch)} rollout={rollout_time:.2f}s train={train_time:.2f}s", flush=True)
+            self._apply_pending_reconfiguration(step)
             if self.step_callback is not None:
                 self.step_callback(step, stats, batch)
             self._run_periodic_evaluation(workflow, dataset, step)
@@ -591,6 +606,23 @@ class AsyncRLTrainer:
             self._grp_future = None
             self._apply_decision(decision)
         grp.observe_batch([{"input_len": t.get("prompt_len", 0), "output_len": t.get("output_len", 0)} for t in batch])
+        plan = grp.active_plan
+        if self.calibrator is not None and plan is not None:
+            # measured vs modelled phase times of the active plan: the calibrator's efficiencies rescale the
+            # planner's B200 model before it is asked for the next decision
+            from libra_b200.infra.cost_model.calibrator import EpochRunData
+
+            self.calibrator.update(EpochRunData(
+                t_train_real=float(stats["train_time"]) + float(stats.get("recompute_logprob_time", 0.0)),
+                t_rollout_real=float(stats["rollout_time"]), t_train_predicted=float(plan.t_train),
+                t_rollout_predicted=float(plan.t_rollout),
+                gen_lengths=[float(t.get("output_len", 0)) for t in batch],
+                prompt_lengths=[float(t.get("prompt_len", 0)) for t in batch], epoch_id=step))
+            cm = getattr(getattr(grp, "evaluator", None), "analytic", None)
+            if cm is not None:
+                if not hasattr(self, "_calib_base"):
+                    self._calib_base = (cm.training_model.train_mfu, cm.rollout_model.decode_bw_util)
+                self.calibrator.apply_to_cost_model(cm, *self._calib_base)
         metrics = grp.observe_runtime(step=step, dispatcher_metrics=self.dispatcher.get_runtime_metrics()
                                       if self.dispatcher else {},
                                       step_stats={"rollout_time": stats["rollout_time"],
@@ -604,13 +636,84 @@ class AsyncRLTrainer:
             self._apply_decision(grp.plan_if_needed(step, cfg, None, metrics))
 
     def _apply_decision(self, decision) -> None:
+        """Rank 0: log the planner's decision; a reconfiguration is applied at the
+        end of the step by ``_apply_pending_reconfiguration`` with every rank."""
         self.last_planner_decision = decision
         log = os.path.join(self.config.log_dir, "global_resource_planner_decisions.jsonl")
         os.makedirs(self.config.log_dir, exist_ok=True)
         with open(log, "a", encoding="utf-8") as fh:
             fh.write(json.dumps(decision.to_dict(), default=str) + "\n")
-        if decision.should_reconfigure and self.runtime_elastic_executor is not None:
-            self.runtime_elastic_executor.execute(decision)
+        if self.runtime_elastic_executor is not None and (
+                decision.should_reconfigure or getattr(decision, "elastic_hybrid_signal", None) is not None):
+            self._pending_decision = decision
+
+    def _apply_pending_reconfiguration(self, step: int) -> None:
+        """Collective (every rank, end of step, outside any other collective).
+
+        Rank 0 broadcasts whether the planner asked for a reconfiguration.  If
+        so, rank 0 runs ``RuntimeElasticExecutor.execute`` — which, for
+        strategies that move GPUs (cluster swap), posts a drain request and
+        waits for the peer ranks' ready files — while the other ranks poll
+        the coordination directory and answer requests
+        (``follow_reconfiguration_request``) until rank 0 reaches the closing
+        barrier.  The applied layout lands in the shared config object, so the
+        next history record shows it."""
+        flag = 1 if (self.is_main_process and self._pending_decision is not None) else 0
+        if self.world_size > 1 and dist.is_initialized():
+            dev = self.train_engine.device if getattr(self.train_engine, "device", None) is not None and \
+                dist.get_backend() == "nccl" else torch.device("cpu")
+            t = torch.tensor([flag], dtype=torch.int32, device=dev)
+            dist.broadcast(t, src=0)
+            flag = int(t.item())
+        if not flag:
+            return
+        if self.is_main_process:
+            decision, self._pending_decision = self._pending_decision, None
+            try:
+                result = self.runtime_elastic_executor.execute(decision)
+                record = {"step": step, **result.to_dict(),
+                          "layout": {"train_gpus": self.config.train_gpus, "rollout_gpus": self.config.rollout_gpus,
+                                     "rollout_tp_list": list(self.config.heterogeneous_rollout.tp_list)}}
+            except Exception as exc:  # noqa: BLE001 - a failed reconfiguration keeps the current layout
+                record = {"step": step, "applied": False, "reason": f"error: {type(exc).__name__}: {exc}"}
+            self.reconfigurations.append(record)
+            self.stats["reconfiguration"] = record
+            pool = getattr(self.runtime_elastic_executor, "elastic_pool", None)
+            if pool is not None and getattr(self.train_engine, "elastic_gradient_domain", None) is None:
+                self.train_engine.elastic_gradient_domain = pool.gradient_domain
+            with open(os.path.join(self.config.log_dir, "runtime_reconfigurations.jsonl"), "a",
+                      encoding="utf-8") as fh:
+                fh.write(json.dumps(record, default=str) + "\n")
+            if self.world_size > 1 and dist.is_initialized():
+                dist.barrier()
+            return
+        from libra_b200.infra.elastic.runtime_executor import follow_reconfiguration_request
+
+        p = self.config.global_resource_planner
+        coord = getattr(p, "runtime_reconfiguration_coord_dir", "") or os.path.join(self.config.log_dir,
+                                                                                    "runtime_reconfiguration")
+        drain = None
+        if self.dispatcher is not None:
+            def drain(timeout=float(p.runtime_drain_timeout_s)):
+                self.dispatcher.pause()
+                self.dispatcher.wait_until_idle(timeout=timeout)
+        work = dist.barrier(async_op=True)
+        answered = set()
+        while not work.is_completed():
+            cid = None
+            req = Path(coord) / "request.json"
+            if req.exists():
+                try:
+                    cid = json.loads(req.read_text(encoding="utf-8")).get("coord_id")
+                except (OSError, ValueError):
+                    cid = None
+            if cid and cid not in answered:
+                follow_reconfiguration_request(coord, self.rank, drain=drain)
+                answered.add(cid)
+            time.sleep(0.02)
+        work.wait()
+        if drain is not None and answered:
+            self.dispatcher.resume()
 
     def _save_checkpoint(self, step: int) -> None:
         from libra_b200.engine.checkpointing import DistributedCheckpointManager

@@ -18,12 +18,12 @@ def _free_port() -> int:
     return port
 
 
-def _run(tmp_path, task, *extra, **env_extra):
+def _run(tmp_path, task, *extra, steps=3, **env_extra):
     env = dict(os.environ, DIST_BACKEND="gloo", CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="2", **env_extra)
     out = tmp_path / "stats.json"
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
            "--master-port", str(_free_port()), os.path.join(ROOT, "examples", "synthetic_grpo.py"),
-           "--config", os.path.join(ROOT, "libra_b200", "configs", "tiny_cpu_gloo.yaml"), "--total-steps", "3",
+           "--config", os.path.join(ROOT, "libra_b200", "configs", "tiny_cpu_gloo.yaml"), "--total-steps", str(steps),
            "--log-dir", str(tmp_path), "--stats-out", str(out), "--task", task, *extra]
     proc = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert proc.returncode == 0, proc.stderr[-3000:]
@@ -31,10 +31,11 @@ def _run(tmp_path, task, *extra, **env_extra):
 
 
 def test_two_rank_async_grpo_plumbing(tmp_path):
-    stats = _run(tmp_path, "target_token")
-    assert stats["n_trajectories"] == 16 and stats["version"] == 3
+    """The CPU/gloo plumbing configuration: 2 ranks, 10 steps, staleness bound 1."""
+    stats = _run(tmp_path, "target_token", steps=10)
+    assert stats["n_trajectories"] == 16 and stats["version"] == 10
     hist = glob.glob(str(tmp_path / "history" / "*history_*.jsonl"))
-    assert hist and len(open(hist[0]).read().splitlines()) == 3
+    assert hist and len(open(hist[0]).read().splitlines()) == 10
     traces = glob.glob(str(tmp_path / "phase_trace" / "phase_trace_rank*.jsonl"))
     assert len(traces) == 2
     phases = {json.loads(l)["phase"] for l in open(sorted(traces)[0]) if '"phase_span"' in l}
@@ -58,3 +59,18 @@ def test_periodic_evaluation_rank0_with_sentinel(tmp_path):
     assert 0.0 <= rows[0]["eval_accuracy"] <= 1.0 and rows[0]["eval_failures"] == 0
     samples = (tmp_path / "eval" / "eval_samples_step_2.jsonl").read_text().splitlines()
     assert 1 <= len(samples) <= 6
+
+
+def test_online_replanning_applies_forced_decisions(tmp_path):
+    """Planner on, forced reconfiguration every step: rank 0 applies each decision through the
+    RuntimeElasticExecutor while rank 1 answers the drain request between steps."""
+    stats = _run(tmp_path, "target_token", "--replan-every", "1", steps=4, GRP_FORCE_RUNTIME_RECONFIGURE="1",
+                 GRP_FORCE_ROLLOUT_TP_LIST="1")
+    assert stats["version"] == 4
+    recs = [json.loads(l) for l in (tmp_path / "runtime_reconfigurations.jsonl").read_text().splitlines()]
+    assert [r["step"] for r in recs] == [1, 2, 3]
+    assert all(r["applied"] and "peer_reconfig_drain:1" in r["actions"] for r in recs)
+    assert (tmp_path / "runtime_reconfiguration" / "ready" / "rank_1.json").exists()
+    hist = glob.glob(str(tmp_path / "history" / "*history_*.jsonl"))
+    rows = [json.loads(l) for l in open(hist[0]).read().splitlines()]
+    assert rows[-1]["resource_config"]["rollout_gpus"] == 1

@@ -17,6 +17,15 @@ split layout is fixed by ``max_model_len`` (not by the current lengths) and
 its split workspace is preallocated, so the same graph serves every step of a
 generation.
 
+Dense models on one GPU take the fused decode path: every linear layer is a
+stream-K tcgen05 GEMM into an fp32 accumulator (all SMs stream every weight,
+however few rows the batch has), and the work after it is one fused kernel
+(q/k norm + RoPE + KV-cache write; residual add + RMSNorm; SwiGLU; sampling),
+which also clears the accumulator for its next use.  Attention is the
+stream-K paged decode kernel, whose grid is one CTA per SM whatever the
+lengths.  Per layer: 4 GEMMs + 5 kernels.  ``LIBRA_DECODE_FUSED=0`` keeps the
+unfused kernels (bf16 GEMM epilogues, split-layout attention).
+
 The vLLM servers of the reference do the same with their CUDA-graph mode
 (the reference's launch scripts run them with ``--enforce-eager`` instead);
 this engine always captures unless ``LIBRA_DECODE_GRAPHS=0``.
@@ -79,6 +88,23 @@ class DecodeGraphs:
         self.attn_out = torch.zeros(B, nq, cfg.head_dim, dtype=torch.bfloat16, device=dev)
         self.part_out = torch.zeros(B, nq, self.S, cfg.head_dim, dtype=torch.float32, device=dev)
         self.part_ml = torch.zeros(B, nq, self.S, 2, dtype=torch.float32, device=dev)
+        self.fused = self._fused_supported()
+        if self.fused:
+            H, F = cfg.hidden_size, cfg.intermediate_size
+            V = runner.lm_head.shape[0]
+            nkv = runner.nkv
+            f32 = dict(dtype=torch.float32, device=dev)
+            bf = dict(dtype=torch.bfloat16, device=dev)
+            # stream-K accumulators: zero now, and every consumer leaves them zero
+            self.acc_qkv = torch.zeros(B, (nq + 2 * nkv) * cfg.head_dim, **f32)
+            self.acc_h = torch.zeros(B, H, **f32)
+            self.acc_gu = torch.zeros(B, 2 * F, **f32)
+            self.acc_logits = torch.zeros(B, V, **f32)
+            self.xbuf = torch.zeros(B, H, **bf)
+            self.hbuf = torch.zeros(B, H, **bf)
+            self.qbuf = torch.zeros(B, nq, cfg.head_dim, **bf)
+            self.abuf = torch.zeros(B, F, **bf)
+            self.attn_ws = ops.decode_workspace(B, nq, cfg.head_dim, dev)
         self._pad_rows(0, B)
         # per-row cache of what the block-table staging row holds: (seq_id, blocks written)
         self._row_owner: List[Optional[str]] = [None] * B
@@ -88,8 +114,55 @@ class DecodeGraphs:
         self.replays = 0
         self.io_bytes = {"h2d": 0, "d2h": 0}
 
+    def _fused_supported(self) -> bool:
+        r, cfg = self.r, self.cfg
+        if os.environ.get("LIBRA_DECODE_FUSED", "1") == "0" or self.device.type != "cuda":
+            return False
+        return (not cfg.is_moe and r.tp_size == 1 and cfg.head_dim == 128 and self.bs == 16
+                and cfg.num_attention_heads % cfg.num_key_value_heads == 0
+                and cfg.num_attention_heads // cfg.num_key_value_heads in (1, 2, 4, 5, 8)
+                and cfg.num_key_value_heads <= 8 and cfg.hidden_size % 8 == 0 and cfg.hidden_size <= 8192)
+
+    def reset_accumulators(self) -> None:
+        """Zero the stream-K accumulators and attention counters (after a
+        failed replay, whose consumers may not have run)."""
+        if self.fused:
+            for t in (self.acc_qkv, self.acc_h, self.acc_gu, self.acc_logits, self.attn_ws[2]):
+                t.zero_()
+
     # ------------------------------------------------------------------ forward recorded in the graphs
+    def _forward_fused(self, b: int) -> None:
+        r, cfg, p = self.r, self.cfg, self.r.p
+        eps = cfg.rms_norm_eps
+        tok, slot, seed, pos64 = self.d64[0, :b], self.d64[1, :b], self.d64[2, :b], self.d64[3, :b]
+        pos32, lens = self.d32[0, :b], self.d32[1, :b]
+        x, h = self.xbuf[:b], self.hbuf[:b]
+        acc_h = self.acc_h[:b]
+        torch.index_select(p["embed_tokens"], 0, tok, out=x)
+        # acc_h is zero here, so this is the first layer's input RMSNorm
+        ops.decode_residual_norm(x, acc_h, p["layers.0.input_layernorm"], h, eps)
+        part_o, part_ml, counters = self.attn_ws
+        L = cfg.num_hidden_layers
+        for layer in range(L):
+            pre = f"layers.{layer}."
+            ops.gemm_streamk(h, p[pre + "qkv_proj"], self.acc_qkv[:b])
+            ops.decode_qkv_post(self.acc_qkv[:b], p[pre + "q_norm"], p[pre + "k_norm"], pos32, r.cos, r.sin, slot,
+                                self.qbuf[:b], self.kv.k[layer], self.kv.v[layer], eps)
+            attn = ops.decode_attention(self.qbuf[:b], self.kv.k[layer], self.kv.v[layer], self.dtbl, lens,
+                                        self.attn_out[:b], part_o, part_ml, counters, r.scale)
+            ops.gemm_streamk(attn.view(b, -1), p[pre + "o_proj"], acc_h)
+            ops.decode_residual_norm(x, acc_h, p[pre + "post_attention_layernorm"], h, eps)
+            ops.gemm_streamk(h, p[pre + "gate_up_proj"], self.acc_gu[:b])
+            ops.decode_swiglu(self.acc_gu[:b], self.abuf[:b])
+            ops.gemm_streamk(self.abuf[:b], p[pre + "down_proj"], acc_h)
+            nxt = p[f"layers.{layer + 1}.input_layernorm"] if layer + 1 < L else p["norm"]
+            ops.decode_residual_norm(x, acc_h, nxt, h, eps)
+        ops.gemm_streamk(h, r.lm_head, self.acc_logits[:b])
+        ops.sample_tokens(self.acc_logits[:b], self.df[:b], seed, pos64, self.out_tok[:b], self.out_lp[:b])
+
     def _forward(self, b: int) -> None:
+        if self.fused:
+            return self._forward_fused(b)
         r, cfg, p = self.r, self.cfg, self.r.p
         tok, slot, seed, pos64 = self.d64[0, :b], self.d64[1, :b], self.d64[2, :b], self.d64[3, :b]
         pos32, lens = self.d32[0, :b], self.d32[1, :b]

@@ -546,6 +546,87 @@ def sample_tokens(logits, temperature, seeds, positions, out_tok, out_lp, next_t
     return out_tok, out_lp
 
 
+def gemm_streamk(a, w, acc):
+    """``acc += a . w^T`` with the stream-K mode of the tcgen05 GEMM: every SM
+    takes an equal share of the tiles x K-blocks iterations, so a skinny GEMM
+    (a decode step's few rows) streams the weight on all SMs.  ``acc`` is fp32
+    [M, N]; the fused decode consumers read it and leave it zeroed."""
+    if a.device.type != "cuda":
+        acc.add_(a.float() @ w.float().t())
+        return acc
+    ext().gemm_bf16(a, w, acc, False, False, EPI_ACC_F32, None, error_flag(a.device), True)
+    return acc
+
+
+def _take(acc, rows=None):
+    v = (acc if rows is None else acc[:rows]).clone()
+    (acc if rows is None else acc[:rows]).zero_()
+    return v
+
+
+def decode_qkv_post(acc, qw, kw, pos, cos, sin, slot, q_out, k_cache, v_cache, eps: float):
+    """Fused decode step after the QKV GEMM: round the fp32 accumulator to bf16,
+    per-head RMSNorm of q and k, RoPE at ``pos``, q -> ``q_out`` [B, nq, D],
+    k and v of the new token straight into cache row ``slot``; zeroes the
+    accumulator rows it read."""
+    if acc.device.type != "cuda":
+        B, nq, D = q_out.shape
+        nkv = k_cache.shape[2]
+        x = _take(acc, B).to(torch.bfloat16)
+        q, k, v = ref.qk_norm_rope(x, qw, kw, pos[:B], cos, sin, nq, nkv, eps)
+        q_out.copy_(q)
+        k_cache.view(-1, nkv, D)[slot[:B]] = k.to(k_cache.dtype)
+        v_cache.view(-1, nkv, D)[slot[:B]] = v.to(v_cache.dtype)
+        return q_out
+    ext().decode_qkv_post(acc, qw, kw, pos, cos, sin, slot, q_out, k_cache, v_cache, float(eps))
+    return q_out
+
+
+def decode_residual_norm(x, acc, w, h_out, eps: float):
+    """``x = bf16(x + acc)`` in place, ``h_out = RMSNorm(x) * w``; zeroes ``acc[:B]``."""
+    if x.device.type != "cuda":
+        x.copy_((x.float() + _take(acc, x.shape[0])).to(x.dtype))
+        h_out.copy_(ref.rmsnorm(x, w, eps))
+        return h_out
+    ext().decode_residual_norm(x, acc, w, h_out, float(eps))
+    return h_out
+
+
+def decode_swiglu(acc, a):
+    """``a = silu(bf16(gate)) * bf16(up)`` from the gate/up accumulator [B, 2F]; zeroes it."""
+    if a.device.type != "cuda":
+        B, F = a.shape
+        gu = _take(acc, B).to(torch.bfloat16).float()
+        a.copy_((torch.nn.functional.silu(gu[:, :F]) * gu[:, F:]).to(a.dtype))
+        return a
+    ext().decode_swiglu(acc, a)
+    return a
+
+
+def decode_attention(q, k_cache, v_cache, block_tables, seq_lens, out, part_o, part_ml, counters, scale: float):
+    """Paged decode attention for rows ``0..out.shape[0]-1``: stream-K over the
+    sequences' KV blocks (one CTA per SM, every CTA the same share), partial
+    results merged in the kernel.  Workspace ``part_o`` [SMs + B, Hq, D] /
+    ``part_ml`` [SMs + B, Hq, 2] fp32 and ``counters`` [B] int32 (zero before
+    the first call; the kernel leaves them zero) are the caller's, so the call
+    allocates nothing and can be captured."""
+    if q.device.type != "cuda":
+        B = out.shape[0]
+        return paged_decode(q[:B], k_cache, v_cache, block_tables, seq_lens, out, None, None, 0, scale)
+    ext().decode_attention(q, k_cache, v_cache, block_tables, seq_lens, out, part_o, part_ml, counters,
+                           error_flag(q.device), float(scale))
+    return out
+
+
+def decode_workspace(max_batch: int, num_heads: int, head_dim: int, device):
+    """Workspace of ``decode_attention`` for up to ``max_batch`` rows."""
+    sms = torch.cuda.get_device_properties(device).multi_processor_count if device.type == "cuda" else 1
+    slots = sms + max_batch
+    return (torch.zeros(slots, num_heads, head_dim, dtype=torch.float32, device=device),
+            torch.zeros(slots, num_heads, 2, dtype=torch.float32, device=device),
+            torch.zeros(max_batch, dtype=torch.int32, device=device))
+
+
 # ---------------------------------------------------------------------------
 # optimizer
 # ---------------------------------------------------------------------------

@@ -9,7 +9,7 @@ void gemm_allgather(torch::Tensor a, torch::Tensor b, bool b_mn, torch::Tensor y
                     std::vector<int64_t> ready, torch::Tensor gath, torch::Tensor counter, int64_t me, int64_t call,
                     torch::Tensor err);
 void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, bool b_mn, int64_t epi,
-               c10::optional<torch::Tensor> residual, torch::Tensor err);
+               c10::optional<torch::Tensor> residual, torch::Tensor err, bool streamk);
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps);
 torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dw,
                           bool accumulate_dw, c10::optional<torch::Tensor> dx_accum);
@@ -83,12 +83,30 @@ void ep_pull(std::vector<int64_t> tx, std::vector<int64_t> flags, int64_t me, in
              torch::Tensor src_row, int64_t k, int64_t max_rows, torch::Tensor out, c10::optional<torch::Tensor> gath,
              int64_t epoch, int64_t grid, torch::Tensor err);
 }  // namespace ep
+void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
+                      torch::Tensor seq_lens, torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml,
+                      torch::Tensor counters, torch::Tensor err, double scale);
+void decode_qkv_post(torch::Tensor acc, torch::Tensor qw, torch::Tensor kw, torch::Tensor pos, torch::Tensor cos_t,
+                     torch::Tensor sin_t, torch::Tensor slot, torch::Tensor q_out, torch::Tensor k_cache,
+                     torch::Tensor v_cache, double eps);
+void decode_residual_norm(torch::Tensor x, torch::Tensor acc, torch::Tensor w, torch::Tensor h_out, double eps);
+void decode_swiglu(torch::Tensor acc, torch::Tensor a);
 }  // namespace libra
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("decode_attention", &libra::decode_attention,
+        "paged decode attention, stream-K over KV blocks with an in-kernel merge (no allocation)", py::arg("q"),
+        py::arg("k_cache"), py::arg("v_cache"), py::arg("block_tables"), py::arg("seq_lens"), py::arg("out"),
+        py::arg("part_o"), py::arg("part_ml"), py::arg("counters"), py::arg("err"), py::arg("scale"));
+  m.def("decode_qkv_post", &libra::decode_qkv_post,
+        "fused decode: qkv accumulator -> q/k RMSNorm + RoPE -> q and the paged KV cache (zeroes the accumulator)");
+  m.def("decode_residual_norm", &libra::decode_residual_norm,
+        "fused decode: x += acc (bf16), h = RMSNorm(x) * w (zeroes the accumulator)");
+  m.def("decode_swiglu", &libra::decode_swiglu, "fused decode: SwiGLU of the gate/up accumulator (zeroes it)");
   m.doc() = "libra_b200 sm_100a kernels";
   m.def("gemm_bf16", &libra::gemm_bf16, "tcgen05 bf16 GEMM", py::arg("a"), py::arg("b"), py::arg("c"),
-        py::arg("a_mn"), py::arg("b_mn"), py::arg("epi"), py::arg("residual"), py::arg("err"));
+        py::arg("a_mn"), py::arg("b_mn"), py::arg("epi"), py::arg("residual"), py::arg("err"),
+        py::arg("streamk") = false);
   m.def("gemm_swiglu", &libra::gemm_swiglu, "tcgen05 gate/up GEMM with fused SwiGLU epilogue", py::arg("x"),
         py::arg("w"), py::arg("a"), py::arg("gu"), py::arg("err"));
   m.def("grouped_gemm", &libra::grouped_gemm,

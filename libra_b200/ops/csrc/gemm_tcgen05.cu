@@ -196,11 +196,50 @@ __device__ __forceinline__ void store_tile_row(uint32_t tacc, int row, int nb, i
   }
 }
 
+// Work of one CTA of the single-CTA kernel, as segments (tile, [kb0, kb1)):
+//  * streamk == 0: whole tiles blockIdx.x, blockIdx.x + gridDim.x, ...
+//  * streamk != 0 (accumulate epilogue): the contiguous share
+//    [c * T / G, (c + 1) * T / G) of the T = tiles x K-blocks iterations,
+//    walked tile by tile.  Skinny GEMMs (a decode step's M <= 128 rows) have
+//    too few output tiles to keep every SM streaming the weight; this way all
+//    G CTAs move the same number of K blocks whatever the tile count.
+struct Work {
+  int nkb, step, it, hi;
+  bool sk;
+  __device__ __forceinline__ Work(int num_tiles, int num_kb, int streamk) : nkb(num_kb), sk(streamk != 0) {
+    if (sk) {
+      const long long T = (long long)num_tiles * num_kb;
+      it = (int)(T * blockIdx.x / gridDim.x);
+      hi = (int)(T * (blockIdx.x + 1) / gridDim.x);
+      step = 0;
+    } else {
+      it = blockIdx.x;
+      hi = num_tiles;
+      step = gridDim.x;
+    }
+  }
+  __device__ __forceinline__ bool next(int& tile, int& kb0, int& kb1) {
+    if (it >= hi) return false;
+    if (!sk) {
+      tile = it;
+      kb0 = 0;
+      kb1 = nkb;
+      it += step;
+      return true;
+    }
+    tile = it / nkb;
+    kb0 = it - tile * nkb;
+    kb1 = min(nkb, kb0 + (hi - it));
+    it += kb1 - kb0;
+    return true;
+  }
+};
+
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* __restrict__ C,
                      const __nv_bfloat16* __restrict__ R, int M, int N, int K, int ldc, int ldr, int* err,
-                     __nv_bfloat16* __restrict__ C2, int ldc2) {
+                     __nv_bfloat16* __restrict__ C2, int ldc2, int streamk = 0) {
   static_assert(EPI != kSwiGLU || (BN == 256 && !B_MN), "SwiGLU epilogue: BN 256, K-major weight");
   // output columns per tile: BN, or 128 features for SwiGLU (N is then F)
   constexpr int kTileN = EPI == kSwiGLU ? 128 : BN;
@@ -251,11 +290,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_phase = 0;  // per stage: ever issued / parity of last issue
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      Work wk(num_tiles, num_kb, streamk);
+      int tile, kb0, kb1;
+      while (ok && wk.next(tile, kb0, kb1)) {
         int mb, nb;
         tile_coords(tile, num_m, num_n, mb, nb);
         const int m0 = mb * BM, n0 = nb * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, err, kTimeoutSmemEmpty)) { ok = false; break; }
           mbar_expect_tx(&full[stage], CF::kStageBytes);
           uint8_t* a_dst = smA + stage * CF::kStageA;
@@ -293,13 +334,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      Work wk(num_tiles, num_kb, streamk);
+      int tile, kb0, kb1;
+      for (; ok && wk.next(tile, kb0, kb1); ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, err, kTimeoutTmemEmpty)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, err, kTimeoutTmaFull)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smA + stage * CF::kStageA);
@@ -312,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                         : make_sw128_desc(a_addr + k * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? make_sw128_desc(b_addr + k * 2048, 64 * BK * 2, 1024)
                                         : make_sw128_desc(b_addr + k * 32, 16, 1024);
-            umma_f16(d_tmem, adesc, bdesc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            umma_f16(d_tmem, adesc, bdesc, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
           if (++stage == S) { stage = 0; phase ^= 1u; }
@@ -329,15 +372,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     const int row_in_tile = quarter * 32 + lane;
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+    Work wk(num_tiles, num_kb, streamk);
+    int tile, kb0, kb1;
+    for (; wk.next(tile, kb0, kb1); ++local) {
       int mb, nb;
       tile_coords(tile, num_m, num_n, mb, nb);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, err, kTimeoutTmemFull)) break;
       tc_fence_after();
+      // a tile that this CTA covers over the whole K range is added with plain
+      // loads and stores; a partial one (stream-K) with reductions at L2
       store_tile_row<BN, EPI>(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN, mb * BM + row_in_tile, nb, M,
-                              N, C, R, ldc, ldr, C2, ldc2);
+                              N, C, R, ldc, ldr, C2, ldc2, kb0 > 0 || kb1 < num_kb);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -1107,7 +1154,7 @@ static int num_sms() {
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, void* c, const __nv_bfloat16* r, int M, int N, int K,
-                   int ldc, int ldr, int* err, cudaStream_t st) {
+                   int ldc, int ldr, int* err, cudaStream_t st, bool streamk = false) {
   auto kern = gemm_bf16_kernel<BN, A_MN, B_MN, EPI>;
   constexpr int smem = Cfg<BN>::kSmemBytes;
   static bool configured = false;  // one static per instantiation
@@ -1116,8 +1163,11 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, void* c, const 
     configured = true;
   }
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  const int grid = tiles < num_sms() ? tiles : num_sms();
-  kern<<<grid, kThreads, smem, st>>>(ta, tb, c, r, M, N, K, ldc, ldr, err, nullptr, 0);
+  // stream-K: every SM takes a share of the tiles x K-blocks iterations (at least one each)
+  const long long units = (EPI == kAccumF32 && streamk) ? (long long)tiles * ((K + BK - 1) / BK) : tiles;
+  const int grid = units < num_sms() ? (int)units : num_sms();
+  kern<<<grid, kThreads, smem, st>>>(ta, tb, c, r, M, N, K, ldc, ldr, err, nullptr, 0,
+                                     (EPI == kAccumF32 && streamk) ? 1 : 0);
   LIBRA_LAUNCH_CHECK();
 }
 
@@ -1209,11 +1259,12 @@ static void dispatch_pair(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUt
 
 template <int BN, int EPI>
 static void dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, void* c,
-                           const __nv_bfloat16* r, int M, int N, int K, int ldc, int ldr, int* err, cudaStream_t st) {
-  if (!a_mn && !b_mn) launch<BN, false, false, EPI>(ta, tb, c, r, M, N, K, ldc, ldr, err, st);
-  else if (!a_mn && b_mn) launch<BN, false, true, EPI>(ta, tb, c, r, M, N, K, ldc, ldr, err, st);
-  else if (a_mn && b_mn) launch<BN, true, true, EPI>(ta, tb, c, r, M, N, K, ldc, ldr, err, st);
-  else launch<BN, true, false, EPI>(ta, tb, c, r, M, N, K, ldc, ldr, err, st);
+                           const __nv_bfloat16* r, int M, int N, int K, int ldc, int ldr, int* err, cudaStream_t st,
+                           bool streamk = false) {
+  if (!a_mn && !b_mn) launch<BN, false, false, EPI>(ta, tb, c, r, M, N, K, ldc, ldr, err, st, streamk);
+  else if (!a_mn && b_mn) launch<BN, false, true, EPI>(ta, tb, c, r, M, N, K, ldc, ldr, err, st, streamk);
+  else if (a_mn && b_mn) launch<BN, true, true, EPI>(ta, tb, c, r, M, N, K, ldc, ldr, err, st, streamk);
+  else launch<BN, true, false, EPI>(ta, tb, c, r, M, N, K, ldc, ldr, err, st, streamk);
 }
 
 // SwiGLU launch (K-major A, K-major gate_up weight).
@@ -1232,7 +1283,7 @@ static void launch_swiglu(const CUtensorMap& ta, const CUtensorMap& tb, __nv_bfl
   }
   const int tiles = ((M + BM - 1) / BM) * (F / 128);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  kern<<<grid, kThreads, smem, st>>>(ta, tb, a_out, nullptr, M, F, K, lda_out, 0, err, gu_out, ldgu);
+  kern<<<grid, kThreads, smem, st>>>(ta, tb, a_out, nullptr, M, F, K, lda_out, 0, err, gu_out, ldgu, 0);
   LIBRA_LAUNCH_CHECK();
 }
 
@@ -1399,7 +1450,7 @@ void gemm_allgather(torch::Tensor a, torch::Tensor b, bool b_mn, torch::Tensor y
 //   c: [M, N] bf16 (epi 0/3) or fp32 (epi 1/2)
 //   residual: [M, N] bf16 for epi 3 (may be c itself)
 void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, bool b_mn, int64_t epi,
-               c10::optional<torch::Tensor> residual, torch::Tensor err) {
+               c10::optional<torch::Tensor> residual, torch::Tensor err, bool streamk) {
   using namespace gemm;
   LIBRA_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm_bf16: CUDA tensors required");
   LIBRA_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm_bf16: bf16 operands");
@@ -1449,7 +1500,8 @@ void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, boo
   const c10::cuda::CUDAGuard guard(a.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (trace) fprintf(stderr, "[gemm] stream=%p\n", (void*)st);
-  const bool paired = use_pair(M, N);
+  LIBRA_CHECK(!streamk || epi == kAccumF32, "gemm_bf16: stream-K needs the accumulate epilogue");
+  const bool paired = !streamk && use_pair(M, N);
   const int BN = (N <= 128) ? 128 : 256;
   CUtensorMap ta = a_mn ? make_map(a.data_ptr(), M, K, a.stride(0), 64, 64) : make_map(a.data_ptr(), K, M, a.stride(0), 64, BM);
   // a CTA of a pair loads 128 of the tile's 256 B rows
@@ -1461,8 +1513,8 @@ void gemm_bf16(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, boo
   const int ldc = (int)c.stride(0);
 #define LIBRA_GEMM_EPI(E)                                                                                   \
   if (paired) dispatch_pair<E>(a_mn, b_mn, ta, tb, cp, rptr, M, N, K, ldc, (int)ldr, errp, st);          \
-  else if (BN == 128) dispatch_major<128, E>(a_mn, b_mn, ta, tb, cp, rptr, M, N, K, ldc, (int)ldr, errp, st); \
-  else dispatch_major<256, E>(a_mn, b_mn, ta, tb, cp, rptr, M, N, K, ldc, (int)ldr, errp, st);
+  else if (BN == 128) dispatch_major<128, E>(a_mn, b_mn, ta, tb, cp, rptr, M, N, K, ldc, (int)ldr, errp, st, streamk); \
+  else dispatch_major<256, E>(a_mn, b_mn, ta, tb, cp, rptr, M, N, K, ldc, (int)ldr, errp, st, streamk);
   switch (epi) {
     case kStoreBf16: LIBRA_GEMM_EPI(kStoreBf16); break;
     case kStoreF32: LIBRA_GEMM_EPI(kStoreF32); break;

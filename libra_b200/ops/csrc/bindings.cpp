@@ -49,7 +49,7 @@ void paged_decode_v2(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
                      torch::Tensor seq_lens, torch::Tensor out, torch::Tensor part_out, torch::Tensor part_ml,
                      int64_t split_len, double scale);
 void sample_tokens(torch::Tensor logits, torch::Tensor temperature, torch::Tensor seeds, torch::Tensor positions,
-                   torch::Tensor out_tok, torch::Tensor out_lp, c10::optional<torch::Tensor> next_tok);
+                   torch::Tensor out_tok, torch::Tensor out_lp, c10::optional<torch::Tensor> next_tok, bool pdl);
 }  // namespace rollout
 namespace reshard {
 void weight_reshard(torch::Tensor items, int64_t grid);
@@ -85,24 +85,34 @@ void ep_pull(std::vector<int64_t> tx, std::vector<int64_t> flags, int64_t me, in
 }  // namespace ep
 void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                       torch::Tensor seq_lens, torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml,
-                      torch::Tensor counters, torch::Tensor err, double scale);
+                      torch::Tensor counters, torch::Tensor err, double scale, bool pdl);
 void decode_qkv_post(torch::Tensor acc, torch::Tensor qw, torch::Tensor kw, torch::Tensor pos, torch::Tensor cos_t,
                      torch::Tensor sin_t, torch::Tensor slot, torch::Tensor q_out, torch::Tensor k_cache,
-                     torch::Tensor v_cache, double eps);
-void decode_residual_norm(torch::Tensor x, torch::Tensor acc, torch::Tensor w, torch::Tensor h_out, double eps);
-void decode_swiglu(torch::Tensor acc, torch::Tensor a);
+                     torch::Tensor v_cache, double eps, bool pdl);
+void decode_residual_norm(torch::Tensor x, torch::Tensor acc, torch::Tensor w, torch::Tensor h_out, double eps,
+                          bool pdl);
+void decode_swiglu(torch::Tensor acc, torch::Tensor a, bool pdl);
+void gemm_decode(torch::Tensor x, torch::Tensor w, torch::Tensor acc, torch::Tensor err, bool pdl);
 }  // namespace libra
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_attention", &libra::decode_attention,
         "paged decode attention, stream-K over KV blocks with an in-kernel merge (no allocation)", py::arg("q"),
         py::arg("k_cache"), py::arg("v_cache"), py::arg("block_tables"), py::arg("seq_lens"), py::arg("out"),
-        py::arg("part_o"), py::arg("part_ml"), py::arg("counters"), py::arg("err"), py::arg("scale"));
+        py::arg("part_o"), py::arg("part_ml"), py::arg("counters"), py::arg("err"), py::arg("scale"),
+        py::arg("pdl") = false);
   m.def("decode_qkv_post", &libra::decode_qkv_post,
-        "fused decode: qkv accumulator -> q/k RMSNorm + RoPE -> q and the paged KV cache (zeroes the accumulator)");
+        "fused decode: qkv accumulator -> q/k RMSNorm + RoPE -> q and the paged KV cache (zeroes the accumulator)",
+        py::arg("acc"), py::arg("qw"), py::arg("kw"), py::arg("pos"), py::arg("cos"), py::arg("sin"), py::arg("slot"),
+        py::arg("q_out"), py::arg("k_cache"), py::arg("v_cache"), py::arg("eps"), py::arg("pdl") = false);
   m.def("decode_residual_norm", &libra::decode_residual_norm,
-        "fused decode: x += acc (bf16), h = RMSNorm(x) * w (zeroes the accumulator)");
-  m.def("decode_swiglu", &libra::decode_swiglu, "fused decode: SwiGLU of the gate/up accumulator (zeroes it)");
+        "fused decode: x += acc (bf16), h = RMSNorm(x) * w (zeroes the accumulator)", py::arg("x"), py::arg("acc"),
+        py::arg("w"), py::arg("h_out"), py::arg("eps"), py::arg("pdl") = false);
+  m.def("decode_swiglu", &libra::decode_swiglu, "fused decode: SwiGLU of the gate/up accumulator (zeroes it)",
+        py::arg("acc"), py::arg("a"), py::arg("pdl") = false);
+  m.def("gemm_decode", &libra::gemm_decode,
+        "decode-step skinny GEMM acc += x w^T on tcgen05 (weights as the 128-row MMA operand, stream-K over all SMs)",
+        py::arg("x"), py::arg("w"), py::arg("acc"), py::arg("err"), py::arg("pdl") = false);
   m.doc() = "libra_b200 sm_100a kernels";
   m.def("gemm_bf16", &libra::gemm_bf16, "tcgen05 bf16 GEMM", py::arg("a"), py::arg("b"), py::arg("c"),
         py::arg("a_mn"), py::arg("b_mn"), py::arg("epi"), py::arg("residual"), py::arg("err"),
@@ -132,7 +142,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "paged decode attention with caller-owned split workspace (graph-capturable)");
   m.def("sample_tokens", &libra::rollout::sample_tokens,
         "Gumbel-max temperature sampling with the sampled token's logprob", py::arg("logits"), py::arg("temperature"),
-        py::arg("seeds"), py::arg("positions"), py::arg("out_tok"), py::arg("out_lp"), py::arg("next_tok") = py::none());
+        py::arg("seeds"), py::arg("positions"), py::arg("out_tok"), py::arg("out_lp"), py::arg("next_tok") = py::none(),
+        py::arg("pdl") = false);
   m.def("flash_fwd", &libra::attn::flash_fwd, "tcgen05 varlen GQA attention forward", py::arg("q"), py::arg("k"),
         py::arg("v"), py::arg("cu_seqlens"), py::arg("tiles"), py::arg("scale"), py::arg("causal"), py::arg("err"),
         py::arg("cu_k") = py::none());

@@ -435,6 +435,14 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int m, int n, int a_mn_ma
          | ((uint32_t)(m >> 4) << 24);  // M / 16
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialisation may start while its
+// stream predecessor is still running; pdl_wait() blocks until that grid has
+// completed and its memory is visible.  Without the launch attribute both are
+// no-ops.  pdl_launch_dependents() lets the next such kernel start launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- misc
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

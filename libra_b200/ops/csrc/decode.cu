@@ -27,6 +27,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "tmap.cuh"
 
 namespace libra {
 namespace decode {
@@ -74,6 +75,8 @@ __global__ void __launch_bounds__(256)
                     const float* __restrict__ sin_t, const int64_t* __restrict__ slot, __nv_bfloat16* __restrict__ q_out,
                     __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache, int B, int nq, int nkv,
                     float eps) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int heads = nq + nkv;
   const int lane = threadIdx.x & 31, grp = lane >> 3, j = lane & 7;
   const unsigned gmask = 0xFFu << (grp * 8);
@@ -142,6 +145,8 @@ constexpr int kRnVec = 4;
 __global__ void __launch_bounds__(kRnThreads)
     residual_norm_kernel(__nv_bfloat16* __restrict__ x, float* __restrict__ acc, const __nv_bfloat16* __restrict__ w,
                          __nv_bfloat16* __restrict__ h_out, int H, float eps) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int row = blockIdx.x;
   const int nvec = H >> 3;
   __nv_bfloat16* xr = x + (size_t)row * H;
@@ -189,6 +194,8 @@ __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.f + __
 
 __global__ void __launch_bounds__(256)
     swiglu_kernel(float* __restrict__ acc, __nv_bfloat16* __restrict__ a, int B, int F) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int per_row = F >> 3;
   const int total = B * per_row;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
@@ -203,8 +210,7 @@ __global__ void __launch_bounds__(256)
 }
 
 // ------------------------------------------------------------------ paged decode attention
-// Cache (per layer): k/v [num_blocks, 16, Hkv, 128] bf16, so one cache block
-// of one layer is a contiguous 16 * Hkv * 256-byte run for K and one for V.
+// Cache (per layer): k/v [num_blocks, 16, Hkv, 128] bf16.
 //
 // Work split (stream-K): the cache blocks of all B sequences, concatenated in
 // batch order, are TB = sum_b ceil(len_b / 16) units; CTA c of the grid G
@@ -212,69 +218,90 @@ __global__ void __launch_bounds__(256)
 // same number of bytes however uneven the lengths are, and the grid does not
 // depend on them, so one captured launch serves every step.  A CTA walks its
 // units sequence by sequence ("segments"):
-//  * one thread streams whole K and V blocks into an S-stage shared-memory
-//    ring with cp.async.bulk (mbarrier completion);
-//  * two warps per KV head, each scoring 8 tokens of every block for the G
-//    query heads of that KV head: lane l owns dims [4l, 4l+4), scores are
-//    reduced across the warp with a reduce-scatter butterfly (each level
-//    halves the values a lane holds), online softmax in the log2 domain;
-//  * at the end of a segment the two warps of a head merge their states; a
-//    sequence that lies inside one CTA is written out directly, otherwise the
-//    CTA writes its partial (m, l, o) to workspace slot c + b (unique: the CTA
-//    ranges are ordered like the sequences) and bumps the sequence's counter;
-//    the CTA that brings the counter to the sequence's segment count merges
-//    all partials, writes the output and resets the counter for the next
-//    launch.
+//  * one thread streams the K and V tiles of every block into an S-stage
+//    shared-memory ring with TMA: per KV head and 64-dim half one 16-row x
+//    128-byte box with the 128-byte swizzle, so the ldmatrix reads below are
+//    free of bank conflicts;
+//  * one warp per KV head runs the block on the tensor cores (mma.sync
+//    m16n8k16, bf16 in, fp32 out): S = Q K^T with the head's G query rows
+//    (padded to 16) as A and K as B, online softmax on the accumulator
+//    fragments in the log2 domain, then O += P V with P taken straight from
+//    the S fragments (the C layout of one m16n8 pair is the A layout of the
+//    next m16n8k16).  Decode is bound by the KV read; the tensor cores keep
+//    the arithmetic to a few instructions per 16 tokens, so the warps keep up
+//    with HBM;
+//  * at the end of a segment a sequence that lies inside one CTA is written
+//    out directly; otherwise the CTA writes its partial (m, l, o) to
+//    workspace slot c + b (unique: the CTA ranges are ordered like the
+//    sequences) and bumps the sequence's counter; the CTA that brings the
+//    counter to the sequence's segment count merges all partials, writes the
+//    output and resets the counter for the next launch.
 // Every wait is bounded; on a timeout the kernel records kTimeoutAttnKV,
 // waits for its own copies in flight and returns.
 constexpr int kBS = 16;
 constexpr int kMaxB = 1024;
-constexpr int kComb = 132;  // per (KV head, query head) merge record: m, l, 2 pad, o[128]; 16-byte multiple
-
-template <int N, int O>
-__device__ __forceinline__ void rs_level(float* v, int lane) {
-  if constexpr (O >= 1) {
-    if constexpr (N > 1) {
-      const bool up = (lane & O) != 0;
-#pragma unroll
-      for (int i = 0; i < N / 2; ++i) {
-        const float send = up ? v[i] : v[i + N / 2];
-        const float keep = up ? v[i + N / 2] : v[i];
-        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, O);
-      }
-      rs_level<N / 2, O / 2>(v, lane);
-    } else {
-      v[0] += __shfl_xor_sync(0xffffffffu, v[0], O);
-      rs_level<1, O / 2>(v, lane);
-    }
-  }
-}
+constexpr int kHalfTile = kBS * 128;  // bytes of one 16-row x 64-dim swizzled box
 
 __device__ __forceinline__ int owner_cta(int x, int TB, int G) {
   return (int)(((long long)(x + 1) * G - 1) / TB);
 }
 
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// D = A(16x16, row) . B(16x8, col) + D, bf16 inputs, fp32 accumulators
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Address of 16-byte chunk `c16` (0..15) of row `r` (0..15) of a head's K or V
+// tile: two 64-dim boxes, each 16 rows x 128 B with the 128-byte swizzle.
+__device__ __forceinline__ uint32_t tile_addr(uint32_t base, int r, int c16) {
+  return base + (uint32_t)((c16 >> 3) * kHalfTile + r * 128 + (((c16 & 7) ^ (r & 7)) << 4));
+}
+
 template <int G>
-__global__ void __launch_bounds__(512, 1)
-    decode_attn_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ kc,
-                       const __nv_bfloat16* __restrict__ vc, const int* __restrict__ tables, int max_blocks,
+__global__ void __launch_bounds__(256, 1)
+    decode_attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                       const __nv_bfloat16* __restrict__ q, const int* __restrict__ tables, int max_blocks,
                        const int* __restrict__ lens, int B, int Hkv, int S, __nv_bfloat16* __restrict__ out,
                        float* __restrict__ part_o, float* __restrict__ part_ml, int* __restrict__ counters,
                        float scale_log2, int* err) {
-  constexpr int GP = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8;
-  constexpr int NV = 8 * GP;                  // scores per lane before the reduction
-  constexpr int V = NV >= 32 ? NV / 32 : 1;  // after it
-  extern __shared__ __align__(128) uint8_t sm[];
+  static_assert(G >= 1 && G <= 8, "1 to 8 query heads per KV head");
+  extern __shared__ __align__(1024) uint8_t sm_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nthreads = blockDim.x;
   const int Hq = Hkv * G;
-  const int row_el = Hkv * kD;                  // elements per token row of the cache
-  const uint32_t blk_bytes = kBS * row_el * 2;  // one K (or V) block
-  const uint32_t stage_bytes = 2 * blk_bytes;
+  const uint32_t head_bytes = 2 * kHalfTile;             // one head's K (or V) tile of a block
+  const uint32_t stage_bytes = 2 * Hkv * head_bytes;     // K tiles of every head, then V tiles
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + (size_t)S * stage_bytes);
-  int* pre = reinterpret_cast<int*>(full + 8);                      // [B + 1]
-  float* p_all = reinterpret_cast<float*>(pre + ((B + 1 + 3) & ~3));  // [warps][9][GP]
+  int* pre = reinterpret_cast<int*>(full + 8);  // [B + 1]
   __shared__ int s_last;
+  pdl_wait();
+  pdl_launch_dependents();
 
   if (warp == 0) {  // prefix sums of the per-sequence block counts
     int carry = 0;
@@ -293,6 +320,8 @@ __global__ void __launch_bounds__(512, 1)
     if (lane == 0) pre[0] = 0;
   }
   if (tid == 0) {
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
     for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
     fence_barrier_init();
   }
@@ -308,7 +337,6 @@ __global__ void __launch_bounds__(512, 1)
   const int NC = min((int)gridDim.x, TB);
   if (c >= NC) return;
   const int lo = (int)((long long)TB * c / NC), hi = (int)((long long)TB * (c + 1) / NC);
-  // first sequence of this range: the largest b with pre[b] <= lo
   int b0 = 0;
   {
     int l = 0, r = B - 1;
@@ -323,19 +351,24 @@ __global__ void __launch_bounds__(512, 1)
   int ld_it = lo, ld_b = b0;
   auto issue = [&](int it) {
     while (pre[ld_b + 1] <= it) ++ld_b;
-    const int j = it - pre[ld_b];
-    const int blk = tables[(size_t)ld_b * max_blocks + j];
+    const int blk = tables[(size_t)ld_b * max_blocks + (it - pre[ld_b])];
     const int st = (it - lo) % S;
     uint8_t* dst = sm + (size_t)st * stage_bytes;
     mbar_expect_tx(&full[st], stage_bytes);
-    bulk_load(dst, kc + (size_t)blk * kBS * row_el, blk_bytes, &full[st]);
-    bulk_load(dst + blk_bytes, vc + (size_t)blk * kBS * row_el, blk_bytes, &full[st]);
+    for (int h = 0; h < Hkv; ++h) {
+#pragma unroll
+      for (int d = 0; d < 2; ++d) {
+        tma_load_3d(dst + h * head_bytes + d * kHalfTile, &tmK, &full[st], 64 * d, h, blk * kBS);
+        tma_load_3d(dst + (Hkv + h) * head_bytes + d * kHalfTile, &tmV, &full[st], 64 * d, h, blk * kBS);
+      }
+    }
   };
   if (tid == 0)
     for (; ld_it < hi && ld_it < lo + S; ++ld_it) issue(ld_it);
 
-  const int h = warp >> 1, half = warp & 1;
-  float* p_s = p_all + warp * 9 * GP;
+  const int h = warp;             // this warp's KV head
+  const int gid = lane >> 2, tig = lane & 3;
+  const bool row_real = gid < G;  // this thread's query row (head h*G + gid) is a real head
   bool aborted = false;
   int it = lo, cur_b = b0;
   while (it < hi) {
@@ -343,28 +376,22 @@ __global__ void __launch_bounds__(512, 1)
     const int seq_lo = pre[cur_b], seq_hi = pre[cur_b + 1];
     const int seg_end = min(hi, seq_hi);
     const int len = lens[cur_b];
-    // this warp's query heads, this lane's four dims, in log2 units
-    float qr[G][4];
+    // Q fragments (A operand): row gid = query head h*G + gid, rows >= G (and 8..15) are zero
+    uint32_t qa[8][2];
+    {
+      const __nv_bfloat16* qr = q + ((size_t)cur_b * Hq + h * G + (row_real ? gid : 0)) * kD;
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const uint2 u = *reinterpret_cast<const uint2*>(q + ((size_t)cur_b * Hq + h * G + g) * kD + 4 * lane);
-      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-      const float2 bq = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-      qr[g][0] = a.x * scale_log2;
-      qr[g][1] = a.y * scale_log2;
-      qr[g][2] = bq.x * scale_log2;
-      qr[g][3] = bq.y * scale_log2;
+      for (int ks = 0; ks < 8; ++ks) {
+        qa[ks][0] = row_real ? *reinterpret_cast<const uint32_t*>(qr + ks * 16 + 2 * tig) : 0u;
+        qa[ks][1] = row_real ? *reinterpret_cast<const uint32_t*>(qr + ks * 16 + 8 + 2 * tig) : 0u;
+      }
     }
-    float m_run[V], l_run[V], o[G][4];
+    float o[16][4];
 #pragma unroll
-    for (int j = 0; j < V; ++j) {
-      m_run[j] = -INFINITY;
-      l_run[j] = 0.f;
-    }
+    for (int dt = 0; dt < 16; ++dt)
 #pragma unroll
-    for (int g = 0; g < G; ++g)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) o[g][e] = 0.f;
+      for (int e = 0; e < 4; ++e) o[dt][e] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
     for (; it < seg_end; ++it) {
       const int st = (it - lo) % S;
       const uint32_t ph = ((it - lo) / S) & 1u;
@@ -375,147 +402,79 @@ __global__ void __launch_bounds__(512, 1)
       }
       // every warp is done with block it-1: its stage takes block it-1+S
       if (tid == 0 && it > lo && ld_it < hi) issue(ld_it++);
-      if (h < Hkv) {
-        const __nv_bfloat16* Ks = reinterpret_cast<const __nv_bfloat16*>(sm + (size_t)st * stage_bytes) +
-                                  (size_t)(half * 8) * row_el + h * kD + 4 * lane;
-        const __nv_bfloat16* Vs = Ks + kBS * row_el;
-        float sc[NV];
+      const uint32_t kbase = smem_u32(sm + (size_t)st * stage_bytes + h * head_bytes);
+      const uint32_t vbase = kbase + Hkv * head_bytes;
+      // ---- S = Q K^T: two n-tiles of 8 tokens, 8 k-steps of 16 dims
+      float s[2][4];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const uint2 u = *reinterpret_cast<const uint2*>(Ks + (size_t)t * row_el);
-          const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-          const float2 bb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+      for (int nt = 0; nt < 2; ++nt) {
 #pragma unroll
-          for (int g = 0; g < GP; ++g) {
-            if (g < G) {
-              float acc = qr[g][0] * a.x;
-              acc = fmaf(qr[g][1], a.y, acc);
-              acc = fmaf(qr[g][2], bb.x, acc);
-              acc = fmaf(qr[g][3], bb.y, acc);
-              sc[t * GP + g] = acc;
-            } else {
-              sc[t * GP + g] = 0.f;
-            }
-          }
+        for (int e = 0; e < 4; ++e) s[nt][e] = 0.f;
+#pragma unroll
+        for (int kp = 0; kp < 4; ++kp) {  // k-steps 2kp, 2kp+1
+          const int mi = lane >> 3;
+          uint32_t b00, b01, b10, b11;
+          ldsm_x4(tile_addr(kbase, nt * 8 + (lane & 7), 4 * kp + mi), b00, b01, b10, b11);
+          mma_bf16(s[nt], qa[2 * kp][0], 0u, qa[2 * kp][1], 0u, b00, b01);
+          mma_bf16(s[nt], qa[2 * kp + 1][0], 0u, qa[2 * kp + 1][1], 0u, b10, b11);
         }
-        rs_level<NV, 16>(sc, lane);
-        // lane holds token t = lane / 4 of this half; its values belong to heads gidx(j)
-        const int t = lane >> 2;
-        const int pos = (it - seq_lo) * kBS + half * 8 + t;
-        const bool valid = pos < len;
+      }
+      // ---- online softmax over this block's 16 tokens (row gid; rows 8..15 are padding)
+      const int tok0 = (it - seq_lo) * kBS;
+      float v[4];
 #pragma unroll
-        for (int j = 0; j < V; ++j) {
-          const int g = GP >= 4 ? (lane & 3) * (GP / 4) + j : (GP == 2 ? (lane >> 1) & 1 : 0);
-          const float s = valid ? sc[j] : -INFINITY;
-          float mx = s;
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-          const float m_new = fmaxf(m_run[j], mx);
-          const float alpha = m_new == -INFINITY ? 1.f : exp2f(m_run[j] - m_new);
-          const float p = s == -INFINITY ? 0.f : exp2f(s - m_new);
-          float ps = p;
-          ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-          ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-          ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-          l_run[j] = l_run[j] * alpha + ps;
-          m_run[j] = m_new;
-          p_s[t * GP + g] = p;
-          if (t == 0) p_s[8 * GP + g] = alpha;
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int pos = tok0 + nt * 8 + 2 * tig + e;
+          v[nt * 2 + e] = pos < len ? s[nt][e] * scale_log2 : -INFINITY;
         }
-        __syncwarp();
+      float mx = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(m_run, mx);
+      const float alpha = m_new == -INFINITY ? 1.f : exp2f(m_run - m_new);
+      float p[4];
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float a = p_s[8 * GP + g];
+      for (int e = 0; e < 4; ++e) p[e] = v[e] == -INFINITY ? 0.f : exp2f(v[e] - m_new);
+      l_run = l_run * alpha + (p[0] + p[1] + p[2] + p[3]);
+      m_run = m_new;
 #pragma unroll
-          for (int e = 0; e < 4; ++e) o[g][e] *= a;
-        }
+      for (int dt = 0; dt < 16; ++dt) {
+        o[dt][0] *= alpha;
+        o[dt][1] *= alpha;
+      }
+      const uint32_t pa0 = pack_bf16x2(p[0], p[1]);  // P[gid][2tig..], tokens 0-7
+      const uint32_t pa2 = pack_bf16x2(p[2], p[3]);  // tokens 8-15
+      // ---- O += P V: 16 n-tiles of 8 dims
 #pragma unroll
-        for (int tt = 0; tt < 8; ++tt) {
-          const uint2 u = *reinterpret_cast<const uint2*>(Vs + (size_t)tt * row_el);
-          const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-          const float2 bb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
-          float pr[GP];
-#pragma unroll
-          for (int g4 = 0; g4 < GP; g4 += (GP >= 4 ? 4 : GP)) {
-            if constexpr (GP >= 4) {
-              const float4 f = *reinterpret_cast<const float4*>(p_s + tt * GP + g4);
-              pr[g4] = f.x;
-              pr[g4 + 1] = f.y;
-              pr[g4 + 2] = f.z;
-              pr[g4 + 3] = f.w;
-            } else {
-#pragma unroll
-              for (int g = 0; g < GP; ++g) pr[g] = p_s[tt * GP + g];
-            }
-          }
-#pragma unroll
-          for (int g = 0; g < G; ++g) {
-            o[g][0] = fmaf(pr[g], a.x, o[g][0]);
-            o[g][1] = fmaf(pr[g], a.y, o[g][1]);
-            o[g][2] = fmaf(pr[g], bb.x, o[g][2]);
-            o[g][3] = fmaf(pr[g], bb.y, o[g][3]);
-          }
-        }
-        __syncwarp();
+      for (int dp = 0; dp < 8; ++dp) {  // dim tiles 2dp, 2dp+1
+        const int mi = lane >> 3;
+        uint32_t b00, b01, b10, b11;
+        ldsm_x4_t(tile_addr(vbase, (mi & 1) * 8 + (lane & 7), 2 * dp + (mi >> 1)), b00, b01, b10, b11);
+        mma_bf16(o[2 * dp], pa0, 0u, pa2, 0u, b00, b01);
+        mma_bf16(o[2 * dp + 1], pa0, 0u, pa2, 0u, b10, b11);
       }
     }
     if (aborted) break;
-    // ---- segment end: merge the two warps of every head through the stage of the last block
-    __syncthreads();
-    float* comb = reinterpret_cast<float*>(sm + (size_t)((it - 1 - lo) % S) * stage_bytes);  // [Hkv][G][kComb]
-    float mh[G], lh[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const int src = GP >= 4 ? g / (GP / 4) : (GP == 2 ? 2 * g : 0);
-      const int j = GP >= 4 ? g % (GP / 4) : 0;
-      float mv = 0.f, lv = 0.f;
-#pragma unroll
-      for (int jj = 0; jj < V; ++jj)
-        if (jj == j) {
-          mv = m_run[jj];
-          lv = l_run[jj];
-        }
-      mh[g] = __shfl_sync(0xffffffffu, mv, src);
-      lh[g] = __shfl_sync(0xffffffffu, lv, src);
-    }
-    if (h < Hkv && half == 1) {
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        float* cg = comb + ((size_t)h * G + g) * kComb;
-        *reinterpret_cast<float4*>(cg + 4 + 4 * lane) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
-        if (lane == 0) {
-          cg[0] = mh[g];
-          cg[1] = lh[g];
-        }
-      }
-    }
-    __syncthreads();
+    // ---- segment end
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
     const bool whole = seq_lo >= lo && seq_hi <= hi;
-    if (h < Hkv && half == 0) {
+    const int hq = h * G + gid;
+    if (row_real) {
+      if (whole) {
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        __nv_bfloat16* orow = out + ((size_t)cur_b * Hq + hq) * kD + 2 * tig;
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float* cg = comb + ((size_t)h * G + g) * kComb;
-        const float m1 = cg[0], l1 = cg[1];
-        const float4 o1 = *reinterpret_cast<const float4*>(cg + 4 + 4 * lane);
-        const float M = fmaxf(mh[g], m1);
-        const float a0 = mh[g] == -INFINITY ? 0.f : exp2f(mh[g] - M);
-        const float a1 = m1 == -INFINITY ? 0.f : exp2f(m1 - M);
-        const float L = lh[g] * a0 + l1 * a1;
-        float r[4] = {o[g][0] * a0 + o1.x * a1, o[g][1] * a0 + o1.y * a1, o[g][2] * a0 + o1.z * a1,
-                      o[g][3] * a0 + o1.w * a1};
-        const int hq = h * G + g;
-        if (whole) {
-          const float inv = L > 0.f ? 1.f / L : 0.f;
-          uint2 pk;
-          pk.x = pack_bf16x2(r[0] * inv, r[1] * inv);
-          pk.y = pack_bf16x2(r[2] * inv, r[3] * inv);
-          *reinterpret_cast<uint2*>(out + ((size_t)cur_b * Hq + hq) * kD + 4 * lane) = pk;
-        } else {
-          const size_t slot = (size_t)(c + cur_b) * Hq + hq;
-          __stcg(reinterpret_cast<float4*>(part_o + slot * kD + 4 * lane), make_float4(r[0], r[1], r[2], r[3]));
-          if (lane == 0) __stcg(reinterpret_cast<float2*>(part_ml + slot * 2), make_float2(M, L));
-        }
+        for (int dt = 0; dt < 16; ++dt)
+          *reinterpret_cast<uint32_t*>(orow + dt * 8) = pack_bf16x2(o[dt][0] * inv, o[dt][1] * inv);
+      } else {
+        const size_t slot = (size_t)(c + cur_b) * Hq + hq;
+        float* prow = part_o + slot * kD + 2 * tig;
+#pragma unroll
+        for (int dt = 0; dt < 16; ++dt) __stcg(reinterpret_cast<float2*>(prow + dt * 8), make_float2(o[dt][0], o[dt][1]));
+        if (tig == 0) __stcg(reinterpret_cast<float2*>(part_ml + slot * 2), make_float2(m_run, l_run));
       }
     }
     if (!whole) {
@@ -533,14 +492,14 @@ __global__ void __launch_bounds__(512, 1)
         __threadfence();
         const int c0 = owner_cta(seq_lo, TB, NC), c1 = owner_cta(seq_hi - 1, TB, NC);
         for (int i = tid; i < Hq * (kD / 4); i += nthreads) {
-          const int hq = i / (kD / 4), d4 = i - hq * (kD / 4);
+          const int hh = i / (kD / 4), d4 = i - hh * (kD / 4);
           float M = -INFINITY;
           for (int cc = c0; cc <= c1; ++cc)
-            M = fmaxf(M, __ldcg(part_ml + ((size_t)(cc + cur_b) * Hq + hq) * 2));
+            M = fmaxf(M, __ldcg(part_ml + ((size_t)(cc + cur_b) * Hq + hh) * 2));
           float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
           float den = 0.f;
           for (int cc = c0; cc <= c1; ++cc) {
-            const size_t slot = (size_t)(cc + cur_b) * Hq + hq;
+            const size_t slot = (size_t)(cc + cur_b) * Hq + hh;
             const float2 ml = __ldcg(reinterpret_cast<const float2*>(part_ml + slot * 2));
             if (ml.x == -INFINITY) continue;
             const float w = exp2f(ml.x - M);
@@ -555,11 +514,11 @@ __global__ void __launch_bounds__(512, 1)
           uint2 pk;
           pk.x = pack_bf16x2(num.x * inv, num.y * inv);
           pk.y = pack_bf16x2(num.z * inv, num.w * inv);
-          *reinterpret_cast<uint2*>(out + ((size_t)cur_b * Hq + hq) * kD + 4 * d4) = pk;
+          *reinterpret_cast<uint2*>(out + ((size_t)cur_b * Hq + hh) * kD + 4 * d4) = pk;
         }
       }
+      __syncthreads();
     }
-    __syncthreads();  // the merge area (a stage) and p_s are free again
   }
   if (aborted && tid == 0) {
     // copies issued for units [it, ld_it) may still be in flight
@@ -577,16 +536,24 @@ static int sm_count() {
   return n;
 }
 
+// 3-D map over one layer's cache [rows = blocks x 16, Hkv, 128]: box = 16 rows of one head, 64 dims
+static CUtensorMap cache_map(const torch::Tensor& c) {
+  const int64_t rows = c.size(0) * c.size(1), hkv = c.size(2);
+  cuuint64_t dims[3] = {(cuuint64_t)kD, (cuuint64_t)hkv, (cuuint64_t)rows};
+  cuuint64_t strides[2] = {(cuuint64_t)kD * 2, (cuuint64_t)(hkv * kD * 2)};
+  cuuint32_t box[3] = {64, 1, (cuuint32_t)kBS};
+  return tmap::make_bf16(c.data_ptr(), 3, dims, strides, box);
+}
+
 template <int G>
 static void launch_attn(const torch::Tensor& q, const torch::Tensor& kc, const torch::Tensor& vc,
                         const torch::Tensor& tables, const torch::Tensor& lens, int B, torch::Tensor& out,
                         torch::Tensor& part_o, torch::Tensor& part_ml, torch::Tensor& counters, int* err,
-                        float scale_log2, cudaStream_t st) {
-  constexpr int GP = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8;
+                        float scale_log2, cudaStream_t st, bool pdl) {
   const int Hkv = (int)kc.size(2);
-  const int threads = 64 * Hkv;
-  const size_t stage_bytes = (size_t)2 * kBS * Hkv * kD * 2;
-  const size_t extra = 64 + (size_t)((B + 1 + 3) & ~3) * 4 + (size_t)(threads / 32) * 9 * GP * 4;
+  const int threads = 32 * Hkv;
+  const size_t stage_bytes = (size_t)2 * Hkv * 2 * kHalfTile;
+  const size_t extra = 1024 /*alignment*/ + 64 + (size_t)(B + 1) * 4;
   // 227 KB per CTA, less a margin for the kernel's static shared memory
   constexpr size_t kMaxSmem = 226 * 1024;
   int S = (int)std::min<size_t>(8, (kMaxSmem - extra) / stage_bytes);
@@ -600,12 +567,11 @@ static void launch_attn(const torch::Tensor& q, const torch::Tensor& kc, const t
                 cudaGetErrorString(e));
     configured = smem;
   }
-  kern<<<sm_count(), threads, smem, st>>>(
-      (const __nv_bfloat16*)q.data_ptr(), (const __nv_bfloat16*)kc.data_ptr(), (const __nv_bfloat16*)vc.data_ptr(),
-      tables.data_ptr<int>(), (int)tables.size(1), lens.data_ptr<int>(), B, Hkv, S,
-      (__nv_bfloat16*)out.data_ptr(), part_o.data_ptr<float>(), part_ml.data_ptr<float>(), counters.data_ptr<int>(),
-      scale_log2, err);
-  LIBRA_LAUNCH_CHECK();
+  const CUtensorMap tk = cache_map(kc), tv = cache_map(vc);
+  launch_kernel(kern, dim3(sm_count()), dim3(threads), smem, st, pdl, tk, tv, (const __nv_bfloat16*)q.data_ptr(),
+                tables.data_ptr<int>(), (int)tables.size(1), lens.data_ptr<int>(), B, Hkv, S,
+                (__nv_bfloat16*)out.data_ptr(), part_o.data_ptr<float>(), part_ml.data_ptr<float>(),
+                counters.data_ptr<int>(), scale_log2, err);
 }
 
 }  // namespace decode
@@ -614,10 +580,11 @@ static void launch_attn(const torch::Tensor& q, const torch::Tensor& kc, const t
 // [>=B] int32 (tokens including the new one, whose KV is already in the cache); out [B, Hq, 128] bf16.
 // Workspace (caller-owned, nothing is allocated, so the call can be captured in a CUDA graph):
 // part_o [>= SMs + B, Hq, 128] fp32, part_ml [>= SMs + B, Hq, 2] fp32, counters [>= B] int32, zero
-// before the first call (the kernel leaves them zero).
+// before the first call (the kernel leaves them zero).  pdl: programmatic dependent launch (every
+// kernel of the fused decode step waits for its predecessor with griddepcontrol.wait).
 void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                       torch::Tensor seq_lens, torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml,
-                      torch::Tensor counters, torch::Tensor err, double scale) {
+                      torch::Tensor counters, torch::Tensor err, double scale, bool pdl) {
   using namespace decode;
   LIBRA_CHECK(q.is_cuda() && q.scalar_type() == at::kBFloat16 && q.dim() == 3 && q.is_contiguous() &&
                   q.size(2) == kD,
@@ -650,11 +617,11 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
   const float sl2 = (float)(scale * 1.4426950408889634);  // log2(e)
   int* errp = err.data_ptr<int>();
   switch (Hq / Hkv) {
-    case 1: launch_attn<1>(q, k_cache, v_cache, block_tables, seq_lens, B, out, part_o, part_ml, counters, errp, sl2, st); break;
-    case 2: launch_attn<2>(q, k_cache, v_cache, block_tables, seq_lens, B, out, part_o, part_ml, counters, errp, sl2, st); break;
-    case 4: launch_attn<4>(q, k_cache, v_cache, block_tables, seq_lens, B, out, part_o, part_ml, counters, errp, sl2, st); break;
-    case 5: launch_attn<5>(q, k_cache, v_cache, block_tables, seq_lens, B, out, part_o, part_ml, counters, errp, sl2, st); break;
-    case 8: launch_attn<8>(q, k_cache, v_cache, block_tables, seq_lens, B, out, part_o, part_ml, counters, errp, sl2, st); break;
+    case 1: launch_attn<1>(q, k_cache, v_cache, block_tables, seq_lens, B, out, part_o, part_ml, counters, errp, sl2, st, pdl); break;
+    case 2: launch_attn<2>(q, k_cache, v_cache, block_tables, seq_lens, B, out, part_o, part_ml, counters, errp, sl2, st, pdl); break;
+    case 4: launch_attn<4>(q, k_cache, v_cache, block_tables, seq_lens, B, out, part_o, part_ml, counters, errp, sl2, st, pdl); break;
+    case 5: launch_attn<5>(q, k_cache, v_cache, block_tables, seq_lens, B, out, part_o, part_ml, counters, errp, sl2, st, pdl); break;
+    case 8: launch_attn<8>(q, k_cache, v_cache, block_tables, seq_lens, B, out, part_o, part_ml, counters, errp, sl2, st, pdl); break;
     default: LIBRA_CHECK(false, "decode_attention: unsupported GQA group size %d", Hq / Hkv);
   }
 }
@@ -664,7 +631,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_ca
 // caches [blocks, block_size, nkv, 128] bf16 receive the new token's normed+rotated K and its V.
 void decode_qkv_post(torch::Tensor acc, torch::Tensor qw, torch::Tensor kw, torch::Tensor pos, torch::Tensor cos_t,
                      torch::Tensor sin_t, torch::Tensor slot, torch::Tensor q_out, torch::Tensor k_cache,
-                     torch::Tensor v_cache, double eps) {
+                     torch::Tensor v_cache, double eps, bool pdl) {
   using namespace decode;
   const int B = (int)q_out.size(0), nq = (int)q_out.size(1), nkv = (int)k_cache.size(2);
   LIBRA_CHECK(q_out.is_contiguous() && q_out.scalar_type() == at::kBFloat16 && q_out.dim() == 3 && q_out.size(2) == kD,
@@ -684,18 +651,17 @@ void decode_qkv_post(torch::Tensor acc, torch::Tensor qw, torch::Tensor kw, torc
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int items = B * (nq + nkv);
   const int grid = (items + 31) / 32;
-  qkv_post_kernel<<<grid, 256, 0, st>>>(acc.data_ptr<float>(), (int)acc.stride(0),
-                                        (const __nv_bfloat16*)qw.data_ptr(), (const __nv_bfloat16*)kw.data_ptr(),
-                                        pos.data_ptr<int>(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
-                                        slot.data_ptr<int64_t>(), (__nv_bfloat16*)q_out.data_ptr(),
-                                        (__nv_bfloat16*)k_cache.data_ptr(), (__nv_bfloat16*)v_cache.data_ptr(), B, nq,
-                                        nkv, (float)eps);
-  LIBRA_LAUNCH_CHECK();
+  launch_kernel(qkv_post_kernel, dim3(grid), dim3(256), 0, st, pdl, acc.data_ptr<float>(), (int)acc.stride(0),
+                (const __nv_bfloat16*)qw.data_ptr(), (const __nv_bfloat16*)kw.data_ptr(), pos.data_ptr<int>(),
+                cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), slot.data_ptr<int64_t>(),
+                (__nv_bfloat16*)q_out.data_ptr(), (__nv_bfloat16*)k_cache.data_ptr(),
+                (__nv_bfloat16*)v_cache.data_ptr(), B, nq, nkv, (float)eps);
 }
 
 // x [B, H] bf16 (updated in place: x = bf16(x + acc)); acc [>=B, H] fp32 read and zeroed; w [H] bf16;
 // h_out [B, H] bf16 = RMSNorm(x) * w.  H % 8 == 0, H <= 8192.
-void decode_residual_norm(torch::Tensor x, torch::Tensor acc, torch::Tensor w, torch::Tensor h_out, double eps) {
+void decode_residual_norm(torch::Tensor x, torch::Tensor acc, torch::Tensor w, torch::Tensor h_out, double eps,
+                          bool pdl) {
   using namespace decode;
   const int B = (int)x.size(0), H = (int)x.size(1);
   LIBRA_CHECK(x.is_contiguous() && x.scalar_type() == at::kBFloat16 && h_out.is_contiguous() &&
@@ -708,14 +674,13 @@ void decode_residual_norm(torch::Tensor x, torch::Tensor acc, torch::Tensor w, t
   if (B == 0) return;
   const c10::cuda::CUDAGuard guard(x.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  residual_norm_kernel<<<B, kRnThreads, 0, st>>>((__nv_bfloat16*)x.data_ptr(), acc.data_ptr<float>(),
-                                                 (const __nv_bfloat16*)w.data_ptr(),
-                                                 (__nv_bfloat16*)h_out.data_ptr(), H, (float)eps);
-  LIBRA_LAUNCH_CHECK();
+  launch_kernel(residual_norm_kernel, dim3(B), dim3(kRnThreads), 0, st, pdl, (__nv_bfloat16*)x.data_ptr(),
+                acc.data_ptr<float>(), (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)h_out.data_ptr(), H,
+                (float)eps);
 }
 
 // acc [>=B, 2F] fp32 (gate columns then up columns), read and zeroed; a [B, F] bf16.
-void decode_swiglu(torch::Tensor acc, torch::Tensor a) {
+void decode_swiglu(torch::Tensor acc, torch::Tensor a, bool pdl) {
   using namespace decode;
   const int B = (int)a.size(0), F = (int)a.size(1);
   LIBRA_CHECK(a.is_contiguous() && a.scalar_type() == at::kBFloat16 && F % 8 == 0,
@@ -727,8 +692,8 @@ void decode_swiglu(torch::Tensor acc, torch::Tensor a) {
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int total = B * (F / 8);
   const int grid = std::min((total + 255) / 256, sm_count() * 8);
-  swiglu_kernel<<<grid, 256, 0, st>>>(acc.data_ptr<float>(), (__nv_bfloat16*)a.data_ptr(), B, F);
-  LIBRA_LAUNCH_CHECK();
+  launch_kernel(swiglu_kernel, dim3(grid), dim3(256), 0, st, pdl, acc.data_ptr<float>(), (__nv_bfloat16*)a.data_ptr(),
+                B, F);
 }
 
 }  // namespace libra

@@ -26,6 +26,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "tmap.cuh"
 
 namespace libra {
 namespace rollout {
@@ -344,6 +345,8 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
     T* __restrict__ logits, int64_t ld, int V, const float* __restrict__ temperature,
     const int64_t* __restrict__ seeds, const int64_t* __restrict__ positions, int64_t* __restrict__ out_tok,
     float* __restrict__ out_lp, int64_t* __restrict__ next_tok) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int row = blockIdx.x;
   T* x = logits + (size_t)row * ld;
   const float Tm = temperature[row];
@@ -428,7 +431,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
 // next decode step's input buffer).
 // fp32 logits (the fused decode step's accumulator) are zeroed behind the read, 16-byte aligned rows.
 void sample_tokens(torch::Tensor logits, torch::Tensor temperature, torch::Tensor seeds, torch::Tensor positions,
-                   torch::Tensor out_tok, torch::Tensor out_lp, c10::optional<torch::Tensor> next_tok) {
+                   torch::Tensor out_tok, torch::Tensor out_lp, c10::optional<torch::Tensor> next_tok, bool pdl) {
   const bool f32 = logits.scalar_type() == at::kFloat;
   LIBRA_CHECK(logits.is_cuda() && (f32 || logits.scalar_type() == at::kBFloat16) && logits.dim() == 2 &&
                   logits.stride(1) == 1 && logits.stride(0) % 4 == 0 &&
@@ -451,15 +454,16 @@ void sample_tokens(torch::Tensor logits, torch::Tensor temperature, torch::Tenso
   const c10::cuda::CUDAGuard guard(logits.device());
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (f32)
-    sample_kernel<float, true><<<B, kSampleThreads, 0, st>>>(logits.data_ptr<float>(), logits.stride(0), V,
-                                                             temperature.data_ptr<float>(), seeds.data_ptr<int64_t>(),
-                                                             positions.data_ptr<int64_t>(),
-                                                             out_tok.data_ptr<int64_t>(), out_lp.data_ptr<float>(), nt);
+    launch_kernel(sample_kernel<float, true>, dim3(B), dim3(kSampleThreads), 0, st, pdl, logits.data_ptr<float>(),
+                  (int64_t)logits.stride(0), V, (const float*)temperature.data_ptr<float>(),
+                  (const int64_t*)seeds.data_ptr<int64_t>(), (const int64_t*)positions.data_ptr<int64_t>(),
+                  out_tok.data_ptr<int64_t>(), out_lp.data_ptr<float>(), nt);
   else
-    sample_kernel<__nv_bfloat16, false><<<B, kSampleThreads, 0, st>>>(
-        (__nv_bfloat16*)logits.data_ptr(), logits.stride(0), V, temperature.data_ptr<float>(),
-        seeds.data_ptr<int64_t>(), positions.data_ptr<int64_t>(), out_tok.data_ptr<int64_t>(),
-        out_lp.data_ptr<float>(), nt);
+    launch_kernel(sample_kernel<__nv_bfloat16, false>, dim3(B), dim3(kSampleThreads), 0, st, pdl,
+                  (__nv_bfloat16*)logits.data_ptr(), (int64_t)logits.stride(0), V,
+                  (const float*)temperature.data_ptr<float>(), (const int64_t*)seeds.data_ptr<int64_t>(),
+                  (const int64_t*)positions.data_ptr<int64_t>(), out_tok.data_ptr<int64_t>(),
+                  out_lp.data_ptr<float>(), nt);
   LIBRA_LAUNCH_CHECK();
 }
 

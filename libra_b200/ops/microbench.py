@@ -1,6 +1,7 @@
 """Kernel microbenchmarks: achieved TFLOP/s or GB/s of each sm_100a kernel.
 
     python -m libra_b200.ops.microbench gemm [--shapes M,N,K;...] [--iters 20]
+    python -m libra_b200.ops.microbench decode [--batch 64] [--lens 510x64]
     python -m libra_b200.ops.microbench all
 
 Timing: CUDA events on the launching stream after warm-up, synchronize on both
@@ -156,9 +157,108 @@ def bench_attention(iters: int, lens=None):
         ops.check_kernel_errors()
 
 
+# Qwen3-4B decode-step GEMMs: (name, N out, K in); M is the decode batch
+QWEN3_4B_DECODE = [("qkv", 6144, 2560), ("o", 2560, 4096), ("gate_up", 19456, 2560), ("down", 2560, 9728),
+                   ("lm_head", 151936, 2560)]
+
+
+def _time_graph(fn, calls: int, replays: int = 5) -> float:
+    """Device time per call of ``fn`` captured ``calls`` times in one CUDA graph
+    (no host launch cost between the calls)."""
+    fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(calls):
+                fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(replays):
+        g.replay()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / (replays * calls)
+
+
+def bench_decode(iters: int, batch: int = 64, lens=None):
+    """Decode-step kernels, each call captured in a CUDA graph so the device
+    time is measured without host launch gaps: the decode GEMM (weight GB/s;
+    several weight copies rotate so every call reads HBM, not L2; with and
+    without programmatic dependent launch) against torch.matmul on the same
+    skinny shape, and the stream-K paged attention (KV GB/s)."""
+    M = batch
+    for name, N, K in QWEN3_4B_DECODE:
+        copies = max(2, -(-400 * 2 ** 20 // (N * K * 2)))  # >= 400 MB of weights in rotation
+        ws = [torch.randn(N, K, device="cuda").to(torch.bfloat16) for _ in range(copies)]
+        a = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+        acc = torch.zeros(M, N, device="cuda")
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        i = [0]
+
+        def ours(pdl):
+            def f():
+                ops.gemm_decode(a, ws[i[0] % copies], acc, pdl=pdl)
+                i[0] += 1
+            return f
+
+        def ref():
+            torch.matmul(a, ws[i[0] % copies].t(), out=out)
+            i[0] += 1
+
+        calls = max(copies, iters)
+        ms = _time_graph(ours(False), calls)
+        ms_pdl = _time_graph(ours(True), calls)
+        ms_ref = _time_graph(ref, calls)
+        gb = N * K * 2 / 1e9
+        ops.check_kernel_errors()
+        print(json.dumps({"kernel": "gemm_decode", "case": name, "M": M, "N": N, "K": K, "ms": ms,
+                          "weight_gbs": gb / (ms / 1e3), "ms_pdl": ms_pdl, "weight_gbs_pdl": gb / (ms_pdl / 1e3),
+                          "torch_ms": ms_ref, "torch_gbs": gb / (ms_ref / 1e3)}), flush=True)
+    # attention: Qwen3-4B heads, one layer's cache, several layers' caches in rotation
+    lens = lens or [510] * batch
+    Hkv, G, D, bs = 8, 4, 128, 16
+    Hq = Hkv * G
+    B = len(lens)
+    nblk = sum(-(-L // bs) for L in lens)
+    kv_bytes = 2 * sum(lens) * Hkv * D * 2
+    copies = max(2, -(-400 * 2 ** 20 // kv_bytes))
+    caches = [(torch.randn(nblk, bs, Hkv, D, device="cuda").to(torch.bfloat16),
+               torch.randn(nblk, bs, Hkv, D, device="cuda").to(torch.bfloat16)) for _ in range(copies)]
+    width = max(-(-L // bs) for L in lens)
+    bt = torch.zeros(B, width, dtype=torch.int32)
+    cur = 0
+    for r, L in enumerate(lens):
+        n = -(-L // bs)
+        bt[r, :n] = torch.arange(cur, cur + n)
+        cur += n
+    bt = bt.cuda()
+    lens_t = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    q = torch.randn(B, Hq, D, device="cuda").to(torch.bfloat16)
+    out = torch.empty(B, Hq, D, device="cuda", dtype=torch.bfloat16)
+    ws_o, ws_ml, counters = ops.decode_workspace(B, Hq, D, q.device)
+    j = [0]
+
+    def attn():
+        kc, vc = caches[j[0] % copies]
+        ops.decode_attention(q, kc, vc, bt, lens_t, out, ws_o, ws_ml, counters, 1.0 / D ** 0.5)
+        j[0] += 1
+
+    ms = _time_graph(attn, max(copies, iters))
+    ops.check_kernel_errors()
+    print(json.dumps({"kernel": "decode_attention", "batch": B, "mean_len": sum(lens) / B, "ms": ms,
+                      "kv_gbs": kv_bytes / 1e9 / (ms / 1e3)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "elementwise", "attention", "swiglu", "all"])
+    ap.add_argument("what", choices=["gemm", "elementwise", "attention", "swiglu", "decode", "all"])
+    ap.add_argument("--batch", type=int, default=64, help="decode: batch rows")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--shapes", default="", help="name:M,N,K,a_mn,b_mn;...")
     ap.add_argument("--lens", default="", help="attention: sequence lengths, e.g. 2048x4")
@@ -176,6 +276,12 @@ def main():
         bench_elementwise(args.iters)
     if args.what in ("swiglu", "all"):
         bench_swiglu(args.iters)
+    if args.what in ("decode", "all"):
+        lens = None
+        if args.lens:
+            n, c = args.lens.split("x")
+            lens = [int(n)] * int(c)
+        bench_decode(args.iters, args.batch, lens)
     if args.what in ("attention", "all"):
         lens = None
         if args.lens:

@@ -29,6 +29,27 @@ def test_gemm_streamk_matches_fp32(M, N, K):
     assert err < 2e-3 * max(1.0, ref.abs().max().item()), err
 
 
+@pytest.mark.parametrize("M,N,K", [(1, 256, 64), (7, 6144, 2560), (33, 2560, 4096), (64, 2560, 9728),
+                                   (64, 19456, 2560), (100, 1000, 704), (128, 2560, 4096), (129, 384, 2560),
+                                   (256, 6144, 2560), (64, 151936 // 8, 2560)])
+@pytest.mark.parametrize("pdl", [False, True])
+def test_gemm_decode_matches_fp32(M, N, K, pdl):
+    from libra_b200 import ops
+
+    torch.manual_seed(M * 3 + N + K)
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    w = (torch.randn(N, K, device="cuda") / math.sqrt(K)).bfloat16()
+    acc = torch.randn(M, N, device="cuda")
+    start = acc.clone()
+    ops.gemm_decode(x, w, acc, pdl=pdl)
+    ops.gemm_decode(x, w, acc, pdl=pdl)  # accumulates: start + 2 x
+    torch.cuda.synchronize()
+    ops.check_kernel_errors(x.device)
+    ref = start + 2 * (x.float() @ w.float().t())
+    err = (acc - ref).abs().max().item()
+    assert err < 2e-3 * max(1.0, ref.abs().max().item()), err
+
+
 def test_qkv_post_matches_reference():
     from libra_b200 import ops
     from libra_b200.ops import reference as ref
@@ -144,23 +165,21 @@ def test_sample_fp32_logits_zeroes_and_matches_bf16():
     from libra_b200 import ops
 
     torch.manual_seed(3)
-    B, V = 5, 151936 + 3
-    logits = (3 * torch.randn(B, V + 1, device="cuda"))[:, :V].contiguous()
-    logits = logits.bfloat16().float()  # exactly representable in bf16, so both paths see the same values
+    B, V, W = 5, 151937, 151940  # a vocabulary tail (V % 4 = 1) inside rows padded to 16 bytes
+    buf = (3 * torch.randn(B, W, device="cuda")).bfloat16().float()  # exact in bf16: both paths see the same
+    logits = buf[:, :V]
     temp = torch.tensor([1.0, 0.0, 0.7, 1.3, 1.0], device="cuda")
     seeds = torch.arange(B, device="cuda", dtype=torch.long) * 11 + 5
     pos = torch.arange(B, device="cuda", dtype=torch.long) + 100
     t1, l1 = torch.empty(B, dtype=torch.long, device="cuda"), torch.empty(B, device="cuda")
     t2, l2 = torch.empty_like(t1), torch.empty_like(l1)
-    ops.sample_tokens(logits.bfloat16(), temp, seeds, pos, t1, l1)
-    f = logits.clone()
-    if (f.stride(0) * 4) % 16:
-        pytest.skip("row stride not 16-byte aligned")
-    ops.sample_tokens(f, temp, seeds, pos, t2, l2)
+    ops.sample_tokens(buf.bfloat16()[:, :V], temp, seeds, pos, t1, l1)
+    ops.sample_tokens(logits, temp, seeds, pos, t2, l2)
     torch.cuda.synchronize()
     assert torch.equal(t1, t2)
     assert (l1 - l2).abs().max().item() < 1e-4
-    assert f.abs().max().item() == 0.0
+    assert buf[:, :V].abs().max().item() == 0.0  # the fp32 logits are zeroed behind the read
+    assert buf[:, V:].abs().max().item() > 0.0   # and nothing past the vocabulary
 
 
 def test_fused_decode_graphs_match_unfused(monkeypatch):

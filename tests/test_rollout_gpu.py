@@ -158,6 +158,9 @@ def test_decode_graphs_match_eager_steps(monkeypatch):
 
     def run(graphs: bool):
         monkeypatch.setenv("LIBRA_DECODE_GRAPHS", "1" if graphs else "0")
+        # the unfused captured step (bf16 GEMM epilogues, like the eager step); the fused one is
+        # compared against it in test_decode_fused_gpu.py
+        monkeypatch.setenv("LIBRA_DECODE_FUSED", "0")
         llm = LLMEngine(eng.cfg, eng.params, kv_blocks=512, block_size=16, max_model_len=1024, max_running=64)
         res = {}
         ids = [llm.add_request(p, sp, callback=lambda r: res.__setitem__(r.request_id, r))

@@ -75,8 +75,9 @@ __global__ void __launch_bounds__(256)
                     const float* __restrict__ sin_t, const int64_t* __restrict__ slot, __nv_bfloat16* __restrict__ q_out,
                     __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache, int B, int nq, int nkv,
                     float eps) {
-  pdl_wait();
+  // the next kernel may start launching now: it waits for this one before reading what it writes
   pdl_launch_dependents();
+  pdl_wait();
   const int heads = nq + nkv;
   const int lane = threadIdx.x & 31, grp = lane >> 3, j = lane & 7;
   const unsigned gmask = 0xFFu << (grp * 8);
@@ -145,8 +146,9 @@ constexpr int kRnVec = 4;
 __global__ void __launch_bounds__(kRnThreads)
     residual_norm_kernel(__nv_bfloat16* __restrict__ x, float* __restrict__ acc, const __nv_bfloat16* __restrict__ w,
                          __nv_bfloat16* __restrict__ h_out, int H, float eps) {
-  pdl_wait();
+  // the next kernel may start launching now: it waits for this one before reading what it writes
   pdl_launch_dependents();
+  pdl_wait();
   const int row = blockIdx.x;
   const int nvec = H >> 3;
   __nv_bfloat16* xr = x + (size_t)row * H;
@@ -194,8 +196,9 @@ __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.f + __
 
 __global__ void __launch_bounds__(256)
     swiglu_kernel(float* __restrict__ acc, __nv_bfloat16* __restrict__ a, int B, int F) {
-  pdl_wait();
+  // the next kernel may start launching now: it waits for this one before reading what it writes
   pdl_launch_dependents();
+  pdl_wait();
   const int per_row = F >> 3;
   const int total = B * per_row;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
@@ -218,10 +221,12 @@ __global__ void __launch_bounds__(256)
 // same number of bytes however uneven the lengths are, and the grid does not
 // depend on them, so one captured launch serves every step.  A CTA walks its
 // units sequence by sequence ("segments"):
-//  * one thread streams the K and V tiles of every block into an S-stage
-//    shared-memory ring with TMA: per KV head and 64-dim half one 16-row x
-//    128-byte box with the 128-byte swizzle, so the ldmatrix reads below are
-//    free of bank conflicts;
+//  * a producer warp streams the K and V tiles of every block into an
+//    S-stage shared-memory ring with TMA: per KV head and 64-dim half one
+//    16-row x 128-byte box with the 128-byte swizzle, so the ldmatrix reads
+//    below are free of bank conflicts.  A stage is refilled as soon as every
+//    compute warp has arrived on its "empty" barrier; the compute warps never
+//    wait for each other inside a segment;
 //  * one warp per KV head runs the block on the tensor cores (mma.sync
 //    m16n8k16, bf16 in, fp32 out): S = Q K^T with the head's G query rows
 //    (padded to 16) as A and K as B, online softmax on the accumulator
@@ -282,8 +287,23 @@ __device__ __forceinline__ uint32_t tile_addr(uint32_t base, int r, int c16) {
   return base + (uint32_t)((c16 >> 3) * kHalfTile + r * 128 + (((c16 & 7) ^ (r & 7)) << 4));
 }
 
+// Named barrier over the compute warps (the producer warp does not take
+// part); returns whether `pred` held in every participating thread.
+__device__ __forceinline__ bool compute_bar_and(int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "barrier.red.and.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 template <int G>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(288, 1)
     decode_attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                        const __nv_bfloat16* __restrict__ q, const int* __restrict__ tables, int max_blocks,
                        const int* __restrict__ lens, int B, int Hkv, int S, __nv_bfloat16* __restrict__ out,
@@ -293,15 +313,17 @@ __global__ void __launch_bounds__(256, 1)
   extern __shared__ __align__(1024) uint8_t sm_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nthreads = blockDim.x;
+  const int ncomp = 32 * Hkv;  // compute threads: one warp per KV head; warp Hkv is the producer
   const int Hq = Hkv * G;
   const uint32_t head_bytes = 2 * kHalfTile;             // one head's K (or V) tile of a block
   const uint32_t stage_bytes = 2 * Hkv * head_bytes;     // K tiles of every head, then V tiles
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + (size_t)S * stage_bytes);
-  int* pre = reinterpret_cast<int*>(full + 8);  // [B + 1]
+  uint64_t* empty = full + 8;
+  int* pre = reinterpret_cast<int*>(empty + 8);  // [B + 1]
   __shared__ int s_last;
-  pdl_wait();
+  // the next kernel may start launching now: it waits for this one before reading what it writes
   pdl_launch_dependents();
+  pdl_wait();
 
   if (warp == 0) {  // prefix sums of the per-sequence block counts
     int carry = 0;
@@ -322,7 +344,10 @@ __global__ void __launch_bounds__(256, 1)
   if (tid == 0) {
     prefetch_tmap(&tmK);
     prefetch_tmap(&tmV);
-    for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], Hkv);
+    }
     fence_barrier_init();
   }
   __syncthreads();
@@ -331,7 +356,7 @@ __global__ void __launch_bounds__(256, 1)
   if (c == 0) {  // sequences without any KV: zero output
     for (int b = 0; b < B; ++b)
       if (pre[b + 1] == pre[b])
-        for (int i = tid; i < Hq * kD; i += nthreads) out[(size_t)b * Hq * kD + i] = __float2bfloat16(0.f);
+        for (int i = tid; i < Hq * kD; i += blockDim.x) out[(size_t)b * Hq * kD + i] = __float2bfloat16(0.f);
   }
   // with fewer units than CTAs the extra CTAs sit out, so every working CTA has at least one unit
   const int NC = min((int)gridDim.x, TB);
@@ -347,29 +372,38 @@ __global__ void __launch_bounds__(256, 1)
     b0 = l;
     while (pre[b0 + 1] <= lo) ++b0;  // skip empty sequences
   }
-  // ---- producer state (thread 0)
-  int ld_it = lo, ld_b = b0;
-  auto issue = [&](int it) {
-    while (pre[ld_b + 1] <= it) ++ld_b;
-    const int blk = tables[(size_t)ld_b * max_blocks + (it - pre[ld_b])];
-    const int st = (it - lo) % S;
-    uint8_t* dst = sm + (size_t)st * stage_bytes;
-    mbar_expect_tx(&full[st], stage_bytes);
-    for (int h = 0; h < Hkv; ++h) {
-#pragma unroll
-      for (int d = 0; d < 2; ++d) {
-        tma_load_3d(dst + h * head_bytes + d * kHalfTile, &tmK, &full[st], 64 * d, h, blk * kBS);
-        tma_load_3d(dst + (Hkv + h) * head_bytes + d * kHalfTile, &tmV, &full[st], 64 * d, h, blk * kBS);
-      }
-    }
-  };
-  if (tid == 0)
-    for (; ld_it < hi && ld_it < lo + S; ++ld_it) issue(ld_it);
 
+  if (warp == Hkv) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int b = b0, it = lo;
+      for (; it < hi; ++it) {
+        const int st = (it - lo) % S;
+        const uint32_t ph = ((it - lo) / S) & 1u;
+        if (!mbar_wait(&empty[st], ph ^ 1u, err, kTimeoutAttnKV)) break;
+        while (pre[b + 1] <= it) ++b;
+        const int blk = tables[(size_t)b * max_blocks + (it - pre[b])];
+        uint8_t* dst = sm + (size_t)st * stage_bytes;
+        mbar_expect_tx(&full[st], stage_bytes);
+        for (int hh = 0; hh < Hkv; ++hh) {
+#pragma unroll
+          for (int d = 0; d < 2; ++d) {
+            tma_load_3d(dst + hh * head_bytes + d * kHalfTile, &tmK, &full[st], 64 * d, hh, blk * kBS);
+            tma_load_3d(dst + (Hkv + hh) * head_bytes + d * kHalfTile, &tmV, &full[st], 64 * d, hh, blk * kBS);
+          }
+        }
+      }
+      // the copies of the last S units must land before the CTA exits
+      for (int k = max(lo, it - S); k < it; ++k) mbar_wait(&full[(k - lo) % S], ((k - lo) / S) & 1u, nullptr, 0);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------ compute warps
   const int h = warp;             // this warp's KV head
   const int gid = lane >> 2, tig = lane & 3;
   const bool row_real = gid < G;  // this thread's query row (head h*G + gid) is a real head
-  bool aborted = false;
+  bool ok = true;
   int it = lo, cur_b = b0;
   while (it < hi) {
     while (pre[cur_b + 1] <= it) ++cur_b;
@@ -392,16 +426,13 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
       for (int e = 0; e < 4; ++e) o[dt][e] = 0.f;
     float m_run = -INFINITY, l_run = 0.f;
-    for (; it < seg_end; ++it) {
+    for (; ok && it < seg_end; ++it) {
       const int st = (it - lo) % S;
       const uint32_t ph = ((it - lo) / S) & 1u;
-      const bool ok = mbar_wait(&full[st], ph, err, kTimeoutAttnKV);
-      if (!__syncthreads_and(ok)) {
-        aborted = true;
+      if (!mbar_wait(&full[st], ph, err, kTimeoutAttnKV)) {
+        ok = false;
         break;
       }
-      // every warp is done with block it-1: its stage takes block it-1+S
-      if (tid == 0 && it > lo && ld_it < hi) issue(ld_it++);
       const uint32_t kbase = smem_u32(sm + (size_t)st * stage_bytes + h * head_bytes);
       const uint32_t vbase = kbase + Hkv * head_bytes;
       // ---- S = Q K^T: two n-tiles of 8 tokens, 8 k-steps of 16 dims
@@ -455,9 +486,12 @@ __global__ void __launch_bounds__(256, 1)
         mma_bf16(o[2 * dp], pa0, 0u, pa2, 0u, b00, b01);
         mma_bf16(o[2 * dp + 1], pa0, 0u, pa2, 0u, b10, b11);
       }
+      // this warp is done with the stage (its ldmatrix results are consumed above)
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
     }
-    if (aborted) break;
-    // ---- segment end
+    // ---- segment end (every compute warp gets here for every segment, also after a timeout)
+    if (!compute_bar_and(ncomp, ok)) break;
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
     const bool whole = seq_lo >= lo && seq_hi <= hi;
@@ -479,7 +513,7 @@ __global__ void __launch_bounds__(256, 1)
     }
     if (!whole) {
       __threadfence();
-      __syncthreads();
+      compute_bar_and(ncomp, true);
       if (tid == 0) {
         const int nseg = owner_cta(seq_hi - 1, TB, NC) - owner_cta(seq_lo, TB, NC) + 1;
         const int old = atomicAdd(&counters[cur_b], 1);
@@ -487,42 +521,71 @@ __global__ void __launch_bounds__(256, 1)
         if (last) counters[cur_b] = 0;
         s_last = last;
       }
-      __syncthreads();
+      compute_bar_and(ncomp, true);
       if (s_last) {
         __threadfence();
         const int c0 = owner_cta(seq_lo, TB, NC), c1 = owner_cta(seq_hi - 1, TB, NC);
-        for (int i = tid; i < Hq * (kD / 4); i += nthreads) {
-          const int hh = i / (kD / 4), d4 = i - hh * (kD / 4);
-          float M = -INFINITY;
-          for (int cc = c0; cc <= c1; ++cc)
-            M = fmaxf(M, __ldcg(part_ml + ((size_t)(cc + cur_b) * Hq + hh) * 2));
-          float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
-          float den = 0.f;
-          for (int cc = c0; cc <= c1; ++cc) {
-            const size_t slot = (size_t)(cc + cur_b) * Hq + hh;
-            const float2 ml = __ldcg(reinterpret_cast<const float2*>(part_ml + slot * 2));
-            if (ml.x == -INFINITY) continue;
-            const float w = exp2f(ml.x - M);
-            const float4 ov = __ldcg(reinterpret_cast<const float4*>(part_o + slot * kD) + d4);
-            num.x = fmaf(w, ov.x, num.x);
-            num.y = fmaf(w, ov.y, num.y);
-            num.z = fmaf(w, ov.z, num.z);
-            num.w = fmaf(w, ov.w, num.w);
-            den = fmaf(w, ml.y, den);
+        // Merge: thread t owns items (head warp + k Hkv, dims 4 lane..) for k < G and walks the
+        // partial slots CH at a time with every load of the chunk in flight before any is used
+        constexpr int CH = G >= 8 ? 2 : (G >= 4 ? 4 : 8);
+        float M[G], den[G];
+        float4 num[G];
+#pragma unroll
+        for (int k = 0; k < G; ++k) {
+          M[k] = -INFINITY;
+          den[k] = 0.f;
+          num[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        for (int cc = c0; cc <= c1; cc += CH) {
+          float2 ml[G][CH];
+          float4 ov[G][CH];
+#pragma unroll
+          for (int k = 0; k < G; ++k)
+#pragma unroll
+            for (int u = 0; u < CH; ++u) {
+              if (cc + u <= c1) {
+                const size_t slot = (size_t)(cc + u + cur_b) * Hq + warp + k * Hkv;
+                ml[k][u] = __ldcg(reinterpret_cast<const float2*>(part_ml + slot * 2));
+                ov[k][u] = __ldcg(reinterpret_cast<const float4*>(part_o + slot * kD) + lane);
+              } else {
+                ml[k][u] = make_float2(-INFINITY, 0.f);
+                ov[k][u] = make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+            }
+#pragma unroll
+          for (int k = 0; k < G; ++k) {
+            float Mn = M[k];
+#pragma unroll
+            for (int u = 0; u < CH; ++u) Mn = fmaxf(Mn, ml[k][u].x);
+            if (Mn == -INFINITY) continue;
+            const float a = M[k] == -INFINITY ? 0.f : exp2f(M[k] - Mn);
+            float4 acc = make_float4(num[k].x * a, num[k].y * a, num[k].z * a, num[k].w * a);
+            float d = den[k] * a;
+#pragma unroll
+            for (int u = 0; u < CH; ++u) {
+              const float w = ml[k][u].x == -INFINITY ? 0.f : exp2f(ml[k][u].x - Mn);
+              acc.x = fmaf(w, ov[k][u].x, acc.x);
+              acc.y = fmaf(w, ov[k][u].y, acc.y);
+              acc.z = fmaf(w, ov[k][u].z, acc.z);
+              acc.w = fmaf(w, ov[k][u].w, acc.w);
+              d = fmaf(w, ml[k][u].y, d);
+            }
+            num[k] = acc;
+            den[k] = d;
+            M[k] = Mn;
           }
-          const float inv = den > 0.f ? 1.f / den : 0.f;
+        }
+#pragma unroll
+        for (int k = 0; k < G; ++k) {
+          const float inv = den[k] > 0.f ? 1.f / den[k] : 0.f;
           uint2 pk;
-          pk.x = pack_bf16x2(num.x * inv, num.y * inv);
-          pk.y = pack_bf16x2(num.z * inv, num.w * inv);
-          *reinterpret_cast<uint2*>(out + ((size_t)cur_b * Hq + hh) * kD + 4 * d4) = pk;
+          pk.x = pack_bf16x2(num[k].x * inv, num[k].y * inv);
+          pk.y = pack_bf16x2(num[k].z * inv, num[k].w * inv);
+          *reinterpret_cast<uint2*>(out + ((size_t)cur_b * Hq + warp + k * Hkv) * kD + 4 * lane) = pk;
         }
       }
-      __syncthreads();
+      compute_bar_and(ncomp, true);
     }
-  }
-  if (aborted && tid == 0) {
-    // copies issued for units [it, ld_it) may still be in flight
-    for (int k = it; k < ld_it; ++k) mbar_wait(&full[(k - lo) % S], ((k - lo) / S) & 1u, nullptr, 0);
   }
 }
 
@@ -551,9 +614,9 @@ static void launch_attn(const torch::Tensor& q, const torch::Tensor& kc, const t
                         torch::Tensor& part_o, torch::Tensor& part_ml, torch::Tensor& counters, int* err,
                         float scale_log2, cudaStream_t st, bool pdl) {
   const int Hkv = (int)kc.size(2);
-  const int threads = 32 * Hkv;
+  const int threads = 32 * (Hkv + 1);  // a warp per KV head + the producer warp
   const size_t stage_bytes = (size_t)2 * Hkv * 2 * kHalfTile;
-  const size_t extra = 1024 /*alignment*/ + 64 + (size_t)(B + 1) * 4;
+  const size_t extra = 1024 /*alignment*/ + 128 + (size_t)(B + 1) * 4;
   // 227 KB per CTA, less a margin for the kernel's static shared memory
   constexpr size_t kMaxSmem = 226 * 1024;
   int S = (int)std::min<size_t>(8, (kMaxSmem - extra) / stage_bytes);

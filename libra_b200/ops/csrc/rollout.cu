@@ -345,8 +345,8 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(
     T* __restrict__ logits, int64_t ld, int V, const float* __restrict__ temperature,
     const int64_t* __restrict__ seeds, const int64_t* __restrict__ positions, int64_t* __restrict__ out_tok,
     float* __restrict__ out_lp, int64_t* __restrict__ next_tok) {
-  pdl_wait();
   pdl_launch_dependents();
+  pdl_wait();
   const int row = blockIdx.x;
   T* x = logits + (size_t)row * ld;
   const float Tm = temperature[row];

@@ -79,8 +79,9 @@ def barrier(world):
 
 
 def emit(rank, record):
+    # the record goes to the process's real stdout; everything else printed during the run goes to stderr
     if rank == 0:
-        print(json.dumps(record), flush=True)
+        print(json.dumps(record), file=sys.__stdout__, flush=True)
 
 
 def base_record(args, world, impl):
@@ -616,7 +617,14 @@ def run_reference_grpo(args, rank, world, local):
 
 
 def main():
+    import contextlib
+
     args = parse_args()
+    with contextlib.redirect_stdout(sys.stderr):  # stdout carries the one JSON record (emit) and nothing else
+        _main(args)
+
+
+def _main(args):
     rank, world, local = setup_dist(args.gpus)
     try:
         if not torch.cuda.is_available():

@@ -3,6 +3,9 @@
     nccl        all-gather health check over every GPU of the box (reference
                 scripts/nccl_allgather_preflight.py:30-53), spawned with one
                 process per GPU, a short process-group timeout, max over ranks.
+    nvlink      device-timed peer copy bandwidth of every ordered GPU pair
+                (one process; flags pairs below a fraction of the expected
+                per-direction NVLink bandwidth).
     grp         startup Global Resource Planner preflight from a config
                 (reference scripts/run_global_resource_preflight.py).
     placement   initial rollout/train placement of a config, printed as JSON
@@ -71,6 +74,83 @@ def cmd_nccl(a) -> int:
     mp.start_processes(_nccl_worker, args=(world, a.port, a.numel, a.iters, out), nprocs=world, join=True,
                        start_method="spawn")
     res = json.load(open(out))
+    print(json.dumps(res))
+    return 0 if res["ok"] else 1
+
+
+def classify_links(pairs: list, expect_gbs: float, min_fraction: float) -> dict:
+    """Judge measured peer-copy bandwidths: a pair is slow below
+    ``min_fraction * expect_gbs``.  ``pairs`` holds dicts with src, dst, gbs."""
+    floor = expect_gbs * min_fraction
+    slow = [p for p in pairs if p["gbs"] < floor]
+    vals = [p["gbs"] for p in pairs]
+    return {"ok": bool(pairs) and not slow, "pairs": len(pairs), "min_gbs": min(vals) if vals else 0.0,
+            "max_gbs": max(vals) if vals else 0.0, "median_gbs": sorted(vals)[len(vals) // 2] if vals else 0.0,
+            "floor_gbs": floor, "slow": slow}
+
+
+def measure_peer_copy(src_dev: int, dst_dev: int, nbytes: int, iters: int, bidirectional: bool = False) -> float:
+    """Device-timed copy from GPU ``src_dev`` into GPU ``dst_dev`` over NVLink
+    (peer access enabled by the runtime copy engine path), GB/s per direction.
+    Bidirectional: both directions run at once on two streams, and the figure
+    is per direction.  Timed with CUDA events on the copying streams after one
+    warm-up copy, and the slower direction is reported."""
+    import torch
+
+    n = nbytes // 2
+    a = torch.empty(n, dtype=torch.bfloat16, device=f"cuda:{src_dev}").fill_(1.0)
+    b = torch.empty(n, dtype=torch.bfloat16, device=f"cuda:{dst_dev}")
+    jobs = [(a, b, src_dev)]
+    if bidirectional:
+        a2 = torch.empty(n, dtype=torch.bfloat16, device=f"cuda:{dst_dev}").fill_(2.0)
+        b2 = torch.empty(n, dtype=torch.bfloat16, device=f"cuda:{src_dev}")
+        jobs.append((a2, b2, dst_dev))
+    streams = [torch.cuda.Stream(device=d) for _, _, d in jobs]
+    for (x, y, d), s in zip(jobs, streams):
+        with torch.cuda.stream(s):
+            y.copy_(x, non_blocking=True)
+    for d in {src_dev, dst_dev}:
+        torch.cuda.synchronize(d)
+    evs = []
+    for (x, y, d), s in zip(jobs, streams):
+        with torch.cuda.device(d), torch.cuda.stream(s):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for _ in range(iters):
+                y.copy_(x, non_blocking=True)
+            e1.record(s)
+            evs.append((e0, e1))
+    for d in {src_dev, dst_dev}:
+        torch.cuda.synchronize(d)
+    ms = max(e0.elapsed_time(e1) for e0, e1 in evs) / iters
+    ok = bool((b[:: max(1, n // 64)] == 1.0).all())
+    if not ok:
+        raise RuntimeError(f"peer copy {src_dev}->{dst_dev} delivered wrong data")
+    return n * 2 / (ms / 1e3) / 1e9
+
+
+def cmd_nvlink(a) -> int:
+    """Peer copy bandwidth between every ordered GPU pair of the box (the B200
+    replacement of the all-gather health check: on one NVSwitch box every
+    pair should see the same bandwidth, so one slow pair marks a bad link)."""
+    import torch
+
+    world = a.gpus or torch.cuda.device_count()
+    if world < 2:
+        print(json.dumps({"ok": False, "error": f"needs two or more CUDA devices, found {world}"}))
+        return 1
+    pairs = []
+    for s in range(world):
+        for d in range(world):
+            if s == d or (a.first_only and s != 0):
+                continue
+            if not torch.cuda.can_device_access_peer(s, d):
+                pairs.append({"src": s, "dst": d, "gbs": 0.0, "error": "no peer access"})
+                continue
+            gbs = measure_peer_copy(s, d, a.mbytes << 20, a.iters, bidirectional=a.bidirectional)
+            pairs.append({"src": s, "dst": d, "gbs": round(gbs, 1)})
+    res = classify_links(pairs, a.expect_gbs, a.min_fraction)
+    res.update({"world": world, "bytes": a.mbytes << 20, "bidirectional": a.bidirectional, "results": pairs})
     print(json.dumps(res))
     return 0 if res["ok"] else 1
 
@@ -167,6 +247,15 @@ def main(argv=None) -> int:
     p.add_argument("--iters", type=int, default=10)
     p.add_argument("--port", type=int, default=29531)
     p.set_defaults(fn=cmd_nccl)
+    p = sub.add_parser("nvlink")
+    p.add_argument("--gpus", type=int, default=0)
+    p.add_argument("--mbytes", type=int, default=256, help="copy size per pair, MiB")
+    p.add_argument("--iters", type=int, default=10)
+    p.add_argument("--bidirectional", action="store_true")
+    p.add_argument("--first-only", action="store_true", help="only pairs from GPU 0")
+    p.add_argument("--expect-gbs", type=float, default=770.0, help="expected per-direction peer copy GB/s")
+    p.add_argument("--min-fraction", type=float, default=0.6)
+    p.set_defaults(fn=cmd_nvlink)
     p = sub.add_parser("grp")
     p.add_argument("--config", required=True)
     p.add_argument("--profile", default="", help="length-profile JSONL (else a synthetic history)")

@@ -117,3 +117,30 @@ def test_cot_env():
     assert done and r == 1.0
     with pytest.raises(NoLegalActionException):
         env.step("more")
+
+
+def test_preflight_nvlink_classification(capsys):
+    import torch
+
+    from libra_b200.infra.preflight.__main__ import classify_links, main
+
+    pairs = [{"src": 0, "dst": 1, "gbs": 760.0}, {"src": 1, "dst": 0, "gbs": 742.0}]
+    res = classify_links(pairs, expect_gbs=770.0, min_fraction=0.6)
+    assert res["ok"] and res["min_gbs"] == 742.0 and res["max_gbs"] == 760.0 and not res["slow"]
+    res = classify_links(pairs + [{"src": 0, "dst": 2, "gbs": 120.0}], expect_gbs=770.0, min_fraction=0.6)
+    assert not res["ok"] and [p["dst"] for p in res["slow"]] == [2]
+    assert not classify_links([], 770.0, 0.6)["ok"]
+    if torch.cuda.device_count() < 2:
+        assert main(["nvlink"]) == 1
+        assert "needs two or more" in capsys.readouterr().out
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+def test_preflight_nvlink_probe_two_gpus(capsys):
+    from libra_b200.infra.preflight.__main__ import main
+
+    rc = main(["nvlink", "--gpus", "2", "--mbytes", "64", "--iters", "4", "--min-fraction", "0.3"])
+    out = json.loads(capsys.readouterr().out)
+    assert out["pairs"] == 2 and out["min_gbs"] > 0
+    assert rc == 0, out

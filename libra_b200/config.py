@@ -207,6 +207,12 @@ class ProfilingConfig(ConfigSection):
     theta_slowdown: float = 1.0
     prefill_mfu: float = 0.55
     decode_bw_util: float = 0.85
+    # B200 additions (0 keeps the reference's steady-batch rollout model): fixed latency of one decode
+    # step per layer (kernel chain, pipeline fill) and the extra time per running sequence per layer;
+    # when either is set, an instance's makespan is simulated step by step (continuous batching, the
+    # batch shrinking as sequences finish) instead of assuming a full steady batch
+    decode_layer_overhead_s: float = 0.0
+    decode_row_layer_s: float = 0.0
     prefill_chunk_size: int = 1024
     kv_frag_rate: float = 0.04
     act_workspace_bytes: float = 1.0e9

@@ -143,3 +143,37 @@ class ShadowCalibrator:
         rm = cost_model.rollout_model
         tm.train_mfu = _clip(baseline_mfu * self.params.eta_comp / 0.5, 0.05, 1.0)
         rm.decode_bw_util = _clip(baseline_bw_util * self.params.eta_mem / 0.5, 0.05, 1.0)
+
+
+# ------------------------------------------------------------------ offline fit of the B200 decode profile
+def fit_decode_profile(samples: List[Dict[str, float]], n_layers: int, mem_bw: float) -> Dict[str, float]:
+    """Fit the rollout model's decode-step terms to measured whole-step times.
+
+    Each sample is one measured decode step of the engine: ``batch`` running
+    sequences, ``weight_bytes`` and ``kv_bytes`` read, ``ms`` per step (the
+    decode microbenchmark's CUDA-event time).  Model:
+    ``ms = n_layers * (layer_overhead + batch * row_layer) + bytes / (mem_bw * util)``,
+    solved by least squares for (layer_overhead, row_layer, 1/util).  Returns
+    the ``profiling`` keys ``decode_layer_overhead_s``, ``decode_row_layer_s``
+    and ``decode_bw_util`` plus the fit's largest relative error."""
+    import numpy as np
+
+    if len(samples) < 3:
+        raise ValueError("need at least three measured decode steps")
+    A = np.array([[n_layers, n_layers * s["batch"], (s["weight_bytes"] + s["kv_bytes"]) / mem_bw] for s in samples])
+    y = np.array([s["ms"] / 1e3 for s in samples])
+    (a, r, inv_u), *_ = np.linalg.lstsq(A, y, rcond=None)
+    a, r = max(float(a), 0.0), max(float(r), 0.0)
+    util = 1.0 / float(inv_u) if inv_u > 0 else 1.0
+    util = min(max(util, 0.05), 1.0)
+    pred = A @ np.array([a, r, 1.0 / util])
+    err = float(np.max(np.abs(pred - y) / y))
+    return {"decode_layer_overhead_s": a, "decode_row_layer_s": r, "decode_bw_util": util, "max_rel_error": err}
+
+
+def fit_train_mfu(measured_s: float, predicted_s: float, mfu_used: float) -> float:
+    """Training MFU that makes the FLOP-based prediction match a measured step
+    (the time is inverse in the MFU)."""
+    if measured_s <= 0 or predicted_s <= 0:
+        raise ValueError("times must be positive")
+    return _clip(mfu_used * predicted_s / measured_s, 0.05, 1.0)

@@ -102,7 +102,8 @@ class RolloutCostModel:
                  dtype_bytes: int, flops_peak: float, mem_bw: float, mem_capacity: float, tp_comm_overhead: float,
                  prefill_mfu: float = 0.55, decode_bw_util: float = 0.85, prefill_chunk_size: int = 1024,
                  kv_frag_rate: float = 0.04, act_workspace_bytes: float = 1.0e9, max_queue_limit: int = 256,
-                 effective_num_params: Optional[float] = None, n_heads: int = 0):
+                 effective_num_params: Optional[float] = None, n_heads: int = 0,
+                 decode_layer_overhead_s: float = 0.0, decode_row_layer_s: float = 0.0):
         self.P = num_params
         self.P_active = effective_num_params or num_params
         self.d_model, self.n_layers = d_model, n_layers
@@ -114,6 +115,8 @@ class RolloutCostModel:
         self.L_chunk = prefill_chunk_size
         self.kv_frag_rate, self.act_workspace = kv_frag_rate, act_workspace_bytes
         self.max_queue_limit = max_queue_limit
+        self.decode_layer_overhead_s = decode_layer_overhead_s
+        self.decode_row_layer_s = decode_row_layer_s
 
     def compute_token_kv_bytes(self, tp: int) -> float:
         """KV bytes per token held by ONE GPU of a TP group (heads replicated if tp > kv)."""
@@ -168,9 +171,61 @@ class RolloutCostModel:
             load[best] += req.total_length
         return insts
 
+    def simulate_instance_makespan(self, requests: List[RequestInfo], tp: int) -> float:
+        """Step-by-step makespan of one instance that admits every request at
+        once (up to the steady batch) and decodes one token per running
+        sequence per step, the batch shrinking as sequences finish; a finished
+        sequence's slot goes to the next waiting request.  Step time = fixed
+        latency + running rows x per-row time + (weights / tp + resident KV) /
+        (bandwidth x utilisation).  Between two finish events the running set is
+        constant and its KV grows by one token per sequence per step, so each
+        segment is summed in closed form."""
+        import heapq
+
+        ap, ag = _mean(r.prompt_length for r in requests), _mean(r.gen_length for r in requests)
+        cap = max(1, int(self.compute_steady_state_batch(tp, ap, ag)))
+        kv_tok = self.compute_token_kv_bytes(tp)
+        w = self.P_active * self.dtype_bytes / tp
+        bw = self.mem_bw * max(self.decode_bw_util, 1e-6)
+        fixed = self.n_layers * self.decode_layer_overhead_s + self._tp_sync(tp)
+        row = self.n_layers * self.decode_row_layer_s
+        waiting = list(requests)
+        prefill = sum(r.prompt_length for r in requests) / max(self.L_chunk, 1) * \
+            self.compute_prefill_step_time(1, self.L_chunk, tp)
+        heap: List[Tuple[int, int]] = []  # (finish step, request index)
+        ctx0 = {}                         # request index -> (start step, prompt length)
+        step, nxt, total, kv_at_step = 0, 0, 0.0, 0.0
+
+        def admit(at: int) -> None:
+            nonlocal nxt
+            while nxt < len(waiting) and len(heap) < cap:
+                r = waiting[nxt]
+                heapq.heappush(heap, (at + max(1, r.gen_length), nxt))
+                ctx0[nxt] = (at, r.prompt_length)
+                nxt += 1
+
+        admit(0)
+        while heap:
+            end = heap[0][0]
+            k = end - step
+            if k > 0:
+                n = len(heap)
+                # resident KV tokens at the first step of the segment
+                kv0 = sum(p + (step - s0) for s0, p in (ctx0[i] for _, i in heap))
+                kv_sum = k * kv0 + n * k * (k - 1) / 2.0
+                total += k * (fixed + n * row) + (k * w + kv_sum * kv_tok) / bw
+                step = end
+            while heap and heap[0][0] == step:
+                _, i = heapq.heappop(heap)
+                del ctx0[i]
+            admit(step)
+        return prefill + total
+
     def compute_instance_makespan(self, requests: List[RequestInfo], tp: int) -> float:
         if not requests:
             return 0.0
+        if self.decode_layer_overhead_s > 0.0 or self.decode_row_layer_s > 0.0:
+            return self.simulate_instance_makespan(requests, tp)
         ap, ag = _mean(r.prompt_length for r in requests), _mean(r.gen_length for r in requests)
         b = self.compute_steady_state_batch(tp, ap, ag)
         prefill = sum(r.prompt_length for r in requests) / max(self.L_chunk, 1) * \
@@ -395,7 +450,8 @@ class CostModel:
         self.rollout_model = RolloutCostModel(
             ma.num_params, ma.d_model, ma.n_layers, ma.n_kv_heads, ma.head_dim, ma.dtype_bytes, peak, bw,
             hw.mem_capacity, hw.tp_comm_overhead, pf.prefill_mfu, pf.decode_bw_util, pf.prefill_chunk_size,
-            pf.kv_frag_rate, pf.act_workspace_bytes, effective_num_params=ma.effective_num_params, n_heads=ma.n_heads)
+            pf.kv_frag_rate, pf.act_workspace_bytes, effective_num_params=ma.effective_num_params, n_heads=ma.n_heads,
+            decode_layer_overhead_s=pf.decode_layer_overhead_s, decode_row_layer_s=pf.decode_row_layer_s)
         self.training_model = TrainingCostModel(
             ma.num_params, ma.d_model, ma.n_layers, ma.n_kv_heads, ma.head_dim, ma.dtype_bytes, peak, bw,
             hw.mem_capacity, link, hw.bw_inter_node, hw.gpus_per_node, hw.latency_inter_node,

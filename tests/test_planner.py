@@ -156,3 +156,48 @@ def test_calibrator_change_point():
     cal.update(EpochRunData(t_train_real=40.0, t_train_predicted=10.0, gen_lengths=[5000.0] * 4, epoch_id=7))
     st = cal.get_statistics()
     assert st["is_change_point"] and st["change_point_count"] == 1 and cal.params.eta_comp < 0.5
+
+
+def test_b200_profile_predicts_measured_grpo_phases(tmp_path):
+    """With the B200 profile of the presets, the cost model reproduces the
+    phases of the 1-GPU Qwen3-4B GRPO step measured with ``python bench.py``
+    (synthetic workload steps 3-7: rollout 17.97 s, train 5.85 s per step)."""
+    from libra_b200.workflow.synthetic import WORKLOADS, rollout_requests
+
+    cfg = _cfg(tmp_path)
+    cm = CostModel(cfg.hardware, cfg.model_arch, cfg.profiling, max_seq_length=5136)
+    train, roll = [], []
+    for s in range(3, 8):
+        reqs = [RequestInfo(len(r.prompt), r.response_len)
+                for r in rollout_requests(WORKLOADS["qwen3-4b-grpo"], s, rank=0, prompts=8)]
+        tok = sum(r.total_length for r in reqs)
+        train.append(cm.evaluate_training(TrainParallelConfig(tp=1, pp=1, dp=1, b_micro=8), 64, tok // 64)[0])
+        roll.append(cm.evaluate_rollout(RolloutClusterConfig([1]), reqs)[0])
+    assert abs(sum(train) / 5 - 5.85) / 5.85 < 0.1
+    assert abs(sum(roll) / 5 - 17.97) / 17.97 < 0.1
+
+
+def test_fit_decode_profile_recovers_terms():
+    from libra_b200.infra.cost_model.calibrator import fit_decode_profile, fit_train_mfu
+
+    L, bw, a, r, u = 36, 6.5e12, 40e-6, 4e-7, 0.9
+    samples = []
+    for b, kv in ((4, 1e9), (16, 5e9), (64, 2e10), (64, 4e9), (32, 8e9)):
+        ms = (L * (a + b * r) + (8e9 + kv) / (bw * u)) * 1e3
+        samples.append({"batch": b, "weight_bytes": 8e9, "kv_bytes": kv, "ms": ms})
+    fit = fit_decode_profile(samples, L, bw)
+    assert abs(fit["decode_layer_overhead_s"] - a) / a < 1e-6
+    assert abs(fit["decode_row_layer_s"] - r) / r < 1e-6
+    assert abs(fit["decode_bw_util"] - u) < 1e-6 and fit["max_rel_error"] < 1e-9
+    assert abs(fit_train_mfu(5.85, 6.05, 0.55) - 0.55 * 6.05 / 5.85) < 1e-12
+
+
+def test_simulated_makespan_is_bounded_by_the_longest_generation(tmp_path):
+    cfg = _cfg(tmp_path)
+    cm = CostModel(cfg.hardware, cfg.model_arch, cfg.profiling, max_seq_length=5136)
+    rm = cm.rollout_model
+    reqs = [RequestInfo(300, 100) for _ in range(63)] + [RequestInfo(300, 4000)]
+    t = rm.compute_instance_makespan(reqs, 1)
+    per_step_floor = cfg.model_arch.n_layers * cfg.profiling.decode_layer_overhead_s
+    assert t > 4000 * per_step_floor  # the long request's 4000 steps cannot overlap
+    assert rm.compute_instance_makespan(reqs[:63], 1) < 0.1 * t

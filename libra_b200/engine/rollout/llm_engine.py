@@ -107,7 +107,10 @@ class LLMEngine:
             kv_blocks = PagedKVCache.blocks_for_budget(budget, cfg.num_hidden_layers, block_size, nkv, cfg.head_dim)
         self.kv = PagedKVCache(cfg.num_hidden_layers, kv_blocks, block_size, nkv, cfg.head_dim, self.device,
                                next(iter(params.values())).dtype)
-        self.runner = InferenceRunner(cfg, params, self.kv, tp_group, tp_size)
+        # a step carries at most the prefill budget plus one decode token per running sequence (a single
+        # longer prompt falls back to the unfused all-reduce for its step)
+        self.runner = InferenceRunner(cfg, params, self.kv, tp_group, tp_size,
+                                      max_step_tokens=max_batch_tokens + max_running)
         self.max_batch_tokens = max_batch_tokens
         self.max_running = max_running
         self.max_model_len = max_model_len or cfg.max_position_embeddings

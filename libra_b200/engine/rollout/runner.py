@@ -53,15 +53,33 @@ def _extend_attention_ref(q, k, v, q_start: int):
 
 class InferenceRunner:
     def __init__(self, cfg: Qwen3Config, params: Dict[str, torch.Tensor], kv_cache: PagedKVCache,
-                 tp_group=None, tp_size: int = 1):
+                 tp_group=None, tp_size: int = 1, max_step_tokens: int = 0):
         self.cfg, self.p, self.kv = cfg, params, kv_cache
         self.device = next(iter(params.values())).device
         self.tp_group, self.tp_size = tp_group, tp_size
+        self.peer_ar = self._make_peer_allreduce(max_step_tokens)
         self.nq = cfg.num_attention_heads // tp_size
         self.nkv = max(1, cfg.num_key_value_heads // tp_size)
         cos, sin = ops.ref.rope_tables(cfg.max_position_embeddings, cfg.head_dim, cfg.rope_theta, self.device)
         self.cos, self.sin = cos, sin
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
+
+    def _make_peer_allreduce(self, max_rows: int):
+        """Tensor-parallel ranks on NCCL (one box) reduce the row-parallel GEMM
+        outputs over NVLink peer memory, fused with the residual add and the
+        next RMSNorm (``PeerAllReduce``).  ``LIBRA_TP_PEER_AR=0`` keeps the NCCL
+        all-reduce; gloo ranks and mixture-of-experts layers always do."""
+        import os
+
+        import torch.distributed as dist
+
+        if (self.tp_size <= 1 or self.device.type != "cuda" or self.cfg.is_moe or max_rows <= 0
+                or os.environ.get("LIBRA_TP_PEER_AR", "1") == "0"
+                or dist.get_backend(self.tp_group) != "nccl"):
+            return None
+        from libra_b200.parallel.peer_allreduce import PeerAllReduce
+
+        return PeerAllReduce(self.tp_group, max_rows, self.cfg.hidden_size, self.device)
 
     @property
     def lm_head(self):
@@ -150,7 +168,28 @@ class InferenceRunner:
             x = vocab_parallel_embedding(tok_t, self.p["embed_tokens"], self.tp_group, dist.get_rank(self.tp_group))
         else:
             x = self.p["embed_tokens"].index_select(0, tok_t)
-        for layer in range(cfg.num_hidden_layers):
+        peer = self.peer_ar if self.peer_ar is not None and x.shape[0] <= self.peer_ar.max_rows else None
+        L = cfg.num_hidden_layers
+        if peer is not None:
+            # fused path: each row-parallel GEMM writes its partial into the peer buffer; one kernel sums
+            # the TP partials over NVLink, adds the residual and applies the next RMSNorm
+            h = ops.rmsnorm(x, p["layers.0.input_layernorm"], cfg.rms_norm_eps)
+            for layer in range(L):
+                pre = f"layers.{layer}."
+                qkv = ops.linear(h, p[pre + "qkv_proj"])
+                q, k, v = ops.qk_norm_rope(qkv, p[pre + "q_norm"], p[pre + "k_norm"], pos_t, self.cos, self.sin,
+                                           self.nq, self.nkv, cfg.rms_norm_eps)
+                self.kv.write(layer, slot_t, k, v)
+                attn = self._attention(layer, q, items, offsets, decode_only)
+                ops.gemm(attn.reshape(attn.shape[0], -1), p[pre + "o_proj"], out=peer.partial(x.shape[0]))
+                x, h = peer.reduce_add_rmsnorm(x, p[pre + "post_attention_layernorm"], cfg.rms_norm_eps)
+                ops.gemm(ops.linear_swiglu(h, p[pre + "gate_up_proj"]), p[pre + "down_proj"],
+                         out=peer.partial(x.shape[0]))
+                nxt = p[f"layers.{layer + 1}.input_layernorm"] if layer + 1 < L else p["norm"]
+                x, h = peer.reduce_add_rmsnorm(x, nxt, cfg.rms_norm_eps)
+            last = h.index_select(0, last_rows)
+            return self._finish_step(items, last)
+        for layer in range(L):
             pre = f"layers.{layer}."
             h = ops.rmsnorm(x, p[pre + "input_layernorm"], cfg.rms_norm_eps)
             qkv = ops.linear(h, p[pre + "qkv_proj"])
@@ -167,6 +206,9 @@ class InferenceRunner:
             else:
                 x = self._row_parallel(ops.linear_swiglu(h, p[pre + "gate_up_proj"]), p[pre + "down_proj"], x)
         last = ops.rmsnorm(x.index_select(0, last_rows), p["norm"], cfg.rms_norm_eps)
+        return self._finish_step(items, last)
+
+    def _finish_step(self, items: Sequence[WorkItem], last: torch.Tensor) -> torch.Tensor:
         logits = ops.linear(last, self.lm_head)
         if self.tp_size > 1:
             from libra_b200.parallel.tensor_parallel import gather_vocab_logits

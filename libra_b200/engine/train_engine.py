@@ -70,6 +70,8 @@ class B200TrainEngine:
     """Native GRPO training engine (single process per GPU)."""
 
     train_backend = "b200"
+    _peer_grad = None      # PeerGradReduce when the DP exchange runs over peer memory
+    _sq_ready = False      # the reduce left the global squared gradient norm in sq_norm
 
     def __init__(self, model: Any = "qwen3-4b", learning_rate: float = 1e-6, kl_coef: float = 0.001,
                  clip_epsilon: float = 0.2, micro_batch_size: int = 4, recompute_micro_batch_size: int = 0,
@@ -77,7 +79,7 @@ class B200TrainEngine:
                  use_distributed_optimizer: bool = True, dp_group=None, temperature: float = 1.0,
                  max_grad_norm: float = 1.0, tp_size: int = 1, model_path: str = "",
                  max_tokens_per_micro_batch: int = 16384, max_tokens_per_recompute_batch: int = 65536,
-                 ep_size: int = 1):
+                 ep_size: int = 1, sequence_parallel: bool = False):
         self.cfg: Qwen3Config = get_config(model)
         self.model_path = model_path
         self.optim = OptimConfig(lr=learning_rate, max_grad_norm=max_grad_norm)
@@ -92,6 +94,7 @@ class B200TrainEngine:
         self.use_distributed_optimizer = use_distributed_optimizer
         self.temperature = temperature
         self.tp_size = tp_size
+        self.sequence_parallel = bool(sequence_parallel) and tp_size > 1
         self.ep_size = max(1, int(ep_size))
         if self.ep_size > 1 and not self.cfg.is_moe:
             raise ValueError(f"ep_size={self.ep_size} needs a mixture-of-experts model")
@@ -198,11 +201,22 @@ class B200TrainEngine:
             self.ep_exchange = PeerExpertExchange(self.ep_group, rows, self.cfg.hidden_size, dev)
         self.model = Qwen3Model(self.cfg, self.params, recompute=self.recompute_activations, tp_group=self.tp_group,
                                 tp_size=self.tp_size, tp_rank=self.tp_rank, ep_group=self.ep_group,
-                                ep_size=self.ep_size, ep_exchange=self.ep_exchange)
+                                ep_size=self.ep_size, ep_exchange=self.ep_exchange,
+                                sequence_parallel=self.sequence_parallel)
+        self.sequence_parallel = self.model.sp  # off for mixture-of-experts layers
+        if (self.sequence_parallel and dev.type == "cuda" and dist.get_backend(self.tp_group) == "nccl"
+                and os.environ.get("LIBRA_SP_FUSED", "1") != "0"):
+            # row-parallel linears (o_proj, down_proj: output width H) reduce-scatter inside the GEMM
+            # kernel over NVLink peer memory, for chunks up to the larger token budget
+            from libra_b200.parallel.sequence_parallel import enable_fused_sequence_parallel, sp_multiple
+
+            m = sp_multiple(self.tp_size, dev)
+            rows = max(self.max_tokens_per_micro_batch, self.max_tokens_per_recompute_batch)
+            enable_fused_sequence_parallel(self.tp_group, (rows + m - 1) // m * m, [self.cfg.hidden_size], [], dev)
         from libra_b200.parallel.tensor_parallel import tp_partial_grad_params
 
-        self._tp_partial = [self.params[n].main_grad for n in tp_partial_grad_params(list(self.params))
-                            ] if self.tp_size > 1 else []
+        self._tp_partial = [self.params[n].main_grad for n in tp_partial_grad_params(
+            list(self.params), self.sequence_parallel)] if self.tp_size > 1 else []
         # replicated (1-D) parameters inside this rank's optimizer shard: the
         # global grad norm counts them once, not once per TP rank
         self._tp_replicated = []
@@ -214,6 +228,10 @@ class B200TrainEngine:
                     a, b = max(a, lo), min(b, hi)
                     if a < b:
                         self._tp_replicated.append((a - lo, b - lo))
+        self._peer_grad = None
+        self._sq_ready = False
+        if self._peer_dp_applies():
+            self.enable_peer_data_parallel()
 
     def _init_expert_parallel(self) -> None:
         """Expert-parallel groups inside the data-parallel group: ``ep_group`` =
@@ -307,7 +325,12 @@ class B200TrainEngine:
         ``traj_weights[i]`` is the loss weight of every action token of
         trajectory i (see ``loss_weights``)."""
         ids, masks = zip(*(self._traj_tensors(t) for t in trajectories))
-        batch = pack_sequences(list(ids), list(masks))
+        pad = 1
+        if self.sequence_parallel:
+            from libra_b200.parallel.sequence_parallel import sp_multiple
+
+            pad = sp_multiple(self.tp_size, self.device)
+        batch = pack_sequences(list(ids), list(masks), pad_multiple=pad)
         extra: Dict[str, torch.Tensor] = {}
         if with_old_logprobs:
             old = torch.cat([t["logprobs"].reshape(-1).float() for t in trajectories])
@@ -478,7 +501,11 @@ class B200TrainEngine:
         if self.dp_size <= 1 or not dist.is_initialized():
             return
         dense = self.flat_grad[:self.dense_numel]
-        if self.sharded:
+        if self._peer_grad is not None:
+            # one kernel: pull this rank's shard from every rank over NVLink, average, global sum of squares
+            self._peer_grad.reduce(self.grad_shard, scale=1.0 / self.dp_size, sq_norm=self.sq_norm)
+            self._sq_ready = True
+        elif self.sharded:
             if self._gloo():  # gloo has no reduce_scatter_tensor
                 dist.all_reduce(dense, op=dist.ReduceOp.SUM, group=self.dp_group)
                 self.grad_shard.copy_(dense[self.shard_start:self.shard_start + self.shard_numel])
@@ -505,8 +532,11 @@ class B200TrainEngine:
 
     def _optimizer_step(self) -> None:
         self.step_count += 1
-        self.sq_norm.zero_()
-        ops.grad_sq_norm(self.grad_shard, self.sq_norm)
+        if self._sq_ready:  # the peer reduce-scatter left the global sum of squares of the dense gradient
+            self._sq_ready = False
+        else:
+            self.sq_norm.zero_()
+            ops.grad_sq_norm(self.grad_shard, self.sq_norm)
         if self.tp_size > 1:
             rep = torch.zeros(1, dtype=torch.float32, device=self.device)
             for a, b in self._tp_replicated:
@@ -517,7 +547,7 @@ class B200TrainEngine:
             total = both[:1].clone()
             dist.all_reduce(total, group=self.tp_group)
             self.sq_norm.copy_(total - (self.tp_size - 1) * both[1:])
-        elif self.sharded:
+        elif self.sharded and self._peer_grad is None:
             dist.all_reduce(self.sq_norm, op=dist.ReduceOp.SUM, group=self.dp_group)
         o = self.optim
         if self.x_master is not None:
@@ -544,6 +574,35 @@ class B200TrainEngine:
                        step=self.step_count, max_grad_norm=o.max_grad_norm, sq_norm=self.sq_norm)
         if self.sharded:
             self._gather_params(shard_param)
+
+    def _peer_dp_applies(self) -> bool:
+        """Whether the data-parallel gradient and parameter exchange runs over
+        NVLink peer memory: a sharded distributed optimizer on NCCL ranks of one
+        box (CUDA IPC), TP=1, at most 8 ranks; ``LIBRA_PEER_DP=0`` keeps NCCL.
+        Every rank reaches the same answer (the host check is collective)."""
+        if (self.device.type != "cuda" or not self.sharded or not dist.is_initialized() or self._gloo()
+                or self.tp_size != 1 or self.dp_size > 8 or self.shard_numel % 4
+                or os.environ.get("LIBRA_PEER_DP", "1") == "0"):
+            return False
+        hosts = [None] * self.dp_size
+        dist.all_gather_object(hosts, os.uname().nodename, group=self.dp_group)
+        return len(set(hosts)) == 1
+
+    def enable_peer_data_parallel(self) -> None:
+        """Collective over the DP group: gradient reduce-scatter (fused with the
+        1/dp average and the global norm) and the parameter all-gather (fused
+        into AdamW) over NVLink peer memory instead of NCCL."""
+        from libra_b200.parallel.peer_grad_reduce import PeerGradReduce
+
+        self._peer_grad = PeerGradReduce(self.dp_group, self.flat_grad, self.shard_start, self.shard_numel)
+        self.enable_fused_param_gather()
+
+    def close_peer_data_parallel(self) -> None:
+        for attr in ("_peer_grad", "_peer_param_gather"):
+            obj = getattr(self, attr, None)
+            if obj is not None:
+                obj.close()
+                setattr(self, attr, None)
 
     def enable_fused_param_gather(self) -> bool:
         """Collective over the DP group: fuse the distributed optimizer's parameter all-gather into the
@@ -572,6 +631,7 @@ class B200TrainEngine:
 
     def release_optimizer_state(self) -> None:
         """Drop master/Adam/gradient buffers (inference-only holders of the weights)."""
+        self.close_peer_data_parallel()
         self.master = self.exp_avg = self.exp_avg_sq = None
         self.grad_shard = None
         self.flat_grad = torch.zeros(0, dtype=torch.float32, device=self.device)
@@ -794,4 +854,5 @@ def create_train_engine(config) -> B200TrainEngine:
                            use_distributed_optimizer=config.use_distributed_optimizer,
                            temperature=config.temperature, model_path=config.model_path,
                            tp_size=int(getattr(config, "train_tp_size", 1) or 1),
-                           ep_size=int(getattr(config, "train_ep_size", 1) or 1))
+                           ep_size=int(getattr(config, "train_ep_size", 1) or 1),
+                           sequence_parallel=bool(getattr(config, "sequence_parallel", False)))

@@ -275,9 +275,20 @@ class PackedBatch:
 
 
 def pack_sequences(seqs: List[torch.Tensor], masks: Optional[List[torch.Tensor]] = None,
-                   pin: bool = False) -> PackedBatch:
+                   pin: bool = False, pad_multiple: int = 1) -> PackedBatch:
     """Pack 1-D token tensors; ``masks[i][t] = 1`` marks tokens[t] as an action token
-    (its logprob is computed from the row t-1)."""
+    (its logprob is computed from the row t-1).  ``pad_multiple > 1`` appends
+    one padding sequence (token 0, no action rows) so the token count is a
+    multiple of it (sequence parallelism splits the rows evenly)."""
+    total = sum(int(s.numel()) for s in seqs)
+    if pad_multiple > 1 and total % pad_multiple:
+        pad = pad_multiple - total % pad_multiple
+        seqs = list(seqs) + [torch.zeros(pad, dtype=torch.long)]
+        if masks is not None:
+            masks = list(masks) + [torch.zeros(pad, dtype=torch.bool)]
+        else:
+            masks = [torch.ones(int(s.numel()), dtype=torch.bool) for s in seqs[:-1]] + \
+                [torch.zeros(pad, dtype=torch.bool)]
     lens = [int(s.numel()) for s in seqs]
     cu = torch.zeros(len(seqs) + 1, dtype=torch.int32)
     cu[1:] = torch.tensor(lens, dtype=torch.int32).cumsum(0)
@@ -320,12 +331,15 @@ class Qwen3Model(nn.Module):
 
     def __init__(self, cfg: Qwen3Config, params: Dict[str, torch.Tensor], recompute: bool = False,
                  tp_group=None, tp_size: int = 1, tp_rank: int = 0, ep_group=None, ep_size: int = 1,
-                 ep_exchange=None):
+                 ep_exchange=None, sequence_parallel: bool = False):
         super().__init__()
         self.cfg = cfg
         self.p = params
         self.recompute = recompute
         self.tp_group, self.tp_size, self.tp_rank = tp_group, tp_size, tp_rank
+        # sequence parallelism: the residual stream holds T / tp token rows per rank (the packed batch's
+        # token count must divide evenly: pack with pad_multiple = sp_multiple(tp, device))
+        self.sp = bool(sequence_parallel) and tp_size > 1 and not cfg.is_moe
         # expert parallelism: this rank holds num_experts / ep_size experts; tokens travel to their
         # experts' owners through ``ep_exchange`` (peer-memory kernels) or all-to-all over ``ep_group``
         self.ep_group, self.ep_size, self.ep_exchange = ep_group, ep_size, ep_exchange
@@ -340,8 +354,14 @@ class Qwen3Model(nn.Module):
     def _attention_block(self, i: int, x, pos, cu, max_len, tiles=None):
         p, cfg = self.p, self.cfg
         pre = f"layers.{i}."
-        h = self._tp_in(ops.rmsnorm(x, p[pre + "input_layernorm"], cfg.rms_norm_eps))
-        qkv = ops.linear(h, p[pre + "qkv_proj"])
+        if self.sp:
+            from libra_b200.parallel.sequence_parallel import sp_column_parallel_linear
+
+            qkv = sp_column_parallel_linear(ops.rmsnorm(x, p[pre + "input_layernorm"], cfg.rms_norm_eps),
+                                            p[pre + "qkv_proj"], self.tp_group)
+        else:
+            h = self._tp_in(ops.rmsnorm(x, p[pre + "input_layernorm"], cfg.rms_norm_eps))
+            qkv = ops.linear(h, p[pre + "qkv_proj"])
         q, k, v = ops.qk_norm_rope(qkv, p[pre + "q_norm"], p[pre + "k_norm"], pos, self.rope_cos, self.rope_sin,
                                    self.nq_local, self.nkv_local, cfg.rms_norm_eps)
         attn = ops.varlen_causal_attention(q, k, v, cu, max_len, tiles=tiles)
@@ -360,7 +380,12 @@ class Qwen3Model(nn.Module):
             from libra_b200.models.moe import moe_mlp
 
             return moe_mlp(h, x, p[pre + "router"], p[pre + "experts.w1"], p[pre + "experts.w2"], cfg)
-        a = ops.linear_swiglu(self._tp_in(h), p[pre + "gate_up_proj"])
+        if self.sp:
+            from libra_b200.parallel.sequence_parallel import sp_gather
+
+            a = ops.linear_swiglu(sp_gather(h, self.tp_group), p[pre + "gate_up_proj"])
+        else:
+            a = ops.linear_swiglu(self._tp_in(h), p[pre + "gate_up_proj"])
         return self._row_parallel(a, p[pre + "down_proj"], x)
 
     def _tp_in(self, h):
@@ -374,6 +399,10 @@ class Qwen3Model(nn.Module):
     def _row_parallel(self, a, w, residual):
         if self.tp_size == 1:
             return ops.linear(a, w, residual=residual)
+        if self.sp:
+            from libra_b200.parallel.sequence_parallel import sp_row_parallel_linear
+
+            return sp_row_parallel_linear(a, w, residual, self.tp_group)
         from libra_b200.parallel.tensor_parallel import row_parallel_linear
 
         return row_parallel_linear(a, w, residual, self.tp_group)
@@ -392,14 +421,32 @@ class Qwen3Model(nn.Module):
         return vocab_parallel_embedding(tokens, w, self.tp_group, self.tp_rank)
 
     def hidden_states(self, batch: PackedBatch) -> torch.Tensor:
-        x = self.embed(batch.tokens)
+        if self.sp:
+            from libra_b200.parallel.sequence_parallel import sp_scatter
+            from libra_b200.parallel.tensor_parallel import vocab_parallel_embedding
+
+            if batch.num_tokens % self.tp_size:
+                raise ValueError(f"sequence parallelism needs a token count divisible by tp={self.tp_size} "
+                                 f"(pack with pad_multiple); got {batch.num_tokens}")
+            # per-rank partial embedding (its vocab shard), reduce-scattered into this rank's token rows
+            x = sp_scatter(vocab_parallel_embedding(batch.tokens, self.p["embed_tokens"], self.tp_group,
+                                                    self.tp_rank, reduce=False), self.tp_group)
+        else:
+            x = self.embed(batch.tokens)
         for i in range(self.cfg.num_hidden_layers):
             if self.recompute and torch.is_grad_enabled():
                 x = torch.utils.checkpoint.checkpoint(self._layer, i, x, batch.positions, batch.cu_seqlens,
                                                       batch.max_seqlen, batch.tiles, use_reentrant=False)
             else:
                 x = self._layer(i, x, batch.positions, batch.cu_seqlens, batch.max_seqlen, batch.tiles)
-        return ops.rmsnorm(x, self.p["norm"], self.cfg.rms_norm_eps)
+        h = ops.rmsnorm(x, self.p["norm"], self.cfg.rms_norm_eps)
+        if self.sp:
+            from libra_b200.parallel.sequence_parallel import sp_gather_to_replicated
+
+            # every rank scores its vocab shard for all rows; the vocab-parallel logprob hands back the
+            # complete row gradient on every rank
+            h = sp_gather_to_replicated(h, self.tp_group)
+        return h
 
     @property
     def lm_head_weight(self):

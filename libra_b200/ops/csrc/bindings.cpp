@@ -35,6 +35,9 @@ void adamw_step_allgather(torch::Tensor master, torch::Tensor grad, torch::Tenso
                           c10::optional<torch::Tensor> sq_norm, double max_norm, double grad_scale,
                           std::vector<int64_t> param_peers, std::vector<int64_t> flag_peers, int64_t me, int64_t epoch,
                           torch::Tensor err, int64_t grid_ctas);
+void grad_reduce_scatter_peer(torch::Tensor out, double scale, c10::optional<torch::Tensor> sq_out,
+                              std::vector<int64_t> src_peers, std::vector<int64_t> flag_peers, int64_t me,
+                              int64_t epoch, torch::Tensor err, int64_t grid_ctas);
 torch::Tensor paged_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                                      torch::Tensor block_tables, torch::Tensor seq_lens, int64_t max_len,
                                      double scale);
@@ -135,6 +138,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &libra::adamw_step);
   m.def("adamw_step_allgather", &libra::adamw_step_allgather,
         "AdamW on this rank's shard with the bf16 result stored into every rank's parameter buffer");
+  m.def("grad_reduce_scatter_peer", &libra::grad_reduce_scatter_peer,
+        "distributed-optimizer gradient reduce-scatter over peer memory, fused with 1/dp scaling and the global "
+        "sum of squares");
   m.def("paged_decode_attention", &libra::paged_decode_attention);
   m.def("weight_reshard", &libra::reshard::weight_reshard,
         "trainer -> rollout weight sync: planned 2-D copies (peer sources over NVLink, fp32/bf16 -> bf16)");

@@ -92,14 +92,14 @@ def row_parallel_linear_allreduce(a, w_local, residual, group):
 
 class _VocabParallelEmbedding(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, tokens, w_local, group, rank):
+    def forward(ctx, tokens, w_local, group, rank, reduce=True):
         V_l = w_local.shape[0]
         lo = rank * V_l
         local = (tokens >= lo) & (tokens < lo + V_l)
         idx = torch.where(local, tokens - lo, torch.zeros_like(tokens))
         out = w_local.index_select(0, idx) * local.unsqueeze(-1).to(w_local.dtype)
         out = out.contiguous()
-        if _ws(group) > 1:
+        if reduce and _ws(group) > 1:
             dist.all_reduce(out, group=group)
         ctx.save_for_backward(idx, local)
         ctx.wref = w_local
@@ -113,14 +113,16 @@ class _VocabParallelEmbedding(torch.autograd.Function):
         main = getattr(w, "main_grad", None)
         if main is not None:
             main.index_add_(0, idx, gl)
-            return None, None, None, None
+            return None, None, None, None, None
         out = torch.zeros(w.shape, dtype=torch.float32, device=w.device)
         out.index_add_(0, idx, gl)
-        return None, out.to(w.dtype), None, None
+        return None, out.to(w.dtype), None, None, None
 
 
-def vocab_parallel_embedding(tokens, w_local, group, rank):
-    return _VocabParallelEmbedding.apply(tokens, w_local, group, rank)
+def vocab_parallel_embedding(tokens, w_local, group, rank, reduce: bool = True):
+    """Embedding rows of this rank's vocab shard (zero elsewhere), summed over
+    the group (``reduce``) or left partial for a reduce-scatter."""
+    return _VocabParallelEmbedding.apply(tokens, w_local, group, rank, reduce)
 
 
 def _combine(stats_m, stats_s, zt, group):
@@ -266,7 +268,12 @@ def shard_full_params(full: dict, cfg, tp_size: int, tp_rank: int) -> dict:
     return {k: v.contiguous() for k, v in out.items()}
 
 
-def tp_partial_grad_params(names) -> list:
-    """Replicated parameters whose gradient differs per TP rank (applied to
-    local heads only) and must be all-reduced over the TP group."""
-    return [n for n in names if n.endswith("q_norm") or n.endswith("k_norm")]
+def tp_partial_grad_params(names, sequence_parallel: bool = False) -> list:
+    """Replicated parameters whose gradient differs per TP rank and must be
+    all-reduced over the TP group: the per-head q/k norms (local heads only)
+    and, with sequence parallelism, every RMSNorm weight of the residual stream
+    (local token rows only)."""
+    out = [n for n in names if n.endswith("q_norm") or n.endswith("k_norm")]
+    if sequence_parallel:
+        out += [n for n in names if n == "norm" or n.endswith("layernorm")]
+    return out

@@ -45,11 +45,11 @@ def _model_inputs(cfg_name="tiny"):
     return cfg, {k: v.clone() for k, v in views.items()}, pack_sequences(seqs)
 
 
-def _run_model(cfg, params, batch, tp_group=None, tp_size=1, tp_rank=0):
+def _run_model(cfg, params, batch, tp_group=None, tp_size=1, tp_rank=0, sp=False):
     from libra_b200.models.qwen3 import Qwen3Model
 
     ps = {k: torch.nn.Parameter(v.clone()) for k, v in params.items()}
-    m = Qwen3Model(cfg, ps, tp_group=tp_group, tp_size=tp_size, tp_rank=tp_rank)
+    m = Qwen3Model(cfg, ps, tp_group=tp_group, tp_size=tp_size, tp_rank=tp_rank, sequence_parallel=sp)
     lp = m.action_logprobs(batch)
     w = torch.linspace(0.5, 1.5, lp.numel())
     (lp * w).sum().backward()
@@ -71,6 +71,31 @@ def _tp_worker(rank, world, port, out_dir):
     for n, gr in grads.items():
         torch.testing.assert_close(gr, ref_local[n], rtol=1e-3, atol=1e-4, msg=n)
     open(os.path.join(out_dir, f"tp_ok_{rank}"), "w").close()
+    dist.destroy_process_group()
+
+
+def _sp_worker(rank, world, port, out_dir):
+    """Tensor + sequence parallelism: residual stream split over tokens, all-gather before the
+    column-parallel linears, reduce-scatter after the row-parallel ones."""
+    _init(rank, world, port)
+    from libra_b200.models.qwen3 import pack_sequences
+    from libra_b200.parallel.tensor_parallel import shard_full_params, tp_partial_grad_params
+
+    cfg, full, _ = _model_inputs()
+    g = torch.Generator().manual_seed(0)
+    seqs = [torch.randint(4, cfg.vocab_size, (n,), generator=g) for n in (9, 14, 6)]  # 29 tokens: padded to 30
+    batch = pack_sequences(seqs, pad_multiple=world)
+    assert batch.num_tokens == 30 and int(batch.action_rows.max()) < 29
+    ref_lp, ref_g = _run_model(cfg, full, pack_sequences(seqs))
+    local = shard_full_params(full, cfg, world, rank)
+    lp, grads = _run_model(cfg, local, batch, dist.group.WORLD, world, rank, sp=True)
+    for n in tp_partial_grad_params(list(grads), sequence_parallel=True):
+        dist.all_reduce(grads[n])
+    torch.testing.assert_close(lp, ref_lp, rtol=1e-4, atol=1e-4)
+    ref_local = shard_full_params(ref_g, cfg, world, rank)
+    for n, gr in grads.items():
+        torch.testing.assert_close(gr, ref_local[n], rtol=1e-3, atol=1e-4, msg=n)
+    open(os.path.join(out_dir, f"sp_ok_{rank}"), "w").close()
     dist.destroy_process_group()
 
 
@@ -132,7 +157,8 @@ def _ep_worker(rank, world, port, out_dir):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("kind,fn", [("tp", _tp_worker), ("pp", _pp_worker), ("ep", _ep_worker)])
+@pytest.mark.parametrize("kind,fn", [("tp", _tp_worker), ("sp", _sp_worker), ("pp", _pp_worker),
+                                     ("ep", _ep_worker)])
 def test_parallel_equivalence(tmp_path, kind, fn):
     _spawn(fn, 2, str(tmp_path))
     assert {p.name for p in tmp_path.iterdir()} == {f"{kind}_ok_0", f"{kind}_ok_1"}
@@ -151,13 +177,15 @@ def test_mesh_layout():
         ParallelMesh(8, tp=3)
 
 
-def _tp_engine_worker(rank, world, port, out_dir):
+def _tp_engine_worker(rank, world, port, out_dir, sp=False):
     _init(rank, world, port)
     from libra_b200.engine.train_engine import B200TrainEngine
     from libra_b200.workflow.synthetic import GRPOWorkload, LengthDist
 
-    eng = B200TrainEngine("tiny", device="cpu", tp_size=2, learning_rate=1e-3, use_distributed_optimizer=False)
+    eng = B200TrainEngine("tiny", device="cpu", tp_size=2, learning_rate=1e-3, use_distributed_optimizer=False,
+                          sequence_parallel=sp)
     eng.initialize()
+    assert eng.model.sp == sp
     wl = GRPOWorkload("t", vocab_size=eng.cfg.vocab_size, prompts_per_step=2, group_size=4,
                       prompt=LengthDist(12, 0.3, 4, 24), response=LengthDist(16, 0.3, 2, 32))
     trajs = wl.trajectories(0)
@@ -174,8 +202,9 @@ def _tp_engine_worker(rank, world, port, out_dir):
     dist.destroy_process_group()
 
 
-def test_tp_engine_keeps_replicated_params_in_sync(tmp_path):
-    _spawn(_tp_engine_worker, 2, str(tmp_path))
+@pytest.mark.parametrize("sp", [False, True])
+def test_tp_engine_keeps_replicated_params_in_sync(tmp_path, sp):
+    _spawn(_tp_engine_worker, 2, str(tmp_path), sp)
     assert {p.name for p in tmp_path.iterdir()} == {"tpe_ok_0", "tpe_ok_1"}
 
 

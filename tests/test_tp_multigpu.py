@@ -62,6 +62,7 @@ def _worker(rank, world, port, out_dir):
     greedy = SamplingParams(max_tokens=8, temperature=0.0)
     ref_out = LLMEngine(cfg, full, kv_blocks=256).generate_sync(prompts, greedy)
     eng = LLMEngine(cfg, local, kv_blocks=256, tp_group=dist.group.WORLD, tp_size=world, tp_channel=chan)
+    assert eng.runner.peer_ar is not None  # row-parallel outputs reduced over peer memory (+ residual + RMSNorm)
     if rank == 0:
         out = eng.generate_sync(prompts, greedy)
         eng.shutdown()

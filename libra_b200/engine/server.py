@@ -169,10 +169,14 @@ def main(argv=None) -> None:
         import torch.distributed as dist
 
         local = int(os.environ.get("LOCAL_RANK", "0"))
-        torch.cuda.set_device(local)
-        device = f"cuda:{local}"
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=torch.device("cuda", local))
+        if a.device == "cpu" or not torch.cuda.is_available():  # CPU ranks (tests): gloo, fp32 reference ops
+            device = "cpu"
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+        else:
+            torch.cuda.set_device(local)
+            device = f"cuda:{local}"
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                    device_id=torch.device("cuda", local))
         if dist.get_world_size() != a.tp:
             raise SystemExit(f"--tp {a.tp} needs exactly {a.tp} processes, got {dist.get_world_size()}")
         rank, tp_group = dist.get_rank(), dist.group.WORLD

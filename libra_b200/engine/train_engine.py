@@ -594,7 +594,8 @@ class B200TrainEngine:
         into AdamW) over NVLink peer memory instead of NCCL."""
         from libra_b200.parallel.peer_grad_reduce import PeerGradReduce
 
-        self._peer_grad = PeerGradReduce(self.dp_group, self.flat_grad, self.shard_start, self.shard_numel)
+        group = self.dp_group if self.dp_group is not None else dist.group.WORLD
+        self._peer_grad = PeerGradReduce(group, self.flat_grad, self.shard_start, self.shard_numel)
         self.enable_fused_param_gather()
 
     def close_peer_data_parallel(self) -> None:
@@ -615,7 +616,8 @@ class B200TrainEngine:
             return False
         from libra_b200.parallel.peer_param_gather import PeerParamGather
 
-        self._peer_param_gather = PeerParamGather(self.dp_group, self.flat_param, self.shard_start, self.shard_numel)
+        group = self.dp_group if self.dp_group is not None else dist.group.WORLD
+        self._peer_param_gather = PeerParamGather(group, self.flat_param, self.shard_start, self.shard_numel)
         return True
 
     def _reduce_stats(self, stats: Dict[str, float]) -> Dict[str, float]:

@@ -68,9 +68,11 @@ class PeerGradReduce:
 
         if flat_grad.dtype != torch.float32 or not flat_grad.is_cuda or not flat_grad.is_contiguous():
             raise ValueError("flat_grad must be a contiguous fp32 CUDA tensor")
+        if group is None and dist.is_initialized():
+            group = dist.group.WORLD  # torch.distributed's meaning of "no group"
         self.group = group
-        self.n = dist.get_world_size(group) if dist.is_initialized() and group is not None else 1
-        self.me = dist.get_rank(group) if dist.is_initialized() and group is not None else 0
+        self.n = dist.get_world_size(group) if group is not None else 1
+        self.me = dist.get_rank(group) if group is not None else 0
         if self.n > MAX_RANKS:
             raise ValueError(f"at most {MAX_RANKS} ranks")
         if shard_start % 4 or shard_numel % 4:

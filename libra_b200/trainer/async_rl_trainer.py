@@ -88,6 +88,7 @@ class AsyncRLTrainer:
         self.train_engine = train_engine
         self.rollout_engine = rollout_engine
         self._local_engines: List[Any] = []
+        self._tp_groups: List[Any] = []  # TP-k rollout buckets running as server process groups
         self.staleness_manager: Optional[StalenessManager] = None
         self.async_runner: Optional[AsyncTaskRunner] = None
         self.dispatcher: Optional[BatchTaskDispatcher] = None
@@ -149,12 +150,65 @@ class AsyncRLTrainer:
             raise RuntimeError("global_resource_planner.initial_allocation_strategy='grp' requires the GRP "
                                "preflight plan (PreflightPlanner) to be applied before training starts")
 
+    def _make_tp_bucket(self, inst) -> Any:
+        """A TP-k bucket (k > 1) as k server processes, one per GPU of ``inst.gpus``
+        (``engine/tp_bucket.py``), reached through the HTTP client; the trainer
+        syncs weights into it over NVLink (or from a checkpoint on CPU ranks)."""
+        from libra_b200.engine.tp_bucket import TPServerGroup
+
+        c = self.config
+        eng = self.train_engine
+        cuda = torch.cuda.is_available() and eng.device.type == "cuda"
+        log_dir = os.path.join(c.log_dir, "rollout_servers")
+        os.makedirs(log_dir, exist_ok=True)
+        name = getattr(inst, "instance_id", "") or f"tp{inst.tp}-" + "-".join(str(g) for g in inst.gpus)
+        group = TPServerGroup(os.path.basename(str(c.model_path)) or "qwen3-4b", int(inst.tp), list(inst.gpus),
+                              kv_memory_fraction=float(c.heterogeneous_rollout.gpu_memory_utilization) * 0.5,
+                              device="cuda" if cuda else "cpu", log_path=os.path.join(log_dir, f"{name}.log"),
+                              startup_timeout=float(c.heterogeneous_rollout.startup_timeout))
+        self._tp_groups.append(group)
+        return group.client(instance_id=name)
+
+    def _hetero_tp_buckets(self) -> bool:
+        """Whether the config starts TP-k server groups (same answer on every rank)."""
+        c = self.config
+        return (c.rollout_backend in ("native", "local") and bool(c.heterogeneous_rollout.enabled)
+                and any(int(getattr(i, "tp", 1) or 1) > 1 for i in c.heterogeneous_rollout.instances)
+                and os.environ.get("LIBRA_TP_BUCKET_PROCESSES", "1") != "0")
+
+    def _sync_tp_groups(self, version: int) -> None:
+        """Weight sync into the TP-k server groups.  Collective over the trainer
+        ranks (the peer request gathers every trainer TP rank's buffer handle;
+        the disk path writes a distributed checkpoint); rank 0, which owns the
+        rollout pool, posts it."""
+        if not self._hetero_tp_buckets():
+            return
+        eng = self.train_engine
+        timeout = float(self.config.rollout_weight_sync_timeout_s)
+        if eng.flat_param.is_cuda:
+            from libra_b200.infra.sync.peer_weight_sync import publish
+
+            req = publish(eng)
+            req["version"] = int(version)
+            for group in self._tp_groups:  # each server rank pulls its own TP slice over NVLink
+                group.reload_peer(req, timeout=timeout)
+        else:
+            from libra_b200.engine.checkpointing import DistributedCheckpointManager
+
+            vdir = DistributedCheckpointManager(self.config.sync_path).save(
+                eng, int(version), export_for_rollout=True, include_optimizer=False, export_only=True)
+            for group in self._tp_groups:
+                group.reload_disk(str(vdir), int(version), timeout=timeout)
+
     def _make_local_engine(self, inst) -> Any:
-        """In-process rollout instance on the first GPU of ``inst.gpus`` with its own weight copy."""
+        """In-process rollout instance on the first GPU of ``inst.gpus`` with its own weight copy;
+        TP-k instances (k > 1) become server groups (``_make_tp_bucket``)."""
         from libra_b200.engine.rollout.llm_engine import LLMEngine
         from libra_b200.engine.rollout_engine import LocalRolloutEngine
         from libra_b200.engine.tokenizer import load_tokenizer
 
+        if int(getattr(inst, "tp", 1) or 1) > 1 and os.environ.get("LIBRA_TP_BUCKET_PROCESSES", "1") != "0":
+            return self._make_tp_bucket(inst)
         eng = self.train_engine
         if torch.cuda.is_available() and getattr(inst, "gpus", None):
             dev = torch.device("cuda", int(inst.gpus[0]) % torch.cuda.device_count())
@@ -241,6 +295,8 @@ class AsyncRLTrainer:
         self.train_engine.set_version(self.initial_model_version)
         if self.rollout_engine is None:
             self._build_rollout_engine()
+            # TP-k server groups start from their own initialisation: give them the trainer's weights
+            self._sync_tp_groups(self.initial_model_version)
         else:
             from libra_b200.engine.rollout_engine import LocalRolloutEngine
 
@@ -395,9 +451,10 @@ class AsyncRLTrainer:
                 else:
                     src = src or {k: v.detach() for k, v in self.train_engine.params.items()}
                     llm.update_weights(src, version=target_version)
-        elif self.config.rollout_backend not in ("mock",) and (
+        elif self.config.rollout_backend not in ("mock",) and not self._hetero_tp_buckets() and (
                 self.config.rollout_weight_sync_mode != "none" or self.config.require_rollout_weight_sync):
             self._sync_weights_disk(target_version)
+        self._sync_tp_groups(target_version)
         return time.perf_counter() - t0
 
     def _sync_weights_disk(self, version: int) -> None:
@@ -733,6 +790,9 @@ class AsyncRLTrainer:
             self.dispatcher = None
         for llm in self._local_engines:
             llm.shutdown()
+        for group in self._tp_groups:
+            group.close()
+        self._tp_groups = []
         if self._grp_pool is not None:
             self._grp_pool.shutdown(wait=False)
         if self.history_collector is not None:

@@ -134,6 +134,8 @@ def _engine_worker(rank, world, port, out_dir):
         eng.initialize()
         assert (eng._peer_grad is not None) == (mode == "1")
         assert (getattr(eng, "_peer_param_gather", None) is not None) == (mode == "1")
+        if mode == "1":
+            assert eng._peer_grad.n == world and eng._peer_param_gather.n == world
         engines[mode] = eng
     wl = GRPOWorkload("peer-dp", vocab_size=engines["1"].cfg.vocab_size, prompts_per_step=2, group_size=4,
                       prompt=LengthDist(48, 0.3, 16, 96), response=LengthDist(64, 0.3, 8, 128))

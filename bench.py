@@ -78,10 +78,16 @@ def barrier(world):
         dist.barrier()
 
 
+_RECORD_OUT = None  # the process's original stdout; fd 1 itself is pointed at stderr during the run
+
+
 def emit(rank, record):
-    # the record goes to the process's real stdout; everything else printed during the run goes to stderr
+    # the record goes to the process's real stdout; everything else printed during the run, including
+    # native libraries writing to fd 1 (NCCL's version banner), goes to stderr
     if rank == 0:
-        print(json.dumps(record), file=sys.__stdout__, flush=True)
+        out = _RECORD_OUT or sys.__stdout__
+        out.write(json.dumps(record) + "\n")
+        out.flush()
 
 
 def base_record(args, world, impl):
@@ -619,9 +625,14 @@ def run_reference_grpo(args, rank, world, local):
 def main():
     import contextlib
 
+    global _RECORD_OUT
     args = parse_args()
+    sys.stdout.flush()
+    _RECORD_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)  # native writes to fd 1 land on stderr
     with contextlib.redirect_stdout(sys.stderr):  # stdout carries the one JSON record (emit) and nothing else
         _main(args)
+    _RECORD_OUT.flush()
 
 
 def _main(args):

@@ -708,8 +708,9 @@ class AsyncRLConfig:
                    "exchanged inside the data-parallel group)")
         yield (0.0 <= self.megatron_optimizer_offload_fraction <= 1.0,
                "megatron_optimizer_offload_fraction must lie in [0, 1]")
-        yield (not self.megatron_optimizer_cpu_offload and self.megatron_optimizer_offload_fraction == 0.0,
-               "optimizer CPU offload is not used: the optimizer state stays in HBM (180 GB per GPU)")
+        yield (self.megatron_optimizer_offload_fraction == 0.0 or self.megatron_optimizer_cpu_offload,
+               "megatron_optimizer_offload_fraction > 0 moves part of the optimizer state to the host: it needs "
+               "megatron_optimizer_cpu_offload=true")
         yield (self.megatron_checkpoint_format == "torch_dist",
                f"megatron_checkpoint_format={self.megatron_checkpoint_format!r}: checkpoints are written as "
                "torch_dist (DCP) directories")

@@ -248,9 +248,10 @@ class DistributedCheckpointManager:
             if include_optimizer and getattr(engine, "master", None) is not None:
                 r = engine.get_data_parallel_rank() if engine.sharded else 0
                 if engine.sharded or _rank() == 0:
-                    sd[f"optimizer.shard_{r}.master"] = engine.master
-                    sd[f"optimizer.shard_{r}.exp_avg"] = engine.exp_avg
-                    sd[f"optimizer.shard_{r}.exp_avg_sq"] = engine.exp_avg_sq
+                    state = engine.optimizer_state_tensors() if hasattr(engine, "optimizer_state_tensors") else \
+                        {"master": engine.master, "exp_avg": engine.exp_avg, "exp_avg_sq": engine.exp_avg_sq}
+                    for n, t in state.items():
+                        sd[f"optimizer.shard_{r}.{n}"] = t
                 sd["optimizer.step"] = torch.tensor(engine.step_count)
             self._progress(vdir, version, "before_dist_checkpoint_save")
             dcp.save(sd, checkpoint_id=str(ddir))
@@ -294,11 +295,17 @@ class DistributedCheckpointManager:
         tmpl: Dict[str, Any] = {f"model.{k}": v.clone() for k, v in to_mcore(params, cfg).items()}
         if load_optimizer and getattr(engine, "master", None) is not None:
             r = engine.get_data_parallel_rank() if engine.sharded else 0
-            tmpl[f"optimizer.shard_{r}.master"] = engine.master
-            tmpl[f"optimizer.shard_{r}.exp_avg"] = engine.exp_avg
-            tmpl[f"optimizer.shard_{r}.exp_avg_sq"] = engine.exp_avg_sq
+            split = bool(getattr(engine, "_offload_k", 0))
+            state = engine.optimizer_state_tensors() if split else \
+                {"master": engine.master, "exp_avg": engine.exp_avg, "exp_avg_sq": engine.exp_avg_sq}
+            for n, t in state.items():
+                tmpl[f"optimizer.shard_{r}.{n}"] = t
             tmpl["optimizer.step"] = torch.tensor(0)
         dcp.load(tmpl, checkpoint_id=str(vdir / "megatron_dist"))
+        if load_optimizer and getattr(engine, "_offload_k", 0):
+            r = engine.get_data_parallel_rank() if engine.sharded else 0
+            engine.load_optimizer_state_tensors({n: tmpl[f"optimizer.shard_{r}.{n}"]
+                                                 for n in ("master", "exp_avg", "exp_avg_sq")})
         from_mcore({k[len("model."):]: v for k, v in tmpl.items() if k.startswith("model.")}, params, cfg)
         if "optimizer.step" in tmpl:
             engine.step_count = int(tmpl["optimizer.step"])

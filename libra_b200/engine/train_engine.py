@@ -71,6 +71,7 @@ class B200TrainEngine:
 
     train_backend = "b200"
     _peer_grad = None      # PeerGradReduce when the DP exchange runs over peer memory
+    _offload_k = 0         # elements of the dense optimizer shard stepped on the host
     _sq_ready = False      # the reduce left the global squared gradient norm in sq_norm
 
     def __init__(self, model: Any = "qwen3-4b", learning_rate: float = 1e-6, kl_coef: float = 0.001,
@@ -79,7 +80,8 @@ class B200TrainEngine:
                  use_distributed_optimizer: bool = True, dp_group=None, temperature: float = 1.0,
                  max_grad_norm: float = 1.0, tp_size: int = 1, model_path: str = "",
                  max_tokens_per_micro_batch: int = 16384, max_tokens_per_recompute_batch: int = 65536,
-                 ep_size: int = 1, sequence_parallel: bool = False):
+                 ep_size: int = 1, sequence_parallel: bool = False, precision_aware_optimizer: bool = False,
+                 optimizer_cpu_offload: bool = False, optimizer_offload_fraction: float = 0.0):
         self.cfg: Qwen3Config = get_config(model)
         self.model_path = model_path
         self.optim = OptimConfig(lr=learning_rate, max_grad_norm=max_grad_norm)
@@ -95,6 +97,15 @@ class B200TrainEngine:
         self.temperature = temperature
         self.tp_size = tp_size
         self.sequence_parallel = bool(sequence_parallel) and tp_size > 1
+        # precision-aware optimizer (MCore use_precision_aware_optimizer): Adam moments stored in bf16
+        # (updated in fp32 inside the kernel), fp32 master weights; 8 instead of 12 bytes per parameter
+        self.precision_aware_optimizer = bool(precision_aware_optimizer)
+        # optimizer CPU offload: this fraction of the dense optimizer shard keeps its master weights and
+        # moments in host memory (pinned on GPU engines) and is stepped on the CPU
+        frac = float(optimizer_offload_fraction) if optimizer_cpu_offload else 0.0
+        if not 0.0 <= frac <= 1.0:
+            raise ValueError("optimizer_offload_fraction must lie in [0, 1]")
+        self.optimizer_offload_fraction = frac
         self.ep_size = max(1, int(ep_size))
         if self.ep_size > 1 and not self.cfg.is_moe:
             raise ValueError(f"ep_size={self.ep_size} needs a mixture-of-experts model")
@@ -177,9 +188,22 @@ class B200TrainEngine:
         shard = self.dense_numel // self.dp_size if self.sharded else self.dense_numel
         self.shard_numel = shard
         self.shard_start = self.dp_rank * shard if self.sharded else 0
-        self.master = self.flat_param[self.shard_start:self.shard_start + shard].float().clone()
-        self.exp_avg = torch.zeros_like(self.master)
-        self.exp_avg_sq = torch.zeros_like(self.master)
+        mdt = torch.bfloat16 if self.precision_aware_optimizer else torch.float32
+        # offloaded prefix [0, k) of the shard lives on the host; the device keeps [k, shard)
+        k = int(shard * self.optimizer_offload_fraction) // 4 * 4
+        self._offload_k = k
+        src = self.flat_param[self.shard_start:self.shard_start + shard]
+        self.master = src[k:].float().clone()
+        self.exp_avg = torch.zeros(self.master.shape, dtype=mdt, device=dev)
+        self.exp_avg_sq = torch.zeros(self.master.shape, dtype=mdt, device=dev)
+        self._host_opt = None
+        if k:
+            pin = dict(pin_memory=dev.type == "cuda")
+            host_master = src[:k].float().cpu()
+            self._host_opt = {"master": host_master.pin_memory() if dev.type == "cuda" else host_master.clone(),
+                              "exp_avg": torch.zeros(k, dtype=mdt, **pin), "exp_avg_sq": torch.zeros(k, dtype=mdt, **pin),
+                              "grad": torch.zeros(k, dtype=torch.float32, **pin),
+                              "param": torch.zeros(k, dtype=torch.bfloat16, **pin)}
         self.grad_shard = (torch.zeros(shard, dtype=torch.float32, device=dev) if self.sharded
                            else self.flat_grad[:self.dense_numel])
         self.sq_norm = torch.zeros(1, dtype=torch.float32, device=dev)
@@ -563,6 +587,9 @@ class B200TrainEngine:
                            beta1=o.betas[0], beta2=o.betas[1], eps=o.eps, weight_decay=o.weight_decay,
                            step=self.step_count, max_grad_norm=o.max_grad_norm, sq_norm=self.sq_norm)
         shard_param = self.flat_param[self.shard_start:self.shard_start + self.shard_numel]
+        if self._offload_k:
+            self._offloaded_step(shard_param)
+            return
         peer = getattr(self, "_peer_param_gather", None)
         if peer is not None:  # AdamW stores the new bf16 shard straight into every rank's parameters
             peer.step(self.master, self.grad_shard, self.exp_avg, self.exp_avg_sq, lr=o.lr, beta1=o.betas[0],
@@ -574,6 +601,48 @@ class B200TrainEngine:
                        step=self.step_count, max_grad_norm=o.max_grad_norm, sq_norm=self.sq_norm)
         if self.sharded:
             self._gather_params(shard_param)
+
+    def _offloaded_step(self, shard_param: torch.Tensor) -> None:
+        """AdamW with the optimizer state split between host and device: the
+        device part runs as a kernel while the host steps its prefix (fp32
+        math with torch's CPU kernels); the host result goes back with one
+        pinned copy, then the data-parallel gather completes the parameters."""
+        o, k, h = self.optim, self._offload_k, self._host_opt
+        hp = dict(lr=o.lr, beta1=o.betas[0], beta2=o.betas[1], eps=o.eps, weight_decay=o.weight_decay,
+                  step=self.step_count, max_grad_norm=o.max_grad_norm)
+        cuda = self.device.type == "cuda"
+        h["grad"].copy_(self.grad_shard[:k], non_blocking=cuda)
+        sq_host = self.sq_norm.to("cpu", non_blocking=cuda)
+        done = torch.cuda.Event() if cuda else None
+        if cuda:
+            done.record()
+        if self.master.numel():
+            ops.adamw_step(self.master, self.grad_shard[k:], self.exp_avg, self.exp_avg_sq, shard_param[k:],
+                           sq_norm=self.sq_norm, **hp)
+        if cuda:
+            done.synchronize()
+        ops.adamw_step(h["master"], h["grad"], h["exp_avg"], h["exp_avg_sq"], h["param"], sq_norm=sq_host, **hp)
+        shard_param[:k].copy_(h["param"], non_blocking=cuda)
+        self.io_bytes["d2h"] += 4 * k + 4
+        self.io_bytes["h2d"] += 2 * k
+        if self.sharded:
+            self._gather_params(shard_param)
+
+    def optimizer_state_tensors(self) -> Dict[str, torch.Tensor]:
+        """Full-shard master weights and moments (host and device parts joined
+        on the host when part of the state is offloaded)."""
+        names = ("master", "exp_avg", "exp_avg_sq")
+        if not self._offload_k:
+            return {n: getattr(self, n) for n in names}
+        return {n: torch.cat([self._host_opt[n], getattr(self, n).cpu()]) for n in names}
+
+    def load_optimizer_state_tensors(self, state: Dict[str, torch.Tensor]) -> None:
+        k = self._offload_k
+        for n in ("master", "exp_avg", "exp_avg_sq"):
+            t = state[n]
+            if k:
+                self._host_opt[n].copy_(t[:k])
+            getattr(self, n).copy_(t[k:])
 
     def _peer_dp_applies(self) -> bool:
         """Whether the data-parallel gradient and parameter exchange runs over
@@ -596,7 +665,8 @@ class B200TrainEngine:
 
         group = self.dp_group if self.dp_group is not None else dist.group.WORLD
         self._peer_grad = PeerGradReduce(group, self.flat_grad, self.shard_start, self.shard_numel)
-        self.enable_fused_param_gather()
+        if not self._offload_k:  # with part of the state on the host the gather runs after both halves
+            self.enable_fused_param_gather()
 
     def close_peer_data_parallel(self) -> None:
         for attr in ("_peer_grad", "_peer_param_gather"):
@@ -635,6 +705,7 @@ class B200TrainEngine:
         """Drop master/Adam/gradient buffers (inference-only holders of the weights)."""
         self.close_peer_data_parallel()
         self.master = self.exp_avg = self.exp_avg_sq = None
+        self._host_opt, self._offload_k = None, 0
         self.grad_shard = None
         self.flat_grad = torch.zeros(0, dtype=torch.float32, device=self.device)
         for p in self.params.values():
@@ -857,4 +928,9 @@ def create_train_engine(config) -> B200TrainEngine:
                            temperature=config.temperature, model_path=config.model_path,
                            tp_size=int(getattr(config, "train_tp_size", 1) or 1),
                            ep_size=int(getattr(config, "train_ep_size", 1) or 1),
-                           sequence_parallel=bool(getattr(config, "sequence_parallel", False)))
+                           sequence_parallel=bool(getattr(config, "sequence_parallel", False)),
+                           precision_aware_optimizer=bool(getattr(config, "megatron_use_precision_aware_optimizer",
+                                                                  False)),
+                           optimizer_cpu_offload=bool(getattr(config, "megatron_optimizer_cpu_offload", False)),
+                           optimizer_offload_fraction=float(getattr(config, "megatron_optimizer_offload_fraction",
+                                                                    0.0)))

@@ -649,14 +649,17 @@ def adamw_step(master, grad, exp_avg, exp_avg_sq, param_bf16, *, lr, beta1, beta
                max_grad_norm=0.0, sq_norm=None, grad_scale=1.0):
     """One AdamW update over flat fp32 buffers, writing the bf16 copy too."""
     if master.device.type != "cuda":
-        g = grad * grad_scale
+        # fp32 math whatever the moment dtype (bf16 moments are rounded once, on the store)
+        g = grad.float() * grad_scale
         if max_grad_norm > 0:
-            total = g.norm() if sq_norm is None else sq_norm.sqrt() * grad_scale
+            total = g.norm() if sq_norm is None else sq_norm.float().sqrt() * grad_scale
             g = g * torch.clamp(max_grad_norm / (total + 1e-6), max=1.0)
-        exp_avg.mul_(beta1).add_(g, alpha=1 - beta1)
-        exp_avg_sq.mul_(beta2).addcmul_(g, g, value=1 - beta2)
+        m = exp_avg.float().mul_(beta1).add_(g, alpha=1 - beta1)
+        v = exp_avg_sq.float().mul_(beta2).addcmul_(g, g, value=1 - beta2)
         bc1, bc2 = 1 - beta1 ** step, 1 - beta2 ** step
-        master.sub_(lr * ((exp_avg / bc1) / ((exp_avg_sq / bc2).sqrt() + eps) + weight_decay * master))
+        master.sub_(lr * ((m / bc1) / ((v / bc2).sqrt() + eps) + weight_decay * master))
+        exp_avg.copy_(m)
+        exp_avg_sq.copy_(v)
         param_bf16.copy_(master)
         return
     ext().adamw_step(master, grad, exp_avg, exp_avg_sq, param_bf16, lr, beta1, beta2, eps, weight_decay, step,

@@ -235,9 +235,30 @@ struct AdamPeers {
   int* err;
 };
 
-template <bool kPeer>
-__global__ void adamw_kernel(float* __restrict__ master, const float* __restrict__ grad, float* __restrict__ m,
-                             float* __restrict__ v, __nv_bfloat16* __restrict__ param, int64_t n, float lr, float beta1,
+// Adam moments in fp32, or in bf16 for the precision-aware optimizer (computed in fp32, stored rounded
+// to nearest even): four consecutive moments per thread either way.
+__device__ __forceinline__ float4 load_moment4(const float* p, int64_t i) { return reinterpret_cast<const float4*>(p)[i]; }
+__device__ __forceinline__ float4 load_moment4(const __nv_bfloat16* p, int64_t i) {
+  const uint2 u = reinterpret_cast<const uint2*>(p)[i];
+  const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&u.x);
+  const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
+  return make_float4(__low2float(a), __high2float(a), __low2float(b), __high2float(b));
+}
+__device__ __forceinline__ void store_moment4(float* p, int64_t i, float4 v) { reinterpret_cast<float4*>(p)[i] = v; }
+__device__ __forceinline__ void store_moment4(__nv_bfloat16* p, int64_t i, float4 v) {
+  uint2 u;
+  u.x = pack_bf16x2(v.x, v.y);
+  u.y = pack_bf16x2(v.z, v.w);
+  reinterpret_cast<uint2*>(p)[i] = u;
+}
+__device__ __forceinline__ float moment_at(const float* p, int64_t i) { return p[i]; }
+__device__ __forceinline__ float moment_at(const __nv_bfloat16* p, int64_t i) { return __bfloat162float(p[i]); }
+__device__ __forceinline__ void moment_set(float* p, int64_t i, float v) { p[i] = v; }
+__device__ __forceinline__ void moment_set(__nv_bfloat16* p, int64_t i, float v) { p[i] = __float2bfloat16(v); }
+
+template <bool kPeer, typename MT>
+__global__ void adamw_kernel(float* __restrict__ master, const float* __restrict__ grad, MT* __restrict__ m,
+                             MT* __restrict__ v, __nv_bfloat16* __restrict__ param, int64_t n, float lr, float beta1,
                              float beta2, float eps, float wd, float bc1, float bc2, const float* __restrict__ sq_norm,
                              float max_norm, float grad_scale, const AdamPeers peers) {
   float clip = grad_scale;
@@ -249,8 +270,8 @@ __global__ void adamw_kernel(float* __restrict__ master, const float* __restrict
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
     float4 p = reinterpret_cast<float4*>(master)[i];
     const float4 g4 = reinterpret_cast<const float4*>(grad)[i];
-    float4 m4 = reinterpret_cast<float4*>(m)[i];
-    float4 v4 = reinterpret_cast<float4*>(v)[i];
+    float4 m4 = load_moment4(m, i);
+    float4 v4 = load_moment4(v, i);
     float* pp = &p.x;
     const float* gg = &g4.x;
     float* mm = &m4.x;
@@ -264,8 +285,8 @@ __global__ void adamw_kernel(float* __restrict__ master, const float* __restrict
       pp[e] = pp[e] - lr * (mhat / (sqrtf(vhat) + eps) + wd * pp[e]);
     }
     reinterpret_cast<float4*>(master)[i] = p;
-    reinterpret_cast<float4*>(m)[i] = m4;
-    reinterpret_cast<float4*>(v)[i] = v4;
+    store_moment4(m, i, m4);
+    store_moment4(v, i, v4);
     uint2 pk;
     pk.x = pack_bf16x2(p.x, p.y);
     pk.y = pack_bf16x2(p.z, p.w);
@@ -277,9 +298,11 @@ __global__ void adamw_kernel(float* __restrict__ master, const float* __restrict
   }
   for (int64_t i = n4 * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const float g = grad[i] * clip;
-    m[i] = beta1 * m[i] + (1.f - beta1) * g;
-    v[i] = beta2 * v[i] + (1.f - beta2) * g * g;
-    master[i] -= lr * ((m[i] / bc1) / (sqrtf(v[i] / bc2) + eps) + wd * master[i]);
+    const float mi = beta1 * moment_at(m, i) + (1.f - beta1) * g;
+    const float vi = beta2 * moment_at(v, i) + (1.f - beta2) * g * g;
+    moment_set(m, i, mi);
+    moment_set(v, i, vi);
+    master[i] -= lr * ((mi / bc1) / (sqrtf(vi / bc2) + eps) + wd * master[i]);
     if constexpr (kPeer) {
       for (int r = 0; r < peers.n; ++r) reinterpret_cast<__nv_bfloat16*>(peers.param[r])[i] = __float2bfloat16(master[i]);
     } else {
@@ -383,9 +406,10 @@ void grad_sq_norm(torch::Tensor grad, torch::Tensor out) {
 void adamw_step(torch::Tensor master, torch::Tensor grad, torch::Tensor m, torch::Tensor v, torch::Tensor param,
                 double lr, double beta1, double beta2, double eps, double wd, int64_t step,
                 c10::optional<torch::Tensor> sq_norm, double max_norm, double grad_scale) {
-  LIBRA_CHECK(master.scalar_type() == at::kFloat && grad.scalar_type() == at::kFloat && m.scalar_type() == at::kFloat &&
-                  v.scalar_type() == at::kFloat && param.scalar_type() == at::kBFloat16,
-              "adamw_step: fp32 master/grad/m/v and bf16 param");
+  LIBRA_CHECK(master.scalar_type() == at::kFloat && grad.scalar_type() == at::kFloat &&
+                  param.scalar_type() == at::kBFloat16 && m.scalar_type() == v.scalar_type() &&
+                  (m.scalar_type() == at::kFloat || m.scalar_type() == at::kBFloat16),
+              "adamw_step: fp32 master/grad, fp32 or bf16 moments (both the same), bf16 param");
   const int64_t n = master.numel();
   LIBRA_CHECK(grad.numel() == n && m.numel() == n && v.numel() == n && param.numel() == n, "adamw_step: size mismatch");
   LIBRA_CHECK(master.is_contiguous() && grad.is_contiguous() && m.is_contiguous() && v.is_contiguous() &&
@@ -395,10 +419,17 @@ void adamw_step(torch::Tensor master, torch::Tensor grad, torch::Tensor m, torch
   if (n == 0) return;
   const float bc1 = (float)(1.0 - std::pow(beta1, (double)step));
   const float bc2 = (float)(1.0 - std::pow(beta2, (double)step));
-  adamw_kernel<false><<<sm_count() * 4, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
-      master.data_ptr<float>(), grad.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
-      (__nv_bfloat16*)param.data_ptr(), n, (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd, bc1, bc2,
-      sq_norm.has_value() ? sq_norm->data_ptr<float>() : nullptr, (float)max_norm, (float)grad_scale, AdamPeers{});
+  const float* sq = sq_norm.has_value() ? sq_norm->data_ptr<float>() : nullptr;
+  if (m.scalar_type() == at::kBFloat16)
+    adamw_kernel<false, __nv_bfloat16><<<sm_count() * 4, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
+        master.data_ptr<float>(), grad.data_ptr<float>(), (__nv_bfloat16*)m.data_ptr(), (__nv_bfloat16*)v.data_ptr(),
+        (__nv_bfloat16*)param.data_ptr(), n, (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd, bc1, bc2, sq,
+        (float)max_norm, (float)grad_scale, AdamPeers{});
+  else
+    adamw_kernel<false, float><<<sm_count() * 4, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
+        master.data_ptr<float>(), grad.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+        (__nv_bfloat16*)param.data_ptr(), n, (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd, bc1, bc2, sq,
+        (float)max_norm, (float)grad_scale, AdamPeers{});
   LIBRA_LAUNCH_CHECK();
 }
 
@@ -411,9 +442,10 @@ void adamw_step_allgather(torch::Tensor master, torch::Tensor grad, torch::Tenso
                           c10::optional<torch::Tensor> sq_norm, double max_norm, double grad_scale,
                           std::vector<int64_t> param_peers, std::vector<int64_t> flag_peers, int64_t me, int64_t epoch,
                           torch::Tensor err, int64_t grid_ctas) {
-  LIBRA_CHECK(master.scalar_type() == at::kFloat && grad.scalar_type() == at::kFloat && m.scalar_type() == at::kFloat &&
-                  v.scalar_type() == at::kFloat,
-              "adamw_step_allgather: fp32 master/grad/m/v");
+  LIBRA_CHECK(master.scalar_type() == at::kFloat && grad.scalar_type() == at::kFloat &&
+                  m.scalar_type() == v.scalar_type() &&
+                  (m.scalar_type() == at::kFloat || m.scalar_type() == at::kBFloat16),
+              "adamw_step_allgather: fp32 master/grad, fp32 or bf16 moments (both the same)");
   const int64_t n = master.numel();
   LIBRA_CHECK(grad.numel() == n && m.numel() == n && v.numel() == n, "adamw_step_allgather: size mismatch");
   LIBRA_CHECK(master.is_contiguous() && grad.is_contiguous() && m.is_contiguous() && v.is_contiguous(),
@@ -440,10 +472,17 @@ void adamw_step_allgather(torch::Tensor master, torch::Tensor grad, torch::Tenso
   const float bc1 = (float)(1.0 - std::pow(beta1, (double)step));
   const float bc2 = (float)(1.0 - std::pow(beta2, (double)step));
   // launched even for an empty shard: the peers wait for this rank's arrivals
-  adamw_kernel<true><<<grid, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
-      master.data_ptr<float>(), grad.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), nullptr, n,
-      (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd, bc1, bc2,
-      sq_norm.has_value() ? sq_norm->data_ptr<float>() : nullptr, (float)max_norm, (float)grad_scale, peers);
+  const float* sq = sq_norm.has_value() ? sq_norm->data_ptr<float>() : nullptr;
+  if (m.scalar_type() == at::kBFloat16)
+    adamw_kernel<true, __nv_bfloat16><<<grid, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
+        master.data_ptr<float>(), grad.data_ptr<float>(), (__nv_bfloat16*)m.data_ptr(), (__nv_bfloat16*)v.data_ptr(),
+        nullptr, n, (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd, bc1, bc2, sq, (float)max_norm,
+        (float)grad_scale, peers);
+  else
+    adamw_kernel<true, float><<<grid, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
+        master.data_ptr<float>(), grad.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), nullptr, n,
+        (float)lr, (float)beta1, (float)beta2, (float)eps, (float)wd, bc1, bc2, sq, (float)max_norm,
+        (float)grad_scale, peers);
   LIBRA_LAUNCH_CHECK();
 }
 

@@ -34,7 +34,7 @@ def test_numeric_string_coercion():
     ({"train_pp_size": 2}, "train_pp_size=2: the native engine keeps every layer"),
     ({"train_cp_size": 2, "train_gpus": 8}, "train_cp_size=2: sequences are not split"),
     ({"train_backend": "deepspeed"}, "train_backend"),
-    ({"megatron_optimizer_offload_fraction": 0.5}, "optimizer CPU offload"),
+    ({"megatron_optimizer_offload_fraction": 0.5}, "needs megatron_optimizer_cpu_offload=true"),
     ({"train_ep_size": 2, "train_gpus": 2}, "needs a mixture-of-experts model"),
     ({"train_tp_size": 3, "train_gpus": 3, "batch_size": 3, "micro_batch_size": 1}, "train_tp_size=3 must divide"),
 ])
@@ -77,6 +77,11 @@ def test_parallel_layout_reaches_the_engine():
     c14 = AsyncRLConfig.from_file(os.path.join(CFG_DIR, "qwen3_14b_agentic_tp4.yaml"))
     e14 = create_train_engine(c14)
     assert e14.tp_size == 4 and e14.ep_size == 1 and e14.cfg.hidden_size == 5120
+    assert e14.sequence_parallel  # base.yaml turns sequence parallelism on for TP > 1
+    c14.megatron_use_precision_aware_optimizer = True
+    c14.megatron_optimizer_cpu_offload, c14.megatron_optimizer_offload_fraction = True, 0.25
+    e14b = create_train_engine(c14)
+    assert e14b.precision_aware_optimizer and e14b.optimizer_offload_fraction == 0.25
     c30 = AsyncRLConfig.from_file(os.path.join(CFG_DIR, "qwen3_30b_a3b_ep8.yaml"))
     e30 = create_train_engine(c30)
     assert e30.tp_size == 1 and e30.ep_size == 8 and e30.cfg.num_experts == 128

@@ -207,6 +207,45 @@ def test_adamw_matches_reference():
     assert torch.allclose(p.float().cpu(), rp.float(), atol=1e-2)
 
 
+def test_adamw_bf16_moments_match_reference():
+    """Precision-aware optimizer state: bf16 moments updated in fp32 by the kernel (plain and
+    parameter-gather variants) against the fp32-math CPU reference with the same bf16 storage."""
+    from libra_b200 import ops
+    from libra_b200.parallel.peer_param_gather import PeerParamGather
+
+    n = 100_003
+    g = torch.Generator(device=DEV).manual_seed(4)
+    master0 = torch.randn(n, device=DEV, generator=g)
+    grad = torch.randn(n, device=DEV, generator=g)
+    sq = grad.pow(2).sum().reshape(1)
+    hp = dict(lr=1e-3, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.01, max_grad_norm=1.0)
+    rm, rmm, rv = master0.cpu(), torch.zeros(n, dtype=torch.bfloat16), torch.zeros(n, dtype=torch.bfloat16)
+    rp = torch.zeros(n, dtype=torch.bfloat16)
+    master, m = master0.clone(), torch.zeros(n, dtype=torch.bfloat16, device=DEV)
+    v, p = torch.zeros_like(m), torch.zeros(n, dtype=torch.bfloat16, device=DEV)
+    m2, v2, master2 = m.clone(), v.clone(), master0.clone()
+    for step in (1, 2, 3):
+        ops.adamw_step(master, grad, m, v, p, step=step, sq_norm=sq, **hp)
+        ops.adamw_step(rm, grad.cpu(), rmm, rv, rp, step=step, sq_norm=sq.cpu(), **hp)
+    torch.cuda.synchronize()
+    ops.check_kernel_errors()
+    assert m.dtype == torch.bfloat16
+    torch.testing.assert_close(master.cpu(), rm, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(m.float().cpu(), rmm.float(), rtol=1e-2, atol=1e-6)
+    torch.testing.assert_close(v.float().cpu(), rv.float(), rtol=1e-2, atol=1e-8)
+    # the fused parameter-gather variant with bf16 moments (one rank): same state, same parameters
+    k = n - n % 4
+    flat = torch.zeros(k, dtype=torch.bfloat16, device=DEV)
+    pg = PeerParamGather(None, flat, 0, k)
+    for step in (1, 2, 3):
+        pg.step(master2[:k], grad[:k], m2[:k], v2[:k], step=step, sq_norm=sq, **hp)
+    torch.cuda.synchronize()
+    ops.check_kernel_errors()
+    assert torch.equal(master2[:k], master[:k]) and torch.equal(m2[:k], m[:k]) and torch.equal(v2[:k], v[:k])
+    assert torch.equal(flat[:k], p[:k])
+    pg.close()
+
+
 # ---------------------------------------------------------------- model
 def test_model_matches_fp32_reference():
     """tiny-gpu model: CUDA kernels vs the same weights on the CPU fp32 path."""

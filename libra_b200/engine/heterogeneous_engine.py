@@ -39,6 +39,9 @@ class HeterogeneousRolloutEngine:
         self._rr = 0
         self._inflight = 0
         self._inflight_lock = threading.Lock()
+        # C-MLFQ requests: token context after their last turn (prompt + output), for KV migration
+        self._contexts: Dict[str, List[int]] = {}
+        self.kv_migrations = {"count": 0, "tokens": 0, "seconds": 0.0}
         for i, c in enumerate(self.instance_configs):
             scheduler.register_instance(i, c["instance_id"], int(c["tp_degree"]))
 
@@ -76,6 +79,10 @@ class HeterogeneousRolloutEngine:
             res = await engine.generate(prompt, max_new_tokens=max_new_tokens, temperature=temperature, top_p=top_p,
                                         n=n, input_tokens=input_tokens, **kwargs)
             out_tokens = len(res.get("token_ids") or res.get("tokens") or [])
+            if managed and request_id and res.get("token_ids") is not None:
+                ids = res.get("prompt_token_ids") if isinstance(prompt, str) else prompt
+                if ids is not None:
+                    self._contexts[request_id] = list(ids) + list(res["token_ids"])
             res["_schedule_info"] = {"instance_index": idx, "instance_id": cfg["instance_id"],
                                      "tp_degree": cfg["tp_degree"], "category": route.category,
                                      "is_fallback": route.is_fallback, "reason": route.reason, "prompt_id": prompt_id,
@@ -126,10 +133,27 @@ class HeterogeneousRolloutEngine:
         return None
 
     def execute_cmlfq_migration(self, request_id: str, decision: Any):
-        if hasattr(self.scheduler, "execute_migration"):
-            with self._lock:
-                return self.scheduler.execute_migration(request_id, decision)
-        return None
+        """Move a C-MLFQ request to the bucket the decision names and, when both
+        instances are in-process engines, bring its KV prefix along: the
+        cached blocks of its context are copied GPU to GPU into the target's
+        prefix cache, so its next turn there prefills only the new tokens."""
+        if not hasattr(self.scheduler, "execute_migration"):
+            return None
+        with self._lock:
+            old = self.scheduler.get_request_route(request_id) if hasattr(self.scheduler, "get_request_route") else None
+            res = self.scheduler.execute_migration(request_id, decision)
+        ctx = self._contexts.get(request_id)
+        if old is not None and res is not None and res.instance_index >= 0 and ctx and \
+                old.instance_index != res.instance_index:
+            src = getattr(self.engines[old.instance_index], "engine", None)
+            dst = getattr(self.engines[res.instance_index], "engine", None)
+            if src is not None and dst is not None and hasattr(src, "migrate_prefix_to"):
+                t0 = time.perf_counter()
+                n = src.migrate_prefix_to(dst, ctx)
+                self.kv_migrations["count"] += 1 if n else 0
+                self.kv_migrations["tokens"] += n
+                self.kv_migrations["seconds"] += time.perf_counter() - t0
+        return res
 
     def route_cmlfq_tool_return(self, request_id: str, tool_result: Any, generated_tokens: int):
         decision = self.on_tool_return(request_id, tool_result, generated_tokens)
@@ -138,11 +162,13 @@ class HeterogeneousRolloutEngine:
         return decision
 
     def finish_cmlfq_request(self, request_id: str, total_output_tokens: int) -> None:
+        self._contexts.pop(request_id, None)
         if request_id and hasattr(self.scheduler, "finish_request"):
             with self._lock:
                 self.scheduler.finish_request(request_id, total_output_tokens)
 
     def cancel_cmlfq_request(self, request_id: str) -> None:
+        self._contexts.pop(request_id, None)
         if request_id and hasattr(self.scheduler, "cancel_request"):
             with self._lock:
                 self.scheduler.cancel_request(request_id)

@@ -197,5 +197,50 @@ class PagedKVCache:
         self.k[layer].view(-1, self.kv_heads, self.head_dim).index_copy_(0, slots, k)
         self.v[layer].view(-1, self.kv_heads, self.head_dim).index_copy_(0, slots, v)
 
+    # -------------------------------------------------------------- migration between instances
+    def cached_blocks(self, tokens: List[int]) -> List[Tuple[int, str]]:
+        """(block, hash) of the longest run of full blocks of ``tokens`` that
+        this cache holds in its prefix cache (read only: refcounts unchanged)."""
+        out, parent, bs = [], "", self.block_size
+        for s in range(0, (len(tokens) // bs) * bs, bs):
+            h = _block_hash(parent, tokens[s:s + bs])
+            b = self.alloc.cached.get(h)
+            if b is None:
+                break
+            out.append((b, h))
+            parent = h
+        return out
+
+    def import_blocks(self, src: "PagedKVCache", blocks: List[Tuple[int, str]]) -> int:
+        """Copy ``src``'s cached blocks (a hash chain from ``cached_blocks``)
+        into this cache as prefix-cached blocks, so the next request with that
+        prefix here skips its prefill.  Every layer's K and V move in one
+        gather + one peer copy + one scatter each (NVLink when the caches sit
+        on different GPUs).  Stops at the free capacity.  Returns the tokens
+        now cached here for that prefix."""
+        if (src.num_layers, src.block_size, src.kv_heads, src.head_dim) != \
+                (self.num_layers, self.block_size, self.kv_heads, self.head_dim):
+            raise ValueError("KV caches of different shapes: migrate through a head reshard")
+        pinned, todo, have = [], [], 0
+        for b, h in blocks:
+            if not todo and h in self.alloc.cached:
+                pinned.append(self.alloc.lookup(h))  # keep the present head of the chain while allocating
+                have += 1
+            else:
+                todo.append((b, h))
+        todo = todo[:max(0, self.alloc.num_free())]
+        dst = [self.alloc.allocate() for _ in todo]
+        if todo:
+            si = torch.tensor([b for b, _ in todo], dtype=torch.long, device=src.k.device)
+            di = torch.tensor(dst, dtype=torch.long, device=self.k.device)
+            for s_pool, d_pool in ((src.k, self.k), (src.v, self.v)):
+                d_pool.index_copy_(1, di, s_pool.index_select(1, si).to(self.k.device))
+        for b, (_, h) in zip(dst, todo):
+            self.alloc.register(b, h)
+            self.alloc.release(b)  # unreferenced and cached: reusable by a matching prefix
+        for b in pinned:
+            self.alloc.release(b)
+        return (have + len(todo)) * self.block_size
+
     def usage(self) -> float:
         return 1.0 - self.alloc.num_free() / max(1, self.alloc.num_blocks)

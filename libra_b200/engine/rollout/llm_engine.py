@@ -344,6 +344,29 @@ class LLMEngine:
                 self.resume()
         return time.perf_counter() - t0
 
+    @torch.no_grad()
+    def migrate_prefix_to(self, other: "LLMEngine", tokens: List[int]) -> int:
+        """Copy this engine's cached KV of ``tokens``'s prefix into ``other``'s
+        cache (the next turn of a migrated multi-turn request then starts from
+        that prefix instead of recomputing it).  Both engines pause for the
+        copy; engines on different weight versions do not exchange KV.
+        Returns the prefix tokens now cached on ``other``."""
+        if other is self or self.version != other.version or self.tp_size != 1 or other.tp_size != 1:
+            return 0
+        pauses = [(e, e._paused.is_set()) for e in (self, other)]
+        for e, _ in pauses:
+            e.pause()
+        try:
+            n = other.kv.import_blocks(self.kv, self.kv.cached_blocks(list(tokens)))
+            if other.device.type == "cuda":
+                torch.cuda.synchronize(other.device)
+        finally:
+            for e, was in pauses:
+                if not was:
+                    e.resume()
+        self.stats["migrated_out_tokens"] = self.stats.get("migrated_out_tokens", 0) + n
+        return n
+
     # ------------------------------------------------------------------ scheduling
     def _admit(self) -> List[_Request]:
         admitted, budget = [], self.max_batch_tokens - len(self.running)

@@ -84,3 +84,79 @@ def test_sampler_top_k_and_greedy():
     t, lp = sample(logits, torch.tensor([0.0, 1.0]), torch.tensor([1.0, 1.0]), torch.tensor([-1, 1]))
     assert t.tolist() == [1, 0]
     assert torch.allclose(lp[1], torch.log_softmax(logits[1], -1)[0])
+
+
+def test_kv_prefix_migration_between_engines(tiny):
+    """A multi-turn request moved to another instance takes its KV prefix along:
+    the target's next turn reuses the migrated blocks (no prefill of the old
+    context) and produces the same tokens as on the source."""
+    src = LLMEngine(tiny.cfg, tiny.params, kv_blocks=128, block_size=4)
+    dst = LLMEngine(tiny.cfg, tiny.params, kv_blocks=128, block_size=4)
+    params = SamplingParams(max_tokens=4, temperature=0.0)
+    prompt = list(range(40, 61))
+    first = src.generate_sync([prompt], params)[0]
+    ctx = prompt + first.output_tokens
+    moved = src.migrate_prefix_to(dst, ctx)
+    assert moved == (len(ctx) // 4) * 4 and moved >= 20
+    # the copied blocks hold the source's K/V bit for bit
+    blocks_src = src.kv.cached_blocks(ctx)
+    blocks_dst = dst.kv.cached_blocks(ctx)
+    assert [h for _, h in blocks_src] == [h for _, h in blocks_dst]
+    for (bs_, _), (bd, _) in zip(blocks_src, blocks_dst):
+        assert torch.equal(src.kv.k[:, bs_], dst.kv.k[:, bd]) and torch.equal(src.kv.v[:, bs_], dst.kv.v[:, bd])
+    turn2 = ctx + [3, 4, 5]
+    before = dst.stats["cached_prefix_tokens"]
+    out_dst = dst.generate_sync([turn2], params)[0]
+    assert dst.stats["cached_prefix_tokens"] - before >= 20
+    assert out_dst.output_tokens == src.generate_sync([turn2], params)[0].output_tokens
+    # a second migration of the same prefix finds it present and copies nothing new
+    assert src.migrate_prefix_to(dst, ctx) == moved
+    # engines on different weight versions do not exchange KV
+    dst.update_weights({}, version=5)
+    assert src.migrate_prefix_to(dst, ctx) == 0
+
+
+def test_hetero_pool_migrates_kv_with_the_request(tiny):
+    """C-MLFQ migration of a multi-turn request between two in-process
+    instances carries the request's cached context to the target."""
+    from types import SimpleNamespace
+
+    from libra_b200.engine.heterogeneous_engine import HeterogeneousRolloutEngine
+    from libra_b200.engine.rollout_engine import LocalRolloutEngine
+    from libra_b200.engine.tokenizer import ByteTokenizer
+
+    engines = [LocalRolloutEngine(LLMEngine(tiny.cfg, tiny.params, kv_blocks=128, block_size=4),
+                                  ByteTokenizer(tiny.cfg.vocab_size)) for _ in range(2)]
+    cfgs = [{"instance_id": f"i{i}", "tp_degree": 1} for i in range(2)]
+
+    class _Sched:  # two-bucket stand-in with the C-MLFQ request-route interface
+        def __init__(self):
+            self.where = {}
+
+        def register_instance(self, *a):
+            pass
+
+        def get_request_route(self, rid):
+            i = self.where.get(rid)
+            return None if i is None else SimpleNamespace(instance_index=i, pending=False, category="short",
+                                                          is_fallback=False, reason="", request_id=rid)
+
+        def execute_migration(self, rid, decision):
+            self.where[rid] = 1
+            return self.get_request_route(rid)
+
+        def finish_request(self, rid, n):
+            self.where.pop(rid, None)
+
+    sched = _Sched()
+    sched.where["r1"] = 0
+    pool = HeterogeneousRolloutEngine(engines, cfgs, sched)
+    prompt = list(range(40, 61))
+    res = asyncio.run(pool.generate(prompt, max_new_tokens=4, temperature=0.0, request_id="r1"))
+    assert res["_schedule_info"]["instance_index"] == 0
+    pool.execute_cmlfq_migration("r1", SimpleNamespace(should_migrate=True, target_bucket="long"))
+    assert pool.kv_migrations["count"] == 1 and pool.kv_migrations["tokens"] >= 20
+    ctx = prompt + res["token_ids"]
+    assert engines[1].engine.kv.cached_blocks(ctx)
+    for e in engines:
+        e.engine.shutdown()

@@ -195,3 +195,36 @@ def test_decode_graphs_seeded_sampling_is_batch_independent(monkeypatch):
     res = crowd.generate_sync(others[:2] + [list(range(10, 30))] + others[2:],
                               SamplingParams(max_tokens=20, temperature=1.0, seed=99))
     assert res[2].output_tokens == a.output_tokens
+
+
+@pytest.mark.multigpu
+def test_kv_prefix_migration_across_gpus():
+    """KV prefix migration from an engine on GPU 0 to one on GPU 1 (peer copy
+    over NVLink): the target reuses the migrated prefix and decodes the same
+    greedy tokens."""
+    from libra_b200.engine.rollout.llm_engine import LLMEngine
+    from libra_b200.engine.rollout.sampler import SamplingParams
+    from libra_b200.models.qwen3 import ParamLayout, get_config, init_params, param_shapes
+
+    cfg = get_config("tiny-gpu")
+    engines = []
+    for d in (0, 1):
+        dev = torch.device("cuda", d)
+        lay = ParamLayout(param_shapes(cfg))
+        flat = torch.empty(lay.numel, dtype=torch.bfloat16, device=dev)
+        views = lay.views(flat)
+        init_params(cfg, views, seed=3)
+        engines.append(LLMEngine(cfg, views, kv_blocks=256, block_size=16, max_model_len=2048, flat=flat))
+    src, dst = engines
+    params = SamplingParams(max_tokens=8, temperature=0.0)
+    prompt = list(range(100, 400))
+    first = src.generate_sync([prompt], params)[0]
+    ctx = prompt + first.output_tokens
+    moved = src.migrate_prefix_to(dst, ctx)
+    assert moved == (len(ctx) // 16) * 16
+    turn2 = ctx + [7, 8, 9]
+    before = dst.stats["cached_prefix_tokens"]
+    a = dst.generate_sync([turn2], params)[0]
+    assert dst.stats["cached_prefix_tokens"] - before >= moved - 16
+    b = src.generate_sync([turn2], params)[0]
+    assert a.output_tokens == b.output_tokens

@@ -61,6 +61,21 @@ def main(argv=None) -> None:
     wall = (time.perf_counter() - t0) * 1e3 / a.steps
     ms = e0.elapsed_time(e1) / a.steps
     g_ = llm._graphs
+    # the same captured step replayed back to back with no host work in between: the device's share
+    graph_ms = None
+    if g_ is not None and llm.running:
+        b = g_.bucket(len(llm.running))
+        for _ in range(3):
+            g_.graphs[b].replay()
+        torch.cuda.synchronize()
+        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2.record()
+        for _ in range(50):
+            g_.graphs[b].replay()
+        e3.record()
+        torch.cuda.synchronize()
+        graph_ms = e2.elapsed_time(e3) / 50
+        g_.reset_accumulators()
     # one decode step under the profiler: per-kernel device time
     from torch.profiler import ProfilerActivity, profile
 
@@ -77,6 +92,7 @@ def main(argv=None) -> None:
     kv_bytes = a.batch * ctx * cfg.num_hidden_layers * cfg.num_key_value_heads * cfg.head_dim * 2 * 2
     print(json.dumps({"model": a.model, "batch": a.batch, "context_at_end": ctx, "ms_per_step": round(ms, 3),
                       "wall_ms_per_step": round(wall, 3), "host_ms_per_step": round(host * 1e3 / a.steps, 3),
+                      "graph_only_ms_per_step": round(graph_ms, 3) if graph_ms is not None else None,
                       "graph_replays": g_.replays if g_ else 0, "weights_gb": flat.numel() * 2 / 1e9,
                       "kv_gb_per_step_at_end": kv_bytes / 1e9, "profiled_step_kernels_ms": top,
                       "profiled_step_device_ms": round(sum(kern.values()), 3)}), flush=True)

@@ -682,11 +682,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPeer ? kPeerThreads
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * acc);
       if constexpr (kPeerAR) {
-        __threadfence_system();  // this lane's partial rows are visible to the owner before the count
+        // the warp's partial rows are visible to the owner before the count: the warp barrier orders every
+        // lane's stores before lane 0's system-scope fence (cumulative), which precedes the release; one
+        // fence per warp instead of one per lane (the per-lane fences were the kernel's top stall)
         __syncwarp();
-        if (lane == 0)
+        if (lane == 0) {
+          __threadfence_system();
           red_add_release_sys(reinterpret_cast<int*>(par.flags[peer_owner(par, mb)]) + par.parity * 2 * par.max_rb + mb,
                               1);
+        }
       }
     }
   } else {
@@ -829,11 +833,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPeer ? kPeerThreads
           }
         }
       }
-      __threadfence_system();
-      __syncthreads();
-      if (threadIdx.x < n)
+      __syncthreads();  // every thread's sums are stored; the signalling threads fence once for the CTA
+      if (threadIdx.x < n) {
+        __threadfence_system();
         red_add_release_sys(reinterpret_cast<int*>(par.flags[threadIdx.x]) + par.parity * 2 * par.max_rb +
                                 par.max_rb + mb, 1);
+      }
     }
     // ---- C: gathered row blocks (+ residual) into the output.  With the
     // reduce-scatter the wait alone remains: no rank may overwrite its partial

@@ -26,7 +26,7 @@ namespace libra {
 namespace tp {
 
 constexpr int kMaxRanks = 8;
-constexpr int kMaxCtas = 128;
+constexpr int kMaxCtas = 512;  // up to 4096 rows in one wave of 8-warp CTAs
 constexpr int kWarps = 8;
 
 struct PeerPtrs {
@@ -127,7 +127,7 @@ std::vector<torch::Tensor> allreduce_add_rmsnorm(std::vector<int64_t> data_ptrs,
               "tp_allreduce: residual must be a contiguous CUDA bf16 [B, H] tensor");
   const int B = (int)residual.size(0), H = (int)residual.size(1);
   LIBRA_CHECK(H % 8 == 0 && w.numel() == H && w.scalar_type() == at::kBFloat16, "tp_allreduce: H %% 8 and w [H]");
-  LIBRA_CHECK(grid >= 1 && grid <= kMaxCtas, "tp_allreduce: grid must be in [1, 128]");
+  LIBRA_CHECK(grid >= 1 && grid <= kMaxCtas, "tp_allreduce: grid must be in [1, %d]", kMaxCtas);
   LIBRA_CHECK(slot_offset_bytes % 16 == 0, "tp_allreduce: slot offset must be 16-byte aligned");
   PeerPtrs p{};
   for (int i = 0; i < n; ++i) {

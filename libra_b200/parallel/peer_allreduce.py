@@ -19,7 +19,7 @@ import torch.distributed as dist
 
 from libra_b200 import ops
 
-MAX_CTAS = 128
+MAX_CTAS = 512
 MAX_RANKS = 8
 WARPS = 8
 

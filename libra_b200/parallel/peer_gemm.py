@@ -222,8 +222,14 @@ def row_parallel_fused(a, w, residual, fused: PeerGemmAllReduce):
 
 
 def _bench(argv=None) -> None:
-    """torchrun --nproc-per-node N -m libra_b200.parallel.peer_gemm --rows 16384 --cols 2560 --inner 2048:
-    device time of the fused kernel against our GEMM + NCCL all-reduce (max over ranks)."""
+    """torchrun --nproc-per-node N -m libra_b200.parallel.peer_gemm --rows 16384 --cols 2560 --inner 2048
+    [--mode ar|rs|ag|all]: device time of each fused kernel against our GEMM + the NCCL collective
+    (max over ranks), and the fraction of its roofline: the slower of the GEMM at the measured
+    1622 TFLOP/s burst peak and the bytes that must cross NVLink at 770 GB/s per direction.
+
+    ar: y = sum_r a_r w_r^T on every rank (M x N bf16 all-reduced);
+    rs: this rank's M/n rows of that sum (reduce-scatter);
+    ag: y = [a_0; ...; a_{n-1}] w^T from row shards a_r of M/n rows (all-gather of A, K columns)."""
     import argparse
     import datetime
     import json
@@ -234,26 +240,21 @@ def _bench(argv=None) -> None:
     ap.add_argument("--cols", dest="n", type=int, default=2560)
     ap.add_argument("--inner", dest="k", type=int, default=2048)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--mode", default="ar", choices=["ar", "rs", "ag", "all"])
+    ap.add_argument("--peak-tflops", type=float, default=1622.0)
+    ap.add_argument("--link-gbs", type=float, default=770.0)
     args = ap.parse_args(argv)
     rank = int(os.environ.get("RANK", "0"))
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                             device_id=torch.device("cuda", torch.cuda.current_device()))
+    world = dist.get_world_size()
+    M, N, K = args.m, args.n, args.k
     g = torch.Generator(device="cuda").manual_seed(rank)
-    a = torch.randn(args.m, args.k, device="cuda", generator=g).bfloat16()
-    w = (torch.randn(args.n, args.k, device="cuda", generator=g) / args.k ** 0.5).bfloat16()
-    f = PeerGemmAllReduce(dist.group.WORLD, args.m, args.n, "cuda")
+    a = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).bfloat16()
 
-    def fused():
-        return f(a, w)
-
-    def baseline():
-        y = ops.gemm(a, w)
-        dist.all_reduce(y)
-        return y
-
-    res = {}
-    for name, fn in (("fused", fused), ("gemm_plus_nccl", baseline)):
+    def timed(fn):
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
@@ -266,15 +267,52 @@ def _bench(argv=None) -> None:
         torch.cuda.synchronize()
         t = torch.tensor([e0.elapsed_time(e1) / args.iters], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        res[name] = t.item()
-    ops.check_kernel_errors()
-    flops = 2.0 * args.m * args.n * args.k
-    if rank == 0:
-        print(json.dumps({"kernel": "gemm_allreduce", "ranks": dist.get_world_size(), "M": args.m, "N": args.n,
-                          "K": args.k, "fused_ms": res["fused"], "gemm_plus_nccl_ms": res["gemm_plus_nccl"],
-                          "speedup": res["gemm_plus_nccl"] / res["fused"],
-                          "fused_tflops_per_gpu": flops / res["fused"] / 1e9}), flush=True)
-    f.close()
+        return t.item()
+
+    modes = ["ar", "rs", "ag"] if args.mode == "all" else [args.mode]
+    for mode in modes:
+        if mode in ("ar", "rs"):
+            f = PeerGemmAllReduce(dist.group.WORLD, M, N, "cuda")
+            flops = 2.0 * M * N * K
+            link = (world - 1) / world * M * N * 2 * (2 if mode == "ar" else 1)  # bytes into (and out of) a rank
+            if mode == "ar":
+                fused, base = (lambda: f(a, w)), None
+
+                def base():
+                    y = ops.gemm(a, w)
+                    dist.all_reduce(y)
+                    return y
+            else:
+                out = torch.empty(M // world, N, dtype=torch.bfloat16, device="cuda")
+                fused = lambda: f.reduce_scatter(a, w)  # noqa: E731
+
+                def base():
+                    dist.reduce_scatter_tensor(out, ops.gemm(a, w))
+                    return out
+        else:
+            S = M // world
+            f = PeerAllGatherGemm(dist.group.WORLD, S, K, "cuda")
+            shard = a[:S].contiguous()
+            full = torch.empty(M, K, dtype=torch.bfloat16, device="cuda")
+            flops = 2.0 * M * N * K
+            link = (world - 1) * S * K * 2
+            fused = lambda: f(shard, w)  # noqa: E731
+
+            def base():
+                dist.all_gather_into_tensor(full, shard)
+                return ops.gemm(full, w)
+        tf, tb = timed(fused), timed(base)
+        ops.check_kernel_errors()
+        bound = max(flops / (args.peak_tflops * 1e12), link / (args.link_gbs * 1e9)) * 1e3
+        if rank == 0:
+            print(json.dumps({"kernel": {"ar": "gemm_allreduce", "rs": "gemm_reduce_scatter",
+                                         "ag": "allgather_gemm"}[mode], "ranks": world, "M": M, "N": N, "K": K,
+                              "fused_ms": round(tf, 4), "gemm_plus_nccl_ms": round(tb, 4),
+                              "speedup": round(tb / tf, 3), "roofline_ms": round(bound, 4),
+                              "fused_of_roofline": round(bound / tf, 3), "nccl_of_roofline": round(bound / tb, 3),
+                              "fused_tflops_per_gpu": round(flops / tf / 1e9, 1)}), flush=True)
+        f.close()
+        dist.barrier()
     dist.destroy_process_group()
 
 

@@ -678,14 +678,16 @@ class AsyncRLConfig:
         Every ``train_backend`` value selects the same engine, so the rules
         are the engine's: tensor parallelism must divide the heads, the FFN
         and the vocabulary; experts are spread over expert-parallel ranks
-        inside the data-parallel group; one pipeline stage and one context
-        shard per rank; checkpoints in the ``torch_dist`` layout."""
+        inside the data-parallel group; pipeline stages (with TP=1, EP=1) hold
+        contiguous layer ranges; one context shard per rank; checkpoints in
+        the ``torch_dist`` layout."""
         arch = self.model_arch
         tp, ep = self.train_tp_size, self.train_ep_size
         heads, kv = arch.n_heads, arch.n_kv_heads
-        yield (self.train_pp_size == 1,
-               f"train_pp_size={self.train_pp_size}: the native engine keeps every layer on each rank "
-               "(pipeline stages are only available through libra_b200.parallel.pipeline)")
+        yield (self.train_pp_size == 1 or (tp == 1 and ep == 1),
+               f"train_pp_size={self.train_pp_size}: pipeline stages run with train_tp_size=1 and train_ep_size=1")
+        yield (self.train_pp_size <= arch.n_layers,
+               f"train_pp_size={self.train_pp_size} exceeds the model's {arch.n_layers} layers")
         yield (self.train_cp_size == 1,
                f"train_cp_size={self.train_cp_size}: sequences are not split across ranks; long contexts run as "
                "packed variable-length attention on one rank")

@@ -81,7 +81,7 @@ class B200TrainEngine:
                  max_grad_norm: float = 1.0, tp_size: int = 1, model_path: str = "",
                  max_tokens_per_micro_batch: int = 16384, max_tokens_per_recompute_batch: int = 65536,
                  ep_size: int = 1, sequence_parallel: bool = False, precision_aware_optimizer: bool = False,
-                 optimizer_cpu_offload: bool = False, optimizer_offload_fraction: float = 0.0):
+                 optimizer_cpu_offload: bool = False, optimizer_offload_fraction: float = 0.0, pp_size: int = 1):
         self.cfg: Qwen3Config = get_config(model)
         self.model_path = model_path
         self.optim = OptimConfig(lr=learning_rate, max_grad_norm=max_grad_norm)
@@ -96,6 +96,8 @@ class B200TrainEngine:
         self.use_distributed_optimizer = use_distributed_optimizer
         self.temperature = temperature
         self.tp_size = tp_size
+        # pipeline parallelism: this rank holds a contiguous range of layers (1F1B over NCCL p2p)
+        self.pp_size = max(1, int(pp_size))
         self.sequence_parallel = bool(sequence_parallel) and tp_size > 1
         # precision-aware optimizer (MCore use_precision_aware_optimizer): Adam moments stored in bf16
         # (updated in fp32 inside the kernel), fp32 master weights; 8 instead of 12 bytes per parameter
@@ -137,6 +139,7 @@ class B200TrainEngine:
             ops.ext()  # fail loudly when the kernels are not built
         self.max_seq_length = max_seq_length
         self.tp_group, self.tp_rank, self.mesh = None, 0, None
+        self._init_pipeline()
         if self.tp_size > 1:
             # TP groups are consecutive ranks (inside the box); DP runs across them
             from libra_b200.parallel.mesh import ParallelMesh
@@ -153,6 +156,8 @@ class B200TrainEngine:
         self.dp_rank = dist.get_rank(self.dp_group) if dist.is_initialized() else 0
         self._init_expert_parallel()
         shapes = param_shapes(self.cfg, self.tp_size, self.tp_rank, self.ep_size)
+        if self.pp_size > 1:
+            shapes = [(n, sh) for n, sh in shapes if self._stage_owns(n)]
         unit = ParamLayout.ALIGN * self.dp_size
         if self.ep_size > 1:
             # dense parameters first (sharded over the data-parallel group by the distributed optimizer),
@@ -174,7 +179,17 @@ class B200TrainEngine:
         self.flat_grad = torch.zeros(self.padded_numel, dtype=torch.float32, device=dev)
         views = self.layout.views(self.flat_param)
         E_l = self.cfg.num_experts // self.ep_size if self.cfg.is_moe else 0
-        init_params(self.cfg, views, seed=self.seed + 7919 * self.tp_rank, expert_offset=self.ep_rank * E_l)
+        if self.pp_size > 1:
+            # every stage takes its slice of the full model's initialisation (identical to one rank's)
+            full_layout = ParamLayout(param_shapes(self.cfg))
+            full = full_layout.views(torch.empty(full_layout.numel, dtype=torch.bfloat16, device=dev))
+            init_params(self.cfg, full, seed=self.seed)
+            with torch.no_grad():
+                for name, v in views.items():
+                    v.copy_(full[name])
+            del full
+        else:
+            init_params(self.cfg, views, seed=self.seed + 7919 * self.tp_rank, expert_offset=self.ep_rank * E_l)
         grad_views = self.layout.views(self.flat_grad)
         self.params: Dict[str, torch.nn.Parameter] = {}
         for name, v in views.items():
@@ -228,6 +243,17 @@ class B200TrainEngine:
                                 ep_size=self.ep_size, ep_exchange=self.ep_exchange,
                                 sequence_parallel=self.sequence_parallel)
         self.sequence_parallel = self.model.sp  # off for mixture-of-experts layers
+        if self.pp_size > 1:
+            from libra_b200.parallel.pipeline import P2P
+
+            self._p2p = P2P(None, self.pp_prev, self.pp_next, dtype=torch.bfloat16, device=dev)
+            # the last stage counts the tied embedding once in the global gradient norm
+            self._pp_dup = []
+            if self.pp_rank == self.pp_size - 1 and self.cfg.tie_word_embeddings and "embed_tokens" in self.params:
+                a, b = self.layout.segment("embed_tokens")
+                lo, hi = self.shard_start, self.shard_start + self.shard_numel
+                if max(a, lo) < min(b, hi):
+                    self._pp_dup.append((max(a, lo) - lo, min(b, hi) - lo))
         if (self.sequence_parallel and dev.type == "cuda" and dist.get_backend(self.tp_group) == "nccl"
                 and os.environ.get("LIBRA_SP_FUSED", "1") != "0"):
             # row-parallel linears (o_proj, down_proj: output width H) reduce-scatter inside the GEMM
@@ -256,6 +282,109 @@ class B200TrainEngine:
         self._sq_ready = False
         if self._peer_dp_applies():
             self.enable_peer_data_parallel()
+
+    def _init_pipeline(self) -> None:
+        """Pipeline stages over the mesh (TP, DP, PP fastest first): this rank's
+        layer range, its neighbours in the pipeline, and the group that sums the
+        tied word embedding's gradient between the first and the last stage."""
+        self.pp_rank, self.pp_group, self.pp_prev, self.pp_next, self.pp_embed_group = 0, None, None, None, None
+        self.stage_layers = range(self.cfg.num_hidden_layers)
+        if self.pp_size <= 1:
+            return
+        if self.tp_size != 1 or self.ep_size != 1:
+            raise ValueError("pipeline parallelism runs with tp_size=1 and ep_size=1")
+        if not dist.is_initialized():
+            raise RuntimeError("pipeline parallelism needs an initialized process group")
+        from libra_b200.parallel.mesh import ParallelMesh
+        from libra_b200.parallel.pipeline import PipelineStage
+
+        rank = dist.get_rank()
+        self.mesh = ParallelMesh(dist.get_world_size(), pp=self.pp_size)
+        c = self.mesh.coords(rank)
+        self.pp_rank = c.pp
+        self.pp_group = self.mesh.group("pp", rank)
+        if self.dp_group is None:
+            self.dp_group = self.mesh.group("dp", rank)
+        members = self.mesh.members("pp", rank)
+        self.pp_prev = members[self.pp_rank - 1] if self.pp_rank > 0 else None
+        self.pp_next = members[self.pp_rank + 1] if self.pp_rank + 1 < self.pp_size else None
+        self.pp_first, self.pp_last = members[0], members[-1]
+        self.stage_layers = PipelineStage.split_layers(self.cfg.num_hidden_layers, self.pp_size)[self.pp_rank]
+        if self.cfg.tie_word_embeddings:
+            for d in range(self.mesh.dp):  # every rank creates every group, in the same order
+                ranks = [self.mesh.rank_of(dp=d, pp=0), self.mesh.rank_of(dp=d, pp=self.pp_size - 1)]
+                grp = dist.new_group(ranks)
+                if rank in ranks:
+                    self.pp_embed_group = grp
+
+    def _stage_owns(self, name: str) -> bool:
+        first, last = self.pp_rank == 0, self.pp_rank == self.pp_size - 1
+        if name.startswith("layers."):
+            return int(name.split(".")[1]) in self.stage_layers
+        if name == "embed_tokens":
+            return first or (last and self.cfg.tie_word_embeddings)
+        return last  # final norm, untied LM head
+
+    # ------------------------------------------------------------------ pipeline stages
+    def _pp_stage(self, mb: Dict[str, Any], x: Optional[torch.Tensor]) -> torch.Tensor:
+        """This stage's layers; the last stage returns the action tokens' logprobs."""
+        m, batch = self.model, mb["batch"]
+        if self.pp_rank == 0:
+            x = m.embed(batch.tokens)
+        for i in self.stage_layers:
+            if self.recompute_activations and torch.is_grad_enabled():
+                x = torch.utils.checkpoint.checkpoint(m._layer, i, x, batch.positions, batch.cu_seqlens,
+                                                      batch.max_seqlen, batch.tiles, use_reentrant=False)
+            else:
+                x = m._layer(i, x, batch.positions, batch.cu_seqlens, batch.max_seqlen, batch.tiles)
+        if self.pp_rank < self.pp_size - 1:
+            return x
+        h = ops.rmsnorm(x, m.p["norm"], self.cfg.rms_norm_eps)
+        rows = h.index_select(0, batch.action_rows)
+        return ops.lm_head_logprob(rows, m.lm_head_weight, batch.action_targets, self.temperature)
+
+    @torch.no_grad()
+    def _pp_logprobs(self, device_batches: List[Dict[str, Any]]) -> List[torch.Tensor]:
+        """Forward-only pipeline over the chunks (each stage receives, runs its
+        layers, sends on; the sends are asynchronous, so consecutive chunks
+        overlap across stages); the last stage's logprobs are broadcast to every
+        stage of the pipeline."""
+        out = []
+        last = self.pp_rank == self.pp_size - 1
+        for mb in device_batches:
+            y = self._pp_stage(mb, self._p2p.recv_forward())
+            if last:
+                out.append(y.float().contiguous())
+            else:
+                self._p2p.send_forward(y)
+                out.append(torch.empty(int(mb["batch"].action_rows.numel()), dtype=torch.float32,
+                                       device=self.device))
+        self._p2p.wait_sends()
+        for t in out:
+            dist.broadcast(t, src=self.pp_last, group=self.pp_group)
+        return out
+
+    def _pp_forward_backward(self, device_micro_batches: List[Dict[str, Any]], acc: torch.Tensor) -> None:
+        """1F1B over the chunks (parallel/pipeline.py): the last stage turns
+        logprobs into the GRPO loss; afterwards the first and last stages sum
+        the tied embedding's gradient and the loss statistics reach every stage."""
+        from libra_b200.parallel.pipeline import allreduce_tied_embedding_grad, one_f_one_b
+
+        last = self.pp_rank == self.pp_size - 1
+
+        def stage(mb, x):
+            y = self._pp_stage(mb, x)
+            if not last:
+                return y
+            loss, pg, kl = self.loss(y, mb["old_logp"], mb["adv"], mb.get("w"))
+            acc.add_(torch.stack([loss.detach(), pg.detach(), kl.detach()]))
+            return loss
+
+        with nvtx.nvtx_range("forward_backward"):
+            one_f_one_b(stage, device_micro_batches, self._p2p, self.pp_size, self.pp_rank)
+        if self.pp_embed_group is not None:
+            allreduce_tied_embedding_grad(self.params["embed_tokens"], self.pp_embed_group)
+        dist.broadcast(acc, src=self.pp_last, group=self.pp_group)
 
     def _init_expert_parallel(self) -> None:
         """Expert-parallel groups inside the data-parallel group: ``ep_group`` =
@@ -320,12 +449,17 @@ class B200TrainEngine:
         return getattr(self, "dp_size", 1)
 
     def is_batch_source(self) -> bool:
-        return True  # TP=1: every rank is a DP replica that owns its batch
+        # every DP replica owns its batch; with pipeline stages its first stage collects it
+        return getattr(self, "pp_rank", 0) == 0
 
     def get_local_batch_size(self, global_batch_size: int) -> int:
         return int(global_batch_size) // max(1, self.get_data_parallel_world_size())
 
     def distribute_trajectories(self, trajectories):
+        if self.pp_size > 1 and getattr(self, "pp_group", None) is not None:
+            box = [trajectories or []]  # the replica's first stage hands its batch to the other stages
+            dist.broadcast_object_list(box, src=self.pp_first, group=self.pp_group)
+            return box[0]
         return trajectories or []
 
     def align_distributed_trajectories(self, trajectories):
@@ -451,10 +585,15 @@ class B200TrainEngine:
     def recompute_logprobs(self, trajectories: List[Dict[str, Any]]) -> None:
         """Refresh trajectory["logprobs"] with the current policy (host tensors in, host tensors out)."""
         results = []
-        for chunk, host in self.prepare_recompute(trajectories):
-            dev_mb = self.to_device(host)
-            with nvtx.nvtx_range("recompute_forward"):
-                lp = self.model.action_logprobs(dev_mb["batch"], self.temperature)
+        prepared = self.prepare_recompute(trajectories)
+        pp_lps = self._pp_logprobs([self.to_device(h) for _, h in prepared]) if self.pp_size > 1 else None
+        for j, (chunk, host) in enumerate(prepared):
+            if pp_lps is not None:
+                lp = pp_lps[j]
+            else:
+                dev_mb = self.to_device(host)
+                with nvtx.nvtx_range("recompute_forward"):
+                    lp = self.model.action_logprobs(dev_mb["batch"], self.temperature)
             results.append((chunk, host["batch"], lp.to("cpu", non_blocking=True)))
             self.io_bytes["d2h"] += lp.numel() * lp.element_size()
         if self.device.type == "cuda":
@@ -483,7 +622,9 @@ class B200TrainEngine:
         """Forward/backward over device-resident weighted chunks + optimizer step."""
         self.flat_grad.zero_()
         acc = torch.zeros(3, dtype=torch.float32, device=self.device)
-        for mb in device_micro_batches:
+        if self.pp_size > 1:
+            self._pp_forward_backward(device_micro_batches, acc)
+        for mb in device_micro_batches if self.pp_size == 1 else []:
             with nvtx.nvtx_range("forward_backward"):
                 logp = self.model.action_logprobs(mb["batch"], self.temperature)
                 loss, pg, kl = self.loss(logp, mb["old_logp"], mb["adv"], mb.get("w"))
@@ -573,6 +714,17 @@ class B200TrainEngine:
             self.sq_norm.copy_(total - (self.tp_size - 1) * both[1:])
         elif self.sharded and self._peer_grad is None:
             dist.all_reduce(self.sq_norm, op=dist.ReduceOp.SUM, group=self.dp_group)
+        if self.pp_size > 1:
+            # every stage holds its own layers: sum the stages, the tied embedding once (first stage's copy)
+            dup = torch.zeros(1, dtype=torch.float32, device=self.device)
+            if self.pp_rank == self.pp_size - 1 and self.cfg.tie_word_embeddings:
+                for a, b in self._pp_dup:
+                    dup += self.grad_shard[a:b].float().pow(2).sum()
+                if self.sharded:
+                    dist.all_reduce(dup, group=self.dp_group)
+            total = self.sq_norm - dup
+            dist.all_reduce(total, group=self.pp_group)
+            self.sq_norm.copy_(total)
         o = self.optim
         if self.x_master is not None:
             # experts: the global norm adds every EP rank's experts once; the AdamW update of this rank's
@@ -909,8 +1061,9 @@ def create_train_engine(config) -> B200TrainEngine:
     Every ``train_backend`` value maps onto the native engine; the model preset
     is taken from ``model_path`` when it names a preset, else from model_arch.
     The parallel layout comes from the config: ``train_tp_size`` (tensor
-    parallel groups of consecutive ranks) and ``train_ep_size`` (experts spread
-    over that many data-parallel ranks).
+    parallel groups of consecutive ranks), ``train_ep_size`` (experts spread
+    over that many data-parallel ranks), ``train_pp_size`` (pipeline stages of
+    contiguous layers, 1F1B) and ``sequence_parallel``.
     """
     name = os.path.basename(str(config.model_path)).lower()
     try:
@@ -919,8 +1072,6 @@ def create_train_engine(config) -> B200TrainEngine:
         from libra_b200.models.qwen3 import config_from_arch
 
         cfg = config_from_arch(config.model_arch)
-    if int(getattr(config, "train_pp_size", 1)) != 1:
-        raise ValueError("the native engine runs with train_pp_size=1")
     return B200TrainEngine(model=cfg, learning_rate=config.learning_rate, kl_coef=config.kl_coef,
                            clip_epsilon=config.clip_epsilon, micro_batch_size=config.micro_batch_size,
                            recompute_micro_batch_size=config.recompute_micro_batch_size, seed=config.seed,
@@ -933,4 +1084,5 @@ def create_train_engine(config) -> B200TrainEngine:
                                                                   False)),
                            optimizer_cpu_offload=bool(getattr(config, "megatron_optimizer_cpu_offload", False)),
                            optimizer_offload_fraction=float(getattr(config, "megatron_optimizer_offload_fraction",
-                                                                    0.0)))
+                                                                    0.0)),
+                           pp_size=int(getattr(config, "train_pp_size", 1) or 1))

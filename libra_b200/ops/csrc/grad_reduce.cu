@@ -71,24 +71,37 @@ __global__ void __launch_bounds__(512) grad_rs_peer_kernel(float* __restrict__ o
   if (ok) {
     const int64_t n4 = n >> 2;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + t; i < n4; i += stride) {
-      float4 v[N];
+    // U grid-stride steps per iteration: N x U 16-byte loads in flight per thread (few ranks leave
+    // the loop latency-bound with one step)
+    constexpr int U = N <= 4 ? 2 : 1;
+    for (int64_t i0 = blockIdx.x * (int64_t)blockDim.x + t; i0 < n4; i0 += stride * U) {
+      float4 v[U][N];
 #pragma unroll
-      for (int r = 0; r < N; ++r) v[r] = __ldcs(reinterpret_cast<const float4*>(P.src[r]) + i);
-      float4 s = v[0];
+      for (int u = 0; u < U; ++u) {
+        const int64_t i = i0 + u * stride;
 #pragma unroll
-      for (int r = 1; r < N; ++r) {
-        s.x += v[r].x;
-        s.y += v[r].y;
-        s.z += v[r].z;
-        s.w += v[r].w;
+        for (int r = 0; r < N; ++r)
+          v[u][r] = i < n4 ? __ldcs(reinterpret_cast<const float4*>(P.src[r]) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      s.x *= scale;
-      s.y *= scale;
-      s.z *= scale;
-      s.w *= scale;
-      reinterpret_cast<float4*>(out)[i] = s;
-      acc += s.x * s.x + s.y * s.y + s.z * s.z + s.w * s.w;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t i = i0 + u * stride;
+        if (i >= n4) break;
+        float4 s = v[u][0];
+#pragma unroll
+        for (int r = 1; r < N; ++r) {
+          s.x += v[u][r].x;
+          s.y += v[u][r].y;
+          s.z += v[u][r].z;
+          s.w += v[u][r].w;
+        }
+        s.x *= scale;
+        s.y *= scale;
+        s.z *= scale;
+        s.w *= scale;
+        reinterpret_cast<float4*>(out)[i] = s;
+        acc += s.x * s.x + s.y * s.y + s.z * s.z + s.w * s.w;
+      }
     }
     for (int64_t i = n4 * 4 + blockIdx.x * (int64_t)blockDim.x + t; i < n; i += stride) {
       float s = 0.f;

@@ -232,8 +232,9 @@ class AsyncRLTrainer:
         from libra_b200.engine.tokenizer import load_tokenizer
 
         eng = self.train_engine
-        if int(getattr(eng, "tp_size", 1)) != 1:
-            raise ValueError("rollout_backend='colocated' runs a full model per GPU: use train_tp_size=1")
+        if int(getattr(eng, "tp_size", 1)) != 1 or int(getattr(eng, "pp_size", 1)) != 1:
+            raise ValueError("rollout_backend='colocated' runs a full model per GPU: use train_tp_size=1 and "
+                             "train_pp_size=1")
         c = self.config
         flat = eng.flat_param.detach().clone()
         cfg = eng.cfg
@@ -425,16 +426,18 @@ class AsyncRLTrainer:
         return chosen
 
     def _distribute(self, batch):
-        """Scatter data-parallel slices (whole groups) when rank 0 is the only batch source."""
+        """Scatter data-parallel slices (whole groups) when rank 0 is the only
+        batch source: one slice per data-parallel replica, so the tensor-parallel
+        ranks and pipeline stages of a replica all receive the same trajectories."""
         if not self._single_batch_source:
             return self.train_engine.distribute_trajectories(batch)
-        world = self.world_size
+        dp = max(1, int(self.train_engine.get_data_parallel_world_size()))
         payload = [None]
         if self.is_main_process:
-            per = len(batch) // world
-            payload = [[batch[r * per:(r + 1) * per] for r in range(world)]]
+            per = len(batch) // dp
+            payload = [[batch[d * per:(d + 1) * per] for d in range(dp)]]
         dist.broadcast_object_list(payload, src=0)
-        return payload[0][self.rank]
+        return payload[0][int(self.train_engine.get_data_parallel_rank())]
 
     # ================================================================== weight sync
     def _sync_weights(self, target_version: int) -> float:

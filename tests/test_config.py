@@ -31,7 +31,7 @@ def test_numeric_string_coercion():
     ({"batch_size": 30}, "batch_size must be divisible"),
     ({"weight_sync_mode": "foo"}, "weight_sync_mode"),
     ({"rollout_weight_sync_mode": "nccl"}, "requires weight_sync_mode"),
-    ({"train_pp_size": 2}, "train_pp_size=2: the native engine keeps every layer"),
+    ({"train_pp_size": 2, "train_tp_size": 2, "train_gpus": 4}, "pipeline stages run with train_tp_size=1"),
     ({"train_cp_size": 2, "train_gpus": 8}, "train_cp_size=2: sequences are not split"),
     ({"train_backend": "deepspeed"}, "train_backend"),
     ({"megatron_optimizer_offload_fraction": 0.5}, "needs megatron_optimizer_cpu_offload=true"),
@@ -85,6 +85,6 @@ def test_parallel_layout_reaches_the_engine():
     c30 = AsyncRLConfig.from_file(os.path.join(CFG_DIR, "qwen3_30b_a3b_ep8.yaml"))
     e30 = create_train_engine(c30)
     assert e30.tp_size == 1 and e30.ep_size == 8 and e30.cfg.num_experts == 128
-    with pytest.raises(ValueError, match="train_pp_size"):
-        c30.train_pp_size = 2
-        create_train_engine(c30)
+    c4 = AsyncRLConfig.from_file(os.path.join(CFG_DIR, "qwen3_4b_grpo_8xb200.yaml"))
+    c4.train_tp_size, c4.train_pp_size = 1, 2
+    assert create_train_engine(c4).pp_size == 2

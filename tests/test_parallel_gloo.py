@@ -242,3 +242,53 @@ def _ep_engine_worker(rank, world, port, out_dir):
 def test_expert_parallel_engine_matches_one_rank(tmp_path):
     _spawn(_ep_engine_worker, 2, str(tmp_path))
     assert {p.name for p in tmp_path.iterdir()} == {"epe_ok_0", "epe_ok_1"}
+
+
+def _pp_engine_worker(rank, world, port, out_dir, pp):
+    """Pipeline-parallel engine (tied embeddings across the first and last
+    stage, 1F1B over p2p, DP replicas on identical data) against one rank."""
+    _init(rank, world, port)
+    import copy
+
+    from libra_b200.engine.train_engine import B200TrainEngine
+    from libra_b200.workflow.synthetic import GRPOWorkload, LengthDist
+
+    wl = GRPOWorkload("t", vocab_size=1024, prompts_per_step=2, group_size=4, prompt=LengthDist(12, 0.3, 4, 24),
+                      response=LengthDist(16, 0.3, 2, 32))
+    trajs = wl.trajectories(0)
+    solo = None
+    for r in range(world):  # every rank creates every one-rank group, in the same order
+        g = dist.new_group([r])
+        if r == rank:
+            solo = g
+    kw = dict(device="cpu", seed=3, learning_rate=1e-3, micro_batch_size=2, max_tokens_per_micro_batch=48)
+    ref = B200TrainEngine("tiny", dp_group=solo, **kw)
+    ref.initialize()
+    eng = B200TrainEngine("tiny", pp_size=pp, **kw)
+    eng.initialize()
+    assert eng.pp_size == pp and len(eng.params) < len(ref.params)
+    for n, p in eng.params.items():
+        torch.testing.assert_close(p.detach(), ref.params[n].detach(), rtol=0, atol=0, msg=n)
+    t_ref, t_pp = copy.deepcopy(trajs), copy.deepcopy(trajs)
+    ref.recompute_logprobs(t_ref)
+    eng.recompute_logprobs(t_pp)
+    for a, b in zip(t_pp, t_ref):
+        torch.testing.assert_close(a["logprobs"], b["logprobs"], rtol=1e-4, atol=1e-5)
+    s_ref = ref.grpo_update(t_ref)
+    s_pp = eng.grpo_update(t_pp)
+    assert abs(s_pp["loss"] - s_ref["loss"]) < 1e-5 and abs(s_pp["grad_norm"] - s_ref["grad_norm"]) < 1e-4 * \
+        max(1.0, s_ref["grad_norm"]), (s_pp, s_ref)
+    for n, p in eng.params.items():
+        torch.testing.assert_close(p.detach().float(), ref.params[n].detach().float(), rtol=1e-2, atol=1e-3, msg=n)
+    # the replica's first stage owns the batch; the other stages receive it from there
+    assert eng.is_batch_source() == (eng.pp_rank == 0)
+    got = eng.distribute_trajectories(trajs if eng.pp_rank == 0 else None)
+    assert len(got) == len(trajs)
+    open(os.path.join(out_dir, f"ppe_ok_{rank}"), "w").close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,pp", [(2, 2), (4, 2)])
+def test_pipeline_engine_matches_one_rank(tmp_path, world, pp):
+    _spawn(_pp_engine_worker, world, str(tmp_path), pp)
+    assert {p.name for p in tmp_path.iterdir()} == {f"ppe_ok_{r}" for r in range(world)}

@@ -65,11 +65,29 @@ def mcore_qkv_rows(cfg: Qwen3Config, nq: Optional[int] = None, nkv: Optional[int
     return torch.tensor(rows, dtype=torch.long)
 
 
+def _optim_prefix(engine, dp_rank: int) -> str:
+    """Key prefix of one data-parallel shard of the optimizer state; tensor-
+    parallel ranks and pipeline stages hold different parameters, so each has
+    its own shards."""
+    pre = "optimizer."
+    if int(getattr(engine, "tp_size", 1)) > 1:
+        pre += f"tp{int(engine.tp_rank)}."
+    if int(getattr(engine, "pp_size", 1)) > 1:
+        pre += f"pp{int(engine.pp_rank)}."
+    return f"{pre}shard_{dp_rank}"
+
+
 def to_mcore(params: Dict[str, torch.Tensor], cfg: Qwen3Config) -> Dict[str, torch.Tensor]:
+    """MCore names for the parameters present (a pipeline stage holds a subset: its
+    layers keep their global indices, as in MCore's pipeline-parallel checkpoints)."""
     perm = mcore_qkv_rows(cfg)
-    out: Dict[str, torch.Tensor] = {"embedding.word_embeddings.weight": params["embed_tokens"]}
+    out: Dict[str, torch.Tensor] = {}
+    if "embed_tokens" in params:
+        out["embedding.word_embeddings.weight"] = params["embed_tokens"]
     for i in range(cfg.num_hidden_layers):
         p, m = f"layers.{i}.", f"decoder.layers.{i}."
+        if p + "input_layernorm" not in params:
+            continue
         out[m + "input_layernorm.weight"] = params[p + "input_layernorm"]
         out[m + "self_attention.linear_qkv.weight"] = params[p + "qkv_proj"].index_select(0, perm.to(params[p + "qkv_proj"].device))
         out[m + "self_attention.q_layernorm.weight"] = params[p + "q_norm"]
@@ -85,8 +103,9 @@ def to_mcore(params: Dict[str, torch.Tensor], cfg: Qwen3Config) -> Dict[str, tor
         else:
             out[m + "mlp.linear_fc1.weight"] = params[p + "gate_up_proj"]
             out[m + "mlp.linear_fc2.weight"] = params[p + "down_proj"]
-    out["decoder.final_layernorm.weight"] = params["norm"]
-    if not cfg.tie_word_embeddings:
+    if "norm" in params:
+        out["decoder.final_layernorm.weight"] = params["norm"]
+    if not cfg.tie_word_embeddings and "lm_head" in params:
         out["output_layer.weight"] = params["lm_head"]
     return out
 
@@ -94,9 +113,12 @@ def to_mcore(params: Dict[str, torch.Tensor], cfg: Qwen3Config) -> Dict[str, tor
 def from_mcore(sd: Dict[str, torch.Tensor], params: Dict[str, torch.Tensor], cfg: Qwen3Config) -> None:
     inv = torch.argsort(mcore_qkv_rows(cfg))
     with torch.no_grad():
-        params["embed_tokens"].copy_(sd["embedding.word_embeddings.weight"])
+        if "embed_tokens" in params:
+            params["embed_tokens"].copy_(sd["embedding.word_embeddings.weight"])
         for i in range(cfg.num_hidden_layers):
             p, m = f"layers.{i}.", f"decoder.layers.{i}."
+            if p + "input_layernorm" not in params:
+                continue
             params[p + "input_layernorm"].copy_(sd[m + "input_layernorm.weight"])
             qkv = sd[m + "self_attention.linear_qkv.weight"]
             params[p + "qkv_proj"].copy_(qkv.index_select(0, inv.to(qkv.device)))
@@ -112,8 +134,9 @@ def from_mcore(sd: Dict[str, torch.Tensor], params: Dict[str, torch.Tensor], cfg
             else:
                 params[p + "gate_up_proj"].copy_(sd[m + "mlp.linear_fc1.weight"])
                 params[p + "down_proj"].copy_(sd[m + "mlp.linear_fc2.weight"])
-        params["norm"].copy_(sd["decoder.final_layernorm.weight"])
-        if not cfg.tie_word_embeddings:
+        if "norm" in params:
+            params["norm"].copy_(sd["decoder.final_layernorm.weight"])
+        if not cfg.tie_word_embeddings and "lm_head" in params:
             params["lm_head"].copy_(sd["output_layer.weight"])
 
 
@@ -247,16 +270,18 @@ class DistributedCheckpointManager:
             sd.update({f"model.{k}": v for k, v in to_mcore(params, cfg).items()})
             if include_optimizer and getattr(engine, "master", None) is not None:
                 r = engine.get_data_parallel_rank() if engine.sharded else 0
-                if engine.sharded or _rank() == 0:
+                if engine.sharded or engine.get_data_parallel_rank() == 0:
                     state = engine.optimizer_state_tensors() if hasattr(engine, "optimizer_state_tensors") else \
                         {"master": engine.master, "exp_avg": engine.exp_avg, "exp_avg_sq": engine.exp_avg_sq}
                     for n, t in state.items():
-                        sd[f"optimizer.shard_{r}.{n}"] = t
+                        sd[f"{_optim_prefix(engine, r)}.{n}"] = t
                 sd["optimizer.step"] = torch.tensor(engine.step_count)
             self._progress(vdir, version, "before_dist_checkpoint_save")
             dcp.save(sd, checkpoint_id=str(ddir))
             _barrier()
             self._progress(vdir, version, "after_dist_checkpoint_save")
+        if export_for_rollout and hasattr(engine, "export_params"):
+            params = engine.export_params()  # pipeline stages: the full set on rank 0 (collective)
         if export_for_rollout and _rank() == 0:
             from safetensors.torch import save_file
 
@@ -299,12 +324,12 @@ class DistributedCheckpointManager:
             state = engine.optimizer_state_tensors() if split else \
                 {"master": engine.master, "exp_avg": engine.exp_avg, "exp_avg_sq": engine.exp_avg_sq}
             for n, t in state.items():
-                tmpl[f"optimizer.shard_{r}.{n}"] = t
+                tmpl[f"{_optim_prefix(engine, r)}.{n}"] = t
             tmpl["optimizer.step"] = torch.tensor(0)
         dcp.load(tmpl, checkpoint_id=str(vdir / "megatron_dist"))
         if load_optimizer and getattr(engine, "_offload_k", 0):
             r = engine.get_data_parallel_rank() if engine.sharded else 0
-            engine.load_optimizer_state_tensors({n: tmpl[f"optimizer.shard_{r}.{n}"]
+            engine.load_optimizer_state_tensors({n: tmpl[f"{_optim_prefix(engine, r)}.{n}"]
                                                  for n in ("master", "exp_avg", "exp_avg_sq")})
         from_mcore({k[len("model."):]: v for k, v in tmpl.items() if k.startswith("model.")}, params, cfg)
         if "optimizer.step" in tmpl:

@@ -386,6 +386,23 @@ class B200TrainEngine:
             allreduce_tied_embedding_grad(self.params["embed_tokens"], self.pp_embed_group)
         dist.broadcast(acc, src=self.pp_last, group=self.pp_group)
 
+    def export_params(self) -> Dict[str, torch.Tensor]:
+        """Every parameter of the model for an export (HF weights for rollout):
+        with pipeline stages, the stages of the first data-parallel replica
+        send theirs to its first stage (collective over that pipeline; the
+        other replicas return their own subset)."""
+        local = {k: v.detach() for k, v in self.params.items()}
+        if self.pp_size <= 1 or self.mesh.coords(dist.get_rank()).dp != 0:
+            return local
+        parts = [None] * self.pp_size if self.pp_rank == 0 else None
+        dist.gather_object({k: v.cpu() for k, v in local.items()}, parts, dst=self.pp_first, group=self.pp_group)
+        if self.pp_rank != 0:
+            return local
+        full: Dict[str, torch.Tensor] = {}
+        for part in parts:
+            full.update(part)
+        return full
+
     def _init_expert_parallel(self) -> None:
         """Expert-parallel groups inside the data-parallel group: ``ep_group`` =
         ``ep_size`` consecutive DP ranks that split the experts between them;

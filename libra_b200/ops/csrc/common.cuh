@@ -40,6 +40,16 @@
 
 namespace libra {
 
+// Kernel attributes (cudaFuncSetAttribute) apply to the current device only, so
+// the launchers that set them once remember it per device: one process can
+// drive several GPUs (in-process rollout instances, KV migration between them).
+constexpr int kMaxDevices = 64;
+inline int current_device_index() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d < 0 ? 0 : (d < kMaxDevices ? d : kMaxDevices - 1);
+}
+
 enum ErrorCode : int {
   kOk = 0,
   kTimeoutTmaFull = 1,

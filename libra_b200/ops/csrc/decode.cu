@@ -623,7 +623,8 @@ static void launch_attn(const torch::Tensor& q, const torch::Tensor& kc, const t
   LIBRA_CHECK(S >= 2, "decode_attention: %d KV heads leave room for %d pipeline stages", Hkv, S);
   const size_t smem = (size_t)S * stage_bytes + extra;
   auto kern = decode_attn_kernel<G>;
-  static size_t configured = 0;  // one per instantiation: the largest dynamic size set so far
+  static size_t configured_dev[kMaxDevices] = {};  // per instantiation and device: largest size set so far
+  size_t& configured = configured_dev[current_device_index()];
   if (smem > configured) {
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     LIBRA_CHECK(e == cudaSuccess, "decode_attention: cannot reserve %zu bytes of shared memory: %s", smem,

@@ -242,12 +242,13 @@ static void launch(const CUtensorMap& tw, const CUtensorMap& tx, float* acc, int
                    cudaStream_t st, bool pdl) {
   auto kern = gemm_decode_kernel<NB>;
   constexpr int smem = Cfg<NB>::kSmemBytes;
-  static bool configured = false;
-  if (!configured) {
+  static bool configured[kMaxDevices] = {};  // per device: the attribute is set on the current one
+  const int cfg_dev = current_device_index();
+  if (!configured[cfg_dev]) {
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     LIBRA_CHECK(e == cudaSuccess, "gemm_decode: cannot reserve %d bytes of shared memory: %s", smem,
                 cudaGetErrorString(e));
-    configured = true;
+    configured[cfg_dev] = true;
   }
   const long long units = (long long)((N + kFeat - 1) / kFeat) * ((K + BK - 1) / BK);
   const int grid = units < num_sms() ? (int)units : num_sms();

@@ -466,10 +466,10 @@ std::vector<torch::Tensor> flash_fwd(torch::Tensor q, torch::Tensor k, torch::Te
   const int n_tiles = (int)tiles.size(0);
   if (T == 0 || n_tiles == 0 || k.size(0) == 0) return {o, lse};
   const CUtensorMap mq = head_map(q), mk = head_map(k), mv = head_map(v);
-  static bool configured = false;
-  if (!configured) {
+  static bool configured[kMaxDevices] = {};  // per device: the attribute is set on the current one
+  if (!configured[current_device_index()]) {
     cudaFuncSetAttribute(flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    configured = true;
+    configured[current_device_index()] = true;
   }
   int dev, sms;
   cudaGetDevice(&dev);

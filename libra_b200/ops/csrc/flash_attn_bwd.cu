@@ -698,11 +698,11 @@ std::vector<torch::Tensor> flash_bwd(torch::Tensor dout, torch::Tensor q, torch:
       (int)T_pad, lse2p.data_ptr<float>(), dltp.data_ptr<float>());
   LIBRA_LAUNCH_CHECK();
   const CUtensorMap mq = head_map(q), mk = head_map(k), mv = head_map(v), mdo = head_map(dout);
-  static bool configured = false;
-  if (!configured) {
+  static bool configured[kMaxDevices] = {};  // per device: the attributes are set on the current one
+  if (!configured[current_device_index()]) {
     cudaFuncSetAttribute(flash_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dqk::kSmemBytes);
     cudaFuncSetAttribute(flash_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dkv::kSmemBytes);
-    configured = true;
+    configured[current_device_index()] = true;
   }
   int dev, sms;
   cudaGetDevice(&dev);

@@ -1162,10 +1162,10 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, void* c, const 
                    int ldc, int ldr, int* err, cudaStream_t st, bool streamk = false) {
   auto kern = gemm_bf16_kernel<BN, A_MN, B_MN, EPI>;
   constexpr int smem = Cfg<BN>::kSmemBytes;
-  static bool configured = false;  // one static per instantiation
-  if (!configured) {
+  static bool configured[kMaxDevices] = {};  // per instantiation and device
+  if (!configured[current_device_index()]) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    configured = true;
+    configured[current_device_index()] = true;
   }
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   // stream-K: every SM takes a share of the tiles x K-blocks iterations (at least one each)
@@ -1219,7 +1219,8 @@ static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, void* c, c
                         const PeerAG* ag = nullptr) {
   auto kern = gemm_pair_kernel<A_MN, B_MN, EPI, kPeer>;
   constexpr int smem = pair::kSmemBytes;
-  static int max_clusters = 0;  // one static per instantiation
+  static int max_clusters_dev[kMaxDevices] = {};  // per instantiation and device
+  int& max_clusters = max_clusters_dev[current_device_index()];
   if (!max_clusters) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     max_clusters = pair_clusters(kern, smem, kPeer ? kPeerThreads : kThreads);
@@ -1281,10 +1282,10 @@ static void launch_swiglu(const CUtensorMap& ta, const CUtensorMap& tb, __nv_bfl
   }
   auto kern = gemm_bf16_kernel<256, false, false, kSwiGLU>;
   constexpr int smem = Cfg<256>::kSmemBytes;
-  static bool configured = false;
-  if (!configured) {
+  static bool configured[kMaxDevices] = {};  // per device
+  if (!configured[current_device_index()]) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    configured = true;
+    configured[current_device_index()] = true;
   }
   const int tiles = ((M + BM - 1) / BM) * (F / 128);
   const int grid = tiles < num_sms() ? tiles : num_sms();

@@ -67,7 +67,7 @@ def merge_dicts(base: dict, override: dict) -> dict:
 def read_config_file(path: str) -> dict:
     """Read a .yaml/.yml/.json file into a dict."""
     if not os.path.isfile(path):
-        raise FileNotFoundError(f"Configuration file does not exist: {path}")
+        raise FileNotFoundError(f"config file not found: {path}")
     suffix = os.path.splitext(path)[1].lower()
     with open(path, "r", encoding="utf-8") as handle:
         if suffix in (".yaml", ".yml"):
@@ -76,7 +76,7 @@ def read_config_file(path: str) -> dict:
             return yaml.safe_load(handle) or {}
         if suffix == ".json":
             return json.load(handle)
-    raise ValueError(f"Unsupported configuration file format: '{suffix}', use .yaml / .yml / .json")
+    raise ValueError(f"cannot read a {suffix or 'suffix-less'} config file ({path}): expected YAML or JSON")
 
 
 def _abs_from(path: str, directory: str) -> str:
@@ -96,7 +96,7 @@ def compose_config_dict(raw: dict, directory: str, visited: Optional[set] = None
     if base is not None:
         base_path = _abs_from(base, directory)
         if base_path in visited:
-            raise ValueError(f"Detected a cyclic configuration reference: {base_path}")
+            raise ValueError(f"base_config chain loops back to {base_path} (cyclic config inheritance)")
         visited.add(base_path)
         result = compose_config_dict(read_config_file(base_path), os.path.dirname(base_path), visited)
     for include_key, section in (("hardware_config", "hardware"), ("model_arch_config", "model_arch")):
@@ -798,12 +798,8 @@ def load_config(config_path: Optional[str] = None) -> AsyncRLConfig:
     """Load from an explicit path or ``$ASYNC_RL_CONFIG``."""
     path = config_path or os.environ.get("ASYNC_RL_CONFIG")
     if not path:
-        raise ValueError(
-            "No configuration file was specified. Provide one using one of the following methods:\n"
-            "  1. function argument: load_config('configs/gsm8k.yaml')\n"
-            "  2. command line: python train.py --config configs/gsm8k.yaml\n"
-            "  3. environment variable: export ASYNC_RL_CONFIG=configs/gsm8k.yaml"
-        )
+        raise ValueError("no config given: pass a path to load_config(), --config on the command line, or set "
+                         "ASYNC_RL_CONFIG")
     return AsyncRLConfig.from_file(path)
 
 

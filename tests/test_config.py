@@ -66,7 +66,7 @@ def test_merge_and_roundtrip(tmp_path):
 
 def test_load_config_requires_path(monkeypatch):
     monkeypatch.delenv("ASYNC_RL_CONFIG", raising=False)
-    with pytest.raises(ValueError, match="No configuration file"):
+    with pytest.raises(ValueError, match="no config given"):
         load_config(None)
 
 

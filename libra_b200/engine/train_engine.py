@@ -265,6 +265,13 @@ class B200TrainEngine:
             enable_fused_sequence_parallel(self.tp_group, (rows + m - 1) // m * m, [self.cfg.hidden_size], [], dev)
         from libra_b200.parallel.tensor_parallel import tp_partial_grad_params
 
+        if (self.tp_size > 1 and dev.type == "cuda" and dist.get_backend(self.tp_group) == "nccl"
+                and os.environ.get("LIBRA_TP_PEER_LOGPROB", "1") != "0"):
+            # the LM head's per-row shard statistics are exchanged over peer memory (one kernel, no NCCL)
+            from libra_b200.parallel.tensor_parallel import enable_peer_logprob_exchange
+
+            enable_peer_logprob_exchange(self.tp_group, max(self.max_tokens_per_micro_batch,
+                                                            self.max_tokens_per_recompute_batch), dev)
         self._tp_partial = [self.params[n].main_grad for n in tp_partial_grad_params(
             list(self.params), self.sequence_parallel)] if self.tp_size > 1 else []
         # replicated (1-D) parameters inside this rank's optimizer shard: the

@@ -35,6 +35,9 @@ void adamw_step_allgather(torch::Tensor master, torch::Tensor grad, torch::Tenso
                           c10::optional<torch::Tensor> sq_norm, double max_norm, double grad_scale,
                           std::vector<int64_t> param_peers, std::vector<int64_t> flag_peers, int64_t me, int64_t epoch,
                           torch::Tensor err, int64_t grid_ctas);
+std::vector<torch::Tensor> vocab_stats_exchange(std::vector<int64_t> data_ptrs, std::vector<int64_t> flag_ptrs,
+                                                int64_t me, int64_t max_rows, torch::Tensor m, torch::Tensor s,
+                                                torch::Tensor zt, int64_t epoch, torch::Tensor err);
 void grad_reduce_scatter_peer(torch::Tensor out, double scale, c10::optional<torch::Tensor> sq_out,
                               std::vector<int64_t> src_peers, std::vector<int64_t> flag_peers, int64_t me,
                               int64_t epoch, torch::Tensor err, int64_t grid_ctas);
@@ -138,6 +141,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &libra::adamw_step);
   m.def("adamw_step_allgather", &libra::adamw_step_allgather,
         "AdamW on this rank's shard with the bf16 result stored into every rank's parameter buffer");
+  m.def("vocab_stats_exchange", &libra::vocab_stats_exchange,
+        "vocab-parallel log-softmax: per-row (max, sum-exp, target logit) exchange over peer memory -> (lse, target)");
   m.def("grad_reduce_scatter_peer", &libra::grad_reduce_scatter_peer,
         "distributed-optimizer gradient reduce-scatter over peer memory, fused with 1/dp scaling and the global "
         "sum of squares");

@@ -125,8 +125,66 @@ def vocab_parallel_embedding(tokens, w_local, group, rank, reduce: bool = True):
     return _VocabParallelEmbedding.apply(tokens, w_local, group, rank, reduce)
 
 
+class PeerLogprobExchange:
+    """The vocab-parallel log-softmax's per-row (max, sum-exp, target logit)
+    exchange in one kernel over NVLink peer memory (``vocab_stats_exchange`` in
+    ``ops/csrc/vocab_exchange.cu``) instead of two NCCL all-reduces.  Each rank
+    of the TP group maps every rank's exchange area (CUDA IPC); calls are
+    collective and in the same order on every rank."""
+
+    MAX_RANKS, MAX_CTAS = 8, 256
+
+    def __init__(self, group, max_rows: int, device):
+        from libra_b200.parallel.peer_grad_reduce import map_peer_tensors
+
+        self.group = group
+        self.n, self.me = _ws(group), _rank(group)
+        if self.n > self.MAX_RANKS:
+            raise ValueError(f"at most {self.MAX_RANKS} ranks")
+        self.max_rows = int(max_rows)
+        self.data = torch.zeros(2 * self.MAX_RANKS * self.max_rows * 4, dtype=torch.float32, device=device)
+        self.flags = torch.zeros(self.MAX_CTAS * self.MAX_RANKS, dtype=torch.int32, device=device)
+        (self.data_ptrs, self.flag_ptrs), self._opened = map_peer_tensors(group, [self.data, self.flags], self.n,
+                                                                          self.me)
+        self.calls = 0
+        if self.n > 1:
+            torch.cuda.synchronize(device)
+            dist.barrier(group=group)
+
+    def close(self) -> None:
+        for b in self._opened:
+            ops.ext().ipc_close(b)
+        self._opened = []
+
+    def __call__(self, stats_m, stats_s, zt):
+        lse, z = ops.ext().vocab_stats_exchange(self.data_ptrs, self.flag_ptrs, self.me, self.max_rows,
+                                                stats_m.float().contiguous(), stats_s.float().contiguous(),
+                                                zt.float().contiguous(), self.calls + 1, ops.error_flag(zt.device))
+        self.calls += 1
+        return lse, z
+
+
+_LOGPROB_EXCHANGE: dict = {}
+
+
+def enable_peer_logprob_exchange(group, max_rows: int, device) -> None:
+    """Collective over the TP group: route the vocab-parallel logprob's shard
+    statistics through the peer-memory exchange for up to ``max_rows`` rows."""
+    if id(group) not in _LOGPROB_EXCHANGE:
+        _LOGPROB_EXCHANGE[id(group)] = PeerLogprobExchange(group, max_rows, device)
+
+
+def disable_peer_logprob_exchange() -> None:
+    for x in _LOGPROB_EXCHANGE.values():
+        x.close()
+    _LOGPROB_EXCHANGE.clear()
+
+
 def _combine(stats_m, stats_s, zt, group):
     """Global (lse, target logit) from per-shard (max, sum-exp, target logit)."""
+    x = _LOGPROB_EXCHANGE.get(id(group)) if stats_m.is_cuda else None
+    if x is not None and stats_m.numel() <= x.max_rows:
+        return x(stats_m, stats_s, zt)
     M = stats_m.clone()
     if _ws(group) > 1:
         dist.all_reduce(M, op=dist.ReduceOp.MAX, group=group)

@@ -30,10 +30,22 @@ def main():
     ap.add_argument("--log-dir", default="")
     ap.add_argument("--stats-out", default="")
     ap.add_argument("--eval-interval", type=int, default=-1, help="override eval_interval (-1 = keep the config's)")
+    ap.add_argument("--train-tp", type=int, default=0, help="override train_tp_size")
+    ap.add_argument("--train-pp", type=int, default=0, help="override train_pp_size")
     ap.add_argument("--replan-every", type=int, default=0,
                     help="turn on the Global Resource Planner with online replanning every N steps")
     a = ap.parse_args()
     cfg = load_config(a.config)
+    if a.train_tp or a.train_pp:
+        from libra_b200.config import AsyncRLConfig
+
+        d = cfg.to_dict()
+        d.update(train_dp_size=0, tp_size=0)
+        if a.train_tp:
+            d["train_tp_size"] = a.train_tp
+        if a.train_pp:
+            d["train_pp_size"] = a.train_pp
+        cfg = AsyncRLConfig.from_dict(d)  # validated and derived again (data-parallel size)
     if a.replan_every > 0:
         p = cfg.global_resource_planner
         p.enabled, p.initial_allocation_strategy = True, "configured"

@@ -394,11 +394,23 @@ class B200TrainEngine:
         dist.broadcast(acc, src=self.pp_last, group=self.pp_group)
 
     def export_params(self) -> Dict[str, torch.Tensor]:
-        """Every parameter of the model for an export (HF weights for rollout):
-        with pipeline stages, the stages of the first data-parallel replica
-        send theirs to its first stage (collective over that pipeline; the
-        other replicas return their own subset)."""
+        """Every parameter of the full (unsharded) model for an export (HF weights
+        for rollout, an in-process rollout engine): tensor-parallel shards are
+        gathered to the replica's first TP rank and merged; pipeline stages send
+        theirs to the first stage.  Collective over the first data-parallel
+        replica's TP or pipeline group; other ranks return their own tensors."""
         local = {k: v.detach() for k, v in self.params.items()}
+        if self.tp_size > 1:
+            if self.mesh.coords(dist.get_rank()).dp != 0:
+                return local
+            first = dist.get_global_rank(self.tp_group, 0)
+            parts = [None] * self.tp_size if self.tp_rank == 0 else None
+            dist.gather_object({k: v.cpu() for k, v in local.items()}, parts, dst=first, group=self.tp_group)
+            if self.tp_rank != 0:
+                return local
+            from libra_b200.parallel.tensor_parallel import merge_tp_shards
+
+            return merge_tp_shards(parts, self.cfg, self.tp_size)
         if self.pp_size <= 1 or self.mesh.coords(dist.get_rank()).dp != 0:
             return local
         parts = [None] * self.pp_size if self.pp_rank == 0 else None

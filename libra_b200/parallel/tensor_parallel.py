@@ -326,6 +326,45 @@ def shard_full_params(full: dict, cfg, tp_size: int, tp_rank: int) -> dict:
     return {k: v.contiguous() for k, v in out.items()}
 
 
+def merge_tp_shards(parts: list, cfg, tp_size: int) -> dict:
+    """Inverse of ``shard_full_params``: full (TP=1) tensors from the TP ranks'
+    local dicts (``parts[r]`` = rank r's).  KV heads replicated over several
+    ranks (tp > kv heads) are taken once."""
+    if tp_size == 1:
+        return dict(parts[0])
+    D = cfg.head_dim
+    nq, nkv = cfg.num_attention_heads, cfg.num_key_value_heads
+    nq_l, kv_l = nq // tp_size, max(1, nkv // tp_size)
+    owners = []  # first rank holding each kv group
+    for r in range(tp_size):
+        kv0 = r * nkv // tp_size
+        if not owners or owners[-1][0] != kv0:
+            owners.append((kv0, r))
+    out = {}
+    for name in parts[0]:
+        ts = [p[name] for p in parts]
+        if name.endswith("qkv_proj"):
+            q = torch.cat([t[:nq_l * D] for t in ts])
+            k = torch.cat([ts[r][nq_l * D:(nq_l + kv_l) * D] for _, r in owners])
+            v = torch.cat([ts[r][(nq_l + kv_l) * D:] for _, r in owners])
+            out[name] = torch.cat([q, k, v])
+        elif name.endswith("o_proj") or name.endswith("down_proj"):
+            out[name] = torch.cat(ts, dim=1)
+        elif name.endswith("gate_up_proj"):
+            F = ts[0].shape[0] // 2
+            out[name] = torch.cat([t[:F] for t in ts] + [t[F:] for t in ts])
+        elif name.endswith("experts.w1"):
+            F = ts[0].shape[1] // 2
+            out[name] = torch.cat([t[:, :F] for t in ts] + [t[:, F:] for t in ts], dim=1)
+        elif name.endswith("experts.w2"):
+            out[name] = torch.cat(ts, dim=2)
+        elif name in ("embed_tokens", "lm_head"):
+            out[name] = torch.cat(ts)
+        else:
+            out[name] = ts[0]  # replicated
+    return out
+
+
 def tp_partial_grad_params(names, sequence_parallel: bool = False) -> list:
     """Replicated parameters whose gradient differs per TP rank and must be
     all-reduced over the TP group: the per-head q/k norms (local heads only)

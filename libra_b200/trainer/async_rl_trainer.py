@@ -214,7 +214,8 @@ class AsyncRLTrainer:
             dev = torch.device("cuda", int(inst.gpus[0]) % torch.cuda.device_count())
         else:
             dev = eng.device
-        params = {k: v.detach().to(dev, copy=True) for k, v in eng.params.items()}
+        src = getattr(self, "_full_export", None) or {k: v.detach() for k, v in eng.params.items()}
+        params = {k: v.to(dev, copy=True) for k, v in src.items()}
         tok = load_tokenizer(self.config.tokenizer_path, eng.cfg.vocab_size)
         llm = LLMEngine(eng.cfg, params, instance_id=getattr(inst, "instance_id", "") or f"local-{dev}",
                         kv_memory_fraction=float(self.config.heterogeneous_rollout.gpu_memory_utilization) * 0.5,
@@ -295,7 +296,11 @@ class AsyncRLTrainer:
             self.train_engine.initialize(max_seq_length=self.config.max_seq_length)
         self.train_engine.set_version(self.initial_model_version)
         if self.rollout_engine is None:
+            # a TP- or pipeline-sharded trainer hands in-process rollout engines the full model (collective)
+            self._full_export = self._export_full_params() if self.config.rollout_backend in ("native", "local") \
+                else None
             self._build_rollout_engine()
+            self._full_export = None
             # TP-k server groups start from their own initialisation: give them the trainer's weights
             self._sync_tp_groups(self.initial_model_version)
         else:
@@ -440,10 +445,22 @@ class AsyncRLTrainer:
         return payload[0][int(self.train_engine.get_data_parallel_rank())]
 
     # ================================================================== weight sync
+    def _export_full_params(self):
+        """Full-model parameters when the trainer is TP- or pipeline-sharded (collective over the first
+        replica; rank 0 gets the model), else None."""
+        eng = self.train_engine
+        if int(getattr(eng, "tp_size", 1)) > 1 or int(getattr(eng, "pp_size", 1)) > 1:
+            return eng.export_params()
+        return None
+
     def _sync_weights(self, target_version: int) -> float:
         """Push the trainer's weights to every rollout instance; returns seconds."""
         t0 = time.perf_counter()
-        if self._local_engines:
+        full = self._export_full_params() if self.config.rollout_backend in ("native", "local") else None
+        if full is not None and self._local_engines:
+            for llm in self._local_engines:
+                llm.update_weights(full, version=target_version)
+        elif self._local_engines:
             # in-process instances: one copy of the flat buffer when the layouts match, else per tensor
             # (device-to-device; NVLink peer copies across GPUs)
             src_flat = getattr(self.train_engine, "flat_param", None)

@@ -307,3 +307,20 @@ def _pp_engine_worker(rank, world, port, out_dir, pp):
 def test_pipeline_engine_matches_one_rank(tmp_path, world, pp):
     _spawn(_pp_engine_worker, world, str(tmp_path), pp)
     assert {p.name for p in tmp_path.iterdir() if p.name.startswith("ppe_ok")} == {f"ppe_ok_{r}" for r in range(world)}
+
+
+@pytest.mark.parametrize("tp", [2, 4])
+def test_merge_tp_shards_inverts_sharding(tp):
+    """Full parameters -> per-rank TP shards -> merged again is the identity
+    (tiny has 2 KV heads, so TP=4 replicates each KV head on two ranks)."""
+    from libra_b200.models.qwen3 import get_config
+    from libra_b200.parallel.tensor_parallel import merge_tp_shards, shard_full_params
+
+    cfg, full, _ = _model_inputs()
+    parts = [shard_full_params(full, cfg, tp, r) for r in range(tp)]
+    merged = merge_tp_shards(parts, cfg, tp)
+    assert set(merged) == set(full)
+    for n, t in full.items():
+        assert torch.equal(merged[n], t), n
+    moe = get_config("tiny-moe")
+    assert moe.is_moe

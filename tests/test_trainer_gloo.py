@@ -74,3 +74,16 @@ def test_online_replanning_applies_forced_decisions(tmp_path):
     hist = glob.glob(str(tmp_path / "history" / "*history_*.jsonl"))
     rows = [json.loads(l) for l in open(hist[0]).read().splitlines()]
     assert rows[-1]["resource_config"]["rollout_gpus"] == 1
+
+
+def test_two_rank_pipeline_parallel_training(tmp_path):
+    """Two pipeline stages of one data-parallel replica: rank 0 generates the
+    batch, both stages receive the same trajectories, the update runs 1F1B."""
+    stats = _run(tmp_path, "target_token", "--train-pp", "2", steps=3)
+    assert stats["version"] == 3 and stats["n_trajectories"] == 32
+
+
+def test_two_rank_tensor_parallel_training(tmp_path):
+    """Two tensor-parallel ranks (sequence parallel) of one replica train on the same batch."""
+    stats = _run(tmp_path, "target_token", "--train-tp", "2", steps=2)
+    assert stats["version"] == 2 and stats["n_trajectories"] == 32

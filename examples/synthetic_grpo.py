@@ -32,15 +32,24 @@ def main():
     ap.add_argument("--eval-interval", type=int, default=-1, help="override eval_interval (-1 = keep the config's)")
     ap.add_argument("--train-tp", type=int, default=0, help="override train_tp_size")
     ap.add_argument("--train-pp", type=int, default=0, help="override train_pp_size")
+    ap.add_argument("--train-ep", type=int, default=0, help="override train_ep_size")
+    ap.add_argument("--model", default="", help="override model_path (a preset name) and its architecture summary")
     ap.add_argument("--replan-every", type=int, default=0,
                     help="turn on the Global Resource Planner with online replanning every N steps")
     a = ap.parse_args()
     cfg = load_config(a.config)
-    if a.train_tp or a.train_pp:
-        from libra_b200.config import AsyncRLConfig
+    if a.train_tp or a.train_pp or a.train_ep or a.model:
+        from libra_b200.config import AsyncRLConfig, read_config_file
 
         d = cfg.to_dict()
         d.update(train_dp_size=0, tp_size=0)
+        if a.train_ep:
+            d["train_ep_size"] = a.train_ep
+        if a.model:
+            d["model_path"] = a.model
+            arch = os.path.join(os.path.dirname(os.path.abspath(a.config)), "model_arch_config", f"{a.model}.yaml")
+            if os.path.exists(arch):
+                d["model_arch"] = read_config_file(arch)
         if a.train_tp:
             d["train_tp_size"] = a.train_tp
         if a.train_pp:

@@ -400,6 +400,18 @@ class B200TrainEngine:
         theirs to the first stage.  Collective over the first data-parallel
         replica's TP or pipeline group; other ranks return their own tensors."""
         local = {k: v.detach() for k, v in self.params.items()}
+        if self.ep_size > 1:
+            # experts are split over the first EP group: gather them in EP-rank order (the dense part is
+            # the same on every rank)
+            if self.dp_rank >= self.ep_size:
+                return local
+            mine = {k: v.cpu() for k, v in local.items() if is_expert_param(k)}
+            parts = [None] * self.ep_size
+            dist.all_gather_object(parts, mine, group=self.ep_group)
+            out = dict(local)
+            for k in mine:
+                out[k] = torch.cat([p[k] for p in parts]).to(local[k].device)
+            return out
         if self.tp_size > 1:
             if self.mesh.coords(dist.get_rank()).dp != 0:
                 return local

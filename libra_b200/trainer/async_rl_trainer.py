@@ -449,7 +449,8 @@ class AsyncRLTrainer:
         """Full-model parameters when the trainer is TP- or pipeline-sharded (collective over the first
         replica; rank 0 gets the model), else None."""
         eng = self.train_engine
-        if int(getattr(eng, "tp_size", 1)) > 1 or int(getattr(eng, "pp_size", 1)) > 1:
+        if int(getattr(eng, "tp_size", 1)) > 1 or int(getattr(eng, "pp_size", 1)) > 1 or \
+                int(getattr(eng, "ep_size", 1)) > 1:
             return eng.export_params()
         return None
 

@@ -87,3 +87,11 @@ def test_two_rank_tensor_parallel_training(tmp_path):
     """Two tensor-parallel ranks (sequence parallel) of one replica train on the same batch."""
     stats = _run(tmp_path, "target_token", "--train-tp", "2", steps=2)
     assert stats["version"] == 2 and stats["n_trajectories"] == 32
+
+
+def test_two_rank_expert_parallel_training(tmp_path):
+    """A mixture-of-experts model with its experts split over two data-parallel
+    ranks (EP=2): each rank trains its own batch, the in-process rollout engine
+    gets every expert."""
+    stats = _run(tmp_path, "target_token", "--model", "tiny-moe", "--train-ep", "2", steps=2)
+    assert stats["version"] == 2 and stats["n_trajectories"] == 16

@@ -131,6 +131,9 @@ class B200TrainEngine:
         self._pending_hybrid_gradients: List[Any] = []
         self.elastic_update_publisher = None  # callable(reduced flat grad, step, version) for lockstep hybrids
         self.elastic_payload_wait_s = 0.0  # >0: wait this long for every active hybrid replica's payload
+        # True when the hybrid replicas trained their own shares of this replica's batch: the merged
+        # gradient is then the mean over the core and the hybrids (each already a mean over its share)
+        self.elastic_average_merged = False
 
     # ------------------------------------------------------------------ setup
     def initialize(self, max_seq_length: int = 2048) -> None:
@@ -960,6 +963,8 @@ class B200TrainEngine:
             if g.numel() != self.flat_grad.numel():
                 raise ValueError(f"hybrid payload has {g.numel()} elements, expected {self.flat_grad.numel()}")
             self.flat_grad.add_(g.to(device=self.flat_grad.device, dtype=torch.float32).view(-1))
+        if used and self.elastic_average_merged:
+            self.flat_grad.div_(1 + len(used))
         return len(used)
 
     def _wait_for_hybrid_payloads(self, step: int, timeout_s: float) -> bool:

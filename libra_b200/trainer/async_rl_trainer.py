@@ -89,6 +89,7 @@ class AsyncRLTrainer:
         self.rollout_engine = rollout_engine
         self._local_engines: List[Any] = []
         self._tp_groups: List[Any] = []  # TP-k rollout buckets running as server process groups
+        self.last_hybrid_dispatch: Optional[Dict[str, Any]] = None  # the latest batch share given to hybrids
         self.staleness_manager: Optional[StalenessManager] = None
         self.async_runner: Optional[AsyncTaskRunner] = None
         self.dispatcher: Optional[BatchTaskDispatcher] = None
@@ -444,6 +445,45 @@ class AsyncRLTrainer:
         dist.broadcast_object_list(payload, src=0)
         return payload[0][int(self.train_engine.get_data_parallel_rank())]
 
+    # ================================================================== elastic hybrid replicas
+    def _dispatch_hybrid(self, batch, step: int):
+        """Share this replica's batch with its active hybrid replicas (Elastic
+        Hybrid Pool): whole GRPO groups are dealt round-robin between the core
+        and each hybrid, every hybrid gets its share as a task file, and the
+        core trains the rest; before the optimizer step the engine waits
+        (bounded) for the hybrids' gradients and averages them with its own.
+        Returns the core's share (the whole batch when no hybrid is active)."""
+        eng = self.train_engine
+        dom = getattr(eng, "elastic_gradient_domain", None)
+        if dom is None or not batch:
+            return batch
+        hybrids = list(dom.active_hybrid_ids_for_core(f"dp{eng.get_data_parallel_rank()}"))
+        if not hybrids:
+            eng.elastic_payload_wait_s, eng.elastic_average_merged = 0.0, False
+            return batch
+        from libra_b200.infra.elastic.worker import write_task
+
+        groups: Dict[Any, List[Any]] = {}
+        for t in batch:
+            groups.setdefault(t.get("grpo_group_id", id(t)), []).append(t)
+        shares: List[List[Any]] = [[] for _ in range(len(hybrids) + 1)]
+        for i, g in enumerate(groups.values()):
+            shares[i % len(shares)].extend(g)
+        p = self.config.global_resource_planner
+        task_dir = p.hybrid_worker_task_dir
+        nxt = int(eng.step_count) + 1
+        sent = 0
+        for rid, part in zip(hybrids, shares[1:]):
+            if part:
+                write_task(task_dir, rid, nxt, part, state_version=int(eng.get_version()),
+                           membership_epoch=dom.membership_epoch(rid))
+                sent += len(part)
+        eng.elastic_payload_wait_s = float(p.hybrid_active_gradient_timeout_s)
+        eng.elastic_average_merged = True
+        self.last_hybrid_dispatch = {"step": step, "hybrids": hybrids, "core": len(shares[0]),
+                                     "hybrid_trajectories": sent}
+        return shares[0] or batch
+
     # ================================================================== weight sync
     def _export_full_params(self):
         """Full-model parameters when the trainer is TP- or pipeline-sharded (collective over the first
@@ -524,6 +564,7 @@ class AsyncRLTrainer:
             if not batch:
                 continue
             batch = self.train_engine.align_distributed_trajectories(batch)
+            batch = self._dispatch_hybrid(batch, step)
             rollout_time = time.time() - t_step
             t_adv = time.time()
             if not self._advantage_stats:

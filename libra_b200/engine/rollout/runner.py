@@ -7,9 +7,12 @@ packed into one stream, so the GEMMs (tcgen05 kernel) see every token of the
 step at once; attention is split:
 
 * decode rows -> ``paged_decode_attention`` (sm_100a kernel, KV read in place);
-* extend rows -> the sequence's KV is gathered to a contiguous buffer and run
-  through causal varlen attention with the queries aligned to the end of the
-  key range.
+* extend rows -> causal varlen attention (tcgen05 flash kernel) with the
+  queries aligned to the end of each sequence's key range.  The gather plan is
+  built once per step (``_ExtendPlan``): when every extending sequence is a
+  fresh prefill its keys are this step's K/V rows and nothing is copied from
+  the cache; otherwise one flat slot index gathers every sequence's whole key
+  range from the paged pool with one ``index_select`` per layer.
 * CPU tensors use the fp32 reference for both.
 
 Only the last position of each sequence goes through the final norm and the
@@ -51,6 +54,69 @@ def _extend_attention_ref(q, k, v, q_start: int):
     return (s.softmax(-1) @ vv).transpose(0, 1).to(q.dtype)
 
 
+@dataclass
+class _ExtendPlan:
+    """How one step's extend attention finds its queries and keys.
+
+    ``items`` are the indices of the work items with more than one new token.
+    Their queries are rows ``q_rows`` of the step's token stream, or the
+    leading ``n_q`` rows when ``q_rows`` is None.  Keys come from this step's
+    K/V at the query rows when ``key_slots`` is None (every such item starts at
+    position 0), else from the paged cache at the flat slots ``key_slots`` (the
+    whole range 0..len of each item, in item order)."""
+
+    items: List[int]
+    n_q: int
+    q_rows: Optional[torch.Tensor]
+    key_slots: Optional[torch.Tensor]
+    cu_q: List[int]
+    cu_k: List[int]
+    cu_q_dev: Optional[torch.Tensor] = None
+    cu_k_dev: Optional[torch.Tensor] = None
+    tiles: Optional[torch.Tensor] = None
+
+    def queries(self, q: torch.Tensor) -> torch.Tensor:
+        return q[:self.n_q] if self.q_rows is None else q.index_select(0, self.q_rows)
+
+    def keys(self, kv: PagedKVCache, layer: int, k: torch.Tensor, v: torch.Tensor):
+        if self.key_slots is None:
+            return self.queries(k), self.queries(v)
+        kf = kv.k[layer].view(-1, kv.kv_heads, kv.head_dim)
+        vf = kv.v[layer].view(-1, kv.kv_heads, kv.head_dim)
+        return kf.index_select(0, self.key_slots), vf.index_select(0, self.key_slots)
+
+
+def build_extend_plan(items: Sequence[WorkItem], offsets: List[int], kv: PagedKVCache, device) -> Optional[_ExtendPlan]:
+    """The extend-attention gather plan of one step (host work once per step,
+    not once per layer)."""
+    ext = [i for i, it in enumerate(items) if len(it.tokens) - it.start > 1]
+    if not ext:
+        return None
+    cu_q, cu_k, rows = [0], [0], []
+    for i in ext:
+        it = items[i]
+        n_new = len(it.tokens) - it.start
+        cu_q.append(cu_q[-1] + n_new)
+        cu_k.append(cu_k[-1] + len(it.tokens))
+        rows.extend(range(offsets[i], offsets[i] + n_new))
+    n_q = cu_q[-1]
+    contiguous = rows == list(range(n_q))
+    q_rows = None if contiguous else torch.tensor(rows, dtype=torch.long).to(device, non_blocking=True)
+    fresh = all(items[i].start == 0 for i in ext)
+    key_slots = None
+    if not fresh:
+        key_slots = torch.cat([kv.slot_mapping(items[i].seq_id, 0, len(items[i].tokens)) for i in ext])
+        key_slots = key_slots.to(device, non_blocking=True)
+    plan = _ExtendPlan(ext, n_q, q_rows, key_slots, cu_q, cu_k)
+    if torch.device(device).type == "cuda":
+        from libra_b200.ops.attention import attn_tiles
+
+        plan.cu_q_dev = torch.tensor(cu_q, dtype=torch.int32).to(device, non_blocking=True)
+        plan.cu_k_dev = torch.tensor(cu_k, dtype=torch.int32).to(device, non_blocking=True)
+        plan.tiles = attn_tiles(cu_q, True, device)
+    return plan
+
+
 class InferenceRunner:
     def __init__(self, cfg: Qwen3Config, params: Dict[str, torch.Tensor], kv_cache: PagedKVCache,
                  tp_group=None, tp_size: int = 1, max_step_tokens: int = 0):
@@ -85,11 +151,14 @@ class InferenceRunner:
     def lm_head(self):
         return self.p["embed_tokens"] if self.cfg.tie_word_embeddings else self.p["lm_head"]
 
-    def _attention(self, layer: int, q, items: Sequence[WorkItem], offsets: List[int], decode_only: bool):
+    def _attention(self, layer: int, q, k, v, items: Sequence[WorkItem], offsets: List[int]):
         dev = q.device
-        out = torch.empty_like(q)
+        plan = self._ext_plan
+        if plan is not None and plan.n_q == q.shape[0] and plan.q_rows is None:
+            out = None  # every row extends: the kernel's output is the whole result
+        else:
+            out = torch.empty_like(q)
         dec = [i for i, it in enumerate(items) if len(it.tokens) - it.start == 1]
-        ext = [i for i in range(len(items)) if i not in set(dec)]
         if dec:
             rows = torch.tensor([offsets[i] for i in dec], device=dev, dtype=torch.long)
             if dev.type == "cuda" and self.cfg.head_dim == 128:
@@ -104,37 +173,28 @@ class InferenceRunner:
                 out.index_copy_(0, rows, o)
             else:
                 for i in dec:
-                    k, v = self.kv.gather(layer, items[i].seq_id, len(items[i].tokens))
-                    out[offsets[i]:offsets[i] + 1] = _extend_attention_ref(q[offsets[i]:offsets[i] + 1], k, v,
+                    kk, vv = self.kv.gather(layer, items[i].seq_id, len(items[i].tokens))
+                    out[offsets[i]:offsets[i] + 1] = _extend_attention_ref(q[offsets[i]:offsets[i] + 1], kk, vv,
                                                                            len(items[i].tokens) - 1)
-        if ext:
-            if dev.type == "cuda" and self.cfg.head_dim == 128:
-                ks, vs, cu_q, cu_k, rows = [], [], [0], [0], []
-                for i in ext:
-                    it = items[i]
-                    k, v = self.kv.gather(layer, it.seq_id, len(it.tokens))
-                    ks.append(k)
-                    vs.append(v)
-                    n_new = len(it.tokens) - it.start
-                    cu_q.append(cu_q[-1] + n_new)
-                    cu_k.append(cu_k[-1] + len(it.tokens))
-                    rows.append(torch.arange(offsets[i], offsets[i] + n_new, device=dev))
-                rows_t = torch.cat(rows)
-                from libra_b200.ops.attention import attn_tiles
-
-                # queries are the new suffix of each sequence; keys span the whole (cached) prefix
-                o, _ = ops.ext().flash_fwd(q.index_select(0, rows_t).contiguous(), torch.cat(ks).contiguous(),
-                                           torch.cat(vs).contiguous(), torch.tensor(cu_q, device=dev, dtype=torch.int32),
-                                           attn_tiles(cu_q, True, dev), self.scale, True, ops.error_flag(dev),
-                                           torch.tensor(cu_k, device=dev, dtype=torch.int32))
-                out.index_copy_(0, rows_t, o)
-            else:
-                for i in ext:
-                    it = items[i]
-                    n_new = len(it.tokens) - it.start
-                    k, v = self.kv.gather(layer, it.seq_id, len(it.tokens))
-                    out[offsets[i]:offsets[i] + n_new] = _extend_attention_ref(q[offsets[i]:offsets[i] + n_new],
-                                                                               k, v, it.start)
+        if plan is None:
+            return out
+        qe = plan.queries(q)
+        ke, ve = plan.keys(self.kv, layer, k, v)
+        if dev.type == "cuda" and self.cfg.head_dim == 128:
+            # queries are the new suffix of each sequence; keys span the whole (cached) prefix
+            o, _ = ops.ext().flash_fwd(qe.contiguous(), ke.contiguous(), ve.contiguous(), plan.cu_q_dev,
+                                       plan.tiles, self.scale, True, ops.error_flag(dev), plan.cu_k_dev)
+        else:
+            o = torch.empty_like(qe)
+            for j, i in enumerate(plan.items):
+                a, b, c, d = plan.cu_q[j], plan.cu_q[j + 1], plan.cu_k[j], plan.cu_k[j + 1]
+                o[a:b] = _extend_attention_ref(qe[a:b], ke[c:d], ve[c:d], items[i].start)
+        if out is None:
+            return o
+        if plan.q_rows is None:
+            out[:plan.n_q] = o
+        else:
+            out.index_copy_(0, plan.q_rows, o)
         return out
 
     @torch.no_grad()
@@ -157,7 +217,7 @@ class InferenceRunner:
         last_rows = torch.tensor([o + len(it.tokens) - it.start - 1 for o, it in zip(offsets, items)],
                                  dtype=torch.long).to(dev, non_blocking=True)
         self._tables = {}
-        decode_only = all(len(it.tokens) - it.start == 1 for it in items)
+        self._ext_plan = build_extend_plan(items, offsets, self.kv, dev)
         dec_items = [it for it in items if len(it.tokens) - it.start == 1]
         self._lens_dec = torch.tensor([len(it.tokens) for it in dec_items], dtype=torch.int32).to(dev)
         self._max_len_dec = max((len(it.tokens) for it in dec_items), default=1)
@@ -180,7 +240,7 @@ class InferenceRunner:
                 q, k, v = ops.qk_norm_rope(qkv, p[pre + "q_norm"], p[pre + "k_norm"], pos_t, self.cos, self.sin,
                                            self.nq, self.nkv, cfg.rms_norm_eps)
                 self.kv.write(layer, slot_t, k, v)
-                attn = self._attention(layer, q, items, offsets, decode_only)
+                attn = self._attention(layer, q, k, v, items, offsets)
                 ops.gemm(attn.reshape(attn.shape[0], -1), p[pre + "o_proj"], out=peer.partial(x.shape[0]))
                 x, h = peer.reduce_add_rmsnorm(x, p[pre + "post_attention_layernorm"], cfg.rms_norm_eps)
                 ops.gemm(ops.linear_swiglu(h, p[pre + "gate_up_proj"]), p[pre + "down_proj"],
@@ -196,7 +256,7 @@ class InferenceRunner:
             q, k, v = ops.qk_norm_rope(qkv, p[pre + "q_norm"], p[pre + "k_norm"], pos_t, self.cos, self.sin,
                                        self.nq, self.nkv, cfg.rms_norm_eps)
             self.kv.write(layer, slot_t, k, v)
-            attn = self._attention(layer, q, items, offsets, decode_only)
+            attn = self._attention(layer, q, k, v, items, offsets)
             x = self._row_parallel(attn.reshape(attn.shape[0], -1), p[pre + "o_proj"], x)
             h = ops.rmsnorm(x, p[pre + "post_attention_layernorm"], cfg.rms_norm_eps)
             if cfg.is_moe:

@@ -160,3 +160,42 @@ def test_hetero_pool_migrates_kv_with_the_request(tiny):
     assert engines[1].engine.kv.cached_blocks(ctx)
     for e in engines:
         e.engine.shutdown()
+
+
+def test_runner_mixed_step_matches_full_forward(tiny):
+    """One runner step over a decode row, an extend with a cached prefix and a
+    fresh prefill, in that order (the extend queries are not the leading rows
+    and their keys come from the paged cache): the last-position logits equal
+    a full recompute of each sequence."""
+    from libra_b200.engine.rollout.runner import InferenceRunner, WorkItem, build_extend_plan
+
+    cfg = tiny.cfg
+    kv = PagedKVCache(cfg.num_hidden_layers, 64, 4, cfg.num_key_value_heads, cfg.head_dim, "cpu")
+    run = InferenceRunner(cfg, tiny.params, kv)
+    a, b = list(range(3, 14)), list(range(50, 59))
+    run.step([WorkItem("a", a, 0), WorkItem("b", b, 0)])  # fill the cache for both
+    a2, b2, c = a + [21], b + [7, 8, 9, 10], list(range(80, 87))
+    items = [WorkItem("a", a2, len(a)), WorkItem("b", b2, len(b)), WorkItem("c", c, 0)]
+    got = run.step(items).float()
+    plan = build_extend_plan(items, [0, 1, 5], kv, "cpu")
+    assert plan.items == [1, 2] and plan.q_rows is not None and plan.key_slots is not None
+    assert plan.cu_q == [0, 4, 11] and plan.cu_k == [0, len(b2), len(b2) + len(c)]
+    for row, seq in enumerate((a2, b2, c)):
+        want = tiny.model.logits(pack_sequences([torch.tensor(seq)]))[-1].float()
+        torch.testing.assert_close(got[row], want, rtol=2e-2, atol=2e-2)
+
+
+def test_extend_plan_fresh_prefill_reads_no_cache():
+    """Fresh prefills only: queries are the leading rows and the keys are the
+    step's own K/V (no slot gather)."""
+    from libra_b200.engine.rollout.runner import WorkItem, build_extend_plan
+
+    kv = PagedKVCache(1, 16, 4, 1, 8, "cpu")
+    items = [WorkItem("x", [1, 2, 3], 0), WorkItem("y", [4, 5, 6, 7, 8], 0)]
+    for it in items:
+        kv.reserve(it.seq_id, len(it.tokens))
+    plan = build_extend_plan(items, [0, 3], kv, "cpu")
+    assert plan.q_rows is None and plan.key_slots is None and plan.n_q == 8
+    k = torch.arange(8.0).view(8, 1, 1)
+    assert torch.equal(plan.keys(kv, 0, k, k)[0], k)
+    assert build_extend_plan([WorkItem("x", [1, 2], 1)], [0], kv, "cpu") is None

@@ -9,13 +9,21 @@ and ``docs/megatron_core_backend.md:30-39``)::
     <sync_path>/v<N>/megatron_checkpoint_manifest.json
     <sync_path>/v<N>/sync_progress/rank_<R>.json
 
-The sharded state dict uses Megatron-Core GPT key names
-(``decoder.layers.{i}.self_attention.linear_qkv.weight`` ...), with the QKV
-rows in Megatron's per-query-group order ``[group][q heads of group, k, v]``
-(this engine keeps them as ``[all q | all k | all v]``; ``mcore_qkv_rows``
-is the row permutation).  fc1 is ``[gate; up]`` in both.  Optimizer state is
-the distributed-optimizer layout: every DP rank saves its flat fp32 shard of
-master weights and Adam moments (``optimizer.shard_<r>.*``) plus the step.
+``megatron_dist`` holds Megatron-Core's model-space layout (``mcore_layout``):
+one DCP tensor per parameter kind in its global shape, layers stacked on a
+leading axis (``decoder.layers.self_attention.linear_qkv.weight`` is
+``[layers, (q + 2 kv) * head_dim, hidden]`` with the rows per query group),
+tensor-parallel and expert-parallel ranks writing their chunks at global
+offsets, and the distributed optimizer's fp32 master weights and Adam moments
+under ``optimizer.state.{fp32_param,exp_avg,exp_avg_sq}.<key>`` in the same
+shapes.  A checkpoint written at one TP/PP/EP/DP layout loads at another: each
+rank reads the chunks it needs.  Non-tensor state (iteration, optimizer step
+and hyper-parameters) is in ``common.pt``; ``metadata.json`` names the
+backends, as Megatron-Core's loader expects.
+
+``to_mcore`` / ``from_mcore`` are the per-layer state-dict names of the same
+tensors for one unsharded model (QKV in per-group order, fc1 ``[gate; up]``,
+GroupedMLP expert-major ``weight1`` / ``weight2``).
 """
 
 from __future__ import annotations
@@ -30,6 +38,8 @@ from typing import Any, Dict, Optional
 import torch
 import torch.distributed as dist
 
+from libra_b200.engine.mcore_layout import (OPTIM_KINDS, ChunkLoadPlanner, ChunkSavePlanner, ShardInfo,
+                                            model_space_items)
 from libra_b200.models.qwen3 import Qwen3Config
 
 
@@ -65,16 +75,124 @@ def mcore_qkv_rows(cfg: Qwen3Config, nq: Optional[int] = None, nkv: Optional[int
     return torch.tensor(rows, dtype=torch.long)
 
 
-def _optim_prefix(engine, dp_rank: int) -> str:
-    """Key prefix of one data-parallel shard of the optimizer state; tensor-
-    parallel ranks and pipeline stages hold different parameters, so each has
-    its own shards."""
-    pre = "optimizer."
-    if int(getattr(engine, "tp_size", 1)) > 1:
-        pre += f"tp{int(engine.tp_rank)}."
-    if int(getattr(engine, "pp_size", 1)) > 1:
-        pre += f"pp{int(engine.pp_rank)}."
-    return f"{pre}shard_{dp_rank}"
+MCORE_METADATA = {"sharded_backend": "torch_dist", "sharded_backend_version": 1,
+                  "common_backend": "torch", "common_backend_version": 1}
+
+
+def _shard_info(engine) -> ShardInfo:
+    return ShardInfo(tp_size=int(getattr(engine, "tp_size", 1)), tp_rank=int(getattr(engine, "tp_rank", 0)),
+                     ep_size=int(getattr(engine, "ep_size", 1)), ep_rank=int(getattr(engine, "ep_rank", 0)))
+
+
+def _param_group(engine) -> Dict[str, Any]:
+    o = engine.optim
+    return {"step": int(engine.step_count), "lr": float(o.lr), "betas": tuple(o.betas), "eps": float(o.eps),
+            "weight_decay": float(o.weight_decay), "max_grad_norm": float(o.max_grad_norm)}
+
+
+_STATE_NAMES = {"fp32_param": "master", "exp_avg": "exp_avg", "exp_avg_sq": "exp_avg_sq"}
+_EXPERT_NAMES = {"fp32_param": "x_master", "exp_avg": "x_m", "exp_avg_sq": "x_v"}
+
+
+def _dense_params(engine):
+    """(name, shape, start, end) in the flat buffer of the parameters that the
+    distributed optimizer shards over the data-parallel group, by offset."""
+    out = []
+    for name, p in engine.params.items():
+        a = engine.layout.offsets[name]
+        if a < engine.dense_numel:
+            out.append((name, tuple(p.shape), a, a + p.numel()))
+    return sorted(out, key=lambda x: x[2])
+
+
+def _expert_state(engine) -> Dict[str, Dict[str, torch.Tensor]]:
+    """This rank's expert parameters' optimizer state (held whole by every rank
+    with those experts), as parameter-shaped views."""
+    out = {k: {} for k in OPTIM_KINDS}
+    if getattr(engine, "x_master", None) is None:
+        return out
+    for name, p in engine.params.items():
+        a = engine.layout.offsets[name]
+        if a >= engine.dense_numel:
+            for kind, attr in _EXPERT_NAMES.items():
+                out[kind][name] = getattr(engine, attr)[a - engine.dense_numel:a - engine.dense_numel + p.numel()] \
+                    .view(p.shape)
+    return out
+
+
+def _optimizer_state_for_save(engine) -> Dict[str, Dict[str, torch.Tensor]]:
+    """kind -> {parameter name -> full local (TP/EP-shard) state tensor} for the
+    parameters this rank writes.  A parameter inside one data-parallel shard is
+    written by that shard's rank; one that straddles shards is assembled on the
+    rank holding its first element from the pieces of the others (point-to-point
+    over the data-parallel group; every rank walks the same list in order)."""
+    state = engine.optimizer_state_tensors()
+    out = _expert_state(engine)
+    S, s0 = engine.shard_numel, engine.shard_start
+    me = engine.get_data_parallel_rank()
+    if not engine.sharded:
+        if me == 0:
+            for name, shape, a, b in _dense_params(engine):
+                for kind, attr in _STATE_NAMES.items():
+                    out[kind][name] = state[attr][a:b].view(shape)
+        return out
+    group = engine.dp_group
+    xdev = engine.device if dist.get_backend(group) == "nccl" else torch.device("cpu")
+    for name, shape, a, b in _dense_params(engine):
+        r0, r1 = a // S, (b - 1) // S
+        if r0 == r1:
+            if me == r0:
+                for kind, attr in _STATE_NAMES.items():
+                    out[kind][name] = state[attr][a - s0:b - s0].view(shape)
+            continue
+        if me == r0:
+            buf = torch.empty(3, b - a, dtype=torch.float32, device=xdev)
+            for j, attr in enumerate(_STATE_NAMES.values()):
+                buf[j, :(r0 + 1) * S - a].copy_(state[attr][a - s0:])
+        for r in range(r0 + 1, r1 + 1):
+            lo, hi = max(a, r * S), min(b, (r + 1) * S)
+            if me == r:
+                piece = torch.stack([state[attr][lo - s0:hi - s0].float().to(xdev) for attr in _STATE_NAMES.values()])
+                dist.send(piece, group=group, group_dst=r0)
+            elif me == r0:
+                piece = torch.empty(3, hi - lo, dtype=torch.float32, device=xdev)
+                dist.recv(piece, group=group, group_src=r)
+                buf[:, lo - a:hi - a].copy_(piece)
+        if me == r0:
+            for j, (kind, attr) in enumerate(_STATE_NAMES.items()):
+                out[kind][name] = buf[j].to(state[attr].dtype).view(shape)
+    return out
+
+
+class _OptimizerLoad:
+    """Load targets for the optimizer state: parameter-shaped views into this
+    rank's shard for parameters inside it, temporaries for parameters that
+    straddle its edges (their overlap is copied in by ``finish``)."""
+
+    def __init__(self, engine):
+        self.engine = engine
+        self.state = engine.optimizer_state_tensors()
+        self.targets = _expert_state(engine)
+        self.partial = []
+        S, s0 = engine.shard_numel, engine.shard_start
+        for name, shape, a, b in _dense_params(engine):
+            lo, hi = max(a, s0), min(b, s0 + S)
+            if lo >= hi:
+                continue
+            for kind, attr in _STATE_NAMES.items():
+                src = self.state[attr]
+                if lo == a and hi == b:
+                    self.targets[kind][name] = src[a - s0:b - s0].view(shape)
+                else:
+                    t = torch.zeros(shape, dtype=src.dtype, device=src.device)
+                    self.targets[kind][name] = t
+                    self.partial.append((attr, t, lo - a, hi - a, lo - s0))
+
+    def finish(self) -> None:
+        for attr, t, x0, x1, d0 in self.partial:
+            self.state[attr][d0:d0 + x1 - x0].copy_(t.reshape(-1)[x0:x1])
+        if getattr(self.engine, "_offload_k", 0):
+            self.engine.load_optimizer_state_tensors(self.state)
 
 
 def to_mcore(params: Dict[str, torch.Tensor], cfg: Qwen3Config) -> Dict[str, torch.Tensor]:
@@ -266,18 +384,20 @@ class DistributedCheckpointManager:
             self._progress(vdir, version, "dist_checkpoint_skipped")
         else:
             self._progress(vdir, version, "before_sharded_state_dict")
-            sd: Dict[str, Any] = {"checkpoint_version": 3.0, "iteration": int(version)}
-            sd.update({f"model.{k}": v for k, v in to_mcore(params, cfg).items()})
-            if include_optimizer and getattr(engine, "master", None) is not None:
-                r = engine.get_data_parallel_rank() if engine.sharded else 0
-                if engine.sharded or engine.get_data_parallel_rank() == 0:
-                    state = engine.optimizer_state_tensors() if hasattr(engine, "optimizer_state_tensors") else \
-                        {"master": engine.master, "exp_avg": engine.exp_avg, "exp_avg_sq": engine.exp_avg_sq}
-                    for n, t in state.items():
-                        sd[f"{_optim_prefix(engine, r)}.{n}"] = t
-                sd["optimizer.step"] = torch.tensor(engine.step_count)
+            info = _shard_info(engine)
+            chunks = model_space_items(params, cfg, info)
+            with_optim = include_optimizer and getattr(engine, "master", None) is not None
+            if with_optim:
+                for kind, tensors in _optimizer_state_for_save(engine).items():
+                    chunks.update(model_space_items(tensors, cfg, info, prefix=f"optimizer.state.{kind}."))
             self._progress(vdir, version, "before_dist_checkpoint_save")
-            dcp.save(sd, checkpoint_id=str(ddir))
+            dcp.save({}, checkpoint_id=str(ddir), planner=ChunkSavePlanner(chunks))
+            if _rank() == 0:
+                common = {"checkpoint_version": 3.0, "iteration": int(version)}
+                if with_optim:
+                    common["optimizer"] = {"param_groups": [_param_group(engine)]}
+                torch.save(common, ddir / "common.pt")
+                _write_json(ddir / "metadata.json", MCORE_METADATA)
             _barrier()
             self._progress(vdir, version, "after_dist_checkpoint_save")
         if export_for_rollout and hasattr(engine, "export_params"):
@@ -296,7 +416,8 @@ class DistributedCheckpointManager:
                 version=int(version), checkpoint_format=self.checkpoint_format,
                 distributed_checkpoint="" if export_only else str(ddir),
                 rollout_export=str(vdir) if export_for_rollout else "", world_size=_world(),
-                tensor_parallel_size=int(getattr(engine, "tp_size", 1)), pipeline_parallel_size=1,
+                tensor_parallel_size=int(getattr(engine, "tp_size", 1)),
+                pipeline_parallel_size=int(getattr(engine, "pp_size", 1)),
                 context_parallel_size=1, expert_parallel_size=int(getattr(engine, "ep_size", 1)),
                 data_parallel_size=int(engine.get_data_parallel_world_size()),
                 includes_optimizer=bool(include_optimizer and not export_only), completed_at=time.time())
@@ -316,24 +437,21 @@ class DistributedCheckpointManager:
         if not (vdir / "megatron_checkpoint_manifest.json").exists():
             raise FileNotFoundError(f"Incomplete checkpoint: {vdir / 'megatron_checkpoint_manifest.json'} does not exist")
         cfg = engine.cfg
+        ddir = vdir / "megatron_dist"
+        info = _shard_info(engine)
         params = {k: v.detach() for k, v in engine.params.items()}
-        tmpl: Dict[str, Any] = {f"model.{k}": v.clone() for k, v in to_mcore(params, cfg).items()}
-        if load_optimizer and getattr(engine, "master", None) is not None:
-            r = engine.get_data_parallel_rank() if engine.sharded else 0
-            split = bool(getattr(engine, "_offload_k", 0))
-            state = engine.optimizer_state_tensors() if split else \
-                {"master": engine.master, "exp_avg": engine.exp_avg, "exp_avg_sq": engine.exp_avg_sq}
-            for n, t in state.items():
-                tmpl[f"{_optim_prefix(engine, r)}.{n}"] = t
-            tmpl["optimizer.step"] = torch.tensor(0)
-        dcp.load(tmpl, checkpoint_id=str(vdir / "megatron_dist"))
-        if load_optimizer and getattr(engine, "_offload_k", 0):
-            r = engine.get_data_parallel_rank() if engine.sharded else 0
-            engine.load_optimizer_state_tensors({n: tmpl[f"{_optim_prefix(engine, r)}.{n}"]
-                                                 for n in ("master", "exp_avg", "exp_avg_sq")})
-        from_mcore({k[len("model."):]: v for k, v in tmpl.items() if k.startswith("model.")}, params, cfg)
-        if "optimizer.step" in tmpl:
-            engine.step_count = int(tmpl["optimizer.step"])
+        chunks = model_space_items(params, cfg, info)
+        common = torch.load(ddir / "common.pt", weights_only=True) if (ddir / "common.pt").exists() else {}
+        optim = None
+        if load_optimizer and getattr(engine, "master", None) is not None and "optimizer" in common:
+            optim = _OptimizerLoad(engine)
+            for kind, tensors in optim.targets.items():
+                chunks.update(model_space_items(tensors, cfg, info, prefix=f"optimizer.state.{kind}."))
+        with torch.no_grad():
+            dcp.load({}, checkpoint_id=str(ddir), planner=ChunkLoadPlanner(chunks))
+            if optim is not None:
+                optim.finish()
+                engine.step_count = int(common["optimizer"]["param_groups"][0]["step"])
         engine.set_version(int(version))
         _barrier()
         return int(version)

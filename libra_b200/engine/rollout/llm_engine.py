@@ -449,13 +449,18 @@ class LLMEngine:
         with nvtx.nvtx_range("prefill" if admitted else "decode"):
             logits = self.runner.step(items)
         temps = torch.tensor([r.params.temperature for r in batch], device=logits.device, dtype=torch.float32)
-        if logits.device.type == "cuda" and all(r.params.top_p >= 1.0 and r.params.top_k <= 0 for r in batch):
-            # the fused sampler (same Philox stream as the captured decode steps)
+        if logits.device.type == "cuda":
+            # the fused samplers (same Philox stream as the captured decode steps)
             seeds = torch.tensor([r.seed for r in batch], dtype=torch.long).to(logits.device, non_blocking=True)
             pos = torch.tensor([r.n_tokens - 1 for r in batch], dtype=torch.long).to(logits.device, non_blocking=True)
             toks = torch.empty(len(batch), dtype=torch.long, device=logits.device)
             lps = torch.empty(len(batch), dtype=torch.float32, device=logits.device)
-            ops.sample_tokens(logits.contiguous(), temps, seeds, pos, toks, lps)
+            if all(r.params.top_p >= 1.0 and r.params.top_k <= 0 for r in batch):
+                ops.sample_tokens(logits.contiguous(), temps, seeds, pos, toks, lps)
+            else:
+                top_p = torch.tensor([r.params.top_p for r in batch], dtype=torch.float32).to(logits.device)
+                top_k = torch.tensor([r.params.top_k for r in batch], dtype=torch.long).to(logits.device)
+                ops.sample_tokens_filtered(logits.contiguous(), temps, top_p, top_k, seeds, pos, toks, lps)
         else:
             top_p = torch.tensor([r.params.top_p for r in batch], device=logits.device, dtype=torch.float32)
             top_k = torch.tensor([r.params.top_k for r in batch], device=logits.device, dtype=torch.long)

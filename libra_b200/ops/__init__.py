@@ -546,6 +546,51 @@ def sample_tokens(logits, temperature, seeds, positions, out_tok, out_lp, next_t
     return out_tok, out_lp
 
 
+def filtered_keep_mask(x: torch.Tensor, top_p: float, top_k: int) -> torch.Tensor:
+    """Tokens kept by top-k and top-p on one row of scaled logits ``x`` (fp32):
+    the k largest values and the nucleus (a token stays while the probability
+    mass strictly above it is at most ``top_p``); values tied with a threshold
+    are all kept.  The rule of ``sample_tokens_filtered``."""
+    V = x.numel()
+    thr = torch.tensor(float("-inf"))
+    if 0 < top_k < V:
+        thr = torch.maximum(thr, x.topk(top_k).values[-1])
+    if top_p < 1.0:
+        p = torch.softmax(x, -1)
+        sx, order = torch.sort(x, descending=True)
+        ps = p[order]
+        above = torch.cumsum(ps, 0) - ps
+        # ties share the mass above their first occurrence
+        first = torch.searchsorted(-sx, -sx, side="left")
+        ok = above[first] <= top_p
+        thr = torch.maximum(thr, sx[ok].min())
+    return x >= thr
+
+
+def sample_tokens_filtered(logits, temperature, top_p, top_k, seeds, positions, out_tok, out_lp):
+    """Temperature sampling restricted to the top-k tokens and the top-p
+    nucleus (thresholds by radix select on the device, then Gumbel-max over the
+    kept tokens on the Philox stream of ``sample_tokens``), with the token's
+    logprob under the unfiltered temperature-scaled distribution.
+    ``temperature <= 0`` is greedy; ``top_k <= 0`` and ``top_p >= 1`` disable
+    the filters.  Writes ``out_tok`` (int64) / ``out_lp`` (fp32)."""
+    if logits.device.type != "cuda":
+        for b in range(logits.shape[0]):
+            t = float(temperature[b])
+            x = logits[b].float() / (t if t > 0 else 1.0)
+            if t > 0:
+                keep = filtered_keep_mask(x, float(top_p[b]), int(top_k[b]))
+                g = torch.Generator().manual_seed((int(seeds[b]) * 1000003 + int(positions[b])) & 0x7FFFFFFF)
+                tok = int(torch.multinomial(torch.softmax(x.masked_fill(~keep, float("-inf")), -1), 1, generator=g))
+            else:
+                tok = int(x.argmax())
+            out_tok[b] = tok
+            out_lp[b] = x.log_softmax(-1)[tok]
+        return out_tok, out_lp
+    ext().sample_tokens_filtered(logits, temperature, top_p, top_k, seeds, positions, out_tok, out_lp)
+    return out_tok, out_lp
+
+
 def gemm_streamk(a, w, acc):
     """``acc += a . w^T`` with the stream-K mode of the tcgen05 GEMM: every SM
     takes an equal share of the tiles x K-blocks iterations, so a skinny GEMM

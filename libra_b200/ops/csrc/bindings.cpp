@@ -56,6 +56,8 @@ void paged_decode_v2(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
                      int64_t split_len, double scale);
 void sample_tokens(torch::Tensor logits, torch::Tensor temperature, torch::Tensor seeds, torch::Tensor positions,
                    torch::Tensor out_tok, torch::Tensor out_lp, c10::optional<torch::Tensor> next_tok, bool pdl);
+void sample_tokens_filtered(torch::Tensor logits, torch::Tensor temperature, torch::Tensor top_p, torch::Tensor top_k,
+                            torch::Tensor seeds, torch::Tensor positions, torch::Tensor out_tok, torch::Tensor out_lp);
 }  // namespace rollout
 namespace reshard {
 void weight_reshard(torch::Tensor items, int64_t grid);
@@ -155,6 +157,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "Gumbel-max temperature sampling with the sampled token's logprob", py::arg("logits"), py::arg("temperature"),
         py::arg("seeds"), py::arg("positions"), py::arg("out_tok"), py::arg("out_lp"), py::arg("next_tok") = py::none(),
         py::arg("pdl") = false);
+  m.def("sample_tokens_filtered", &libra::rollout::sample_tokens_filtered,
+        "top-k / top-p (nucleus) temperature sampling by radix-selected thresholds + Gumbel-max, with logprobs");
   m.def("flash_fwd", &libra::attn::flash_fwd, "tcgen05 varlen GQA attention forward", py::arg("q"), py::arg("k"),
         py::arg("v"), py::arg("cu_seqlens"), py::arg("tiles"), py::arg("scale"), py::arg("causal"), py::arg("err"),
         py::arg("cu_k") = py::none());

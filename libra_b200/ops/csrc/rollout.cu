@@ -467,5 +467,261 @@ void sample_tokens(torch::Tensor logits, torch::Tensor temperature, torch::Tenso
   LIBRA_LAUNCH_CHECK();
 }
 
+
+// ---------------------------------------------------------------------------
+// sample_tokens_filtered — temperature sampling restricted to the top-k tokens
+// and to the top-p nucleus, with the same Philox/Gumbel stream as
+// sample_tokens (unfiltered rows draw the same token from both kernels).
+//
+// Both filters keep the tokens whose scaled logit is at least a threshold, so
+// each is found by a radix select on the order-preserving 32-bit key of the
+// scaled logit, 8 bits per pass from the most significant end (4 passes):
+//   * top-k: the key of the k-th largest value (bucket counts);
+//   * top-p: the smallest key t whose "probability mass strictly above t" is
+//     at most p, the rule of the sorted cumulative-sum formulation (a token is
+//     dropped when the mass before it exceeds p); masses are summed in 2^-32
+//     fixed point so the threshold does not depend on the order of the
+//     shared-memory atomics.
+// Tokens tied with the threshold value are all kept.  The combined threshold is
+// the larger of the two; Gumbel-max then runs over the kept tokens, and the
+// logprob is the token's under the unfiltered temperature-scaled distribution.
+// One CTA per row.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+constexpr int kFiltThreads = 512;
+
+struct FiltShared {
+  unsigned int cnt[256];
+  unsigned long long mass[256];
+  uint32_t prefix;
+  unsigned long long above;
+  float m, s;
+};
+
+__device__ __forceinline__ void radix_pass_clear(FiltShared& sh) {
+  for (int b = threadIdx.x; b < 256; b += blockDim.x) {
+    sh.cnt[b] = 0u;
+    sh.mass[b] = 0ull;
+  }
+}
+
+// Key of the k-th largest scaled value of the row.
+template <typename T>
+__device__ uint32_t select_topk_key(const T* x, int V, float inv, int k, FiltShared& sh) {
+  uint32_t prefix = 0u, mask = 0u;
+  int remaining = k;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    radix_pass_clear(sh);
+    __syncthreads();
+    for (int j = threadIdx.x; j < V; j += blockDim.x) {
+      const uint32_t key = order_key(load1(x + j) * inv);
+      if ((key & mask) == prefix) atomicAdd(&sh.cnt[(key >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int cum = 0, b = 255;
+      for (; b > 0; --b) {
+        if (cum + (int)sh.cnt[b] >= remaining) break;
+        cum += (int)sh.cnt[b];
+      }
+      remaining -= cum;
+      sh.prefix = prefix | ((uint32_t)b << shift);
+    }
+    __syncthreads();
+    prefix = sh.prefix;
+    mask |= 255u << shift;
+    __syncthreads();
+  }
+  return prefix;
+}
+
+// Smallest key t with (mass of keys > t) <= p.
+template <typename T>
+__device__ uint32_t select_topp_key(const T* x, int V, float inv, float m, float s, float p, FiltShared& sh) {
+  const double scale = 4294967296.0;  // 2^32 fixed point
+  const unsigned long long pq = (unsigned long long)(fmaxf(p, 0.f) * scale);
+  const float rs = 1.f / s;
+  uint32_t prefix = 0u, mask = 0u;
+  if (threadIdx.x == 0) sh.above = 0ull;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    radix_pass_clear(sh);
+    __syncthreads();
+    for (int j = threadIdx.x; j < V; j += blockDim.x) {
+      const float v = load1(x + j) * inv;
+      const uint32_t key = order_key(v);
+      if ((key & mask) == prefix) {
+        const uint32_t b = (key >> shift) & 255u;
+        atomicAdd(&sh.cnt[b], 1u);
+        const unsigned long long q = (unsigned long long)((double)(expf(v - m) * rs) * scale);
+        if (q) atomicAdd(&sh.mass[b], q);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned long long run = sh.above, run_chosen = sh.above;
+      int chosen = -1;
+      for (int b = 255; b >= 0; --b) {
+        if (sh.cnt[b] == 0u) continue;
+        if (run > pq) break;
+        chosen = b;
+        run_chosen = run;
+        run += sh.mass[b];
+      }
+      if (chosen < 0) chosen = 0;  // unreachable: the first non-empty bucket always qualifies
+      sh.above = run_chosen;
+      sh.prefix = prefix | ((uint32_t)chosen << shift);
+    }
+    __syncthreads();
+    prefix = sh.prefix;
+    mask |= 255u << shift;
+    __syncthreads();
+  }
+  return prefix;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kFiltThreads) sample_filtered_kernel(
+    const T* __restrict__ logits, int64_t ld, int V, const float* __restrict__ temperature,
+    const float* __restrict__ top_p, const int64_t* __restrict__ top_k, const int64_t* __restrict__ seeds,
+    const int64_t* __restrict__ positions, int64_t* __restrict__ out_tok, float* __restrict__ out_lp) {
+  __shared__ FiltShared sh;
+  __shared__ SampleAcc wacc[kFiltThreads / 32];
+  const int row = blockIdx.x;
+  const T* x = logits + (size_t)row * ld;
+  const float Tm = temperature[row];
+  const bool greedy = !(Tm > 0.f);
+  const float inv = greedy ? 1.f : 1.f / Tm;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // pass 1: max and sum of exp of the scaled logits
+  float m = -INFINITY, s = 0.f;
+  for (int j = threadIdx.x; j < V; j += kFiltThreads) {
+    const float v = load1(x + j) * inv;
+    if (v > m) {
+      s *= expf(m - v);
+      m = v;
+    }
+    s += expf(v - m);
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m, off), os = __shfl_xor_sync(0xffffffffu, s, off);
+    const float nm = fmaxf(m, om);
+    s = (m > -INFINITY ? s * expf(m - nm) : 0.f) + (om > -INFINITY ? os * expf(om - nm) : 0.f);
+    m = nm;
+  }
+  if (lane == 0) wacc[warp] = SampleAcc{m, s, 0.f, 0, 0.f};
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float M = -INFINITY, S = 0.f;
+    for (int w = 0; w < kFiltThreads / 32; ++w) {
+      const float wm = wacc[w].m, ws = wacc[w].s;
+      const float nm = fmaxf(M, wm);
+      S = (M > -INFINITY ? S * expf(M - nm) : 0.f) + (wm > -INFINITY ? ws * expf(wm - nm) : 0.f);
+      M = nm;
+    }
+    sh.m = M;
+    sh.s = S;
+  }
+  __syncthreads();
+  m = sh.m;
+  s = sh.s;
+  // thresholds
+  uint32_t thr = 0u;
+  if (!greedy) {
+    const int64_t k = top_k[row];
+    if (k > 0 && k < V) thr = select_topk_key<T>(x, V, inv, (int)k, sh);
+    const float p = top_p[row];
+    if (p < 1.f) {
+      const uint32_t tp = select_topp_key<T>(x, V, inv, m, s, p, sh);
+      thr = tp > thr ? tp : thr;
+    }
+  }
+  // Gumbel-max over the kept tokens (the Philox counter layout of sample_kernel)
+  const uint64_t seed = (uint64_t)seeds[row];
+  const uint64_t pos = (uint64_t)positions[row];
+  const uint2 key = make_uint2((uint32_t)seed, (uint32_t)(seed >> 32));
+  SampleAcc a{-INFINITY, 0.f, -INFINITY, 0x7fffffff, 0.f};
+  const int groups = (V + 3) / 4;
+  for (int i = threadIdx.x; i < groups; i += kFiltThreads) {
+    uint4 r = make_uint4(0u, 0u, 0u, 0u);
+    if (!greedy) r = philox4x32_10(make_uint4((uint32_t)i, (uint32_t)pos, (uint32_t)(pos >> 32), 0x5A17u), key);
+    const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int j = 4 * i + e;
+      if (j >= V) break;
+      const float v = load1(x + j) * inv;
+      if (order_key(v) < thr) continue;
+      const float sc = greedy ? v : v + gumbel(rr[e]);
+      if (sc > a.best || (sc == a.best && j < a.idx)) {
+        a.best = sc;
+        a.idx = j;
+        a.val = v;
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, a.best, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, a.idx, off);
+    const float ov = __shfl_xor_sync(0xffffffffu, a.val, off);
+    if (ob > a.best || (ob == a.best && oi < a.idx)) {
+      a.best = ob;
+      a.idx = oi;
+      a.val = ov;
+    }
+  }
+  __syncthreads();  // wacc reuse
+  if (lane == 0) wacc[warp] = a;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    SampleAcc t = wacc[0];
+    for (int w = 1; w < kFiltThreads / 32; ++w)
+      if (wacc[w].best > t.best || (wacc[w].best == t.best && wacc[w].idx < t.idx)) t = wacc[w];
+    const bool ok = t.idx >= 0 && t.idx < V;
+    out_tok[row] = ok ? t.idx : 0;
+    out_lp[row] = ok ? t.val - m - logf(s) : -INFINITY;
+  }
+}
+
+// logits [B, V] bf16 or fp32 (unit inner stride); temperature / top_p fp32 [B]; top_k / seeds / positions
+// int64 [B] (top_k <= 0 or >= V: no top-k; top_p >= 1: no nucleus); outputs int64 / fp32 [B].
+void sample_tokens_filtered(torch::Tensor logits, torch::Tensor temperature, torch::Tensor top_p, torch::Tensor top_k,
+                            torch::Tensor seeds, torch::Tensor positions, torch::Tensor out_tok, torch::Tensor out_lp) {
+  const bool f32 = logits.scalar_type() == at::kFloat;
+  LIBRA_CHECK(logits.is_cuda() && (f32 || logits.scalar_type() == at::kBFloat16) && logits.dim() == 2 &&
+                  logits.stride(1) == 1,
+              "sample_tokens_filtered: logits must be bf16 or fp32 [B, V] with unit inner stride");
+  const int B = (int)logits.size(0), V = (int)logits.size(1);
+  auto dev_vec = [&](const torch::Tensor& t, at::ScalarType ty) {
+    return t.is_cuda() && t.device() == logits.device() && t.scalar_type() == ty && t.is_contiguous() &&
+           t.numel() >= B;
+  };
+  LIBRA_CHECK(dev_vec(temperature, at::kFloat) && dev_vec(top_p, at::kFloat),
+              "sample_tokens_filtered: temperature / top_p fp32 [B] on the logits' device");
+  LIBRA_CHECK(dev_vec(top_k, at::kLong) && dev_vec(seeds, at::kLong) && dev_vec(positions, at::kLong),
+              "sample_tokens_filtered: top_k / seeds / positions int64 [B] on the logits' device");
+  LIBRA_CHECK(dev_vec(out_tok, at::kLong) && dev_vec(out_lp, at::kFloat),
+              "sample_tokens_filtered: outputs int64 / fp32 [B] on the logits' device");
+  if (B == 0 || V == 0) return;
+  const c10::cuda::CUDAGuard guard(logits.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (f32)
+    sample_filtered_kernel<float><<<B, kFiltThreads, 0, st>>>(
+        logits.data_ptr<float>(), (int64_t)logits.stride(0), V, temperature.data_ptr<float>(),
+        top_p.data_ptr<float>(), top_k.data_ptr<int64_t>(), seeds.data_ptr<int64_t>(),
+        positions.data_ptr<int64_t>(), out_tok.data_ptr<int64_t>(), out_lp.data_ptr<float>());
+  else
+    sample_filtered_kernel<__nv_bfloat16><<<B, kFiltThreads, 0, st>>>(
+        (const __nv_bfloat16*)logits.data_ptr(), (int64_t)logits.stride(0), V, temperature.data_ptr<float>(),
+        top_p.data_ptr<float>(), top_k.data_ptr<int64_t>(), seeds.data_ptr<int64_t>(),
+        positions.data_ptr<int64_t>(), out_tok.data_ptr<int64_t>(), out_lp.data_ptr<float>());
+  LIBRA_LAUNCH_CHECK();
+}
+
 }  // namespace rollout
 }  // namespace libra

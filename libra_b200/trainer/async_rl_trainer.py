@@ -47,6 +47,7 @@ from libra_b200.infra.execution.batch_dispatcher import BatchTaskDispatcher, Tas
 from libra_b200.infra.observability.history_collector import HistoryDataCollector
 from libra_b200.infra.observability.phase_tracer import PhaseTracer
 from libra_b200.infra.sync.staleness import StalenessManager
+from libra_b200.utils.snapshot import snapshot
 from libra_b200.utils import nvtx
 
 
@@ -841,7 +842,7 @@ class AsyncRLTrainer:
         mgr.save(self.train_engine, step + 1, export_for_rollout=False)
         if self.is_main_process:
             light = {"step": step, "version": self.train_engine.get_version(),
-                     "stats": {k: v for k, v in self.stats.items() if isinstance(v, (int, float, str))},
+                     "stats": snapshot(self.stats),
                      "config": self.config.to_dict()}
             torch.save(light, os.path.join(self.config.log_dir, "checkpoints", f"step_{step}.pt"))
             mgr.prune(self.config.keep_latest_checkpoints, protect=self.start_step or None)

@@ -36,3 +36,40 @@ def test_history_and_analysis(tmp_path):
     prof = (tmp_path / "prof.jsonl").read_text().splitlines()
     assert len(prof) == 6
     assert json.load(open(h.summary_path))["total_steps"] == 3
+
+
+def test_checkpoint_snapshot_breaks_cycles_and_limits_depth():
+    """Trainer stats go into checkpoints as plain, acyclic, depth-limited data
+    (reference tests/test_checkpoint_snapshot.py)."""
+    import io
+
+    import torch
+
+    from libra_b200.utils.snapshot import RECURSIVE, TOO_DEEP, snapshot
+
+    def depth(v):
+        if isinstance(v, dict):
+            return 1 + max((depth(x) for x in v.values()), default=0)
+        if isinstance(v, list):
+            return 1 + max((depth(x) for x in v), default=0)
+        return 0
+
+    rec = {"reward": 0.5}
+    rec["self"] = rec
+    nested = cur = {}
+    for i in range(100):
+        cur["next"] = {}
+        cur = cur["next"]
+        cur["index"] = i
+    shared = [1, 2]
+    snap = snapshot({"recursive": rec, "nested": nested, "a": shared, "b": shared,
+                     "t": torch.ones(3), "big": torch.zeros(1000, 2), "nan": float("nan"), "obj": object()},
+                    max_depth=32)
+    assert snap["recursive"]["self"] == RECURSIVE and snap["recursive"]["reward"] == 0.5
+    assert depth(snap) <= 33 and TOO_DEEP in str(snap["nested"])
+    assert snap["a"] == snap["b"] == [1, 2]  # shared (not cyclic) values are copied, not marked
+    assert snap["t"] == [1.0, 1.0, 1.0] and snap["big"].startswith("<tensor (1000, 2)")
+    assert snap["nan"] == "nan" and snap["obj"].startswith("<object")
+    buf = io.BytesIO()
+    torch.save(snap, buf)
+    assert buf.tell() > 0

@@ -199,3 +199,31 @@ def test_extend_plan_fresh_prefill_reads_no_cache():
     k = torch.arange(8.0).view(8, 1, 1)
     assert torch.equal(plan.keys(kv, 0, k, k)[0], k)
     assert build_extend_plan([WorkItem("x", [1, 2], 1)], [0], kv, "cpu") is None
+
+
+def test_filtered_keep_mask_rule():
+    """top-k keeps the k largest; top-p keeps a token while the mass strictly
+    above it is at most p; ties with a threshold are kept; the CPU sampler
+    draws inside the kept set."""
+    from libra_b200 import ops
+
+    x = torch.tensor([3.0, 2.0, 1.0, 0.0])
+    p = torch.softmax(x, -1)  # ~[0.64, 0.24, 0.09, 0.03]
+    assert ops.filtered_keep_mask(x, 1.0, 2).tolist() == [True, True, False, False]
+    assert ops.filtered_keep_mask(x, 0.5, -1).tolist() == [True, False, False, False]
+    assert ops.filtered_keep_mask(x, float(p[0]) + 1e-4, -1).tolist() == [True, True, False, False]
+    assert ops.filtered_keep_mask(x, 0.7, 3).tolist() == [True, True, False, False]
+    tied = torch.tensor([1.0, 2.0, 2.0, 0.5])
+    assert ops.filtered_keep_mask(tied, 1.0, 1).tolist() == [False, True, True, False]
+    assert ops.filtered_keep_mask(tied, 0.1, -1).tolist() == [False, True, True, False]
+    g = torch.Generator().manual_seed(0)
+    logits = torch.randn(3, 50, generator=g)
+    tok, lp = torch.empty(3, dtype=torch.long), torch.empty(3)
+    ops.sample_tokens_filtered(logits, torch.tensor([1.0, 0.0, 2.0]), torch.tensor([0.6, 0.6, 1.0]),
+                               torch.tensor([-1, 3, 4]), torch.tensor([1, 2, 3]), torch.tensor([5, 6, 7]), tok, lp)
+    assert int(tok[1]) == int(logits[1].argmax())
+    for b, (t, pp, k) in enumerate(((1.0, 0.6, -1), (1.0, 0.6, 3), (2.0, 1.0, 4))):
+        x = logits[b] / t
+        if b != 1:
+            assert bool(ops.filtered_keep_mask(x, pp, k)[int(tok[b])])
+        assert abs(float(lp[b]) - float(torch.log_softmax(x, -1)[int(tok[b])])) < 1e-5

@@ -145,6 +145,55 @@ def test_sample_tokens_greedy_logprob_and_distribution():
     assert (freq - prob).abs().max().item() < 0.015, (freq, prob)
 
 
+def test_sample_tokens_filtered_against_fp32_rule():
+    """Top-k / top-p sampling kernel against the fp32 rule (``filtered_keep_mask``
+    on logits * (1/T)): unfiltered rows equal ``sample_tokens``; every draw lies
+    in the kept set; logprobs are the unfiltered ones; the empirical
+    distribution over many positions is the renormalised filtered softmax."""
+    from libra_b200 import ops
+
+    torch.manual_seed(2)
+    dev = "cuda"
+    B, V = 8, 151936
+    logits = (torch.randn(B, V, device=dev) * 3).bfloat16()
+    temp = torch.tensor([1.0, 0.5, 2.0, 0.0, 1.0, 0.5, 1.0, 2.0], device=dev)
+    top_p = torch.tensor([1.0, 0.9, 0.5, 0.9, 1.0, 0.3, 0.95, 1.0], device=dev)
+    top_k = torch.tensor([-1, -1, 50, 20, 1000, 0, 5, 7], dtype=torch.long, device=dev)
+    seeds = torch.arange(B, dtype=torch.long, device=dev) * 104729 + 3
+    pos = torch.arange(B, dtype=torch.long, device=dev) + 50
+    tok, lp = torch.empty(B, dtype=torch.long, device=dev), torch.empty(B, device=dev)
+    ops.sample_tokens_filtered(logits, temp, top_p, top_k, seeds, pos, tok, lp)
+    ref_tok, ref_lp = torch.empty_like(tok), torch.empty_like(lp)
+    ops.sample_tokens(logits, temp, seeds, pos, ref_tok, ref_lp)
+    assert int(tok[0]) == int(ref_tok[0]) and abs(float(lp[0]) - float(ref_lp[0])) < 1e-5
+    for b in range(B):
+        t = float(temp[b])
+        x = logits[b].float() * (1.0 / t if t > 0 else 1.0)
+        if t <= 0:
+            assert int(tok[b]) == int(x.argmax())
+        else:
+            keep = ops.filtered_keep_mask(x, min(1.0, float(top_p[b]) + 1e-3), int(top_k[b]))
+            assert bool(keep[int(tok[b])]), (b, int(tok[b]))
+        assert abs(float(lp[b]) - float(torch.log_softmax(x, -1)[int(tok[b])])) < 2e-3
+    # distribution on a small vocabulary: draws from the renormalised kept set
+    V2, N = 32, 20000
+    small = (torch.randn(V2, device=dev) * 1.5).bfloat16()
+    for k, p in ((8, 1.0), (-1, 0.7), (10, 0.8)):
+        rows = small.unsqueeze(0).expand(N, V2).contiguous()
+        ones = torch.ones(N, device=dev)
+        oT, oL = torch.empty(N, dtype=torch.long, device=dev), torch.empty(N, device=dev)
+        ops.sample_tokens_filtered(rows, ones, torch.full((N,), p, device=dev),
+                                   torch.full((N,), k, dtype=torch.long, device=dev),
+                                   torch.full((N,), 77, dtype=torch.long, device=dev),
+                                   torch.arange(N, dtype=torch.long, device=dev), oT, oL)
+        x = small.float()
+        keep = ops.filtered_keep_mask(x, p, k)
+        want = torch.softmax(x.masked_fill(~keep, float("-inf")), -1)
+        freq = torch.bincount(oT, minlength=V2).float() / N
+        assert float(freq[~keep].sum()) == 0.0, (k, p)
+        assert (freq - want).abs().max().item() < 0.015, (k, p, freq, want)
+
+
 def test_decode_graphs_match_eager_steps(monkeypatch):
     """Greedy generation through the captured decode graphs equals the eager path token for token."""
     from libra_b200.engine.rollout.llm_engine import LLMEngine

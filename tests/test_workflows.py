@@ -213,3 +213,16 @@ def test_dataset_evaluation_greedy_and_failures():
     assert abs(out["eval_accuracy"] - 0.4) < 1e-9
     assert abs(out["eval_reward_mean"] - 1.75 / 5) < 1e-9 and out["eval_reward_max"] == 1.0
     assert len(out["eval_records"]) == 2 and out["eval_records"][1]["accurate"] is False
+
+
+def test_rollout_index_gives_distinct_reproducible_seeds():
+    """The GRPO group's members (rollout_index) sample with distinct seeds; the
+    same (prompt, version, index, turn) always gets the same seed."""
+    eng = ScriptedEngine(TOK, ["[ISSUE]a[/ISSUE]"] * 3)
+    wf = R2EGymWorkflow(tokenizer=TOK, max_turns=1, max_new_tokens=32, temperature=0.8, top_p=0.95)
+    row = {"prompt": "commit details", "target_issue": "x", "repo_name": "r", "commit_hash": "c"}
+    for idx in (0, 1, 0):
+        asyncio.run(wf.run_episode(eng, row, version=3, rollout_index=idx))
+    first, second, again = [c["seed"] for c in eng.calls]
+    assert first != second and first == again
+    assert all(c["temperature"] == 0.8 and c["top_p"] == 0.95 for c in eng.calls)

@@ -165,7 +165,7 @@ def test_sample_tokens_filtered_against_fp32_rule():
     ops.sample_tokens_filtered(logits, temp, top_p, top_k, seeds, pos, tok, lp)
     ref_tok, ref_lp = torch.empty_like(tok), torch.empty_like(lp)
     ops.sample_tokens(logits, temp, seeds, pos, ref_tok, ref_lp)
-    assert int(tok[0]) == int(ref_tok[0]) and abs(float(lp[0]) - float(ref_lp[0])) < 1e-5
+    assert int(tok[0]) == int(ref_tok[0]) and abs(float(lp[0]) - float(ref_lp[0])) < 1e-4
     for b in range(B):
         t = float(temp[b])
         x = logits[b].float() * (1.0 / t if t > 0 else 1.0)

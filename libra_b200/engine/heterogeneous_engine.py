@@ -20,6 +20,7 @@ import logging
 import os
 import threading
 import time
+import uuid
 from typing import Any, Dict, List, Optional
 
 from libra_b200.infra.scheduling import SchedulerFactory
@@ -146,14 +147,37 @@ class HeterogeneousRolloutEngine:
         if old is not None and res is not None and res.instance_index >= 0 and ctx and \
                 old.instance_index != res.instance_index:
             src = getattr(self.engines[old.instance_index], "engine", None)
-            dst = getattr(self.engines[res.instance_index], "engine", None)
+            target = self.engines[res.instance_index]
+            dst = getattr(target, "engine", None)
+            t0, n = time.perf_counter(), 0
             if src is not None and dst is not None and hasattr(src, "migrate_prefix_to"):
-                t0 = time.perf_counter()
                 n = src.migrate_prefix_to(dst, ctx)
-                self.kv_migrations["count"] += 1 if n else 0
-                self.kv_migrations["tokens"] += n
-                self.kv_migrations["seconds"] += time.perf_counter() - t0
+            elif src is not None and hasattr(src, "export_prefix") and hasattr(target, "import_prefix"):
+                n = self._migrate_to_server(src, target, ctx)
+            self.kv_migrations["count"] += 1 if n else 0
+            self.kv_migrations["tokens"] += n
+            self.kv_migrations["seconds"] += time.perf_counter() - t0
         return res
+
+    def _migrate_to_server(self, src, target, ctx) -> int:
+        """In-process engine -> server instance (e.g. a TP-k process group): the
+        prefix's KV goes through a file in shared memory, which every server
+        rank reads for its own KV heads.  Failures leave the request to
+        recompute its prefix on the target."""
+        import tempfile
+
+        root = "/dev/shm" if os.path.isdir("/dev/shm") and os.access("/dev/shm", os.W_OK) else tempfile.gettempdir()
+        path = os.path.join(root, f"libra_kv_{os.getpid()}_{uuid.uuid4().hex}.safetensors")
+        try:
+            payload = src.export_prefix(ctx, path)
+            return target.import_prefix(payload) if payload["tokens"] else 0
+        except (OSError, ValueError, RuntimeError) as exc:
+            log.warning("KV migration to %s failed (%s); the request recomputes its prefix",
+                        getattr(target, "instance_id", "?"), exc)
+            return 0
+        finally:
+            if os.path.exists(path):
+                os.unlink(path)
 
     def route_cmlfq_tool_return(self, request_id: str, tool_result: Any, generated_tokens: int):
         decision = self.on_tool_return(request_id, tool_result, generated_tokens)

@@ -221,22 +221,60 @@ class PagedKVCache:
         if (src.num_layers, src.block_size, src.kv_heads, src.head_dim) != \
                 (self.num_layers, self.block_size, self.kv_heads, self.head_dim):
             raise ValueError("KV caches of different shapes: migrate through a head reshard")
+
+        def fetch(pos: List[int]):
+            si = torch.tensor([blocks[i][0] for i in pos], dtype=torch.long, device=src.k.device)
+            return src.k.index_select(1, si), src.v.index_select(1, si)
+
+        return self._import([h for _, h in blocks], fetch)
+
+    def block_hashes(self, tokens: List[int]) -> List[str]:
+        """Prefix-cache hash chain of the full blocks of ``tokens``."""
+        out, parent, bs = [], "", self.block_size
+        for s in range(0, (len(tokens) // bs) * bs, bs):
+            parent = _block_hash(parent, tokens[s:s + bs])
+            out.append(parent)
+        return out
+
+    def export_blocks(self, blocks: List[Tuple[int, str]]) -> Tuple[torch.Tensor, torch.Tensor]:
+        """K and V of ``blocks`` as [layers, blocks, block_size, kv_heads, head_dim]."""
+        idx = torch.tensor([b for b, _ in blocks], dtype=torch.long, device=self.k.device)
+        return self.k.index_select(1, idx), self.v.index_select(1, idx)
+
+    def import_block_tensors(self, tokens: List[int], k: torch.Tensor, v: torch.Tensor) -> int:
+        """Prefix-cache the blocks of ``tokens`` from K/V given as
+        [layers, blocks, block_size, kv_heads, head_dim] (this cache's heads);
+        block j holds tokens [j * block_size, (j + 1) * block_size)."""
+        if k.shape != v.shape or tuple(k.shape[:1]) + tuple(k.shape[2:]) != \
+                (self.num_layers, self.block_size, self.kv_heads, self.head_dim):
+            raise ValueError(f"KV blocks of shape {tuple(k.shape)} do not fit this cache")
+        hashes = self.block_hashes(tokens)[:k.shape[1]]
+
+        def fetch(pos: List[int]):
+            i = torch.tensor(pos, dtype=torch.long, device=k.device)
+            return k.index_select(1, i), v.index_select(1, i)
+
+        return self._import(hashes, fetch)
+
+    def _import(self, hashes: List[str], fetch) -> int:
+        """Register a hash chain as prefix-cached blocks; ``fetch(positions)``
+        gives the K/V of the chain positions that are not cached here yet."""
         pinned, todo, have = [], [], 0
-        for b, h in blocks:
+        for i, h in enumerate(hashes):
             if not todo and h in self.alloc.cached:
                 pinned.append(self.alloc.lookup(h))  # keep the present head of the chain while allocating
                 have += 1
             else:
-                todo.append((b, h))
+                todo.append(i)
         todo = todo[:max(0, self.alloc.num_free())]
         dst = [self.alloc.allocate() for _ in todo]
         if todo:
-            si = torch.tensor([b for b, _ in todo], dtype=torch.long, device=src.k.device)
+            kk, vv = fetch(todo)
             di = torch.tensor(dst, dtype=torch.long, device=self.k.device)
-            for s_pool, d_pool in ((src.k, self.k), (src.v, self.v)):
-                d_pool.index_copy_(1, di, s_pool.index_select(1, si).to(self.k.device))
-        for b, (_, h) in zip(dst, todo):
-            self.alloc.register(b, h)
+            self.k.index_copy_(1, di, kk.to(self.k.device, self.k.dtype))
+            self.v.index_copy_(1, di, vv.to(self.v.device, self.v.dtype))
+        for b, i in zip(dst, todo):
+            self.alloc.register(b, hashes[i])
             self.alloc.release(b)  # unreferenced and cached: reusable by a matching prefix
         for b in pinned:
             self.alloc.release(b)

@@ -186,6 +186,11 @@ class LLMEngine:
                     self.version = int(version)
             for op, args in plan.get("ops", []):
                 getattr(self.kv, op)(*args) if op != "clear_cache" else self.kv.alloc.clear_cache()
+            if plan.get("import_kv") is not None:
+                try:
+                    self._import_prefix_local(plan["import_kv"])
+                except (OSError, ValueError, KeyError) as exc:  # the leader hit the same check and reports it
+                    print(f"KV import skipped on TP rank {self.tp_rank}: {exc}")
             if plan.get("items"):
                 self.runner.step([WorkItem(rid, toks, start) for rid, toks, start in plan["items"]])
             if plan.get("stop"):
@@ -365,6 +370,62 @@ class LLMEngine:
                 if not was:
                     e.resume()
         self.stats["migrated_out_tokens"] = self.stats.get("migrated_out_tokens", 0) + n
+        return n
+
+    def export_prefix(self, tokens: List[int], path: str) -> Dict:
+        """Write this engine's cached KV of ``tokens``'s prefix to ``path``
+        (safetensors: ``k`` and ``v`` as [layers, blocks, block_size, kv_heads,
+        head_dim]) for another process's engine to import (``import_prefix``);
+        returns the JSON request that describes it."""
+        from safetensors.torch import save_file
+
+        if self.tp_size != 1:
+            raise ValueError("KV export needs a single-rank engine (all KV heads in one cache)")
+        was_paused = self._paused.is_set()
+        self.pause()
+        try:
+            blocks = self.kv.cached_blocks(list(tokens))
+            k, v = self.kv.export_blocks(blocks)
+            save_file({"k": k.contiguous().cpu(), "v": v.contiguous().cpu()}, path)
+        finally:
+            if not was_paused:
+                self.resume()
+        n = len(blocks) * self.kv.block_size
+        return {"path": path, "tokens": [int(t) for t in tokens[:n]], "version": int(self.version),
+                "block_size": self.kv.block_size, "num_layers": self.kv.num_layers,
+                "kv_heads": self.cfg.num_key_value_heads, "head_dim": self.kv.head_dim}
+
+    def import_prefix(self, request: Dict) -> int:
+        """Prefix-cache KV exported by ``export_prefix`` (another process's
+        engine at the same weight version); with TP every rank imports its own
+        KV heads, in step with the leader.  Returns the prefix tokens now cached."""
+        was_paused = self._paused.is_set()
+        self.pause()
+        try:
+            if self.tp_size > 1:
+                self._publish(import_kv=request)
+            return self._import_prefix_local(request)
+        finally:
+            if not was_paused:
+                self.resume()
+
+    def _import_prefix_local(self, request: Dict) -> int:
+        from safetensors.torch import load_file
+
+        kv, cfg = self.kv, self.cfg
+        if int(request.get("version", -1)) != int(self.version):
+            return 0  # KV of other weights would be wrong here
+        if (int(request["block_size"]), int(request["num_layers"]), int(request["kv_heads"]),
+                int(request["head_dim"])) != (kv.block_size, kv.num_layers, cfg.num_key_value_heads, kv.head_dim):
+            raise ValueError("exported KV does not match this engine's model or block size")
+        data = load_file(str(request["path"]), device=str(self.device))
+        k, v = data["k"], data["v"]
+        if self.tp_size > 1:  # this rank's KV heads (neighbouring ranks share a head when tp > kv heads)
+            kv0 = self.tp_rank * cfg.num_key_value_heads // self.tp_size
+            k = k[:, :, :, kv0:kv0 + kv.kv_heads]
+            v = v[:, :, :, kv0:kv0 + kv.kv_heads]
+        n = kv.import_block_tensors([int(t) for t in request["tokens"]], k, v)
+        self.stats["migrated_in_tokens"] = self.stats.get("migrated_in_tokens", 0) + n
         return n
 
     # ------------------------------------------------------------------ scheduling

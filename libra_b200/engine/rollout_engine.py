@@ -120,6 +120,18 @@ class HTTPRolloutEngine:
                 "token_ids": c.get("token_ids") or [], "prompt_token_ids": c.get("prompt_token_ids") or [],
                 "logprobs": lp.get("token_logprobs") or [], "finish_reason": c.get("finish_reason", "length")}
 
+    def import_prefix(self, request: Dict[str, Any], timeout: float = 120.0) -> int:
+        """Hand the server KV exported by ``LLMEngine.export_prefix`` (blocking;
+        C-MLFQ migration runs on the scheduler's thread).  Returns the prefix
+        tokens now cached there."""
+        import json
+        import urllib.request
+
+        req = urllib.request.Request(f"{self.base_url}/import_kv", data=json.dumps(request).encode(), method="POST",
+                                     headers={"Content-Type": "application/json"})
+        with urllib.request.urlopen(req, timeout=timeout) as r:
+            return int(json.loads(r.read() or b"{}").get("tokens", 0))
+
     def wait_for_ready(self, timeout: float = 300.0, interval: float = 1.0) -> bool:
         import urllib.request
 

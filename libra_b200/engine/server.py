@@ -16,6 +16,10 @@ Routes (the reference serves the same ones from a patched vLLM API server,
   CUDA IPC handles, no pickled objects) and reshard this rank's slice into the
   served weights in place with the ``weight_reshard`` kernel (peer-memory
   weight sync).
+* ``POST /import_kv`` ``{"path", "tokens", "version", ...}`` - prefix-cache the
+  KV blocks another engine exported (``LLMEngine.export_prefix``, a
+  safetensors file); with TP every rank takes its own KV heads (C-MLFQ
+  migration of a multi-turn request into this instance).
 
     python -m libra_b200.engine.server --model qwen3-4b --device cuda:4 --port 8000
 """
@@ -96,6 +100,17 @@ def build_app(engine, tokenizer, model_name: str = "libra", weight_loader=None) 
                     await loop.run_in_executor(None, lambda: engine.update_weights(params, version, reload_request=req))
             return web.json_response({"status": "ok", "version": engine.version, "seconds": time.perf_counter() - t0})
 
+    async def import_kv(request: web.Request):
+        body = await request.json()
+        if not isinstance(body.get("path"), str) or not isinstance(body.get("tokens"), list):
+            return web.json_response({"error": "import_kv needs path and tokens"}, status=400)
+        loop = asyncio.get_running_loop()
+        try:
+            n = await loop.run_in_executor(None, engine.import_prefix, body)
+        except (OSError, ValueError, KeyError) as exc:
+            return web.json_response({"error": str(exc)}, status=400)
+        return web.json_response({"status": "ok", "tokens": int(n)})
+
     app.router.add_get("/health", health)
     app.router.add_get("/v1/models", models)
     app.router.add_get("/metrics", metrics)
@@ -103,6 +118,7 @@ def build_app(engine, tokenizer, model_name: str = "libra", weight_loader=None) 
     app.router.add_post("/reload_weights", lambda r: reload(r, "disk"))
     app.router.add_post("/reload_weights_peer", lambda r: reload(r, "peer"))
     app.router.add_post("/reload_weights_nccl", lambda r: reload(r, "peer"))
+    app.router.add_post("/import_kv", import_kv)
     return app
 
 

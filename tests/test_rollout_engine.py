@@ -1,6 +1,7 @@
 """Rollout engine: paged-KV generation equals naive full recompute (CPU reference ops)."""
 
 import asyncio
+import os
 
 import pytest
 import torch
@@ -227,3 +228,81 @@ def test_filtered_keep_mask_rule():
         if b != 1:
             assert bool(ops.filtered_keep_mask(x, pp, k)[int(tok[b])])
         assert abs(float(lp[b]) - float(torch.log_softmax(x, -1)[int(tok[b])])) < 1e-5
+
+
+@pytest.mark.parametrize("tp", [1, 2, 4])
+def test_kv_block_export_import_with_head_slices(tp):
+    """Exported blocks land in TP caches as each rank's KV heads (tp=4 shares
+    each of 2 heads between two ranks) and register the prefix hash chain."""
+    torch.manual_seed(0)
+    src = PagedKVCache(2, 16, 4, 2, 8, "cpu", dtype=torch.float32)
+    toks = list(range(30, 41))  # 2 full blocks + 3 tokens
+    src.reserve("s", len(toks))
+    slots = src.slot_mapping("s", 0, len(toks))
+    for layer in range(2):
+        src.write(layer, slots, torch.randn(len(toks), 2, 8), torch.randn(len(toks), 2, 8))
+    src.commit("s", toks)
+    blocks = src.cached_blocks(toks)
+    assert len(blocks) == 2 and [h for _, h in blocks] == src.block_hashes(toks)
+    k, v = src.export_blocks(blocks)
+    assert k.shape == (2, 2, 4, 2, 8)
+    kv_l = max(1, 2 // tp)
+    for r in range(tp):
+        kv0 = r * 2 // tp
+        dst = PagedKVCache(2, 16, 4, kv_l, 8, "cpu", dtype=torch.float32)
+        assert dst.import_block_tensors(toks, k[:, :, :, kv0:kv0 + kv_l], v[:, :, :, kv0:kv0 + kv_l]) == 8
+        assert dst.match_prefix("t", toks + [99]) == 8
+        got = dst.gather(0, "t", 8)[0]
+        want = src.gather(0, "s", 8)[0][:, kv0:kv0 + kv_l]
+        assert torch.equal(got, want)
+
+
+def test_hetero_pool_migrates_kv_into_a_server_instance(tiny):
+    """Migration target without an in-process engine (a server client): the
+    pool exports the context's KV to a file, the target imports it, and the
+    file is removed afterwards."""
+    from types import SimpleNamespace
+
+    from libra_b200.engine import heterogeneous_engine as he
+    from libra_b200.engine.rollout_engine import LocalRolloutEngine
+    from libra_b200.engine.tokenizer import ByteTokenizer
+
+    class _Server:  # the HTTP client's import interface, served by an engine of another "process"
+        instance_id = "server"
+
+        def __init__(self):
+            self.llm = LLMEngine(tiny.cfg, tiny.params, kv_blocks=128, block_size=4)
+            self.paths = []
+
+        def import_prefix(self, payload):
+            self.paths.append(payload["path"])
+            return self.llm.import_prefix(payload)
+
+    class _Sched:
+        where = {"r1": 0}
+
+        def register_instance(self, *a):
+            pass
+
+        def get_request_route(self, rid):
+            i = self.where.get(rid)
+            return None if i is None else SimpleNamespace(instance_index=i, pending=False, category="short",
+                                                          is_fallback=False, reason="", request_id=rid)
+
+        def execute_migration(self, rid, decision):
+            self.where[rid] = 1
+            return self.get_request_route(rid)
+
+    local = LocalRolloutEngine(LLMEngine(tiny.cfg, tiny.params, kv_blocks=128, block_size=4),
+                               ByteTokenizer(tiny.cfg.vocab_size))
+    server = _Server()
+    pool = he.HeterogeneousRolloutEngine([local, server], [{"instance_id": "i0", "tp_degree": 1},
+                                                           {"instance_id": "server", "tp_degree": 2}], _Sched())
+    prompt = list(range(40, 61))
+    res = asyncio.run(pool.generate(prompt, max_new_tokens=4, temperature=0.0, request_id="r1"))
+    pool.execute_cmlfq_migration("r1", SimpleNamespace(should_migrate=True))
+    ctx = prompt + res["token_ids"]
+    assert pool.kv_migrations["count"] == 1 and pool.kv_migrations["tokens"] == (len(ctx) // 4) * 4
+    assert server.llm.kv.cached_blocks(ctx) and server.llm.stats["migrated_in_tokens"] > 0
+    assert server.paths and not os.path.exists(server.paths[0])
+    local.engine.shutdown()

@@ -54,6 +54,15 @@ def _extend_attention_ref(q, k, v, q_start: int):
     return (s.softmax(-1) @ vv).transpose(0, 1).to(q.dtype)
 
 
+def _to_device(values: List[int], dtype, device) -> torch.Tensor:
+    """Small host list -> device tensor without a stream synchronisation (a
+    pinned staging copy on CUDA)."""
+    t = torch.tensor(values, dtype=dtype)
+    if torch.device(device).type == "cuda":
+        return t.pin_memory().to(device, non_blocking=True)
+    return t
+
+
 @dataclass
 class _ExtendPlan:
     """How one step's extend attention finds its queries and keys.
@@ -101,7 +110,7 @@ def build_extend_plan(items: Sequence[WorkItem], offsets: List[int], kv: PagedKV
         rows.extend(range(offsets[i], offsets[i] + n_new))
     n_q = cu_q[-1]
     contiguous = rows == list(range(n_q))
-    q_rows = None if contiguous else torch.tensor(rows, dtype=torch.long).to(device, non_blocking=True)
+    q_rows = None if contiguous else _to_device(rows, torch.long, device)
     fresh = all(items[i].start == 0 for i in ext)
     key_slots = None
     if not fresh:
@@ -111,8 +120,8 @@ def build_extend_plan(items: Sequence[WorkItem], offsets: List[int], kv: PagedKV
     if torch.device(device).type == "cuda":
         from libra_b200.ops.attention import attn_tiles
 
-        plan.cu_q_dev = torch.tensor(cu_q, dtype=torch.int32).to(device, non_blocking=True)
-        plan.cu_k_dev = torch.tensor(cu_k, dtype=torch.int32).to(device, non_blocking=True)
+        plan.cu_q_dev = _to_device(cu_q, torch.int32, device)
+        plan.cu_k_dev = _to_device(cu_k, torch.int32, device)
         plan.tiles = attn_tiles(cu_q, True, device)
     return plan
 
@@ -158,9 +167,9 @@ class InferenceRunner:
             out = None  # every row extends: the kernel's output is the whole result
         else:
             out = torch.empty_like(q)
-        dec = [i for i, it in enumerate(items) if len(it.tokens) - it.start == 1]
+        dec = self._dec
         if dec:
-            rows = torch.tensor([offsets[i] for i in dec], device=dev, dtype=torch.long)
+            rows = self._dec_rows
             if dev.type == "cuda" and self.cfg.head_dim == 128:
                 ids = [items[i].seq_id for i in dec]
                 tbl = self._tables.get(tuple(ids))
@@ -218,9 +227,11 @@ class InferenceRunner:
                                  dtype=torch.long).to(dev, non_blocking=True)
         self._tables = {}
         self._ext_plan = build_extend_plan(items, offsets, self.kv, dev)
-        dec_items = [it for it in items if len(it.tokens) - it.start == 1]
-        self._lens_dec = torch.tensor([len(it.tokens) for it in dec_items], dtype=torch.int32).to(dev)
-        self._max_len_dec = max((len(it.tokens) for it in dec_items), default=1)
+        # per-step host tables, copied once (asynchronously) rather than once per layer
+        self._dec = [i for i, it in enumerate(items) if len(it.tokens) - it.start == 1]
+        self._dec_rows = _to_device([offsets[i] for i in self._dec], torch.long, dev)
+        self._lens_dec = _to_device([len(items[i].tokens) for i in self._dec], torch.int32, dev)
+        self._max_len_dec = max((len(items[i].tokens) for i in self._dec), default=1)
         if self.tp_size > 1:
             from libra_b200.parallel.tensor_parallel import vocab_parallel_embedding
             import torch.distributed as dist

@@ -34,6 +34,7 @@ def main():
     ap.add_argument("--train-pp", type=int, default=0, help="override train_pp_size")
     ap.add_argument("--train-ep", type=int, default=0, help="override train_ep_size")
     ap.add_argument("--model", default="", help="override model_path (a preset name) and its architecture summary")
+    ap.add_argument("--save-interval", type=int, default=-1, help="override save_interval (-1 = keep the config's)")
     ap.add_argument("--replan-every", type=int, default=0,
                     help="turn on the Global Resource Planner with online replanning every N steps")
     a = ap.parse_args()
@@ -64,6 +65,8 @@ def main():
         cfg.total_steps = a.total_steps
     if a.eval_interval >= 0:
         cfg.eval_interval = a.eval_interval
+    if a.save_interval >= 0:
+        cfg.save_interval = a.save_interval
     if a.log_dir:
         cfg.log_dir = a.log_dir
         cfg.sync_path = os.path.join(a.log_dir, "weights")

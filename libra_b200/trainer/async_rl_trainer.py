@@ -99,6 +99,7 @@ class AsyncRLTrainer:
         self.stats: Dict[str, Any] = {}
         self._tracker = None
         self.start_step = int(os.environ.get("RL_TRAIN_START_STEP", "0") or 0)
+        self.resumed_from: Optional[int] = None
         self.initial_model_version = int(os.environ.get("RL_INITIAL_MODEL_VERSION", str(self.start_step))
                                          or self.start_step)
         self._task_counter = itertools.count()
@@ -296,6 +297,7 @@ class AsyncRLTrainer:
 
             self.train_engine = create_train_engine(self.config)
             self.train_engine.initialize(max_seq_length=self.config.max_seq_length)
+        self._resume_from_checkpoint()
         self.train_engine.set_version(self.initial_model_version)
         if self.rollout_engine is None:
             # a TP- or pipeline-sharded trainer hands in-process rollout engines the full model (collective)
@@ -605,6 +607,8 @@ class AsyncRLTrainer:
                           "recompute_logprob_time": recompute_time, "step_time": step_time,
                           "version": self.train_engine.get_version(), **self._advantage_stats})
             self._advantage_stats = {}
+            if self.resumed_from is not None:
+                stats["resumed_from"] = self.resumed_from
             self.stats = stats
             if self.is_main_process:
                 self._record_history(step, batch, stats)
@@ -834,6 +838,27 @@ class AsyncRLTrainer:
         work.wait()
         if drain is not None and answered:
             self.dispatcher.resume()
+
+    def _resume_from_checkpoint(self) -> None:
+        """Resume (collective): with ``RL_TRAIN_START_STEP=S > 0`` and a checkpoint
+        version ``S`` under ``<log_dir>/checkpoints`` (written after step ``S - 1``),
+        every rank loads its weights and optimizer state from it, whatever the
+        parallel layout that wrote it.  Without one, the engine keeps the
+        weights it was initialised with (``model_path``)."""
+        if self.start_step <= 0:
+            return
+        from libra_b200.engine.checkpointing import DistributedCheckpointManager, all_versions
+
+        root = os.path.join(self.config.log_dir, "checkpoints")
+        if self.start_step not in all_versions(root):
+            if self.is_main_process:
+                print(f"RL_TRAIN_START_STEP={self.start_step}: no checkpoint v{self.start_step} under {root}; "
+                      "starting from the initial weights")
+            return
+        DistributedCheckpointManager(root).load(self.train_engine, self.start_step)
+        self.resumed_from = self.start_step
+        if self.is_main_process:
+            print(f"resumed from {root}/v{self.start_step}")
 
     def _save_checkpoint(self, step: int) -> None:
         from libra_b200.engine.checkpointing import DistributedCheckpointManager

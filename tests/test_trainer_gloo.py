@@ -95,3 +95,14 @@ def test_two_rank_expert_parallel_training(tmp_path):
     gets every expert."""
     stats = _run(tmp_path, "target_token", "--model", "tiny-moe", "--train-ep", "2", steps=2)
     assert stats["version"] == 2 and stats["n_trajectories"] == 16
+
+
+def test_resume_from_checkpoint_continues_the_run(tmp_path):
+    """A 2-rank run saves checkpoints every 2 steps; a second run with
+    RL_TRAIN_START_STEP=2 loads version 2 (weights + sharded optimizer state)
+    and finishes the remaining steps to the same final version."""
+    first = _run(tmp_path, "target_token", "--save-interval", "2", steps=4)
+    assert first["version"] == 4
+    assert os.path.isdir(tmp_path / "checkpoints" / "v2" / "megatron_dist")
+    again = _run(tmp_path, "target_token", "--save-interval", "0", steps=4, RL_TRAIN_START_STEP="2")
+    assert again["resumed_from"] == 2 and again["version"] == 4

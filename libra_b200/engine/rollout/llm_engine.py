@@ -509,20 +509,25 @@ class LLMEngine:
         self._publish(items)
         with nvtx.nvtx_range("prefill" if admitted else "decode"):
             logits = self.runner.step(items)
-        temps = torch.tensor([r.params.temperature for r in batch], device=logits.device, dtype=torch.float32)
         if logits.device.type == "cuda":
-            # the fused samplers (same Philox stream as the captured decode steps)
-            seeds = torch.tensor([r.seed for r in batch], dtype=torch.long).to(logits.device, non_blocking=True)
-            pos = torch.tensor([r.n_tokens - 1 for r in batch], dtype=torch.long).to(logits.device, non_blocking=True)
-            toks = torch.empty(len(batch), dtype=torch.long, device=logits.device)
-            lps = torch.empty(len(batch), dtype=torch.float32, device=logits.device)
+            # the fused samplers (same Philox stream as the captured decode steps); their per-request inputs
+            # go up through pinned staging, so the host does not wait for the step's kernels here
+            from libra_b200.engine.rollout.runner import _to_device
+
+            dev = logits.device
+            temps = _to_device([r.params.temperature for r in batch], torch.float32, dev)
+            seeds = _to_device([r.seed for r in batch], torch.long, dev)
+            pos = _to_device([r.n_tokens - 1 for r in batch], torch.long, dev)
+            toks = torch.empty(len(batch), dtype=torch.long, device=dev)
+            lps = torch.empty(len(batch), dtype=torch.float32, device=dev)
             if all(r.params.top_p >= 1.0 and r.params.top_k <= 0 for r in batch):
                 ops.sample_tokens(logits.contiguous(), temps, seeds, pos, toks, lps)
             else:
-                top_p = torch.tensor([r.params.top_p for r in batch], dtype=torch.float32).to(logits.device)
-                top_k = torch.tensor([r.params.top_k for r in batch], dtype=torch.long).to(logits.device)
+                top_p = _to_device([r.params.top_p for r in batch], torch.float32, dev)
+                top_k = _to_device([r.params.top_k for r in batch], torch.long, dev)
                 ops.sample_tokens_filtered(logits.contiguous(), temps, top_p, top_k, seeds, pos, toks, lps)
         else:
+            temps = torch.tensor([r.params.temperature for r in batch], dtype=torch.float32)
             top_p = torch.tensor([r.params.top_p for r in batch], device=logits.device, dtype=torch.float32)
             top_k = torch.tensor([r.params.top_k for r in batch], device=logits.device, dtype=torch.long)
             gens = [r.generator for r in batch] if any(r.generator is not None for r in batch) else None

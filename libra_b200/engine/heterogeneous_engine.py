@@ -164,9 +164,17 @@ class HeterogeneousRolloutEngine:
         prefix's KV goes through a file in shared memory, which every server
         rank reads for its own KV heads.  Failures leave the request to
         recompute its prefix on the target."""
+        import shutil
         import tempfile
 
-        root = "/dev/shm" if os.path.isdir("/dev/shm") and os.access("/dev/shm", os.W_OK) else tempfile.gettempdir()
+        kv = src.kv
+        need = 2 * len(ctx) * kv.num_layers * kv.kv_heads * kv.head_dim * kv.k.element_size()
+        root = tempfile.gettempdir()
+        try:  # shared memory when it has room (container /dev/shm is often small), else the temp dir
+            if os.access("/dev/shm", os.W_OK) and shutil.disk_usage("/dev/shm").free > 2 * need:
+                root = "/dev/shm"
+        except OSError:
+            pass
         path = os.path.join(root, f"libra_kv_{os.getpid()}_{uuid.uuid4().hex}.safetensors")
         try:
             payload = src.export_prefix(ctx, path)

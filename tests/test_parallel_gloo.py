@@ -295,6 +295,19 @@ def _pp_engine_worker(rank, world, port, out_dir, pp):
     DistributedCheckpointManager(ck).load(back, 1)
     for n, p in back.params.items():
         torch.testing.assert_close(p.detach(), eng.params[n].detach(), rtol=0, atol=0, msg=n)
+    # the stages' checkpoint loads into one unpipelined replica: same weights and fp32 master weights
+    whole = B200TrainEngine("tiny", dp_group=solo, **dict(kw, seed=17))
+    whole.initialize()
+    DistributedCheckpointManager(ck).load(whole, 1)
+    master = eng.optimizer_state_tensors()["master"]
+    if eng.sharded:
+        parts = [torch.empty_like(master) for _ in range(eng.dp_size)]
+        dist.all_gather(parts, master, group=eng.dp_group)
+        master = torch.cat(parts)
+    for n, p in eng.params.items():
+        assert torch.equal(whole.params[n].detach(), p.detach()), n
+        o, w = eng.layout.offsets[n], whole.layout.offsets[n]
+        assert torch.equal(whole.master[w:w + p.numel()], master[o:o + p.numel()]), n
     # the replica's first stage owns the batch; the other stages receive it from there
     assert eng.is_batch_source() == (eng.pp_rank == 0)
     got = eng.distribute_trajectories(trajs if eng.pp_rank == 0 else None)

@@ -88,3 +88,24 @@ def test_parallel_layout_reaches_the_engine():
     c4 = AsyncRLConfig.from_file(os.path.join(CFG_DIR, "qwen3_4b_grpo_8xb200.yaml"))
     c4.train_tp_size, c4.train_pp_size = 1, 2
     assert create_train_engine(c4).pp_size == 2
+
+
+def test_presets_give_each_data_parallel_replica_complete_grpo_groups():
+    """Every shipped preset splits its batch into whole GRPO groups per
+    data-parallel replica (reference tests/test_production_ehp_ab_config.py)
+    and names GPUs of one 8-GPU box (a preset may time-share them between
+    training and rollout)."""
+    import glob
+    import os
+
+    from libra_b200.config import AsyncRLConfig
+
+    root = os.path.join(os.path.dirname(os.path.dirname(__file__)), "libra_b200", "configs")
+    presets = [f for f in sorted(glob.glob(os.path.join(root, "*.yaml"))) if not f.endswith("base.yaml")]
+    assert len(presets) >= 4
+    for f in presets:
+        c = AsyncRLConfig.from_file(f)
+        local = c.batch_size // max(1, c.train_dp_size)
+        assert c.batch_size % max(1, c.train_dp_size) == 0 and local % c.n_samples == 0, f
+        assert max(c.train_gpus, c.rollout_gpus) <= 8 and 0.0 <= c.r2e_stop_reward <= 1.0, f
+        assert all(0 <= g < 8 for inst in c.heterogeneous_rollout.instances for g in inst.gpus), f
